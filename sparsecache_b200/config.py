@@ -1,0 +1,235 @@
+"""Typed configuration: model geometry, CacheBlend, P/D and drafter settings.
+
+Model presets cover the geometries the workloads name: the tiny CPU plumbing
+decoder, Llama-3.1-8B and Llama-3.1-70B architectures (random init; no
+checkpoints are downloaded), and a small head_dim-128 geometry used by the
+GPU kernel tests.  Flag names mirror the reference CLIs
+(src/sparsecache/qa.py:22-35, experiments/reuse_cacheblend_pipeline.py:194-236).
+"""
+from __future__ import annotations
+
+import json
+from dataclasses import asdict, dataclass, field, replace
+from typing import Any
+
+
+@dataclass(frozen=True)
+class RopeScaling:
+    """Llama-3.1 frequency-dependent RoPE scaling ("llama3" rope type)."""
+
+    factor: float = 8.0
+    low_freq_factor: float = 1.0
+    high_freq_factor: float = 4.0
+    original_max_position_embeddings: int = 8192
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    """Geometry of a Llama-style decoder (RMSNorm, GQA, SwiGLU, rotate-half RoPE)."""
+
+    name: str
+    n_layers: int
+    d_model: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    rms_eps: float = 1e-5
+    rope_theta: float = 500000.0
+    rope_scaling: RopeScaling | None = None
+    max_positions: int = 131072
+    bos_token_id: int = 1
+    eos_token_ids: tuple[int, ...] = ()
+    # number of low ids reserved as "special" (synthetic ids avoid them)
+    n_special: int = 0
+
+    @property
+    def q_size(self) -> int:
+        return self.n_heads * self.head_dim
+
+    @property
+    def kv_size(self) -> int:
+        return self.n_kv_heads * self.head_dim
+
+    @property
+    def qkv_rows(self) -> int:
+        return self.q_size + 2 * self.kv_size
+
+    @property
+    def kv_bytes_per_token(self) -> int:
+        """BF16 K+V bytes of one token over all layers."""
+        return 2 * self.n_layers * self.kv_size * 2
+
+    def n_params(self) -> int:
+        per_layer = (
+            self.d_model * self.qkv_rows
+            + self.q_size * self.d_model
+            + 3 * self.d_model * self.ffn
+            + 2 * self.d_model
+        )
+        return self.n_layers * per_layer + 2 * self.vocab * self.d_model + self.d_model
+
+    def to_dict(self) -> dict[str, Any]:
+        data = asdict(self)
+        data["eos_token_ids"] = list(self.eos_token_ids)
+        return data
+
+    def to_json(self) -> str:
+        return json.dumps(self.to_dict(), sort_keys=True)
+
+    @staticmethod
+    def from_dict(data: dict[str, Any]) -> "ModelConfig":
+        data = dict(data)
+        scaling = data.get("rope_scaling")
+        if isinstance(scaling, dict):
+            data["rope_scaling"] = RopeScaling(**scaling)
+        data["eos_token_ids"] = tuple(data.get("eos_token_ids", ()))
+        return ModelConfig(**data)
+
+    def with_layers(self, n_layers: int) -> "ModelConfig":
+        return replace(self, n_layers=n_layers)
+
+
+LLAMA3_EOS = (128001, 128008, 128009)
+
+PRESETS: dict[str, ModelConfig] = {
+    # CPU plumbing decoder: 2 layers, d 256, 4 heads / 2 KV heads, head_dim 64,
+    # SwiGLU 688, RMSNorm eps 1e-5, RoPE theta 500000, vocab 1024.
+    "tiny": ModelConfig(
+        name="tiny",
+        n_layers=2,
+        d_model=256,
+        n_heads=4,
+        n_kv_heads=2,
+        head_dim=64,
+        ffn=688,
+        vocab=1024,
+        max_positions=8192,
+        bos_token_id=1,
+        eos_token_ids=(2,),
+        n_special=4,
+    ),
+    # Small head_dim-128 geometry for GPU kernel / engine tests.
+    "tiny128": ModelConfig(
+        name="tiny128",
+        n_layers=3,
+        d_model=512,
+        n_heads=4,
+        n_kv_heads=2,
+        head_dim=128,
+        ffn=1024,
+        vocab=4096,
+        max_positions=16384,
+        rope_scaling=RopeScaling(),
+        bos_token_id=1,
+        eos_token_ids=(2,),
+        n_special=4,
+    ),
+    "llama3-8b": ModelConfig(
+        name="llama3-8b",
+        n_layers=32,
+        d_model=4096,
+        n_heads=32,
+        n_kv_heads=8,
+        head_dim=128,
+        ffn=14336,
+        vocab=128256,
+        rope_scaling=RopeScaling(),
+        bos_token_id=128000,
+        eos_token_ids=LLAMA3_EOS,
+        n_special=0,
+    ),
+    "llama3-70b": ModelConfig(
+        name="llama3-70b",
+        n_layers=80,
+        d_model=8192,
+        n_heads=64,
+        n_kv_heads=8,
+        head_dim=128,
+        ffn=28672,
+        vocab=128256,
+        rope_scaling=RopeScaling(),
+        bos_token_id=128000,
+        eos_token_ids=LLAMA3_EOS,
+        n_special=0,
+    ),
+}
+
+
+def get_model_config(name: str) -> ModelConfig:
+    try:
+        return PRESETS[name]
+    except KeyError as exc:
+        raise KeyError(f"unknown model preset {name!r}; have {sorted(PRESETS)}") from exc
+
+
+DEVIATION_METRICS = ("value", "key", "kv", "value_l1", "key_l1", "kv_l1")
+
+
+@dataclass(frozen=True)
+class CacheBlendConfig:
+    """Selective-recompute parameters (README.md:169-185 of the reference).
+
+    ``keep_prefix`` True is the strict independent-document protocol in which
+    the system prefix and the question suffix are both mandatory active rows
+    (reuse_cacheblend_pipeline.py:605-616); False is the legacy
+    S-conditioned path where only the suffix is mandatory (modeling.py:234-242).
+    """
+
+    check_layer: int = 1
+    recompute_ratio: float = 0.15
+    deviation_metric: str = "value"
+    keep_prefix: bool = True
+    max_new_tokens: int = 24
+
+    def __post_init__(self) -> None:
+        if not 0 < self.recompute_ratio <= 1:
+            raise ValueError("recompute_ratio must lie in (0, 1]")
+        if self.deviation_metric not in DEVIATION_METRICS:
+            raise ValueError(f"deviation_metric must be one of {DEVIATION_METRICS}")
+        if self.check_layer < 0:
+            raise ValueError("check_layer must be non-negative")
+
+    @property
+    def dev_mode(self) -> int:
+        """Bit mask understood by the fused deviation epilogue (1 key, 2 value, 4 L1)."""
+        metric = self.deviation_metric
+        mode = 0
+        if metric.startswith("key") or metric.startswith("kv"):
+            mode |= 1
+        if metric.startswith("value") or metric.startswith("kv"):
+            mode |= 2
+        if metric.endswith("_l1"):
+            mode |= 4
+        return mode
+
+
+@dataclass(frozen=True)
+class ProgressiveConfig:
+    """Progressive P/D transfer and drafting parameters (pd_progressive_kv_pipeline.py:459-616)."""
+
+    stage_fractions: tuple[float, ...] = (0.1, 0.4, 0.7, 1.0)
+    anchor_tokens: int = 256
+    draft_tokens: int = 4
+    commit_window: int | None = None  # None = W infinity (single final verifier)
+    transport_gbps: float | None = None
+    eager_serial_wire: bool = False
+    page_tokens: int = 64
+
+
+@dataclass(frozen=True)
+class DrafterConfig:
+    """Sparse-KV drafter geometry and memory selection."""
+
+    hidden: int = 512
+    heads: int = 4
+    head_dim: int = 128
+    memory_heads: int = 8
+    memory_layers: tuple[int, ...] = (8, 20, 31)
+    seed_layers: tuple[int, ...] = (2, 16, 29)
+    sink_tokens: int = 64
+    recent_tokens: int = 512
+    chunk_tokens: int = 64
+    chunk_budget: int = 2048
+    extra: dict[str, Any] = field(default_factory=dict)

@@ -1,0 +1,467 @@
+// PyTorch bindings of the sm_100a kernels.  Every op launches on the
+// current torch CUDA stream and validates shapes, dtypes and alignment
+// before launch (TMA needs 16-byte aligned bases and row strides).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "kernels.h"
+
+namespace {
+
+using torch::Tensor;
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == torch::kBFloat16, #x " must be bf16")
+#define CHECK_I32(x) TORCH_CHECK((x).scalar_type() == torch::kInt32, #x " must be int32")
+#define CHECK_F32(x) TORCH_CHECK((x).scalar_type() == torch::kFloat32, #x " must be float32")
+#define CHECK_ALIGN16(x) \
+  TORCH_CHECK((reinterpret_cast<uintptr_t>((x).data_ptr()) & 15) == 0, #x " must be 16-byte aligned")
+
+void check_cuda(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e));
+}
+
+int num_sms() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (n[dev] == 0) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev];
+}
+
+// Per-device status word the tcgen05 kernels write when a bounded wait expires.
+Tensor& status_tensor(const Tensor& like) {
+  static Tensor st[64];
+  const int dev = like.get_device();
+  if (!st[dev].defined()) {
+    st[dev] = torch::zeros({1}, torch::TensorOptions().dtype(torch::kInt32).device(like.device()));
+  }
+  return st[dev];
+}
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream(); }
+
+void check_matrix(const Tensor& t, const char* name) {
+  CHECK_CUDA(t);
+  CHECK_BF16(t);
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.stride(1) == 1, name, " must be row-major");
+  TORCH_CHECK((t.stride(0) * 2) % 16 == 0, name, " row stride must be a multiple of 16 bytes");
+  CHECK_ALIGN16(t);
+}
+
+sc::GemmArgs base_gemm(const Tensor& a, const Tensor& w, int epi, int bn) {
+  check_matrix(a, "a");
+  check_matrix(w, "w");
+  TORCH_CHECK(a.size(1) == w.size(1), "K mismatch");
+  TORCH_CHECK(bn == 128 || bn == 256, "bn must be 128 or 256");
+  sc::GemmArgs g{};
+  g.a = reinterpret_cast<const __nv_bfloat16*>(a.data_ptr());
+  g.b = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  g.M = (int)a.size(0);
+  g.N = (int)w.size(0);
+  g.K = (int)a.size(1);
+  g.lda = (int)a.stride(0);
+  g.ldb = (int)w.stride(0);
+  g.epi = epi;
+  g.bn = bn;
+  g.num_sms = num_sms();
+  g.status = status_tensor(a).data_ptr<int>();
+  return g;
+}
+
+void run_gemm(const sc::GemmArgs& g) {
+  if (g.M == 0 || g.N == 0) return;
+  check_cuda(sc::gemm_bf16_tc(g, cur_stream()), "gemm_bf16_tc");
+}
+
+// out = a @ w^T
+void gemm_store(Tensor a, Tensor w, Tensor out, int64_t bn) {
+  const c10::cuda::CUDAGuard guard(a.device());
+  auto g = base_gemm(a, w, sc::EPI_STORE, (int)bn);
+  check_matrix(out, "out");
+  TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == w.size(0), "out shape");
+  TORCH_CHECK(g.N % 32 == 0, "N must be a multiple of 32");
+  g.ep.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  g.ep.ldo = (int)out.stride(0);
+  run_gemm(g);
+}
+
+// out = residual + bf16(a @ w^T)   (out may alias residual)
+void gemm_residual(Tensor a, Tensor w, Tensor out, Tensor residual, int64_t bn) {
+  const c10::cuda::CUDAGuard guard(a.device());
+  auto g = base_gemm(a, w, sc::EPI_RESIDUAL, (int)bn);
+  check_matrix(out, "out");
+  check_matrix(residual, "residual");
+  TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == w.size(0), "out shape");
+  TORCH_CHECK(residual.sizes() == out.sizes(), "residual shape");
+  TORCH_CHECK(g.N % 32 == 0, "N must be a multiple of 32");
+  g.ep.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  g.ep.ldo = (int)out.stride(0);
+  g.ep.residual = reinterpret_cast<const __nv_bfloat16*>(residual.data_ptr());
+  g.ep.ldr = (int)residual.stride(0);
+  run_gemm(g);
+}
+
+// out[:, j] = silu(gate_j) * up_j with w_gu rows interleaved in blocks of bn/2
+void gemm_swiglu(Tensor a, Tensor w_gu, Tensor out, int64_t bn) {
+  const c10::cuda::CUDAGuard guard(a.device());
+  auto g = base_gemm(a, w_gu, sc::EPI_SWIGLU, (int)bn);
+  check_matrix(out, "out");
+  TORCH_CHECK(w_gu.size(0) % bn == 0, "gate/up rows must be a multiple of bn");
+  TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == w_gu.size(0) / 2, "out shape");
+  g.ep.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  g.ep.ldo = (int)out.stride(0);
+  run_gemm(g);
+}
+
+// Fused QKV projection + RoPE + K/V cache scatter (+ optional deviation partials).
+void gemm_qkv(Tensor a, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_cache,
+              Tensor rope_pos, Tensor cache_slot, Tensor rope_table, int64_t n_q_heads,
+              int64_t n_kv_heads, c10::optional<Tensor> dev_part, int64_t dev_mode, int64_t bn) {
+  const c10::cuda::CUDAGuard guard(a.device());
+  auto g = base_gemm(a, w_qkv, sc::EPI_QKV, (int)bn);
+  check_matrix(q_out, "q_out");
+  TORCH_CHECK(w_qkv.size(0) == (n_q_heads + 2 * n_kv_heads) * 128, "w_qkv rows");
+  TORCH_CHECK(q_out.size(0) >= a.size(0) && q_out.size(1) == n_q_heads * 128, "q_out shape");
+  CHECK_CUDA(k_cache); CHECK_BF16(k_cache); CHECK_CUDA(v_cache); CHECK_BF16(v_cache);
+  TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(0) == n_kv_heads && k_cache.size(2) == 128 &&
+                  k_cache.is_contiguous(), "k_cache must be [n_kv_heads, cap, 128] contiguous");
+  TORCH_CHECK(v_cache.sizes() == k_cache.sizes() && v_cache.is_contiguous(), "v_cache shape");
+  CHECK_I32(rope_pos); CHECK_I32(cache_slot); CHECK_F32(rope_table);
+  TORCH_CHECK(rope_pos.numel() >= a.size(0) && cache_slot.numel() >= a.size(0), "positions");
+  TORCH_CHECK(rope_table.dim() == 2 && rope_table.size(1) == 128, "rope_table [P, 64*2]");
+  g.ep.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
+  g.ep.ldq = (int)q_out.stride(0);
+  g.ep.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr());
+  g.ep.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
+  g.ep.cache_cap = (int)k_cache.size(1);
+  g.ep.rope_pos = rope_pos.data_ptr<int>();
+  g.ep.cache_slot = cache_slot.data_ptr<int>();
+  g.ep.rope_table = reinterpret_cast<const float2*>(rope_table.data_ptr<float>());
+  g.ep.n_q_heads = (int)n_q_heads;
+  g.ep.n_kv_heads = (int)n_kv_heads;
+  if (dev_part.has_value() && dev_part->defined()) {
+    CHECK_F32(*dev_part);
+    TORCH_CHECK(dev_part->numel() >= a.size(0) * 2 * n_kv_heads, "dev_part size");
+    g.ep.dev_part = dev_part->data_ptr<float>();
+    g.ep.dev_mode = (int)dev_mode;
+  }
+  run_gemm(g);
+}
+
+// ---------------------------------------------------------------- GEMV
+sc::GemvArgs base_gemv(const Tensor& x, const Tensor& w, c10::optional<Tensor> norm_w, double eps,
+                       int epi) {
+  check_matrix(x, "x");
+  check_matrix(w, "w");
+  TORCH_CHECK(x.size(1) == w.size(1), "K mismatch");
+  sc::GemvArgs g{};
+  g.w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  g.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  g.ldx = (int)x.stride(0);
+  g.M = (int)x.size(0);
+  g.N = (int)w.size(0);
+  g.K = (int)w.size(1);
+  if (norm_w.has_value() && norm_w->defined()) {
+    CHECK_BF16(*norm_w);
+    CHECK_ALIGN16(*norm_w);
+    g.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w->data_ptr());
+  }
+  g.eps = (float)eps;
+  g.epi = epi;
+  g.num_sms = num_sms();
+  return g;
+}
+
+void run_gemv(const sc::GemvArgs& g) { check_cuda(sc::gemv_bf16(g, cur_stream()), "gemv_bf16"); }
+
+void gemv_store(Tensor x, Tensor w, c10::optional<Tensor> norm_w, double eps, Tensor out) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto g = base_gemv(x, w, norm_w, eps, sc::GEMV_STORE);
+  CHECK_BF16(out);
+  g.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  g.ldo = (int)out.stride(0);
+  run_gemv(g);
+}
+
+void gemv_residual(Tensor x, Tensor w, c10::optional<Tensor> norm_w, double eps, Tensor out,
+                   Tensor residual) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto g = base_gemv(x, w, norm_w, eps, sc::GEMV_RESIDUAL);
+  CHECK_BF16(out); CHECK_BF16(residual);
+  g.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  g.ldo = (int)out.stride(0);
+  g.residual = reinterpret_cast<const __nv_bfloat16*>(residual.data_ptr());
+  g.ldr = (int)residual.stride(0);
+  run_gemv(g);
+}
+
+void gemv_swiglu(Tensor x, Tensor w_gu, c10::optional<Tensor> norm_w, double eps, Tensor out) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto g = base_gemv(x, w_gu, norm_w, eps, sc::GEMV_SWIGLU);
+  CHECK_BF16(out);
+  TORCH_CHECK(w_gu.size(0) % 256 == 0, "gate/up rows must be a multiple of 256");
+  g.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  g.ldo = (int)out.stride(0);
+  run_gemv(g);
+}
+
+void gemv_qkv(Tensor x, Tensor w_qkv, c10::optional<Tensor> norm_w, double eps, Tensor q_out,
+              Tensor k_cache, Tensor v_cache, Tensor pos, Tensor rope_table, int64_t n_q_heads,
+              int64_t n_kv_heads) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto g = base_gemv(x, w_qkv, norm_w, eps, sc::GEMV_QKV);
+  CHECK_I32(pos); CHECK_F32(rope_table);
+  TORCH_CHECK(w_qkv.size(0) == (n_q_heads + 2 * n_kv_heads) * 128, "w_qkv rows");
+  TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(2) == 128 && k_cache.is_contiguous(), "k_cache");
+  g.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
+  g.ldq = (int)q_out.stride(0);
+  g.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr());
+  g.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
+  g.cache_cap = (int)k_cache.size(1);
+  g.pos = pos.data_ptr<int>();
+  g.rope_table = reinterpret_cast<const float2*>(rope_table.data_ptr<float>());
+  g.n_q_heads = (int)n_q_heads;
+  g.n_kv_heads = (int)n_kv_heads;
+  run_gemv(g);
+}
+
+int64_t gemv_argmax_grid(int64_t n_rows) {
+  const int64_t pairs = n_rows / 2;
+  int64_t grid = (pairs + 7) / 8;
+  const int64_t cap = (int64_t)num_sms() * 8;
+  return grid < cap ? grid : cap;
+}
+
+void gemv_argmax(Tensor x, Tensor w, c10::optional<Tensor> norm_w, double eps, Tensor part_val,
+                 Tensor part_idx, Tensor counter, Tensor out_token,
+                 c10::optional<Tensor> token_log, c10::optional<Tensor> gen_count,
+                 c10::optional<Tensor> embed, c10::optional<Tensor> next_hidden,
+                 c10::optional<Tensor> pos_advance) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto g = base_gemv(x, w, norm_w, eps, sc::GEMV_ARGMAX);
+  CHECK_F32(part_val); CHECK_I32(part_idx); CHECK_I32(out_token);
+  const int64_t grid = gemv_argmax_grid(w.size(0));
+  TORCH_CHECK(part_val.numel() >= grid * x.size(0) && part_idx.numel() >= grid * x.size(0),
+              "argmax partial buffers too small");
+  g.part_val = part_val.data_ptr<float>();
+  g.part_idx = part_idx.data_ptr<int>();
+  g.counter = reinterpret_cast<unsigned int*>(counter.data_ptr<int>());
+  g.out_token = out_token.data_ptr<int>();
+  if (token_log.has_value() && token_log->defined()) {
+    TORCH_CHECK(gen_count.has_value() && gen_count->defined(), "gen_count required");
+    g.token_log = token_log->data_ptr<int>();
+    g.gen_count = gen_count->data_ptr<int>();
+  }
+  if (embed.has_value() && embed->defined()) {
+    TORCH_CHECK(next_hidden.has_value() && next_hidden->defined(), "next_hidden required");
+    g.embed = reinterpret_cast<const __nv_bfloat16*>(embed->data_ptr());
+    g.next_hidden = reinterpret_cast<__nv_bfloat16*>(next_hidden->data_ptr());
+  }
+  if (pos_advance.has_value() && pos_advance->defined()) g.pos_advance = pos_advance->data_ptr<int>();
+  run_gemv(g);
+}
+
+// ----------------------------------------------------------- attention
+void attention_prefill(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tensor k_cache,
+                       Tensor v_cache, c10::optional<Tensor> kpos, int64_t n_keys,
+                       int64_t n_heads, double scale, Tensor out) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  check_matrix(q, "q");
+  check_matrix(out, "out");
+  CHECK_I32(qpos);
+  TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(2) == 128 && k_cache.is_contiguous(), "k_cache");
+  TORCH_CHECK(v_cache.sizes() == k_cache.sizes() && v_cache.is_contiguous(), "v_cache");
+  TORCH_CHECK(n_keys <= k_cache.size(1), "n_keys exceeds cache capacity");
+  sc::AttnPrefillArgs p{};
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.ldq = (int)q.stride(0);
+  if (q_rows.has_value() && q_rows->defined()) {
+    CHECK_I32(*q_rows);
+    p.q_rows = q_rows->data_ptr<int>();
+  }
+  p.qpos = qpos.data_ptr<int>();
+  p.n_rows = (int)out.size(0);
+  TORCH_CHECK(qpos.numel() >= p.n_rows, "qpos too short");
+  p.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
+  p.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  p.cache_cap = (int)k_cache.size(1);
+  if (kpos.has_value() && kpos->defined()) {
+    CHECK_I32(*kpos);
+    TORCH_CHECK(kpos->numel() >= n_keys, "kpos too short");
+    p.kpos = kpos->data_ptr<int>();
+  }
+  p.n_keys = (int)n_keys;
+  p.n_heads = (int)n_heads;
+  p.n_kv_heads = (int)k_cache.size(0);
+  p.head_dim = 128;
+  p.scale = (float)scale;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.ldo = (int)out.stride(0);
+  check_cuda(sc::attention_prefill(p, cur_stream()), "attention_prefill");
+}
+
+void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int64_t n_heads,
+                      double scale, int64_t splits, Tensor part_o, Tensor part_ml,
+                      Tensor counters, Tensor out) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  CHECK_BF16(q); CHECK_BF16(out); CHECK_I32(pos);
+  TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(2) == 128 && k_cache.is_contiguous(), "k_cache");
+  sc::AttnDecodeArgs a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.M = (int)q.size(0);
+  a.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
+  a.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  a.cache_cap = (int)k_cache.size(1);
+  a.pos = pos.data_ptr<int>();
+  a.n_heads = (int)n_heads;
+  a.n_kv_heads = (int)k_cache.size(0);
+  a.scale = (float)scale;
+  a.splits = (int)splits;
+  TORCH_CHECK(part_o.numel() >= n_heads * a.M * splits * 128, "part_o too small");
+  TORCH_CHECK(part_ml.numel() >= n_heads * a.M * splits * 2, "part_ml too small");
+  a.part_o = part_o.data_ptr<float>();
+  a.part_ml = part_ml.data_ptr<float>();
+  a.counters = reinterpret_cast<unsigned int*>(counters.data_ptr<int>());
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  check_cuda(sc::attention_decode(a, cur_stream()), "attention_decode");
+}
+
+// ------------------------------------------------------------ pointwise
+void rmsnorm(Tensor x, c10::optional<Tensor> rows, Tensor w, double eps, Tensor out) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_matrix(x, "x");
+  check_matrix(out, "out");
+  const int* r = nullptr;
+  if (rows.has_value() && rows->defined()) { CHECK_I32(*rows); r = rows->data_ptr<int>(); }
+  check_cuda(sc::rmsnorm_bf16(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                              (int)x.stride(0), r,
+                              reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+                              reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)out.stride(0),
+                              (int)out.size(0), (int)out.size(1), (float)eps, cur_stream()),
+             "rmsnorm");
+}
+
+void embedding(Tensor ids, Tensor table, Tensor out) {
+  const c10::cuda::CUDAGuard guard(ids.device());
+  CHECK_I32(ids);
+  check_matrix(table, "table");
+  check_matrix(out, "out");
+  check_cuda(sc::embedding_bf16(ids.data_ptr<int>(),
+                                reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
+                                reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)ids.numel(),
+                                (int)table.size(1), cur_stream()),
+             "embedding");
+}
+
+void gather_rows(Tensor x, Tensor rows, Tensor out) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_matrix(x, "x");
+  check_matrix(out, "out");
+  CHECK_I32(rows);
+  check_cuda(sc::gather_rows_bf16(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                                  (int)x.stride(0), rows.data_ptr<int>(),
+                                  reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                                  (int)out.stride(0), (int)out.size(0), (int)out.size(1),
+                                  cur_stream()),
+             "gather_rows");
+}
+
+// docs: int32 [n_docs, 6] = (ptr_lo, ptr_hi, n_tokens, src_pos, dst_slot, dst_pos), on device
+void compose_relocate(Tensor docs, Tensor offsets, int64_t total_tokens, int64_t layer_begin,
+                      int64_t layer_end, int64_t n_layers, Tensor cache, int64_t n_kv_heads,
+                      Tensor rope_table) {
+  const c10::cuda::CUDAGuard guard(cache.device());
+  CHECK_I32(docs); CHECK_I32(offsets); CHECK_BF16(cache); CHECK_F32(rope_table);
+  TORCH_CHECK(docs.is_cuda() && offsets.is_cuda(), "docs/offsets on device");
+  TORCH_CHECK(docs.dim() == 2 && docs.size(1) == 6 && docs.is_contiguous(), "docs [n, 6]");
+  TORCH_CHECK(cache.dim() == 5 && cache.size(1) == 2 && cache.size(2) == n_kv_heads &&
+                  cache.size(4) == 128 && cache.is_contiguous(),
+              "cache must be [L, 2, n_kv_heads, cap, 128]");
+  static_assert(sizeof(sc::ComposeDoc) == 24, "ComposeDoc layout");
+  sc::ComposeArgs a{};
+  a.docs = reinterpret_cast<const sc::ComposeDoc*>(docs.data_ptr<int>());
+  a.n_docs = (int)docs.size(0);
+  a.doc_token_offset = offsets.data_ptr<int>();
+  a.total_tokens = (int)total_tokens;
+  a.layer_begin = (int)layer_begin;
+  a.layer_end = (int)layer_end;
+  a.n_layers = (int)n_layers;
+  a.cache = reinterpret_cast<__nv_bfloat16*>(cache.data_ptr());
+  a.cache_cap = (int)cache.size(3);
+  a.n_kv_heads = (int)n_kv_heads;
+  a.rope_table = reinterpret_cast<const float2*>(rope_table.data_ptr<float>());
+  check_cuda(sc::compose_relocate(a, cur_stream()), "compose_relocate");
+}
+
+void cacheblend_select(Tensor dev_part, int64_t n_kv_heads, int64_t dev_mode, int64_t total_rows,
+                       int64_t doc_begin, int64_t doc_end, int64_t k, bool keep_prefix,
+                       Tensor active, Tensor n_active, Tensor scores,
+                       c10::optional<Tensor> checksum) {
+  const c10::cuda::CUDAGuard guard(dev_part.device());
+  CHECK_F32(dev_part); CHECK_I32(active); CHECK_I32(n_active); CHECK_F32(scores);
+  TORCH_CHECK(scores.numel() >= std::max<int64_t>(1, doc_end - doc_begin), "scores scratch");
+  sc::SelectArgs a{};
+  a.dev_part = dev_part.data_ptr<float>();
+  a.n_kv_heads = (int)n_kv_heads;
+  a.dev_mode = (int)dev_mode;
+  a.total_rows = (int)total_rows;
+  a.doc_begin = (int)doc_begin;
+  a.doc_end = (int)doc_end;
+  a.k = (int)k;
+  a.keep_prefix = keep_prefix ? 1 : 0;
+  a.active = active.data_ptr<int>();
+  a.n_active = n_active.data_ptr<int>();
+  a.scores = scores.data_ptr<float>();
+  if (checksum.has_value() && checksum->defined()) {
+    TORCH_CHECK(checksum->scalar_type() == torch::kInt64, "checksum int64");
+    a.checksum = reinterpret_cast<long long*>(checksum->data_ptr<int64_t>());
+  }
+  check_cuda(sc::cacheblend_select(a, cur_stream()), "cacheblend_select");
+}
+
+void arange_i32(Tensor out, int64_t start) {
+  const c10::cuda::CUDAGuard guard(out.device());
+  CHECK_I32(out);
+  check_cuda(sc::fill_arange_i32(out.data_ptr<int>(), (int)out.numel(), (int)start, cur_stream()),
+             "arange");
+}
+
+void index_i32(Tensor src, Tensor idx, Tensor out) {
+  const c10::cuda::CUDAGuard guard(out.device());
+  CHECK_I32(src); CHECK_I32(idx); CHECK_I32(out);
+  check_cuda(sc::index_i32(src.data_ptr<int>(), idx.data_ptr<int>(), out.data_ptr<int>(),
+                           (int)out.numel(), cur_stream()),
+             "index_i32");
+}
+
+Tensor status(Tensor like) { return status_tensor(like); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of sparsecache_b200";
+  m.def("gemm_store", &gemm_store);
+  m.def("gemm_residual", &gemm_residual);
+  m.def("gemm_swiglu", &gemm_swiglu);
+  m.def("gemm_qkv", &gemm_qkv);
+  m.def("gemv_store", &gemv_store);
+  m.def("gemv_residual", &gemv_residual);
+  m.def("gemv_swiglu", &gemv_swiglu);
+  m.def("gemv_qkv", &gemv_qkv);
+  m.def("gemv_argmax", &gemv_argmax);
+  m.def("gemv_argmax_grid", &gemv_argmax_grid);
+  m.def("attention_prefill", &attention_prefill);
+  m.def("attention_decode", &attention_decode);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("embedding", &embedding);
+  m.def("gather_rows", &gather_rows);
+  m.def("compose_relocate", &compose_relocate);
+  m.def("cacheblend_select", &cacheblend_select);
+  m.def("arange_i32", &arange_i32);
+  m.def("index_i32", &index_i32);
+  m.def("status", &status);
+  m.def("num_sms", &num_sms);
+}

@@ -1,0 +1,405 @@
+// Persistent tcgen05 BF16 GEMM for sm_100a with fused epilogues.
+//
+//   C[M, N] = A[M, K] . B[N, K]^T      (A activations, B nn.Linear weights)
+//
+// One CTA per SM walks a static tile schedule.  Warp roles:
+//   warp 0      TMA producer: 128B-swizzled A/B tiles into a STAGES-deep ring
+//   warp 1      MMA issuer: tcgen05.mma (M=128, N=BN, K=16) into TMEM,
+//               owns the TMEM allocation
+//   warps 2..5  epilogue: tcgen05.ld the fp32 accumulator (one row per
+//               thread), apply the fused epilogue and store bf16
+// The accumulator is double-buffered in TMEM so the epilogue of tile i
+// overlaps the MMAs of tile i+1.  No cluster multicast is used anywhere, so
+// the same kernel is safe inside multi-GPU programs.
+//
+// Fused epilogues (the hot projections of a Llama layer):
+//   EPI_STORE     C = acc
+//   EPI_RESIDUAL  C = R + bf16(acc)                         (o_proj, down_proj)
+//   EPI_SWIGLU    C = silu(gate) * up, gate/up interleaved in 128-col blocks
+//   EPI_QKV       RoPE on Q/K heads at per-row positions; Q to a row-major
+//                 buffer, K/V scattered into the paged layer cache at per-row
+//                 slots; optional per-(row, kv-head) deviation partials of the
+//                 fresh K/V against the cache contents they overwrite (the
+//                 CacheBlend check-layer score, fused).
+//
+// Reference behaviour reproduced: modeling.py:330-342 (_project_qkv with
+// apply_rope), modeling.py:257-264 (scatter of fresh K/V into the composed
+// cache), modeling.py:215-226 / reuse_cacheblend_pipeline.py:586-604
+// (squared deviation of fresh vs cached K or V), HF LlamaMLP SwiGLU.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace sc {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+constexpr int kGemmThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kABytes = kGemmBM * kGemmBK * 2;
+  static constexpr int kBBytes = BN * kGemmBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+};
+
+struct alignas(8) GemmBarriers {
+  uint64_t full[8];
+  uint64_t empty[8];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+};
+
+// --------------------------------------------------------------------------
+// Epilogue helpers (one thread = one output row, 32 columns per TMEM load)
+// --------------------------------------------------------------------------
+__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 w;
+    w.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
+    w.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
+    w.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
+    w.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
+    d[i] = w;
+  }
+}
+
+__device__ __forceinline__ void load_row32(const __nv_bfloat16* src, float* v) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 w = s[i];
+    float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), c = unpack_bf16x2(w.z),
+           d = unpack_bf16x2(w.w);
+    v[8 * i + 0] = a.x; v[8 * i + 1] = a.y; v[8 * i + 2] = b.x; v[8 * i + 3] = b.y;
+    v[8 * i + 4] = c.x; v[8 * i + 5] = c.y; v[8 * i + 6] = d.x; v[8 * i + 7] = d.y;
+  }
+}
+
+template <int BN, int EPI>
+__device__ __forceinline__ void gemm_epilogue_tile(const GemmEpilogue& ep, uint32_t tacc,
+                                                   int row, int tile_n, int M, int N) {
+  const bool row_ok = row < M;
+  if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tacc + c * 32, r);
+      tmem_ld_wait();
+      const int col = tile_n * BN + c * 32;
+      if (row_ok && col < N) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if constexpr (EPI == EPI_RESIDUAL) {
+          float res[32];
+          load_row32(ep.residual + (size_t)row * ep.ldr + col, res);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = res[i] + bf16_round(v[i]);
+        }
+        store_row32(ep.out + (size_t)row * ep.ldo + col, v);
+      }
+    }
+  } else if constexpr (EPI == EPI_SWIGLU) {
+    // Tile columns [0, BN/2) are gate rows, [BN/2, BN) the matching up rows.
+#pragma unroll 1
+    for (int c = 0; c < BN / 64; ++c) {
+      uint32_t g[32], u[32];
+      tmem_ld_32x32b_x32(tacc + c * 32, g);
+      tmem_ld_32x32b_x32(tacc + BN / 2 + c * 32, u);
+      tmem_ld_wait();
+      const int col = tile_n * (BN / 2) + c * 32;
+      if (row_ok) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float gb = bf16_round(__uint_as_float(g[i]));
+          const float ub = bf16_round(__uint_as_float(u[i]));
+          v[i] = bf16_round(silu_f(gb)) * ub;
+        }
+        store_row32(ep.out + (size_t)row * ep.ldo + col, v);
+      }
+    }
+  } else if constexpr (EPI == EPI_QKV) {
+    int pos = 0, slot = 0;
+    if (row_ok) {
+      pos = ep.rope_pos[row];
+      slot = ep.cache_slot[row];
+    }
+#pragma unroll 1
+    for (int j = 0; j < BN / 128; ++j) {
+      const int head = tile_n * (BN / 128) + j;  // index in [q heads | k heads | v heads]
+      const bool is_q = head < ep.n_q_heads;
+      const bool is_k = !is_q && head < ep.n_q_heads + ep.n_kv_heads;
+      const bool is_v = !is_q && !is_k;
+      const int kvh = is_k ? head - ep.n_q_heads : head - ep.n_q_heads - ep.n_kv_heads;
+      __nv_bfloat16* dst = nullptr;
+      if (is_q) {
+        dst = ep.q_out + (size_t)row * ep.ldq + head * 128;
+      } else {
+        __nv_bfloat16* cache = is_k ? ep.k_cache : ep.v_cache;
+        dst = cache + ((size_t)kvh * ep.cache_cap + slot) * 128;
+      }
+      const bool want_dev = ep.dev_part != nullptr &&
+                            ((is_k && (ep.dev_mode & DEV_KEY)) ||
+                             (is_v && (ep.dev_mode & DEV_VALUE)));
+      const bool l1 = (ep.dev_mode & DEV_L1) != 0;
+      float dev = 0.f;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        uint32_t a[32], b[32];
+        tmem_ld_32x32b_x32(tacc + j * 128 + half * 32, a);
+        tmem_ld_32x32b_x32(tacc + j * 128 + 64 + half * 32, b);
+        tmem_ld_wait();
+        if (!row_ok) continue;
+        float xa[32], xb[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          xa[i] = __uint_as_float(a[i]);
+          xb[i] = __uint_as_float(b[i]);
+        }
+        if (!is_v) {
+          const float2* tab = ep.rope_table + (size_t)pos * 64 + half * 32;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float2 cs = tab[i];
+            const float oa = xa[i] * cs.x - xb[i] * cs.y;
+            const float ob = xb[i] * cs.x + xa[i] * cs.y;
+            xa[i] = oa;
+            xb[i] = ob;
+          }
+        }
+        if (want_dev) {
+          float olda[32], oldb[32];
+          load_row32(dst + half * 32, olda);
+          load_row32(dst + 64 + half * 32, oldb);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float da = bf16_round(xa[i]) - olda[i];
+            const float db = bf16_round(xb[i]) - oldb[i];
+            dev += l1 ? (fabsf(da) + fabsf(db)) : (da * da + db * db);
+          }
+        }
+        store_row32(dst + half * 32, xa);
+        store_row32(dst + 64 + half * 32, xb);
+      }
+      if (want_dev && row_ok) {
+        ep.dev_part[(size_t)row * (2 * ep.n_kv_heads) + (is_v ? ep.n_kv_heads : 0) + kvh] = dev;
+      }
+    }
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                   const __grid_constant__ CUtensorMap tmap_b, int M, int N, int K,
+                   GemmEpilogue ep, int* status) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(smem + S * Cfg::kStageBytes);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int num_m = (M + kGemmBM - 1) / kGemmBM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + kGemmBK - 1) / kGemmBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->tmem_full[b], 1);
+      mbar_init(&bars->tmem_empty[b], 4);
+    }
+    mbar_init(&bars->drain, 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued_phase[8];
+      bool issued[8];
+      for (int s = 0; s < S; ++s) issued[s] = false, issued_phase[s] = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int tm = t % num_m, tn = t / num_m;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&bars->empty[stage], phase ^ 1, status, kStatusTimeoutSmemEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * Cfg::kStageBytes;
+          uint8_t* sb = sa + Cfg::kABytes;
+          mbar_arrive_expect_tx(&bars->full[stage], Cfg::kStageBytes);
+          tma_load_2d(sa, &tmap_a, &bars->full[stage], kb * kGemmBK, tm * kGemmBM);
+          tma_load_2d(sb, &tmap_b, &bars->full[stage], kb * kGemmBK, tn * BN);
+          issued[stage] = true;
+          issued_phase[stage] = phase;
+          if (++stage == S) stage = 0, phase ^= 1;
+        }
+      }
+      // Drain: every TMA load issued must have landed before the CTA exits.
+      for (int s = 0; s < S; ++s)
+        if (issued[s]) mbar_wait(&bars->full[s], issued_phase[s], status, kStatusTimeoutDrain);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(kGemmBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      bool any = false;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t tphase = (local >> 1) & 1;
+        if (!mbar_wait(&bars->tmem_empty[buf], tphase ^ 1, status, kStatusTimeoutTmemEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tacc = tmem_base + buf * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&bars->full[stage], phase, status, kStatusTimeoutTmaFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
+          const uint32_t sb = sa + Cfg::kABytes;
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) {
+            const uint64_t ad = make_desc_kmajor_sw128(sa + k * 32);
+            const uint64_t bd = make_desc_kmajor_sw128(sb + k * 32);
+            tc_mma_f16(tacc, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          any = true;
+          tc_commit(&bars->empty[stage]);
+          if (++stage == S) stage = 0, phase ^= 1;
+        }
+        if (!ok) break;
+        tc_commit(&bars->tmem_full[buf]);
+      }
+      if (any) {
+        // Wait for every MMA of this CTA to complete before teardown.
+        tc_commit(&bars->drain);
+        mbar_wait(&bars->drain, 0, status, kStatusTimeoutDrain);
+      }
+    }
+  } else {
+    // ---------------- Epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      const int tm = t % num_m, tn = t / num_m;
+      const int buf = local & 1;
+      const uint32_t tphase = (local >> 1) & 1;
+      if (!mbar_wait(&bars->tmem_full[buf], tphase, status, kStatusTimeoutTmemFull)) break;
+      tc_fence_after();
+      const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
+      const int row = tm * kGemmBM + quarter * 32 + lane;
+      gemm_epilogue_tile<BN, EPI>(ep, tacc, row, tn, M, N);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->tmem_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+// --------------------------------------------------------------------------
+// Host side
+// --------------------------------------------------------------------------
+static PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    fn = reinterpret_cast<PFN_encodeTiled>(p);
+  }
+  return fn;
+}
+
+bool make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                       uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
+                       bool swizzle128) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (enc == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, int EPI>
+static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  CUtensorMap ta, tb;
+  if (!make_tmap_2d_bf16(&ta, g.a, g.K, g.M, g.lda, kGemmBK, kGemmBM, true)) return cudaErrorInvalidValue;
+  if (!make_tmap_2d_bf16(&tb, g.b, g.K, g.N, g.ldb, kGemmBK, BN, true)) return cudaErrorInvalidValue;
+  auto kern = gemm_tc_kernel<BN, EPI>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  const int num_tiles = ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + BN - 1) / BN);
+  int grid = num_tiles < g.num_sms ? num_tiles : g.num_sms;
+  if (grid < 1) grid = 1;
+  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, g.M, g.N, g.K, g.ep, g.status);
+  return cudaGetLastError();
+}
+
+cudaError_t gemm_bf16_tc(const GemmArgs& g, cudaStream_t stream) {
+  const int bn = g.bn;
+  switch (g.epi) {
+    case EPI_STORE:
+      return bn == 128 ? launch_gemm<128, EPI_STORE>(g, stream) : launch_gemm<256, EPI_STORE>(g, stream);
+    case EPI_RESIDUAL:
+      return bn == 128 ? launch_gemm<128, EPI_RESIDUAL>(g, stream)
+                       : launch_gemm<256, EPI_RESIDUAL>(g, stream);
+    case EPI_SWIGLU:
+      return bn == 128 ? launch_gemm<128, EPI_SWIGLU>(g, stream) : launch_gemm<256, EPI_SWIGLU>(g, stream);
+    case EPI_QKV:
+      return bn == 128 ? launch_gemm<128, EPI_QKV>(g, stream) : launch_gemm<256, EPI_QKV>(g, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace sc

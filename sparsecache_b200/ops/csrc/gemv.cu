@@ -1,0 +1,331 @@
+// Weight-streaming small-M GEMV for decode and batched verification.
+//
+// At batch 1 a Llama decode step reads every weight once and does two FLOPs
+// per weight, so it is bound by HBM bandwidth, not by the tensor cores.  This
+// kernel streams W with 128-bit L1-bypassing loads (several in flight per
+// lane), keeps the M <= 8 input rows in shared memory, and fuses the
+// neighbouring pointwise work so a decode layer is five launches:
+//   prologue  optional RMSNorm of x (HF LlamaRMSNorm rounding order)
+//   GEMV_QKV      rows (d, d+64) of one head per warp -> RoPE in registers,
+//                 Q to a buffer, K/V appended to the layer cache at *pos + m
+//   GEMV_RESIDUAL out = residual + bf16(W x)          (o_proj / down_proj)
+//   GEMV_SWIGLU   gate/up rows of one output per warp -> silu(g) * u
+//   GEMV_ARGMAX   LM head: per-CTA (max, first index) partials, the last CTA
+//                 reduces them, logs the token, loads the next embedding row
+//                 and advances the device-side position (decode feedback
+//                 without a host round trip; graph-replayable).
+// Rows are processed in pairs; the pair layout matches the tcgen05 GEMM
+// weight layout (fused QKV, gate/up interleaved in 128-row blocks).
+//
+// Reference behaviour: HF decode step per token (modeling.py:383-417,
+// progressive_kv_feasibility.py:561-613) with argmax over bf16 logits.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace sc {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kUnroll = 4;
+
+__device__ __forceinline__ float dot8(const uint4 w, const uint4 x) {
+  float2 w0 = unpack_bf16x2(w.x), w1 = unpack_bf16x2(w.y), w2 = unpack_bf16x2(w.z),
+         w3 = unpack_bf16x2(w.w);
+  float2 x0 = unpack_bf16x2(x.x), x1 = unpack_bf16x2(x.y), x2 = unpack_bf16x2(x.z),
+         x3 = unpack_bf16x2(x.w);
+  float s = w0.x * x0.x;
+  s = fmaf(w0.y, x0.y, s);
+  s = fmaf(w1.x, x1.x, s);
+  s = fmaf(w1.y, x1.y, s);
+  s = fmaf(w2.x, x2.x, s);
+  s = fmaf(w2.y, x2.y, s);
+  s = fmaf(w3.x, x3.x, s);
+  s = fmaf(w3.y, x3.y, s);
+  return s;
+}
+
+// Pair p -> the two weight rows it reads.
+__device__ __forceinline__ void pair_rows(int epi, int p, int& r0, int& r1) {
+  if (epi == GEMV_QKV) {
+    const int head = p >> 6, i = p & 63;
+    r0 = head * 128 + i;
+    r1 = r0 + 64;
+  } else if (epi == GEMV_SWIGLU) {
+    const int blk = p >> 7, i = p & 127;
+    r0 = blk * 256 + i;
+    r1 = r0 + 128;
+  } else {
+    r0 = 2 * p;
+    r1 = 2 * p + 1;
+  }
+}
+
+}  // namespace
+
+template <int MR>
+__global__ void __launch_bounds__(kThreads)
+    gemv_kernel(GemvArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);  // [MR][K]
+  __shared__ float red[kWarps][MR];
+  __shared__ float s_bval[kWarps][MR];
+  __shared__ int s_bidx[kWarps][MR];
+  __shared__ int s_last;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = a.K;
+  const int M = a.M;
+
+  // ---- stage x (optionally RMS-normalised) into shared memory ----
+  if (a.norm_w == nullptr) {
+    for (int m = 0; m < M; ++m) {
+      const uint4* src = reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx);
+      uint4* dst = reinterpret_cast<uint4*>(xs + (size_t)m * K);
+      for (int c = tid; c < K / 8; c += kThreads) dst[c] = src[c];
+    }
+  } else {
+    float ss[MR];
+#pragma unroll
+    for (int m = 0; m < MR; ++m) ss[m] = 0.f;
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      if (m >= M) break;
+      const uint4* src = reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx);
+      for (int c = tid; c < K / 8; c += kThreads) {
+        const uint4 v = src[c];
+        const float2 f0 = unpack_bf16x2(v.x), f1 = unpack_bf16x2(v.y), f2 = unpack_bf16x2(v.z),
+                     f3 = unpack_bf16x2(v.w);
+        ss[m] += f0.x * f0.x + f0.y * f0.y + f1.x * f1.x + f1.y * f1.y + f2.x * f2.x +
+                 f2.y * f2.y + f3.x * f3.x + f3.y * f3.y;
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      const float v = warp_sum(ss[m]);
+      if (lane == 0) red[warp][m] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      if (m >= M) break;
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) tot += red[w][m];
+      const float r = rsqrtf(tot / (float)K + a.eps);
+      const uint4* src = reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx);
+      const uint4* wn = reinterpret_cast<const uint4*>(a.norm_w);
+      uint4* dst = reinterpret_cast<uint4*>(xs + (size_t)m * K);
+      for (int c = tid; c < K / 8; c += kThreads) {
+        const uint4 v = src[c], g = wn[c];
+        const uint32_t vi[4] = {v.x, v.y, v.z, v.w};
+        const uint32_t gi[4] = {g.x, g.y, g.z, g.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 xf = unpack_bf16x2(vi[q]), gf = unpack_bf16x2(gi[q]);
+          o[q] = pack_bf16x2(gf.x * bf16_round(xf.x * r), gf.y * bf16_round(xf.y * r));
+        }
+        dst[c] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+  __syncthreads();
+
+  const int n_pairs = a.N / 2;
+  const int nchunk = K / 8;
+  const uint4* xs4 = reinterpret_cast<const uint4*>(xs);
+  const int pos0 = (a.epi == GEMV_QKV) ? *a.pos : 0;
+
+  float best_v[MR];
+  int best_i[MR];
+#pragma unroll
+  for (int m = 0; m < MR; ++m) best_v[m] = -INFINITY, best_i[m] = 0x7fffffff;
+
+  for (int p = blockIdx.x * kWarps + warp; p < n_pairs; p += gridDim.x * kWarps) {
+    int r0, r1;
+    pair_rows(a.epi, p, r0, r1);
+    const uint4* w0 = reinterpret_cast<const uint4*>(a.w + (size_t)r0 * K);
+    const uint4* w1 = reinterpret_cast<const uint4*>(a.w + (size_t)r1 * K);
+    float acc0[MR], acc1[MR];
+#pragma unroll
+    for (int m = 0; m < MR; ++m) acc0[m] = acc1[m] = 0.f;
+    for (int c0 = lane; c0 < nchunk; c0 += 32 * kUnroll) {
+      uint4 wa[kUnroll], wb[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + u * 32;
+        if (c < nchunk) {
+          wa[u] = ld_stream_u4(w0 + c);
+          wb[u] = ld_stream_u4(w1 + c);
+        } else {
+          wa[u] = make_uint4(0, 0, 0, 0);
+          wb[u] = make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + u * 32;
+        if (c < nchunk) {
+#pragma unroll
+          for (int m = 0; m < MR; ++m) {
+            if (m < M) {
+              const uint4 xv = xs4[m * nchunk + c];
+              acc0[m] += dot8(wa[u], xv);
+              acc1[m] += dot8(wb[u], xv);
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      acc0[m] = warp_sum(acc0[m]);
+      acc1[m] = warp_sum(acc1[m]);
+    }
+    if (lane != 0) continue;
+    // ---- epilogue (lane 0) ----
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      if (m >= M) break;
+      const float v0 = acc0[m], v1 = acc1[m];
+      switch (a.epi) {
+        case GEMV_STORE:
+          a.out[(size_t)m * a.ldo + r0] = __float2bfloat16_rn(v0);
+          a.out[(size_t)m * a.ldo + r1] = __float2bfloat16_rn(v1);
+          break;
+        case GEMV_RESIDUAL: {
+          const float q0 = __bfloat162float(a.residual[(size_t)m * a.ldr + r0]);
+          const float q1 = __bfloat162float(a.residual[(size_t)m * a.ldr + r1]);
+          a.out[(size_t)m * a.ldo + r0] = __float2bfloat16_rn(q0 + bf16_round(v0));
+          a.out[(size_t)m * a.ldo + r1] = __float2bfloat16_rn(q1 + bf16_round(v1));
+          break;
+        }
+        case GEMV_SWIGLU: {
+          const float g = bf16_round(v0), u = bf16_round(v1);
+          a.out[(size_t)m * a.ldo + p] = __float2bfloat16_rn(bf16_round(silu_f(g)) * u);
+          break;
+        }
+        case GEMV_QKV: {
+          const int head = p >> 6, i = p & 63;
+          const int pos = pos0 + m;
+          float o0 = v0, o1 = v1;
+          const bool is_q = head < a.n_q_heads;
+          const bool is_k = !is_q && head < a.n_q_heads + a.n_kv_heads;
+          if (is_q || is_k) {
+            const float2 cs = a.rope_table[(size_t)pos * 64 + i];
+            o0 = v0 * cs.x - v1 * cs.y;
+            o1 = v1 * cs.x + v0 * cs.y;
+          }
+          __nv_bfloat16* dst;
+          if (is_q) {
+            dst = a.q_out + (size_t)m * a.ldq + head * 128;
+          } else {
+            const int kvh = is_k ? head - a.n_q_heads : head - a.n_q_heads - a.n_kv_heads;
+            dst = (is_k ? a.k_cache : a.v_cache) + ((size_t)kvh * a.cache_cap + pos) * 128;
+          }
+          dst[i] = __float2bfloat16_rn(o0);
+          dst[i + 64] = __float2bfloat16_rn(o1);
+          break;
+        }
+        case GEMV_ARGMAX: {
+          // argmax over bf16-rounded logits, first index on ties
+          const float b0 = bf16_round(v0), b1 = bf16_round(v1);
+          if (b0 > best_v[m] || (b0 == best_v[m] && r0 < best_i[m])) best_v[m] = b0, best_i[m] = r0;
+          if (b1 > best_v[m] || (b1 == best_v[m] && r1 < best_i[m])) best_v[m] = b1, best_i[m] = r1;
+          break;
+        }
+      }
+    }
+  }
+
+  if (a.epi != GEMV_ARGMAX) return;
+
+  // ---- argmax: CTA partials, then the last CTA reduces ----
+  if (lane == 0) {
+#pragma unroll
+    for (int m = 0; m < MR; ++m) s_bval[warp][m] = best_v[m], s_bidx[warp][m] = best_i[m];
+  }
+  __syncthreads();
+  if (tid < M) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int w = 0; w < kWarps; ++w) {
+      const float v = s_bval[w][tid];
+      const int i = s_bidx[w][tid];
+      if (v > bv || (v == bv && i < bi)) bv = v, bi = i;
+    }
+    a.part_val[(size_t)tid * gridDim.x + blockIdx.x] = bv;
+    a.part_idx[(size_t)tid * gridDim.x + blockIdx.x] = bi;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(a.counter, 1u);
+    s_last = (prev == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // Reduce partials of every row: warp m handles row m.
+  if (warp < M) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int b = lane; b < (int)gridDim.x; b += 32) {
+      const float v = __ldcg(a.part_val + (size_t)warp * gridDim.x + b);
+      const int i = __ldcg(a.part_idx + (size_t)warp * gridDim.x + b);
+      if (v > bv || (v == bv && i < bi)) bv = v, bi = i;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
+    }
+    if (lane == 0) {
+      a.out_token[warp] = bi;
+      s_bidx[0][warp] = bi;
+    }
+  }
+  __syncthreads();
+  const int last_tok = s_bidx[0][M - 1];
+  if (tid == 0) {
+    if (a.token_log != nullptr) {
+      const int n = *a.gen_count;
+      a.token_log[n] = last_tok;
+      *a.gen_count = n + 1;
+    }
+    if (a.pos_advance != nullptr) *a.pos_advance += M;
+    *a.counter = 0u;
+  }
+  if (a.embed != nullptr) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.embed + (size_t)last_tok * K);
+    uint4* dst = reinterpret_cast<uint4*>(a.next_hidden);
+    for (int c = tid; c < K / 8; c += kThreads) dst[c] = src[c];
+  }
+}
+
+cudaError_t gemv_bf16(const GemvArgs& a, cudaStream_t stream) {
+  if (a.M < 1 || a.M > 8 || (a.K % 8) != 0 || (a.N % 2) != 0) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)a.M * a.K * 2;
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  const int n_pairs = a.N / 2;
+  int grid = (n_pairs + kWarps - 1) / kWarps;
+  const int cap = (a.num_sms > 0 ? a.num_sms : 148) * 8;
+  if (grid > cap) grid = cap;
+#define SC_LAUNCH_GEMV(MRV)                                                              \
+  {                                                                                      \
+    cudaFuncSetAttribute(gemv_kernel<MRV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                         (int)smem);                                                     \
+    gemv_kernel<MRV><<<grid, kThreads, smem, stream>>>(a);                               \
+  }
+  if (a.M == 1) SC_LAUNCH_GEMV(1)
+  else if (a.M <= 2) SC_LAUNCH_GEMV(2)
+  else if (a.M <= 4) SC_LAUNCH_GEMV(4)
+  else SC_LAUNCH_GEMV(8)
+#undef SC_LAUNCH_GEMV
+  return cudaGetLastError();
+}
+
+}  // namespace sc

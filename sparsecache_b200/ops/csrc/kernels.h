@@ -1,0 +1,193 @@
+// Host-visible argument structs and launchers of the sm_100a kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sc {
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+bool make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                       uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
+                       bool swizzle128);
+
+// ---------------------------------------------------------------- GEMM ----
+enum Epi : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
+enum DevMode : int { DEV_KEY = 1, DEV_VALUE = 2, DEV_L1 = 4 };
+
+struct GemmEpilogue {
+  __nv_bfloat16* out;  // EPI_STORE / RESIDUAL / SWIGLU
+  int ldo;
+  const __nv_bfloat16* residual;  // EPI_RESIDUAL (may alias out)
+  int ldr;
+  // EPI_QKV
+  __nv_bfloat16* q_out;
+  int ldq;
+  __nv_bfloat16* k_cache;  // [n_kv_heads, cache_cap, 128]
+  __nv_bfloat16* v_cache;
+  int cache_cap;
+  const int* rope_pos;      // [M]
+  const int* cache_slot;    // [M]
+  const float2* rope_table; // [max_pos, 64] (cos, sin)
+  int n_q_heads;
+  int n_kv_heads;
+  float* dev_part;  // [M, 2 * n_kv_heads] or null
+  int dev_mode;
+};
+
+struct GemmArgs {
+  const __nv_bfloat16* a;  // [M, K], row stride lda
+  const __nv_bfloat16* b;  // [N, K], row stride ldb
+  int M, N, K, lda, ldb;
+  int epi;
+  int bn;  // 128 or 256
+  int num_sms;
+  GemmEpilogue ep;
+  int* status;
+};
+
+cudaError_t gemm_bf16_tc(const GemmArgs& g, cudaStream_t stream);
+
+// ---------------------------------------------------------------- GEMV ----
+// Small-M (1..8 rows) weight-streaming kernel for decode / verify.
+enum GemvEpi : int {
+  GEMV_STORE = 0,
+  GEMV_RESIDUAL = 1,
+  GEMV_SWIGLU = 2,
+  GEMV_QKV = 3,
+  GEMV_ARGMAX = 4
+};
+
+struct GemvArgs {
+  const __nv_bfloat16* w;  // [N, K]
+  const __nv_bfloat16* x;  // [M, K] (row stride ldx)
+  int ldx;
+  int M, N, K;
+  const __nv_bfloat16* norm_w;  // optional fused RMSNorm of x (weight [K])
+  float eps;
+  int epi;
+  __nv_bfloat16* out;  // STORE/RESIDUAL/SWIGLU: [M, ldo]
+  int ldo;
+  const __nv_bfloat16* residual;
+  int ldr;
+  // QKV
+  __nv_bfloat16* q_out;  // [M, n_q_heads*128]
+  int ldq;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  int cache_cap;
+  const int* pos;  // device scalar: position of row 0 (row m at pos + m)
+  const float2* rope_table;
+  int n_q_heads, n_kv_heads;
+  // ARGMAX (LM head)
+  float* part_val;     // [M, gridDim]
+  int* part_idx;       // [M, gridDim]
+  unsigned int* counter;  // one word, zero on entry, restored to zero
+  int* out_token;      // [M] argmax per row
+  int* token_log;      // optional: token_log[*gen_count] = token of row M-1
+  int* gen_count;      // device scalar advanced by one per call when token_log is set
+  const __nv_bfloat16* embed;  // optional: writes embed[token] of the last row to next_hidden
+  __nv_bfloat16* next_hidden;
+  int* pos_advance;    // optional device scalar incremented by M at the end
+  int num_sms;
+};
+
+cudaError_t gemv_bf16(const GemvArgs& a, cudaStream_t stream);
+
+// ----------------------------------------------------------- attention ----
+struct AttnPrefillArgs {
+  const __nv_bfloat16* q;  // [rows_total, n_heads*128] row stride ldq
+  int ldq;
+  const int* q_rows;  // optional gather of query rows
+  const int* qpos;    // [n_rows]
+  int n_rows;
+  const __nv_bfloat16* k_cache;  // [n_kv_heads, cache_cap, 128]
+  const __nv_bfloat16* v_cache;
+  int cache_cap;
+  const int* kpos;  // optional [n_keys], non-decreasing; null -> kpos[j] = j
+  int n_keys;
+  int n_heads, n_kv_heads, head_dim;
+  float scale;
+  __nv_bfloat16* out;  // [n_rows, n_heads*128]
+  int ldo;
+};
+
+cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream);
+
+struct AttnDecodeArgs {
+  const __nv_bfloat16* q;  // [M, n_heads*128]
+  int M;
+  const __nv_bfloat16* k_cache;
+  const __nv_bfloat16* v_cache;
+  int cache_cap;
+  const int* pos;  // device scalar: position of query row 0; row m sees keys [0, pos+m]
+  int n_heads, n_kv_heads;
+  float scale;
+  int splits;
+  float* part_o;     // [n_heads, M, splits, 128]
+  float* part_ml;    // [n_heads, M, splits, 2]
+  unsigned int* counters;  // [n_kv_heads], zero on entry, restored to zero
+  __nv_bfloat16* out;  // [M, n_heads*128]
+};
+
+cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream);
+
+// ------------------------------------------------------------ pointwise ----
+cudaError_t rmsnorm_bf16(const __nv_bfloat16* x, int ldx, const int* rows, const __nv_bfloat16* w,
+                         __nv_bfloat16* out, int ldo, int M, int D, float eps,
+                         cudaStream_t stream);
+cudaError_t embedding_bf16(const int* ids, const __nv_bfloat16* table, __nv_bfloat16* out, int M,
+                           int D, cudaStream_t stream);
+cudaError_t gather_rows_bf16(const __nv_bfloat16* in, int ldi, const int* rows,
+                             __nv_bfloat16* out, int ldo, int M, int D, cudaStream_t stream);
+
+// Relocate cached keys: rotate every key of [n_kv_heads, n_tokens, 128]
+// blocks from source to target positions (fp32 math, bf16 storage).
+struct ComposeDoc {
+  const __nv_bfloat16* src;  // [L, 2, n_kv_heads, n_tokens, 128] (device or mapped host)
+  int n_tokens;
+  int src_pos;   // RoPE position of the first source token
+  int dst_slot;  // first destination slot
+  int dst_pos;   // RoPE position of the first destination token
+};
+struct ComposeArgs {
+  const ComposeDoc* docs;  // device array
+  int n_docs;
+  const int* doc_token_offset;  // [n_docs + 1] prefix sum of n_tokens
+  int total_tokens;
+  int layer_begin, layer_end, n_layers;
+  __nv_bfloat16* cache;  // [L, 2, n_kv_heads, cache_cap, 128]
+  int cache_cap;
+  int n_kv_heads;
+  const float2* rope_table;
+};
+cudaError_t compose_relocate(const ComposeArgs& a, cudaStream_t stream);
+
+// CacheBlend selection: from deviation partials [T, 2*n_kv_heads] choose the
+// top ceil(ratio * n_doc) document rows in [doc_begin, doc_end), merge with
+// mandatory rows and emit the sorted active list.
+struct SelectArgs {
+  const float* dev_part;
+  int n_kv_heads;
+  int dev_mode;
+  int total_rows;   // T
+  int doc_begin, doc_end;
+  int k;            // number of document rows to select
+  int keep_prefix;  // keep [0, doc_begin) active
+  int* active;      // out [A]
+  int* n_active;    // out scalar
+  float* scores;    // scratch [T]
+  long long* checksum;  // optional out: sum over sorted selected doc positions * rank
+};
+cudaError_t cacheblend_select(const SelectArgs& a, cudaStream_t stream);
+
+cudaError_t fill_arange_i32(int* out, int n, int start, cudaStream_t stream);
+cudaError_t index_i32(const int* src, const int* idx, int* out, int n, cudaStream_t stream);
+
+}  // namespace sc

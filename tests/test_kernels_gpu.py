@@ -1,0 +1,345 @@
+"""Numerics of every sm_100a kernel against a plain PyTorch fp32 reference."""
+import math
+
+import pytest
+import torch
+
+from sparsecache_b200.config import get_model_config
+from sparsecache_b200.models.weights import interleave_gate_up
+from sparsecache_b200.rope import relocate_positions, rope_cos_sin, rope_table
+
+pytestmark = pytest.mark.gpu
+
+
+def _ext():
+    from sparsecache_b200 import ops
+
+    return ops.ext()
+
+
+def _status_ok(dev):
+    st = _ext().status(torch.empty(1, device=dev))
+    assert int(st.item()) == 0, f"kernel reported bounded-wait timeout {int(st.item())}"
+
+
+def _rel_err(out, ref):
+    return ((out.float() - ref).abs().max() / ref.abs().max().clamp_min(1e-6)).item()
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("mnk", [(1, 256, 64), (130, 512, 320), (300, 6144, 4096), (1000, 4096, 1024)])
+def test_gemm_store(cuda_device, bn, mnk):
+    M, N, K = mnk
+    g = torch.Generator(device="cpu").manual_seed(M + N + K)
+    a = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.05).to(cuda_device, torch.bfloat16)
+    out = torch.empty(M, N, device=cuda_device, dtype=torch.bfloat16)
+    _ext().gemm_store(a, w, out, bn)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    ref = a.float() @ w.float().T
+    assert _rel_err(out, ref) < 1e-2
+
+
+def test_gemm_residual_and_swiglu(cuda_device):
+    M, K, F = 257, 512, 1024
+    a = torch.randn(M, K, device=cuda_device).to(torch.bfloat16)
+    w = (torch.randn(K, K, device=cuda_device) * 0.05).to(torch.bfloat16)
+    res = torch.randn(M, K, device=cuda_device).to(torch.bfloat16)
+    out = res.clone()
+    _ext().gemm_residual(a, w, out, out, 256)  # in place
+    torch.cuda.synchronize()
+    ref = res.float() + (a.float() @ w.float().T).to(torch.bfloat16).float()
+    assert _rel_err(out, ref) < 1e-2
+
+    wg = (torch.randn(F, K, device=cuda_device) * 0.05).to(torch.bfloat16)
+    wu = (torch.randn(F, K, device=cuda_device) * 0.05).to(torch.bfloat16)
+    wgu = interleave_gate_up(wg, wu)
+    act = torch.empty(M, F, device=cuda_device, dtype=torch.bfloat16)
+    _ext().gemm_swiglu(a, wgu, act, 256)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    gate = (a.float() @ wg.float().T).to(torch.bfloat16)
+    up = (a.float() @ wu.float().T).to(torch.bfloat16)
+    ref = torch.nn.functional.silu(gate.float()).to(torch.bfloat16).float() * up.float()
+    assert _rel_err(act, ref) < 2e-2
+
+
+def _qkv_reference(a, w, cfg, pos, nq, nkv):
+    y = a.float() @ w.float().T
+    D = 128
+    q = y[:, : nq * D].reshape(-1, nq, D)
+    k = y[:, nq * D : (nq + nkv) * D].reshape(-1, nkv, D)
+    v = y[:, (nq + nkv) * D :].reshape(-1, nkv, D)
+    cos, sin = rope_cos_sin(cfg, pos.cpu(), device=a.device)
+    cos, sin = cos[:, None, :], sin[:, None, :]
+
+    def rot(x):
+        return torch.cat((-x[..., 64:], x[..., :64]), dim=-1)
+
+    return q * cos + rot(q) * sin, k * cos + rot(k) * sin, v
+
+
+@pytest.mark.parametrize("dev_mode", [0, 1, 2, 3, 6])
+def test_gemm_qkv_rope_scatter_deviation(cuda_device, dev_mode):
+    cfg = get_model_config("tiny128")
+    nq, nkv, K, M, cap = 4, 2, 512, 200, 600
+    a = torch.randn(M, K, device=cuda_device).to(torch.bfloat16)
+    w = (torch.randn((nq + 2 * nkv) * 128, K, device=cuda_device) * 0.05).to(torch.bfloat16)
+    pos = torch.sort(torch.randperm(500)[:M]).values.to(torch.int32).to(cuda_device) + 7
+    slot = torch.sort(torch.randperm(cap)[:M]).values.to(torch.int32).to(cuda_device)
+    kc = torch.randn(nkv, cap, 128, device=cuda_device).to(torch.bfloat16)
+    vc = torch.randn(nkv, cap, 128, device=cuda_device).to(torch.bfloat16)
+    kc0, vc0 = kc.clone(), vc.clone()
+    q_out = torch.empty(M, nq * 128, device=cuda_device, dtype=torch.bfloat16)
+    table = rope_table(cfg, 1024, cuda_device)
+    dev = torch.zeros(M, 2 * nkv, device=cuda_device) if dev_mode else None
+    _ext().gemm_qkv(a, w, q_out, kc, vc, pos, slot, table, nq, nkv, dev, dev_mode, 256)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    q, k, v = _qkv_reference(a, w, cfg, pos, nq, nkv)
+    assert _rel_err(q_out.reshape(M, nq, 128), q) < 1e-2
+    sl = slot.long()
+    assert _rel_err(kc[:, sl].transpose(0, 1), k) < 1e-2
+    assert _rel_err(vc[:, sl].transpose(0, 1), v) < 1e-2
+    untouched = torch.ones(cap, dtype=torch.bool, device=cuda_device)
+    untouched[sl] = False
+    assert torch.equal(kc[:, untouched], kc0[:, untouched])
+    if dev_mode:
+        kb = k.to(torch.bfloat16).float()
+        vb = v.to(torch.bfloat16).float()
+        dk = kb - kc0[:, sl].transpose(0, 1).float()
+        dv = vb - vc0[:, sl].transpose(0, 1).float()
+        f = (lambda x: x.abs()) if dev_mode & 4 else (lambda x: x.square())
+        if dev_mode & 1:
+            torch.testing.assert_close(dev[:, :nkv], f(dk).sum(-1), rtol=2e-2, atol=1e-1)
+        if dev_mode & 2:
+            torch.testing.assert_close(dev[:, nkv:], f(dv).sum(-1), rtol=2e-2, atol=1e-1)
+
+
+def _attn_reference(q, kc, vc, qpos, kpos, n_heads):
+    # q [R, H*128]; kc [Hkv, n, 128]
+    R = q.shape[0]
+    Hkv = kc.shape[0]
+    G = n_heads // Hkv
+    qh = q.float().reshape(R, n_heads, 128).transpose(0, 1)  # [H, R, D]
+    k = kc.float().repeat_interleave(G, dim=0)
+    v = vc.float().repeat_interleave(G, dim=0)
+    s = qh @ k.transpose(1, 2) / math.sqrt(128)
+    mask = kpos[None, :] <= qpos[:, None]
+    s = s.masked_fill(~mask[None], float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    return (p @ v).transpose(0, 1).reshape(R, n_heads * 128)
+
+
+@pytest.mark.parametrize("case", ["causal", "selective", "staged"])
+def test_attention_prefill(cuda_device, case):
+    H, Hkv, T = 8, 2, 777
+    cap = 1000
+    kc = torch.randn(Hkv, cap, 128, device=cuda_device).to(torch.bfloat16)
+    vc = torch.randn(Hkv, cap, 128, device=cuda_device).to(torch.bfloat16)
+    kpos = torch.arange(T, device=cuda_device, dtype=torch.int32)
+    if case == "causal":
+        rows = torch.arange(T, device=cuda_device, dtype=torch.int32)
+        qpos = kpos.clone()
+    else:
+        rows = torch.sort(torch.randperm(T)[:150]).values.to(torch.int32).to(cuda_device)
+        qpos = kpos[rows.long()]
+        if case == "staged":  # suffix placed at a later global position
+            kpos = kpos.clone()
+            kpos[-40:] += 300
+            qpos = kpos[rows.long()]
+    qfull = torch.randn(T, H * 128, device=cuda_device).to(torch.bfloat16)
+    out = torch.empty(rows.numel(), H * 128, device=cuda_device, dtype=torch.bfloat16)
+    _ext().attention_prefill(
+        qfull, rows, qpos, kc, vc, kpos if case == "staged" else None, T, H, 1 / math.sqrt(128), out
+    )
+    torch.cuda.synchronize()
+    ref = _attn_reference(qfull[rows.long()], kc[:, :T], vc[:, :T], qpos.long(), kpos.long(), H)
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("M", [1, 5])
+def test_attention_decode(cuda_device, M):
+    H, Hkv, cap = 8, 2, 1200
+    pos0 = 913
+    kc = torch.randn(Hkv, cap, 128, device=cuda_device).to(torch.bfloat16)
+    vc = torch.randn(Hkv, cap, 128, device=cuda_device).to(torch.bfloat16)
+    q = torch.randn(M, H * 128, device=cuda_device).to(torch.bfloat16)
+    pos = torch.tensor([pos0], device=cuda_device, dtype=torch.int32)
+    splits = 16
+    part_o = torch.empty(H * M * splits * 128, device=cuda_device)
+    part_ml = torch.empty(H * M * splits * 2, device=cuda_device)
+    counters = torch.zeros(Hkv, device=cuda_device, dtype=torch.int32)
+    out = torch.empty(M, H * 128, device=cuda_device, dtype=torch.bfloat16)
+    for _ in range(2):  # second call checks the counters were reset
+        _ext().attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), splits, part_o, part_ml, counters, out)
+    torch.cuda.synchronize()
+    n = pos0 + M
+    kpos = torch.arange(n, device=cuda_device)
+    qpos = pos0 + torch.arange(M, device=cuda_device)
+    ref = _attn_reference(q, kc[:, :n], vc[:, :n], qpos, kpos, H)
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+    assert int(counters.abs().sum()) == 0
+
+
+def _rms_ref(x, w, eps):
+    xf = x.float()
+    r = torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps)
+    return (w.float() * (xf * r).to(torch.bfloat16).float())
+
+
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_gemv_variants(cuda_device, M):
+    K, N = 1024, 768
+    eps = 1e-5
+    x = torch.randn(M, K, device=cuda_device).to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(K, device=cuda_device)).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda_device) * 0.05).to(torch.bfloat16)
+    ext = _ext()
+    out = torch.empty(M, N, device=cuda_device, dtype=torch.bfloat16)
+    ext.gemv_store(x, w, nw, eps, out)
+    torch.cuda.synchronize()
+    xn = _rms_ref(x, nw, eps).to(torch.bfloat16).float()
+    assert _rel_err(out, xn @ w.float().T) < 1e-2
+
+    res = torch.randn(M, N, device=cuda_device).to(torch.bfloat16)
+    out2 = res.clone()
+    ext.gemv_residual(x, w, None, eps, out2, out2)
+    torch.cuda.synchronize()
+    ref = res.float() + (x.float() @ w.float().T).to(torch.bfloat16).float()
+    assert _rel_err(out2, ref) < 1e-2
+
+    F = 512
+    wg = (torch.randn(F, K, device=cuda_device) * 0.05).to(torch.bfloat16)
+    wu = (torch.randn(F, K, device=cuda_device) * 0.05).to(torch.bfloat16)
+    act = torch.empty(M, F, device=cuda_device, dtype=torch.bfloat16)
+    ext.gemv_swiglu(x, interleave_gate_up(wg, wu), None, eps, act)
+    torch.cuda.synchronize()
+    g = (x.float() @ wg.float().T).to(torch.bfloat16).float()
+    u = (x.float() @ wu.float().T).to(torch.bfloat16).float()
+    ref = torch.nn.functional.silu(g).to(torch.bfloat16).float() * u
+    assert _rel_err(act, ref) < 2e-2
+
+
+def test_gemv_qkv_and_argmax(cuda_device):
+    cfg = get_model_config("tiny128")
+    nq, nkv, K, cap, V = 4, 2, 512, 300, 4096
+    ext = _ext()
+    x = torch.randn(1, K, device=cuda_device).to(torch.bfloat16)
+    w = (torch.randn((nq + 2 * nkv) * 128, K, device=cuda_device) * 0.05).to(torch.bfloat16)
+    kc = torch.zeros(nkv, cap, 128, device=cuda_device, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    q_out = torch.empty(1, nq * 128, device=cuda_device, dtype=torch.bfloat16)
+    pos = torch.tensor([123], device=cuda_device, dtype=torch.int32)
+    table = rope_table(cfg, 1024, cuda_device)
+    ext.gemv_qkv(x, w, None, 1e-5, q_out, kc, vc, pos, table, nq, nkv)
+    torch.cuda.synchronize()
+    q, k, v = _qkv_reference(x, w, cfg, pos, nq, nkv)
+    assert _rel_err(q_out.reshape(1, nq, 128), q) < 1e-2
+    assert _rel_err(kc[:, 123].unsqueeze(0), k) < 1e-2
+    assert _rel_err(vc[:, 123].unsqueeze(0), v) < 1e-2
+
+    lm = (torch.randn(V, K, device=cuda_device) * 0.05).to(torch.bfloat16)
+    emb = torch.randn(V, K, device=cuda_device).to(torch.bfloat16)
+    grid = ext.gemv_argmax_grid(V)
+    pv = torch.empty(8 * grid, device=cuda_device)
+    pi = torch.empty(8 * grid, device=cuda_device, dtype=torch.int32)
+    counter = torch.zeros(1, device=cuda_device, dtype=torch.int32)
+    tok = torch.empty(3, device=cuda_device, dtype=torch.int32)
+    log = torch.zeros(4, device=cuda_device, dtype=torch.int32)
+    gen = torch.zeros(1, device=cuda_device, dtype=torch.int32)
+    nxt = torch.empty(1, K, device=cuda_device, dtype=torch.bfloat16)
+    pos2 = torch.tensor([10], device=cuda_device, dtype=torch.int32)
+    xs = torch.randn(3, K, device=cuda_device).to(torch.bfloat16)
+    ext.gemv_argmax(xs, lm, None, 1e-5, pv, pi, counter, tok, log, gen, emb, nxt, pos2)
+    torch.cuda.synchronize()
+    logits = (xs.float() @ lm.float().T)
+    top2 = logits.topk(2, dim=-1)
+    for m in range(3):
+        if (top2.values[m, 0] - top2.values[m, 1]) > 1e-2:
+            assert int(tok[m]) == int(top2.indices[m, 0])
+    assert int(gen.item()) == 1 and int(log[0]) == int(tok[2])
+    assert int(pos2.item()) == 13
+    assert int(counter.item()) == 0
+    assert torch.equal(nxt[0], emb[int(tok[2])])
+
+
+def test_rmsnorm_embedding_gather(cuda_device):
+    ext = _ext()
+    V, D = 1000, 512
+    table = torch.randn(V, D, device=cuda_device).to(torch.bfloat16)
+    ids = torch.randint(0, V, (77,), device=cuda_device, dtype=torch.int32)
+    h = torch.empty(77, D, device=cuda_device, dtype=torch.bfloat16)
+    ext.embedding(ids, table, h)
+    assert torch.equal(h, table[ids.long()])
+    w = (1 + 0.1 * torch.randn(D, device=cuda_device)).to(torch.bfloat16)
+    rows = torch.tensor([5, 0, 76], device=cuda_device, dtype=torch.int32)
+    out = torch.empty(3, D, device=cuda_device, dtype=torch.bfloat16)
+    ext.rmsnorm(h, rows, w, 1e-5, out)
+    torch.cuda.synchronize()
+    ref = _rms_ref(h[rows.long()], w, 1e-5)
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2)
+    g = torch.empty(3, D, device=cuda_device, dtype=torch.bfloat16)
+    ext.gather_rows(h, rows, g)
+    assert torch.equal(g, h[rows.long()])
+
+
+@pytest.mark.parametrize("host_source", [False, True])
+def test_compose_relocate(cuda_device, host_source):
+    cfg = get_model_config("tiny128")
+    L, Hkv, cap = 3, 2, 900
+    lens = [37, 120, 64, 5]
+    docs = []
+    for n in lens:
+        t = torch.randn(L, 2, Hkv, n, 128).to(torch.bfloat16)
+        docs.append(t.pin_memory() if host_source else t.to(cuda_device))
+    cache = torch.zeros(L, 2, Hkv, cap, 128, device=cuda_device, dtype=torch.bfloat16)
+    table = rope_table(cfg, 2048, cuda_device)
+    rows, offs, cursor = [], [0], 50
+    for t, n in zip(docs, lens):
+        ptr = t.data_ptr()
+        rows.append([ptr & 0xFFFFFFFF, ptr >> 32, n, 0, cursor, cursor])
+        offs.append(offs[-1] + n)
+        cursor += n
+    doc_t = torch.tensor(rows, dtype=torch.int64)
+    doc_t = torch.where(doc_t >= 2**31, doc_t - 2**32, doc_t).to(torch.int32).to(cuda_device)
+    off_t = torch.tensor(offs, dtype=torch.int32, device=cuda_device)
+    _ext().compose_relocate(doc_t, off_t, offs[-1], 0, L, L, cache, Hkv, table)
+    torch.cuda.synchronize()
+    cursor = 50
+    for t, n in zip(docs, lens):
+        src = t.to(cuda_device)
+        for layer in range(L):
+            k = src[layer, 0].unsqueeze(0)
+            ref_k = relocate_positions(cfg, k, torch.arange(n), torch.arange(cursor, cursor + n))[0]
+            got_k = cache[layer, 0, :, cursor : cursor + n]
+            torch.testing.assert_close(got_k.float(), ref_k.float(), rtol=1e-2, atol=2e-2)
+            assert torch.equal(cache[layer, 1, :, cursor : cursor + n], src[layer, 1])
+        cursor += n
+
+
+@pytest.mark.parametrize("keep_prefix", [True, False])
+def test_cacheblend_select(cuda_device, keep_prefix):
+    ext = _ext()
+    T, nkv, doc_begin, doc_end = 3000, 8, 32, 2950
+    dev = torch.rand(T, 2 * nkv, device=cuda_device)
+    n_doc = doc_end - doc_begin
+    k = math.ceil(0.15 * n_doc)
+    active = torch.empty(T, device=cuda_device, dtype=torch.int32)
+    n_active = torch.empty(1, device=cuda_device, dtype=torch.int32)
+    scores = torch.empty(T, device=cuda_device)
+    ck = torch.zeros(1, device=cuda_device, dtype=torch.int64)
+    ext.cacheblend_select(dev, nkv, 2, T, doc_begin, doc_end, k, keep_prefix, active, n_active, scores, ck)
+    torch.cuda.synchronize()
+    s = dev[doc_begin:doc_end, nkv:].sum(-1)
+    sel = torch.topk(s, k).indices + doc_begin
+    parts = [sel, torch.arange(doc_end, T, device=cuda_device)]
+    if keep_prefix:
+        parts.insert(0, torch.arange(0, doc_begin, device=cuda_device))
+    expect = torch.cat(parts).sort().values
+    n = int(n_active.item())
+    assert n == expect.numel()
+    assert torch.equal(active[:n].long(), expect)
+    ss = sel.sort().values
+    assert int(ck.item()) == int((ss * torch.arange(1, k + 1, device=cuda_device)).sum())
