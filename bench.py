@@ -1,0 +1,419 @@
+"""Headline benchmark: 10-document RAG reuse serving on Llama-3.1-8B-architecture models.
+
+Workload (synthetic, seeded): 150 requests x 10 documents (1,255 unique
+sequences, 245 exact repeats), document lengths ~N(160, 50) clipped to
+[40, 400], system prefix 32, question ~U[12, 40]; random-init BF16
+Llama-3.1-8B architecture.  Each step serves ONE request per GPU through the
+public serving call: compose the request's reused document KV (RoPE
+re-rotated), CacheBlend repair (ratio 0.15, check layer 1, value deviation,
+system+question rows mandatory), 24 greedy tokens.  Data parallel: one
+process per GPU, requests sharded by index; every number is device-timed
+with CUDA events and reduced as the max over ranks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0.  ``value`` = generated tokens per second of
+the whole job (all GPUs); TTFT p50/p99 are reported alongside.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PUBLISHED_CB15_TTFT_MS = 76.9  # reference README: CacheBlend 15%, 1x H200 (no tokens/s is published)
+METRIC = "p50/p99 TTFT and decode tokens/s, 8B/70B 10-doc RAG reuse, 1/2/4/8 B200"
+
+
+# --------------------------------------------------------------------- infra
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def reduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def reduce_sum(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def gather_list(values: list[float], world: int) -> list[float]:
+    if world == 1:
+        return list(values)
+    import torch.distributed as dist
+
+    out = [None] * world
+    dist.all_gather_object(out, list(values))
+    return [v for part in out for v in part]
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples taken during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"sc_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait(timeout=5)
+        self.out.close()
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def percentile(xs, q):
+    if not xs:
+        return None
+    xs = sorted(xs)
+    k = (len(xs) - 1) * q
+    f, c = math.floor(k), math.ceil(k)
+    return xs[f] if f == c else xs[f] + (xs[c] - xs[f]) * (k - f)
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args, world, rank, local):
+    sys.path.insert(0, ROOT)
+    from sparsecache_b200.config import CacheBlendConfig, get_model_config
+    from sparsecache_b200.models.engine import B200Engine
+    from sparsecache_b200.serving.server import RAGServer
+    from sparsecache_b200.store import DocumentKVStore
+    from sparsecache_b200.synthetic import make_requests, workload_summary
+
+    cfg = get_model_config(args.model)
+    dev = torch.device("cuda", local)
+    requests = make_requests("llama8b_rag", cfg)
+    mine = [r for r in requests if r.index % world == rank]
+    need = args.warmup + args.steps
+    served = [mine[i % len(mine)] for i in range(need)]
+    engine = B200Engine.random(cfg, seed=0, device=dev)
+    blend = CacheBlendConfig(check_layer=1, recompute_ratio=args.ratio, deviation_metric="value",
+                             keep_prefix=True, max_new_tokens=args.new_tokens)
+    capacity = max(r.prompt_tokens for r in mine) + args.new_tokens + 64
+    store = DocumentKVStore(cfg, tier="hbm", device=dev)
+    server = RAGServer(engine, store, capacity=capacity, blend=blend)
+    prod = server.produce(mine)
+    torch.cuda.synchronize()
+
+    # ---------------- device-timed region ----------------
+    for r in served[: args.warmup]:
+        server.serve(r, sync=True)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    sampler.start()
+    launches0 = engine.ext.launches
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    handles = [server.serve(r) for r in served[args.warmup:]]
+    t1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop()
+    launches = engine.ext.launches - launches0
+    elapsed_ms = t0.elapsed_time(t1)
+    results = [h.result() for h in handles]
+    my_tokens = sum(args.new_tokens for _ in results)  # device always produces max_new tokens
+    ttfts = gather_list([r.ttft_ms for r in results], world)
+    resp = gather_list([r.response_ms for r in results], world)
+    max_ms = reduce_max(elapsed_ms, world)
+    tokens = reduce_sum(my_tokens, world)
+    value = tokens / (max_ms / 1000.0)
+
+    # ---------------- end-to-end through the public API ----------------
+    # Documents served from the PINNED host tier (composer reads them over
+    # PCIe), prompt ids copied H2D from pinned memory and the generated ids
+    # read back D2H, every step, host-synchronised per request.
+    e2e_reqs = served[args.warmup:]
+    pinned = DocumentKVStore(cfg, tier="pinned")
+    for r in e2e_reqs:
+        for d in r.documents:
+            if d not in pinned:
+                pinned.put(d, store[d].kv)
+    ids_host = [torch.tensor(r.prompt, dtype=torch.int32).pin_memory() for r in e2e_reqs]
+    for r, ih in zip(e2e_reqs[: args.warmup], ids_host):
+        server.serve(r, ids_host=ih, store=pinned, sync=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    e2e_results = [server.serve(r, ids_host=ih, store=pinned, sync=True) for r, ih in zip(e2e_reqs, ids_host)]
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - w0
+    e2e_s = reduce_max(e2e_s, world)
+    e2e_value = reduce_sum(args.new_tokens * len(e2e_results), world) / e2e_s
+    kv_bytes = [sum(pinned[d].kv[blend.check_layer:].numel() * 2 for d in r.documents) for r in e2e_reqs]
+    h2d = statistics.mean(kv_bytes) + statistics.mean(ih.numel() * 4 for ih in ids_host)
+    e2e_ttft = gather_list([r.ttft_ms for r in e2e_results], world)
+
+    summary = workload_summary(requests)
+    out = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "generated tokens/s (all GPUs)",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": max_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded token ids; random-init weights)",
+        "ttft_p50_ms": percentile(ttfts, 0.5),
+        "ttft_p99_ms": percentile(ttfts, 0.99),
+        "response_p50_ms": percentile(resp, 0.5),
+        "tpot_ms": statistics.mean((r - t) / (args.new_tokens - 1) for r, t in zip(resp, ttfts)),
+        "ttft_vs_published_h200_cb15": PUBLISHED_CB15_TTFT_MS / percentile(ttfts, 0.5),
+        "e2e": {"value": e2e_value, "unit": "generated tokens/s (all GPUs)",
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4 * args.new_tokens,
+                "ttft_p50_ms": percentile(e2e_ttft, 0.5), "ttft_p99_ms": percentile(e2e_ttft, 0.99),
+                "store_tier": "pinned host (composer reads over PCIe)"},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+        "config": {
+            "model": f"{args.model} (random init)",
+            "global_batch": world,
+            "seq_len": round(summary["mean_prompt_tokens"]),
+            "parallelism": f"dp{world}",
+            "workload": summary,
+            "cacheblend": {"ratio": args.ratio, "check_layer": 1, "deviation": "value", "mandatory": "system+question"},
+            "new_tokens": args.new_tokens,
+            "store_tier": "hbm",
+            "producer": prod,
+            "l2": "inputs larger than L2: every step streams the 16 GB of weights",
+        },
+    }
+    return out
+
+
+# ------------------------------------------------------------ reference arm
+def _install_cache_shims():
+    """The reference pins transformers<5; the image has 5.x, which dropped the two
+    legacy-cache conversions the reference's stock code calls.  Supply them
+    (on the library, not on the reference) so its unmodified code path runs."""
+    from transformers.cache_utils import DynamicCache
+
+    if not hasattr(DynamicCache, "from_legacy_cache"):
+        def from_legacy_cache(cls, past):
+            cache = cls()
+            for i, (k, v) in enumerate(past):
+                cache.update(k, v, i)
+            return cache
+
+        DynamicCache.from_legacy_cache = classmethod(from_legacy_cache)
+    if not hasattr(DynamicCache, "to_legacy_cache"):
+        DynamicCache.to_legacy_cache = lambda self: tuple((l.keys, l.values) for l in self.layers)
+
+
+def run_reference(args, world, rank, local):
+    ref_root = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "sparsecache")):
+        return {"impl": "reference", "unavailable": "baseline/_ref is not installed"}
+    sys.path.insert(0, ref_root)
+    sys.path.insert(1, ROOT)
+    _install_cache_shims()
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from sparsecache.modeling import cacheblend_generate  # the reference's public API
+    from sparsecache.rope import relocate_key
+    from sparsecache_b200.config import get_model_config
+    from sparsecache_b200.synthetic import make_requests, workload_summary
+
+    cfg = get_model_config(args.model)
+    dev = torch.device("cuda", local)
+    hf_cfg = LlamaConfig(
+        vocab_size=cfg.vocab, hidden_size=cfg.d_model, intermediate_size=cfg.ffn, num_hidden_layers=cfg.n_layers,
+        num_attention_heads=cfg.n_heads, num_key_value_heads=cfg.n_kv_heads, head_dim=cfg.head_dim,
+        rms_norm_eps=cfg.rms_eps, rope_theta=cfg.rope_theta, max_position_embeddings=131072,
+        rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                      "original_max_position_embeddings": 8192},
+        attn_implementation="sdpa", tie_word_embeddings=False)
+    torch.manual_seed(0)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(dev):
+        model = LlamaForCausalLM(hf_cfg)
+    torch.set_default_dtype(prev)
+    model.eval()
+    requests = make_requests("llama8b_rag", cfg)
+    mine = [r for r in requests if r.index % world == rank]
+    need = args.warmup + args.steps
+    served = [mine[i % len(mine)] for i in range(need)]
+
+    @torch.inference_mode()
+    def local_kv(ids):
+        out = model(input_ids=torch.tensor([ids], device=dev), use_cache=True)
+        return tuple((k.cpu(), v.cpu()) for k, v in out.past_key_values.to_legacy_cache())
+
+    doc_cache = {}
+    prefix_caches = []
+    for r in served:
+        system = local_kv(r.prefix)
+        keys = [[k] for k, _ in system]
+        values = [[v] for _, v in system]
+        cursor = len(r.prefix)
+        for d in r.documents:
+            if d not in doc_cache:
+                doc_cache[d] = local_kv(d)
+            for i, (k, v) in enumerate(doc_cache[d]):
+                keys[i].append(relocate_key(model, k, source_start=0, target_start=cursor))
+                values[i].append(v)
+            cursor += len(d)
+        prefix_caches.append(tuple((torch.cat(keys[i], 2), torch.cat(values[i], 2)) for i in range(cfg.n_layers)))
+    eos = set(cfg.eos_token_ids)
+
+    def call(r, pc):
+        return cacheblend_generate(model, full_ids=r.prompt, prefix_cache=pc, system_tokens=len(r.prefix),
+                                   suffix_tokens=len(r.suffix), check_layer=1, recompute_ratio=args.ratio,
+                                   max_new_tokens=args.new_tokens, eos_token_ids=eos)
+
+    for r, pc in zip(served[: args.warmup], prefix_caches):
+        call(r, pc)
+    sampler = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    sampler.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    results = [call(r, pc) for r, pc in zip(served[args.warmup:], prefix_caches[args.warmup:])]
+    t1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop()
+    elapsed_ms = t0.elapsed_time(t1)
+    my_tokens = sum(len(x.token_ids) for x in results)
+    ttfts = gather_list([x.prefill_ms + x.metadata.get("prefix_h2d_ms", 0.0) for x in results], world)
+    max_ms = reduce_max(elapsed_ms, world)
+    tokens = reduce_sum(my_tokens, world)
+    value = tokens / (max_ms / 1000.0)
+    summary = workload_summary(requests)
+    h2d = statistics.mean(sum((k.numel() + v.numel()) * 2 for k, v in pc) for pc in prefix_caches[args.warmup:])
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "generated tokens/s (all GPUs)",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": max_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded token ids; random-init weights)",
+        "ttft_p50_ms": percentile(ttfts, 0.5),
+        "ttft_p99_ms": percentile(ttfts, 0.99),
+        "e2e": {"value": value, "unit": "generated tokens/s (all GPUs)", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": 8 * args.new_tokens,
+                "note": "the reference API call is end to end (pageable H2D of the composed cache inside)"},
+        "gpu_launches": None,
+        "clocks": clocks,
+        "config": {"model": f"{args.model} (random init, HF LlamaForCausalLM sdpa)", "global_batch": world,
+                   "seq_len": round(summary["mean_prompt_tokens"]), "parallelism": f"dp{world}",
+                   "api": "sparsecache.modeling.cacheblend_generate (key deviation, suffix mandatory)",
+                   "ratio": args.ratio, "check_layer": 1, "new_tokens": args.new_tokens,
+                   "l2": "inputs larger than L2: every step streams the 16 GB of weights"},
+    }
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--model", default="llama3-8b")
+    p.add_argument("--ratio", type=float, default=0.15)
+    p.add_argument("--new-tokens", type=int, default=24)
+    args = p.parse_args()
+    if args.warmup < 3:
+        p.error("at least 3 warm-up steps")
+    world, rank, local = dist_setup()
+    if world != args.gpus and rank == 0:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    try:
+        out = run_ours(args, world, rank, local) if args.impl == "ours" else run_reference(args, world, rank, local)
+    finally:
+        pass
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,452 @@
+"""B200 inference engine: a Llama decoder driven entirely by the sm_100a kernels.
+
+Data layout (chosen for the kernels, not translated from the reference):
+  * weights: one fused QKV matrix, gate/up interleaved in 128-row blocks,
+    bf16, contiguous, resident in HBM (weights.py);
+  * KV cache: one contiguous [L, 2, H_kv, capacity, 128] bf16 buffer per
+    serving slot.  Slots are positions, so a composed document cache, the
+    CacheBlend scatter and the decode append all address the same buffer
+    and the decode CUDA graph can be captured once per slot;
+  * RoPE: one fp32 (cos, sin) table indexed by position, shared by the QKV
+    epilogue, the decode GEMV and the composer.
+
+Passes:
+  * ``prefill``         full causal prefill (also the document producer and
+                        the direct-reuse suffix prefill);
+  * ``cacheblend``      the CacheBlend selective recompute (layers < check:
+                        all rows; check layer: fused deviation epilogue +
+                        radix top-k select; later layers: active rows only,
+                        fresh K/V scattered in the QKV epilogue);
+  * ``decode``          greedy decode, one CUDA graph per step: 5 launches
+                        per layer plus the fused LM-head/argmax/embedding
+                        feedback kernel.  The position, the token and the
+                        token log live on the device; the host reads the
+                        tokens once at the end.
+Reference behaviour: modeling.py:33-417, reuse_cacheblend_pipeline.py:322-893.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .. import ops
+from ..config import CacheBlendConfig, ModelConfig
+from ..rope import rope_table
+from .weights import fuse_qkv, interleave_gate_up
+
+
+@dataclass
+class LayerWeights:
+    ln1: torch.Tensor
+    w_qkv: torch.Tensor
+    w_o: torch.Tensor
+    ln2: torch.Tensor
+    w_gu: torch.Tensor
+    w_down: torch.Tensor
+
+
+@dataclass
+class EngineWeights:
+    embed: torch.Tensor
+    layers: list[LayerWeights]
+    norm: torch.Tensor
+    lm_head: torch.Tensor
+
+    @staticmethod
+    def random(config: ModelConfig, *, seed: int, device, std: float = 0.02) -> "EngineWeights":
+        """Seeded random bf16 weights generated directly on the device."""
+        gen = torch.Generator(device=device).manual_seed(seed)
+        bf = torch.bfloat16
+
+        def mat(rows, cols):
+            w = torch.empty(rows, cols, device=device, dtype=bf)
+            w.normal_(0.0, std, generator=gen)
+            return w
+
+        def ones(n):
+            return torch.ones(n, device=device, dtype=bf)
+
+        d, f = config.d_model, config.ffn
+        layers = [
+            LayerWeights(
+                ln1=ones(d),
+                w_qkv=mat(config.qkv_rows, d),
+                w_o=mat(d, config.q_size),
+                ln2=ones(d),
+                w_gu=mat(2 * f, d),
+                w_down=mat(d, f),
+            )
+            for _ in range(config.n_layers)
+        ]
+        return EngineWeights(embed=mat(config.vocab, d), layers=layers, norm=ones(d), lm_head=mat(config.vocab, d))
+
+    @staticmethod
+    def from_oracle(model, device) -> "EngineWeights":
+        """Convert a LlamaOracle's parameters into the kernel layout (bf16)."""
+        bf = torch.bfloat16
+
+        def t(x):
+            return x.detach().to(device=device, dtype=bf).contiguous()
+
+        layers = []
+        for layer in model.layers:
+            layers.append(
+                LayerWeights(
+                    ln1=t(layer.input_layernorm.weight),
+                    w_qkv=t(fuse_qkv(layer.q_proj.weight, layer.k_proj.weight, layer.v_proj.weight)),
+                    w_o=t(layer.o_proj.weight),
+                    ln2=t(layer.post_attention_layernorm.weight),
+                    w_gu=t(interleave_gate_up(layer.gate_proj.weight, layer.up_proj.weight)),
+                    w_down=t(layer.down_proj.weight),
+                )
+            )
+        return EngineWeights(
+            embed=t(model.embed_tokens.weight), layers=layers, norm=t(model.norm.weight), lm_head=t(model.lm_head.weight)
+        )
+
+
+class KVSlot:
+    """A serving slot: one contiguous KV buffer of fixed capacity."""
+
+    def __init__(self, config: ModelConfig, capacity: int, device) -> None:
+        self.capacity = int(capacity)
+        self.data = torch.empty(
+            config.n_layers, 2, config.n_kv_heads, self.capacity, config.head_dim, device=device, dtype=torch.bfloat16
+        )
+
+    def k(self, layer: int) -> torch.Tensor:
+        return self.data[layer, 0]
+
+    def v(self, layer: int) -> torch.Tensor:
+        return self.data[layer, 1]
+
+    def nbytes(self) -> int:
+        return self.data.numel() * 2
+
+
+class _Workspace:
+    """Grow-only device scratch buffers, reused across calls (no per-call allocation)."""
+
+    def __init__(self, device) -> None:
+        self.device = device
+        self.bufs: dict[str, torch.Tensor] = {}
+
+    def get(self, name: str, shape, dtype) -> torch.Tensor:
+        numel = math.prod(shape)
+        buf = self.bufs.get(name)
+        if buf is None or buf.numel() < numel or buf.dtype != dtype:
+            buf = torch.empty(max(numel, 1), device=self.device, dtype=dtype)
+            self.bufs[name] = buf
+        return buf[:numel].view(*shape)
+
+
+class _CountingExt:
+    """Proxy over the extension that counts kernel launches issued from the host."""
+
+    _NOT_KERNELS = {"status", "num_sms", "gemv_argmax_grid"}
+
+    def __init__(self, ext) -> None:
+        self._ext = ext
+        self.launches = 0
+
+    def __getattr__(self, name):
+        fn = getattr(self._ext, name)
+        if name in self._NOT_KERNELS or not callable(fn):
+            return fn
+
+        def counted(*args, **kwargs):
+            self.launches += 1
+            return fn(*args, **kwargs)
+
+        return counted
+
+
+class B200Engine:
+    """Kernel-driven Llama forward passes on one GPU."""
+
+    def __init__(self, config: ModelConfig, weights: EngineWeights, device, *, max_positions: int | None = None) -> None:
+        ops.require_on_gpu()
+        self.cfg = config
+        self.w = weights
+        self.device = torch.device(device)
+        self.ext = _CountingExt(ops.ext())
+        self.max_positions = int(max_positions or min(config.max_positions, 65536))
+        self.rope = rope_table(config, self.max_positions, self.device)
+        self.ws = _Workspace(self.device)
+        self.scale = 1.0 / math.sqrt(config.head_dim)
+        self.num_sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self._graphs: dict[tuple, torch.cuda.CUDAGraph] = {}
+        self.bn = 256
+
+    # ----------------------------------------------------------- helpers
+    @classmethod
+    def random(cls, config: ModelConfig, *, seed: int = 0, device="cuda", **kw) -> "B200Engine":
+        return cls(config, EngineWeights.random(config, seed=seed, device=device), device, **kw)
+
+    @classmethod
+    def from_oracle(cls, model, device="cuda", **kw) -> "B200Engine":
+        return cls(model.config, EngineWeights.from_oracle(model, device), device, **kw)
+
+    def new_slot(self, capacity: int) -> KVSlot:
+        return KVSlot(self.cfg, capacity, self.device)
+
+    def _i32(self, name: str, n: int) -> torch.Tensor:
+        return self.ws.get(name, (n,), torch.int32)
+
+    def _arange(self, name: str, n: int, start: int = 0) -> torch.Tensor:
+        t = self._i32(name, n)
+        self.ext.arange_i32(t, start)
+        return t
+
+    # -------------------------------------------------------- layer body
+    def _attn_mlp(
+        self,
+        layer: int,
+        h: torch.Tensor,
+        q: torch.Tensor,
+        slot: KVSlot,
+        *,
+        q_rows: torch.Tensor | None,
+        qpos: torch.Tensor,
+        n_keys: int,
+        kpos: torch.Tensor | None,
+        n_rows: int,
+    ) -> None:
+        """attention over the slot's keys, o_proj + residual, then the MLP block (in place on h)."""
+        cfg, lw, ext = self.cfg, self.w.layers[layer], self.ext
+        attn = self.ws.get("attn", (n_rows, cfg.q_size), torch.bfloat16)
+        ext.attention_prefill(q, q_rows, qpos, slot.k(layer), slot.v(layer), kpos, n_keys, cfg.n_heads, self.scale, attn)
+        ext.gemm_residual(attn, lw.w_o, h, h, self.bn)
+        x = self.ws.get("x", (n_rows, cfg.d_model), torch.bfloat16)
+        ext.rmsnorm(h, None, lw.ln2, cfg.rms_eps, x)
+        act = self.ws.get("act", (n_rows, cfg.ffn), torch.bfloat16)
+        ext.gemm_swiglu(x, lw.w_gu, act, self.bn)
+        ext.gemm_residual(act, lw.w_down, h, h, self.bn)
+
+    def _full_layer(self, layer: int, h: torch.Tensor, slot: KVSlot, pos: torch.Tensor, slots: torch.Tensor,
+                    n_keys: int, kpos: torch.Tensor | None, dev_part=None, dev_mode: int = 0) -> torch.Tensor:
+        """Norm + fused QKV/RoPE/scatter for every row of h; returns q."""
+        cfg, lw, ext = self.cfg, self.w.layers[layer], self.ext
+        n = h.shape[0]
+        x = self.ws.get("x", (n, cfg.d_model), torch.bfloat16)
+        ext.rmsnorm(h, None, lw.ln1, cfg.rms_eps, x)
+        q = self.ws.get("q", (n, cfg.q_size), torch.bfloat16)
+        ext.gemm_qkv(x, lw.w_qkv, q, slot.k(layer), slot.v(layer), pos, slots, self.rope,
+                     cfg.n_heads, cfg.n_kv_heads, dev_part, dev_mode, self.bn)
+        return q
+
+    # ----------------------------------------------------------- compose
+    def compose(self, slot: KVSlot, blocks, *, first_slot: int, layer_begin: int = 0,
+                source_positions=None, target_positions=None) -> None:
+        """Gather document K/V blocks into ``slot`` after ``first_slot`` and re-rotate keys.
+
+        ``blocks`` are [L, 2, H_kv, n, D] tensors in HBM or pinned host memory
+        (the kernel reads mapped host memory directly).  Document i lands at
+        slots cursor..cursor+n-1; its keys move from source position
+        ``source_positions[i]`` (0 for independently produced documents) to
+        ``target_positions[i]`` (default: its slot).  Layers below
+        ``layer_begin`` are skipped: CacheBlend recomputes them fully.
+        """
+        rows, offsets, cursor = [], [0], first_slot
+        for i, block in enumerate(blocks):
+            n = int(block.shape[3])
+            ptr = int(block.data_ptr())
+            src = 0 if source_positions is None else int(source_positions[i])
+            dst = cursor if target_positions is None else int(target_positions[i])
+            rows.append([ptr & 0xFFFFFFFF, ptr >> 32, n, src, cursor, dst])
+            offsets.append(offsets[-1] + n)
+            cursor += n
+        if cursor > slot.capacity:
+            raise ValueError("composed documents exceed the slot capacity")
+        table = torch.tensor(rows, dtype=torch.int64)
+        table = torch.where(table >= 2**31, table - 2**32, table).to(torch.int32)
+        host = torch.empty((len(rows) * 6 + len(offsets),), dtype=torch.int32, pin_memory=True)
+        host[: len(rows) * 6] = table.reshape(-1)
+        host[len(rows) * 6 :] = torch.tensor(offsets, dtype=torch.int32)
+        dev = self.ws.get("compose_meta", (host.numel(),), torch.int32)
+        dev.copy_(host, non_blocking=True)
+        docs = dev[: len(rows) * 6].view(len(rows), 6)
+        offs = dev[len(rows) * 6 :]
+        self.ext.compose_relocate(docs, offs, offsets[-1], layer_begin, self.cfg.n_layers, self.cfg.n_layers,
+                                  slot.data, self.cfg.n_kv_heads, self.rope)
+
+    # ------------------------------------------------------------ passes
+    def embed(self, ids: torch.Tensor, name: str = "h") -> torch.Tensor:
+        h = self.ws.get(name, (ids.numel(), self.cfg.d_model), torch.bfloat16)
+        self.ext.embedding(ids, self.w.embed, h)
+        return h
+
+    def prefill(self, ids: torch.Tensor, slot: KVSlot, *, start: int = 0, kpos: torch.Tensor | None = None) -> torch.Tensor:
+        """Causal prefill of ``ids`` (int32, device) at positions/slots start.. ; returns final hidden [T, d].
+
+        Keys [0, start) already in the slot are visible (direct prefix reuse).
+        """
+        T = ids.numel()
+        if start + T > slot.capacity or start + T > self.max_positions:
+            raise ValueError("prompt exceeds slot capacity / RoPE table")
+        h = self.embed(ids)
+        pos = self._arange("pos", T, start)
+        for layer in range(self.cfg.n_layers):
+            q = self._full_layer(layer, h, slot, pos, pos, start + T, kpos)
+            self._attn_mlp(layer, h, q, slot, q_rows=None, qpos=pos, n_keys=start + T, kpos=kpos, n_rows=T)
+        return h
+
+    def cacheblend(
+        self,
+        ids: torch.Tensor,
+        slot: KVSlot,
+        *,
+        prefix_tokens: int,
+        suffix_tokens: int,
+        blend: CacheBlendConfig,
+        global_positions: torch.Tensor | None = None,
+    ) -> tuple[torch.Tensor, int, dict]:
+        """Selective recompute over the composed cache already in ``slot``.
+
+        Returns (hidden of the active rows [A, d], A, device-side metadata).
+        The number of active rows A is known on the host (no sync):
+        prefix (strict protocol) + ceil(ratio * N_doc) + suffix.
+        """
+        cfg, ext = self.cfg, self.ext
+        T = ids.numel()
+        raw_len = T - suffix_tokens
+        n_doc = raw_len - prefix_tokens
+        if T > slot.capacity:
+            raise ValueError("prompt exceeds slot capacity")
+        check = blend.check_layer
+        if not 0 <= check < cfg.n_layers:
+            raise ValueError("check_layer lies outside the model")
+        from ..cacheblend import recompute_count
+
+        k_sel = recompute_count(n_doc, blend.recompute_ratio)
+        A = (prefix_tokens if blend.keep_prefix else 0) + k_sel + suffix_tokens
+        h = self.embed(ids)
+        rows = self._arange("rows", T)
+        gpos = rows if global_positions is None else global_positions
+        kpos = global_positions  # None -> key position == slot
+        for layer in range(check):
+            q = self._full_layer(layer, h, slot, gpos, rows, T, kpos)
+            self._attn_mlp(layer, h, q, slot, q_rows=None, qpos=gpos, n_keys=T, kpos=kpos, n_rows=T)
+        # ---- check layer ----
+        dev_part = self.ws.get("dev", (T, 2 * cfg.n_kv_heads), torch.float32)
+        q = self._full_layer(check, h, slot, gpos, rows, T, kpos, dev_part, blend.dev_mode)
+        active = self._i32("active", T)
+        n_active = self._i32("n_active", 1)
+        scores = self.ws.get("scores", (max(1, n_doc),), torch.float32)
+        checksum = self.ws.get("checksum", (1,), torch.int64)
+        ext.cacheblend_select(dev_part, cfg.n_kv_heads, blend.dev_mode, T, prefix_tokens, raw_len, k_sel,
+                              blend.keep_prefix, active, n_active, scores, checksum)
+        act_rows = active[:A]
+        qpos_a = self._i32("qpos_a", A)
+        ext.index_i32(gpos, act_rows, qpos_a)
+        h_a = self.ws.get("h_a", (A, cfg.d_model), torch.bfloat16)
+        ext.gather_rows(h, act_rows, h_a)
+        self._attn_mlp(check, h_a, q, slot, q_rows=act_rows, qpos=qpos_a, n_keys=T, kpos=kpos, n_rows=A)
+        # ---- later layers: active rows only ----
+        for layer in range(check + 1, cfg.n_layers):
+            qa = self._full_layer(layer, h_a, slot, qpos_a, act_rows, T, kpos)
+            self._attn_mlp(layer, h_a, qa, slot, q_rows=None, qpos=qpos_a, n_keys=T, kpos=kpos, n_rows=A)
+        meta = {"active": act_rows, "n_active": n_active, "checksum": checksum, "k_selected": k_sel,
+                "document_tokens": n_doc, "active_rows": A}
+        return h_a, A, meta
+
+    # ------------------------------------------------------------ decode
+    MAX_DECODE_TOKENS = 8192
+
+    def _decode_buffers(self, max_new: int):
+        # Fixed sizes: captured decode graphs hold these addresses.
+        if max_new > self.MAX_DECODE_TOKENS:
+            raise ValueError(f"max_new_tokens above {self.MAX_DECODE_TOKENS}")
+        cfg = self.cfg
+        ws = self.ws
+        grid = self.ext.gemv_argmax_grid(cfg.vocab)
+        return {
+            "h": ws.get("dec_h", (1, cfg.d_model), torch.bfloat16),
+            "q": ws.get("dec_q", (1, cfg.q_size), torch.bfloat16),
+            "attn": ws.get("dec_attn", (1, cfg.q_size), torch.bfloat16),
+            "act": ws.get("dec_act", (1, cfg.ffn), torch.bfloat16),
+            "pos": ws.get("dec_pos", (1,), torch.int32),
+            "tok": ws.get("dec_tok", (8,), torch.int32),
+            "log": ws.get("dec_log", (self.MAX_DECODE_TOKENS,), torch.int32),
+            "gen": ws.get("dec_gen", (1,), torch.int32),
+            "pv": ws.get("dec_pv", (8 * grid,), torch.float32),
+            "pi": ws.get("dec_pi", (8 * grid,), torch.int32),
+            "counter": ws.get("dec_counter", (1,), torch.int32),
+        }
+
+    def _decode_splits(self, capacity: int) -> int:
+        target = max(1, (2 * self.num_sms) // self.cfg.n_kv_heads)
+        splits = max(1, min(target, (capacity + 63) // 64))
+        return splits
+
+    def first_token(self, hidden_row: torch.Tensor, *, position: int, max_new: int) -> dict:
+        """LM head + argmax on the last prompt row; seeds the device-side decode state."""
+        b = self._decode_buffers(max_new)
+        b["gen"].zero_()
+        b["counter"].zero_()
+        b["pos"].fill_(position)
+        self.ext.gemv_argmax(hidden_row, self.w.lm_head, self.w.norm, self.cfg.rms_eps, b["pv"], b["pi"],
+                             b["counter"], b["tok"], b["log"], b["gen"], self.w.embed, b["h"], None)
+        return b
+
+    def _decode_step(self, slot: KVSlot, b: dict, splits: int) -> None:
+        cfg, ext = self.cfg, self.ext
+        H = cfg.n_heads
+        max_splits = max(1, (2 * self.num_sms) // cfg.n_kv_heads)
+        part_o = self.ws.get("dec_part_o", (H * max_splits * 128,), torch.float32)
+        part_ml = self.ws.get("dec_part_ml", (H * max_splits * 2,), torch.float32)
+        counters = self.ws.get("dec_cnt", (cfg.n_kv_heads,), torch.int32)
+        h = b["h"]
+        for layer, lw in enumerate(self.w.layers):
+            ext.gemv_qkv(h, lw.w_qkv, lw.ln1, cfg.rms_eps, b["q"], slot.k(layer), slot.v(layer), b["pos"],
+                         self.rope, cfg.n_heads, cfg.n_kv_heads)
+            ext.attention_decode(b["q"], slot.k(layer), slot.v(layer), b["pos"], H, self.scale, splits,
+                                 part_o, part_ml, counters, b["attn"])
+            ext.gemv_residual(b["attn"], lw.w_o, None, cfg.rms_eps, h, h)
+            ext.gemv_swiglu(h, lw.w_gu, lw.ln2, cfg.rms_eps, b["act"])
+            ext.gemv_residual(b["act"], lw.w_down, None, cfg.rms_eps, h, h)
+        ext.gemv_argmax(h, self.w.lm_head, self.w.norm, cfg.rms_eps, b["pv"], b["pi"], b["counter"], b["tok"],
+                        b["log"], b["gen"], self.w.embed, h, b["pos"])
+
+    def decode(self, slot: KVSlot, n_steps: int, *, max_new: int, use_graph: bool = True) -> None:
+        """Run ``n_steps`` greedy decode steps from the state ``first_token`` left."""
+        if n_steps <= 0:
+            return
+        splits = self._decode_splits(slot.capacity)
+        b = self._decode_buffers(max_new)
+        # counters for the split merge start at zero
+        self.ws.get("dec_cnt", (self.cfg.n_kv_heads,), torch.int32).zero_()
+        if not use_graph:
+            for _ in range(n_steps):
+                self._decode_step(slot, b, splits)
+            return
+        key = (id(slot), splits, max_new)
+        graph = self._graphs.get(key)
+        if graph is None:
+            # one eager step warms up launch attributes; then capture a step
+            # against a scratch copy of the device state so the real state is
+            # only advanced by replays.
+            saved = {k: b[k].clone() for k in ("h", "pos", "gen", "log", "tok")}
+            self._decode_step(slot, b, splits)
+            for k, v in saved.items():
+                b[k].copy_(v)
+            torch.cuda.synchronize(self.device)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self._decode_step(slot, b, splits)
+            for k, v in saved.items():
+                b[k].copy_(v)
+            self._graphs[key] = graph
+        for _ in range(n_steps):
+            graph.replay()
+        # every replay launches the captured kernels: 5 per layer + LM head
+        self.ext.launches += n_steps * (5 * self.cfg.n_layers + 1)
+
+    def generated_tokens(self, max_new: int) -> torch.Tensor:
+        """Device view of the token log (first ``max_new`` entries)."""
+        return self._decode_buffers(max_new)["log"][:max_new]
+
+    def release_graphs(self) -> None:
+        self._graphs.clear()

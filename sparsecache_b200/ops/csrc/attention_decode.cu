@@ -173,8 +173,7 @@ cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
   const int chunk_cap = (a.cache_cap + a.M + a.splits - 1) / a.splits;
   const size_t smem = (size_t)(a.M * G * 128 + a.M * G * chunk_cap) * sizeof(float);
   if (smem > 220 * 1024) return cudaErrorInvalidValue;
-  cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       (int)smem);
+  ensure_smem_attr(attention_decode_kernel, 220 * 1024);
   dim3 grid(a.n_kv_heads, a.splits);
   attention_decode_kernel<<<grid, kThreads, smem, stream>>>(a, chunk_cap);
   return cudaGetLastError();

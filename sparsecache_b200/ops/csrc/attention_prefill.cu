@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream) {
   if (p.head_dim != kD || p.n_rows <= 0) return p.n_rows == 0 ? cudaSuccess : cudaErrorInvalidValue;
   const int smem = kBM * kRowBytes + 4 * kBN * kRowBytes;  // 80 KB
-  cudaFuncSetAttribute(attention_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  ensure_smem_attr(attention_prefill_kernel, smem);
   dim3 grid((p.n_rows + kBM - 1) / kBM, p.n_heads);
   attention_prefill_kernel<<<grid, kThreads, smem, stream>>>(p);
   return cudaGetLastError();

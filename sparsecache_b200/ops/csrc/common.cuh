@@ -324,3 +324,18 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
 }
 
 }  // namespace sc
+
+namespace sc {
+// Raise a kernel's dynamic shared-memory limit once per device (not on every
+// launch: the attribute call is host work and must stay out of graph capture).
+template <typename F>
+inline void ensure_smem_attr(F* func, int bytes) {
+  static int set_bytes[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && set_bytes[dev] < bytes) {
+    cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    set_bytes[dev] = bytes;
+  }
+}
+}  // namespace sc

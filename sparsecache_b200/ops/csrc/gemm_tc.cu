@@ -378,7 +378,7 @@ static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   if (!make_tmap_2d_bf16(&ta, g.a, g.K, g.M, g.lda, kGemmBK, kGemmBM, true)) return cudaErrorInvalidValue;
   if (!make_tmap_2d_bf16(&tb, g.b, g.K, g.N, g.ldb, kGemmBK, BN, true)) return cudaErrorInvalidValue;
   auto kern = gemm_tc_kernel<BN, EPI>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  ensure_smem_attr(kern, Cfg::kSmemBytes);
   const int num_tiles = ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + BN - 1) / BN);
   int grid = num_tiles < g.num_sms ? num_tiles : g.num_sms;
   if (grid < 1) grid = 1;

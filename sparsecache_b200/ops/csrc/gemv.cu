@@ -316,8 +316,7 @@ cudaError_t gemv_bf16(const GemvArgs& a, cudaStream_t stream) {
   if (grid > cap) grid = cap;
 #define SC_LAUNCH_GEMV(MRV)                                                              \
   {                                                                                      \
-    cudaFuncSetAttribute(gemv_kernel<MRV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                         (int)smem);                                                     \
+    ensure_smem_attr(gemv_kernel<MRV>, 200 * 1024);                                       \
     gemv_kernel<MRV><<<grid, kThreads, smem, stream>>>(a);                               \
   }
   if (a.M == 1) SC_LAUNCH_GEMV(1)

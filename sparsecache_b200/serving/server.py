@@ -1,0 +1,146 @@
+"""Single-GPU RAG serving front end: dedup store -> composer -> CacheBlend -> graph decode.
+
+This is the public serving call (``RAGServer.serve``) used by the CLI, the
+data-parallel router and the benchmark.  One request at a time per GPU
+(batch 1, greedy), as the reference measures (reuse_cacheblend_pipeline.py:
+835-893 ``run_full_cacheblend``; modeling.py:33-327).
+
+Device timing: CUDA events on the serving stream bracket TTFT (first token
+ready on the device) and the full response (all new tokens ready).  Nothing
+in ``serve`` synchronises the host unless ``sync=True``; the caller decides
+when to read results.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+
+from ..config import CacheBlendConfig
+from ..models.engine import B200Engine, KVSlot
+from ..store import DocumentKVStore
+from ..synthetic import RAGRequest
+
+
+@dataclass
+class ServeHandle:
+    """In-flight request: events and the pinned host buffer receiving its tokens."""
+
+    request: RAGRequest
+    mode: str
+    start: torch.cuda.Event
+    first: torch.cuda.Event
+    end: torch.cuda.Event
+    tokens_host: torch.Tensor
+    max_new: int
+    eos: frozenset
+    meta: dict[str, Any] = field(default_factory=dict)
+
+    def result(self) -> "ServeResult":
+        self.end.synchronize()
+        toks = [int(t) for t in self.tokens_host[: self.max_new].tolist()]
+        for i, t in enumerate(toks):
+            if t in self.eos:
+                toks = toks[: i + 1]
+                break
+        ttft = self.start.elapsed_time(self.first)
+        total = self.start.elapsed_time(self.end)
+        return ServeResult(tuple(toks), ttft, total, total - ttft, self.mode, dict(self.meta))
+
+
+@dataclass
+class ServeResult:
+    token_ids: tuple[int, ...]
+    ttft_ms: float
+    response_ms: float
+    decode_ms: float
+    mode: str
+    metadata: dict[str, Any]
+
+
+class RAGServer:
+    def __init__(
+        self,
+        engine: B200Engine,
+        store: DocumentKVStore,
+        *,
+        capacity: int,
+        blend: CacheBlendConfig | None = None,
+    ) -> None:
+        self.engine = engine
+        self.store = store
+        self.blend = blend or CacheBlendConfig()
+        self.slot: KVSlot = engine.new_slot(capacity)
+        self.eos = frozenset(engine.cfg.eos_token_ids)
+        self._ids_dev = torch.empty(capacity, dtype=torch.int32, device=engine.device)
+
+    # ---------------------------------------------------------- producer
+    def encode_local(self, tokens) -> torch.Tensor:
+        """Prefill one document alone at positions 0..n-1; returns its [L,2,Hkv,n,D] block."""
+        n = len(tokens)
+        block = KVSlot(self.engine.cfg, n, self.engine.device)
+        ids = torch.tensor(tokens, dtype=torch.int32).to(self.engine.device, non_blocking=True)
+        self.engine.prefill(ids, block)
+        return block.data
+
+    def produce(self, requests) -> dict[str, Any]:
+        docs = [d for r in requests for d in r.documents]
+        return self.store.produce(self.encode_local, docs)
+
+    # ------------------------------------------------------------- serve
+    def serve(
+        self,
+        request: RAGRequest,
+        *,
+        mode: str = "cacheblend",
+        ids_host: torch.Tensor | None = None,
+        store: DocumentKVStore | None = None,
+        max_new_tokens: int | None = None,
+        sync: bool = False,
+    ) -> ServeHandle | ServeResult:
+        """Serve one request.  ``ids_host`` (pinned int32) is copied H2D inside the timed region."""
+        eng = self.engine
+        store = store or self.store
+        blend = self.blend
+        max_new = max_new_tokens or blend.max_new_tokens
+        T = request.prompt_tokens
+        if T + max_new > self.slot.capacity:
+            raise ValueError("request does not fit the serving slot")
+        start, first, end = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        tokens_host = torch.empty(max_new, dtype=torch.int32, pin_memory=True)
+        start.record()
+        ids = self._ids_dev[:T]
+        if ids_host is None:
+            ids_host = torch.tensor(request.prompt, dtype=torch.int32).pin_memory()
+        ids.copy_(ids_host, non_blocking=True)
+        meta: dict[str, Any] = {"prompt_tokens": T}
+        if mode == "cacheblend":
+            blocks = [store[d].kv for d in request.documents]
+            eng.compose(self.slot, blocks, first_slot=len(request.prefix), layer_begin=blend.check_layer)
+            h_a, A, dmeta = eng.cacheblend(
+                ids, self.slot, prefix_tokens=len(request.prefix), suffix_tokens=len(request.suffix), blend=blend
+            )
+            last = h_a[A - 1 : A]
+            meta.update(active_rows=A, document_tokens=dmeta["document_tokens"],
+                        document_tokens_selected=dmeta["k_selected"], checksum_dev=dmeta["checksum"])
+        elif mode == "full":
+            h = eng.prefill(ids, self.slot)
+            last = h[T - 1 : T]
+        elif mode == "direct":
+            blocks = [store[d].kv for d in request.documents]
+            P = len(request.prefix)
+            # the system prefix is prefilled, documents reused as-is, suffix prefilled after them
+            eng.prefill(ids[:P], self.slot)
+            eng.compose(self.slot, blocks, first_slot=P)
+            h = eng.prefill(ids[P + request.document_tokens :], self.slot, start=P + request.document_tokens)
+            last = h[len(request.suffix) - 1 : len(request.suffix)]
+        else:
+            raise ValueError(f"unknown mode {mode!r}")
+        eng.first_token(last, position=T, max_new=max_new)
+        first.record()
+        eng.decode(self.slot, max_new - 1, max_new=max_new)
+        tokens_host.copy_(eng.generated_tokens(max_new), non_blocking=True)
+        end.record()
+        handle = ServeHandle(request, mode, start, first, end, tokens_host, max_new, self.eos, meta)
+        return handle.result() if sync else handle
