@@ -377,9 +377,8 @@ class B200Engine:
         }
 
     def _decode_splits(self, capacity: int) -> int:
-        target = max(1, (2 * self.num_sms) // self.cfg.n_kv_heads)
-        splits = max(1, min(target, (capacity + 63) // 64))
-        return splits
+        """CTAs per kv head (= thread-block cluster size) of the decode attention."""
+        return int(self.ext.attention_decode_cluster(capacity))
 
     def first_token(self, hidden_row: torch.Tensor, *, position: int, max_new: int) -> dict:
         """LM head + argmax on the last prompt row; seeds the device-side decode state."""
@@ -394,16 +393,11 @@ class B200Engine:
     def _decode_step(self, slot: KVSlot, b: dict, splits: int) -> None:
         cfg, ext = self.cfg, self.ext
         H = cfg.n_heads
-        max_splits = max(1, (2 * self.num_sms) // cfg.n_kv_heads)
-        part_o = self.ws.get("dec_part_o", (H * max_splits * 128,), torch.float32)
-        part_ml = self.ws.get("dec_part_ml", (H * max_splits * 2,), torch.float32)
-        counters = self.ws.get("dec_cnt", (cfg.n_kv_heads,), torch.int32)
         h = b["h"]
         for layer, lw in enumerate(self.w.layers):
             ext.gemv_qkv(h, lw.w_qkv, lw.ln1, cfg.rms_eps, b["q"], slot.k(layer), slot.v(layer), b["pos"],
                          self.rope, cfg.n_heads, cfg.n_kv_heads)
-            ext.attention_decode(b["q"], slot.k(layer), slot.v(layer), b["pos"], H, self.scale, splits,
-                                 part_o, part_ml, counters, b["attn"])
+            ext.attention_decode(b["q"], slot.k(layer), slot.v(layer), b["pos"], H, self.scale, splits, b["attn"])
             ext.gemv_residual(b["attn"], lw.w_o, None, cfg.rms_eps, h, h)
             ext.gemv_swiglu(h, lw.w_gu, lw.ln2, cfg.rms_eps, b["act"])
             ext.gemv_residual(b["act"], lw.w_down, None, cfg.rms_eps, h, h)
@@ -416,8 +410,6 @@ class B200Engine:
             return
         splits = self._decode_splits(slot.capacity)
         b = self._decode_buffers(max_new)
-        # counters for the split merge start at zero
-        self.ws.get("dec_cnt", (self.cfg.n_kv_heads,), torch.int32).zero_()
         if not use_graph:
             for _ in range(n_steps):
                 self._decode_step(slot, b, splits)

@@ -1,182 +1,312 @@
-// Split-K decode / verify attention over a paged layer cache.
+// Split-K decode / verify attention over a paged layer cache, merged through
+// distributed shared memory inside a thread-block cluster.
 //
 // The query block is M <= 8 consecutive new tokens (M = 1 for greedy decode,
 // M = gamma + 1 for the batched speculative verifier) at positions
 // *pos .. *pos + M - 1; row m sees keys [0, *pos + m].  The position lives in
 // device memory so a captured CUDA graph replays the same launch every step.
 //
-// Grid: (kv_head, split).  A CTA scores one key chunk for all G = H/H_kv
-// query heads sharing the kv head and all M rows (GQA packing: the K/V chunk
-// is read once for every query vector), writes (max, sum, o[128]) partials,
-// and the last CTA of each kv head merges the splits (a per-head counter,
-// reset by that CTA, makes the merge graph-replayable without a second
-// launch).  Replaces the reference's HF DynamicCache concatenation + SDPA per
-// token (modeling.py:383-417; progressive_kv_feasibility.py:561-613, 616-682).
+// Grid (S, n_kv_heads), cluster (S, 1, 1): the S CTAs of a cluster split the
+// keys of one kv head.  Each CTA stages 128-key K/V sub-chunks into shared
+// memory with cp.async (64 KB in flight per CTA), scores them for all
+// G = H/H_kv query heads and all M rows at once (GQA packing: K/V are read
+// once per kv head), keeps an online softmax per query vector, and leaves its
+// partial (max, sum, o[128]) in its own shared memory.  After a cluster
+// barrier every CTA merges a slice of the outputs by reading its peers'
+// partials over DSMEM; a second barrier keeps the partials alive until all
+// peers are done.  No global scratch, no atomics, one launch.
+//
+// Replaces the reference's per-token HF DynamicCache concatenation + SDPA
+// (modeling.py:383-417; progressive_kv_feasibility.py:561-613, 616-682).
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
+
+namespace cg = cooperative_groups;
 
 namespace sc {
 
 namespace {
-constexpr int kThreads = 128;
-constexpr int kMaxQV = 64;  // M * G
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kSub = 128;     // keys per staged sub-chunk
+constexpr int kMaxQV = 32;    // M * G
+constexpr int kRow = 256;     // bytes per K/V row (128 bf16)
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
+  const int sz = pred ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(sz)
+               : "memory");
+}
 }  // namespace
 
+struct DecodeSmem {
+  __nv_bfloat16 k[kSub * 128];
+  __nv_bfloat16 v[kSub * 128];
+  float s[kMaxQV][kSub];
+  float o[kMaxQV][128];  // partial output of this CTA (unnormalised)
+  float m[kMaxQV];       // running max (log2 domain)
+  float l[kMaxQV];       // running sum
+  float corr[kMaxQV];
+};
+
+// QVT is the compile-time query-vector count (M * G rounded up); the exact
+// decode shapes (QVT == M * G) carry no per-vector guards in the inner loops.
+template <int QVT>
 __global__ void __launch_bounds__(kThreads)
-    attention_decode_kernel(AttnDecodeArgs a, int chunk_cap) {
-  extern __shared__ __align__(16) float dsm[];
+    attention_decode_kernel(AttnDecodeArgs a, int chunk) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  DecodeSmem& sm = *reinterpret_cast<DecodeSmem*>(smem_raw);
+  cg::cluster_group cluster = cg::this_cluster();
+
   const int G = a.n_heads / a.n_kv_heads;
   const int QV = a.M * G;
-  float* qs = dsm;                  // [QV][128]
-  float* sc = qs + QV * 128;        // [QV][chunk_cap]
-  __shared__ int s_last;
-
-  const int kvh = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
+  const int split = blockIdx.x, S = gridDim.x;
+  const int kvh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // *pos and the cache rows [0, *pos) were written at least two launches
+  // back (the LM-head kernel of the previous step and earlier QKV kernels),
+  // so they are read before the programmatic wait; q and the M new rows come
+  // from the QKV kernel right before this one and are read after it.
   const int pos0 = *a.pos;
   const int n_keys = pos0 + a.M;
-  const int chunk = (n_keys + splits - 1) / splits;
   const int k_begin = split * chunk;
   const int k_end = min(n_keys, k_begin + chunk);
-  const int nk = max(0, k_end - k_begin);
   const float sl2 = a.scale * 1.4426950408889634f;
-
-  // q vectors: qv = m * G + gi  -> head kvh * G + gi of row m
-  for (int idx = tid; idx < QV * 128; idx += kThreads) {
-    const int qv = idx >> 7, d = idx & 127;
-    const int m = qv / G, gi = qv % G;
-    qs[idx] = __bfloat162float(a.q[(size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + d]);
-  }
-  __syncthreads();
-
   const __nv_bfloat16* kb = a.k_cache + (size_t)kvh * a.cache_cap * 128;
   const __nv_bfloat16* vb = a.v_cache + (size_t)kvh * a.cache_cap * 128;
-
-  // ---- scores: one key per thread, all query vectors ----
-  for (int j = tid; j < nk; j += kThreads) {
-    const int key = k_begin + j;
-    const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)key * 128);
-    float kf[128];
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      const uint4 v = kr[c];
-      const float2 f0 = unpack_bf16x2(v.x), f1 = unpack_bf16x2(v.y), f2 = unpack_bf16x2(v.z),
-                   f3 = unpack_bf16x2(v.w);
-      kf[8 * c + 0] = f0.x; kf[8 * c + 1] = f0.y; kf[8 * c + 2] = f1.x; kf[8 * c + 3] = f1.y;
-      kf[8 * c + 4] = f2.x; kf[8 * c + 5] = f2.y; kf[8 * c + 6] = f3.x; kf[8 * c + 7] = f3.y;
+  const uint32_t sk = smem_u32(sm.k), sv = smem_u32(sm.v);
+  // stage rows [base, base + nk) whose key index lies in [lo, hi); rows past
+  // nk are zero-filled when zero_tail is set
+  auto stage = [&](int base, int nk, int lo, int hi, bool zero_tail) {
+    for (int i = tid; i < kSub * 16; i += kThreads) {
+      const int r = i >> 4, c = i & 15;
+      const int key = base + r;
+      const bool in = r < nk;
+      if (in ? (key < lo || key >= hi) : !zero_tail) continue;
+      const size_t off = (size_t)(in ? key : 0) * 128 + c * 8;
+      cp_async16(sk + r * kRow + c * 16, kb + off, in);
+      cp_async16(sv + r * kRow + c * 16, vb + off, in);
     }
-    for (int qv = 0; qv < QV; ++qv) {
-      const float* q = qs + qv * 128;
-      float s = 0.f;
+  };
+  if (k_begin < k_end) stage(k_begin, min(kSub, k_end - k_begin), 0, pos0, true);
+  for (int i = tid; i < QV * 128; i += kThreads) sm.o[i / 128][i % 128] = 0.f;
+  if (tid < QV) sm.m[tid] = -INFINITY, sm.l[tid] = 0.f;
+  pdl_wait();
+  pdl_launch_dependents();
+
+  // Scores use LPK lanes per key (LPK = 8 for small query blocks: 4 keys per
+  // warp step and a 3-level shuffle reduction); lane owns DPL dims of every
+  // query vector in registers.
+  constexpr int LPK = QVT <= 8 ? 8 : 32;
+  constexpr int DPL = 128 / LPK;
+  const int sub = lane % LPK;        // dim slice
+  const int kgrp = lane / LPK;       // key slot within the warp step
+  float q[QVT][DPL];
 #pragma unroll
-      for (int d = 0; d < 128; ++d) s = fmaf(q[d], kf[d], s);
-      const int m = qv / G;
-      sc[qv * chunk_cap + j] = (key <= pos0 + m) ? s * sl2 : -INFINITY;
+  for (int qv = 0; qv < QVT; ++qv) {
+    if (qv < QV) {
+      const int m = qv / G, gi = qv % G;
+      const __nv_bfloat16* qp = a.q + (size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + DPL * sub;
+#pragma unroll
+      for (int c = 0; c < DPL / 4; ++c) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(qp + 4 * c);
+        const float2 f0 = unpack_bf16x2(raw.x), f1 = unpack_bf16x2(raw.y);
+        q[qv][4 * c] = f0.x; q[qv][4 * c + 1] = f0.y; q[qv][4 * c + 2] = f1.x; q[qv][4 * c + 3] = f1.y;
+      }
     }
   }
-  __syncthreads();
-
-  // ---- per query vector: max and exp-sum over the chunk (one warp each) ----
-  __shared__ float s_max[kMaxQV], s_sum[kMaxQV];
-  for (int qv = warp; qv < QV; qv += kThreads / 32) {
-    float mx = -INFINITY;
-    for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sc[qv * chunk_cap + j]);
-    mx = warp_max(mx);
-    const float base = (mx == -INFINITY) ? 0.f : mx;
-    float sum = 0.f;
-    for (int j = lane; j < nk; j += 32) {
-      const float e = exp2f(sc[qv * chunk_cap + j] - base);
-      sc[qv * chunk_cap + j] = e;
-      sum += e;
+  for (int base = k_begin; base < k_end; base += kSub) {
+    const int nk = min(kSub, k_end - base);
+    if (base == k_begin) {
+      stage(base, nk, pos0, n_keys, false);  // the new rows, now visible
+    } else {
+      __syncthreads();  // previous sub-chunk fully consumed
+      stage(base, nk, 0, n_keys, true);
     }
-    sum = warp_sum(sum);
-    if (lane == 0) s_max[qv] = mx, s_sum[qv] = sum;
-  }
-  __syncthreads();
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
 
-  // ---- o = p . V : thread owns dims (2*(tid%64), +1) for query vectors tid/64, +2, ... ----
-  {
-    const int d = 2 * (tid & 63);
-    const int q0 = tid >> 6;
-    float acc[kMaxQV / 2][2];
-    const int nq = (QV - q0 + 1) / 2;
+    // scores: each warp step covers 32/LPK keys; LPK lanes split the dims
+    constexpr int KPW = 32 / LPK;
+    for (int j0 = warp * KPW; j0 < nk; j0 += kWarps * KPW) {
+      const int j = j0 + kgrp;
+      const bool valid = j < nk;
+      float kf[DPL];
+      {
+        const __nv_bfloat16* kr = sm.k + (valid ? j : 0) * 128 + DPL * sub;
 #pragma unroll
-    for (int i = 0; i < kMaxQV / 2; ++i) acc[i][0] = acc[i][1] = 0.f;
-    for (int j = 0; j < nk; ++j) {
-      const float2 v = unpack_bf16x2(
-          *reinterpret_cast<const uint32_t*>(vb + (size_t)(k_begin + j) * 128 + d));
+        for (int c = 0; c < DPL / 4; ++c) {
+          const uint2 raw = *reinterpret_cast<const uint2*>(kr + 4 * c);
+          const float2 f0 = unpack_bf16x2(raw.x), f1 = unpack_bf16x2(raw.y);
+          kf[4 * c] = f0.x; kf[4 * c + 1] = f0.y; kf[4 * c + 2] = f1.x; kf[4 * c + 3] = f1.y;
+        }
+      }
+      const int key = base + j;
 #pragma unroll
-      for (int i = 0; i < kMaxQV / 2; ++i) {
-        if (i < nq) {
-          const float pj = sc[(q0 + 2 * i) * chunk_cap + j];
-          acc[i][0] = fmaf(pj, v.x, acc[i][0]);
-          acc[i][1] = fmaf(pj, v.y, acc[i][1]);
+      for (int qv = 0; qv < QVT; ++qv) {
+        if (qv < QV) {
+          float d = 0.f;
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) d = fmaf(q[qv][e], kf[e], d);
+#pragma unroll
+          for (int o = LPK / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+          if (valid && sub == (qv % LPK)) sm.s[qv][j] = (key <= pos0 + qv / G) ? d * sl2 : -INFINITY;
         }
       }
     }
+    __syncthreads();
+
+    // online softmax update, one warp per query vector
+    for (int qv = warp; qv < QV; qv += kWarps) {
+      float mx = -INFINITY;
+      for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sm.s[qv][j]);
+      mx = warp_max(mx);
+      const float m_old = sm.m[qv];
+      const float m_new = fmaxf(m_old, mx);
+      const float base_m = (m_new == -INFINITY) ? 0.f : m_new;
+      float sum = 0.f;
+      for (int j = lane; j < nk; j += 32) {
+        const float e = exp2f(sm.s[qv][j] - base_m);
+        sm.s[qv][j] = e;
+        sum += e;
+      }
+      sum = warp_sum(sum);
+      if (lane == 0) {
+        const float c = exp2f(m_old - base_m);
+        sm.corr[qv] = c;
+        sm.l[qv] = sm.l[qv] * c + sum;
+        sm.m[qv] = m_new;
+      }
+    }
+    __syncthreads();
+
+    // o[qv][d] = o * corr + sum_j p[qv][j] * v[j][d]; thread t owns dim
+    // d = t % 128 for the query vectors qv = t / 128 (mod 2)
+    {
+      constexpr int kHalf = (QVT + 1) / 2;
+      const int d = tid & 127;
+      const int q0 = tid >> 7;
+      float acc[kHalf];
 #pragma unroll
-    for (int i = 0; i < kMaxQV / 2; ++i) {
-      if (i < nq) {
+      for (int i = 0; i < kHalf; ++i) acc[i] = 0.f;
+      float acc2[kHalf];
+#pragma unroll
+      for (int i = 0; i < kHalf; ++i) acc2[i] = 0.f;
+      int j = 0;
+      for (; j + 1 < nk; j += 2) {  // two keys per step: independent FMA chains
+        const float v0 = __bfloat162float(sm.v[j * 128 + d]);
+        const float v1 = __bfloat162float(sm.v[(j + 1) * 128 + d]);
+#pragma unroll
+        for (int i = 0; i < kHalf; ++i) {
+          const int qv = q0 + 2 * i;
+          if (qv < QV) {
+            acc[i] = fmaf(sm.s[qv][j], v0, acc[i]);
+            acc2[i] = fmaf(sm.s[qv][j + 1], v1, acc2[i]);
+          }
+        }
+      }
+      if (j < nk) {
+        const float v0 = __bfloat162float(sm.v[j * 128 + d]);
+#pragma unroll
+        for (int i = 0; i < kHalf; ++i) {
+          const int qv = q0 + 2 * i;
+          if (qv < QV) acc[i] = fmaf(sm.s[qv][j], v0, acc[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kHalf; ++i) acc[i] += acc2[i];
+#pragma unroll
+      for (int i = 0; i < kHalf; ++i) {
         const int qv = q0 + 2 * i;
-        const int m = qv / G, gi = qv % G;
-        const int h = kvh * G + gi;
-        float* po = a.part_o + (((size_t)h * a.M + m) * splits + split) * 128;
-        po[d] = acc[i][0];
-        po[d + 1] = acc[i][1];
+        if (qv < QV) sm.o[qv][d] = sm.o[qv][d] * sm.corr[qv] + acc[i];
       }
     }
   }
-  if (tid < QV) {
-    const int m = tid / G, gi = tid % G;
-    const int h = kvh * G + gi;
-    float* pm = a.part_ml + (((size_t)h * a.M + m) * splits + split) * 2;
-    pm[0] = s_max[tid];
-    pm[1] = s_sum[tid];
-  }
 
-  // ---- last CTA of this kv head merges the splits ----
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const unsigned prev = atomicAdd(a.counters + kvh, 1u);
-    s_last = (prev == (unsigned)splits - 1);
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int idx = tid; idx < QV * 128; idx += kThreads) {
+  // ---- merge the S partials of this kv head through DSMEM ----
+  cluster.sync();
+  for (int idx = split * kThreads + tid; idx < QV * 128; idx += S * kThreads) {
     const int qv = idx >> 7, d = idx & 127;
-    const int m = qv / G, gi = qv % G;
-    const int h = kvh * G + gi;
-    const float* pm = a.part_ml + ((size_t)h * a.M + m) * splits * 2;
-    const float* po = a.part_o + ((size_t)h * a.M + m) * splits * 128;
-    float gmax = -INFINITY;
-    for (int s = 0; s < splits; ++s) gmax = fmaxf(gmax, __ldcg(pm + 2 * s));
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < splits; ++s) {
-      const float ms = __ldcg(pm + 2 * s);
-      if (ms == -INFINITY) continue;
-      const float w = exp2f(ms - gmax);
-      num += w * __ldcg(po + (size_t)s * 128 + d);
-      den += w * __ldcg(pm + 2 * s + 1);
+    // all peer loads are independent: issue them together (<= 16 peers)
+    float mr[16], lr[16], orr[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      if (r < S) {
+        const DecodeSmem* peer = cluster.map_shared_rank(&sm, r);
+        mr[r] = peer->m[qv];
+        lr[r] = peer->l[qv];
+        orr[r] = peer->o[qv][d];
+      }
     }
-    a.out[(size_t)m * a.n_heads * 128 + h * 128 + d] =
+    float gmax = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+      if (r < S) gmax = fmaxf(gmax, mr[r]);
+    float num = 0.f, den = 0.f;
+    if (gmax != -INFINITY) {
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        if (r < S && mr[r] != -INFINITY) {
+          const float w = exp2f(mr[r] - gmax);
+          num += w * orr[r];
+          den += w * lr[r];
+        }
+      }
+    }
+    const int m = qv / G, gi = qv % G;
+    a.out[(size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + d] =
         __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
   }
-  if (tid == 0) a.counters[kvh] = 0u;
+  cluster.sync();
+}
+
+int attention_decode_cluster(int cache_cap) {
+  // 16-CTA clusters (non-portable, supported by B200) when the context is long
+  // enough to give each CTA at least a sub-chunk; 8 otherwise.
+  return cache_cap > 8 * kSub ? 16 : 8;
 }
 
 cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
   const int G = a.n_heads / a.n_kv_heads;
-  if (a.M < 1 || a.M * G > kMaxQV || a.splits < 1) return cudaErrorInvalidValue;
-  // worst case keys per split given the cache capacity
-  const int chunk_cap = (a.cache_cap + a.M + a.splits - 1) / a.splits;
-  const size_t smem = (size_t)(a.M * G * 128 + a.M * G * chunk_cap) * sizeof(float);
-  if (smem > 220 * 1024) return cudaErrorInvalidValue;
-  ensure_smem_attr(attention_decode_kernel, 220 * 1024);
-  dim3 grid(a.n_kv_heads, a.splits);
-  attention_decode_kernel<<<grid, kThreads, smem, stream>>>(a, chunk_cap);
-  return cudaGetLastError();
+  if (a.M < 1 || a.M * G > kMaxQV) return cudaErrorInvalidValue;
+  const int S = a.splits;
+  if (S < 1 || S > 16) return cudaErrorInvalidValue;
+  // keys per CTA: the cache capacity split evenly (rounded to 16 keys)
+  int chunk = (a.cache_cap + a.M + S - 1) / S;
+  chunk = (chunk + 15) / 16 * 16;
+  const int smem = (int)sizeof(DecodeSmem);
+  const int qv = a.M * G;
+  auto kern = qv <= 4 ? attention_decode_kernel<4>
+            : qv <= 8 ? attention_decode_kernel<8>
+            : qv <= 16 ? attention_decode_kernel<16> : attention_decode_kernel<32>;
+  ensure_smem_attr(kern, smem);
+  {
+    static const void* nonportable_done[8] = {nullptr};
+    bool done = false;
+    for (auto* p : nonportable_done) done |= (p == reinterpret_cast<const void*>(kern));
+    if (!done) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      for (auto*& p : nonportable_done)
+        if (p == nullptr) { p = reinterpret_cast<const void*>(kern); break; }
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(S, a.n_kv_heads, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, a, chunk);
 }
 
 }  // namespace sc

@@ -304,8 +304,7 @@ void attention_prefill(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tens
 }
 
 void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int64_t n_heads,
-                      double scale, int64_t splits, Tensor part_o, Tensor part_ml,
-                      Tensor counters, Tensor out) {
+                      double scale, int64_t splits, Tensor out) {
   const c10::cuda::CUDAGuard guard(q.device());
   CHECK_BF16(q); CHECK_BF16(out); CHECK_I32(pos);
   TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(2) == 128 && k_cache.is_contiguous(), "k_cache");
@@ -320,11 +319,6 @@ void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int6
   a.n_kv_heads = (int)k_cache.size(0);
   a.scale = (float)scale;
   a.splits = (int)splits;
-  TORCH_CHECK(part_o.numel() >= n_heads * a.M * splits * 128, "part_o too small");
-  TORCH_CHECK(part_ml.numel() >= n_heads * a.M * splits * 2, "part_ml too small");
-  a.part_o = part_o.data_ptr<float>();
-  a.part_ml = part_ml.data_ptr<float>();
-  a.counters = reinterpret_cast<unsigned int*>(counters.data_ptr<int>());
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   check_cuda(sc::attention_decode(a, cur_stream()), "attention_decode");
 }
@@ -455,6 +449,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_argmax_grid", &gemv_argmax_grid);
   m.def("attention_prefill", &attention_prefill);
   m.def("attention_decode", &attention_decode);
+  m.def("attention_decode_cluster", [](int64_t cap) { return sc::attention_decode_cluster((int)cap); });
   m.def("rmsnorm", &rmsnorm);
   m.def("embedding", &embedding);
   m.def("gather_rows", &gather_rows);

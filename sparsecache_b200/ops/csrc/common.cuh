@@ -302,6 +302,16 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute may start while its predecessor drains.
+// Everything before pdl_wait() must not read data the predecessor writes
+// (weights are fine); pdl_wait() returns once the predecessor has completed
+// and its memory is visible.  Both are no-ops without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -326,16 +336,28 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
 }  // namespace sc
 
 namespace sc {
-// Raise a kernel's dynamic shared-memory limit once per device (not on every
-// launch: the attribute call is host work and must stay out of graph capture).
+// Raise a kernel's dynamic shared-memory limit once per (kernel, device)
+// rather than on every launch: the attribute call is host work and must stay
+// out of CUDA-graph capture.  Keyed by the kernel's address (template
+// instantiations share a signature but are distinct kernels).
 template <typename F>
 inline void ensure_smem_attr(F* func, int bytes) {
-  static int set_bytes[64] = {0};
+  struct Entry { const void* fn; int dev; int bytes; };
+  static Entry table[256];
+  static int used = 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && set_bytes[dev] < bytes) {
-    cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    set_bytes[dev] = bytes;
+  const void* key = reinterpret_cast<const void*>(func);
+  for (int i = 0; i < used; ++i) {
+    if (table[i].fn == key && table[i].dev == dev) {
+      if (table[i].bytes < bytes) {
+        cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        table[i].bytes = bytes;
+      }
+      return;
+    }
   }
+  cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (used < 256) table[used++] = Entry{key, dev, bytes};
 }
 }  // namespace sc

@@ -28,7 +28,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kUnroll = 4;
+constexpr int kUnroll = 8;
 
 __device__ __forceinline__ float dot8(const uint4 w, const uint4 x) {
   float2 w0 = unpack_bf16x2(w.x), w1 = unpack_bf16x2(w.y), w2 = unpack_bf16x2(w.z),
@@ -62,6 +62,21 @@ __device__ __forceinline__ void pair_rows(int epi, int p, int& r0, int& r1) {
   }
 }
 
+__device__ __forceinline__ void load_batch(const uint4* w0, const uint4* w1, int c0, int nchunk,
+                                           uint4 (&wa)[kUnroll], uint4 (&wb)[kUnroll]) {
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) {
+    const int c = c0 + u * 32;
+    if (c < nchunk) {
+      wa[u] = ld_stream_u4(w0 + c);
+      wb[u] = ld_stream_u4(w1 + c);
+    } else {
+      wa[u] = make_uint4(0, 0, 0, 0);
+      wb[u] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
 }  // namespace
 
 template <int MR>
@@ -77,6 +92,23 @@ __global__ void __launch_bounds__(kThreads)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = a.K;
   const int M = a.M;
+  const int n_pairs = a.N / 2;
+  const int nchunk = K / 8;
+
+  // Prefetch this warp's first weight batch before waiting on the previous
+  // kernel: weights never depend on it, so the prologue below overlaps HBM.
+  uint4 wa[kUnroll], wb[kUnroll];
+  const int first_p = blockIdx.x * kWarps + warp;
+  if (first_p < n_pairs) {
+    int r0, r1;
+    pair_rows(a.epi, first_p, r0, r1);
+    load_batch(reinterpret_cast<const uint4*>(a.w + (size_t)r0 * K),
+               reinterpret_cast<const uint4*>(a.w + (size_t)r1 * K), lane, nchunk, wa, wb);
+  }
+  pdl_wait();
+  // Dependents may launch once this kernel has passed its own wait: anything
+  // they read before their wait was written at least two kernels back.
+  pdl_launch_dependents();
 
   // ---- stage x (optionally RMS-normalised) into shared memory ----
   if (a.norm_w == nullptr) {
@@ -133,8 +165,6 @@ __global__ void __launch_bounds__(kThreads)
   }
   __syncthreads();
 
-  const int n_pairs = a.N / 2;
-  const int nchunk = K / 8;
   const uint4* xs4 = reinterpret_cast<const uint4*>(xs);
   const int pos0 = (a.epi == GEMV_QKV) ? *a.pos : 0;
 
@@ -143,7 +173,8 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
   for (int m = 0; m < MR; ++m) best_v[m] = -INFINITY, best_i[m] = 0x7fffffff;
 
-  for (int p = blockIdx.x * kWarps + warp; p < n_pairs; p += gridDim.x * kWarps) {
+  bool preloaded = true;
+  for (int p = first_p; p < n_pairs; p += gridDim.x * kWarps) {
     int r0, r1;
     pair_rows(a.epi, p, r0, r1);
     const uint4* w0 = reinterpret_cast<const uint4*>(a.w + (size_t)r0 * K);
@@ -152,18 +183,8 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int m = 0; m < MR; ++m) acc0[m] = acc1[m] = 0.f;
     for (int c0 = lane; c0 < nchunk; c0 += 32 * kUnroll) {
-      uint4 wa[kUnroll], wb[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int c = c0 + u * 32;
-        if (c < nchunk) {
-          wa[u] = ld_stream_u4(w0 + c);
-          wb[u] = ld_stream_u4(w1 + c);
-        } else {
-          wa[u] = make_uint4(0, 0, 0, 0);
-          wb[u] = make_uint4(0, 0, 0, 0);
-        }
-      }
+      if (!preloaded) load_batch(w0, w1, c0, nchunk, wa, wb);
+      preloaded = false;
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
         const int c = c0 + u * 32;
@@ -314,17 +335,27 @@ cudaError_t gemv_bf16(const GemvArgs& a, cudaStream_t stream) {
   int grid = (n_pairs + kWarps - 1) / kWarps;
   const int cap = (a.num_sms > 0 ? a.num_sms : 148) * 8;
   if (grid > cap) grid = cap;
-#define SC_LAUNCH_GEMV(MRV)                                                              \
-  {                                                                                      \
-    ensure_smem_attr(gemv_kernel<MRV>, 200 * 1024);                                       \
-    gemv_kernel<MRV><<<grid, kThreads, smem, stream>>>(a);                               \
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+#define SC_LAUNCH_GEMV(MRV)                                        \
+  {                                                                \
+    ensure_smem_attr(gemv_kernel<MRV>, 200 * 1024);                \
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<MRV>, a);          \
   }
   if (a.M == 1) SC_LAUNCH_GEMV(1)
   else if (a.M <= 2) SC_LAUNCH_GEMV(2)
   else if (a.M <= 4) SC_LAUNCH_GEMV(4)
   else SC_LAUNCH_GEMV(8)
 #undef SC_LAUNCH_GEMV
-  return cudaGetLastError();
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace sc

@@ -129,14 +129,12 @@ struct AttnDecodeArgs {
   const int* pos;  // device scalar: position of query row 0; row m sees keys [0, pos+m]
   int n_heads, n_kv_heads;
   float scale;
-  int splits;
-  float* part_o;     // [n_heads, M, splits, 128]
-  float* part_ml;    // [n_heads, M, splits, 2]
-  unsigned int* counters;  // [n_kv_heads], zero on entry, restored to zero
+  int splits;  // CTAs per kv head = thread-block cluster size (1..16)
   __nv_bfloat16* out;  // [M, n_heads*128]
 };
 
 cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream);
+int attention_decode_cluster(int cache_cap);
 
 // ------------------------------------------------------------ pointwise ----
 cudaError_t rmsnorm_bf16(const __nv_bfloat16* x, int ldx, const int* rows, const __nv_bfloat16* w,

@@ -104,11 +104,10 @@ def make_requests(spec: WorkloadSpec | str, config: ModelConfig, *, seed: int | 
         return max(mn, min(mx, n))
 
     n_slots = spec.n_samples * spec.docs_per_sample
-    if spec.repeat_uses is not None:
-        repeats = set(rng.sample(range(1, n_slots), spec.repeat_uses))
-    else:
-        frac = spec.repeat_fraction or 0.0
-        repeats = {s for s in range(1, n_slots) if rng.random() < frac}
+    n_repeats = spec.repeat_uses
+    if n_repeats is None:
+        n_repeats = int(round((spec.repeat_fraction or 0.0) * n_slots))
+    repeats = set(rng.sample(range(1, n_slots), min(n_repeats, n_slots - 1)))
     unique: list[tuple[int, ...]] = []
     requests = []
     slot = 0

@@ -37,11 +37,11 @@ def test_prefill_matches_oracle(setup):
     cfg, oracle, engine, store, requests, server = setup
     req = requests[0]
     ids = torch.tensor(req.prompt, dtype=torch.int32, device=engine.device)
-    slot = engine.new_slot(1024)
+    slot = engine.new_slot(2048)
     h = engine.prefill(ids, slot)
     torch.cuda.synchronize()
     hidden, cache = oracle.forward_tokens(torch.tensor(req.prompt), torch.arange(len(req.prompt)))
-    assert _rel(h, hidden[0]) < 5e-2
+    assert _rel(h.cpu(), hidden[0]) < 5e-2
     T = len(req.prompt)
     for layer in range(cfg.n_layers):
         assert _rel(slot.k(layer)[:, :T].cpu(), cache[layer][0][0]) < 5e-2

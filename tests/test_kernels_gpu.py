@@ -167,20 +167,15 @@ def test_attention_decode(cuda_device, M):
     vc = torch.randn(Hkv, cap, 128, device=cuda_device).to(torch.bfloat16)
     q = torch.randn(M, H * 128, device=cuda_device).to(torch.bfloat16)
     pos = torch.tensor([pos0], device=cuda_device, dtype=torch.int32)
-    splits = 16
-    part_o = torch.empty(H * M * splits * 128, device=cuda_device)
-    part_ml = torch.empty(H * M * splits * 2, device=cuda_device)
-    counters = torch.zeros(Hkv, device=cuda_device, dtype=torch.int32)
-    out = torch.empty(M, H * 128, device=cuda_device, dtype=torch.bfloat16)
-    for _ in range(2):  # second call checks the counters were reset
-        _ext().attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), splits, part_o, part_ml, counters, out)
-    torch.cuda.synchronize()
     n = pos0 + M
     kpos = torch.arange(n, device=cuda_device)
     qpos = pos0 + torch.arange(M, device=cuda_device)
     ref = _attn_reference(q, kc[:, :n], vc[:, :n], qpos, kpos, H)
-    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
-    assert int(counters.abs().sum()) == 0
+    for splits in (1, 8, 16):  # cluster sizes, incl. CTAs whose chunk is past the last key
+        out = torch.empty(M, H * 128, device=cuda_device, dtype=torch.bfloat16)
+        _ext().attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), splits, out)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
 
 
 def _rms_ref(x, w, eps):
