@@ -359,3 +359,90 @@ cudaError_t gemv_bf16(const GemvArgs& a, cudaStream_t stream) {
 }
 
 }  // namespace sc
+
+// ===========================================================================
+// Allocation-free entry point (declared in no_alloc.h; no counterpart in the
+// reference).  The LM-head/argmax kernel above needs scratch for its per-CTA
+// (max, index) partials and its completion counter; here that scratch is a
+// fixed-size file-scope device array instead of caller-provided buffers, for
+// callers that cannot allocate device memory.
+// ===========================================================================
+#include "no_alloc.h"
+
+namespace sc {
+namespace {
+
+struct NoAllocScratch {
+  float part_val[SC_NOALLOC_MAX_PARTIALS];
+  int part_idx[SC_NOALLOC_MAX_PARTIALS];
+  unsigned int counter;
+};
+
+// One copy per device that loads the library (~129 KiB), alive until exit.
+static __device__ __align__(256) NoAllocScratch g_noalloc_scratch;
+
+// Device address of g_noalloc_scratch, looked up once per device.  In host
+// code the symbol itself is only a host-side stand-in, never a device
+// address, so it is never passed to a kernel directly.
+NoAllocScratch* g_noalloc_ptr[64] = {nullptr};
+
+}  // namespace
+}  // namespace sc
+
+extern "C" __attribute__((visibility("default"))) const char* sc_noalloc_error_string(int code) {
+  switch (code) {
+    case SC_NOALLOC_OK: return "ok";
+    case SC_NOALLOC_EBADSHAPE:
+      return "shape outside the limits: 1 <= M <= 8, K % 8 == 0, N even, M*K*2 <= 200 KiB";
+    case SC_NOALLOC_ETOOLARGE: return "launch grid * M exceeds the fixed scratch (16384 partials)";
+    case SC_NOALLOC_ESYMBOL: return "cudaGetSymbolAddress of the scratch array failed";
+    case SC_NOALLOC_ELAUNCH: return "memset of the counter or kernel launch failed";
+  }
+  return "unknown error code";
+}
+
+extern "C" __attribute__((visibility("default"))) int sc_lm_head_argmax_noalloc(
+    const void* x, const void* w, const void* norm_w, float eps, int M, int N, int K,
+    int* out_token, cudaStream_t stream) {
+  using namespace sc;
+  if (M < 1 || M > SC_NOALLOC_MAX_ROWS || K < 8 || (K % 8) != 0 || N < 2 || (N % 2) != 0 ||
+      (size_t)M * K * 2 > 200 * 1024)
+    return SC_NOALLOC_EBADSHAPE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SC_NOALLOC_ESYMBOL;
+  // Set-up on the first call on this device (the device is current here).
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
+      return SC_NOALLOC_ESYMBOL;
+    g_noalloc_ptr[dev] = reinterpret_cast<NoAllocScratch*>(p);
+  }
+  NoAllocScratch* scratch = g_noalloc_ptr[dev];
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    sms = 148;
+  int grid = (N / 2 + kWarps - 1) / kWarps;
+  if (grid > sms * 8) grid = sms * 8;
+  if ((long long)grid * M > SC_NOALLOC_MAX_PARTIALS) return SC_NOALLOC_ETOOLARGE;
+
+  // The completion counter must start at zero; the partials are overwritten.
+  if (cudaMemsetAsync(&scratch->counter, 0, sizeof(unsigned int), stream) != cudaSuccess)
+    return SC_NOALLOC_ELAUNCH;
+  GemvArgs a{};
+  a.w = reinterpret_cast<const __nv_bfloat16*>(w);
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x);
+  a.ldx = K;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w);
+  a.eps = eps;
+  a.epi = GEMV_ARGMAX;
+  a.part_val = scratch->part_val;
+  a.part_idx = scratch->part_idx;
+  a.counter = &scratch->counter;
+  a.out_token = out_token;
+  a.num_sms = sms;
+  if (gemv_bf16(a, stream) != cudaSuccess) return SC_NOALLOC_ELAUNCH;
+  return SC_NOALLOC_OK;
+}
