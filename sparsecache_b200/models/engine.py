@@ -354,25 +354,30 @@ class B200Engine:
 
     # ------------------------------------------------------------ decode
     MAX_DECODE_TOKENS = 8192
+    MAX_ROWS = 8
 
-    def _decode_buffers(self, max_new: int):
-        # Fixed sizes: captured decode graphs hold these addresses.
+    def _decode_buffers(self, max_new: int = 0):
+        """Fixed-size decode state (captured decode graphs hold these addresses).
+
+        ``pos`` holds the device scalars [rope position, cache slot, virtual
+        key count, spare] of the next row; the LM-head kernel advances them.
+        """
         if max_new > self.MAX_DECODE_TOKENS:
             raise ValueError(f"max_new_tokens above {self.MAX_DECODE_TOKENS}")
-        cfg = self.cfg
-        ws = self.ws
+        cfg, ws, R = self.cfg, self.ws, self.MAX_ROWS
         grid = self.ext.gemv_argmax_grid(cfg.vocab)
         return {
-            "h": ws.get("dec_h", (1, cfg.d_model), torch.bfloat16),
-            "q": ws.get("dec_q", (1, cfg.q_size), torch.bfloat16),
-            "attn": ws.get("dec_attn", (1, cfg.q_size), torch.bfloat16),
-            "act": ws.get("dec_act", (1, cfg.ffn), torch.bfloat16),
-            "pos": ws.get("dec_pos", (1,), torch.int32),
-            "tok": ws.get("dec_tok", (8,), torch.int32),
+            "h": ws.get("dec_h", (R, cfg.d_model), torch.bfloat16),
+            "q": ws.get("dec_q", (R, cfg.q_size), torch.bfloat16),
+            "attn": ws.get("dec_attn", (R, cfg.q_size), torch.bfloat16),
+            "act": ws.get("dec_act", (R, cfg.ffn), torch.bfloat16),
+            "pos": ws.get("dec_pos", (4,), torch.int32),
+            "tok": ws.get("dec_tok", (R,), torch.int32),
+            "ids": ws.get("dec_ids", (R,), torch.int32),
             "log": ws.get("dec_log", (self.MAX_DECODE_TOKENS,), torch.int32),
             "gen": ws.get("dec_gen", (1,), torch.int32),
-            "pv": ws.get("dec_pv", (8 * grid,), torch.float32),
-            "pi": ws.get("dec_pi", (8 * grid,), torch.int32),
+            "pv": ws.get("dec_pv", (R * grid,), torch.float32),
+            "pi": ws.get("dec_pi", (R * grid,), torch.int32),
             "counter": ws.get("dec_counter", (1,), torch.int32),
         }
 
@@ -380,54 +385,80 @@ class B200Engine:
         """CTAs per kv head (= thread-block cluster size) of the decode attention."""
         return int(self.ext.attention_decode_cluster(capacity))
 
+    def set_decode_state(self, *, position: int, slot: int | None = None, n_virtual: int | None = None) -> None:
+        """Host-side set of the device scalars (stream-ordered, before a step)."""
+        b = self._decode_buffers()
+        vals = torch.tensor([position, position if slot is None else slot,
+                             (position if n_virtual is None else n_virtual), 0], dtype=torch.int32)
+        b["pos"].copy_(vals.pin_memory(), non_blocking=True)
+
     def first_token(self, hidden_row: torch.Tensor, *, position: int, max_new: int) -> dict:
         """LM head + argmax on the last prompt row; seeds the device-side decode state."""
         b = self._decode_buffers(max_new)
         b["gen"].zero_()
         b["counter"].zero_()
-        b["pos"].fill_(position)
+        self.set_decode_state(position=position)
         self.ext.gemv_argmax(hidden_row, self.w.lm_head, self.w.norm, self.cfg.rms_eps, b["pv"], b["pi"],
                              b["counter"], b["tok"], b["log"], b["gen"], self.w.embed, b["h"], None)
         return b
 
-    def _decode_step(self, slot: KVSlot, b: dict, splits: int) -> None:
+    def _forward_rows(self, slot: KVSlot, b: dict, M: int, splits: int, *, view: torch.Tensor | None,
+                      log: bool, feedback: bool) -> None:
+        """One forward of the M rows in b['h'][:M] at the device positions in b['pos'].
+
+        With ``view`` (an int32 slot map of the slot), attention reads the
+        virtual key sequence view[0 : pos[2]] and the new rows are written to
+        cache slots pos[1].. (RoPE positions pos[0]..); otherwise slot ==
+        position and keys are [0, pos[0] + M).
+        """
         cfg, ext = self.cfg, self.ext
         H = cfg.n_heads
-        h = b["h"]
+        h = b["h"][:M]
+        pos = b["pos"]
         for layer, lw in enumerate(self.w.layers):
-            ext.gemv_qkv(h, lw.w_qkv, lw.ln1, cfg.rms_eps, b["q"], slot.k(layer), slot.v(layer), b["pos"],
-                         self.rope, cfg.n_heads, cfg.n_kv_heads)
-            ext.attention_decode(b["q"], slot.k(layer), slot.v(layer), b["pos"], H, self.scale, splits, b["attn"])
-            ext.gemv_residual(b["attn"], lw.w_o, None, cfg.rms_eps, h, h)
-            ext.gemv_swiglu(h, lw.w_gu, lw.ln2, cfg.rms_eps, b["act"])
-            ext.gemv_residual(b["act"], lw.w_down, None, cfg.rms_eps, h, h)
+            ext.gemv_qkv(h, lw.w_qkv, lw.ln1, cfg.rms_eps, b["q"][:M], slot.k(layer), slot.v(layer), pos[0:1],
+                         self.rope, cfg.n_heads, cfg.n_kv_heads, slot=pos[1:2])
+            ext.attention_decode(b["q"][:M], slot.k(layer), slot.v(layer), pos[0:1], H, self.scale, splits,
+                                 b["attn"][:M], page_table=view, page_shift=0,
+                                 n_virtual=pos[2:3] if view is not None else None)
+            ext.gemv_residual(b["attn"][:M], lw.w_o, None, cfg.rms_eps, h, h)
+            ext.gemv_swiglu(h, lw.w_gu, lw.ln2, cfg.rms_eps, b["act"][:M])
+            ext.gemv_residual(b["act"][:M], lw.w_down, None, cfg.rms_eps, h, h)
         ext.gemv_argmax(h, self.w.lm_head, self.w.norm, cfg.rms_eps, b["pv"], b["pi"], b["counter"], b["tok"],
-                        b["log"], b["gen"], self.w.embed, h, b["pos"])
+                        b["log"] if log else None, b["gen"] if log else None,
+                        self.w.embed if feedback else None, b["h"][0:1] if feedback else None,
+                        pos, 3)
 
-    def decode(self, slot: KVSlot, n_steps: int, *, max_new: int, use_graph: bool = True) -> None:
-        """Run ``n_steps`` greedy decode steps from the state ``first_token`` left."""
+    def decode(self, slot: KVSlot, n_steps: int, *, max_new: int, use_graph: bool = True,
+               view: torch.Tensor | None = None) -> None:
+        """Run ``n_steps`` greedy decode steps from the device state.
+
+        Each step feeds back the previous argmax (its embedding is already in
+        h[0]), logs the new token and advances the device scalars.  With a
+        ``view`` the steps attend through the slot map (progressive drafting).
+        """
         if n_steps <= 0:
             return
         splits = self._decode_splits(slot.capacity)
         b = self._decode_buffers(max_new)
         if not use_graph:
             for _ in range(n_steps):
-                self._decode_step(slot, b, splits)
+                self._forward_rows(slot, b, 1, splits, view=view, log=True, feedback=True)
             return
-        key = (id(slot), splits, max_new)
+        key = (id(slot), splits, None if view is None else view.data_ptr())
         graph = self._graphs.get(key)
         if graph is None:
             # one eager step warms up launch attributes; then capture a step
-            # against a scratch copy of the device state so the real state is
+            # against a snapshot of the device state so the real state is
             # only advanced by replays.
             saved = {k: b[k].clone() for k in ("h", "pos", "gen", "log", "tok")}
-            self._decode_step(slot, b, splits)
+            self._forward_rows(slot, b, 1, splits, view=view, log=True, feedback=True)
             for k, v in saved.items():
                 b[k].copy_(v)
             torch.cuda.synchronize(self.device)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                self._decode_step(slot, b, splits)
+                self._forward_rows(slot, b, 1, splits, view=view, log=True, feedback=True)
             for k, v in saved.items():
                 b[k].copy_(v)
             self._graphs[key] = graph
@@ -435,6 +466,27 @@ class B200Engine:
             graph.replay()
         # every replay launches the captured kernels: 5 per layer + LM head
         self.ext.launches += n_steps * (5 * self.cfg.n_layers + 1)
+
+    def verify(self, slot: KVSlot, tokens: torch.Tensor, *, position: int, slot_start: int | None = None,
+               view: torch.Tensor | None = None, n_visible: int | None = None) -> torch.Tensor:
+        """Batched verifier: forward M <= 8 tokens at positions position.. in one pass.
+
+        Writes their K/V (cache slots slot_start.., default = positions) and
+        returns the device int32 argmax prediction after every row (the
+        target's next token given the prefix through that row).  With a
+        ``view`` the keys are view[0 : n_visible] followed by the M new rows.
+        """
+        M = int(tokens.numel())
+        if not 1 <= M <= self.MAX_ROWS:
+            raise ValueError("verify handles 1..8 tokens")
+        b = self._decode_buffers()
+        splits = self._decode_splits(slot.capacity)
+        b["ids"][:M].copy_(tokens.to(torch.int32), non_blocking=True)
+        self.ext.embedding(b["ids"][:M], self.w.embed, b["h"][:M])
+        nv = None if view is None else int(n_visible) + M
+        self.set_decode_state(position=position, slot=slot_start, n_virtual=nv)
+        self._forward_rows(slot, b, M, splits, view=view, log=False, feedback=False)
+        return b["tok"][:M]
 
     def generated_tokens(self, max_new: int) -> torch.Tensor:
         """Device view of the token log (first ``max_new`` entries)."""

@@ -32,6 +32,7 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kSub = 128;     // keys per staged sub-chunk
 constexpr int kMaxQV = 32;    // M * G
+constexpr int kMaxRows = 8;   // largest query block M
 constexpr int kRow = 256;     // bytes per K/V row (128 bf16)
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
@@ -69,8 +70,12 @@ __global__ void __launch_bounds__(kThreads)
   // back (the LM-head kernel of the previous step and earlier QKV kernels),
   // so they are read before the programmatic wait; q and the M new rows come
   // from the QKV kernel right before this one and are read after it.
-  const int pos0 = *a.pos;
-  const int n_keys = pos0 + a.M;
+  const int n_keys = a.n_virtual != nullptr ? *a.n_virtual : *a.pos + a.M;
+  const int pos0 = n_keys - a.M;  // virtual index of query row 0
+  const int page_mask = (1 << a.page_shift) - 1;
+  auto phys = [&](int v) -> int {
+    return a.page_table != nullptr ? (a.page_table[v >> a.page_shift] << a.page_shift) + (v & page_mask) : v;
+  };
   const int k_begin = split * chunk;
   const int k_end = min(n_keys, k_begin + chunk);
   const float sl2 = a.scale * 1.4426950408889634f;
@@ -85,7 +90,7 @@ __global__ void __launch_bounds__(kThreads)
       const int key = base + r;
       const bool in = r < nk;
       if (in ? (key < lo || key >= hi) : !zero_tail) continue;
-      const size_t off = (size_t)(in ? key : 0) * 128 + c * 8;
+      const size_t off = (size_t)(in ? phys(key) : 0) * 128 + c * 8;
       cp_async16(sk + r * kRow + c * 16, kb + off, in);
       cp_async16(sv + r * kRow + c * 16, vb + off, in);
     }
@@ -273,8 +278,10 @@ cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
   if (a.M < 1 || a.M * G > kMaxQV) return cudaErrorInvalidValue;
   const int S = a.splits;
   if (S < 1 || S > 16) return cudaErrorInvalidValue;
-  // keys per CTA: the cache capacity split evenly (rounded to 16 keys)
-  int chunk = (a.cache_cap + a.M + S - 1) / S;
+  // keys per CTA: the cache capacity (+ the largest row block) split evenly,
+  // rounded to 16 keys; independent of M so a row sees the same split
+  // boundaries (and the same rounding) in decode and in batched verification
+  int chunk = (a.cache_cap + kMaxRows + S - 1) / S;
   chunk = (chunk + 15) / 16 * 16;
   const int smem = (int)sizeof(DecodeSmem);
   const int qv = a.M * G;

@@ -210,7 +210,7 @@ void gemv_swiglu(Tensor x, Tensor w_gu, c10::optional<Tensor> norm_w, double eps
 
 void gemv_qkv(Tensor x, Tensor w_qkv, c10::optional<Tensor> norm_w, double eps, Tensor q_out,
               Tensor k_cache, Tensor v_cache, Tensor pos, Tensor rope_table, int64_t n_q_heads,
-              int64_t n_kv_heads) {
+              int64_t n_kv_heads, c10::optional<Tensor> slot) {
   const c10::cuda::CUDAGuard guard(x.device());
   auto g = base_gemv(x, w_qkv, norm_w, eps, sc::GEMV_QKV);
   CHECK_I32(pos); CHECK_F32(rope_table);
@@ -222,6 +222,10 @@ void gemv_qkv(Tensor x, Tensor w_qkv, c10::optional<Tensor> norm_w, double eps, 
   g.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
   g.cache_cap = (int)k_cache.size(1);
   g.pos = pos.data_ptr<int>();
+  if (slot.has_value() && slot->defined()) {
+    CHECK_I32(*slot);
+    g.slot = slot->data_ptr<int>();
+  }
   g.rope_table = reinterpret_cast<const float2*>(rope_table.data_ptr<float>());
   g.n_q_heads = (int)n_q_heads;
   g.n_kv_heads = (int)n_kv_heads;
@@ -239,7 +243,7 @@ void gemv_argmax(Tensor x, Tensor w, c10::optional<Tensor> norm_w, double eps, T
                  Tensor part_idx, Tensor counter, Tensor out_token,
                  c10::optional<Tensor> token_log, c10::optional<Tensor> gen_count,
                  c10::optional<Tensor> embed, c10::optional<Tensor> next_hidden,
-                 c10::optional<Tensor> pos_advance) {
+                 c10::optional<Tensor> pos_advance, int64_t n_advance) {
   const c10::cuda::CUDAGuard guard(x.device());
   auto g = base_gemv(x, w, norm_w, eps, sc::GEMV_ARGMAX);
   CHECK_F32(part_val); CHECK_I32(part_idx); CHECK_I32(out_token);
@@ -260,7 +264,12 @@ void gemv_argmax(Tensor x, Tensor w, c10::optional<Tensor> norm_w, double eps, T
     g.embed = reinterpret_cast<const __nv_bfloat16*>(embed->data_ptr());
     g.next_hidden = reinterpret_cast<__nv_bfloat16*>(next_hidden->data_ptr());
   }
-  if (pos_advance.has_value() && pos_advance->defined()) g.pos_advance = pos_advance->data_ptr<int>();
+  if (pos_advance.has_value() && pos_advance->defined()) {
+    CHECK_I32(*pos_advance);
+    TORCH_CHECK(pos_advance->numel() >= std::max<int64_t>(1, n_advance), "pos_advance too short");
+    g.pos_advance = pos_advance->data_ptr<int>();
+    g.n_advance = (int)n_advance;
+  }
   run_gemv(g);
 }
 
@@ -304,7 +313,8 @@ void attention_prefill(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tens
 }
 
 void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int64_t n_heads,
-                      double scale, int64_t splits, Tensor out) {
+                      double scale, int64_t splits, Tensor out, c10::optional<Tensor> page_table,
+                      int64_t page_shift, c10::optional<Tensor> n_virtual) {
   const c10::cuda::CUDAGuard guard(q.device());
   CHECK_BF16(q); CHECK_BF16(out); CHECK_I32(pos);
   TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(2) == 128 && k_cache.is_contiguous(), "k_cache");
@@ -320,6 +330,15 @@ void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int6
   a.scale = (float)scale;
   a.splits = (int)splits;
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  if (page_table.has_value() && page_table->defined()) {
+    CHECK_I32(*page_table);
+    a.page_table = page_table->data_ptr<int>();
+    a.page_shift = (int)page_shift;
+  }
+  if (n_virtual.has_value() && n_virtual->defined()) {
+    CHECK_I32(*n_virtual);
+    a.n_virtual = n_virtual->data_ptr<int>();
+  }
   check_cuda(sc::attention_decode(a, cur_stream()), "attention_decode");
 }
 
@@ -444,11 +463,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_store", &gemv_store);
   m.def("gemv_residual", &gemv_residual);
   m.def("gemv_swiglu", &gemv_swiglu);
-  m.def("gemv_qkv", &gemv_qkv);
-  m.def("gemv_argmax", &gemv_argmax);
+  m.def("gemv_qkv", &gemv_qkv, py::arg("x"), py::arg("w_qkv"), py::arg("norm_w"), py::arg("eps"),
+        py::arg("q_out"), py::arg("k_cache"), py::arg("v_cache"), py::arg("pos"), py::arg("rope_table"),
+        py::arg("n_q_heads"), py::arg("n_kv_heads"), py::arg("slot") = py::none());
+  m.def("gemv_argmax", &gemv_argmax, py::arg("x"), py::arg("w"), py::arg("norm_w"), py::arg("eps"),
+        py::arg("part_val"), py::arg("part_idx"), py::arg("counter"), py::arg("out_token"),
+        py::arg("token_log"), py::arg("gen_count"), py::arg("embed"), py::arg("next_hidden"),
+        py::arg("pos_advance"), py::arg("n_advance") = 1);
   m.def("gemv_argmax_grid", &gemv_argmax_grid);
   m.def("attention_prefill", &attention_prefill);
-  m.def("attention_decode", &attention_decode);
+  m.def("attention_decode", &attention_decode, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("pos"), py::arg("n_heads"), py::arg("scale"), py::arg("splits"), py::arg("out"),
+        py::arg("page_table") = py::none(), py::arg("page_shift") = 6, py::arg("n_virtual") = py::none());
   m.def("attention_decode_cluster", [](int64_t cap) { return sc::attention_decode_cluster((int)cap); });
   m.def("rmsnorm", &rmsnorm);
   m.def("embedding", &embedding);

@@ -167,6 +167,7 @@ __global__ void __launch_bounds__(kThreads)
 
   const uint4* xs4 = reinterpret_cast<const uint4*>(xs);
   const int pos0 = (a.epi == GEMV_QKV) ? *a.pos : 0;
+  const int slot0 = (a.epi == GEMV_QKV) ? (a.slot != nullptr ? *a.slot : pos0) : 0;
 
   float best_v[MR];
   int best_i[MR];
@@ -244,7 +245,7 @@ __global__ void __launch_bounds__(kThreads)
             dst = a.q_out + (size_t)m * a.ldq + head * 128;
           } else {
             const int kvh = is_k ? head - a.n_q_heads : head - a.n_q_heads - a.n_kv_heads;
-            dst = (is_k ? a.k_cache : a.v_cache) + ((size_t)kvh * a.cache_cap + pos) * 128;
+            dst = (is_k ? a.k_cache : a.v_cache) + ((size_t)kvh * a.cache_cap + slot0 + m) * 128;
           }
           dst[i] = __float2bfloat16_rn(o0);
           dst[i + 64] = __float2bfloat16_rn(o1);
@@ -317,7 +318,10 @@ __global__ void __launch_bounds__(kThreads)
       a.token_log[n] = last_tok;
       *a.gen_count = n + 1;
     }
-    if (a.pos_advance != nullptr) *a.pos_advance += M;
+    if (a.pos_advance != nullptr) {
+      const int n = a.n_advance > 0 ? a.n_advance : 1;
+      for (int i = 0; i < n; ++i) a.pos_advance[i] += M;
+    }
     *a.counter = 0u;
   }
   if (a.embed != nullptr) {

@@ -83,6 +83,7 @@ struct GemvArgs {
   __nv_bfloat16* v_cache;
   int cache_cap;
   const int* pos;  // device scalar: position of row 0 (row m at pos + m)
+  const int* slot; // optional device scalar: cache slot of row 0 (default: *pos)
   const float2* rope_table;
   int n_q_heads, n_kv_heads;
   // ARGMAX (LM head)
@@ -94,7 +95,8 @@ struct GemvArgs {
   int* gen_count;      // device scalar advanced by one per call when token_log is set
   const __nv_bfloat16* embed;  // optional: writes embed[token] of the last row to next_hidden
   __nv_bfloat16* next_hidden;
-  int* pos_advance;    // optional device scalar incremented by M at the end
+  int* pos_advance;    // optional device scalars [n_advance] each incremented by M at the end
+  int n_advance;       // number of scalars at pos_advance (0 means 1)
   int num_sms;
 };
 
@@ -127,6 +129,14 @@ struct AttnDecodeArgs {
   const __nv_bfloat16* v_cache;
   int cache_cap;
   const int* pos;  // device scalar: position of query row 0; row m sees keys [0, pos+m]
+  // Optional paged view: virtual key v lives in physical slot
+  // (page_table[v >> page_shift] << page_shift) + (v & page_mask); the view
+  // holds *n_virtual keys, the last M of which are the query rows themselves
+  // (row m sees virtual keys [0, *n_virtual - M + m]).  Without a page table
+  // the view is the identity over [0, *pos + M).
+  const int* page_table;
+  int page_shift;
+  const int* n_virtual;
   int n_heads, n_kv_heads;
   float scale;
   int splits;  // CTAs per kv head = thread-block cluster size (1..16)
