@@ -125,6 +125,46 @@ class KVSlot:
     def nbytes(self) -> int:
         return self.data.numel() * 2
 
+    @classmethod
+    def from_buffer(cls, config: ModelConfig, capacity: int, buffer: torch.Tensor) -> "KVSlot":
+        """Wrap an existing device buffer (e.g. an IPC-exported one) as a slot."""
+        slot = cls.__new__(cls)
+        slot.capacity = int(capacity)
+        shape = (config.n_layers, 2, config.n_kv_heads, slot.capacity, config.head_dim)
+        n = math.prod(shape)
+        slot.data = buffer.view(torch.bfloat16)[:n].view(*shape)
+        return slot
+
+    @staticmethod
+    def nbytes_for(config: ModelConfig, capacity: int) -> int:
+        return config.n_layers * 2 * config.n_kv_heads * int(capacity) * config.head_dim * 2
+
+
+@dataclass
+class PushTarget:
+    """A peer GPU's slot (mapped into this process) that prefill pushes K/V into.
+
+    ``base`` / ``flags`` are device addresses valid in this process (CUDA IPC
+    mappings of the decode GPU's buffers); after layer l's K/V rows are
+    stored, ``flags[l]`` is released with ``epoch``.
+    """
+
+    base: int
+    capacity: int
+    flags: int
+    epoch: int
+    n_layers: int
+    layer_elems: int  # n_kv_heads * capacity * head_dim
+
+    def k(self, layer: int) -> int:
+        return self.base + (layer * 2 + 0) * self.layer_elems * 2
+
+    def v(self, layer: int) -> int:
+        return self.base + (layer * 2 + 1) * self.layer_elems * 2
+
+    def flag(self, index: int) -> int:
+        return self.flags + 4 * index
+
 
 class _Workspace:
     """Grow-only device scratch buffers, reused across calls (no per-call allocation)."""
@@ -145,7 +185,8 @@ class _Workspace:
 class _CountingExt:
     """Proxy over the extension that counts kernel launches issued from the host."""
 
-    _NOT_KERNELS = {"status", "num_sms", "gemv_argmax_grid"}
+    _NOT_KERNELS = {"status", "num_sms", "gemv_argmax_grid", "attention_decode_cluster", "shared_empty",
+                    "shared_open", "shared_close"}
 
     def __init__(self, ext) -> None:
         self._ext = ext
@@ -226,15 +267,24 @@ class B200Engine:
         ext.gemm_residual(act, lw.w_down, h, h, self.bn)
 
     def _full_layer(self, layer: int, h: torch.Tensor, slot: KVSlot, pos: torch.Tensor, slots: torch.Tensor,
-                    n_keys: int, kpos: torch.Tensor | None, dev_part=None, dev_mode: int = 0) -> torch.Tensor:
-        """Norm + fused QKV/RoPE/scatter for every row of h; returns q."""
+                    n_keys: int, kpos: torch.Tensor | None, dev_part=None, dev_mode: int = 0,
+                    push: PushTarget | None = None) -> torch.Tensor:
+        """Norm + fused QKV/RoPE/scatter for every row of h; returns q.
+
+        With ``push`` the QKV epilogue also stores every K/V row into the
+        peer GPU's slot, and the layer's ready flag is released right after,
+        while this GPU goes on with the layer's attention and MLP.
+        """
         cfg, lw, ext = self.cfg, self.w.layers[layer], self.ext
         n = h.shape[0]
         x = self.ws.get("x", (n, cfg.d_model), torch.bfloat16)
         ext.rmsnorm(h, None, lw.ln1, cfg.rms_eps, x)
         q = self.ws.get("q", (n, cfg.q_size), torch.bfloat16)
         ext.gemm_qkv(x, lw.w_qkv, q, slot.k(layer), slot.v(layer), pos, slots, self.rope,
-                     cfg.n_heads, cfg.n_kv_heads, dev_part, dev_mode, self.bn)
+                     cfg.n_heads, cfg.n_kv_heads, dev_part, dev_mode, self.bn,
+                     push.k(layer) if push else 0, push.v(layer) if push else 0)
+        if push is not None:
+            ext.peer_signal(push.flag(layer), push.epoch)
         return q
 
     # ----------------------------------------------------------- compose
@@ -278,18 +328,22 @@ class B200Engine:
         self.ext.embedding(ids, self.w.embed, h)
         return h
 
-    def prefill(self, ids: torch.Tensor, slot: KVSlot, *, start: int = 0, kpos: torch.Tensor | None = None) -> torch.Tensor:
+    def prefill(self, ids: torch.Tensor, slot: KVSlot, *, start: int = 0, kpos: torch.Tensor | None = None,
+                push: PushTarget | None = None) -> torch.Tensor:
         """Causal prefill of ``ids`` (int32, device) at positions/slots start.. ; returns final hidden [T, d].
 
         Keys [0, start) already in the slot are visible (direct prefix reuse).
+        ``push`` streams every layer's K/V to a decode GPU as it is written.
         """
         T = ids.numel()
         if start + T > slot.capacity or start + T > self.max_positions:
             raise ValueError("prompt exceeds slot capacity / RoPE table")
+        if push is not None and push.capacity != slot.capacity:
+            raise ValueError("the pushed slot must have the local slot's capacity")
         h = self.embed(ids)
         pos = self._arange("pos", T, start)
         for layer in range(self.cfg.n_layers):
-            q = self._full_layer(layer, h, slot, pos, pos, start + T, kpos)
+            q = self._full_layer(layer, h, slot, pos, pos, start + T, kpos, push=push)
             self._attn_mlp(layer, h, q, slot, q_rows=None, qpos=pos, n_keys=start + T, kpos=kpos, n_rows=T)
         return h
 

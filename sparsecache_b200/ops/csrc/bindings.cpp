@@ -119,7 +119,8 @@ void gemm_swiglu(Tensor a, Tensor w_gu, Tensor out, int64_t bn) {
 // Fused QKV projection + RoPE + K/V cache scatter (+ optional deviation partials).
 void gemm_qkv(Tensor a, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_cache,
               Tensor rope_pos, Tensor cache_slot, Tensor rope_table, int64_t n_q_heads,
-              int64_t n_kv_heads, c10::optional<Tensor> dev_part, int64_t dev_mode, int64_t bn) {
+              int64_t n_kv_heads, c10::optional<Tensor> dev_part, int64_t dev_mode, int64_t bn,
+              int64_t k_peer, int64_t v_peer) {
   const c10::cuda::CUDAGuard guard(a.device());
   auto g = base_gemm(a, w_qkv, sc::EPI_QKV, (int)bn);
   check_matrix(q_out, "q_out");
@@ -148,7 +149,59 @@ void gemm_qkv(Tensor a, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_cac
     g.ep.dev_part = dev_part->data_ptr<float>();
     g.ep.dev_mode = (int)dev_mode;
   }
+  // peer pointers (int64 addresses of the decode GPU's layer cache, mapped
+  // into this process with CUDA IPC); 0 disables the push
+  g.ep.k_peer = reinterpret_cast<__nv_bfloat16*>(k_peer);
+  g.ep.v_peer = reinterpret_cast<__nv_bfloat16*>(v_peer);
+  TORCH_CHECK((k_peer == 0) == (v_peer == 0), "k_peer and v_peer go together");
   run_gemm(g);
+}
+
+// ---------------------------------------------------------------- p2p
+std::tuple<Tensor, py::bytes> shared_empty(int64_t nbytes, int64_t device) {
+  const c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  void* p = nullptr;
+  check_cuda(cudaMalloc(&p, (size_t)nbytes), "cudaMalloc (shared buffer)");
+  check_cuda(cudaMemset(p, 0, (size_t)nbytes), "cudaMemset (shared buffer)");
+  cudaIpcMemHandle_t h;
+  check_cuda(cudaIpcGetMemHandle(&h, p), "cudaIpcGetMemHandle");
+  auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device);
+  Tensor t = torch::from_blob(p, {nbytes}, [](void* q) { cudaFree(q); }, opts);
+  return {t, py::bytes(reinterpret_cast<const char*>(&h), sizeof(h))};
+}
+
+int64_t shared_open(py::bytes handle) {
+  std::string raw = handle;
+  TORCH_CHECK(raw.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, raw.data(), sizeof(h));
+  void* p = nullptr;
+  check_cuda(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  return reinterpret_cast<int64_t>(p);
+}
+
+void shared_close(int64_t ptr) {
+  check_cuda(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)), "cudaIpcCloseMemHandle");
+}
+
+void peer_signal(int64_t flag_ptr, int64_t value, c10::optional<Tensor> stamp,
+                 c10::optional<Tensor> value_src) {
+  unsigned long long* st = nullptr;
+  if (stamp.has_value() && stamp->defined()) st = reinterpret_cast<unsigned long long*>(stamp->data_ptr<int64_t>());
+  const int* src = nullptr;
+  if (value_src.has_value() && value_src->defined()) { CHECK_I32(*value_src); src = value_src->data_ptr<int>(); }
+  check_cuda(sc::peer_signal(reinterpret_cast<int*>(flag_ptr), (int)value, src, st, cur_stream()), "peer_signal");
+}
+
+void wait_flag(Tensor flags, int64_t index, int64_t target, int64_t timeout_ns, Tensor status,
+               c10::optional<Tensor> stamp) {
+  const c10::cuda::CUDAGuard guard(flags.device());
+  CHECK_I32(flags); CHECK_I32(status);
+  TORCH_CHECK(index >= 0 && index < flags.numel(), "flag index");
+  unsigned long long* st = nullptr;
+  if (stamp.has_value() && stamp->defined()) st = reinterpret_cast<unsigned long long*>(stamp->data_ptr<int64_t>());
+  check_cuda(sc::wait_flag(flags.data_ptr<int>() + index, (int)target, (long long)timeout_ns,
+                           status.data_ptr<int>(), st, cur_stream()), "wait_flag");
 }
 
 // ---------------------------------------------------------------- GEMV
@@ -459,7 +512,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_store", &gemm_store);
   m.def("gemm_residual", &gemm_residual);
   m.def("gemm_swiglu", &gemm_swiglu);
-  m.def("gemm_qkv", &gemm_qkv);
+  m.def("gemm_qkv", &gemm_qkv, py::arg("a"), py::arg("w_qkv"), py::arg("q_out"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("rope_pos"), py::arg("cache_slot"), py::arg("rope_table"),
+        py::arg("n_q_heads"), py::arg("n_kv_heads"), py::arg("dev_part"), py::arg("dev_mode"), py::arg("bn"),
+        py::arg("k_peer") = 0, py::arg("v_peer") = 0);
+  m.def("shared_empty", &shared_empty);
+  m.def("shared_open", &shared_open);
+  m.def("shared_close", &shared_close);
+  m.def("peer_signal", &peer_signal, py::arg("flag_ptr"), py::arg("value"), py::arg("stamp") = py::none(),
+        py::arg("value_src") = py::none());
+  m.def("wait_flag", &wait_flag, py::arg("flags"), py::arg("index"), py::arg("target"), py::arg("timeout_ns"),
+        py::arg("status"), py::arg("stamp") = py::none());
   m.def("gemv_store", &gemv_store);
   m.def("gemv_residual", &gemv_residual);
   m.def("gemv_swiglu", &gemv_swiglu);

@@ -188,6 +188,12 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmEpilogue& ep, uint3
         }
         store_row32(dst + half * 32, xa);
         store_row32(dst + 64 + half * 32, xb);
+        if (!is_q && ep.k_peer != nullptr) {
+          // fused P->D push: the same row into the decode GPU's slot (NVLink)
+          __nv_bfloat16* peer = (is_k ? ep.k_peer : ep.v_peer) + ((size_t)kvh * ep.cache_cap + slot) * 128;
+          store_row32(peer + half * 32, xa);
+          store_row32(peer + 64 + half * 32, xb);
+        }
       }
       if (want_dev && row_ok) {
         ep.dev_part[(size_t)row * (2 * ep.n_kv_heads) + (is_v ? ep.n_kv_heads : 0) + kvh] = dev;

@@ -39,6 +39,10 @@ struct GemmEpilogue {
   int n_kv_heads;
   float* dev_part;  // [M, 2 * n_kv_heads] or null
   int dev_mode;
+  // optional peer copies of this layer's cache (same layout and capacity):
+  // every K/V row written locally is also stored into the peer GPU's slot
+  __nv_bfloat16* k_peer;
+  __nv_bfloat16* v_peer;
 };
 
 struct GemmArgs {
@@ -196,6 +200,12 @@ struct SelectArgs {
 cudaError_t cacheblend_select(const SelectArgs& a, cudaStream_t stream);
 
 cudaError_t fill_arange_i32(int* out, int n, int start, cudaStream_t stream);
+
+// ------------------------------------------------------------------- p2p ----
+cudaError_t peer_signal(int* flag, int value, const int* value_src, unsigned long long* stamp,
+                        cudaStream_t stream);
+cudaError_t wait_flag(const int* flag, int target, long long timeout_ns, int* status,
+                      unsigned long long* stamp, cudaStream_t stream);
 cudaError_t index_i32(const int* src, const int* idx, int* out, int n, cudaStream_t stream);
 
 }  // namespace sc

@@ -1,0 +1,273 @@
+"""Prefill/decode disaggregation across GPUs with the KV push fused into prefill.
+
+One process per GPU.  The decode rank allocates its serving slot and a small
+flag array with ``shared_empty`` (cudaMalloc + CUDA IPC handle); the prefill
+rank maps both with ``shared_open`` (plain peer mapping over NVLink, no
+multicast object).  Per request (epoch e):
+
+  prefill rank   prefill with ``push``: the QKV GEMM epilogue of every layer
+                 stores each rotated K/V row into its own cache AND into the
+                 decode slot; right after each layer's GEMM a signal kernel
+                 releases flags[layer] = e (system-scope fence + st.release),
+                 while the prefill GPU continues with the layer's attention and
+                 MLP; after the LM head the seed token is written to
+                 flags[L] and flags[L + 1] = e is released.
+  decode rank    a bounded device-side wait on flags[L - 1] (every layer, in
+                 stream order) and flags[L + 1]; the seed token is read on the
+                 device and greedy decode runs from its CUDA graph.
+
+Exposed transfer = time between the prefill rank finishing its prompt and the
+decode rank having every layer's K/V + the seed.  The control path
+(``mode="nccl"``) prefills without push and then sends the whole prompt KV
+with NCCL send/recv per layer (the baseline to beat).
+
+Reference behaviour: the reference's 1P1D handoff goes through an
+out-of-tree LMCache CPU store over ZMQ/TCP with a paced wire
+(docs/RUN_PROGRESSIVE_PD_LIVE.md:3-23, 56-116); here the transport is
+device-initiated NVLink stores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import time
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..config import get_model_config
+from ..models.engine import B200Engine, KVSlot, PushTarget
+from ..synthetic import make_requests
+
+FLAG_SLOTS = 8
+
+
+class PDChannel:
+    """Decode-side slot + flags shared with the prefill rank over CUDA IPC."""
+
+    def __init__(self, engine: B200Engine, *, role: str, capacity: int, prefill_rank: int, decode_rank: int,
+                 group=None) -> None:
+        self.engine = engine
+        self.role = role
+        self.capacity = capacity
+        cfg = engine.cfg
+        self.n_layers = cfg.n_layers
+        ext = ops.ext()
+        dev = engine.device.index
+        handles = None
+        if role == "decode":
+            buf, h_slot = ext.shared_empty(KVSlot.nbytes_for(cfg, capacity), dev)
+            flags, h_flags = ext.shared_empty(4 * (cfg.n_layers + FLAG_SLOTS), dev)
+            self._buffers = (buf, flags)
+            self.slot = KVSlot.from_buffer(cfg, capacity, buf)
+            self.flags = flags.view(torch.int32)
+            self.status = torch.zeros(1, dtype=torch.int32, device=engine.device)
+            self.stamps = torch.zeros(4, dtype=torch.int64, device=engine.device)
+            handles = (h_slot, h_flags)
+        gathered = [None] * dist.get_world_size(group)
+        dist.all_gather_object(gathered, handles, group=group)
+        self.epoch = 0
+        if role == "prefill":
+            h_slot, h_flags = gathered[dist.get_group_rank(group, decode_rank) if group is not None else decode_rank]
+            self.base = ext.shared_open(h_slot)
+            self.flag_base = ext.shared_open(h_flags)
+            self.slot = engine.new_slot(capacity)
+            self.stamps = torch.zeros(4, dtype=torch.int64, device=engine.device)
+
+    def push_target(self) -> PushTarget:
+        cfg = self.engine.cfg
+        return PushTarget(self.base, self.capacity, self.flag_base, self.epoch, cfg.n_layers,
+                          cfg.n_kv_heads * self.capacity * cfg.head_dim)
+
+    def close(self) -> None:
+        if self.role == "prefill":
+            ext = ops.ext()
+            ext.shared_close(self.base)
+            ext.shared_close(self.flag_base)
+
+
+def prefill_request(ch: PDChannel, ids: torch.Tensor, max_new: int) -> None:
+    """Prefill side: prefill with the fused push, then publish the seed token."""
+    eng = ch.engine
+    ext = eng.ext
+    T = ids.numel()
+    push = ch.push_target()
+    h = eng.prefill(ids, ch.slot, push=push)
+    b = eng.first_token(h[T - 1:T], position=T, max_new=max_new)
+    L = ch.n_layers
+    ext.peer_signal(push.flag(L), 0, None, b["tok"][0:1])
+    ext.peer_signal(push.flag(L + 1), push.epoch, ch.stamps[0:1])
+
+
+def decode_request(ch: PDChannel, T: int, max_new: int, timeout_s: float = 20.0) -> None:
+    """Decode side: wait (bounded) for every layer and the seed, then greedy decode."""
+    eng = ch.engine
+    ext = eng.ext
+    L = ch.n_layers
+    ext.wait_flag(ch.flags, L - 1, ch.epoch, int(timeout_s * 1e9), ch.status, ch.stamps[0:1])
+    ext.wait_flag(ch.flags, L + 1, ch.epoch, int(timeout_s * 1e9), ch.status, ch.stamps[1:2])
+    b = eng._decode_buffers(max_new)
+    ext.embedding(ch.flags[L:L + 1], eng.w.embed, b["h"][:1])
+    b["log"][0:1].copy_(ch.flags[L:L + 1])
+    b["gen"].fill_(1)
+    b["counter"].zero_()
+    eng.set_decode_state(position=T)
+    eng.decode(ch.slot, max_new - 1, max_new=max_new)
+
+
+def nccl_prefill_request(eng: B200Engine, slot: KVSlot, ids: torch.Tensor, max_new: int, peer: int) -> torch.Tensor:
+    """Control path: prefill locally, then send every layer's K/V and the seed with NCCL."""
+    T = ids.numel()
+    h = eng.prefill(ids, slot)
+    b = eng.first_token(h[T - 1:T], position=T, max_new=max_new)
+    for layer in range(eng.cfg.n_layers):
+        dist.send(slot.data[layer, :, :, :T].contiguous(), peer)
+    dist.send(b["tok"][0:1].clone(), peer)
+    return b["tok"]
+
+
+def nccl_decode_request(eng: B200Engine, slot: KVSlot, T: int, max_new: int, peer: int) -> None:
+    cfg = eng.cfg
+    buf = torch.empty(2, cfg.n_kv_heads, T, cfg.head_dim, dtype=torch.bfloat16, device=eng.device)
+    for layer in range(cfg.n_layers):
+        dist.recv(buf, peer)
+        slot.data[layer, :, :, :T].copy_(buf)
+    tok = torch.empty(1, dtype=torch.int32, device=eng.device)
+    dist.recv(tok, peer)
+    b = eng._decode_buffers(max_new)
+    eng.ext.embedding(tok, eng.w.embed, b["h"][:1])
+    b["log"][0:1].copy_(tok)
+    b["gen"].fill_(1)
+    eng.set_decode_state(position=T)
+    eng.decode(slot, max_new - 1, max_new=max_new)
+
+
+def run(args) -> dict | None:
+    rank, world = dist.get_rank(), dist.get_world_size()
+    if world % 2:
+        raise ValueError("prefill/decode needs an even number of ranks (pairs)")
+    pairs = world // 2
+    role = "prefill" if rank < pairs else "decode"
+    peer = rank + pairs if role == "prefill" else rank - pairs
+    cfg = get_model_config(args.model)
+    if args.layers:
+        cfg = cfg.with_layers(args.layers)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    engine = B200Engine.random(cfg, seed=0, device=dev, max_positions=65536)
+    requests = make_requests("pd_long", cfg)
+    mine = [r for r in requests if r.index % pairs == rank % pairs]
+    need = args.warmup + args.steps
+    served = [mine[i % len(mine)] for i in range(need)]
+    capacity = max(r.prompt_tokens for r in served) + args.new_tokens + 64
+    # one channel per prefill/decode pair: a 2-rank group
+    groups = [dist.new_group([p, p + pairs]) for p in range(pairs)]
+    group = groups[rank % pairs]
+    ch = PDChannel(engine, role=role, capacity=capacity, prefill_rank=rank % pairs, decode_rank=rank % pairs + pairs,
+                   group=group) if args.mode == "push" else None
+    nccl_slot = engine.new_slot(capacity) if args.mode == "nccl" else None
+    ttft, tpot, exposed = [], [], []
+    for i, req in enumerate(served):
+        ids = torch.tensor(req.prompt, dtype=torch.int32, device=dev)
+        T = req.prompt_tokens
+        if ch is not None:
+            ch.epoch += 1
+        dist.barrier(group=group)
+        torch.cuda.synchronize()
+        t0 = time.monotonic()
+        if role == "prefill":
+            if args.mode == "push":
+                prefill_request(ch, ids, args.new_tokens)
+            else:
+                nccl_prefill_request(engine, nccl_slot, ids, args.new_tokens, peer)
+            torch.cuda.synchronize()
+            t_prefill_end = time.monotonic() - t0
+            rec = torch.tensor([t_prefill_end], dtype=torch.float64, device=dev)
+            dist.send(rec, peer)
+        else:
+            first = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start = torch.cuda.Event(enable_timing=True)
+            start.record()
+            L = cfg.n_layers
+            ext = engine.ext
+            b = engine._decode_buffers(args.new_tokens)
+            if args.mode == "push":
+                ext.wait_flag(ch.flags, L - 1, ch.epoch, int(20e9), ch.status, ch.stamps[0:1])
+                ext.wait_flag(ch.flags, L + 1, ch.epoch, int(20e9), ch.status, ch.stamps[1:2])
+                seed, slot = ch.flags[L:L + 1], ch.slot
+            else:
+                buf = torch.empty(2, cfg.n_kv_heads, T, cfg.head_dim, dtype=torch.bfloat16, device=dev)
+                for layer in range(L):
+                    dist.recv(buf, peer)
+                    nccl_slot.data[layer, :, :, :T].copy_(buf)
+                seed = torch.empty(1, dtype=torch.int32, device=dev)
+                dist.recv(seed, peer)
+                slot = nccl_slot
+            first.record()
+            first.synchronize()
+            t_ready = time.monotonic() - t0
+            if args.mode == "push" and int(ch.status.item()) != 0:
+                raise RuntimeError("decode rank timed out waiting for the pushed KV")
+            ext.embedding(seed, engine.w.embed, b["h"][:1])
+            b["log"][0:1].copy_(seed)
+            b["gen"].fill_(1)
+            engine.set_decode_state(position=T)
+            engine.decode(slot, args.new_tokens - 1, max_new=args.new_tokens)
+            end.record()
+            end.synchronize()
+            rec = torch.empty(1, dtype=torch.float64, device=dev)
+            dist.recv(rec, peer)
+            t_prefill_end = float(rec.item())
+            if i >= args.warmup:
+                ttft.append(t_ready * 1000)
+                exposed.append(max(0.0, (t_ready - t_prefill_end) * 1000))
+                tpot.append(first.elapsed_time(end) / max(1, args.new_tokens - 1))
+    if ch is not None:
+        dist.barrier(group=group)
+        ch.close()
+    stats = None
+    if role == "decode":
+        stats = {"ttft_ms": ttft, "tpot_ms": tpot, "exposed_ms": exposed}
+    gathered = [None] * world
+    dist.all_gather_object(gathered, stats)
+    if rank != 0:
+        return None
+    dec = [g for g in gathered if g is not None]
+    flat = lambda key: [x for g in dec for x in g[key] if x is not None]  # noqa: E731
+    out = {"mode": args.mode, "pairs": pairs, "model": cfg.name, "layers": cfg.n_layers,
+           "new_tokens": args.new_tokens, "requests": args.steps * pairs}
+    for key in ("ttft_ms", "tpot_ms", "exposed_ms"):
+        xs = flat(key)
+        if xs:
+            out[key.replace("_ms", "_p50_ms")] = statistics.median(xs)
+            out[key.replace("_ms", "_max_ms")] = max(xs)
+    return out
+
+
+def main() -> None:
+    p = argparse.ArgumentParser(description="Prefill/decode disaggregation with the fused NVLink KV push")
+    p.add_argument("--model", default="llama3-8b")
+    p.add_argument("--layers", type=int, default=None)
+    p.add_argument("--mode", choices=("push", "nccl"), default="push")
+    p.add_argument("--steps", type=int, default=4)
+    p.add_argument("--warmup", type=int, default=2)
+    p.add_argument("--new-tokens", type=int, default=128)
+    args = p.parse_args()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    try:
+        out = run(args)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+    finally:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
