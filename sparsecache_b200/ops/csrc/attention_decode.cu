@@ -30,7 +30,7 @@ namespace sc {
 namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kSub = 128;     // keys per staged sub-chunk
+constexpr int kSub = 64;      // keys per staged sub-chunk (double-buffered)
 constexpr int kMaxQV = 32;    // M * G
 constexpr int kMaxRows = 8;   // largest query block M
 constexpr int kRow = 256;     // bytes per K/V row (128 bf16)
@@ -43,8 +43,8 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool p
 }  // namespace
 
 struct DecodeSmem {
-  __nv_bfloat16 k[kSub * 128];
-  __nv_bfloat16 v[kSub * 128];
+  __nv_bfloat16 k[2][kSub * 128];  // double-buffered sub-chunks
+  __nv_bfloat16 v[2][kSub * 128];
   float s[kMaxQV][kSub];
   float o[kMaxQV][128];  // partial output of this CTA (unnormalised)
   float m[kMaxQV];       // running max (log2 domain)
@@ -81,10 +81,12 @@ __global__ void __launch_bounds__(kThreads)
   const float sl2 = a.scale * 1.4426950408889634f;
   const __nv_bfloat16* kb = a.k_cache + (size_t)kvh * a.cache_cap * 128;
   const __nv_bfloat16* vb = a.v_cache + (size_t)kvh * a.cache_cap * 128;
-  const uint32_t sk = smem_u32(sm.k), sv = smem_u32(sm.v);
-  // stage rows [base, base + nk) whose key index lies in [lo, hi); rows past
-  // nk are zero-filled when zero_tail is set
-  auto stage = [&](int base, int nk, int lo, int hi, bool zero_tail) {
+  const uint32_t sk0 = smem_u32(sm.k[0]), sv0 = smem_u32(sm.v[0]);
+  constexpr uint32_t kBufBytes = kSub * kRow;
+  // stage rows [base, base + nk) whose key index lies in [lo, hi) into buffer
+  // buf; rows past nk are zero-filled when zero_tail is set
+  auto stage = [&](int buf, int base, int nk, int lo, int hi, bool zero_tail) {
+    const uint32_t sk = sk0 + buf * kBufBytes, sv = sv0 + buf * kBufBytes;
     for (int i = tid; i < kSub * 16; i += kThreads) {
       const int r = i >> 4, c = i & 15;
       const int key = base + r;
@@ -95,7 +97,7 @@ __global__ void __launch_bounds__(kThreads)
       cp_async16(sv + r * kRow + c * 16, vb + off, in);
     }
   };
-  if (k_begin < k_end) stage(k_begin, min(kSub, k_end - k_begin), 0, pos0, true);
+  if (k_begin < k_end) stage(0, k_begin, min(kSub, k_end - k_begin), 0, pos0, true);
   for (int i = tid; i < QV * 128; i += kThreads) sm.o[i / 128][i % 128] = 0.f;
   if (tid < QV) sm.m[tid] = -INFINITY, sm.l[tid] = 0.f;
   pdl_wait();
@@ -122,15 +124,18 @@ __global__ void __launch_bounds__(kThreads)
       }
     }
   }
-  for (int base = k_begin; base < k_end; base += kSub) {
+  int it = 0;
+  for (int base = k_begin; base < k_end; base += kSub, ++it) {
     const int nk = min(kSub, k_end - base);
-    if (base == k_begin) {
-      stage(base, nk, pos0, n_keys, false);  // the new rows, now visible
-    } else {
-      __syncthreads();  // previous sub-chunk fully consumed
-      stage(base, nk, 0, n_keys, true);
+    const int buf = it & 1;
+    if (it == 0) {
+      stage(0, base, nk, pos0, n_keys, false);  // the new rows, now visible
+      asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+    // prefetch the next sub-chunk into the other buffer while this one runs
+    const int nbase = base + kSub;
+    if (nbase < k_end) stage(buf ^ 1, nbase, min(kSub, k_end - nbase), 0, n_keys, true);
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 1;" ::: "memory");
     __syncthreads();
 
     // scores: each warp step covers 32/LPK keys; LPK lanes split the dims
@@ -140,7 +145,7 @@ __global__ void __launch_bounds__(kThreads)
       const bool valid = j < nk;
       float kf[DPL];
       {
-        const __nv_bfloat16* kr = sm.k + (valid ? j : 0) * 128 + DPL * sub;
+        const __nv_bfloat16* kr = sm.k[buf] + (valid ? j : 0) * 128 + DPL * sub;
 #pragma unroll
         for (int c = 0; c < DPL / 4; ++c) {
           const uint2 raw = *reinterpret_cast<const uint2*>(kr + 4 * c);
@@ -201,8 +206,8 @@ __global__ void __launch_bounds__(kThreads)
       for (int i = 0; i < kHalf; ++i) acc2[i] = 0.f;
       int j = 0;
       for (; j + 1 < nk; j += 2) {  // two keys per step: independent FMA chains
-        const float v0 = __bfloat162float(sm.v[j * 128 + d]);
-        const float v1 = __bfloat162float(sm.v[(j + 1) * 128 + d]);
+        const float v0 = __bfloat162float(sm.v[buf][j * 128 + d]);
+        const float v1 = __bfloat162float(sm.v[buf][(j + 1) * 128 + d]);
 #pragma unroll
         for (int i = 0; i < kHalf; ++i) {
           const int qv = q0 + 2 * i;
@@ -213,7 +218,7 @@ __global__ void __launch_bounds__(kThreads)
         }
       }
       if (j < nk) {
-        const float v0 = __bfloat162float(sm.v[j * 128 + d]);
+        const float v0 = __bfloat162float(sm.v[buf][j * 128 + d]);
 #pragma unroll
         for (int i = 0; i < kHalf; ++i) {
           const int qv = q0 + 2 * i;
@@ -228,6 +233,7 @@ __global__ void __launch_bounds__(kThreads)
         if (qv < QV) sm.o[qv][d] = sm.o[qv][d] * sm.corr[qv] + acc[i];
       }
     }
+    __syncthreads();  // buffer `buf` is refilled by the next iteration's prefetch
   }
 
   // ---- merge the S partials of this kv head through DSMEM ----
@@ -310,7 +316,7 @@ cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kern, a, chunk);

@@ -12,6 +12,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 namespace sc {
 
@@ -359,5 +360,18 @@ inline void ensure_smem_attr(F* func, int bytes) {
   }
   cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (used < 256) table[used++] = Entry{key, dev, bytes};
+}
+}  // namespace sc
+
+namespace sc {
+// Programmatic dependent launch is on unless SC_PDL=0 (an experiment and
+// safety switch: every kernel stays correct without it).
+inline bool pdl_enabled() {
+  static int enabled = -1;
+  if (enabled < 0) {
+    const char* e = getenv("SC_PDL");
+    enabled = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return enabled != 0;
 }
 }  // namespace sc

@@ -182,10 +182,18 @@ def run(args) -> dict | None:
         if role == "prefill":
             if args.mode == "push":
                 prefill_request(ch, ids, args.new_tokens)
+                torch.cuda.synchronize()
+                t_prefill_end = time.monotonic() - t0
             else:
-                nccl_prefill_request(engine, nccl_slot, ids, args.new_tokens, peer)
-            torch.cuda.synchronize()
-            t_prefill_end = time.monotonic() - t0
+                # the prompt is done (seed token ready) before any byte is sent
+                h = engine.prefill(ids, nccl_slot)
+                b = engine.first_token(h[T - 1:T], position=T, max_new=args.new_tokens)
+                torch.cuda.synchronize()
+                t_prefill_end = time.monotonic() - t0
+                for layer in range(cfg.n_layers):
+                    dist.send(nccl_slot.data[layer, :, :, :T].contiguous(), peer)
+                dist.send(b["tok"][0:1].clone(), peer)
+                torch.cuda.synchronize()
             rec = torch.tensor([t_prefill_end], dtype=torch.float64, device=dev)
             dist.send(rec, peer)
         else:
@@ -232,7 +240,9 @@ def run(args) -> dict | None:
         ch.close()
     stats = None
     if role == "decode":
-        stats = {"ttft_ms": ttft, "tpot_ms": tpot, "exposed_ms": exposed}
+        last_tokens = engine.generated_tokens(args.new_tokens)[:8].tolist()
+        stats = {"ttft_ms": ttft, "tpot_ms": tpot, "exposed_ms": exposed, "last_tokens": last_tokens,
+                 "prompt_tokens": [r.prompt_tokens for r in served[args.warmup:]]}
     gathered = [None] * world
     dist.all_gather_object(gathered, stats)
     if rank != 0:
@@ -240,7 +250,8 @@ def run(args) -> dict | None:
     dec = [g for g in gathered if g is not None]
     flat = lambda key: [x for g in dec for x in g[key] if x is not None]  # noqa: E731
     out = {"mode": args.mode, "pairs": pairs, "model": cfg.name, "layers": cfg.n_layers,
-           "new_tokens": args.new_tokens, "requests": args.steps * pairs}
+           "new_tokens": args.new_tokens, "requests": args.steps * pairs,
+           "last_tokens": dec[0]["last_tokens"], "prompt_tokens": dec[0]["prompt_tokens"]}
     for key in ("ttft_ms", "tpot_ms", "exposed_ms"):
         xs = flat(key)
         if xs:

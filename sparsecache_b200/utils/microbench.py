@@ -1,0 +1,103 @@
+"""Isolated timings of the sm_100a kernels at Llama-3.1-8B shapes.
+
+    python -m sparsecache_b200.utils.microbench [--only gemm,gemv,attn_decode,attn_prefill]
+
+CUDA events on the launching stream, 10 warm-up launches, mean over N timed
+launches; every case uses tensors that are re-read each launch, so the
+bandwidth figures of the GEMV / decode-attention rows are HBM figures when
+the operand exceeds L2 (126 MB) and L2-assisted otherwise (noted per row).
+Fractions are against the measured copy bandwidth and cuBLAS bf16 rate of
+this machine class (6.46 TB/s, 1.68 PFLOP/s burst).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+HBM_GBS = 6456.5
+BF16_TFLOPS = 1676.9
+
+
+def timeit(fn, n: int = 50, warm: int = 10) -> float:
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+    a.record()
+    for _ in range(n):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / n * 1000.0  # us
+
+
+def main() -> None:
+    from .. import ops
+
+    p = argparse.ArgumentParser()
+    p.add_argument("--only", default="gemm,gemv,attn_decode,attn_prefill")
+    args = p.parse_args()
+    only = set(args.only.split(","))
+    ext = ops.ext()
+    dev = torch.device("cuda:0")
+    res: dict[str, dict] = {}
+    bf = torch.bfloat16
+
+    if "gemv" in only:
+        for name, N, K in (("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 28672, 4096),
+                           ("down", 4096, 14336), ("lm_head", 128256, 4096)):
+            w = (torch.randn(N, K, device=dev) * 0.02).to(bf)
+            x = torch.randn(1, K, device=dev).to(bf)
+            o = torch.empty(1, N, device=dev, dtype=bf)
+            t = timeit(lambda: ext.gemv_store(x, w, None, 1e-5, o))
+            gbs = N * K * 2 / (t * 1e-6) / 1e9
+            res[f"gemv_{name}"] = {"us": t, "GBps": gbs, "frac_of_measured_hbm": gbs / HBM_GBS}
+            del w
+
+    if "gemm" in only:
+        K = 4096
+        for M in (300, 1700, 8192):
+            for name, N in (("qkv", 6144), ("gate_up", 28672)):
+                a = torch.randn(M, K, device=dev).to(bf)
+                w = (torch.randn(N, K, device=dev) * 0.02).to(bf)
+                o = torch.empty(M, N, device=dev, dtype=bf)
+                t = timeit(lambda: ext.gemm_store(a, w, o, 256), n=20)
+                tf = 2 * M * N * K / (t * 1e-6) / 1e12
+                res[f"gemm_M{M}_{name}"] = {"us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS,
+                                            "weight_GBps": N * K * 2 / (t * 1e-6) / 1e9}
+
+    if "attn_decode" in only:
+        H, Hkv = 32, 8
+        for cap in (2048, 18000):
+            kc = torch.randn(Hkv, cap, 128, device=dev).to(bf)
+            vc = torch.randn(Hkv, cap, 128, device=dev).to(bf)
+            q = torch.randn(1, H * 128, device=dev).to(bf)
+            pos = torch.tensor([cap - 16], device=dev, dtype=torch.int32)
+            out = torch.empty(1, H * 128, device=dev, dtype=bf)
+            S = int(ext.attention_decode_cluster(cap))
+            t = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), S, out))
+            kv_bytes = 2 * Hkv * (cap - 15) * 128 * 2
+            gbs = kv_bytes / (t * 1e-6) / 1e9
+            res[f"attn_decode_ctx{cap}"] = {"us": t, "GBps": gbs, "frac_of_measured_hbm": gbs / HBM_GBS,
+                                            "cluster": S, "l2_resident": kv_bytes < 126e6}
+
+    if "attn_prefill" in only:
+        H, Hkv = 32, 8
+        for T in (2048, 16384):
+            kc = torch.randn(Hkv, T, 128, device=dev).to(bf)
+            vc = torch.randn(Hkv, T, 128, device=dev).to(bf)
+            q = torch.randn(T, H * 128, device=dev).to(bf)
+            pos = torch.arange(T, device=dev, dtype=torch.int32)
+            out = torch.empty(T, H * 128, device=dev, dtype=bf)
+            t = timeit(lambda: ext.attention_prefill(q, None, pos, kc, vc, None, T, H, 1 / math.sqrt(128), out), n=10)
+            flops = 4 * 128 * H * T * (T + 1) / 2
+            tf = flops / (t * 1e-6) / 1e12
+            res[f"attn_prefill_causal_T{T}"] = {"us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS}
+    print(json.dumps(res, indent=1))
+
+
+if __name__ == "__main__":
+    main()
