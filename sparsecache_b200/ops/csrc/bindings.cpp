@@ -157,6 +157,116 @@ void gemm_qkv(Tensor a, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_cac
   run_gemm(g);
 }
 
+// ------------------------------------------------- tensor-parallel GEMMs
+// A is row-sharded over `shard_ptrs` (device addresses, peers' shards mapped
+// with CUDA IPC), each [rows, K] with row stride K; the all-gather is fused
+// into the GEMM's TMA producer (see AShards).
+sc::GemmArgs sharded_gemm(const std::vector<int64_t>& shard_ptrs, int64_t rows, int64_t own,
+                          const Tensor& ready, int64_t epoch, int64_t K, const Tensor& w, int epi,
+                          int64_t bn) {
+  check_matrix(w, "w");
+  TORCH_CHECK(!shard_ptrs.empty() && (int)shard_ptrs.size() <= sc::kMaxShards, "1..8 shards");
+  TORCH_CHECK(rows % 128 == 0, "rows per shard must be a multiple of 128");
+  TORCH_CHECK(K == w.size(1) && (K * 2) % 16 == 0, "K");
+  CHECK_I32(ready);
+  sc::GemmArgs g{};
+  for (size_t r = 0; r < shard_ptrs.size(); ++r) {
+    TORCH_CHECK((shard_ptrs[r] & 15) == 0, "shard base must be 16-byte aligned");
+    g.a_shards[r] = reinterpret_cast<const __nv_bfloat16*>(shard_ptrs[r]);
+  }
+  g.a = g.a_shards[0];
+  g.shards.n = (int)shard_ptrs.size();
+  g.shards.rows = (int)rows;
+  g.shards.own = (int)own;
+  g.shards.ready = ready.data_ptr<int>();
+  g.shards.epoch = (int)epoch;
+  g.b = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  g.M = (int)(rows * shard_ptrs.size());
+  g.N = (int)w.size(0);
+  g.K = (int)K;
+  g.lda = (int)K;
+  g.ldb = (int)w.stride(0);
+  g.epi = epi;
+  g.bn = (int)bn;
+  g.num_sms = num_sms();
+  g.status = status_tensor(w).data_ptr<int>();
+  return g;
+}
+
+void gemm_ag_qkv(std::vector<int64_t> shard_ptrs, int64_t rows, int64_t own, Tensor ready, int64_t epoch,
+                 int64_t K, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_cache, Tensor rope_pos,
+                 Tensor cache_slot, Tensor rope_table, int64_t n_q_heads, int64_t n_kv_heads, int64_t bn) {
+  const c10::cuda::CUDAGuard guard(w_qkv.device());
+  auto g = sharded_gemm(shard_ptrs, rows, own, ready, epoch, K, w_qkv, sc::EPI_QKV, bn);
+  check_matrix(q_out, "q_out");
+  TORCH_CHECK(w_qkv.size(0) == (n_q_heads + 2 * n_kv_heads) * 128, "w_qkv rows");
+  TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(0) == n_kv_heads && k_cache.is_contiguous(), "k_cache");
+  g.ep.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
+  g.ep.ldq = (int)q_out.stride(0);
+  g.ep.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr());
+  g.ep.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
+  g.ep.cache_cap = (int)k_cache.size(1);
+  g.ep.rope_pos = rope_pos.data_ptr<int>();
+  g.ep.cache_slot = cache_slot.data_ptr<int>();
+  g.ep.rope_table = reinterpret_cast<const float2*>(rope_table.data_ptr<float>());
+  g.ep.n_q_heads = (int)n_q_heads;
+  g.ep.n_kv_heads = (int)n_kv_heads;
+  run_gemm(g);
+}
+
+void gemm_ag_swiglu(std::vector<int64_t> shard_ptrs, int64_t rows, int64_t own, Tensor ready, int64_t epoch,
+                    int64_t K, Tensor w_gu, Tensor out, int64_t bn) {
+  const c10::cuda::CUDAGuard guard(w_gu.device());
+  auto g = sharded_gemm(shard_ptrs, rows, own, ready, epoch, K, w_gu, sc::EPI_SWIGLU, bn);
+  check_matrix(out, "out");
+  TORCH_CHECK(out.size(0) == g.M && out.size(1) == w_gu.size(0) / 2, "out shape");
+  g.ep.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  g.ep.ldo = (int)out.stride(0);
+  run_gemm(g);
+}
+
+// partial = a @ w^T; rows of owner r are stored into dst_ptrs[r] at slot `sender`
+void gemm_rs(Tensor a, Tensor w, std::vector<int64_t> dst_ptrs, int64_t rows, int64_t sender, int64_t bn) {
+  const c10::cuda::CUDAGuard guard(a.device());
+  auto g = base_gemm(a, w, sc::EPI_RS, (int)bn);
+  TORCH_CHECK(!dst_ptrs.empty() && (int)dst_ptrs.size() <= sc::kMaxShards, "1..8 owners");
+  TORCH_CHECK(rows % 128 == 0 && rows * (int64_t)dst_ptrs.size() == a.size(0), "rows per owner");
+  TORCH_CHECK(g.N % 32 == 0, "N must be a multiple of 32");
+  for (size_t r = 0; r < dst_ptrs.size(); ++r) g.ep.rs_dst[r] = reinterpret_cast<float*>(dst_ptrs[r]);
+  g.ep.rs_rows = (int)rows;
+  g.ep.rs_sender = (int)sender;
+  run_gemm(g);
+}
+
+void rs_reduce(Tensor recv, Tensor flags, int64_t epoch, int64_t timeout_ns, Tensor status, Tensor residual,
+               Tensor out, c10::optional<Tensor> norm_w, c10::optional<Tensor> norm_out, double eps) {
+  const c10::cuda::CUDAGuard guard(recv.device());
+  CHECK_F32(recv); CHECK_I32(flags); CHECK_I32(status);
+  TORCH_CHECK(recv.dim() == 3 && recv.is_contiguous(), "recv [tp, rows, N]");
+  check_matrix(residual, "residual");
+  check_matrix(out, "out");
+  sc::RsReduceArgs a{};
+  a.recv = recv.data_ptr<float>();
+  a.tp = (int)recv.size(0);
+  a.rows = (int)recv.size(1);
+  a.N = (int)recv.size(2);
+  TORCH_CHECK(flags.numel() >= a.tp, "one flag per sender");
+  TORCH_CHECK(residual.size(0) == a.rows && residual.size(1) == a.N, "residual shape");
+  a.flags = flags.data_ptr<int>();
+  a.epoch = (int)epoch;
+  a.timeout_ns = timeout_ns;
+  a.status = status.data_ptr<int>();
+  a.residual = reinterpret_cast<const __nv_bfloat16*>(residual.data_ptr());
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  if (norm_w.has_value() && norm_w->defined()) {
+    TORCH_CHECK(norm_out.has_value() && norm_out->defined(), "norm_out required");
+    a.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w->data_ptr());
+    a.norm_out = reinterpret_cast<__nv_bfloat16*>(norm_out->data_ptr());
+  }
+  a.eps = (float)eps;
+  check_cuda(sc::rs_reduce(a, cur_stream()), "rs_reduce");
+}
+
 // ---------------------------------------------------------------- p2p
 std::tuple<Tensor, py::bytes> shared_empty(int64_t nbytes, int64_t device) {
   const c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
@@ -516,6 +626,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("v_cache"), py::arg("rope_pos"), py::arg("cache_slot"), py::arg("rope_table"),
         py::arg("n_q_heads"), py::arg("n_kv_heads"), py::arg("dev_part"), py::arg("dev_mode"), py::arg("bn"),
         py::arg("k_peer") = 0, py::arg("v_peer") = 0);
+  m.def("peer_signal_many", [](std::vector<int64_t> addrs, int64_t value) {
+    std::vector<int*> p;
+    for (auto a : addrs) p.push_back(reinterpret_cast<int*>(a));
+    check_cuda(sc::peer_signal_many(p.data(), (int)p.size(), (int)value, cur_stream()), "peer_signal_many");
+  });
+  m.def("gemm_ag_qkv", &gemm_ag_qkv);
+  m.def("gemm_ag_swiglu", &gemm_ag_swiglu);
+  m.def("gemm_rs", &gemm_rs);
+  m.def("rs_reduce", &rs_reduce);
   m.def("shared_empty", &shared_empty);
   m.def("shared_open", &shared_open);
   m.def("shared_close", &shared_close);

@@ -126,6 +126,26 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmEpilogue& ep, uint3
         store_row32(ep.out + (size_t)row * ep.ldo + col, v);
       }
     }
+  } else if constexpr (EPI == EPI_RS) {
+    // fused reduce-scatter: the fp32 partial of this row goes straight into
+    // the receive slot of the rank that owns the row (NVLink store for peers)
+    const int shard = row_ok ? row / ep.rs_rows : 0;
+    const int lrow = row - shard * ep.rs_rows;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tacc + c * 32, r);
+      tmem_ld_wait();
+      const int col = tile_n * BN + c * 32;
+      if (row_ok && col < N) {
+        float4* dst = reinterpret_cast<float4*>(
+            ep.rs_dst[shard] + ((size_t)ep.rs_sender * ep.rs_rows + lrow) * N + col);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                               __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+      }
+    }
   } else if constexpr (EPI == EPI_QKV) {
     int pos = 0, slot = 0;
     if (row_ok) {
@@ -202,11 +222,39 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmEpilogue& ep, uint3
   }
 }
 
+// One TMA descriptor per A shard (only maps[0] is used by ordinary GEMMs).
+struct AMaps {
+  CUtensorMap m[kMaxShards];
+};
+
+// Tile t -> (m-tile, n-tile).  With a row-sharded A the m-tiles are rotated so
+// that every rank starts on its own shard while its peers finish theirs.
+__device__ __forceinline__ void tile_coords(int t, int num_m, const AShards& sh, int& tm, int& tn) {
+  tm = t % num_m;
+  tn = t / num_m;
+  if (sh.n > 1) tm = (tm + sh.own * (sh.rows / kGemmBM)) % num_m;
+}
+
+// Bounded acquire-poll of a peer shard's ready flag (written over NVLink).
+__device__ __forceinline__ bool wait_shard_ready(const int* flag, int epoch, int* status) {
+  const long long start = clock64();
+  while (true) {
+    int v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v >= epoch) return true;
+    if (clock64() - start > kSpinLimitCycles) {
+      report_status(status, kStatusTimeoutPeerFlag);
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
+    gemm_tc_kernel(const __grid_constant__ AMaps amaps,
                    const __grid_constant__ CUtensorMap tmap_b, int M, int N, int K,
-                   GemmEpilogue ep, int* status) {
+                   GemmEpilogue ep, AShards shards, int* status) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -235,7 +283,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_proxy_async_smem();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmap_a);
+    for (int r = 0; r < shards.n; ++r) tma_prefetch_desc(&amaps.m[r]);
     tma_prefetch_desc(&tmap_b);
   }
   if (warp == 1) {
@@ -256,8 +304,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool issued[8];
       for (int s = 0; s < S; ++s) issued[s] = false, issued_phase[s] = 0;
       bool ok = true;
+      unsigned confirmed = 1u << shards.own;  // shards known to be ready
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int tm = t % num_m, tn = t / num_m;
+        int tm, tn;
+        tile_coords(t, num_m, shards, tm, tn);
+        int map = 0, ay = tm * kGemmBM;
+        if (shards.n > 1) {
+          map = ay / shards.rows;
+          ay -= map * shards.rows;
+          if (!((confirmed >> map) & 1u) && shards.ready != nullptr) {
+            if (!wait_shard_ready(shards.ready + map, shards.epoch, status)) {
+              ok = false;
+              break;
+            }
+            confirmed |= 1u << map;
+          }
+        }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&bars->empty[stage], phase ^ 1, status, kStatusTimeoutSmemEmpty)) {
             ok = false;
@@ -266,7 +328,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           uint8_t* sa = smem + stage * Cfg::kStageBytes;
           uint8_t* sb = sa + Cfg::kABytes;
           mbar_arrive_expect_tx(&bars->full[stage], Cfg::kStageBytes);
-          tma_load_2d(sa, &tmap_a, &bars->full[stage], kb * kGemmBK, tm * kGemmBM);
+          tma_load_2d(sa, &amaps.m[map], &bars->full[stage], kb * kGemmBK, ay);
           tma_load_2d(sb, &tmap_b, &bars->full[stage], kb * kGemmBK, tn * BN);
           issued[stage] = true;
           issued_phase[stage] = phase;
@@ -327,7 +389,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
-      const int tm = t % num_m, tn = t / num_m;
+      int tm, tn;
+      tile_coords(t, num_m, shards, tm, tn);
       const int buf = local & 1;
       const uint32_t tphase = (local >> 1) & 1;
       if (!mbar_wait(&bars->tmem_full[buf], tphase, status, kStatusTimeoutTmemFull)) break;
@@ -380,15 +443,29 @@ bool make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint6
 template <int BN, int EPI>
 static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
-  CUtensorMap ta, tb;
-  if (!make_tmap_2d_bf16(&ta, g.a, g.K, g.M, g.lda, kGemmBK, kGemmBM, true)) return cudaErrorInvalidValue;
+  AMaps maps;
+  CUtensorMap tb;
+  AShards sh = g.shards;
+  if (sh.n <= 1) {
+    sh.n = 1;
+    sh.rows = g.M;
+    sh.own = 0;
+    sh.ready = nullptr;
+    if (!make_tmap_2d_bf16(&maps.m[0], g.a, g.K, g.M, g.lda, kGemmBK, kGemmBM, true))
+      return cudaErrorInvalidValue;
+  } else {
+    if (sh.n > kMaxShards || sh.rows % kGemmBM != 0 || sh.rows * sh.n != g.M) return cudaErrorInvalidValue;
+    for (int r = 0; r < sh.n; ++r)
+      if (!make_tmap_2d_bf16(&maps.m[r], g.a_shards[r], g.K, sh.rows, g.lda, kGemmBK, kGemmBM, true))
+        return cudaErrorInvalidValue;
+  }
   if (!make_tmap_2d_bf16(&tb, g.b, g.K, g.N, g.ldb, kGemmBK, BN, true)) return cudaErrorInvalidValue;
   auto kern = gemm_tc_kernel<BN, EPI>;
   ensure_smem_attr(kern, Cfg::kSmemBytes);
   const int num_tiles = ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + BN - 1) / BN);
   int grid = num_tiles < g.num_sms ? num_tiles : g.num_sms;
   if (grid < 1) grid = 1;
-  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, g.M, g.N, g.K, g.ep, g.status);
+  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(maps, tb, g.M, g.N, g.K, g.ep, sh, g.status);
   return cudaGetLastError();
 }
 
@@ -404,6 +481,8 @@ cudaError_t gemm_bf16_tc(const GemmArgs& g, cudaStream_t stream) {
       return bn == 128 ? launch_gemm<128, EPI_SWIGLU>(g, stream) : launch_gemm<256, EPI_SWIGLU>(g, stream);
     case EPI_QKV:
       return bn == 128 ? launch_gemm<128, EPI_QKV>(g, stream) : launch_gemm<256, EPI_QKV>(g, stream);
+    case EPI_RS:
+      return bn == 128 ? launch_gemm<128, EPI_RS>(g, stream) : launch_gemm<256, EPI_RS>(g, stream);
   }
   return cudaErrorInvalidValue;
 }

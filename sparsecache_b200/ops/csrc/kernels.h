@@ -18,7 +18,8 @@ bool make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint6
                        bool swizzle128);
 
 // ---------------------------------------------------------------- GEMM ----
-enum Epi : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
+enum Epi : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_RS = 4 };
+constexpr int kMaxShards = 8;
 enum DevMode : int { DEV_KEY = 1, DEV_VALUE = 2, DEV_L1 = 4 };
 
 struct GemmEpilogue {
@@ -43,10 +44,30 @@ struct GemmEpilogue {
   // every K/V row written locally is also stored into the peer GPU's slot
   __nv_bfloat16* k_peer;
   __nv_bfloat16* v_peer;
+  // EPI_RS (GEMM -> reduce-scatter): rows [r * rs_rows, (r + 1) * rs_rows)
+  // belong to rank r; their fp32 partial tile is stored into rank r's receive
+  // buffer (local or peer-mapped) at slot rs_sender: rs_dst[r][rs_sender][row][N]
+  float* rs_dst[kMaxShards];
+  int rs_rows;
+  int rs_sender;
+};
+
+// A operand split by rows over ranks (all-gather fused into the GEMM): shard
+// r holds rows [r * rows, (r + 1) * rows) in its own buffer (peer-mapped for
+// r != own); its TMA map is maps[r].  Before a peer shard is first read the
+// producer waits (bounded) until ready[r] >= epoch.
+struct AShards {
+  int n;       // 1 = ordinary GEMM (maps[0] covers all of A)
+  int rows;    // rows per shard, a multiple of 128
+  int own;
+  const int* ready;
+  int epoch;
 };
 
 struct GemmArgs {
-  const __nv_bfloat16* a;  // [M, K], row stride lda
+  const __nv_bfloat16* a;  // [M, K], row stride lda (shard 0 when sharded)
+  const __nv_bfloat16* a_shards[kMaxShards];  // per-rank shard bases when shards.n > 1
+  AShards shards;
   const __nv_bfloat16* b;  // [N, K], row stride ldb
   int M, N, K, lda, ldb;
   int epi;
@@ -201,11 +222,31 @@ cudaError_t cacheblend_select(const SelectArgs& a, cudaStream_t stream);
 
 cudaError_t fill_arange_i32(int* out, int n, int start, cudaStream_t stream);
 
+// Owner-side reduction of GEMM -> reduce-scatter partials: waits (bounded)
+// until every sender released flags[s] >= epoch, then
+//   out[row] = residual[row] + bf16(sum_s recv[s][row])   (fixed rank order)
+// and optionally norm_out[row] = RMSNorm(out[row]) * norm_w.
+struct RsReduceArgs {
+  const float* recv;  // [tp, rows, N]
+  int tp, rows, N;
+  const int* flags;   // [tp]
+  int epoch;
+  long long timeout_ns;
+  int* status;
+  const __nv_bfloat16* residual;  // [rows, N]
+  __nv_bfloat16* out;             // [rows, N] (may alias residual)
+  const __nv_bfloat16* norm_w;    // optional [N]
+  __nv_bfloat16* norm_out;        // optional [rows, N]
+  float eps;
+};
+cudaError_t rs_reduce(const RsReduceArgs& a, cudaStream_t stream);
+
 // ------------------------------------------------------------------- p2p ----
 cudaError_t peer_signal(int* flag, int value, const int* value_src, unsigned long long* stamp,
                         cudaStream_t stream);
 cudaError_t wait_flag(const int* flag, int target, long long timeout_ns, int* status,
                       unsigned long long* stamp, cudaStream_t stream);
+cudaError_t peer_signal_many(int* const* addrs, int n, int value, cudaStream_t stream);
 cudaError_t index_i32(const int* src, const int* idx, int* out, int n, cudaStream_t stream);
 
 }  // namespace sc

@@ -52,6 +52,28 @@ __global__ void wait_flag_kernel(const int* flag, int target, long long timeout_
   if (stamp != nullptr) *stamp = global_ns();
 }
 
+struct FlagList {
+  int* addr[kMaxShards];
+  int n;
+};
+
+// One launch releases `value` into up to 8 flag words (one per rank).
+__global__ void peer_signal_many_kernel(FlagList flags, int value) {
+  if (threadIdx.x == 0) __threadfence_system();
+  __syncwarp();
+  if (threadIdx.x < flags.n)
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(flags.addr[threadIdx.x]), "r"(value) : "memory");
+}
+
+cudaError_t peer_signal_many(int* const* addrs, int n, int value, cudaStream_t stream) {
+  if (n < 1 || n > kMaxShards) return cudaErrorInvalidValue;
+  FlagList fl{};
+  for (int i = 0; i < n; ++i) fl.addr[i] = addrs[i];
+  fl.n = n;
+  peer_signal_many_kernel<<<1, 32, 0, stream>>>(fl, value);
+  return cudaGetLastError();
+}
+
 cudaError_t peer_signal(int* flag, int value, const int* value_src, unsigned long long* stamp,
                         cudaStream_t stream) {
   peer_signal_kernel<<<1, 32, 0, stream>>>(flag, value, value_src, stamp);
@@ -61,6 +83,87 @@ cudaError_t peer_signal(int* flag, int value, const int* value_src, unsigned lon
 cudaError_t wait_flag(const int* flag, int target, long long timeout_ns, int* status,
                       unsigned long long* stamp, cudaStream_t stream) {
   wait_flag_kernel<<<1, 32, 0, stream>>>(flag, target, timeout_ns, status, stamp);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ rs_reduce
+// One CTA per owned row.  Thread 0 waits (bounded) for every sender's flag,
+// then the CTA sums the tp fp32 partials in rank order, adds the residual with
+// the HF rounding order (residual + bf16(sum)), and optionally emits the
+// RMSNorm of the new row for the next projection.
+constexpr int kRsThreads = 256;
+constexpr int kRsMaxVec = 8;  // float4 per thread: N <= 8192
+
+__global__ void __launch_bounds__(kRsThreads) rs_reduce_kernel(RsReduceArgs a) {
+  __shared__ int s_fail;
+  __shared__ float red[kRsThreads / 32];
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    s_fail = 0;
+    const unsigned long long start = global_ns();
+    for (int s = 0; s < a.tp && !s_fail; ++s) {
+      while (true) {
+        int v;
+        asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(a.flags + s) : "memory");
+        if (v >= a.epoch) break;
+        if ((long long)(global_ns() - start) > a.timeout_ns) {
+          report_status(a.status, kStatusTimeoutPeerFlag);
+          s_fail = 1;
+          break;
+        }
+        __nanosleep(100);
+      }
+    }
+  }
+  __syncthreads();
+  if (s_fail) return;
+  const int nvec = a.N / 4;
+  float vals[kRsMaxVec][4];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRsMaxVec; ++i) {
+    const int c = tid + i * kRsThreads;
+    if (c >= nvec) break;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < a.tp; ++s) {
+      const float4 p = __ldcg(reinterpret_cast<const float4*>(a.recv + ((size_t)s * a.rows + row) * a.N) + c);
+      acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+    }
+    const uint2 rr = *reinterpret_cast<const uint2*>(a.residual + (size_t)row * a.N + 4 * c);
+    const float2 r0 = unpack_bf16x2(rr.x), r1 = unpack_bf16x2(rr.y);
+    vals[i][0] = bf16_round(r0.x + bf16_round(acc.x));
+    vals[i][1] = bf16_round(r0.y + bf16_round(acc.y));
+    vals[i][2] = bf16_round(r1.x + bf16_round(acc.z));
+    vals[i][3] = bf16_round(r1.y + bf16_round(acc.w));
+    *reinterpret_cast<uint2*>(a.out + (size_t)row * a.N + 4 * c) =
+        make_uint2(pack_bf16x2(vals[i][0], vals[i][1]), pack_bf16x2(vals[i][2], vals[i][3]));
+    ss += vals[i][0] * vals[i][0] + vals[i][1] * vals[i][1] + vals[i][2] * vals[i][2] +
+          vals[i][3] * vals[i][3];
+  }
+  if (a.norm_w == nullptr) return;
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kRsThreads / 32; ++w) tot += red[w];
+  const float rinv = rsqrtf(tot / (float)a.N + a.eps);
+#pragma unroll
+  for (int i = 0; i < kRsMaxVec; ++i) {
+    const int c = tid + i * kRsThreads;
+    if (c >= nvec) break;
+    const uint2 gw = *reinterpret_cast<const uint2*>(a.norm_w + 4 * c);
+    const float2 g0 = unpack_bf16x2(gw.x), g1 = unpack_bf16x2(gw.y);
+    *reinterpret_cast<uint2*>(a.norm_out + (size_t)row * a.N + 4 * c) =
+        make_uint2(pack_bf16x2(g0.x * bf16_round(vals[i][0] * rinv), g0.y * bf16_round(vals[i][1] * rinv)),
+                   pack_bf16x2(g1.x * bf16_round(vals[i][2] * rinv), g1.y * bf16_round(vals[i][3] * rinv)));
+  }
+}
+
+cudaError_t rs_reduce(const RsReduceArgs& a, cudaStream_t stream) {
+  if (a.N % 4 != 0 || a.N / 4 > kRsThreads * kRsMaxVec || a.tp < 1 || a.rows < 1) return cudaErrorInvalidValue;
+  rs_reduce_kernel<<<a.rows, kRsThreads, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

@@ -1,0 +1,202 @@
+"""Tensor-parallel Llama with the collectives fused into the GEMMs (NVLink peer memory).
+
+Layout (one process per GPU, TP group of size tp):
+  * column-parallel: QKV (a rank owns n_heads/tp query heads and
+    n_kv_heads/tp KV heads) and gate/up (ffn/tp in 128-row blocks);
+  * row-parallel: o_proj and down_proj (the matching K slices);
+  * sequence-parallel activations between blocks: rank r owns prompt rows
+    [r * rows, (r + 1) * rows) of the residual stream (rows a multiple of 128;
+    the prompt is padded to tp * rows, padded rows sit after every real
+    position so causal attention never reads them).
+
+Per layer and rank (all inside ONE stream, no host sync, no NCCL):
+  1. AG -> QKV GEMM: the TMA producer reads every rank's normed shard
+     directly from its buffer (peer-mapped over CUDA IPC; plain TMA loads, no
+     multicast), own shard first, after a bounded wait on that shard's ready
+     flag; epilogue = RoPE + local K/V cache write.
+  2. attention of the local heads over all rows.
+  3. o_proj GEMM -> RS: the epilogue stores every fp32 partial tile into the
+     receive slot of the rank that owns the rows (NVLink stores), then a
+     signal kernel releases that owner's flag for this sender.
+  4. owner reduction: bounded wait for all senders, fixed-order sum +
+     residual, fused RMSNorm -> the shard the gate/up all-gather reads.
+  5. AG -> gate/up GEMM (SwiGLU epilogue), 6. down GEMM -> RS, 7. reduction
+     fused with the next layer's input RMSNorm.
+Epoch-numbered flags only ever increase, so one flag word per (kind, sender)
+serves every layer; buffer reuse is safe because each rank reaches the next
+write of a buffer only after consuming data every peer produced after its
+last read of it.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, replace
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..config import ModelConfig
+from ..models.engine import B200Engine, EngineWeights, KVSlot, LayerWeights
+from ..models.weights import GATE_UP_BLOCK
+
+FLAG_X, FLAG_X2, FLAG_RS_O, FLAG_RS_D = 0, 1, 2, 3
+TIMEOUT_NS = int(20e9)
+
+
+class TPGroup:
+    """Peer-mapped buffers shared by the ranks of one TP group."""
+
+    def __init__(self, group=None) -> None:
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.size = dist.get_world_size(group)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self._opened: list[int] = []
+        self._keep: list[torch.Tensor] = []
+
+    def shared(self, nbytes: int) -> tuple[torch.Tensor, list[int]]:
+        """Allocate nbytes on every rank; return (local buffer, device address of each rank's buffer)."""
+        ext = ops.ext()
+        buf, handle = ext.shared_empty(int(nbytes), self.device.index)
+        self._keep.append(buf)
+        handles = [None] * self.size
+        dist.all_gather_object(handles, handle, group=self.group)
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(buf.data_ptr())
+            else:
+                p = ext.shared_open(h)
+                self._opened.append(p)
+                ptrs.append(p)
+        return buf, ptrs
+
+    def close(self) -> None:
+        ext = ops.ext()
+        for p in self._opened:
+            ext.shared_close(p)
+        self._opened.clear()
+
+
+def shard_weights(full: EngineWeights, cfg: ModelConfig, rank: int, tp: int) -> EngineWeights:
+    """Column/row-parallel slices of full engine weights for ``rank``."""
+    D = cfg.head_dim
+    hq, hkv, f = cfg.n_heads // tp, cfg.n_kv_heads // tp, cfg.ffn // tp
+    blk = GATE_UP_BLOCK
+    layers = []
+    for lw in full.layers:
+        q = lw.w_qkv[: cfg.q_size]
+        k = lw.w_qkv[cfg.q_size: cfg.q_size + cfg.kv_size]
+        v = lw.w_qkv[cfg.q_size + cfg.kv_size:]
+        qkv = torch.cat((q[rank * hq * D:(rank + 1) * hq * D], k[rank * hkv * D:(rank + 1) * hkv * D],
+                         v[rank * hkv * D:(rank + 1) * hkv * D])).contiguous()
+        gu = lw.w_gu.view(cfg.ffn // blk, 2 * blk, -1)[rank * f // blk:(rank + 1) * f // blk]
+        layers.append(LayerWeights(
+            ln1=lw.ln1, w_qkv=qkv, w_o=lw.w_o[:, rank * hq * D:(rank + 1) * hq * D].contiguous(), ln2=lw.ln2,
+            w_gu=gu.reshape(2 * f, -1).contiguous(), w_down=lw.w_down[:, rank * f:(rank + 1) * f].contiguous()))
+    return EngineWeights(embed=full.embed, layers=layers, norm=full.norm, lm_head=full.lm_head)
+
+
+def local_config(cfg: ModelConfig, tp: int) -> ModelConfig:
+    if cfg.n_heads % tp or cfg.n_kv_heads % tp or cfg.ffn % (tp * GATE_UP_BLOCK):
+        raise ValueError("heads, kv heads and ffn/128 must divide by the TP size")
+    return replace(cfg, n_heads=cfg.n_heads // tp, n_kv_heads=cfg.n_kv_heads // tp, ffn=cfg.ffn // tp)
+
+
+class TPEngine:
+    """Sequence/tensor-parallel prefill over a TP group with fused collectives."""
+
+    def __init__(self, cfg: ModelConfig, weights: EngineWeights, group: TPGroup, *, max_rows: int,
+                 max_positions: int = 65536) -> None:
+        self.full_cfg = cfg
+        self.tp = group.size
+        self.rank = group.rank
+        self.group = group
+        self.lcfg = local_config(cfg, self.tp)
+        # the local engine runs the per-rank kernels (attention, norms, decode)
+        self.engine = B200Engine(self.lcfg, weights, group.device, max_positions=max_positions)
+        self.ext = self.engine.ext
+        self.max_rows = int(math.ceil(max_rows / 128) * 128)
+        d = cfg.d_model
+        R = self.max_rows
+        self.x_buf, self.x_ptrs = group.shared(R * d * 2)
+        self.x2_buf, self.x2_ptrs = group.shared(R * d * 2)
+        self.recv_o_buf, self.recv_o_ptrs = group.shared(self.tp * R * d * 4)
+        self.recv_d_buf, self.recv_d_ptrs = group.shared(self.tp * R * d * 4)
+        self.flag_buf, self.flag_ptrs = group.shared(4 * self.tp * 4)
+        self.flags = self.flag_buf.view(torch.int32).view(4, self.tp)
+        self.status = torch.zeros(1, dtype=torch.int32, device=group.device)
+        self.epoch = 0
+
+    @classmethod
+    def from_full(cls, cfg: ModelConfig, full: EngineWeights, group: TPGroup, **kw) -> "TPEngine":
+        return cls(cfg, shard_weights(full, cfg, group.rank, group.size), group, **kw)
+
+    # ---------------------------------------------------------- helpers
+    def _flag_addr(self, owner: int, kind: int, sender: int) -> int:
+        return self.flag_ptrs[owner] + 4 * (kind * self.tp + sender)
+
+    def _signal_all(self, kind: int, epoch: int) -> None:
+        """Release flag (kind, me) on every rank (self included), one launch."""
+        self.ext.peer_signal_many([self._flag_addr(r, kind, self.rank) for r in range(self.tp)], epoch)
+
+    def new_slot(self, capacity: int) -> KVSlot:
+        return self.engine.new_slot(capacity)
+
+    # ------------------------------------------------------------ prefill
+    def prefill(self, ids: torch.Tensor, slot: KVSlot) -> tuple[torch.Tensor, int, int]:
+        """Prefill ids (all ranks pass the same int32 device ids).
+
+        Returns (this rank's final-normed hidden shard [rows, d], rows, padded
+        length).  The shard owning row T-1 holds the last prompt row.
+        """
+        ext, eng, cfg, lc = self.ext, self.engine, self.full_cfg, self.lcfg
+        T = ids.numel()
+        rows = int(math.ceil(T / (self.tp * 128)) * 128)
+        if rows > self.max_rows:
+            raise ValueError("prompt exceeds the TP buffers")
+        Tp = rows * self.tp
+        if Tp > slot.capacity:
+            raise ValueError("slot capacity below the padded prompt")
+        d = cfg.d_model
+        ids_p = torch.zeros(Tp, dtype=torch.int32, device=ids.device)
+        ids_p[:T] = ids
+        own = slice(self.rank * rows, (self.rank + 1) * rows)
+        h = eng.ws.get("tp_h", (rows, d), torch.bfloat16)
+        ext.embedding(ids_p[own], eng.w.embed, h)
+        x = self.x_buf.view(torch.bfloat16)[: rows * d].view(rows, d)
+        x2 = self.x2_buf.view(torch.bfloat16)[: rows * d].view(rows, d)
+        recv_o = self.recv_o_buf.view(torch.float32)[: self.tp * rows * d].view(self.tp, rows, d)
+        recv_d = self.recv_d_buf.view(torch.float32)[: self.tp * rows * d].view(self.tp, rows, d)
+        ext.rmsnorm(h, None, eng.w.layers[0].ln1, cfg.rms_eps, x)
+        pos = eng._arange("pos", Tp)
+        q = eng.ws.get("q", (Tp, lc.q_size), torch.bfloat16)
+        attn = eng.ws.get("attn", (Tp, lc.q_size), torch.bfloat16)
+        act = eng.ws.get("act", (Tp, lc.ffn), torch.bfloat16)
+        bn = eng.bn
+        for layer, lw in enumerate(eng.w.layers):
+            self.epoch += 1
+            e = self.epoch
+            self._signal_all(FLAG_X, e)
+            ext.gemm_ag_qkv(self.x_ptrs, rows, self.rank, self.flags[FLAG_X], e, d, lw.w_qkv, q, slot.k(layer),
+                            slot.v(layer), pos, pos, eng.rope, lc.n_heads, lc.n_kv_heads, bn)
+            ext.attention_prefill(q, None, pos, slot.k(layer), slot.v(layer), None, Tp, lc.n_heads, eng.scale, attn)
+            ext.gemm_rs(attn, lw.w_o, self.recv_o_ptrs, rows, self.rank, bn)
+            self._signal_all(FLAG_RS_O, e)
+            ext.rs_reduce(recv_o, self.flags[FLAG_RS_O], e, TIMEOUT_NS, self.status, h, h, lw.ln2, x2, cfg.rms_eps)
+            self._signal_all(FLAG_X2, e)
+            ext.gemm_ag_swiglu(self.x2_ptrs, rows, self.rank, self.flags[FLAG_X2], e, d, lw.w_gu, act, bn)
+            ext.gemm_rs(act, lw.w_down, self.recv_d_ptrs, rows, self.rank, bn)
+            self._signal_all(FLAG_RS_D, e)
+            nxt = eng.w.layers[layer + 1].ln1 if layer + 1 < len(eng.w.layers) else eng.w.norm
+            ext.rs_reduce(recv_d, self.flags[FLAG_RS_D], e, TIMEOUT_NS, self.status, h, h, nxt, x, cfg.rms_eps)
+        return x, rows, Tp
+
+    def check_status(self) -> None:
+        st = int(self.status.item())
+        if st:
+            raise RuntimeError(f"a tensor-parallel wait timed out (status {st})")
+
+    def close(self) -> None:
+        self.group.close()

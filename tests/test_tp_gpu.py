@@ -1,0 +1,80 @@
+"""Tensor-parallel prefill with fused AG->GEMM / GEMM->RS against the single-GPU engine (2 GPUs)."""
+import json
+import os
+import socket
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, out_dir):
+    import torch.distributed as dist
+
+    from sparsecache_b200.config import get_model_config
+    from sparsecache_b200.models.engine import B200Engine, EngineWeights
+    from sparsecache_b200.models.llama import LlamaOracle
+    from sparsecache_b200.parallel.tp import TPEngine, TPGroup
+    from sparsecache_b200.synthetic import make_requests
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    result = {"rank": rank}
+    try:
+        cfg = get_model_config("tiny128")
+        oracle = LlamaOracle.random_init(cfg, seed=11, std=0.05)
+        full = EngineWeights.from_oracle(oracle, dev)
+        group = TPGroup()
+        tpe = TPEngine.from_full(cfg, full, group, max_rows=1024)
+        req = make_requests("tiny_plumbing", cfg)[0]
+        T = req.prompt_tokens
+        ids = torch.tensor(req.prompt, dtype=torch.int32, device=dev)
+        slot = tpe.new_slot(2 * 1024)
+        x, rows, Tp = tpe.prefill(ids, slot)
+        torch.cuda.synchronize()
+        tpe.check_status()
+        ref = B200Engine(cfg, full, dev, max_positions=8192)
+        rslot = ref.new_slot(2048)
+        h = ref.prefill(ids, rslot).float()
+        hn = h * torch.rsqrt(h.square().mean(-1, keepdim=True) + cfg.rms_eps) * full.norm.float()
+        lo, hi = rank * rows, min((rank + 1) * rows, T)
+        err = float(((x[: hi - lo].float() - hn[lo:hi]).abs().max() / hn[lo:hi].abs().max()).item())
+        hkv = cfg.n_kv_heads // world
+        kv_err = 0.0
+        for layer in range(cfg.n_layers):
+            a = slot.k(layer)[:, :T].float()
+            b = rslot.k(layer)[rank * hkv:(rank + 1) * hkv, :T].float()
+            kv_err = max(kv_err, float(((a - b).abs().max() / b.abs().max()).item()))
+        result.update(hidden_rel_err=err, kv_rel_err=kv_err, rows=rows, padded=Tp)
+        dist.barrier()
+        tpe.close()
+        dist.barrier()
+    except Exception as exc:  # noqa: BLE001
+        result["error"] = repr(exc)
+    finally:
+        with open(os.path.join(out_dir, f"r{rank}.json"), "w") as f:
+            json.dump(result, f)
+        dist.destroy_process_group()
+
+
+def test_tp2_prefill_matches_single_gpu(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        res = json.loads((tmp_path / f"r{r}.json").read_text())
+        assert "error" not in res, res
+        assert res["hidden_rel_err"] < 3e-2, res
+        assert res["kv_rel_err"] < 3e-2, res
