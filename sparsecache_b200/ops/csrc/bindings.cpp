@@ -157,6 +157,9 @@ void gemm_qkv(Tensor a, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_cac
   run_gemm(g);
 }
 
+sc::GemvArgs base_gemv(const Tensor& x, const Tensor& w, c10::optional<Tensor> norm_w, double eps, int epi);
+void run_gemv(const sc::GemvArgs& g);
+
 // ------------------------------------------------- tensor-parallel GEMMs
 // A is row-sharded over `shard_ptrs` (device addresses, peers' shards mapped
 // with CUDA IPC), each [rows, K] with row stride K; the all-gather is fused
@@ -239,7 +242,8 @@ void gemm_rs(Tensor a, Tensor w, std::vector<int64_t> dst_ptrs, int64_t rows, in
 }
 
 void rs_reduce(Tensor recv, Tensor flags, int64_t epoch, int64_t timeout_ns, Tensor status, Tensor residual,
-               Tensor out, c10::optional<Tensor> norm_w, c10::optional<Tensor> norm_out, double eps) {
+               Tensor out, c10::optional<Tensor> norm_w, c10::optional<Tensor> norm_out, double eps,
+               c10::optional<Tensor> epoch_ptr, int64_t epoch_mul) {
   const c10::cuda::CUDAGuard guard(recv.device());
   CHECK_F32(recv); CHECK_I32(flags); CHECK_I32(status);
   TORCH_CHECK(recv.dim() == 3 && recv.is_contiguous(), "recv [tp, rows, N]");
@@ -264,7 +268,36 @@ void rs_reduce(Tensor recv, Tensor flags, int64_t epoch, int64_t timeout_ns, Ten
     a.norm_out = reinterpret_cast<__nv_bfloat16*>(norm_out->data_ptr());
   }
   a.eps = (float)eps;
+  if (epoch_ptr.has_value() && epoch_ptr->defined()) {
+    CHECK_I32(*epoch_ptr);
+    a.epoch_ptr = epoch_ptr->data_ptr<int>();
+    a.epoch_mul = (int)epoch_mul;
+  }
   check_cuda(sc::rs_reduce(a, cur_stream()), "rs_reduce");
+}
+
+// Row-parallel decode projection with the all-reduce fused into the epilogue.
+void gemv_allreduce(Tensor x, Tensor w, c10::optional<Tensor> norm_w, double eps, std::vector<int64_t> dst_ptrs,
+                    std::vector<int64_t> flag_ptrs, int64_t sender, int64_t epoch, c10::optional<Tensor> epoch_ptr,
+                    int64_t epoch_mul, Tensor counter) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto g = base_gemv(x, w, norm_w, eps, sc::GEMV_ALLREDUCE);
+  TORCH_CHECK(dst_ptrs.size() == flag_ptrs.size() && !dst_ptrs.empty() && dst_ptrs.size() <= 8, "1..8 ranks");
+  for (size_t r = 0; r < dst_ptrs.size(); ++r) {
+    g.ar_dst[r] = reinterpret_cast<float*>(dst_ptrs[r]);
+    g.ar_flag[r] = reinterpret_cast<int*>(flag_ptrs[r]);
+  }
+  g.ar_tp = (int)dst_ptrs.size();
+  g.ar_sender = (int)sender;
+  g.ar_epoch = (int)epoch;
+  if (epoch_ptr.has_value() && epoch_ptr->defined()) {
+    CHECK_I32(*epoch_ptr);
+    g.ar_epoch_ptr = epoch_ptr->data_ptr<int>();
+    g.ar_epoch_mul = (int)epoch_mul;
+  }
+  CHECK_I32(counter);
+  g.counter = reinterpret_cast<unsigned int*>(counter.data_ptr<int>());
+  run_gemv(g);
 }
 
 // ---------------------------------------------------------------- p2p
@@ -634,7 +667,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_ag_qkv", &gemm_ag_qkv);
   m.def("gemm_ag_swiglu", &gemm_ag_swiglu);
   m.def("gemm_rs", &gemm_rs);
-  m.def("rs_reduce", &rs_reduce);
+  m.def("rs_reduce", &rs_reduce, py::arg("recv"), py::arg("flags"), py::arg("epoch"), py::arg("timeout_ns"),
+        py::arg("status"), py::arg("residual"), py::arg("out"), py::arg("norm_w"), py::arg("norm_out"),
+        py::arg("eps"), py::arg("epoch_ptr") = py::none(), py::arg("epoch_mul") = 0);
+  m.def("gemv_allreduce", &gemv_allreduce);
   m.def("shared_empty", &shared_empty);
   m.def("shared_open", &shared_open);
   m.def("shared_close", &shared_close);

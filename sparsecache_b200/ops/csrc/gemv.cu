@@ -251,6 +251,15 @@ __global__ void __launch_bounds__(kThreads)
           dst[i + 64] = __float2bfloat16_rn(o1);
           break;
         }
+        case GEMV_ALLREDUCE: {
+          // row-parallel partial -> every rank's receive slot for this sender
+          for (int r = 0; r < a.ar_tp; ++r) {
+            float* dst = a.ar_dst[r] + ((size_t)a.ar_sender * M + m) * a.N;
+            dst[r0] = v0;
+            dst[r1] = v1;
+          }
+          break;
+        }
         case GEMV_ARGMAX: {
           // argmax over bf16-rounded logits, first index on ties
           const float b0 = bf16_round(v0), b1 = bf16_round(v1);
@@ -262,6 +271,24 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
 
+  if (a.epi == GEMV_ALLREDUCE) {
+    // the last CTA to finish publishes this rank's partial to every rank
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0) {
+      const unsigned prev = atomicAdd(a.counter, 1u);
+      s_last = (prev == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (s_last) {
+      __threadfence_system();
+      const int epoch = a.ar_epoch_ptr ? *a.ar_epoch_ptr * a.ar_epoch_mul + a.ar_epoch : a.ar_epoch;
+      if (tid < a.ar_tp)
+        asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(a.ar_flag[tid]), "r"(epoch) : "memory");
+      if (tid == 0) *a.counter = 0u;
+    }
+    return;
+  }
   if (a.epi != GEMV_ARGMAX) return;
 
   // ---- argmax: CTA partials, then the last CTA reduces ----

@@ -86,7 +86,8 @@ enum GemvEpi : int {
   GEMV_RESIDUAL = 1,
   GEMV_SWIGLU = 2,
   GEMV_QKV = 3,
-  GEMV_ARGMAX = 4
+  GEMV_ARGMAX = 4,
+  GEMV_ALLREDUCE = 5
 };
 
 struct GemvArgs {
@@ -122,6 +123,17 @@ struct GemvArgs {
   __nv_bfloat16* next_hidden;
   int* pos_advance;    // optional device scalars [n_advance] each incremented by M at the end
   int n_advance;       // number of scalars at pos_advance (0 means 1)
+  // ALLREDUCE (row-parallel decode projection under tensor parallelism): the
+  // fp32 partial of every row goes to every rank's receive buffer
+  // ar_dst[r][ar_sender][m][N] (NVLink stores); the last CTA then releases
+  // ar_flag[r] = ar_epoch on every rank (fence.sys + st.release.sys).
+  float* ar_dst[8];
+  int* ar_flag[8];
+  int ar_tp;
+  int ar_sender;
+  int ar_epoch;          // epoch = ar_epoch_ptr ? *ar_epoch_ptr * ar_epoch_mul + ar_epoch : ar_epoch
+  const int* ar_epoch_ptr;
+  int ar_epoch_mul;
   int num_sms;
 };
 
@@ -230,7 +242,9 @@ struct RsReduceArgs {
   const float* recv;  // [tp, rows, N]
   int tp, rows, N;
   const int* flags;   // [tp]
-  int epoch;
+  int epoch;          // epoch = epoch_ptr ? *epoch_ptr * epoch_mul + epoch : epoch
+  const int* epoch_ptr;
+  int epoch_mul;
   long long timeout_ns;
   int* status;
   const __nv_bfloat16* residual;  // [rows, N]

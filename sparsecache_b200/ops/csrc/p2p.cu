@@ -101,12 +101,13 @@ __global__ void __launch_bounds__(kRsThreads) rs_reduce_kernel(RsReduceArgs a) {
   const int tid = threadIdx.x;
   if (tid == 0) {
     s_fail = 0;
+    const int epoch = a.epoch_ptr ? *a.epoch_ptr * a.epoch_mul + a.epoch : a.epoch;
     const unsigned long long start = global_ns();
     for (int s = 0; s < a.tp && !s_fail; ++s) {
       while (true) {
         int v;
         asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(a.flags + s) : "memory");
-        if (v >= a.epoch) break;
+        if (v >= epoch) break;
         if ((long long)(global_ns() - start) > a.timeout_ns) {
           report_status(a.status, kStatusTimeoutPeerFlag);
           s_fail = 1;

@@ -41,6 +41,8 @@ from ..models.engine import B200Engine, EngineWeights, KVSlot, LayerWeights
 from ..models.weights import GATE_UP_BLOCK
 
 FLAG_X, FLAG_X2, FLAG_RS_O, FLAG_RS_D = 0, 1, 2, 3
+FLAG_AR_O, FLAG_AR_D, FLAG_TOKEN, FLAG_TOKEN_EPOCH = 4, 5, 6, 7
+N_FLAG_KINDS = 8
 TIMEOUT_NS = int(20e9)
 
 
@@ -124,10 +126,15 @@ class TPEngine:
         self.x2_buf, self.x2_ptrs = group.shared(R * d * 2)
         self.recv_o_buf, self.recv_o_ptrs = group.shared(self.tp * R * d * 4)
         self.recv_d_buf, self.recv_d_ptrs = group.shared(self.tp * R * d * 4)
-        self.flag_buf, self.flag_ptrs = group.shared(4 * self.tp * 4)
-        self.flags = self.flag_buf.view(torch.int32).view(4, self.tp)
+        self.flag_buf, self.flag_ptrs = group.shared(N_FLAG_KINDS * self.tp * 4)
+        self.flags = self.flag_buf.view(torch.int32).view(N_FLAG_KINDS, self.tp)
+        # decode all-reduce receive slots [tp, 8 rows, d] fp32 (O and down)
+        self.ar_o_buf, self.ar_o_ptrs = group.shared(self.tp * 8 * d * 4)
+        self.ar_d_buf, self.ar_d_ptrs = group.shared(self.tp * 8 * d * 4)
+        self.ar_counters = torch.zeros(2, dtype=torch.int32, device=group.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=group.device)
         self.epoch = 0
+        self.token_epoch = 0
 
     @classmethod
     def from_full(cls, cfg: ModelConfig, full: EngineWeights, group: TPGroup, **kw) -> "TPEngine":
@@ -192,6 +199,87 @@ class TPEngine:
             nxt = eng.w.layers[layer + 1].ln1 if layer + 1 < len(eng.w.layers) else eng.w.norm
             ext.rs_reduce(recv_d, self.flags[FLAG_RS_D], e, TIMEOUT_NS, self.status, h, h, nxt, x, cfg.rms_eps)
         return x, rows, Tp
+
+    # ------------------------------------------------------------- decode
+    def first_token(self, x_shard: torch.Tensor, rows: int, T: int, *, max_new: int) -> None:
+        """The owner of prompt row T-1 runs the LM head and sends the token to every rank."""
+        eng, ext = self.engine, self.ext
+        owner = (T - 1) // rows
+        self.token_epoch += 1
+        b = eng._decode_buffers(max_new)
+        if self.rank == owner:
+            lr = (T - 1) - owner * rows
+            b["counter"].zero_()
+            ext.gemv_argmax(x_shard[lr:lr + 1], eng.w.lm_head, None, self.full_cfg.rms_eps, b["pv"], b["pi"],
+                            b["counter"], b["tok"], None, None, None, None, None)
+            for r in range(self.tp):
+                ext.peer_signal(self._flag_addr(r, FLAG_TOKEN, owner), 0, None, b["tok"][0:1])
+            ext.peer_signal_many([self._flag_addr(r, FLAG_TOKEN_EPOCH, owner) for r in range(self.tp)],
+                                 self.token_epoch)
+        ext.wait_flag(self.flags[FLAG_TOKEN_EPOCH], owner, self.token_epoch, TIMEOUT_NS, self.status)
+        tok = self.flags[FLAG_TOKEN, owner:owner + 1]
+        ext.embedding(tok, eng.w.embed, b["h"][:1])
+        b["log"][0:1].copy_(tok)
+        b["gen"].fill_(1)
+        b["counter"].zero_()
+        # keep the monotonic step counter pos[3]; reset position / slot / view
+        b["pos"][:3].fill_(T)
+
+    def _decode_step(self, slot: KVSlot, splits: int) -> None:
+        eng, ext, cfg, lc = self.engine, self.ext, self.full_cfg, self.lcfg
+        b = eng._decode_buffers()
+        h, pos = b["h"][:1], b["pos"]
+        step = pos[3:4]
+        mul = 2 * lc.n_layers
+        ar_o = self.ar_o_buf.view(torch.float32)[: self.tp * cfg.d_model].view(self.tp, 1, cfg.d_model)
+        ar_d = self.ar_d_buf.view(torch.float32)[: self.tp * cfg.d_model].view(self.tp, 1, cfg.d_model)
+        fo = [self._flag_addr(r, FLAG_AR_O, self.rank) for r in range(self.tp)]
+        fd = [self._flag_addr(r, FLAG_AR_D, self.rank) for r in range(self.tp)]
+        for layer, lw in enumerate(eng.w.layers):
+            ext.gemv_qkv(h, lw.w_qkv, lw.ln1, cfg.rms_eps, b["q"][:1], slot.k(layer), slot.v(layer), pos[0:1],
+                         eng.rope, lc.n_heads, lc.n_kv_heads, slot=pos[1:2])
+            ext.attention_decode(b["q"][:1], slot.k(layer), slot.v(layer), pos[0:1], lc.n_heads, eng.scale, splits,
+                                 b["attn"][:1])
+            ext.gemv_allreduce(b["attn"][:1], lw.w_o, None, cfg.rms_eps, self.ar_o_ptrs, fo, self.rank,
+                               2 * layer + 1, step, mul, self.ar_counters[0:1])
+            ext.rs_reduce(ar_o, self.flags[FLAG_AR_O], 2 * layer + 1, TIMEOUT_NS, self.status, h, h, None, None,
+                          cfg.rms_eps, step, mul)
+            ext.gemv_swiglu(h, lw.w_gu, lw.ln2, cfg.rms_eps, b["act"][:1])
+            ext.gemv_allreduce(b["act"][:1], lw.w_down, None, cfg.rms_eps, self.ar_d_ptrs, fd, self.rank,
+                               2 * layer + 2, step, mul, self.ar_counters[1:2])
+            ext.rs_reduce(ar_d, self.flags[FLAG_AR_D], 2 * layer + 2, TIMEOUT_NS, self.status, h, h, None, None,
+                          cfg.rms_eps, step, mul)
+        ext.gemv_argmax(h, eng.w.lm_head, eng.w.norm, cfg.rms_eps, b["pv"], b["pi"], b["counter"], b["tok"],
+                        b["log"], b["gen"], eng.w.embed, h, pos, 4)
+
+    def decode(self, slot: KVSlot, n_steps: int, *, use_graph: bool = True) -> None:
+        """Greedy decode across the TP group; every rank runs the same steps."""
+        eng = self.engine
+        splits = eng._decode_splits(slot.capacity)
+        if not use_graph:
+            for _ in range(n_steps):
+                self._decode_step(slot, splits)
+            return
+        key = ("tp", id(slot), splits)
+        graph = eng._graphs.get(key)
+        if graph is None:
+            # capture needs warm launch attributes but must not advance the
+            # group's state: warm up with one real step, then roll back only
+            # the local scalars (flags and the step counter keep increasing)
+            b = eng._decode_buffers()
+            saved = {k: b[k].clone() for k in ("h", "gen", "log", "tok")}
+            saved_pos = b["pos"][:3].clone()
+            self._decode_step(slot, splits)
+            for k, v in saved.items():
+                b[k].copy_(v)
+            b["pos"][:3].copy_(saved_pos)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self._decode_step(slot, splits)
+            eng._graphs[key] = graph
+        for _ in range(n_steps):
+            graph.replay()
 
     def check_status(self) -> None:
         st = int(self.status.item())
