@@ -235,7 +235,8 @@ void gemm_rs(Tensor a, Tensor w, std::vector<int64_t> dst_ptrs, int64_t rows, in
   TORCH_CHECK(!dst_ptrs.empty() && (int)dst_ptrs.size() <= sc::kMaxShards, "1..8 owners");
   TORCH_CHECK(rows % 128 == 0 && rows * (int64_t)dst_ptrs.size() == a.size(0), "rows per owner");
   TORCH_CHECK(g.N % 32 == 0, "N must be a multiple of 32");
-  for (size_t r = 0; r < dst_ptrs.size(); ++r) g.ep.rs_dst[r] = reinterpret_cast<float*>(dst_ptrs[r]);
+  for (size_t r = 0; r < dst_ptrs.size(); ++r) g.ep.rs_dst[r] = reinterpret_cast<void*>(dst_ptrs[r]);
+  TORCH_CHECK(g.N % 64 == 0, "N must be a multiple of 64");
   g.ep.rs_rows = (int)rows;
   g.ep.rs_sender = (int)sender;
   run_gemm(g);
@@ -245,12 +246,14 @@ void rs_reduce(Tensor recv, Tensor flags, int64_t epoch, int64_t timeout_ns, Ten
                Tensor out, c10::optional<Tensor> norm_w, c10::optional<Tensor> norm_out, double eps,
                c10::optional<Tensor> epoch_ptr, int64_t epoch_mul) {
   const c10::cuda::CUDAGuard guard(recv.device());
-  CHECK_F32(recv); CHECK_I32(flags); CHECK_I32(status);
+  TORCH_CHECK(recv.scalar_type() == torch::kFloat32 || recv.scalar_type() == torch::kBFloat16, "recv fp32/bf16");
+  CHECK_I32(flags); CHECK_I32(status);
   TORCH_CHECK(recv.dim() == 3 && recv.is_contiguous(), "recv [tp, rows, N]");
   check_matrix(residual, "residual");
   check_matrix(out, "out");
   sc::RsReduceArgs a{};
-  a.recv = recv.data_ptr<float>();
+  a.recv = recv.data_ptr();
+  a.recv_bf16 = recv.scalar_type() == torch::kBFloat16 ? 1 : 0;
   a.tp = (int)recv.size(0);
   a.rows = (int)recv.size(1);
   a.N = (int)recv.size(2);
@@ -663,6 +666,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     std::vector<int*> p;
     for (auto a : addrs) p.push_back(reinterpret_cast<int*>(a));
     check_cuda(sc::peer_signal_many(p.data(), (int)p.size(), (int)value, cur_stream()), "peer_signal_many");
+  });
+  m.def("memcpy_async", [](int64_t dst, int64_t src, int64_t nbytes) {
+    // copy-engine transfer on the current stream (peer addresses included: UVA)
+    check_cuda(cudaMemcpyAsync(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), (size_t)nbytes,
+                               cudaMemcpyDefault, cur_stream()),
+               "memcpy_async");
   });
   m.def("gemm_ag_qkv", &gemm_ag_qkv);
   m.def("gemm_ag_swiglu", &gemm_ag_swiglu);

@@ -42,7 +42,8 @@ struct GemmCfg {
   static constexpr int kBBytes = BN * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+  static constexpr int kEpiStageBytes = 4 * 32 * 33 * 4;  // per-warp transpose tiles (EPI_RS)
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256 + kEpiStageBytes;
 };
 
 struct alignas(8) GemmBarriers {
@@ -84,7 +85,7 @@ __device__ __forceinline__ void load_row32(const __nv_bfloat16* src, float* v) {
 
 template <int BN, int EPI>
 __device__ __forceinline__ void gemm_epilogue_tile(const GemmEpilogue& ep, uint32_t tacc,
-                                                   int row, int tile_n, int M, int N) {
+                                                   int row, int tile_n, int M, int N, uint32_t* stage) {
   const bool row_ok = row < M;
   if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
 #pragma unroll 1
@@ -127,24 +128,37 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmEpilogue& ep, uint3
       }
     }
   } else if constexpr (EPI == EPI_RS) {
-    // fused reduce-scatter: the fp32 partial of this row goes straight into
-    // the receive slot of the rank that owns the row (NVLink store for peers)
-    const int shard = row_ok ? row / ep.rs_rows : 0;
-    const int lrow = row - shard * ep.rs_rows;
+    // fused reduce-scatter: this warp's 32 rows (one owner, rs_rows is a
+    // multiple of 128) are converted to bf16 partials and staged through
+    // shared memory, so every warp store writes one contiguous 128-byte row
+    // segment into the owner's receive slot (NVLink stores for peers)
+    const int lane = threadIdx.x & 31;
+    const int row_base = row - lane;
+    const int shard = row_base < M ? row_base / ep.rs_rows : 0;
+    const int lrow_base = row_base - shard * ep.rs_rows;
+    __nv_bfloat16* dst_base = reinterpret_cast<__nv_bfloat16*>(ep.rs_dst[shard]) +
+                              ((size_t)ep.rs_sender * ep.rs_rows + lrow_base) * N;
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tacc + c * 32, r);
+    for (int c = 0; c < BN / 64; ++c) {
+      uint32_t a[32], b[32];
+      tmem_ld_32x32b_x32(tacc + c * 64, a);
+      tmem_ld_32x32b_x32(tacc + c * 64 + 32, b);
       tmem_ld_wait();
-      const int col = tile_n * BN + c * 32;
-      if (row_ok && col < N) {
-        float4* dst = reinterpret_cast<float4*>(
-            ep.rs_dst[shard] + ((size_t)ep.rs_sender * ep.rs_rows + lrow) * N + col);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                               __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+      for (int i = 0; i < 16; ++i) {
+        stage[lane * 33 + i] = pack_bf16x2(__uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1]));
+        stage[lane * 33 + 16 + i] = pack_bf16x2(__uint_as_float(b[2 * i]), __uint_as_float(b[2 * i + 1]));
       }
+      __syncwarp();
+      const int col = tile_n * BN + c * 64;
+      if (col < N) {
+#pragma unroll 4
+        for (int r = 0; r < 32; ++r) {
+          if (row_base + r < M)
+            *reinterpret_cast<uint32_t*>(dst_base + (size_t)r * N + col + 2 * lane) = stage[r * 33 + lane];
+        }
+      }
+      __syncwarp();
     }
   } else if constexpr (EPI == EPI_QKV) {
     int pos = 0, slot = 0;
@@ -261,6 +275,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(smem + S * Cfg::kStageBytes);
+  uint32_t* epi_stage = reinterpret_cast<uint32_t*>(smem + S * Cfg::kStageBytes + 256);
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -397,7 +412,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
       const int row = tm * kGemmBM + quarter * 32 + lane;
-      gemm_epilogue_tile<BN, EPI>(ep, tacc, row, tn, M, N);
+      gemm_epilogue_tile<BN, EPI>(ep, tacc, row, tn, M, N, epi_stage + quarter * (32 * 33));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->tmem_empty[buf]);

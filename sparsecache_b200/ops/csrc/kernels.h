@@ -45,9 +45,9 @@ struct GemmEpilogue {
   __nv_bfloat16* k_peer;
   __nv_bfloat16* v_peer;
   // EPI_RS (GEMM -> reduce-scatter): rows [r * rs_rows, (r + 1) * rs_rows)
-  // belong to rank r; their fp32 partial tile is stored into rank r's receive
+  // belong to rank r; their bf16 partial tile is stored into rank r's receive
   // buffer (local or peer-mapped) at slot rs_sender: rs_dst[r][rs_sender][row][N]
-  float* rs_dst[kMaxShards];
+  void* rs_dst[kMaxShards];
   int rs_rows;
   int rs_sender;
 };
@@ -239,7 +239,8 @@ cudaError_t fill_arange_i32(int* out, int n, int start, cudaStream_t stream);
 //   out[row] = residual[row] + bf16(sum_s recv[s][row])   (fixed rank order)
 // and optionally norm_out[row] = RMSNorm(out[row]) * norm_w.
 struct RsReduceArgs {
-  const float* recv;  // [tp, rows, N]
+  const void* recv;   // [tp, rows, N], fp32 or bf16 (recv_bf16)
+  int recv_bf16;
   int tp, rows, N;
   const int* flags;   // [tp]
   int epoch;          // epoch = epoch_ptr ? *epoch_ptr * epoch_mul + epoch : epoch

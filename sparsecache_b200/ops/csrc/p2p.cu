@@ -128,8 +128,15 @@ __global__ void __launch_bounds__(kRsThreads) rs_reduce_kernel(RsReduceArgs a) {
     if (c >= nvec) break;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int s = 0; s < a.tp; ++s) {
-      const float4 p = __ldcg(reinterpret_cast<const float4*>(a.recv + ((size_t)s * a.rows + row) * a.N) + c);
-      acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+      const size_t off = ((size_t)s * a.rows + row) * a.N;
+      if (a.recv_bf16) {
+        const uint2 p = __ldcg(reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(a.recv) + off) + c);
+        const float2 p0 = unpack_bf16x2(p.x), p1 = unpack_bf16x2(p.y);
+        acc.x += p0.x; acc.y += p0.y; acc.z += p1.x; acc.w += p1.y;
+      } else {
+        const float4 p = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.recv) + off) + c);
+        acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+      }
     }
     const uint2 rr = *reinterpret_cast<const uint2*>(a.residual + (size_t)row * a.N + 4 * c);
     const float2 r0 = unpack_bf16x2(rr.x), r1 = unpack_bf16x2(rr.y);

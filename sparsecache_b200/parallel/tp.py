@@ -42,7 +42,8 @@ from ..models.weights import GATE_UP_BLOCK
 
 FLAG_X, FLAG_X2, FLAG_RS_O, FLAG_RS_D = 0, 1, 2, 3
 FLAG_AR_O, FLAG_AR_D, FLAG_TOKEN, FLAG_TOKEN_EPOCH = 4, 5, 6, 7
-N_FLAG_KINDS = 8
+FLAG_STAGE_X, FLAG_STAGE_X2 = 8, 9  # local: a peer shard has landed in the staging buffer
+N_FLAG_KINDS = 10
 TIMEOUT_NS = int(20e9)
 
 
@@ -124,8 +125,9 @@ class TPEngine:
         R = self.max_rows
         self.x_buf, self.x_ptrs = group.shared(R * d * 2)
         self.x2_buf, self.x2_ptrs = group.shared(R * d * 2)
-        self.recv_o_buf, self.recv_o_ptrs = group.shared(self.tp * R * d * 4)
-        self.recv_d_buf, self.recv_d_ptrs = group.shared(self.tp * R * d * 4)
+        # bf16 partials of the row-parallel GEMMs, one slot per sender
+        self.recv_o_buf, self.recv_o_ptrs = group.shared(self.tp * R * d * 2)
+        self.recv_d_buf, self.recv_d_ptrs = group.shared(self.tp * R * d * 2)
         self.flag_buf, self.flag_ptrs = group.shared(N_FLAG_KINDS * self.tp * 4)
         self.flags = self.flag_buf.view(torch.int32).view(N_FLAG_KINDS, self.tp)
         # decode all-reduce receive slots [tp, 8 rows, d] fp32 (O and down)
@@ -135,6 +137,11 @@ class TPEngine:
         self.status = torch.zeros(1, dtype=torch.int32, device=group.device)
         self.epoch = 0
         self.token_epoch = 0
+        # local staging of the gathered activations: every remote shard crosses
+        # NVLink once (copy engine), the GEMM re-reads tiles from local memory
+        self.stage_x = torch.empty(self.tp * R, d, device=group.device, dtype=torch.bfloat16)
+        self.stage_x2 = torch.empty(self.tp * R, d, device=group.device, dtype=torch.bfloat16)
+        self.side = torch.cuda.Stream(device=group.device)
 
     @classmethod
     def from_full(cls, cfg: ModelConfig, full: EngineWeights, group: TPGroup, **kw) -> "TPEngine":
@@ -150,6 +157,31 @@ class TPEngine:
 
     def new_slot(self, capacity: int) -> KVSlot:
         return self.engine.new_slot(capacity)
+
+    def _pull_shards(self, kind: int, stage_kind: int, src_ptrs: list[int], stage: torch.Tensor, rows: int,
+                     epoch: int) -> list[int]:
+        """Copy every peer's shard into local staging on the side stream.
+
+        Per remote shard (nearest rank first): a bounded device wait for the
+        owner's ready flag, one copy-engine transfer over NVLink, then a local
+        release of flags[stage_kind][r].  Returns the shard bases the GEMM
+        reads (own shard in place, remote shards from staging).
+        """
+        d = self.full_cfg.d_model
+        nbytes = rows * d * 2
+        bases = []
+        main = torch.cuda.current_stream()
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            for i in range(1, self.tp):
+                r = (self.rank + i) % self.tp
+                self.ext.wait_flag(self.flags[kind], r, epoch, TIMEOUT_NS, self.status)
+                dst = stage[r * rows:(r + 1) * rows]
+                self.ext.memcpy_async(dst.data_ptr(), src_ptrs[r], nbytes)
+                self.ext.peer_signal(self._flag_addr(self.rank, stage_kind, r), epoch)
+        for r in range(self.tp):
+            bases.append(src_ptrs[r] if r == self.rank else stage[r * rows:].data_ptr())
+        return bases
 
     # ------------------------------------------------------------ prefill
     def prefill(self, ids: torch.Tensor, slot: KVSlot) -> tuple[torch.Tensor, int, int]:
@@ -174,8 +206,8 @@ class TPEngine:
         ext.embedding(ids_p[own], eng.w.embed, h)
         x = self.x_buf.view(torch.bfloat16)[: rows * d].view(rows, d)
         x2 = self.x2_buf.view(torch.bfloat16)[: rows * d].view(rows, d)
-        recv_o = self.recv_o_buf.view(torch.float32)[: self.tp * rows * d].view(self.tp, rows, d)
-        recv_d = self.recv_d_buf.view(torch.float32)[: self.tp * rows * d].view(self.tp, rows, d)
+        recv_o = self.recv_o_buf.view(torch.bfloat16)[: self.tp * rows * d].view(self.tp, rows, d)
+        recv_d = self.recv_d_buf.view(torch.bfloat16)[: self.tp * rows * d].view(self.tp, rows, d)
         ext.rmsnorm(h, None, eng.w.layers[0].ln1, cfg.rms_eps, x)
         pos = eng._arange("pos", Tp)
         q = eng.ws.get("q", (Tp, lc.q_size), torch.bfloat16)
@@ -186,14 +218,16 @@ class TPEngine:
             self.epoch += 1
             e = self.epoch
             self._signal_all(FLAG_X, e)
-            ext.gemm_ag_qkv(self.x_ptrs, rows, self.rank, self.flags[FLAG_X], e, d, lw.w_qkv, q, slot.k(layer),
+            bases = self._pull_shards(FLAG_X, FLAG_STAGE_X, self.x_ptrs, self.stage_x, rows, e)
+            ext.gemm_ag_qkv(bases, rows, self.rank, self.flags[FLAG_STAGE_X], e, d, lw.w_qkv, q, slot.k(layer),
                             slot.v(layer), pos, pos, eng.rope, lc.n_heads, lc.n_kv_heads, bn)
             ext.attention_prefill(q, None, pos, slot.k(layer), slot.v(layer), None, Tp, lc.n_heads, eng.scale, attn)
             ext.gemm_rs(attn, lw.w_o, self.recv_o_ptrs, rows, self.rank, bn)
             self._signal_all(FLAG_RS_O, e)
             ext.rs_reduce(recv_o, self.flags[FLAG_RS_O], e, TIMEOUT_NS, self.status, h, h, lw.ln2, x2, cfg.rms_eps)
             self._signal_all(FLAG_X2, e)
-            ext.gemm_ag_swiglu(self.x2_ptrs, rows, self.rank, self.flags[FLAG_X2], e, d, lw.w_gu, act, bn)
+            bases = self._pull_shards(FLAG_X2, FLAG_STAGE_X2, self.x2_ptrs, self.stage_x2, rows, e)
+            ext.gemm_ag_swiglu(bases, rows, self.rank, self.flags[FLAG_STAGE_X2], e, d, lw.w_gu, act, bn)
             ext.gemm_rs(act, lw.w_down, self.recv_d_ptrs, rows, self.rank, bn)
             self._signal_all(FLAG_RS_D, e)
             nxt = eng.w.layers[layer + 1].ln1 if layer + 1 < len(eng.w.layers) else eng.w.norm
