@@ -329,11 +329,13 @@ class B200Engine:
         return h
 
     def prefill(self, ids: torch.Tensor, slot: KVSlot, *, start: int = 0, kpos: torch.Tensor | None = None,
-                push: PushTarget | None = None) -> torch.Tensor:
+                push: PushTarget | None = None, layer_hook=None) -> torch.Tensor:
         """Causal prefill of ``ids`` (int32, device) at positions/slots start.. ; returns final hidden [T, d].
 
         Keys [0, start) already in the slot are visible (direct prefix reuse).
         ``push`` streams every layer's K/V to a decode GPU as it is written.
+        ``layer_hook(layer, h)`` sees the input hidden rows of every layer
+        (the residual stream, before that layer's norm) for feature capture.
         """
         T = ids.numel()
         if start + T > slot.capacity or start + T > self.max_positions:
@@ -343,6 +345,8 @@ class B200Engine:
         h = self.embed(ids)
         pos = self._arange("pos", T, start)
         for layer in range(self.cfg.n_layers):
+            if layer_hook is not None:
+                layer_hook(layer, h)
             q = self._full_layer(layer, h, slot, pos, pos, start + T, kpos, push=push)
             self._attn_mlp(layer, h, q, slot, q_rows=None, qpos=pos, n_keys=start + T, kpos=kpos, n_rows=T)
         return h

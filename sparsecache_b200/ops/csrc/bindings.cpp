@@ -651,6 +651,163 @@ void index_i32(Tensor src, Tensor idx, Tensor out) {
 
 Tensor status(Tensor like) { return status_tensor(like); }
 
+// ------------------------------------------------------- K13 memory attention
+sc::MemAttnArgs mem_args(const Tensor& q, const Tensor& k, const Tensor& v, int64_t layer_stride,
+                         int64_t seq_stride, int64_t tok_stride, int64_t head_stride,
+                         const c10::optional<Tensor>& row_seq, const c10::optional<Tensor>& idx,
+                         int64_t idx_stride, const c10::optional<Tensor>& n_vis, int64_t n_fixed, double scale) {
+  CHECK_CUDA(q); CHECK_BF16(q); CHECK_CUDA(k); CHECK_BF16(k); CHECK_CUDA(v); CHECK_BF16(v);
+  TORCH_CHECK(q.dim() == 4 && q.size(3) == 128 && q.is_contiguous(), "q must be contiguous [L, R, H, 128]");
+  TORCH_CHECK(k.device() == q.device() && v.device() == q.device(), "memory on another device");
+  TORCH_CHECK(tok_stride % 8 == 0 && head_stride % 8 == 0 && seq_stride % 8 == 0 && layer_stride % 8 == 0,
+              "memory strides must be multiples of 8 elements (16-byte rows)");
+  CHECK_ALIGN16(k); CHECK_ALIGN16(v);
+  sc::MemAttnArgs a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  a.v = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  a.layer_stride = layer_stride; a.seq_stride = seq_stride; a.tok_stride = tok_stride; a.head_stride = head_stride;
+  a.L = (int)q.size(0); a.R = (int)q.size(1); a.H = (int)q.size(2);
+  if (row_seq.has_value() && row_seq->defined()) {
+    CHECK_I32(*row_seq);
+    TORCH_CHECK(row_seq->numel() >= a.R, "row_seq too short");
+    a.row_seq = row_seq->data_ptr<int>();
+  }
+  if (idx.has_value() && idx->defined()) { CHECK_I32(*idx); a.idx = idx->data_ptr<int>(); a.idx_stride = idx_stride; }
+  if (n_vis.has_value() && n_vis->defined()) { CHECK_I32(*n_vis); a.n_vis = n_vis->data_ptr<int>(); }
+  a.n_fixed = (int)n_fixed;
+  a.scale = (float)scale;
+  a.scale_log2 = (float)(scale * 1.4426950408889634);
+  return a;
+}
+
+void mem_attn_fwd(Tensor q, Tensor k, Tensor v, int64_t layer_stride, int64_t seq_stride, int64_t tok_stride,
+                  int64_t head_stride, c10::optional<Tensor> row_seq, c10::optional<Tensor> idx, int64_t idx_stride,
+                  c10::optional<Tensor> n_vis, int64_t n_fixed, double scale, Tensor out, Tensor lse) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto a = mem_args(q, k, v, layer_stride, seq_stride, tok_stride, head_stride, row_seq, idx, idx_stride, n_vis,
+                    n_fixed, scale);
+  CHECK_BF16(out); CHECK_F32(lse);
+  TORCH_CHECK(out.sizes() == q.sizes() && out.is_contiguous(), "out shape");
+  TORCH_CHECK(lse.numel() == (int64_t)a.L * a.R * a.H && lse.is_contiguous(), "lse shape");
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.lse = lse.data_ptr<float>();
+  check_cuda(sc::mem_attn_fwd(a, cur_stream()), "mem_attn_fwd");
+}
+
+void mem_attn_bwd(Tensor q, Tensor k, Tensor v, int64_t layer_stride, int64_t seq_stride, int64_t tok_stride,
+                  int64_t head_stride, c10::optional<Tensor> row_seq, c10::optional<Tensor> idx, int64_t idx_stride,
+                  c10::optional<Tensor> n_vis, int64_t n_fixed, double scale, Tensor o, Tensor dout, Tensor lse,
+                  Tensor dq) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto a = mem_args(q, k, v, layer_stride, seq_stride, tok_stride, head_stride, row_seq, idx, idx_stride, n_vis,
+                    n_fixed, scale);
+  CHECK_BF16(o); CHECK_BF16(dout); CHECK_F32(lse); CHECK_F32(dq);
+  TORCH_CHECK(o.sizes() == q.sizes() && o.is_contiguous() && dout.sizes() == q.sizes() && dout.is_contiguous(),
+              "o/dout shape");
+  TORCH_CHECK(dq.sizes() == q.sizes() && dq.is_contiguous(), "dq shape");
+  a.o = reinterpret_cast<const __nv_bfloat16*>(o.data_ptr());
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  a.lse = lse.data_ptr<float>();
+  a.dq = dq.data_ptr<float>();
+  check_cuda(sc::mem_attn_bwd(a, cur_stream()), "mem_attn_bwd");
+}
+
+// ------------------------------------------------------------- K16 AdamW / DP
+void adamw_step(Tensor param, Tensor grad, Tensor exp_avg, Tensor exp_avg_sq, Tensor hyper, Tensor state,
+                Tensor partial, Tensor counter) {
+  const c10::cuda::CUDAGuard guard(param.device());
+  for (const Tensor* t : {&param, &grad, &exp_avg, &exp_avg_sq, &hyper, &state, &partial}) {
+    CHECK_CUDA(*t); CHECK_F32(*t);
+    TORCH_CHECK(t->is_contiguous(), "optimizer buffers must be contiguous");
+  }
+  TORCH_CHECK(grad.numel() == param.numel() && exp_avg.numel() == param.numel() &&
+              exp_avg_sq.numel() == param.numel(), "flat buffer sizes differ");
+  TORCH_CHECK(hyper.numel() >= 6 && state.numel() >= 5, "hyper[6] / state[5]");
+  TORCH_CHECK(counter.scalar_type() == torch::kInt32 && counter.numel() >= 1, "counter int32");
+  sc::AdamArgs a{};
+  a.param = param.data_ptr<float>();
+  a.grad = grad.data_ptr<float>();
+  a.exp_avg = exp_avg.data_ptr<float>();
+  a.exp_avg_sq = exp_avg_sq.data_ptr<float>();
+  a.n = param.numel();
+  a.hyper = hyper.data_ptr<float>();
+  a.state = state.data_ptr<float>();
+  a.partial = partial.data_ptr<float>();
+  a.counter = reinterpret_cast<unsigned*>(counter.data_ptr<int>());
+  check_cuda(sc::adamw_norm(a, (int)partial.numel(), cur_stream()), "adamw_norm");
+  check_cuda(sc::adamw_update(a, cur_stream()), "adamw_update");
+}
+
+void dp_adamw_step(int64_t world, int64_t rank, int64_t n_total, int64_t shard, std::vector<int64_t> grads,
+                   std::vector<int64_t> params, std::vector<int64_t> norms, Tensor flag_grads, Tensor flag_norms,
+                   std::vector<int64_t> peer_flag_norms, std::vector<int64_t> peer_flag_params, Tensor epoch,
+                   int64_t timeout_ns, Tensor status, Tensor red_grad, Tensor exp_avg, Tensor exp_avg_sq,
+                   Tensor hyper, Tensor state, Tensor partial, Tensor counter) {
+  const c10::cuda::CUDAGuard guard(red_grad.device());
+  TORCH_CHECK(world >= 1 && world <= sc::kMaxShards && rank >= 0 && rank < world, "world/rank");
+  TORCH_CHECK((int64_t)grads.size() == world && (int64_t)params.size() == world && (int64_t)norms.size() == world &&
+              (int64_t)peer_flag_norms.size() == world && (int64_t)peer_flag_params.size() == world,
+              "one pointer per rank");
+  TORCH_CHECK(shard * world >= n_total, "shards do not cover the buffer");
+  for (const Tensor* t : {&red_grad, &exp_avg, &exp_avg_sq, &hyper, &state, &partial}) {
+    CHECK_CUDA(*t); CHECK_F32(*t);
+  }
+  TORCH_CHECK(red_grad.numel() >= shard && exp_avg.numel() >= shard && exp_avg_sq.numel() >= shard, "shard buffers");
+  TORCH_CHECK(hyper.numel() >= 7 && state.numel() >= 5, "hyper[7] / state[5]");
+  CHECK_I32(flag_grads); CHECK_I32(flag_norms); CHECK_I32(epoch); CHECK_I32(status); CHECK_I32(counter);
+  sc::DpArgs a{};
+  a.world = (int)world; a.rank = (int)rank; a.n_total = n_total; a.shard = shard;
+  for (int s = 0; s < world; ++s) {
+    a.grads[s] = reinterpret_cast<const float*>(grads[s]);
+    a.params[s] = reinterpret_cast<float*>(params[s]);
+    a.norms[s] = reinterpret_cast<float*>(norms[s]);
+    a.peer_flag_norms[s] = reinterpret_cast<int*>(peer_flag_norms[s]);
+    a.peer_flag_params[s] = reinterpret_cast<int*>(peer_flag_params[s]);
+  }
+  a.flag_grads = flag_grads.data_ptr<int>();
+  a.flag_norms = flag_norms.data_ptr<int>();
+  a.epoch_ptr = epoch.data_ptr<int>();
+  a.timeout_ns = timeout_ns;
+  a.status = status.data_ptr<int>();
+  a.red_grad = red_grad.data_ptr<float>();
+  a.exp_avg = exp_avg.data_ptr<float>();
+  a.exp_avg_sq = exp_avg_sq.data_ptr<float>();
+  a.hyper = hyper.data_ptr<float>();
+  a.state = state.data_ptr<float>();
+  a.partial = partial.data_ptr<float>();
+  a.counter = reinterpret_cast<unsigned*>(counter.data_ptr<int>());
+  const int grid = (int)partial.numel();
+  check_cuda(sc::dp_reduce_norm(a, grid, cur_stream()), "dp_reduce_norm");
+  check_cuda(sc::dp_adamw_gather(a, grid, cur_stream()), "dp_adamw_gather");
+}
+
+void bump_counter(Tensor counter) {
+  const c10::cuda::CUDAGuard guard(counter.device());
+  CHECK_I32(counter);
+  check_cuda(sc::bump_counter(counter.data_ptr<int>(), cur_stream()), "bump_counter");
+}
+
+void signal_epoch(std::vector<int64_t> flag_ptrs, Tensor epoch, int64_t offset) {
+  const c10::cuda::CUDAGuard guard(epoch.device());
+  CHECK_I32(epoch);
+  TORCH_CHECK(!flag_ptrs.empty() && flag_ptrs.size() <= (size_t)sc::kMaxShards, "1..8 flags");
+  sc::FlagPtrs f{};
+  for (size_t i = 0; i < flag_ptrs.size(); ++i) f.addr[i] = reinterpret_cast<int*>(flag_ptrs[i]);
+  f.n = (int)flag_ptrs.size();
+  check_cuda(sc::signal_epoch(f, epoch.data_ptr<int>(), (int)offset, cur_stream()), "signal_epoch");
+}
+
+void wait_all(Tensor flags, int64_t n, Tensor epoch, int64_t offset, int64_t timeout_ns, Tensor status) {
+  const c10::cuda::CUDAGuard guard(flags.device());
+  CHECK_I32(flags); CHECK_I32(epoch); CHECK_I32(status);
+  TORCH_CHECK(n >= 1 && n <= sc::kMaxShards && flags.numel() >= n, "1..8 flags");
+  check_cuda(sc::wait_all(flags.data_ptr<int>(), (int)n, epoch.data_ptr<int>(), (int)offset, timeout_ns,
+                          status.data_ptr<int>(), cur_stream()),
+             "wait_all");
+}
+
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -712,4 +869,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("index_i32", &index_i32);
   m.def("status", &status);
   m.def("num_sms", &num_sms);
+  m.def("mem_attn_fwd", &mem_attn_fwd);
+  m.def("mem_attn_bwd", &mem_attn_bwd);
+  m.def("adamw_step", &adamw_step);
+  m.def("dp_adamw_step", &dp_adamw_step);
+  m.def("bump_counter", &bump_counter);
+  m.def("signal_epoch", &signal_epoch);
+  m.def("wait_all", &wait_all);
 }

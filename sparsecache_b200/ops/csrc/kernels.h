@@ -264,4 +264,93 @@ cudaError_t wait_flag(const int* flag, int target, long long timeout_ns, int* st
 cudaError_t peer_signal_many(int* const* addrs, int n, int value, cudaStream_t stream);
 cudaError_t index_i32(const int* src, const int* idx, int* out, int n, cudaStream_t stream);
 
+// ------------------------------------------------- K13 sparse memory attention
+struct MemAttnArgs {
+  const __nv_bfloat16* q;     // [L, R, H, 128]
+  const __nv_bfloat16* k;     // memory keys (strided, see below)
+  const __nv_bfloat16* v;     // memory values (same strides)
+  long long layer_stride, seq_stride, tok_stride, head_stride;  // elements
+  const int* row_seq;         // [R] row -> sequence (null: all rows sequence 0)
+  const int* idx;             // [S, idx_stride] visible token rows (null: 0..n-1)
+  long long idx_stride;
+  const int* n_vis;           // [S] visible count (null: n_fixed)
+  int n_fixed;
+  int L, R, H;
+  float scale, scale_log2;
+  __nv_bfloat16* out;         // fwd: [L, R, H, 128]
+  float* lse;                 // [L, R, H] base-2 log-sum-exp of the scaled scores
+  const __nv_bfloat16* o;     // bwd: forward output
+  const __nv_bfloat16* dout;  // bwd: gradient of the output
+  float* dq;                  // bwd: [L, R, H, 128] fp32
+};
+cudaError_t mem_attn_fwd(const MemAttnArgs& a, cudaStream_t stream);
+cudaError_t mem_attn_bwd(const MemAttnArgs& a, cudaStream_t stream);
+
+// ------------------------------------------------------ K16 optimizer / DP
+// AdamW over one flat fp32 parameter range with device-side step, learning
+// rate and global gradient-norm clipping (graph-replayable: no host scalars
+// change between steps).  ``hyper`` (device, fp32) holds
+//   [0] lr  [1] beta1  [2] beta2  [3] eps  [4] weight_decay  [5] max_norm
+//   [6] step offset (data parallel: the step is *epoch_ptr + [6], so a resumed
+//       run keeps its bias correction while its flags restart from zero)
+// and ``state`` (device, fp32) is written by the norm pass:
+//   [0] step  [1] 1-beta1^step  [2] 1-beta2^step  [3] grad norm  [4] clip coef
+struct AdamArgs {
+  float* param;        // master fp32 (this rank's shard for DP)
+  const float* grad;   // fp32 gradient (reduced)
+  float* exp_avg;
+  float* exp_avg_sq;
+  long long n;
+  const float* hyper;
+  float* state;
+  float* partial;      // [grid] sum-of-squares partials
+  unsigned* counter;   // last-CTA ticket (zeroed by the kernel that consumes it)
+};
+cudaError_t adamw_norm(const AdamArgs& a, int grid, cudaStream_t stream);
+cudaError_t adamw_update(const AdamArgs& a, cudaStream_t stream);
+
+// Data-parallel gradient reduce-scatter + AdamW + parameter all-gather over
+// CUDA-IPC peer memory.  Rank r owns elements [r*shard, (r+1)*shard) of the
+// flat buffers.  Phase 1 (dp_reduce_norm): wait for every rank's "grads
+// ready" flag, sum the peers' gradients of the owned shard in rank order
+// (deterministic and identical on every rank), write the shard's
+// sum-of-squares into every peer's norm slot and release "norms ready".
+// Phase 2 (dp_adamw_gather): wait for every norm, form the global clip
+// coefficient, run AdamW on the shard and store the new parameters into
+// every peer's parameter buffer, then release "params ready".
+struct DpArgs {
+  int world, rank;
+  long long n_total, shard;         // elements; shard * world >= n_total
+  const float* grads[kMaxShards];   // every rank's flat gradient (peer pointers)
+  float* params[kMaxShards];        // every rank's flat parameters (peer pointers)
+  float* norms[kMaxShards];         // every rank's [world] sum-of-squares slots
+  int* flag_grads;                  // this rank's [world] flags (peers release into them)
+  int* flag_norms;
+  int* peer_flag_norms[kMaxShards]; // where this rank releases its "norm ready"
+  int* peer_flag_params[kMaxShards];
+  const int* epoch_ptr;             // device step counter (epoch = *epoch_ptr)
+  long long timeout_ns;
+  int* status;
+  float* red_grad;                  // [shard] reduced gradient of the owned shard
+  float* exp_avg;                   // [shard]
+  float* exp_avg_sq;                // [shard]
+  const float* hyper;
+  float* state;
+  float* partial;
+  unsigned* counter;
+};
+cudaError_t dp_reduce_norm(const DpArgs& a, int grid, cudaStream_t stream);
+cudaError_t dp_adamw_gather(const DpArgs& a, int grid, cudaStream_t stream);
+cudaError_t bump_counter(int* counter, cudaStream_t stream);
+
+// Release (*epoch_ptr + offset) into up to 8 flag words; bounded wait until
+// flags[0..n) >= *epoch_ptr + offset.
+struct FlagPtrs {
+  int* addr[kMaxShards];
+  int n;
+};
+cudaError_t signal_epoch(const FlagPtrs& flags, const int* epoch_ptr, int offset, cudaStream_t stream);
+cudaError_t wait_all(const int* flags, int n, const int* epoch_ptr, int offset, long long timeout_ns, int* status,
+                     cudaStream_t stream);
+
 }  // namespace sc
