@@ -7,7 +7,8 @@
 // heads equal KV heads (no GQA), so each query is a GEMV over its rows and the
 // kernel is bound by HBM/L2 bandwidth, not by tensor cores: 8 lanes per key
 // (16 dims each, two 16-byte loads for K and two for V), two keys in flight
-// per lane group, fp32 online softmax in base 2, and a shared-memory merge of
+// per lane group with a warp-uniform loop (the 8-lane shuffles need the whole
+// warp), fp32 online softmax in base 2, and a shared-memory merge of
 // the 16 lane groups of the CTA.
 //
 // Backward computes dq only (the memory is an input, not a parameter):
@@ -89,12 +90,15 @@ __global__ void __launch_bounds__(kMemThreads) mem_attn_fwd_kernel(MemAttnArgs a
 #pragma unroll
   for (int i = 0; i < 16; ++i) acc[i] = 0.f;
 
-  for (int j0 = grp; j0 < c.n; j0 += 2 * kGroups) {
-    const int j1 = j0 + kGroups;
-    const bool has1 = j1 < c.n;
+  // The trip count depends on the warp only (shuffles below need all 32 lanes):
+  // warp w takes keys [base, base + 8) with base = 8w, 8w + 32, ...; lane
+  // group g of the warp takes keys base + g and base + 4 + g.
+  for (int base = warp * 8; base < c.n; base += 32) {
+    const int j0 = base + (lane >> 3), j1 = j0 + 4;
+    const bool has0 = j0 < c.n, has1 = j1 < c.n;
     float k0[16], v0[16], k1[16], v1[16];
-    const long long o0 = tok_off(c, j0);
-    const long long o1 = has1 ? tok_off(c, j1) : o0;
+    const long long o0 = tok_off(c, has0 ? j0 : base);
+    const long long o1 = tok_off(c, has1 ? j1 : base);
     load16(c.kb + o0, k0);
     load16(c.vb + o0, v0);
     load16(c.kb + o1, k1);
@@ -107,8 +111,10 @@ __global__ void __launch_bounds__(kMemThreads) mem_attn_fwd_kernel(MemAttnArgs a
     }
     s0 = group_sum8(s0);
     s1 = group_sum8(s1);
+    if (!has0) s0 = -INFINITY;
     if (!has1) s1 = -INFINITY;
     const float mn = fmaxf(m, fmaxf(s0, s1));
+    if (mn == -INFINITY) continue;  // nothing valid yet in this lane group
     const float corr = exp2f(m - mn);
     const float p0 = exp2f(s0 - mn), p1 = exp2f(s1 - mn);
     lsum = lsum * corr + p0 + p1;
@@ -166,12 +172,12 @@ __global__ void __launch_bounds__(kMemThreads) mem_attn_bwd_kernel(MemAttnArgs a
 #pragma unroll
   for (int i = 0; i < 16; ++i) dq[i] = 0.f;
   if (lse2 != -INFINITY) {
-    for (int j0 = grp; j0 < c.n; j0 += 2 * kGroups) {
-      const int j1 = j0 + kGroups;
-      const bool has1 = j1 < c.n;
+    for (int base = warp * 8; base < c.n; base += 32) {  // warp-uniform trip count (see forward)
+      const int j0 = base + (lane >> 3), j1 = j0 + 4;
+      const bool has0 = j0 < c.n, has1 = j1 < c.n;
       float k0[16], v0[16], k1[16], v1[16];
-      const long long o0 = tok_off(c, j0);
-      const long long o1 = has1 ? tok_off(c, j1) : o0;
+      const long long o0 = tok_off(c, has0 ? j0 : base);
+      const long long o1 = tok_off(c, has1 ? j1 : base);
       load16(c.kb + o0, k0);
       load16(c.vb + o0, v0);
       load16(c.kb + o1, k1);
@@ -188,7 +194,7 @@ __global__ void __launch_bounds__(kMemThreads) mem_attn_bwd_kernel(MemAttnArgs a
       s1 = group_sum8(s1);
       dp0 = group_sum8(dp0);
       dp1 = group_sum8(dp1);
-      const float ds0 = exp2f(s0 - lse2) * (dp0 - dd);
+      const float ds0 = has0 ? exp2f(s0 - lse2) * (dp0 - dd) : 0.f;
       const float ds1 = has1 ? exp2f(s1 - lse2) * (dp1 - dd) : 0.f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) dq[i] = fmaf(ds0, k0[i], fmaf(ds1, k1[i], dq[i]));

@@ -447,10 +447,7 @@ class EagleDrafterTrainer:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             self._body()
-        self._graph = g
-        # the capture did not execute the step: replay it for this batch
-        g.replay()
-        self.steps_done += 1
+        self._graph = g  # capturing executed nothing: the next train_step replays it
 
     def train_step(self) -> None:
         """Run one optimizer step on the next batch (asynchronously)."""

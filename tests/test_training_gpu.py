@@ -127,7 +127,7 @@ def test_graph_captured_trainer_matches_eager(cuda_device):
     w1 = m1.memory_attention.query[0].weight
     w2 = m2.memory_attention.query[0].weight
     assert torch.allclose(w1, w2, atol=1e-4), (w1 - w2).abs().max()
-    assert t1.steps_done == t2.steps_done == 8
+    assert t1.steps_done == t2.steps_done == 7
     t1.release()
 
 
