@@ -1,6 +1,6 @@
 """Isolated timings of the sm_100a kernels at Llama-3.1-8B shapes.
 
-    python -m sparsecache_b200.utils.microbench [--only gemm,gemv,attn_decode,attn_prefill]
+    python -m sparsecache_b200.utils.microbench [--only gemm,gemv,attn_decode,attn_prefill,mem_attn,adamw]
 
 CUDA events on the launching stream, 10 warm-up launches, mean over N timed
 launches; every case uses tensors that are re-read each launch, so the
@@ -38,7 +38,7 @@ def main() -> None:
     from .. import ops
 
     p = argparse.ArgumentParser()
-    p.add_argument("--only", default="gemm,gemv,attn_decode,attn_prefill")
+    p.add_argument("--only", default="gemm,gemv,attn_decode,attn_prefill,mem_attn,adamw")
     args = p.parse_args()
     only = set(args.only.split(","))
     ext = ops.ext()
@@ -96,6 +96,52 @@ def main() -> None:
             flops = 4 * 128 * H * T * (T + 1) / 2
             tf = flops / (t * 1e-6) / 1e12
             res[f"attn_prefill_causal_T{T}"] = {"us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS}
+
+    if "mem_attn" in only:
+        # drafter training step: 64 rows (32 positive + 32 contrast), 8 memory heads,
+        # one memory layer of a [64 seq, 3 layers, 2048 visible, 8, 128] bank (1.6 GB > L2)
+        S, L, V, H = 64, 3, 2048, 8
+        mk = torch.randn(S, L, V, H, 128, device=dev).to(bf)
+        mv = torch.randn(S, L, V, H, 128, device=dev).to(bf)
+        q = torch.randn(1, S, H, 128, device=dev).to(bf)
+        rows = torch.arange(S, device=dev, dtype=torch.int32)
+        idx = torch.arange(V, device=dev, dtype=torch.int32).repeat(S, 1)
+        nv = torch.full((S,), V, device=dev, dtype=torch.int32)
+        out = torch.empty_like(q)
+        lse = torch.empty(1, S, H, device=dev)
+        dq = torch.empty(1, S, H, 128, device=dev)
+        strides = (V * H * 128, L * V * H * 128, H * 128, 128)
+        layer = [0]
+
+        def fwd():
+            layer[0] = (layer[0] + 1) % L
+            k, v = mk[:, layer[0]:], mv[:, layer[0]:]
+            ext.mem_attn_fwd(q, k, v, *strides, rows, idx, V, nv, 0, 1 / math.sqrt(128), out, lse)
+
+        def bwd():
+            layer[0] = (layer[0] + 1) % L
+            k, v = mk[:, layer[0]:], mv[:, layer[0]:]
+            ext.mem_attn_bwd(q, k, v, *strides, rows, idx, V, nv, 0, 1 / math.sqrt(128), out, out, lse, dq)
+
+        kv_bytes = 2 * S * V * H * 128 * 2
+        for name, fn in (("fwd", fwd), ("dq_bwd", bwd)):
+            t = timeit(fn, n=30)
+            gbs = kv_bytes / (t * 1e-6) / 1e9
+            res[f"mem_attn_{name}_64x8x2048"] = {"us": t, "GBps": gbs, "frac_of_measured_hbm": gbs / HBM_GBS}
+        del mk, mv
+
+    if "adamw" in only:
+        n = 25_169_920  # the 8B-width EAGLE adapter
+        p_, g_ = torch.randn(n, device=dev), torch.randn(n, device=dev)
+        m_, v_ = torch.zeros(n, device=dev), torch.zeros(n, device=dev)
+        hyper = torch.tensor([1e-4, 0.9, 0.999, 1e-8, 0.01, 1.0, 0.0, 0.0], device=dev)
+        state = torch.zeros(8, device=dev)
+        part = torch.zeros(296, device=dev)
+        cnt = torch.zeros(1, device=dev, dtype=torch.int32)
+        t = timeit(lambda: ext.adamw_step(p_, g_, m_, v_, hyper, state, part, cnt), n=30)
+        byts = n * 4 * (1 + 5 + 2)  # norm pass reads g; update reads p,g,m,v and writes p,m,v
+        gbs = byts / (t * 1e-6) / 1e9
+        res["adamw_25M"] = {"us": t, "GBps": gbs, "frac_of_measured_hbm": gbs / HBM_GBS}
     print(json.dumps(res, indent=1))
 
 

@@ -1,0 +1,142 @@
+"""LongBench metrics/packs, RULER normalisation/packs and chunk priorities
+(behaviours of the reference's test_longbench_metrics.py,
+test_longbench_pd_pack.py, test_build_ruler_pd_pack.py and
+test_ruler_chunk_priorities.py)."""
+import json
+
+import pytest
+
+from sparsecache_b200.evaluation import longbench, priorities, ruler
+
+
+def test_qa_and_rouge_metrics():
+    name, em, score = longbench.score_prediction("2wikimqa", "The Eiffel Tower", ["Eiffel Tower"])
+    assert (name, em, score) == ("qa_f1", 1.0, 1.0)
+    name, _, score = longbench.score_prediction("qmsum", "alpha beta gamma", ["alpha gamma"])
+    assert name == "rouge_l_f1" and score == pytest.approx(0.8, abs=1e-7)
+
+
+def test_retrieval_count_code_classification_and_choice():
+    assert longbench.score_prediction("passage_retrieval_en", "Paragraph 7", ["Paragraph 7"])[1:] == (1.0, 1.0)
+    assert longbench.score_prediction("passage_count", "There are 12.", ["12"])[2] == 1.0
+    assert longbench.score_prediction("lcc", "value = item", ["value = item"])[2] == 1.0
+    assert longbench.score_prediction("lcc", "# comment\nx = 1", ["x = 1"])[2] == 1.0
+    name, _, s = longbench.score_prediction("trec", "Location\nextra", ["Location"], ["Location", "Person"])
+    assert name == "classification_accuracy" and s == 1.0
+    name, em, s = longbench.score_prediction("longbench_v2", "After checking, The correct answer is (C)", ["C"])
+    assert (name, em, s) == ("choice_accuracy", 1.0, 1.0)
+    assert longbench.lcs_length("a b c d".split(), "b d".split()) == 2
+
+
+def test_chunk_alignment_trims_the_middle_or_pads():
+    prompt, cap, removed, pad = longbench.align_context_to_chunk([1] * 10, list(range(1000)), [2] * 6,
+                                                                  max_prompt_tokens=600, chunk_tokens=256)
+    assert len(prompt) == 512 and cap == 1000 - 584 and removed == 584 - 496 and pad == 0
+    assert prompt[10] == 0 and prompt[-7] == 999  # head and tail of the context survive
+    prompt, _, _, pad = longbench.align_context_to_chunk([1] * 10, [5] * 20, [2] * 6, max_prompt_tokens=600,
+                                                         chunk_tokens=256, padding_token_id=9)
+    assert len(prompt) == 256 and pad == 256 - 36 and prompt[30] == 9
+
+
+class _Tok:
+    name_or_path = "fake"
+
+    def __init__(self):
+        self.kwargs = None
+
+    def apply_chat_template(self, messages, **kw):
+        self.kwargs = kw
+        return "PRE " + " | ".join(m["content"] for m in messages) + " SUF"
+
+    @staticmethod
+    def encode(text, add_special_tokens=False):
+        return list(text.encode())
+
+
+def test_longbench_request_row():
+    tok = _Tok()
+    row = {"input": "who?", "context": "x" * 3000, "answers": ["me"]}
+    req = longbench.build_longbench_request(tok, "hotpotqa", row, max_prompt_tokens=2048, chunk_tokens=256,
+                                            disable_thinking=True)
+    assert len(req["prompt"]) % 256 == 0 and len(req["prompt"]) <= 2048
+    assert req["max_tokens"] == 32 and tok.kwargs["enable_thinking"] is False
+
+
+def test_ruler_parse_placements_and_render():
+    prompt = ("x " + ruler.CONTEXT_START + "Document 1:\nAlpha\nbody a\n\nDocument 2:\nBeta\nbody b\n\n"
+              "Document 3:\nGamma\nbody c" + ruler.CONTEXT_END + "Q?<|eot_id|>")
+    docs = ruler.parse_documents(prompt)
+    assert [d["title"] for d in docs] == ["Alpha", "Beta", "Gamma"]
+    for d, s in zip(docs, (False, True, False)):
+        d["supporting"] = s
+    orders = ruler.placement_orders(docs)
+    assert orders["evidence_first"] == [1, 0, 2] and orders["evidence_last"] == [0, 2, 1]
+    assert sorted(orders["evidence_uniform"]) == [0, 1, 2]
+    tok = _Tok()
+    row = {"question": "Q?", "placements": orders, "documents": docs}
+    prefix, rendered, suffix = ruler.render_parts(tok, row, "evidence_first", disable_thinking=True)
+    assert prefix and suffix and rendered[0]["supporting"] and rendered[0]["source_document_index"] == 1
+    assert tok.kwargs["enable_thinking"] is False
+
+
+def test_ruler_fit_documents_exact_budget():
+    docs = [{"token_ids": list(range(50)), "supporting": True}, {"token_ids": list(range(30)), "supporting": False},
+            {"token_ids": list(range(20)), "supporting": False}]
+    fitted, total, mode = ruler.fit_documents(docs, 70)
+    assert mode == "trim_distractors" and sum(map(len, fitted)) == 70 and len(fitted[0]) == 50
+    fitted, _, mode = ruler.fit_documents(docs, 160)
+    assert mode == "repeat_distractors" and sum(map(len, fitted)) == 160 and len(fitted[0]) == 50
+    with pytest.raises(ValueError):
+        ruler.fit_documents(docs, 51)
+
+
+def test_ruler_pack_files(tmp_path):
+    tok = _Tok()
+    docs = [{"title": "A", "text": "alpha " * 40, "supporting": True}, {"title": "B", "text": "beta " * 90,
+                                                                         "supporting": False}]
+    row = {"id": "r0", "question": "Q?", "answers": ["a"], "documents": docs,
+           "placements": ruler.placement_orders(docs)}
+    src = tmp_path / "qa2.jsonl"
+    src.write_text(json.dumps(row) + "\n")
+    man = ruler.build_pack(tok, src, "evidence_last", 1024, tmp_path / "pack")
+    req = json.loads((tmp_path / "pack" / "requests.jsonl").read_text())
+    meta = json.loads((tmp_path / "pack" / "metadata.jsonl").read_text())
+    assert len(req["prompt"]) == 1024 and man["requests"] == 1
+    assert meta["document_spans"][-1]["supporting"] is True
+
+
+def test_bm25_and_oracle_prioritise_relevant_chunks():
+    documents = [{"text": "irrelevant apples", "supporting": False},
+                 {"text": "Scott Derrickson nationality", "supporting": True}]
+    common = dict(request_id="row-1", question="What is Scott Derrickson nationality?", documents=documents,
+                  spans=[{"start_token": 256, "end_token": 512}, {"start_token": 512, "end_token": 768}],
+                  total_chunks=6, chunk_tokens=256, protected_prefix_chunks=1, protected_suffix_chunks=1, seed=7)
+    for mode in ("bm25", "oracle"):
+        order = priorities.priority_for_mode(mode, **common)
+        assert set(order[:2]) == {0, 5} and order.index(2) < order.index(1) and sorted(order) == list(range(6))
+    assert priorities.bm25_scores(common["question"], [d["text"] for d in documents])[1] > 0
+
+
+def test_random_priority_stable_and_protected_first():
+    common = dict(request_id="row-9", question="q", documents=[{"text": "d", "supporting": False}],
+                  spans=[{"start_token": 256, "end_token": 1024}], total_chunks=8, chunk_tokens=256,
+                  protected_prefix_chunks=1, protected_suffix_chunks=2, seed=42)
+    a = priorities.priority_for_mode("random", **common)
+    assert a == priorities.priority_for_mode("random", **common) and set(a[:3]) == {0, 6, 7}
+    assert priorities.uniform_order(9)[:3] == [0, 8, 4]
+
+
+def test_spans_from_prompt_markers():
+    class T:
+        @staticmethod
+        def encode(text, add_special_tokens=False):
+            return list(text.encode())
+
+    source = {"placements": {"original": [1, 0]},
+              "documents": [{"text": "zero", "supporting": False}, {"text": "one", "supporting": True}]}
+    prompt = list("prefix Document 1:\none Document 2:\nzero suffix".encode())
+    spans, docs = priorities.document_spans_from_prompt_markers(T(), prompt, source, "original", 7)
+    assert spans[0]["supporting"] is True and spans[0]["end_token"] == spans[1]["start_token"]
+    assert [d["text"] for d in docs] == ["one", "zero"]
+    cov = priorities.coverage_curve([1, 0], [{"start_token": 0, "end_token": 4, "supporting": True}], 4)
+    assert cov == [0.0, 1.0]
