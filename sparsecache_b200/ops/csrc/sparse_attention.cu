@@ -9,7 +9,7 @@
 // (16 dims each, two 16-byte loads for K and two for V), two keys in flight
 // per lane group with a warp-uniform loop (the 8-lane shuffles need the whole
 // warp), fp32 online softmax in base 2, and a shared-memory merge of
-// the 16 lane groups of the CTA.
+// the CTA's lane groups.
 //
 // Backward computes dq only (the memory is an input, not a parameter):
 //   dq = scale * sum_j p_j (dO.v_j - dO.o) k_j,  p_j = exp2(s_j - lse2)
@@ -24,8 +24,10 @@
 namespace sc {
 
 namespace {
-constexpr int kMemThreads = 128;
-constexpr int kGroups = kMemThreads / 8;  // 16 lane groups of 8 lanes
+// forward: 8 warps (latency-bound loads want many in flight); backward: 4
+// warps (116 registers a thread) so that 4 CTAs fit an SM
+constexpr int kFwdThreads = 256;
+constexpr int kBwdThreads = 128;
 
 __device__ __forceinline__ void load16(const __nv_bfloat16* p, float (&x)[16]) {
   const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
@@ -72,7 +74,8 @@ __device__ __forceinline__ long long tok_off(const RowCtx& c, int j) {
 }
 }  // namespace
 
-__global__ void __launch_bounds__(kMemThreads) mem_attn_fwd_kernel(MemAttnArgs a) {
+__global__ void __launch_bounds__(kFwdThreads) mem_attn_fwd_kernel(MemAttnArgs a) {
+  constexpr int kGroups = kFwdThreads / 8, kKeysPerIter = kFwdThreads / 4;
   __shared__ float s_acc[kGroups][128];
   __shared__ float s_m[kGroups], s_l[kGroups];
   const int h = blockIdx.x, r = blockIdx.y, l = blockIdx.z;
@@ -91,9 +94,9 @@ __global__ void __launch_bounds__(kMemThreads) mem_attn_fwd_kernel(MemAttnArgs a
   for (int i = 0; i < 16; ++i) acc[i] = 0.f;
 
   // The trip count depends on the warp only (shuffles below need all 32 lanes):
-  // warp w takes keys [base, base + 8) with base = 8w, 8w + 32, ...; lane
+  // warp w takes keys [base, base + 8) with base = 8w, 8w + 64, ...; lane
   // group g of the warp takes keys base + g and base + 4 + g.
-  for (int base = warp * 8; base < c.n; base += 32) {
+  for (int base = warp * 8; base < c.n; base += kKeysPerIter) {
     const int j0 = base + (lane >> 3), j1 = j0 + 4;
     const bool has0 = j0 < c.n, has1 = j1 < c.n;
     float k0[16], v0[16], k1[16], v1[16];
@@ -130,6 +133,7 @@ __global__ void __launch_bounds__(kMemThreads) mem_attn_fwd_kernel(MemAttnArgs a
   }
   __syncthreads();
   const int d = threadIdx.x;
+  if (d >= 128) return;
   float mx = -INFINITY;
 #pragma unroll
   for (int g = 0; g < kGroups; ++g) mx = fmaxf(mx, s_m[g]);
@@ -147,7 +151,8 @@ __global__ void __launch_bounds__(kMemThreads) mem_attn_fwd_kernel(MemAttnArgs a
   if (d == 0) a.lse[((long long)l * a.R + r) * a.H + h] = tot > 0.f ? mx + log2f(tot) : -INFINITY;
 }
 
-__global__ void __launch_bounds__(kMemThreads) mem_attn_bwd_kernel(MemAttnArgs a) {
+__global__ void __launch_bounds__(kBwdThreads) mem_attn_bwd_kernel(MemAttnArgs a) {
+  constexpr int kGroups = kBwdThreads / 8, kKeysPerIter = kBwdThreads / 4;
   __shared__ float s_dq[kGroups][128];
   const int h = blockIdx.x, r = blockIdx.y, l = blockIdx.z;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -172,7 +177,7 @@ __global__ void __launch_bounds__(kMemThreads) mem_attn_bwd_kernel(MemAttnArgs a
 #pragma unroll
   for (int i = 0; i < 16; ++i) dq[i] = 0.f;
   if (lse2 != -INFINITY) {
-    for (int base = warp * 8; base < c.n; base += 32) {  // warp-uniform trip count (see forward)
+    for (int base = warp * 8; base < c.n; base += kKeysPerIter) {  // warp-uniform trip count (see forward)
       const int j0 = base + (lane >> 3), j1 = j0 + 4;
       const bool has0 = j0 < c.n, has1 = j1 < c.n;
       float k0[16], v0[16], k1[16], v1[16];
@@ -204,6 +209,7 @@ __global__ void __launch_bounds__(kMemThreads) mem_attn_bwd_kernel(MemAttnArgs a
   for (int i = 0; i < 16; ++i) s_dq[grp][sub * 16 + i] = dq[i];
   __syncthreads();
   const int d = threadIdx.x;
+  if (d >= 128) return;
   float t = 0.f;
 #pragma unroll
   for (int g = 0; g < kGroups; ++g) t += s_dq[g][d];
@@ -212,13 +218,13 @@ __global__ void __launch_bounds__(kMemThreads) mem_attn_bwd_kernel(MemAttnArgs a
 
 cudaError_t mem_attn_fwd(const MemAttnArgs& a, cudaStream_t stream) {
   if (a.L < 1 || a.R < 1 || a.H < 1 || a.H > 65535 || a.R > 65535 || a.L > 64) return cudaErrorInvalidValue;
-  mem_attn_fwd_kernel<<<dim3(a.H, a.R, a.L), kMemThreads, 0, stream>>>(a);
+  mem_attn_fwd_kernel<<<dim3(a.H, a.R, a.L), kFwdThreads, 0, stream>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t mem_attn_bwd(const MemAttnArgs& a, cudaStream_t stream) {
   if (a.L < 1 || a.R < 1 || a.H < 1 || a.H > 65535 || a.R > 65535 || a.L > 64) return cudaErrorInvalidValue;
-  mem_attn_bwd_kernel<<<dim3(a.H, a.R, a.L), kMemThreads, 0, stream>>>(a);
+  mem_attn_bwd_kernel<<<dim3(a.H, a.R, a.L), kBwdThreads, 0, stream>>>(a);
   return cudaGetLastError();
 }
 
