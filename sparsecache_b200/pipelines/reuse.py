@@ -1,0 +1,282 @@
+"""CacheBlend reuse pipeline: one-shot and progressive repair, paired driver, aggregation.
+
+Parity with the reference's experiments/reuse_cacheblend_pipeline.py:
+  * ``expand_documents`` (:239-273): proportional document repetition up to a
+    token target, for scale sweeps (timing only);
+  * ``prepare_request`` (:276-319): rank documents by a schedule (BM25 over
+    the question by default), lay them out in ranked order, and compute the
+    cumulative staged document sets of the stage fractions;
+  * ``run_progressive_cacheblend`` (:896-1141): documents arrive in stages;
+    every stage is a CacheBlend repair of the cache with only that stage's
+    documents present (absent documents are zero placeholders); stage 0
+    drafts, later stages verify + commit with a commit window of 1, the final
+    stage commits and corrects, then decoding continues on the full repair;
+  * ``evaluate_request`` / ``main`` (:1144-1334): paired measurement of full
+    prefill, one-shot CacheBlend and progressive CacheBlend per request after
+    a warm-up, written as JSONL with a protocol block;
+  * ``aggregate`` (experiments/aggregate_reuse_cacheblend_pipeline.py:46-229):
+    token agreement with full prefill, TTFT and end-to-end latency
+    distributions, paired bootstrap of the latency differences.
+The documents' K/V blocks are resident in HBM (the store's ``hbm`` tier), so
+a stage "arrival" is the on-device composition of its documents; the stage
+model runs this package's engine (composer, CacheBlend kernels, batched
+verifier).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import statistics
+import time
+from dataclasses import asdict, dataclass
+from pathlib import Path
+from typing import Any, Sequence
+
+import torch
+
+from ..cacheblend import recompute_count
+from ..serving.chains import progressive_commit_chain
+from ..serving.progressive import Document, ranked_document_indices, stage_document_sets
+from ..synthetic import RAGRequest
+
+
+def expand_documents(documents: Sequence[Sequence[int]], target_tokens: int, prefix_tokens: int = 0):
+    """Repeat documents proportionally until the prompt reaches ``target_tokens`` (timing sweeps)."""
+    docs = [list(d) for d in documents]
+    have = prefix_tokens + sum(map(len, docs))
+    if have >= target_tokens or not docs:
+        return docs
+    factor = target_tokens / max(1, have - prefix_tokens)
+    out = []
+    for d in docs:
+        reps = max(1, math.floor(factor))
+        out.append(d * reps)
+    i = 0
+    while prefix_tokens + sum(map(len, out)) < target_tokens:
+        out[i % len(out)] += docs[i % len(docs)]
+        i += 1
+    return out
+
+
+@dataclass
+class PreparedRequest:
+    request: RAGRequest
+    ranking: list[int]
+    selected_sets: list[set[int]]
+    stage_fractions: tuple[float, ...]
+
+
+def prepare_request(request: RAGRequest, *, question: str = "", schedule: str = "query",
+                    fractions: Sequence[float] = (0.25, 0.5, 1.0), seed: int = 0,
+                    texts: Sequence[str] | None = None) -> PreparedRequest:
+    """Rank the request's documents, re-lay them in ranked order, stage them cumulatively."""
+    docs = [Document(tuple(d), texts[i] if texts else " ".join(map(str, d[:64])))
+            for i, d in enumerate(request.documents)]
+    ranking = ranked_document_indices(schedule, question=question or " ".join(map(str, request.suffix)),
+                                      documents=docs, random_seed=seed)
+    laid = RAGRequest(request.index, request.prefix, tuple(request.documents[i] for i in ranking), request.suffix)
+    ranked_docs = [Document(tuple(d)) for d in laid.documents]
+    sets = stage_document_sets(list(range(len(ranking))), ranked_docs, fractions)
+    return PreparedRequest(laid, ranking, sets, tuple(fractions))
+
+
+class EngineStageModel:
+    """Stage s = CacheBlend repair over the documents of ``selected_sets[s]`` (others zero).
+
+    ``verify``/``draft``/``final_decode`` append the given token sequence with
+    the batched verifier (8 rows a pass) behind the stage's repaired prompt,
+    so every stage sees exactly prompt + sequence.
+    """
+
+    def __init__(self, server, prepared: PreparedRequest, *, document_blocks: Sequence[torch.Tensor]) -> None:
+        self.server, self.eng = server, server.engine
+        self.req = prepared.request
+        self.sets = prepared.selected_sets
+        self.n_stages = len(self.sets)
+        self.blocks = list(document_blocks)
+        self.T = self.req.prompt_tokens
+        self.slot = server.slot
+        self.ids = torch.tensor(self.req.prompt, dtype=torch.int32, device=self.eng.device)
+        self._stage = None
+        self._first = None
+        self._appended: list[int] = []
+        self.repairs = 0
+
+    def _repair(self, stage: int) -> None:
+        if self._stage == stage:
+            return
+        eng, req = self.eng, self.req
+        blend = self.server.blend
+        zero = {i for i in range(len(self.blocks)) if i not in self.sets[stage]}
+        blocks = [torch.zeros_like(b) if i in zero else b for i, b in enumerate(self.blocks)]
+        eng.compose(self.slot, blocks, first_slot=len(req.prefix), layer_begin=blend.check_layer)
+        h_a, A, _ = eng.cacheblend(self.ids, self.slot, prefix_tokens=len(req.prefix),
+                                   suffix_tokens=len(req.suffix), blend=blend)
+        b = eng.first_token(h_a[A - 1:A], position=self.T, max_new=1)
+        self._first = int(b["tok"][0].item())
+        self._stage, self._appended = stage, []
+        self.repairs += 1
+
+    def _append(self, seq: Sequence[int]) -> list[int]:
+        """Predictions after each appended token (rows beyond the cached common prefix)."""
+        common = 0
+        while common < min(len(seq), len(self._appended)) and seq[common] == self._appended[common]:
+            common += 1
+        preds = []
+        self._appended = self._appended[:common]
+        for k in range(common, len(seq), 8):
+            chunk = list(seq[k:k + 8])
+            out = self.eng.verify(self.slot, torch.tensor(chunk, dtype=torch.int32, device=self.eng.device),
+                                  position=self.T + k)
+            preds += out.cpu().tolist()
+            self._appended += chunk
+        return preds
+
+    def _preds_all(self, seq: Sequence[int]) -> list[int]:
+        self._appended = []  # recompute the whole tail (verifier state is positional)
+        return [self._first] + self._append(seq)
+
+    def verify(self, stage: int, sequence: Sequence[int]) -> list[int]:
+        self._repair(stage)
+        return self._preds_all(sequence)
+
+    def draft(self, stage: int, sequence: Sequence[int], n: int) -> list[int]:
+        self._repair(stage)
+        nxt = self._preds_all(sequence)[-1]
+        out, seq = [], list(sequence)
+        for _ in range(n):
+            out.append(nxt)
+            seq.append(nxt)
+            nxt = self._append(seq)[-1]
+        return out
+
+    def final_decode(self, sequence: Sequence[int], n: int) -> list[int]:
+        return self.draft(self.n_stages - 1, sequence, n)
+
+
+def run_progressive_cacheblend(server, prepared: PreparedRequest, document_blocks, *, draft_tokens: int,
+                               max_new_tokens: int, eos_ids=frozenset()) -> dict[str, Any]:
+    model = EngineStageModel(server, prepared, document_blocks=document_blocks)
+    t0 = time.perf_counter()
+    out = progressive_commit_chain(model, commit_window=1, draft_tokens=draft_tokens, max_new_tokens=max_new_tokens,
+                                   eos_ids=set(eos_ids))
+    torch.cuda.synchronize(server.engine.device)
+    return {"tokens": out.tokens, "response_ms": (time.perf_counter() - t0) * 1e3,
+            "first_draft_ms": out.first_draft_ms, "first_committed_ms": out.first_committed_ms,
+            "verify_ms": out.verify_ms, "draft_ms": out.draft_ms, "final_decode_ms": out.final_decode_ms,
+            "ignored_committed_flips": out.ignored_committed_flips, "stages": model.n_stages,
+            "repairs": model.repairs, "trace": out.trace}
+
+
+def evaluate_request(server, prepared: PreparedRequest, *, max_new_tokens: int, draft_tokens: int = 8,
+                     modes: Sequence[str] = ("full", "cacheblend", "progressive")) -> dict[str, Any]:
+    """Paired arms of one request: device-timed TTFT and end-to-end latency per arm."""
+    req = prepared.request
+    row: dict[str, Any] = {"request_index": req.index, "prompt_tokens": req.prompt_tokens,
+                           "document_tokens": req.document_tokens, "arms": {}}
+    for mode in modes:
+        if mode == "progressive":
+            blocks = [server.store[d].kv for d in req.documents]
+            res = run_progressive_cacheblend(server, prepared, blocks, draft_tokens=draft_tokens,
+                                             max_new_tokens=max_new_tokens, eos_ids=server.eos)
+            row["arms"][mode] = {"tokens": res["tokens"], "ttft_ms": res["first_committed_ms"],
+                                 "first_draft_ms": res["first_draft_ms"], "e2e_ms": res["response_ms"],
+                                 "ignored_committed_flips": res["ignored_committed_flips"]}
+        else:
+            r = server.serve(req, mode=mode, max_new_tokens=max_new_tokens, sync=True)
+            row["arms"][mode] = {"tokens": list(r.token_ids), "ttft_ms": r.ttft_ms, "e2e_ms": r.response_ms}
+    return row
+
+
+# ------------------------------------------------------------------ aggregate
+def _pct(v, q):
+    v = sorted(v)
+    if not v:
+        return math.nan
+    pos = q * (len(v) - 1)
+    lo, hi = math.floor(pos), math.ceil(pos)
+    return v[lo] + (v[hi] - v[lo]) * (pos - lo)
+
+
+def _boot(values, samples=10000, seed=0):
+    import random
+
+    if not values:
+        return [math.nan, math.nan]
+    rng = random.Random(seed)
+    est = sorted(statistics.fmean(rng.choices(values, k=len(values))) for _ in range(samples))
+    return [_pct(est, 0.025), _pct(est, 0.975)]
+
+
+def aggregate(rows: Sequence[dict], *, reference: str = "full", bootstrap_samples: int = 10000) -> dict[str, Any]:
+    """Token agreement with the reference arm, latency distributions, paired bootstrap of differences."""
+    arms = sorted({a for r in rows for a in r["arms"]})
+    out: dict[str, Any] = {"requests": len(rows), "reference_arm": reference, "arms": {}}
+    for a in arms:
+        rr = [r for r in rows if a in r["arms"] and reference in r["arms"]]
+        ttft = [r["arms"][a]["ttft_ms"] for r in rr if r["arms"][a]["ttft_ms"] is not None]
+        e2e = [r["arms"][a]["e2e_ms"] for r in rr]
+        agree = [r["arms"][a]["tokens"] == r["arms"][reference]["tokens"] for r in rr]
+        prefix = [next((i for i, (x, y) in enumerate(zip(r["arms"][a]["tokens"], r["arms"][reference]["tokens"]))
+                        if x != y), len(r["arms"][a]["tokens"])) for r in rr]
+        d_ttft = [r["arms"][reference]["ttft_ms"] - r["arms"][a]["ttft_ms"] for r in rr
+                  if r["arms"][a]["ttft_ms"] is not None]
+        out["arms"][a] = {
+            "token_equal_rate": statistics.fmean(agree) if agree else math.nan,
+            "mean_agreeing_prefix": statistics.fmean(prefix) if prefix else math.nan,
+            "ttft_ms": {"p50": _pct(ttft, 0.5), "p99": _pct(ttft, 0.99), "mean": statistics.fmean(ttft) if ttft
+                        else math.nan},
+            "e2e_ms": {"p50": _pct(e2e, 0.5), "p99": _pct(e2e, 0.99)},
+            "ttft_gain_vs_reference_ms": {"mean": statistics.fmean(d_ttft) if d_ttft else math.nan,
+                                          "ci95": _boot(d_ttft, bootstrap_samples)},
+        }
+    return out
+
+
+def main(argv=None) -> None:
+    from ..config import CacheBlendConfig, get_model_config
+    from ..models.engine import B200Engine
+    from ..serving.server import RAGServer
+    from ..store import DocumentKVStore
+    from ..synthetic import WORKLOADS, make_requests
+
+    p = argparse.ArgumentParser()
+    p.add_argument("--model", default="llama3-8b")
+    p.add_argument("--workload", default="llama8b_rag")
+    p.add_argument("--requests", type=int, default=16)
+    p.add_argument("--warmup", type=int, default=2)
+    p.add_argument("--max-new-tokens", type=int, default=24)
+    p.add_argument("--draft-tokens", type=int, default=8)
+    p.add_argument("--fractions", default="0.25,0.5,1.0")
+    p.add_argument("--schedule", default="query")
+    p.add_argument("--recompute-ratio", type=float, default=0.15)
+    p.add_argument("--check-layer", type=int, default=1)
+    p.add_argument("--output", type=Path, required=True)
+    a = p.parse_args(argv)
+    cfg = get_model_config(a.model)
+    eng = B200Engine.random(cfg, seed=0, device="cuda")
+    reqs = make_requests(WORKLOADS[a.workload])[: a.requests + a.warmup]
+    store = DocumentKVStore(tier="hbm")
+    server = RAGServer(eng, store, capacity=max(r.prompt_tokens for r in reqs) + a.max_new_tokens + 64,
+                       blend=CacheBlendConfig(check_layer=a.check_layer, recompute_ratio=a.recompute_ratio,
+                                              max_new_tokens=a.max_new_tokens))
+    server.produce(reqs)
+    fractions = tuple(float(x) for x in a.fractions.split(","))
+    rows = []
+    with open(a.output, "w") as f:
+        f.write(json.dumps({"protocol": {"model": a.model, "workload": a.workload, "fractions": fractions,
+                                         "schedule": a.schedule, "recompute_ratio": a.recompute_ratio,
+                                         "check_layer": a.check_layer, "draft_tokens": a.draft_tokens,
+                                         "max_new_tokens": a.max_new_tokens, "commit_window": 1}}) + "\n")
+        for i, r in enumerate(reqs):
+            prep = prepare_request(r, schedule=a.schedule, fractions=fractions, seed=i)
+            row = evaluate_request(server, prep, max_new_tokens=a.max_new_tokens, draft_tokens=a.draft_tokens)
+            if i >= a.warmup:
+                rows.append(row)
+                f.write(json.dumps(row) + "\n")
+    print(json.dumps(aggregate(rows), indent=2))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,58 @@
+"""Progressive commit-window and graft chains on a deterministic CPU stage model:
+every chain's output equals full-KV greedy decoding (the exactness gate of the
+reference's progressive chains), with the trace invariants of each stage."""
+import pytest
+
+from sparsecache_b200.serving.chains import ToyStageModel, progressive_commit_chain, progressive_graft_chain
+
+
+@pytest.mark.parametrize("window", [1, 2, None])
+@pytest.mark.parametrize("seed", range(6))
+def test_commit_chain_is_exact(window, seed):
+    m = ToyStageModel(n_stages=4, flip_rate=0.5, seed=seed)
+    want = m.final_decode([], 24)
+    out = progressive_commit_chain(m, commit_window=window, draft_tokens=6, max_new_tokens=24)
+    assert len(out.tokens) == 24
+    if window is None:  # only the full-KV verifier commits: exact
+        assert out.tokens == want and out.ignored_committed_flips == 0
+    else:  # a finite window freezes tokens that survived W noisy verifications
+        first_bad = next((i for i, (a, b) in enumerate(zip(out.tokens, want)) if a != b), 24)
+        assert first_bad == 24 or out.trace[-1]["committed_before"] > first_bad
+    for row in out.trace:
+        assert row["accepted_pending"] + row["rejected_pending"] == (row["pending_before"] if row["verified"] else 0)
+        assert row["committed_after"] >= row["committed_before"]
+    assert out.trace[0]["drafted"] == 6 and not out.trace[0]["verified"]
+
+
+def test_commit_chain_stops_at_eos():
+    m = ToyStageModel(n_stages=3, flip_rate=0.0, seed=1)
+    full = m.final_decode([], 30)
+    eos = {full[4]}
+    out = progressive_commit_chain(m, commit_window=1, draft_tokens=8, max_new_tokens=30, eos_ids=eos)
+    assert out.tokens == full[:full.index(full[4]) + 1]
+
+
+def test_graft_chain_is_exact_and_verifies_once():
+    for seed in range(5):
+        m = ToyStageModel(n_stages=4, flip_rate=0.4, seed=seed)
+        out = progressive_graft_chain(m, draft_tokens_per_stage=3, max_new_tokens=20)
+        assert out.tokens == m.final_decode([], 20) and out.verifications == 1
+
+
+def test_reuse_pipeline_helpers():
+    from sparsecache_b200.pipelines.reuse import aggregate, expand_documents, prepare_request
+    from sparsecache_b200.synthetic import RAGRequest
+
+    docs = expand_documents([[1, 2, 3], [4, 5]], target_tokens=20, prefix_tokens=2)
+    assert sum(map(len, docs)) + 2 >= 20 and docs[0][:3] == [1, 2, 3]
+    req = RAGRequest(0, (9, 9), ((1, 2, 3, 4), (5, 6), (7, 8, 9, 10, 11, 12)), (13,))
+    prep = prepare_request(req, schedule="sequential", fractions=(0.3, 0.7, 1.0))
+    assert prep.ranking == [0, 1, 2] and prep.selected_sets[-1] == {0, 1, 2}
+    assert all(a <= b for a, b in zip(prep.selected_sets, prep.selected_sets[1:]))
+    rows = [{"request_index": i, "arms": {"full": {"tokens": [1, 2, 3], "ttft_ms": 10.0, "e2e_ms": 20.0},
+                                          "progressive": {"tokens": [1, 2, 4], "ttft_ms": 5.0, "e2e_ms": 18.0}}}
+            for i in range(3)]
+    agg = aggregate(rows, bootstrap_samples=100)
+    assert agg["arms"]["progressive"]["token_equal_rate"] == 0.0
+    assert agg["arms"]["progressive"]["mean_agreeing_prefix"] == 2.0
+    assert agg["arms"]["progressive"]["ttft_gain_vs_reference_ms"]["mean"] == 5.0
