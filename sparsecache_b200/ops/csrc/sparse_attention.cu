@@ -24,9 +24,10 @@
 namespace sc {
 
 namespace {
-// forward: 8 warps (latency-bound loads want many in flight); backward: 4
-// warps (116 registers a thread) so that 4 CTAs fit an SM
-constexpr int kFwdThreads = 256;
+// 4 warps a CTA in both directions: the loads of the next key pair are in
+// flight while the current pair is computed, so 4 resident CTAs an SM keep
+// enough bytes in flight
+constexpr int kFwdThreads = 128;
 constexpr int kBwdThreads = 128;
 
 __device__ __forceinline__ void load16(const __nv_bfloat16* p, float (&x)[16]) {
@@ -72,6 +73,37 @@ __device__ __forceinline__ RowCtx row_ctx(const MemAttnArgs& a, int l, int r, in
 __device__ __forceinline__ long long tok_off(const RowCtx& c, int j) {
   return (long long)(c.idx ? __ldg(c.idx + j) : j) * c.tok_stride;
 }
+
+// The K/V bytes one lane needs for its two keys of one loop iteration, kept
+// packed (32 registers) so that the next iteration's loads can be in flight
+// while this one is computed.
+struct KvRaw {
+  uint4 k0[2], v0[2], k1[2], v1[2];
+};
+
+__device__ __forceinline__ void fetch(const RowCtx& c, int base, int lane, KvRaw& r) {
+  const int j0 = base + (lane >> 3), j1 = j0 + 4;
+  const long long o0 = tok_off(c, j0 < c.n ? j0 : base);
+  const long long o1 = tok_off(c, j1 < c.n ? j1 : base);
+  const uint4* k0 = reinterpret_cast<const uint4*>(c.kb + o0);
+  const uint4* v0 = reinterpret_cast<const uint4*>(c.vb + o0);
+  const uint4* k1 = reinterpret_cast<const uint4*>(c.kb + o1);
+  const uint4* v1 = reinterpret_cast<const uint4*>(c.vb + o1);
+  r.k0[0] = __ldg(k0); r.k0[1] = __ldg(k0 + 1);
+  r.v0[0] = __ldg(v0); r.v0[1] = __ldg(v0 + 1);
+  r.k1[0] = __ldg(k1); r.k1[1] = __ldg(k1 + 1);
+  r.v1[0] = __ldg(v1); r.v1[1] = __ldg(v1 + 1);
+}
+
+__device__ __forceinline__ void unpack16(const uint4 (&u)[2], float (&x)[16]) {
+  const unsigned w[8] = {u[0].x, u[0].y, u[0].z, u[0].w, u[1].x, u[1].y, u[1].z, u[1].w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float2 f = unpack_bf16x2(w[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
 }  // namespace
 
 __global__ void __launch_bounds__(kFwdThreads) mem_attn_fwd_kernel(MemAttnArgs a) {
@@ -94,36 +126,42 @@ __global__ void __launch_bounds__(kFwdThreads) mem_attn_fwd_kernel(MemAttnArgs a
   for (int i = 0; i < 16; ++i) acc[i] = 0.f;
 
   // The trip count depends on the warp only (shuffles below need all 32 lanes):
-  // warp w takes keys [base, base + 8) with base = 8w, 8w + 64, ...; lane
-  // group g of the warp takes keys base + g and base + 4 + g.
-  for (int base = warp * 8; base < c.n; base += kKeysPerIter) {
+  // warp w takes keys [base, base + 8) with base = 8w, 8w + 8 * warps, ...;
+  // lane group g of the warp takes keys base + g and base + 4 + g.  The next
+  // iteration's K/V rows are fetched before this iteration is computed.
+  KvRaw cur, nxt;
+  int base = warp * 8;
+  if (base < c.n) fetch(c, base, lane, cur);
+  for (; base < c.n; base += kKeysPerIter) {
+    if (base + kKeysPerIter < c.n) fetch(c, base + kKeysPerIter, lane, nxt);
     const int j0 = base + (lane >> 3), j1 = j0 + 4;
     const bool has0 = j0 < c.n, has1 = j1 < c.n;
-    float k0[16], v0[16], k1[16], v1[16];
-    const long long o0 = tok_off(c, has0 ? j0 : base);
-    const long long o1 = tok_off(c, has1 ? j1 : base);
-    load16(c.kb + o0, k0);
-    load16(c.vb + o0, v0);
-    load16(c.kb + o1, k1);
-    load16(c.vb + o1, v1);
+    float kk0[16], kk1[16];
+    unpack16(cur.k0, kk0);
+    unpack16(cur.k1, kk1);
     float s0 = 0.f, s1 = 0.f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      s0 = fmaf(q[i], k0[i], s0);
-      s1 = fmaf(q[i], k1[i], s1);
+      s0 = fmaf(q[i], kk0[i], s0);
+      s1 = fmaf(q[i], kk1[i], s1);
     }
     s0 = group_sum8(s0);
     s1 = group_sum8(s1);
     if (!has0) s0 = -INFINITY;
     if (!has1) s1 = -INFINITY;
     const float mn = fmaxf(m, fmaxf(s0, s1));
-    if (mn == -INFINITY) continue;  // nothing valid yet in this lane group
-    const float corr = exp2f(m - mn);
-    const float p0 = exp2f(s0 - mn), p1 = exp2f(s1 - mn);
-    lsum = lsum * corr + p0 + p1;
+    if (mn != -INFINITY) {  // else nothing valid yet in this lane group
+      const float corr = exp2f(m - mn);
+      const float p0 = exp2f(s0 - mn), p1 = exp2f(s1 - mn);
+      lsum = lsum * corr + p0 + p1;
+      float vv0[16], vv1[16];
+      unpack16(cur.v0, vv0);
+      unpack16(cur.v1, vv1);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) acc[i] = fmaf(acc[i], corr, fmaf(p0, v0[i], p1 * v1[i]));
-    m = mn;
+      for (int i = 0; i < 16; ++i) acc[i] = fmaf(acc[i], corr, fmaf(p0, vv0[i], p1 * vv1[i]));
+      m = mn;
+    }
+    cur = nxt;
   }
 #pragma unroll
   for (int i = 0; i < 16; ++i) s_acc[grp][sub * 16 + i] = acc[i];
@@ -177,16 +215,18 @@ __global__ void __launch_bounds__(kBwdThreads) mem_attn_bwd_kernel(MemAttnArgs a
 #pragma unroll
   for (int i = 0; i < 16; ++i) dq[i] = 0.f;
   if (lse2 != -INFINITY) {
-    for (int base = warp * 8; base < c.n; base += kKeysPerIter) {  // warp-uniform trip count (see forward)
+    KvRaw cur, nxt;  // warp-uniform trip count and next-iteration prefetch (see forward)
+    int base = warp * 8;
+    if (base < c.n) fetch(c, base, lane, cur);
+    for (; base < c.n; base += kKeysPerIter) {
+      if (base + kKeysPerIter < c.n) fetch(c, base + kKeysPerIter, lane, nxt);
       const int j0 = base + (lane >> 3), j1 = j0 + 4;
       const bool has0 = j0 < c.n, has1 = j1 < c.n;
       float k0[16], v0[16], k1[16], v1[16];
-      const long long o0 = tok_off(c, has0 ? j0 : base);
-      const long long o1 = tok_off(c, has1 ? j1 : base);
-      load16(c.kb + o0, k0);
-      load16(c.vb + o0, v0);
-      load16(c.kb + o1, k1);
-      load16(c.vb + o1, v1);
+      unpack16(cur.k0, k0);
+      unpack16(cur.v0, v0);
+      unpack16(cur.k1, k1);
+      unpack16(cur.v1, v1);
       float s0 = 0.f, s1 = 0.f, dp0 = 0.f, dp1 = 0.f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -203,6 +243,7 @@ __global__ void __launch_bounds__(kBwdThreads) mem_attn_bwd_kernel(MemAttnArgs a
       const float ds1 = has1 ? exp2f(s1 - lse2) * (dp1 - dd) : 0.f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) dq[i] = fmaf(ds0, k0[i], fmaf(ds1, k1[i], dq[i]));
+      cur = nxt;
     }
   }
 #pragma unroll

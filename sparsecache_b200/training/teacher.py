@@ -378,7 +378,18 @@ def extract_teacher(engine, prompts: Sequence[torch.Tensor], *, kv_layers: Seque
         engine.first_token(h[T - 1:T], position=T, max_new=continuation_tokens)
         engine.decode(s, continuation_tokens - 1, max_new=continuation_tokens)
         input_ids = engine.generated_tokens(continuation_tokens).clone().to(torch.int32)
-        hc = engine.prefill(input_ids, s, start=T)
+        boundary: dict[int, torch.Tensor] = {}
+
+        def cont_hook(layer: int, hh: torch.Tensor) -> None:
+            if layer - 1 in seed_layers:
+                boundary[layer - 1] = hh.clone()
+
+        hc = engine.prefill(input_ids, s, start=T, layer_hook=cont_hook)
+        if cfg.n_layers - 1 in seed_layers:
+            boundary[cfg.n_layers - 1] = hc.clone()
+        # seed-layer hidden states after every continuation token: the
+        # post-verification boundary features of windowed training (v5)
+        cont_seed = torch.stack([boundary[l] for l in seed_layers], dim=1)  # [t, seeds, d]
         x = hc.float()
         normed = (x * torch.rsqrt(x.square().mean(-1, keepdim=True) + cfg.rms_eps)).to(torch.bfloat16) * w.norm
         logits = (normed @ w.lm_head.t()).float()
@@ -400,7 +411,8 @@ def extract_teacher(engine, prompts: Sequence[torch.Tensor], *, kv_layers: Seque
             "input_ids": input_ids.long().cpu(), "labels": labels.long().cpu(),
             "teacher_topk_ids": top_ids.long().cpu(), "teacher_topk_logprobs": top_lp.cpu(),
             "teacher_hidden": normed.cpu(), "priority_page_scores": scores.float().cpu(),
-            "query_cos": qc, "query_sin": qs, "prompt_ids": prompt.cpu()})
+            "query_cos": qc, "query_sin": qs, "prompt_ids": prompt.cpu(),
+            "continuation_seed_hidden": cont_seed.cpu()})
         samples.append(TeacherSample(i, T, tensors, None))
     return samples
 
@@ -431,3 +443,54 @@ def visible_fraction_of(n_visible: int, prompt_tokens: int) -> float:
 
 def chunk_count(prompt_tokens: int, chunk: int = 64) -> int:
     return math.ceil(prompt_tokens / chunk)
+
+
+def _atomic_save(tensors: dict[str, torch.Tensor], path: Path) -> None:
+    from safetensors.torch import save_file
+
+    tmp = path.with_suffix(path.suffix + ".tmp")
+    save_file({k: v.contiguous() for k, v in tensors.items()}, str(tmp))
+    tmp.replace(path)
+
+
+def write_teacher_dataset(samples: Sequence[TeacherSample], out_dir: Path, *, target_fingerprint: str,
+                          kv_layers: Sequence[int], seed_layers: Sequence[int], head_dim: int, kv_heads: int,
+                          target_hidden_size: int, vocab_size: int, priority_page_size: int = 64,
+                          target_model: str = "random-init", with_boundaries: bool = False) -> Path:
+    """Write samples in the reference's teacher format; returns the manifest path.
+
+    Static K/V and traces go to a v3 manifest; with ``with_boundaries`` a v5
+    manifest is written next to it that chains to the v3 one (traces plus
+    ``continuation_seed_hidden``), as the reference's extender does.  Memory
+    must be the full prompt's K/V (not a cut view).
+    """
+    out_dir = Path(out_dir)
+    out_dir.mkdir(parents=True, exist_ok=True)
+    v3 = required_fields(3)
+    rows, rows5 = [], []
+    for s in samples:
+        if "memory_token_index" in s.tensors:
+            raise ValueError("the reference format stores the full prompt memory (extract with keep_full_memory)")
+        f = out_dir / f"sample_{s.request_index:05d}.safetensors"
+        _atomic_save({k: s.tensors[k] for k in v3}, f)
+        rows.append({"request_index": s.request_index, "file": f.name, "prompt_tokens": s.prompt_tokens,
+                     "draft_training_tokens": s.horizon, "file_sha256": sha256_file(f),
+                     "source_dataset": s.source_group})
+        if with_boundaries:
+            f5 = out_dir / f"trace_{s.request_index:05d}.safetensors"
+            trace = {k: s.tensors[k] for k in required_fields(5) - _STATIC_FIELDS}
+            _atomic_save(trace, f5)
+            rows5.append({**rows[-1], "file": f5.name, "file_sha256": sha256_file(f5)})
+    common = {"target_model": target_model, "target_fingerprint": target_fingerprint, "kv_layers": list(kv_layers),
+              "seed_layers": list(seed_layers), "head_dim": head_dim, "kv_heads": kv_heads,
+              "target_hidden_size": target_hidden_size, "vocab_size": vocab_size,
+              "priority_page_size": priority_page_size}
+    m3 = out_dir / "manifest.json"
+    m3.write_text(json.dumps({"schema_version": 3, "format": TEACHER_FORMATS[2], **common, "samples": rows},
+                             indent=2, sort_keys=True) + "\n")
+    if not with_boundaries:
+        return m3
+    m5 = out_dir / "manifest_v5.json"
+    m5.write_text(json.dumps({"schema_version": 5, "format": TEACHER_FORMATS[4], "base_manifest": str(m3.resolve()),
+                              **common, "samples": rows5}, indent=2, sort_keys=True) + "\n")
+    return m5
