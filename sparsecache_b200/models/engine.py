@@ -187,6 +187,7 @@ class _CountingExt:
 
     _NOT_KERNELS = {"status", "num_sms", "gemv_argmax_grid", "attention_decode_cluster", "shared_empty",
                     "shared_open", "shared_close"}
+    _MULTI = {"gemm_store", "gemm_residual"}
 
     def __init__(self, ext) -> None:
         self._ext = ext
@@ -198,8 +199,10 @@ class _CountingExt:
             return fn
 
         def counted(*args, **kwargs):
-            self.launches += 1
-            return fn(*args, **kwargs)
+            out = fn(*args, **kwargs)
+            # ops that may issue several kernels return how many they launched
+            self.launches += out if isinstance(out, int) and name in self._MULTI else 1
+            return out
 
         return counted
 
@@ -266,6 +269,11 @@ class B200Engine:
         ext.gemm_swiglu(x, lw.w_gu, act, self.bn)
         ext.gemm_residual(act, lw.w_down, h, h, self.bn)
 
+    def _qkv_bn(self, rows: int) -> int:
+        """128-column tiles when 256-column tiles would leave SMs idle (small M)."""
+        tiles = -(-rows // 128) * -(-self.cfg.qkv_rows // 256)
+        return 128 if tiles < self.num_sms else self.bn
+
     def _full_layer(self, layer: int, h: torch.Tensor, slot: KVSlot, pos: torch.Tensor, slots: torch.Tensor,
                     n_keys: int, kpos: torch.Tensor | None, dev_part=None, dev_mode: int = 0,
                     push: PushTarget | None = None) -> torch.Tensor:
@@ -281,7 +289,7 @@ class B200Engine:
         ext.rmsnorm(h, None, lw.ln1, cfg.rms_eps, x)
         q = self.ws.get("q", (n, cfg.q_size), torch.bfloat16)
         ext.gemm_qkv(x, lw.w_qkv, q, slot.k(layer), slot.v(layer), pos, slots, self.rope,
-                     cfg.n_heads, cfg.n_kv_heads, dev_part, dev_mode, self.bn,
+                     cfg.n_heads, cfg.n_kv_heads, dev_part, dev_mode, self._qkv_bn(n),
                      push.k(layer) if push else 0, push.v(layer) if push else 0)
         if push is not None:
             ext.peer_signal(push.flag(layer), push.epoch)

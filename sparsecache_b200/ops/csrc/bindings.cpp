@@ -76,8 +76,37 @@ void run_gemm(const sc::GemmArgs& g) {
   check_cuda(sc::gemm_bf16_tc(g, cur_stream()), "gemm_bf16_tc");
 }
 
+// Split-K for STORE/RESIDUAL GEMMs whose output has too few tiles to fill the
+// SMs (small M): K-slices write fp32 partials, an ordered reduce applies the
+// epilogue.  splits < 0 picks automatically; 1 disables.
+int auto_splits(const sc::GemmArgs& g) {
+  const int tiles = ((g.M + 127) / 128) * ((g.N + g.bn - 1) / g.bn);
+  const int num_kb = (g.K + 63) / 64;
+  if (2 * tiles > g.num_sms) return 1;
+  int s = g.num_sms / tiles;
+  if (s > num_kb / 8) s = num_kb / 8;  // at least 8 k-blocks (K = 512) per slice
+  if (s > 8) s = 8;
+  return s < 2 ? 1 : s;
+}
+
+bool run_gemm_split(sc::GemmArgs g, int64_t splits, const Tensor& like) {
+  const int s = splits < 0 ? auto_splits(g) : (int)splits;
+  if (s <= 1 || g.M == 0) return false;
+  Tensor ws = torch::empty({s, g.M, g.N}, like.options().dtype(torch::kFloat32));
+  const __nv_bfloat16* residual = g.epi == sc::EPI_RESIDUAL ? g.ep.residual : nullptr;
+  const int ldr = g.ep.ldr;
+  __nv_bfloat16* out = g.ep.out;
+  const int ldo = g.ep.ldo;
+  g.epi = sc::EPI_PARTIAL;
+  g.splits = s;
+  g.ep.ws = ws.data_ptr<float>();
+  check_cuda(sc::gemm_bf16_tc(g, cur_stream()), "gemm_bf16_tc (split-K)");
+  check_cuda(sc::splitk_reduce(g.ep.ws, s, g.M, g.N, residual, ldr, out, ldo, cur_stream()), "splitk_reduce");
+  return true;
+}
+
 // out = a @ w^T
-void gemm_store(Tensor a, Tensor w, Tensor out, int64_t bn) {
+int64_t gemm_store(Tensor a, Tensor w, Tensor out, int64_t bn, int64_t splits) {
   const c10::cuda::CUDAGuard guard(a.device());
   auto g = base_gemm(a, w, sc::EPI_STORE, (int)bn);
   check_matrix(out, "out");
@@ -85,11 +114,13 @@ void gemm_store(Tensor a, Tensor w, Tensor out, int64_t bn) {
   TORCH_CHECK(g.N % 32 == 0, "N must be a multiple of 32");
   g.ep.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   g.ep.ldo = (int)out.stride(0);
+  if (run_gemm_split(g, splits, a)) return 2;  // kernels launched
   run_gemm(g);
+  return 1;
 }
 
 // out = residual + bf16(a @ w^T)   (out may alias residual)
-void gemm_residual(Tensor a, Tensor w, Tensor out, Tensor residual, int64_t bn) {
+int64_t gemm_residual(Tensor a, Tensor w, Tensor out, Tensor residual, int64_t bn, int64_t splits) {
   const c10::cuda::CUDAGuard guard(a.device());
   auto g = base_gemm(a, w, sc::EPI_RESIDUAL, (int)bn);
   check_matrix(out, "out");
@@ -101,7 +132,9 @@ void gemm_residual(Tensor a, Tensor w, Tensor out, Tensor residual, int64_t bn) 
   g.ep.ldo = (int)out.stride(0);
   g.ep.residual = reinterpret_cast<const __nv_bfloat16*>(residual.data_ptr());
   g.ep.ldr = (int)residual.stride(0);
+  if (run_gemm_split(g, splits, a)) return 2;  // kernels launched
   run_gemm(g);
+  return 1;
 }
 
 // out[:, j] = silu(gate_j) * up_j with w_gu rows interleaved in blocks of bn/2
@@ -812,8 +845,10 @@ void wait_all(Tensor flags, int64_t n, Tensor epoch, int64_t offset, int64_t tim
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of sparsecache_b200";
-  m.def("gemm_store", &gemm_store);
-  m.def("gemm_residual", &gemm_residual);
+  m.def("gemm_store", &gemm_store, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("bn"),
+        py::arg("splits") = -1);
+  m.def("gemm_residual", &gemm_residual, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("residual"),
+        py::arg("bn"), py::arg("splits") = -1);
   m.def("gemm_swiglu", &gemm_swiglu);
   m.def("gemm_qkv", &gemm_qkv, py::arg("a"), py::arg("w_qkv"), py::arg("q_out"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("rope_pos"), py::arg("cache_slot"), py::arg("rope_table"),

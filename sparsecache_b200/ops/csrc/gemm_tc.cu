@@ -16,6 +16,11 @@
 //   EPI_STORE     C = acc
 //   EPI_RESIDUAL  C = R + bf16(acc)                         (o_proj, down_proj)
 //   EPI_SWIGLU    C = silu(gate) * up, gate/up interleaved in 128-col blocks
+//   EPI_PARTIAL   split-K: the fp32 partial of K-slice ks goes to
+//                 ws[ks][M][N]; splitk_reduce sums the slices in slice order
+//                 and applies the STORE / RESIDUAL epilogue.  Used when a
+//                 small-M GEMM has fewer output tiles than SMs (the o_proj and
+//                 down_proj of CacheBlend's active rows).
 //   EPI_QKV       RoPE on Q/K heads at per-row positions; Q to a row-major
 //                 buffer, K/V scattered into the paged layer cache at per-row
 //                 slots; optional per-(row, kv-head) deviation partials of the
@@ -85,9 +90,26 @@ __device__ __forceinline__ void load_row32(const __nv_bfloat16* src, float* v) {
 
 template <int BN, int EPI>
 __device__ __forceinline__ void gemm_epilogue_tile(const GemmEpilogue& ep, uint32_t tacc,
-                                                   int row, int tile_n, int M, int N, uint32_t* stage) {
+                                                   int row, int tile_n, int M, int N, uint32_t* stage,
+                                                   int ks) {
   const bool row_ok = row < M;
-  if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
+  if constexpr (EPI == EPI_PARTIAL) {
+    float* dst = ep.ws + ((size_t)ks * M + row) * N;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tacc + c * 32, r);
+      tmem_ld_wait();
+      const int col = tile_n * BN + c * 32;
+      if (row_ok && col < N) {
+        float4* d4 = reinterpret_cast<float4*>(dst + col);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          d4[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                              __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+      }
+    }
+  } else if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       uint32_t r[32];
@@ -268,7 +290,7 @@ template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ AMaps amaps,
                    const __grid_constant__ CUtensorMap tmap_b, int M, int N, int K,
-                   GemmEpilogue ep, AShards shards, int* status) {
+                   GemmEpilogue ep, AShards shards, int splits, int* status) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -281,8 +303,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int lane = lane_id();
   const int num_m = (M + kGemmBM - 1) / kGemmBM;
   const int num_n = (N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
   const int num_kb = (K + kGemmBK - 1) / kGemmBK;
+  // work unit u = (tile u / splits, K-slice u % splits); slice ks covers
+  // k-blocks [ks * num_kb / splits, (ks + 1) * num_kb / splits)
+  const int num_units = num_m * num_n * splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -320,9 +344,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int s = 0; s < S; ++s) issued[s] = false, issued_phase[s] = 0;
       bool ok = true;
       unsigned confirmed = 1u << shards.own;  // shards known to be ready
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         int tm, tn;
-        tile_coords(t, num_m, shards, tm, tn);
+        tile_coords(u / splits, num_m, shards, tm, tn);
+        const int ks = u % splits;
+        const int kb0 = ks * num_kb / splits, kb1 = (ks + 1) * num_kb / splits;
         int map = 0, ay = tm * kGemmBM;
         if (shards.n > 1) {
           map = ay / shards.rows;
@@ -335,7 +361,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             confirmed |= 1u << map;
           }
         }
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&bars->empty[stage], phase ^ 1, status, kStatusTimeoutSmemEmpty)) {
             ok = false;
             break;
@@ -363,7 +389,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int local = 0;
       bool ok = true;
       bool any = false;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
+        const int ks = u % splits;
+        const int kb0 = ks * num_kb / splits, kb1 = (ks + 1) * num_kb / splits;
         const int buf = local & 1;
         const uint32_t tphase = (local >> 1) & 1;
         if (!mbar_wait(&bars->tmem_empty[buf], tphase ^ 1, status, kStatusTimeoutTmemEmpty)) {
@@ -372,7 +400,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         const uint32_t tacc = tmem_base + buf * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&bars->full[stage], phase, status, kStatusTimeoutTmaFull)) {
             ok = false;
             break;
@@ -384,7 +412,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int k = 0; k < kGemmBK / 16; ++k) {
             const uint64_t ad = make_desc_kmajor_sw128(sa + k * 32);
             const uint64_t bd = make_desc_kmajor_sw128(sb + k * 32);
-            tc_mma_f16(tacc, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            tc_mma_f16(tacc, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           any = true;
           tc_commit(&bars->empty[stage]);
@@ -403,16 +431,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ---------------- Epilogue (warps 2..5) ----------------
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     int local = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
       int tm, tn;
-      tile_coords(t, num_m, shards, tm, tn);
+      tile_coords(u / splits, num_m, shards, tm, tn);
       const int buf = local & 1;
       const uint32_t tphase = (local >> 1) & 1;
       if (!mbar_wait(&bars->tmem_full[buf], tphase, status, kStatusTimeoutTmemFull)) break;
       tc_fence_after();
       const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
       const int row = tm * kGemmBM + quarter * 32 + lane;
-      gemm_epilogue_tile<BN, EPI>(ep, tacc, row, tn, M, N, epi_stage + quarter * (32 * 33));
+      gemm_epilogue_tile<BN, EPI>(ep, tacc, row, tn, M, N, epi_stage + quarter * (32 * 33), u % splits);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->tmem_empty[buf]);
@@ -477,10 +505,12 @@ static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   if (!make_tmap_2d_bf16(&tb, g.b, g.K, g.N, g.ldb, kGemmBK, BN, true)) return cudaErrorInvalidValue;
   auto kern = gemm_tc_kernel<BN, EPI>;
   ensure_smem_attr(kern, Cfg::kSmemBytes);
-  const int num_tiles = ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + BN - 1) / BN);
-  int grid = num_tiles < g.num_sms ? num_tiles : g.num_sms;
+  const int splits = EPI == EPI_PARTIAL ? (g.splits < 1 ? 1 : g.splits) : 1;
+  if (splits > (g.K + kGemmBK - 1) / kGemmBK) return cudaErrorInvalidValue;  // every slice needs a k-block
+  const int num_units = ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + BN - 1) / BN) * splits;
+  int grid = num_units < g.num_sms ? num_units : g.num_sms;
   if (grid < 1) grid = 1;
-  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(maps, tb, g.M, g.N, g.K, g.ep, sh, g.status);
+  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(maps, tb, g.M, g.N, g.K, g.ep, sh, splits, g.status);
   return cudaGetLastError();
 }
 
@@ -498,8 +528,47 @@ cudaError_t gemm_bf16_tc(const GemmArgs& g, cudaStream_t stream) {
       return bn == 128 ? launch_gemm<128, EPI_QKV>(g, stream) : launch_gemm<256, EPI_QKV>(g, stream);
     case EPI_RS:
       return bn == 128 ? launch_gemm<128, EPI_RS>(g, stream) : launch_gemm<256, EPI_RS>(g, stream);
+    case EPI_PARTIAL:
+      return bn == 128 ? launch_gemm<128, EPI_PARTIAL>(g, stream) : launch_gemm<256, EPI_PARTIAL>(g, stream);
   }
   return cudaErrorInvalidValue;
+}
+
+// Sum of the K-slice partials in slice order, then the STORE or RESIDUAL
+// epilogue (out = residual + bf16(sum), the HF rounding order).
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N,
+                                     const __nv_bfloat16* residual, int ldr, __nv_bfloat16* out, int ldo) {
+  const int n4 = N / 4;
+  const long long total = (long long)M * n4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(i / n4), c = (int)(i % n4) * 4;
+    float4 acc = __ldcs(reinterpret_cast<const float4*>(ws + (size_t)row * N + c));
+    for (int s = 1; s < splits; ++s) {
+      const float4 p = __ldcs(reinterpret_cast<const float4*>(ws + ((size_t)s * M + row) * N + c));
+      acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+    }
+    float v[4] = {acc.x, acc.y, acc.z, acc.w};
+    if (residual != nullptr) {
+      const uint2 rr = *reinterpret_cast<const uint2*>(residual + (size_t)row * ldr + c);
+      const float2 r0 = unpack_bf16x2(rr.x), r1 = unpack_bf16x2(rr.y);
+      v[0] = r0.x + bf16_round(v[0]);
+      v[1] = r0.y + bf16_round(v[1]);
+      v[2] = r1.x + bf16_round(v[2]);
+      v[3] = r1.y + bf16_round(v[3]);
+    }
+    *reinterpret_cast<uint2*>(out + (size_t)row * ldo + c) =
+        make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+  }
+}
+
+cudaError_t splitk_reduce(const float* ws, int splits, int M, int N, const __nv_bfloat16* residual, int ldr,
+                          __nv_bfloat16* out, int ldo, cudaStream_t stream) {
+  if (N % 4 != 0 || splits < 1) return cudaErrorInvalidValue;
+  const long long total = (long long)M * (N / 4);
+  const int grid = (int)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
+  splitk_reduce_kernel<<<grid < 1 ? 1 : grid, 256, 0, stream>>>(ws, splits, M, N, residual, ldr, out, ldo);
+  return cudaGetLastError();
 }
 
 }  // namespace sc

@@ -18,7 +18,7 @@ bool make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint6
                        bool swizzle128);
 
 // ---------------------------------------------------------------- GEMM ----
-enum Epi : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_RS = 4 };
+enum Epi : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_RS = 4, EPI_PARTIAL = 5 };
 constexpr int kMaxShards = 8;
 enum DevMode : int { DEV_KEY = 1, DEV_VALUE = 2, DEV_L1 = 4 };
 
@@ -50,6 +50,8 @@ struct GemmEpilogue {
   void* rs_dst[kMaxShards];
   int rs_rows;
   int rs_sender;
+  // EPI_PARTIAL (split-K): fp32 partial of K-slice ks at ws[ks][row][col]
+  float* ws;
 };
 
 // A operand split by rows over ranks (all-gather fused into the GEMM): shard
@@ -72,12 +74,15 @@ struct GemmArgs {
   int M, N, K, lda, ldb;
   int epi;
   int bn;  // 128 or 256
+  int splits;  // EPI_PARTIAL: number of K slices (>= 1)
   int num_sms;
   GemmEpilogue ep;
   int* status;
 };
 
 cudaError_t gemm_bf16_tc(const GemmArgs& g, cudaStream_t stream);
+cudaError_t splitk_reduce(const float* ws, int splits, int M, int N, const __nv_bfloat16* residual, int ldr,
+                          __nv_bfloat16* out, int ldo, cudaStream_t stream);
 
 // ---------------------------------------------------------------- GEMV ----
 // Small-M (1..8 rows) weight-streaming kernel for decode / verify.

@@ -24,9 +24,8 @@
 namespace sc {
 
 namespace {
-// 4 warps a CTA in both directions: the loads of the next key pair are in
-// flight while the current pair is computed, so 4 resident CTAs an SM keep
-// enough bytes in flight
+// 4 warps a CTA in both directions; the forward keeps the loads of the next
+// key pair in flight while the current pair is computed
 constexpr int kFwdThreads = 128;
 constexpr int kBwdThreads = 128;
 
@@ -215,18 +214,19 @@ __global__ void __launch_bounds__(kBwdThreads) mem_attn_bwd_kernel(MemAttnArgs a
 #pragma unroll
   for (int i = 0; i < 16; ++i) dq[i] = 0.f;
   if (lse2 != -INFINITY) {
-    KvRaw cur, nxt;  // warp-uniform trip count and next-iteration prefetch (see forward)
-    int base = warp * 8;
-    if (base < c.n) fetch(c, base, lane, cur);
-    for (; base < c.n; base += kKeysPerIter) {
-      if (base + kKeysPerIter < c.n) fetch(c, base + kKeysPerIter, lane, nxt);
+    // warp-uniform trip count (see forward); no register prefetch here: the
+    // backward already holds q, dO and the dq accumulator, and measured
+    // faster with 4 resident CTAs an SM than with the prefetch buffers
+    for (int base = warp * 8; base < c.n; base += kKeysPerIter) {
       const int j0 = base + (lane >> 3), j1 = j0 + 4;
       const bool has0 = j0 < c.n, has1 = j1 < c.n;
       float k0[16], v0[16], k1[16], v1[16];
-      unpack16(cur.k0, k0);
-      unpack16(cur.v0, v0);
-      unpack16(cur.k1, k1);
-      unpack16(cur.v1, v1);
+      const long long o0 = tok_off(c, has0 ? j0 : base);
+      const long long o1 = tok_off(c, has1 ? j1 : base);
+      load16(c.kb + o0, k0);
+      load16(c.vb + o0, v0);
+      load16(c.kb + o1, k1);
+      load16(c.vb + o1, v1);
       float s0 = 0.f, s1 = 0.f, dp0 = 0.f, dp1 = 0.f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -243,7 +243,6 @@ __global__ void __launch_bounds__(kBwdThreads) mem_attn_bwd_kernel(MemAttnArgs a
       const float ds1 = has1 ? exp2f(s1 - lse2) * (dp1 - dd) : 0.f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) dq[i] = fmaf(ds0, k0[i], fmaf(ds1, k1[i], dq[i]));
-      cur = nxt;
     }
   }
 #pragma unroll

@@ -48,55 +48,86 @@ FLAG_SLOTS = 8
 
 
 class PDChannel:
-    """Decode-side slot + flags shared with the prefill rank over CUDA IPC."""
+    """Decode-side slots + flags shared with the prefill rank over CUDA IPC.
+
+    ``n_slots`` decode slots let the prefill rank push request i+1 while the
+    decode rank still decodes request i.  Slot s has its own flag block
+    (``n_layers`` layer flags, the seed token, the completion flag); the
+    prefill rank owns ``free`` flags (one per slot) that the decode rank
+    releases when it is done with a slot, and waits on them (bounded) before
+    pushing into a slot again.
+    """
 
     def __init__(self, engine: B200Engine, *, role: str, capacity: int, prefill_rank: int, decode_rank: int,
-                 group=None) -> None:
+                 group=None, n_slots: int = 1) -> None:
         self.engine = engine
         self.role = role
         self.capacity = capacity
+        self.n_slots = n_slots
         cfg = engine.cfg
         self.n_layers = cfg.n_layers
+        self.flag_stride = cfg.n_layers + FLAG_SLOTS
         ext = ops.ext()
         dev = engine.device.index
+        self.slot_bytes = KVSlot.nbytes_for(cfg, capacity)
+        self.status = torch.zeros(1, dtype=torch.int32, device=engine.device)
+        self.stamps = torch.zeros(4, dtype=torch.int64, device=engine.device)
         handles = None
         if role == "decode":
-            buf, h_slot = ext.shared_empty(KVSlot.nbytes_for(cfg, capacity), dev)
-            flags, h_flags = ext.shared_empty(4 * (cfg.n_layers + FLAG_SLOTS), dev)
+            buf, h_slot = ext.shared_empty(self.slot_bytes * n_slots, dev)
+            flags, h_flags = ext.shared_empty(4 * self.flag_stride * n_slots, dev)
             self._buffers = (buf, flags)
-            self.slot = KVSlot.from_buffer(cfg, capacity, buf)
-            self.flags = flags.view(torch.int32)
-            self.status = torch.zeros(1, dtype=torch.int32, device=engine.device)
-            self.stamps = torch.zeros(4, dtype=torch.int64, device=engine.device)
+            self.slots = [KVSlot.from_buffer(cfg, capacity, buf[i * self.slot_bytes:(i + 1) * self.slot_bytes])
+                          for i in range(n_slots)]
+            self.slot = self.slots[0]
+            self.all_flags = flags.view(torch.int32)
+            self.flags = self.all_flags[: self.flag_stride]
             handles = (h_slot, h_flags)
+        else:
+            free, h_free = ext.shared_empty(4 * max(n_slots, 4), dev)
+            self._free = free
+            self.free = free.view(torch.int32)
+            handles = (h_free,)
         gathered = [None] * dist.get_world_size(group)
         dist.all_gather_object(gathered, handles, group=group)
         self.epoch = 0
+
+        def peer(rank):
+            return gathered[dist.get_group_rank(group, rank) if group is not None else rank]
+
         if role == "prefill":
-            h_slot, h_flags = gathered[dist.get_group_rank(group, decode_rank) if group is not None else decode_rank]
+            h_slot, h_flags = peer(decode_rank)
             self.base = ext.shared_open(h_slot)
             self.flag_base = ext.shared_open(h_flags)
             self.slot = engine.new_slot(capacity)
-            self.stamps = torch.zeros(4, dtype=torch.int64, device=engine.device)
+        else:
+            (h_free,) = peer(prefill_rank)
+            self.free_base = ext.shared_open(h_free)
 
-    def push_target(self) -> PushTarget:
+    def push_target(self, index: int = 0) -> PushTarget:
         cfg = self.engine.cfg
-        return PushTarget(self.base, self.capacity, self.flag_base, self.epoch, cfg.n_layers,
+        return PushTarget(self.base + index * self.slot_bytes, self.capacity,
+                          self.flag_base + 4 * self.flag_stride * index, self.epoch, cfg.n_layers,
                           cfg.n_kv_heads * self.capacity * cfg.head_dim)
 
+    def slot_flags(self, index: int) -> torch.Tensor:
+        return self.all_flags[index * self.flag_stride:(index + 1) * self.flag_stride]
+
     def close(self) -> None:
+        ext = ops.ext()
         if self.role == "prefill":
-            ext = ops.ext()
             ext.shared_close(self.base)
             ext.shared_close(self.flag_base)
+        else:
+            ext.shared_close(self.free_base)
 
 
-def prefill_request(ch: PDChannel, ids: torch.Tensor, max_new: int) -> None:
-    """Prefill side: prefill with the fused push, then publish the seed token."""
+def prefill_request(ch: PDChannel, ids: torch.Tensor, max_new: int, index: int = 0) -> None:
+    """Prefill side: prefill with the fused push into decode slot ``index``, then publish the seed token."""
     eng = ch.engine
     ext = eng.ext
     T = ids.numel()
-    push = ch.push_target()
+    push = ch.push_target(index)
     h = eng.prefill(ids, ch.slot, push=push)
     b = eng.first_token(h[T - 1:T], position=T, max_new=max_new)
     L = ch.n_layers
@@ -104,20 +135,30 @@ def prefill_request(ch: PDChannel, ids: torch.Tensor, max_new: int) -> None:
     ext.peer_signal(push.flag(L + 1), push.epoch, ch.stamps[0:1])
 
 
-def decode_request(ch: PDChannel, T: int, max_new: int, timeout_s: float = 20.0) -> None:
-    """Decode side: wait (bounded) for every layer and the seed, then greedy decode."""
-    eng = ch.engine
-    ext = eng.ext
-    L = ch.n_layers
-    ext.wait_flag(ch.flags, L - 1, ch.epoch, int(timeout_s * 1e9), ch.status, ch.stamps[0:1])
-    ext.wait_flag(ch.flags, L + 1, ch.epoch, int(timeout_s * 1e9), ch.status, ch.stamps[1:2])
+def wait_ready(ch: PDChannel, index: int = 0, timeout_s: float = 20.0) -> None:
+    """Decode side: bounded device wait for every layer of slot ``index`` and its seed."""
+    ext, L, flags = ch.engine.ext, ch.n_layers, ch.slot_flags(index)
+    ext.wait_flag(flags, L - 1, ch.epoch, int(timeout_s * 1e9), ch.status, ch.stamps[0:1])
+    ext.wait_flag(flags, L + 1, ch.epoch, int(timeout_s * 1e9), ch.status, ch.stamps[1:2])
+
+
+def decode_ready(ch: PDChannel, T: int, max_new: int, index: int = 0) -> None:
+    """Decode side, after ``wait_ready``: greedy decode from the pushed KV and seed."""
+    eng, L = ch.engine, ch.n_layers
+    flags = ch.slot_flags(index)
     b = eng._decode_buffers(max_new)
-    ext.embedding(ch.flags[L:L + 1], eng.w.embed, b["h"][:1])
-    b["log"][0:1].copy_(ch.flags[L:L + 1])
+    eng.ext.embedding(flags[L:L + 1], eng.w.embed, b["h"][:1])
+    b["log"][0:1].copy_(flags[L:L + 1])
     b["gen"].fill_(1)
     b["counter"].zero_()
     eng.set_decode_state(position=T)
-    eng.decode(ch.slot, max_new - 1, max_new=max_new)
+    eng.decode(ch.slots[index], max_new - 1, max_new=max_new)
+
+
+def decode_request(ch: PDChannel, T: int, max_new: int, timeout_s: float = 20.0, index: int = 0) -> None:
+    """Decode side: wait (bounded) for every layer and the seed, then greedy decode."""
+    wait_ready(ch, index, timeout_s)
+    decode_ready(ch, T, max_new, index)
 
 
 def nccl_prefill_request(eng: B200Engine, slot: KVSlot, ids: torch.Tensor, max_new: int, peer: int) -> torch.Tensor:

@@ -239,7 +239,7 @@ def main(argv=None) -> None:
     from ..models.engine import B200Engine
     from ..serving.server import RAGServer
     from ..store import DocumentKVStore
-    from ..synthetic import WORKLOADS, make_requests
+    from ..synthetic import make_requests
 
     p = argparse.ArgumentParser()
     p.add_argument("--model", default="llama3-8b")
@@ -256,8 +256,8 @@ def main(argv=None) -> None:
     a = p.parse_args(argv)
     cfg = get_model_config(a.model)
     eng = B200Engine.random(cfg, seed=0, device="cuda")
-    reqs = make_requests(WORKLOADS[a.workload])[: a.requests + a.warmup]
-    store = DocumentKVStore(tier="hbm")
+    reqs = make_requests(a.workload, cfg)[: a.requests + a.warmup]
+    store = DocumentKVStore(cfg, tier="hbm", device=eng.device)
     server = RAGServer(eng, store, capacity=max(r.prompt_tokens for r in reqs) + a.max_new_tokens + 64,
                        blend=CacheBlendConfig(check_layer=a.check_layer, recompute_ratio=a.recompute_ratio,
                                               max_new_tokens=a.max_new_tokens))

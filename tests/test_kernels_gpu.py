@@ -41,6 +41,30 @@ def test_gemm_store(cuda_device, bn, mnk):
     assert _rel_err(out, ref) < 1e-2
 
 
+@pytest.mark.parametrize("mnk", [(300, 4096, 14336), (200, 4096, 4096), (64, 1024, 1024)])
+def test_gemm_split_k_residual(cuda_device, mnk):
+    """Split-K (fp32 slice partials + ordered reduce) equals the single-pass GEMM within bf16 rounding."""
+    M, N, K = mnk
+    g = torch.Generator(device="cpu").manual_seed(M * 7 + K)
+    a = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(cuda_device, torch.bfloat16)
+    res = torch.randn(M, N, generator=g).to(cuda_device, torch.bfloat16)
+    ref = res.float() + (a.float() @ w.float().T).to(torch.bfloat16).float()
+    outs = {}
+    for splits in (1, 2, 3, -1):
+        out = res.clone()
+        launched = _ext().gemm_residual(a, w, out, out, 256, splits)
+        torch.cuda.synchronize()
+        _status_ok(cuda_device)
+        assert launched == (1 if splits == 1 else launched)
+        assert _rel_err(out, ref) < 1e-2, splits
+        outs[splits] = out
+    st = torch.empty(M, N, device=cuda_device, dtype=torch.bfloat16)
+    assert _ext().gemm_store(a, w, st, 256, 3) == 2
+    torch.cuda.synchronize()
+    assert _rel_err(st, a.float() @ w.float().T) < 1e-2
+
+
 def test_gemm_residual_and_swiglu(cuda_device):
     M, K, F = 257, 512, 1024
     a = torch.randn(M, K, device=cuda_device).to(torch.bfloat16)
@@ -80,8 +104,9 @@ def _qkv_reference(a, w, cfg, pos, nq, nkv):
     return q * cos + rot(q) * sin, k * cos + rot(k) * sin, v
 
 
+@pytest.mark.parametrize("bn", [128, 256])
 @pytest.mark.parametrize("dev_mode", [0, 1, 2, 3, 6])
-def test_gemm_qkv_rope_scatter_deviation(cuda_device, dev_mode):
+def test_gemm_qkv_rope_scatter_deviation(cuda_device, dev_mode, bn):
     cfg = get_model_config("tiny128")
     nq, nkv, K, M, cap = 4, 2, 512, 200, 600
     a = torch.randn(M, K, device=cuda_device).to(torch.bfloat16)
@@ -94,7 +119,7 @@ def test_gemm_qkv_rope_scatter_deviation(cuda_device, dev_mode):
     q_out = torch.empty(M, nq * 128, device=cuda_device, dtype=torch.bfloat16)
     table = rope_table(cfg, 1024, cuda_device)
     dev = torch.zeros(M, 2 * nkv, device=cuda_device) if dev_mode else None
-    _ext().gemm_qkv(a, w, q_out, kc, vc, pos, slot, table, nq, nkv, dev, dev_mode, 256)
+    _ext().gemm_qkv(a, w, q_out, kc, vc, pos, slot, table, nq, nkv, dev, dev_mode, bn)
     torch.cuda.synchronize()
     _status_ok(cuda_device)
     q, k, v = _qkv_reference(a, w, cfg, pos, nq, nkv)

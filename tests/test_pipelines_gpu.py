@@ -20,7 +20,7 @@ def test_progressive_cacheblend_final_stage_matches_one_shot(cuda_device):
     cfg = get_model_config("tiny128")
     engine = B200Engine.from_oracle(LlamaOracle.random_init(cfg, seed=5, std=0.05), cuda_device, max_positions=8192)
     reqs = make_requests("tiny_plumbing", cfg)[:2]
-    server = RAGServer(engine, DocumentKVStore(tier="hbm"), capacity=4096,
+    server = RAGServer(engine, DocumentKVStore(cfg, tier="hbm", device=cuda_device), capacity=4096,
                        blend=CacheBlendConfig(check_layer=1, recompute_ratio=0.15, max_new_tokens=12))
     server.produce(reqs)
     prep = prepare_request(reqs[0], schedule="sequential", fractions=(0.3, 0.6, 1.0))
