@@ -38,7 +38,7 @@ def main() -> None:
     from .. import ops
 
     p = argparse.ArgumentParser()
-    p.add_argument("--only", default="gemm,gemv,attn_decode,attn_prefill,mem_attn,adamw")
+    p.add_argument("--only", default="gemm,gemm_small,gemv,attn_decode,attn_prefill,mem_attn,adamw")
     args = p.parse_args()
     only = set(args.only.split(","))
     ext = ops.ext()
@@ -68,6 +68,30 @@ def main() -> None:
                 tf = 2 * M * N * K / (t * 1e-6) / 1e12
                 res[f"gemm_M{M}_{name}"] = {"us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS,
                                             "weight_GBps": N * K * 2 / (t * 1e-6) / 1e9}
+
+    if "gemm_small" in only or "gemm_down_splitk" in only:
+        # CacheBlend active rows (~15% of a 1.7k-token prompt): the layer's four
+        # projections as the engine issues them (128-wide QKV tiles, split-K o/down)
+        M = 300
+        cases = (("qkv_bn128", 6144, 4096, "store", 128), ("o_splitk", 4096, 4096, "residual", 256),
+                 ("gate_up", 28672, 4096, "swiglu", 256), ("down_splitk", 4096, 14336, "residual", 256))
+        if "gemm_small" not in only:
+            cases = cases[3:]
+        for name, N, K, kind, bn in cases:
+            a = torch.randn(M, K, device=dev).to(bf)
+            w = (torch.randn(N, K, device=dev) * 0.02).to(bf)
+            o = torch.empty(M, N // 2 if kind == "swiglu" else N, device=dev, dtype=bf)
+            if kind == "store":
+                fn = lambda: ext.gemm_store(a, w, o, bn, -1)  # noqa: E731
+            elif kind == "residual":
+                fn = lambda: ext.gemm_residual(a, w, o, o, bn, -1)  # noqa: E731
+            else:
+                fn = lambda: ext.gemm_swiglu(a, w, o, bn)  # noqa: E731
+            t = timeit(fn, n=20)
+            tf = 2 * M * N * K / (t * 1e-6) / 1e12
+            res[f"gemm_M{M}_{name}"] = {"us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS,
+                                        "weight_GBps": N * K * 2 / (t * 1e-6) / 1e9,
+                                        "weight_frac_of_measured_hbm": N * K * 2 / (t * 1e-6) / 1e9 / HBM_GBS}
 
     if "attn_decode" in only:
         H, Hkv = 32, 8
