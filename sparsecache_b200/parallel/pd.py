@@ -301,6 +301,112 @@ def run(args) -> dict | None:
     return out
 
 
+def serve_poisson(args) -> dict | None:
+    """Open-loop serving of Poisson arrivals on prefill/decode pairs.
+
+    Each pair draws seeded exponential inter-arrival gaps at ``arrival_rate``
+    requests/s.  The prefill rank starts request i at max(arrival_i, its
+    previous prefill end), waits (bounded, on the device) until decode slot
+    i mod n_slots is free again, and prefills with the fused push into that
+    slot.  The decode rank decodes the requests in order; after each it
+    releases the slot's free flag in the prefill rank's memory.  So a
+    request's prefill and its KV transfer overlap the previous request's
+    decode.  Per request: TTFT = decode-side readiness of KV + seed minus the
+    arrival time; TPOT from CUDA events around the decode; exposed transfer =
+    readiness minus the prefill rank's prefill end (host monotonic clock,
+    one machine).
+    """
+    import random
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    if world % 2:
+        raise ValueError("prefill/decode needs an even number of ranks (pairs)")
+    pairs = world // 2
+    role = "prefill" if rank < pairs else "decode"
+    pair = rank % pairs
+    cfg = get_model_config(args.model)
+    if args.layers:
+        cfg = cfg.with_layers(args.layers)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    engine = B200Engine.random(cfg, seed=0, device=dev, max_positions=65536)
+    mine = [r for r in make_requests("pd_long", cfg) if r.index % pairs == pair]
+    n = args.warmup + args.steps
+    served = [mine[i % len(mine)] for i in range(n)]
+    capacity = max(r.prompt_tokens for r in served) + args.new_tokens + 64
+    groups = [dist.new_group([p, p + pairs]) for p in range(pairs)]
+    group = groups[pair]
+    ch = PDChannel(engine, role=role, capacity=capacity, prefill_rank=pair, decode_rank=pair + pairs, group=group,
+                   n_slots=args.slots)
+    rng = random.Random(args.seed * 1000 + pair)
+    arrivals, t = [], 0.0
+    for i in range(n):
+        arrivals.append(t)
+        t += rng.expovariate(args.arrival_rate) if i >= args.warmup else 0.5
+    ext = engine.ext
+    timeout_ns = int(60e9)
+    dist.barrier(group=group)
+    torch.cuda.synchronize()
+    t0 = time.monotonic()
+    rec: list[dict] = []
+    for i, req in enumerate(served):
+        s = i % args.slots
+        ch.epoch = i + 1
+        T = req.prompt_tokens
+        if role == "prefill":
+            wait = arrivals[i] - (time.monotonic() - t0)
+            if wait > 0:
+                time.sleep(wait)
+            t_start = time.monotonic() - t0
+            if i >= args.slots:  # the decode rank has finished the slot's previous request
+                ext.wait_flag(ch.free, s, i + 1 - args.slots, timeout_ns, ch.status)
+            prefill_request(ch, torch.tensor(req.prompt, dtype=torch.int32, device=dev), args.new_tokens, index=s)
+            torch.cuda.synchronize()
+            rec.append({"i": i, "start": t_start, "prefill_end": time.monotonic() - t0})
+        else:
+            wait_ready(ch, s, timeout_s=60.0)
+            torch.cuda.synchronize()
+            t_ready = time.monotonic() - t0
+            a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+            a.record()
+            decode_ready(ch, T, args.new_tokens, index=s)
+            b.record()
+            ext.peer_signal(ch.free_base + 4 * s, i + 1)
+            b.synchronize()
+            rec.append({"i": i, "ready": t_ready, "arrival": arrivals[i], "prompt_tokens": T,
+                        "tpot_ms": a.elapsed_time(b) / max(1, args.new_tokens - 1)})
+    torch.cuda.synchronize()
+    if int(ch.status.item()) != 0:
+        raise RuntimeError("a bounded peer-flag wait timed out")
+    gathered = [None] * world
+    dist.all_gather_object(gathered, (role, pair, rec))
+    dist.barrier()
+    ch.close()
+    if rank != 0:
+        return None
+    pre = {(p, r["i"]): r for role_, p, rr in gathered if role_ == "prefill" for r in rr}
+    rows = []
+    for role_, p, rr in gathered:
+        if role_ != "decode":
+            continue
+        for r in rr:
+            if r["i"] < args.warmup:
+                continue
+            pr = pre[(p, r["i"])]
+            rows.append({"ttft_ms": (r["ready"] - r["arrival"]) * 1e3, "tpot_ms": r["tpot_ms"],
+                         "exposed_ms": max(0.0, (r["ready"] - pr["prefill_end"]) * 1e3),
+                         "queue_ms": (pr["start"] - r["arrival"]) * 1e3, "prompt_tokens": r["prompt_tokens"]})
+
+    def pct(key, q):
+        v = sorted(x[key] for x in rows)
+        return v[min(len(v) - 1, int(round(q * (len(v) - 1))))] if v else None
+
+    return {"mode": "push_poisson", "pairs": pairs, "arrival_rate_per_pair": args.arrival_rate, "slots": args.slots,
+            "model": cfg.name, "layers": cfg.n_layers, "new_tokens": args.new_tokens, "requests": len(rows),
+            **{f"{k}_p{int(q * 100)}": pct(k, q) for k in ("ttft_ms", "tpot_ms", "exposed_ms", "queue_ms")
+               for q in (0.5, 0.99)},
+            "mean_prompt_tokens": statistics.fmean(r["prompt_tokens"] for r in rows) if rows else None}
+
+
 def main() -> None:
     p = argparse.ArgumentParser(description="Prefill/decode disaggregation with the fused NVLink KV push")
     p.add_argument("--model", default="llama3-8b")
@@ -309,12 +415,16 @@ def main() -> None:
     p.add_argument("--steps", type=int, default=4)
     p.add_argument("--warmup", type=int, default=2)
     p.add_argument("--new-tokens", type=int, default=128)
+    p.add_argument("--arrival-rate", type=float, default=0.0,
+                   help="requests/s per pair; > 0 serves open-loop Poisson arrivals")
+    p.add_argument("--slots", type=int, default=2, help="decode slots per pair (Poisson mode)")
+    p.add_argument("--seed", type=int, default=0)
     args = p.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     try:
-        out = run(args)
+        out = serve_poisson(args) if args.arrival_rate > 0 else run(args)
         if out is not None:
             print(json.dumps(out), flush=True)
     finally:
