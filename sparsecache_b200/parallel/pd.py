@@ -312,9 +312,10 @@ def serve_poisson(args) -> dict | None:
     releases the slot's free flag in the prefill rank's memory.  So a
     request's prefill and its KV transfer overlap the previous request's
     decode.  Per request: TTFT = decode-side readiness of KV + seed minus the
-    arrival time; TPOT from CUDA events around the decode; exposed transfer =
-    readiness minus the prefill rank's prefill end (host monotonic clock,
-    one machine).
+    arrival time; TPOT from CUDA events around the decode; the decoder queue =
+    readiness minus the prefill rank's prefill end (the pushed KV is complete
+    when the prefill ends; the closed-loop mode measures the exposed
+    transfer itself).  Host monotonic clock, one machine.
     """
     import random
 
@@ -393,8 +394,11 @@ def serve_poisson(args) -> dict | None:
                 continue
             pr = pre[(p, r["i"])]
             rows.append({"ttft_ms": (r["ready"] - r["arrival"]) * 1e3, "tpot_ms": r["tpot_ms"],
-                         "exposed_ms": max(0.0, (r["ready"] - pr["prefill_end"]) * 1e3),
-                         "queue_ms": (pr["start"] - r["arrival"]) * 1e3, "prompt_tokens": r["prompt_tokens"]})
+                         # KV + seed are complete on the decode GPU at prefill end (the push is fused
+                         # into the prefill); what remains is the wait for the decoder to be free
+                         "decoder_queue_ms": max(0.0, (r["ready"] - pr["prefill_end"]) * 1e3),
+                         "prefill_queue_ms": (pr["start"] - r["arrival"]) * 1e3,
+                         "prefill_ms": (pr["prefill_end"] - pr["start"]) * 1e3, "prompt_tokens": r["prompt_tokens"]})
 
     def pct(key, q):
         v = sorted(x[key] for x in rows)
@@ -402,7 +406,8 @@ def serve_poisson(args) -> dict | None:
 
     return {"mode": "push_poisson", "pairs": pairs, "arrival_rate_per_pair": args.arrival_rate, "slots": args.slots,
             "model": cfg.name, "layers": cfg.n_layers, "new_tokens": args.new_tokens, "requests": len(rows),
-            **{f"{k}_p{int(q * 100)}": pct(k, q) for k in ("ttft_ms", "tpot_ms", "exposed_ms", "queue_ms")
+            **{f"{k}_p{int(q * 100)}": pct(k, q) for k in ("ttft_ms", "tpot_ms", "prefill_ms", "prefill_queue_ms",
+                                                                 "decoder_queue_ms")
                for q in (0.5, 0.99)},
             "mean_prompt_tokens": statistics.fmean(r["prompt_tokens"] for r in rows) if rows else None}
 
