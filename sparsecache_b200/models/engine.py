@@ -469,7 +469,7 @@ class B200Engine:
         return b
 
     def _forward_rows(self, slot: KVSlot, b: dict, M: int, splits: int, *, view: torch.Tensor | None,
-                      log: bool, feedback: bool) -> None:
+                      log: bool, feedback: bool, layers=None) -> None:
         """One forward of the M rows in b['h'][:M] at the device positions in b['pos'].
 
         With ``view`` (an int32 slot map of the slot), attention reads the
@@ -481,7 +481,9 @@ class B200Engine:
         H = cfg.n_heads
         h = b["h"][:M]
         pos = b["pos"]
-        for layer, lw in enumerate(self.w.layers):
+        order = range(len(self.w.layers)) if layers is None else layers
+        for layer in order:  # a layer subset (layer-sparse drafting) skips the others as identity
+            lw = self.w.layers[layer]
             ext.gemv_qkv(h, lw.w_qkv, lw.ln1, cfg.rms_eps, b["q"][:M], slot.k(layer), slot.v(layer), pos[0:1],
                          self.rope, cfg.n_heads, cfg.n_kv_heads, slot=pos[1:2])
             ext.attention_decode(b["q"][:M], slot.k(layer), slot.v(layer), pos[0:1], H, self.scale, splits,
@@ -496,7 +498,7 @@ class B200Engine:
                         pos, 3)
 
     def decode(self, slot: KVSlot, n_steps: int, *, max_new: int, use_graph: bool = True,
-               view: torch.Tensor | None = None) -> None:
+               view: torch.Tensor | None = None, layers: tuple[int, ...] | None = None) -> None:
         """Run ``n_steps`` greedy decode steps from the device state.
 
         Each step feeds back the previous argmax (its embedding is already in
@@ -509,22 +511,22 @@ class B200Engine:
         b = self._decode_buffers(max_new)
         if not use_graph:
             for _ in range(n_steps):
-                self._forward_rows(slot, b, 1, splits, view=view, log=True, feedback=True)
+                self._forward_rows(slot, b, 1, splits, view=view, log=True, feedback=True, layers=layers)
             return
-        key = (id(slot), splits, None if view is None else view.data_ptr())
+        key = (id(slot), splits, None if view is None else view.data_ptr(), layers)
         graph = self._graphs.get(key)
         if graph is None:
             # one eager step warms up launch attributes; then capture a step
             # against a snapshot of the device state so the real state is
             # only advanced by replays.
             saved = {k: b[k].clone() for k in ("h", "pos", "gen", "log", "tok")}
-            self._forward_rows(slot, b, 1, splits, view=view, log=True, feedback=True)
+            self._forward_rows(slot, b, 1, splits, view=view, log=True, feedback=True, layers=layers)
             for k, v in saved.items():
                 b[k].copy_(v)
             torch.cuda.synchronize(self.device)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                self._forward_rows(slot, b, 1, splits, view=view, log=True, feedback=True)
+                self._forward_rows(slot, b, 1, splits, view=view, log=True, feedback=True, layers=layers)
             for k, v in saved.items():
                 b[k].copy_(v)
             self._graphs[key] = graph

@@ -1,0 +1,136 @@
+"""Compute-only draft screens on the engine: layer-sparse / layer-subset drafts and the
+sparse-page draft crossover.
+
+Counterparts of the reference's vLLM compute screens
+(experiments/benchmark_layer_sparse_draft.py, benchmark_layer_subset_draft.py,
+benchmark_sparse_draft_crossover.py, benchmark_eagle3_draft.py): instead of out-of-tree vLLM
+backends, the drafts run on this package's engine.
+  * ``layer_draft_screen``: greedy drafts computed with a subset of the target's layers (the
+    first N, or a frozen pattern; skipped layers are identity) against the full model's greedy
+    continuation: accepted prefix and per-token draft time (CUDA graph per subset).
+  * ``sparse_page_crossover``: per-token cost of a draft step whose attention reads a page view
+    (64 sink + 512 recent + evenly spaced 64-token pages up to the visible fraction) against a
+    full-context step, over fractions and context lengths: where sparse drafting stops paying.
+The EAGLE drafter's screen is ``training.drafter_trainer.evaluate_drafter``.
+"""
+from __future__ import annotations
+
+import json
+from typing import Any, Sequence
+
+import torch
+
+from ..models.sparse_kv_draft import accepted_prefix_length, sink_recent_topk_indices
+
+
+def _events():
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+@torch.inference_mode()
+def layer_draft_screen(engine, prompt: Sequence[int], patterns: dict[str, Sequence[int]], *,
+                       draft_tokens: int = 8) -> list[dict[str, Any]]:
+    dev = engine.device
+    T = len(prompt)
+    slot = engine.new_slot(T + draft_tokens + 64)
+    ids = torch.tensor(list(prompt), dtype=torch.int32, device=dev)
+    h = engine.prefill(ids, slot)
+    last = h[T - 1:T].clone()
+
+    def run(layers):
+        engine.first_token(last, position=T, max_new=draft_tokens)
+        engine.decode(slot, 1, max_new=draft_tokens, layers=layers)  # capture / warm
+        engine.first_token(last, position=T, max_new=draft_tokens)
+        a, b = _events()
+        a.record()
+        engine.decode(slot, draft_tokens - 1, max_new=draft_tokens, layers=layers)
+        b.record()
+        b.synchronize()
+        return engine.generated_tokens(draft_tokens).tolist(), a.elapsed_time(b) / max(1, draft_tokens - 1)
+
+    ref, full_ms = run(None)
+    out = [{"pattern": "full", "layers": engine.cfg.n_layers, "accepted_prefix": draft_tokens - 1,
+            "ms_per_token": full_ms, "relative_cost": 1.0}]
+    for name, layers in patterns.items():
+        toks, ms = run(tuple(int(x) for x in layers))
+        out.append({"pattern": name, "layers": len(layers),
+                    "accepted_prefix": accepted_prefix_length(toks[1:], ref[1:]), "ms_per_token": ms,
+                    "relative_cost": ms / full_ms})
+    return out
+
+
+def page_view(T: int, fraction: float, *, page: int = 64, sink: int = 64, recent: int = 512) -> torch.Tensor:
+    """Sorted visible token indices of a sink + recent + evenly spaced pages view."""
+    budget = max(sink + recent, int(T * fraction))
+    return sink_recent_topk_indices(T, None, sink=sink, recent=recent, chunk=page, budget=budget)
+
+
+@torch.inference_mode()
+def sparse_page_crossover(engine, context_lengths: Sequence[int], fractions: Sequence[float], *,
+                          reps: int = 20, seed: int = 0) -> list[dict[str, Any]]:
+    dev = engine.device
+    g = torch.Generator().manual_seed(seed)
+    rows = []
+    for T in context_lengths:
+        slot = engine.new_slot(T + 64)
+        ids = torch.randint(0, engine.cfg.vocab, (T,), generator=g, dtype=torch.int32).to(dev)
+        engine.prefill(ids, slot)
+        tok = torch.tensor([1], dtype=torch.int32)
+        view = torch.zeros(slot.capacity, dtype=torch.int32, device=dev)
+
+        def step(n_vis=None):
+            if n_vis is None:
+                engine.verify(slot, tok, position=T)
+            else:
+                engine.verify(slot, tok, position=T, slot_start=T, view=view, n_visible=n_vis)
+
+        def timed(fn):
+            for _ in range(3):
+                fn()
+            a, b = _events()
+            a.record()
+            for _ in range(reps):
+                fn()
+            b.record()
+            b.synchronize()
+            return a.elapsed_time(b) / reps
+
+        full_ms = timed(step)
+        for f in fractions:
+            idx = page_view(T, f)
+            view[: idx.numel()].copy_(idx.to(torch.int32))
+            view[idx.numel()] = T  # the draft row's own slot follows the visible keys
+            ms = timed(lambda: step(idx.numel()))
+            rows.append({"context_tokens": T, "visible_fraction": idx.numel() / T, "requested_fraction": f,
+                         "draft_step_ms": ms, "full_step_ms": full_ms, "speedup": full_ms / ms})
+    return rows
+
+
+def main(argv=None) -> None:
+    import argparse
+
+    from ..config import get_model_config
+    from ..models.engine import B200Engine
+
+    p = argparse.ArgumentParser()
+    p.add_argument("--model", default="llama3-8b")
+    p.add_argument("--prompt-tokens", type=int, default=4096)
+    p.add_argument("--draft-tokens", type=int, default=8)
+    p.add_argument("--contexts", default="8192,32768")
+    p.add_argument("--fractions", default="0.05,0.1,0.2,0.5")
+    a = p.parse_args(argv)
+    cfg = get_model_config(a.model)
+    ctxs = [int(x) for x in a.contexts.split(",")]
+    eng = B200Engine.random(cfg, seed=0, device="cuda", max_positions=max(ctxs + [a.prompt_tokens]) + 256)
+    L = cfg.n_layers
+    g = torch.Generator().manual_seed(1)
+    prompt = torch.randint(0, cfg.vocab, (a.prompt_tokens,), generator=g).tolist()
+    patterns = {f"first_{n}": list(range(n)) for n in (L // 4, L // 2, 3 * L // 4)}
+    patterns["every_other"] = list(range(0, L, 2))
+    print(json.dumps({"layer_draft": layer_draft_screen(eng, prompt, patterns, draft_tokens=a.draft_tokens),
+                      "sparse_page_crossover": sparse_page_crossover(
+                          eng, ctxs, [float(x) for x in a.fractions.split(",")])}, indent=1))
+
+
+if __name__ == "__main__":
+    main()

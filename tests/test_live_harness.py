@@ -204,3 +204,45 @@ def test_launcher_process_control_and_fail_closed(tmp_path):
     man = launcher.execute(job, tmp_path / "run", gate=lambda: {"status": "failed"})
     assert man["status"] == "failed" and "gate" in man["error"]
     assert (tmp_path / "run" / "run_manifest.json").exists()
+
+
+def test_scheduling_benchmark_shares_one_prefill(tmp_path):
+    from sparsecache_b200.evaluation.priorities import priority_for_mode
+    from sparsecache_b200.serving.live import validate
+
+    px, _ = _stack(tmp_path)
+    reqs = [{"model": "toy", "prompt": list(range(3 + i, 600 + i)), "max_tokens": 6, "temperature": 0}
+            for i in range(2)]
+    pri = {s: {i: priority_for_mode(s, request_id=str(i), question="q", documents=[{"text": "a", "supporting": True}],
+                                    spans=[{"start_token": 0, "end_token": 256}], total_chunks=3, chunk_tokens=256,
+                                    protected_prefix_chunks=1, protected_suffix_chunks=1, seed=0)
+               for i in range(2)} for s in validate.SCHEDULES}
+
+    async def go():
+        async with httpx.AsyncClient(transport=httpx.ASGITransport(app=px.app), base_url="http://proxy") as c:
+            return await validate.run_scheduling_benchmark(c, "/v1/completions", reqs, pri)
+
+    recs = asyncio.run(go())
+    assert len(recs) == 2 * 5 * 2
+    agg = validate.aggregate_scheduling(recs, expected_requests=2, bootstrap_samples=50)
+    assert agg["status"] == "passed", agg["gates"]
+    assert sum(r["prefill_reused"] is False for r in recs) == 2
+
+
+def test_latency_cell_validator():
+    from sparsecache_b200.serving.live.validate import validate_latency_cell
+
+    def row(i, order):
+        return {"dataset_index": i, "protocol": {"fixed_token_horizon": True, "paired_measurement": True,
+                                                 "require_exclusive_gpu": True, "initial_gpu_used_bytes": 0},
+                "schedules": {"uniform": {"full_target": {"timing_token_ids": [1, 2]},
+                                          "chains": {"inf": {"measurement_order": order, "timing_token_ids": [1, 2],
+                                                             "pipeline": {"response_ms": 50.0, "verify_ms": 10.0,
+                                                                          "final_decode_ms": 30.0}}}}}}
+
+    ok = validate_latency_cell([row(0, "full_target_then_pipeline"), row(1, "pipeline_then_full_target")],
+                               expected_count=2)
+    assert ok["passed"], ok["failures"]
+    bad = validate_latency_cell([row(0, "full_target_then_pipeline"), row(0, "full_target_then_pipeline"),
+                                 row(2, "full_target_then_pipeline")], expected_count=2, max_unattributed_ms=5.0)
+    assert not bad["passed"] and len(bad["failures"]) >= 3
