@@ -1,0 +1,163 @@
+"""Progressive P/D pipeline driver: full-target transfer vs draft-while-loading, paired per request.
+
+Parity with the reference's experiments/pd_progressive_kv_pipeline.py:
+  * ``auto_draft_tokens`` (:1363-1381): the draft horizon of a request is the
+    number of target decode steps that fit in the residual wire window (the
+    bytes still in flight after the first tranche, at the controlled link
+    rate, times a utilisation factor), capped by the configured horizon;
+  * ``run_full_target`` (:1066-1117): every tranche lands, then the target
+    decodes greedily from the full KV;
+  * ``run_chain`` (:1120-1243): the continuous draft-while-loading chain with
+    one final verifier (``serving.progressive.continuous_graft_chain``);
+  * ``evaluate_request`` / ``main`` (:1246-1699): rank documents by a schedule,
+    stage them into tranches (anchor = prefix + first ranked documents +
+    suffix), run both arms in alternating order on the same staged request,
+    check the greedy outputs are identical, and write JSONL rows with the
+    transfer, draft and verification breakdown.
+  * ``aggregate`` (experiments/aggregate_pd_progressive_kv_pipeline.py):
+    token equality, accepted drafts, TTFT/response distributions, paired gains.
+The transport is the pinned-host tranche stager with an optional paced link
+(``TrancheStager``); the prefill producer is this package's engine.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import statistics
+import time
+from pathlib import Path
+from typing import Any, Sequence
+
+import torch
+
+from ..serving.progressive import (Document, TrancheStager, continuous_graft_chain, ranked_document_indices,
+                                   stage_document_sets)
+
+
+def auto_draft_tokens(*, prompt_tokens: int, first_stage_tokens: int, bytes_per_token: float, transport_gbps: float,
+                      tpot_ms: float, max_draft_tokens: int, utilization: float = 1.0) -> tuple[int, float]:
+    """(draft horizon, residual wire ms) of one request."""
+    if tpot_ms <= 0 or not 0 < utilization <= 1 or transport_gbps <= 0:
+        raise ValueError("invalid auto-draft parameters")
+    residual_ms = (prompt_tokens - first_stage_tokens) * bytes_per_token * 8 / (transport_gbps * 1e6)
+    return max(1, min(max_draft_tokens, math.floor(residual_ms * utilization / tpot_ms))), residual_ms
+
+
+def run_full_target(engine, stager: TrancheStager, *, seed_token: int, prompt_tokens: int, max_new_tokens: int,
+                    clock=time.perf_counter) -> dict[str, Any]:
+    """Baseline arm: wait for every tranche, then greedy decode from the full KV."""
+    t0 = clock()
+    for i in range(len(stager.stages)):
+        stager.launch(i)
+    for i in range(len(stager.stages)):
+        stager.wait_on_compute_stream(i)
+    b = engine._decode_buffers(max_new_tokens)
+    b["ids"][:1].fill_(int(seed_token))
+    engine.ext.embedding(b["ids"][:1], engine.w.embed, b["h"][:1])
+    b["log"][0:1].fill_(int(seed_token))
+    b["gen"].fill_(1)
+    b["counter"].zero_()
+    engine.set_decode_state(position=prompt_tokens)
+    torch.cuda.current_stream(engine.device).synchronize()
+    ready = (clock() - t0) * 1e3
+    engine.decode(stager.slot, max_new_tokens - 1, max_new=max_new_tokens)
+    tokens = engine.generated_tokens(max_new_tokens).tolist()
+    torch.cuda.current_stream(engine.device).synchronize()
+    return {"tokens": tokens, "first_ready_ms": ready, "response_ms": (clock() - t0) * 1e3,
+            "transfer": stager.finish()}
+
+
+def aggregate(rows: Sequence[dict]) -> dict[str, Any]:
+    def col(arm, key):
+        return [r[arm][key] for r in rows if r.get(arm) and r[arm].get(key) is not None]
+
+    def stats(x):
+        if not x:
+            return None
+        x = sorted(x)
+        return {"mean": statistics.fmean(x), "p50": x[len(x) // 2], "p99": x[min(len(x) - 1, int(0.99 * len(x)))]}
+
+    gains = [r["full_target"]["response_ms"] - r["chain"]["response_ms"] for r in rows]
+    return {"requests": len(rows),
+            "token_equality_rate": statistics.fmean(r["tokens_equal"] for r in rows) if rows else None,
+            "accepted_draft_tokens": stats([r["chain"]["accepted"] for r in rows]),
+            "full_target_response_ms": stats(col("full_target", "response_ms")),
+            "chain_response_ms": stats(col("chain", "response_ms")),
+            "full_target_first_ready_ms": stats(col("full_target", "first_ready_ms")),
+            "chain_first_ready_ms": stats(col("chain", "first_ready_ms")),
+            "response_gain_ms": stats(gains)}
+
+
+def main(argv=None) -> None:
+    from ..config import get_model_config
+    from ..models.engine import B200Engine
+    from ..synthetic import make_requests
+
+    p = argparse.ArgumentParser()
+    p.add_argument("--model", default="llama3-8b")
+    p.add_argument("--workload", default="pd_long")
+    p.add_argument("--requests", type=int, default=8)
+    p.add_argument("--schedule", default="query")
+    p.add_argument("--stage-fractions", default="0.25,0.5,0.75,1.0")
+    p.add_argument("--max-new-tokens", type=int, default=32)
+    p.add_argument("--draft-tokens", type=int, default=7)
+    p.add_argument("--transport-gbps", type=float, default=100.0)
+    p.add_argument("--auto-draft-tpot-ms", type=float, default=None)
+    p.add_argument("--auto-draft-utilization", type=float, default=1.0)
+    p.add_argument("--output", type=Path, required=True)
+    a = p.parse_args(argv)
+    cfg = get_model_config(a.model)
+    eng = B200Engine.random(cfg, seed=0, device="cuda", max_positions=65536)
+    reqs = make_requests(a.workload, cfg)[: a.requests]
+    fractions = tuple(float(x) for x in a.stage_fractions.split(","))
+    bytes_per_token = cfg.n_layers * 2 * cfg.n_kv_heads * cfg.head_dim * 2
+    rows = []
+    with open(a.output, "w") as f:
+        f.write(json.dumps({"protocol": {**vars(a), "output": str(a.output), "fixed_token_horizon": True,
+                                         "paired_measurement": True}}) + "\n")
+        for i, r in enumerate(reqs):
+            T = r.prompt_tokens
+            docs = [Document(tuple(d), " ".join(map(str, d[:64]))) for d in r.documents]
+            ranking = ranked_document_indices(a.schedule, question=" ".join(map(str, r.suffix)), documents=docs,
+                                              random_seed=i)
+            sets = stage_document_sets(ranking, docs, fractions)
+            first = len(r.prefix) + len(r.suffix) + sum(len(docs[j].token_ids) for j in sets[0])
+            gamma, residual = (a.draft_tokens, None)
+            if a.auto_draft_tpot_ms is not None:
+                gamma, residual = auto_draft_tokens(prompt_tokens=T, first_stage_tokens=first,
+                                                    bytes_per_token=bytes_per_token,
+                                                    transport_gbps=a.transport_gbps, tpot_ms=a.auto_draft_tpot_ms,
+                                                    max_draft_tokens=a.draft_tokens,
+                                                    utilization=a.auto_draft_utilization)
+            # producer: prefill the whole prompt once; its slot is the tranches' source
+            src = eng.new_slot(T + a.max_new_tokens + 64)
+            ids = torch.tensor(r.prompt, dtype=torch.int32, device=eng.device)
+            h = eng.prefill(ids, src)
+            seed = int(eng.first_token(h[T - 1:T], position=T, max_new=1)["tok"][0].item())
+            host = src.data[:, :, :, :T].cpu().pin_memory()
+            arms = ("full_target", "chain") if i % 2 == 0 else ("chain", "full_target")
+            row: dict[str, Any] = {"request_index": i, "prompt_tokens": T, "draft_tokens": gamma,
+                                   "residual_wire_ms": residual, "measurement_order": "->".join(arms)}
+            for arm in arms:
+                dst = eng.new_slot(T + a.max_new_tokens + 64)
+                stager = TrancheStager(host, dst, prefix_tokens=len(r.prefix), documents=docs,
+                                       suffix_tokens=len(r.suffix), ranking=ranking, selected_sets=sets,
+                                       transport_gbps=a.transport_gbps)
+                if arm == "full_target":
+                    row[arm] = run_full_target(eng, stager, seed_token=seed, prompt_tokens=T,
+                                               max_new_tokens=a.max_new_tokens)
+                else:
+                    res = continuous_graft_chain(eng, stager, seed_token=seed, prompt_tokens=T,
+                                                 max_draft_tokens=gamma, max_new_tokens=a.max_new_tokens)
+                    row[arm] = {"tokens": list(res.token_ids), "first_ready_ms": res.first_token_ready_ms,
+                                "response_ms": res.response_ms, "accepted": res.accepted,
+                                "drafts": list(res.draft_tokens), "transfer": res.transfer}
+            row["tokens_equal"] = row["full_target"]["tokens"] == row["chain"]["tokens"]
+            rows.append(row)
+            f.write(json.dumps(row, default=str) + "\n")
+    print(json.dumps(aggregate(rows), indent=2))
+
+
+if __name__ == "__main__":
+    main()

@@ -140,3 +140,43 @@ def test_spans_from_prompt_markers():
     assert [d["text"] for d in docs] == ["one", "zero"]
     cov = priorities.coverage_curve([1, 0], [{"start_token": 0, "end_token": 4, "supporting": True}], 4)
     assert cov == [0.0, 1.0]
+
+
+def test_pack_audits_matrix_coverage_and_quality(tmp_path):
+    import hashlib
+
+    from sparsecache_b200.evaluation import audits
+
+    d = tmp_path / "hotpotqa"
+    d.mkdir()
+    (d / "requests.jsonl").write_text("".join(json.dumps({"prompt": [1] * 512}) + "\n" for _ in range(3)))
+    (d / "metadata.jsonl").write_text("".join(json.dumps({"request_index": i, "dataset": "hotpotqa",
+                                                          "answers": ["paris"]}) + "\n" for i in range(3)))
+    h = lambda p: hashlib.sha256(p.read_bytes()).hexdigest()  # noqa: E731
+    (d / "manifest.json").write_text(json.dumps({"dataset": "hotpotqa", "chunk_tokens": 256,
+                                                 "requests_sha256": h(d / "requests.jsonl"),
+                                                 "metadata_sha256": h(d / "metadata.jsonl")}))
+    assert audits.audit_pack(d, expected_dataset="hotpotqa")["rows"] == 3
+    m = audits.audit_dataset_matrix(tmp_path, ["hotpotqa", "musique"])
+    assert m["status"] == "failed" and "hotpotqa" in m["cells"] and m["failures"][0].startswith("musique")
+    cov = audits.priority_coverage([2, 0, 1], [{"start_token": 512, "end_token": 768, "supporting": True}], 256)
+    assert cov["0.5"] == 1.0
+    q = audits.quality_audit([{"request_index": 0, "token_ids": [1, 2]}],
+                             [{"request_index": 0, "dataset": "hotpotqa", "answers": ["Paris"]}],
+                             decode=lambda ids: "paris")
+    assert q["overall"] == 1.0
+
+
+def test_pd_pipeline_auto_draft_and_aggregate():
+    from sparsecache_b200.pipelines.pd import aggregate, auto_draft_tokens
+
+    g, wire = auto_draft_tokens(prompt_tokens=16384, first_stage_tokens=4096, bytes_per_token=131072,
+                                transport_gbps=100.0, tpot_ms=3.5, max_draft_tokens=7)
+    assert wire == pytest.approx(12288 * 131072 * 8 / 1e8) and g == 7
+    g, _ = auto_draft_tokens(prompt_tokens=1000, first_stage_tokens=990, bytes_per_token=131072,
+                             transport_gbps=100.0, tpot_ms=3.5, max_draft_tokens=7)
+    assert g == 1
+    rows = [{"tokens_equal": True, "full_target": {"response_ms": 100.0, "first_ready_ms": 40.0},
+             "chain": {"response_ms": 90.0, "first_ready_ms": 30.0, "accepted": 3}}]
+    agg = aggregate(rows)
+    assert agg["token_equality_rate"] == 1.0 and agg["response_gain_ms"]["mean"] == 10.0
