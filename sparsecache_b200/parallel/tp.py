@@ -286,6 +286,58 @@ class TPEngine:
         ext.gemv_argmax(h, eng.w.lm_head, eng.w.norm, cfg.rms_eps, b["pv"], b["pi"], b["counter"], b["tok"],
                         b["log"], b["gen"], eng.w.embed, h, pos, 4)
 
+    def decode_breakdown(self, slot: KVSlot, reps: int = 3) -> dict[str, float]:
+        """Per-op device time of one eager decode step (ms, summed over layers, mean of ``reps``).
+
+        CUDA events bracket each op of the step (qkv, attention, o + all-reduce
+        send, o reduce, gate/up, down + all-reduce send, down reduce, LM head);
+        every rank runs the same steps.  Events between kernels add small gaps,
+        so the total exceeds the graph-replayed TPOT a little.
+        """
+        eng, ext, cfg, lc = self.engine, self.ext, self.full_cfg, self.lcfg
+        splits = eng._decode_splits(slot.capacity)
+        names = ("qkv", "attention", "o_allreduce_send", "o_reduce", "gate_up", "down_allreduce_send", "down_reduce",
+                 "lm_head")
+        acc = {n: 0.0 for n in names}
+        orig_step = self._decode_step
+
+        for _ in range(reps):
+            marks: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
+
+            class _Timed:  # wraps the extension: every call between two events
+                def __getattr__(_s, name):
+                    fn = getattr(ext, name)
+                    label = {"gemv_qkv": "qkv", "attention_decode": "attention", "gemv_swiglu": "gate_up",
+                             "gemv_argmax": "lm_head"}.get(name)
+                    if name == "gemv_allreduce":
+                        label = "o_allreduce_send" if sum(m[0].startswith("o_a") for m in marks) <= \
+                            sum(m[0].startswith("down_a") for m in marks) else "down_allreduce_send"
+                    if name == "rs_reduce":
+                        label = "o_reduce" if sum(m[0] == "o_reduce" for m in marks) <= \
+                            sum(m[0] == "down_reduce" for m in marks) else "down_reduce"
+                    if label is None:
+                        return fn
+
+                    def call(*a, **k):
+                        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+                        e0.record()
+                        out = fn(*a, **k)
+                        e1.record()
+                        marks.append((label, e0, e1))
+                        return out
+
+                    return call
+
+            self.ext = _Timed()
+            try:
+                orig_step(slot, splits)
+            finally:
+                self.ext = ext
+            torch.cuda.synchronize()
+            for label, e0, e1 in marks:
+                acc[label] += e0.elapsed_time(e1) / reps
+        return acc
+
     def decode(self, slot: KVSlot, n_steps: int, *, use_graph: bool = True) -> None:
         """Greedy decode across the TP group; every rank runs the same steps."""
         eng = self.engine

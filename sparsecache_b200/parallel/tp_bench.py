@@ -78,6 +78,8 @@ def main() -> None:
     p.add_argument("--tokens", type=int, default=8192)
     p.add_argument("--new-tokens", type=int, default=32)
     p.add_argument("--iters", type=int, default=5)
+    p.add_argument("--breakdown", action="store_true", help="per-op decode step breakdown (eager, CUDA events)")
+    p.add_argument("--decode-only", action="store_true", help="skip the per-op prefill comparisons")
     args = p.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -109,7 +111,21 @@ def main() -> None:
         tpe.decode(slot, 2)  # capture + warm
         out["tpot_ms"] = device_time(lambda: tpe.decode(slot, 1), 16)
         tpe.check_status()
+        if args.breakdown:  # eager step with events around every op, max over ranks
+            bd = tpe.decode_breakdown(slot)
+            t = torch.tensor([bd[k] for k in sorted(bd)], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            out["decode_breakdown_ms"] = dict(zip(sorted(bd), t.tolist()))
+            tpe.check_status()
 
+        if args.decode_only:
+            dist.barrier()
+            eng.release_graphs()
+            if rank == 0:
+                print(json.dumps(out), flush=True)
+            dist.barrier()
+            tpe.close()
+            return
         # ---- per-op: AG -> QKV GEMM ----
         d = cfg.d_model
         lw = eng.w.layers[0]

@@ -118,7 +118,8 @@ def main(argv=None) -> None:
                                          "paired_measurement": True}}) + "\n")
         for i, r in enumerate(reqs):
             T = r.prompt_tokens
-            docs = [Document(tuple(d), " ".join(map(str, d[:64]))) for d in r.documents]
+            docs = [Document(tuple(d), " ".join(map(str, d[:64])), start=b, end=e)
+                    for d, (b, e) in zip(r.documents, r.document_ranges())]
             ranking = ranked_document_indices(a.schedule, question=" ".join(map(str, r.suffix)), documents=docs,
                                               random_seed=i)
             sets = stage_document_sets(ranking, docs, fractions)

@@ -93,7 +93,7 @@ def main() -> None:
                                         "weight_GBps": N * K * 2 / (t * 1e-6) / 1e9,
                                         "weight_frac_of_measured_hbm": N * K * 2 / (t * 1e-6) / 1e9 / HBM_GBS}
 
-    if "attn_decode" in only:
+    if "attn_decode" in only or "attn_decode_sweep" in only:
         H, Hkv = 32, 8
         for cap in (2048, 18000):
             kc = torch.randn(Hkv, cap, 128, device=dev).to(bf)
@@ -102,6 +102,10 @@ def main() -> None:
             pos = torch.tensor([cap - 16], device=dev, dtype=torch.int32)
             out = torch.empty(1, H * 128, device=dev, dtype=bf)
             S = int(ext.attention_decode_cluster(cap))
+            if "attn_decode_sweep" in only:  # cluster-size sweep
+                for s_try in (4, 8, 16):
+                    t_s = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), s_try, out))
+                    res[f"attn_decode_ctx{cap}_S{s_try}"] = {"us": t_s}
             t = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), S, out))
             kv_bytes = 2 * Hkv * (cap - 15) * 128 * 2
             gbs = kv_bytes / (t * 1e-6) / 1e9
