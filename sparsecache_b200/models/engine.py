@@ -185,7 +185,8 @@ class _Workspace:
 class _CountingExt:
     """Proxy over the extension that counts kernel launches issued from the host."""
 
-    _NOT_KERNELS = {"status", "num_sms", "gemv_argmax_grid", "attention_decode_cluster", "shared_empty",
+    _NOT_KERNELS = {"status", "num_sms", "gemv_argmax_grid", "attention_decode_cluster", "attention_decode_outer",
+                    "shared_empty",
                     "shared_open", "shared_close"}
     _MULTI = {"gemm_store", "gemm_residual"}
 
@@ -432,7 +433,11 @@ class B200Engine:
             raise ValueError(f"max_new_tokens above {self.MAX_DECODE_TOKENS}")
         cfg, ws, R = self.cfg, self.ws, self.MAX_ROWS
         grid = self.ext.gemv_argmax_grid(cfg.vocab)
+        if "dec_attn_cnt" not in ws.bufs:  # tickets of the cross-cluster merge: zero between launches
+            ws.bufs["dec_attn_cnt"] = torch.zeros(cfg.n_kv_heads, device=self.device, dtype=torch.int32)
         return {
+            "attn_ws": ws.get("dec_attn_ws", (cfg.n_kv_heads * 16 * 32 * 130,), torch.float32),
+            "attn_cnt": ws.bufs["dec_attn_cnt"],
             "h": ws.get("dec_h", (R, cfg.d_model), torch.bfloat16),
             "q": ws.get("dec_q", (R, cfg.q_size), torch.bfloat16),
             "attn": ws.get("dec_attn", (R, cfg.q_size), torch.bfloat16),
@@ -488,7 +493,8 @@ class B200Engine:
                          self.rope, cfg.n_heads, cfg.n_kv_heads, slot=pos[1:2])
             ext.attention_decode(b["q"][:M], slot.k(layer), slot.v(layer), pos[0:1], H, self.scale, splits,
                                  b["attn"][:M], page_table=view, page_shift=0,
-                                 n_virtual=pos[2:3] if view is not None else None)
+                                 n_virtual=pos[2:3] if view is not None else None, ws=b["attn_ws"],
+                                 counters=b["attn_cnt"])
             ext.gemv_residual(b["attn"][:M], lw.w_o, None, cfg.rms_eps, h, h)
             ext.gemv_swiglu(h, lw.w_gu, lw.ln2, cfg.rms_eps, b["act"][:M])
             ext.gemv_residual(b["act"][:M], lw.w_down, None, cfg.rms_eps, h, h)

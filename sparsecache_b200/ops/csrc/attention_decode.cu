@@ -34,6 +34,7 @@ constexpr int kSub = 64;      // keys per staged sub-chunk (double-buffered)
 constexpr int kMaxQV = 32;    // M * G
 constexpr int kMaxRows = 8;   // largest query block M
 constexpr int kRow = 256;     // bytes per K/V row (128 bf16)
+constexpr int kMaxOuter = 16; // clusters per kv head (second split level)
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
   const int sz = pred ? 16 : 0;
@@ -56,14 +57,16 @@ struct DecodeSmem {
 // decode shapes (QVT == M * G) carry no per-vector guards in the inner loops.
 template <int QVT>
 __global__ void __launch_bounds__(kThreads)
-    attention_decode_kernel(AttnDecodeArgs a, int chunk) {
+    attention_decode_kernel(AttnDecodeArgs a, int chunk, int outer) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   DecodeSmem& sm = *reinterpret_cast<DecodeSmem*>(smem_raw);
   cg::cluster_group cluster = cg::this_cluster();
 
   const int G = a.n_heads / a.n_kv_heads;
   const int QV = a.M * G;
-  const int split = blockIdx.x, S = gridDim.x;
+  const int S = gridDim.x / outer;          // CTAs of one cluster
+  const int split = blockIdx.x % S;         // rank within the cluster
+  const int cidx = blockIdx.x / S;          // cluster index of this kv head
   const int kvh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // *pos and the cache rows [0, *pos) were written at least two launches
@@ -76,7 +79,7 @@ __global__ void __launch_bounds__(kThreads)
   auto phys = [&](int v) -> int {
     return a.page_table != nullptr ? (a.page_table[v >> a.page_shift] << a.page_shift) + (v & page_mask) : v;
   };
-  const int k_begin = split * chunk;
+  const int k_begin = blockIdx.x * chunk;  // global split index over all clusters
   const int k_end = min(n_keys, k_begin + chunk);
   const float sl2 = a.scale * 1.4426950408889634f;
   const __nv_bfloat16* kb = a.k_cache + (size_t)kvh * a.cache_cap * 128;
@@ -266,11 +269,60 @@ __global__ void __launch_bounds__(kThreads)
         }
       }
     }
+    if (outer == 1) {
+      const int m = qv / G, gi = qv % G;
+      a.out[(size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + d] =
+          __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
+    } else {
+      float* part = a.ws + (((size_t)kvh * kMaxOuter + cidx) * kMaxQV + qv) * 130;
+      part[2 + d] = num;
+      if (d == 0) {
+        part[0] = gmax;
+        part[1] = den;
+      }
+    }
+  }
+  cluster.sync();
+  if (outer == 1) return;
+  // the last CTA of this kv head merges the clusters' partials in cluster order
+  __shared__ unsigned s_ticket;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_ticket = atomicAdd(a.counters + kvh, 1u);
+  __syncthreads();
+  if (s_ticket != (unsigned)(S * outer - 1)) return;
+  __threadfence();
+  for (int idx = tid; idx < QV * 128; idx += kThreads) {
+    const int qv = idx >> 7, d = idx & 127;
+    const float* base = a.ws + ((size_t)kvh * kMaxOuter * kMaxQV + qv) * 130;
+    float gmax = -INFINITY;
+    for (int c = 0; c < outer; ++c) gmax = fmaxf(gmax, __ldcg(base + (size_t)c * kMaxQV * 130));
+    float num = 0.f, den = 0.f;
+    if (gmax != -INFINITY) {
+      for (int c = 0; c < outer; ++c) {
+        const float* pc = base + (size_t)c * kMaxQV * 130;
+        const float mc = __ldcg(pc);
+        if (mc == -INFINITY) continue;
+        const float w = exp2f(mc - gmax);
+        num += w * __ldcg(pc + 2 + d);
+        den += w * __ldcg(pc + 1);
+      }
+    }
     const int m = qv / G, gi = qv % G;
     a.out[(size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + d] =
         __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
   }
-  cluster.sync();
+  if (tid == 0) a.counters[kvh] = 0u;
+}
+
+// Clusters per kv head: enough CTAs for about two per SM when the kv heads are
+// few (tensor parallelism) or the context long, at least 128 keys per CTA.
+int attention_decode_outer(int cache_cap, int n_kv_heads, int cluster, int num_sms) {
+  int r = (2 * num_sms + cluster * n_kv_heads / 2) / (cluster * n_kv_heads);
+  const int by_keys = cache_cap / (cluster * 128);
+  if (r > by_keys) r = by_keys;
+  if (r > kMaxOuter) r = kMaxOuter;
+  return r < 1 ? 1 : r;
 }
 
 int attention_decode_cluster(int cache_cap) {
@@ -284,10 +336,19 @@ cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
   if (a.M < 1 || a.M * G > kMaxQV) return cudaErrorInvalidValue;
   const int S = a.splits;
   if (S < 1 || S > 16) return cudaErrorInvalidValue;
-  // keys per CTA: the cache capacity (+ the largest row block) split evenly,
-  // rounded to 16 keys; independent of M so a row sees the same split
-  // boundaries (and the same rounding) in decode and in batched verification
-  int chunk = (a.cache_cap + kMaxRows + S - 1) / S;
+  int outer = 1;
+  if (a.ws != nullptr && a.counters != nullptr) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    outer = attention_decode_outer(a.cache_cap, a.n_kv_heads, S, sms);
+  }
+  // keys per CTA: the cache capacity (+ the largest row block) split evenly
+  // over all S * outer CTAs, rounded to 16 keys; independent of M so a row
+  // sees the same split boundaries (and the same rounding) in decode and in
+  // batched verification
+  const int total = S * outer;
+  int chunk = (a.cache_cap + kMaxRows + total - 1) / total;
   chunk = (chunk + 15) / 16 * 16;
   const int smem = (int)sizeof(DecodeSmem);
   const int qv = a.M * G;
@@ -306,7 +367,7 @@ cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
     }
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(S, a.n_kv_heads, 1);
+  cfg.gridDim = dim3(S * outer, a.n_kv_heads, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -319,7 +380,7 @@ cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
   attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kern, a, chunk);
+  return cudaLaunchKernelEx(&cfg, kern, a, chunk, outer);
 }
 
 }  // namespace sc

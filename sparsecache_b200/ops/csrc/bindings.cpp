@@ -546,7 +546,8 @@ void attention_prefill(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tens
 
 void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int64_t n_heads,
                       double scale, int64_t splits, Tensor out, c10::optional<Tensor> page_table,
-                      int64_t page_shift, c10::optional<Tensor> n_virtual) {
+                      int64_t page_shift, c10::optional<Tensor> n_virtual, c10::optional<Tensor> ws,
+                      c10::optional<Tensor> counters) {
   const c10::cuda::CUDAGuard guard(q.device());
   CHECK_BF16(q); CHECK_BF16(out); CHECK_I32(pos);
   TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(2) == 128 && k_cache.is_contiguous(), "k_cache");
@@ -570,6 +571,14 @@ void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int6
   if (n_virtual.has_value() && n_virtual->defined()) {
     CHECK_I32(*n_virtual);
     a.n_virtual = n_virtual->data_ptr<int>();
+  }
+  if (ws.has_value() && ws->defined()) {
+    TORCH_CHECK(counters.has_value() && counters->defined(), "counters required with ws");
+    CHECK_F32(*ws); CHECK_I32(*counters);
+    TORCH_CHECK(ws->numel() >= (int64_t)a.n_kv_heads * 16 * 32 * 130, "ws too small");
+    TORCH_CHECK(counters->numel() >= a.n_kv_heads, "one counter per kv head");
+    a.ws = ws->data_ptr<float>();
+    a.counters = reinterpret_cast<unsigned*>(counters->data_ptr<int>());
   }
   check_cuda(sc::attention_decode(a, cur_stream()), "attention_decode");
 }
@@ -893,7 +902,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_prefill", &attention_prefill);
   m.def("attention_decode", &attention_decode, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("pos"), py::arg("n_heads"), py::arg("scale"), py::arg("splits"), py::arg("out"),
-        py::arg("page_table") = py::none(), py::arg("page_shift") = 6, py::arg("n_virtual") = py::none());
+        py::arg("page_table") = py::none(), py::arg("page_shift") = 6, py::arg("n_virtual") = py::none(),
+        py::arg("ws") = py::none(), py::arg("counters") = py::none());
+  m.def("attention_decode_outer", [](int64_t cap, int64_t kvh, int64_t cluster, int64_t sms) {
+    return sc::attention_decode_outer((int)cap, (int)kvh, (int)cluster, (int)sms);
+  });
   m.def("attention_decode_cluster", [](int64_t cap) { return sc::attention_decode_cluster((int)cap); });
   m.def("rmsnorm", &rmsnorm);
   m.def("embedding", &embedding);

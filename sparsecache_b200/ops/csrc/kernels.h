@@ -181,12 +181,21 @@ struct AttnDecodeArgs {
   const int* n_virtual;
   int n_heads, n_kv_heads;
   float scale;
-  int splits;  // CTAs per kv head = thread-block cluster size (1..16)
+  int splits;  // CTAs per cluster = thread-block cluster size (1..16)
   __nv_bfloat16* out;  // [M, n_heads*128]
+  // Optional second split level for long contexts / few kv heads: R clusters
+  // per kv head, each merging its CTAs through DSMEM and leaving a partial
+  // (max, sum, numerator) in ws; the last CTA of the kv head (atomic ticket
+  // in counters[kvh], reset to zero by it) merges the R partials in cluster
+  // order.  R is chosen from the capacity and the head count only, so a row's
+  // result does not depend on M.
+  float* ws;           // [n_kv_heads][16][32][130] fp32 (null: one cluster per kv head)
+  unsigned* counters;  // [n_kv_heads], zero between launches
 };
 
 cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream);
 int attention_decode_cluster(int cache_cap);
+int attention_decode_outer(int cache_cap, int n_kv_heads, int cluster, int num_sms);
 
 // ------------------------------------------------------------ pointwise ----
 cudaError_t rmsnorm_bf16(const __nv_bfloat16* x, int ldx, const int* rows, const __nv_bfloat16* w,

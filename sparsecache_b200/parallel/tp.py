@@ -273,7 +273,7 @@ class TPEngine:
             ext.gemv_qkv(h, lw.w_qkv, lw.ln1, cfg.rms_eps, b["q"][:1], slot.k(layer), slot.v(layer), pos[0:1],
                          eng.rope, lc.n_heads, lc.n_kv_heads, slot=pos[1:2])
             ext.attention_decode(b["q"][:1], slot.k(layer), slot.v(layer), pos[0:1], lc.n_heads, eng.scale, splits,
-                                 b["attn"][:1])
+                                 b["attn"][:1], ws=b["attn_ws"], counters=b["attn_cnt"])
             ext.gemv_allreduce(b["attn"][:1], lw.w_o, None, cfg.rms_eps, self.ar_o_ptrs, fo, self.rank,
                                2 * layer + 1, step, mul, self.ar_counters[0:1])
             ext.rs_reduce(ar_o, self.flags[FLAG_AR_O], 2 * layer + 1, TIMEOUT_NS, self.status, h, h, None, None,

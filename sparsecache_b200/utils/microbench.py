@@ -106,11 +106,31 @@ def main() -> None:
                 for s_try in (4, 8, 16):
                     t_s = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), s_try, out))
                     res[f"attn_decode_ctx{cap}_S{s_try}"] = {"us": t_s}
-            t = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), S, out))
+            ws = torch.zeros(Hkv * 16 * 32 * 130, device=dev)
+            cnt = torch.zeros(Hkv, device=dev, dtype=torch.int32)
+            R = int(ext.attention_decode_outer(cap, Hkv, S, ext.num_sms()))
+            t = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), S, out, ws=ws,
+                                                    counters=cnt))
             kv_bytes = 2 * Hkv * (cap - 15) * 128 * 2
             gbs = kv_bytes / (t * 1e-6) / 1e9
             res[f"attn_decode_ctx{cap}"] = {"us": t, "GBps": gbs, "frac_of_measured_hbm": gbs / HBM_GBS,
-                                            "cluster": S, "l2_resident": kv_bytes < 126e6}
+                                            "cluster": S, "clusters_per_kv_head": R,
+                                            "l2_resident": kv_bytes < 126e6}
+
+    if "attn_decode_tp" in only:
+        # one kv head per GPU (70B at TP8), 16k context: one cluster vs several clusters per kv head
+        H, Hkv, cap = 8, 1, 16384
+        kc = torch.randn(Hkv, cap, 128, device=dev).to(bf)
+        vc = torch.randn(Hkv, cap, 128, device=dev).to(bf)
+        q = torch.randn(1, H * 128, device=dev).to(bf)
+        pos = torch.tensor([cap - 16], device=dev, dtype=torch.int32)
+        out = torch.empty(1, H * 128, device=dev, dtype=bf)
+        ws = torch.zeros(Hkv * 16 * 32 * 130, device=dev)
+        cnt = torch.zeros(Hkv, device=dev, dtype=torch.int32)
+        kv_bytes = 2 * Hkv * (cap - 15) * 128 * 2
+        for name, kw in (("one_cluster", {}), ("two_level", {"ws": ws, "counters": cnt})):
+            t = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), 16, out, **kw))
+            res[f"attn_decode_tp8_70b_ctx{cap}_{name}"] = {"us": t, "GBps": kv_bytes / (t * 1e-6) / 1e9}
 
     if "attn_prefill" in only:
         H, Hkv = 32, 8

@@ -203,6 +203,34 @@ def test_attention_decode(cuda_device, M):
         torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("M", [1, 4])
+@pytest.mark.parametrize("hkv,cap", [(1, 16384), (2, 6000), (8, 18000)])
+def test_attention_decode_two_level_split(cuda_device, M, hkv, cap):
+    """Several clusters per kv head (few kv heads / long contexts): the ticketed
+    cross-cluster merge equals the reference, twice in a row (the tickets reset)."""
+    G = 8 if hkv == 1 else 4
+    H = hkv * G
+    pos0 = cap - 40
+    g = torch.Generator(device="cpu").manual_seed(cap + M)
+    kc = torch.randn(hkv, cap, 128, generator=g).to(cuda_device, torch.bfloat16)
+    vc = torch.randn(hkv, cap, 128, generator=g).to(cuda_device, torch.bfloat16)
+    q = torch.randn(M, H * 128, generator=g).to(cuda_device, torch.bfloat16)
+    pos = torch.tensor([pos0], device=cuda_device, dtype=torch.int32)
+    n = pos0 + M
+    ref = _attn_reference(q, kc[:, :n], vc[:, :n], pos0 + torch.arange(M, device=cuda_device),
+                          torch.arange(n, device=cuda_device), H)
+    ws = torch.zeros(hkv * 16 * 32 * 130, device=cuda_device)
+    cnt = torch.zeros(hkv, device=cuda_device, dtype=torch.int32)
+    outer = _ext().attention_decode_outer(cap, hkv, 16, _ext().num_sms())
+    assert outer > 1
+    for _ in range(2):
+        out = torch.empty(M, H * 128, device=cuda_device, dtype=torch.bfloat16)
+        _ext().attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), 16, out, ws=ws, counters=cnt)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+        assert int(cnt.sum()) == 0
+
+
 def _rms_ref(x, w, eps):
     xf = x.float()
     r = torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps)
