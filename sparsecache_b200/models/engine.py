@@ -434,7 +434,7 @@ class B200Engine:
         cfg, ws, R = self.cfg, self.ws, self.MAX_ROWS
         grid = self.ext.gemv_argmax_grid(cfg.vocab)
         if "dec_attn_cnt" not in ws.bufs:  # tickets of the cross-cluster merge: zero between launches
-            ws.bufs["dec_attn_cnt"] = torch.zeros(cfg.n_kv_heads, device=self.device, dtype=torch.int32)
+            ws.bufs["dec_attn_cnt"] = torch.zeros(cfg.n_kv_heads * 8, device=self.device, dtype=torch.int32)
         return {
             "attn_ws": ws.get("dec_attn_ws", (cfg.n_kv_heads * 16 * 32 * 130,), torch.float32),
             "attn_cnt": ws.bufs["dec_attn_cnt"],

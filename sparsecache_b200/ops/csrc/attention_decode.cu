@@ -1,20 +1,19 @@
 // Split-K decode / verify attention over a paged layer cache, merged through
-// distributed shared memory inside a thread-block cluster.
+// distributed shared memory inside a thread-block cluster (and, for few kv
+// heads or long contexts, across several clusters per kv head).
 //
 // The query block is M <= 8 consecutive new tokens (M = 1 for greedy decode,
 // M = gamma + 1 for the batched speculative verifier) at positions
 // *pos .. *pos + M - 1; row m sees keys [0, *pos + m].  The position lives in
 // device memory so a captured CUDA graph replays the same launch every step.
 //
-// Grid (S, n_kv_heads), cluster (S, 1, 1): the S CTAs of a cluster split the
-// keys of one kv head.  Each CTA stages 128-key K/V sub-chunks into shared
-// memory with cp.async (64 KB in flight per CTA), scores them for all
-// G = H/H_kv query heads and all M rows at once (GQA packing: K/V are read
-// once per kv head), keeps an online softmax per query vector, and leaves its
-// partial (max, sum, o[128]) in its own shared memory.  After a cluster
-// barrier every CTA merges a slice of the outputs by reading its peers'
-// partials over DSMEM; a second barrier keeps the partials alive until all
-// peers are done.  No global scratch, no atomics, one launch.
+// Grid (S * R, n_kv_heads, ceil(M * G / 4)), cluster (S, 1, 1): the S CTAs of
+// a cluster split a key range of one kv head; R clusters per kv head split
+// the keys further.  K/V rows are read once per kv head for the 4 query
+// vectors of a z-block (GQA packing) straight into registers; each CTA leaves
+// its partial (max, sum, o[128]) in shared memory, the cluster merges them
+// over DSMEM, and with R > 1 the last CTA of the kv head merges the clusters'
+// partials from a small global workspace (atomic ticket, reset by that CTA).
 //
 // Replaces the reference's per-token HF DynamicCache concatenation + SDPA
 // (modeling.py:383-417; progressive_kv_feasibility.py:561-613, 616-682).
@@ -30,228 +29,234 @@ namespace sc {
 namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kSub = 64;      // keys per staged sub-chunk (double-buffered)
+constexpr int kSub = 64;      // minimum keys per CTA for 16-CTA clusters
 constexpr int kMaxQV = 32;    // M * G
 constexpr int kMaxRows = 8;   // largest query block M
-constexpr int kRow = 256;     // bytes per K/V row (128 bf16)
 constexpr int kMaxOuter = 16; // clusters per kv head (second split level)
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
-  const int sz = pred ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(sz)
-               : "memory");
-}
 }  // namespace
 
-struct DecodeSmem {
-  __nv_bfloat16 k[2][kSub * 128];  // double-buffered sub-chunks
-  __nv_bfloat16 v[2][kSub * 128];
-  float s[kMaxQV][kSub];
-  float o[kMaxQV][128];  // partial output of this CTA (unnormalised)
-  float m[kMaxQV];       // running max (log2 domain)
-  float l[kMaxQV];       // running sum
-  float corr[kMaxQV];
+// ---------------------------------------------------------------------------
+// Register-resident decode attention: no shared-memory staging and no block
+// barrier inside the key loop.  Grid (S * R, n_kv_heads, ceil(QV / 4)):
+// z-block z handles query vectors 4z .. 4z + 3 (a query vector = one row m and
+// one query head of the kv head's group), so each vector's arithmetic is the
+// same whatever M is (decode M = 1 and batched verification M <= 8 give
+// bit-identical rows).  In a CTA, lane group g (8 lanes, 16 dims each) of warp
+// w takes keys base + g and base + 4 + g of base = k_begin + 8w, + 64, ...;
+// the next pair's K/V rows are loaded into registers while the current pair
+// is scored, so the loop is one load latency per 64 keys.  Per vector, the
+// lane group keeps an online softmax (max, sum, 16-dim accumulator); the 4
+// groups of a warp merge through shuffles, the 8 warps through shared memory,
+// and the CTAs of the cluster through DSMEM.
+constexpr int kRQ = 4;  // query vectors per z-block
+
+struct RegSmem {
+  float wo[kWarps][kRQ][128];  // per-warp partial accumulators
+  float wm[kWarps][kRQ], wl[kWarps][kRQ];
+  float o[kRQ][128];           // this CTA's partial (DSMEM-visible)
+  float m[kRQ], l[kRQ];
 };
 
-// QVT is the compile-time query-vector count (M * G rounded up); the exact
-// decode shapes (QVT == M * G) carry no per-vector guards in the inner loops.
-template <int QVT>
-__global__ void __launch_bounds__(kThreads)
-    attention_decode_kernel(AttnDecodeArgs a, int chunk, int outer) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  DecodeSmem& sm = *reinterpret_cast<DecodeSmem*>(smem_raw);
-  cg::cluster_group cluster = cg::this_cluster();
+__device__ __forceinline__ void reg_load16(const __nv_bfloat16* p, uint4 (&u)[2]) {
+  u[0] = __ldg(reinterpret_cast<const uint4*>(p));
+  u[1] = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+}
 
+__device__ __forceinline__ void reg_unpack16(const uint4 (&u)[2], float (&x)[16]) {
+  const unsigned w[8] = {u[0].x, u[0].y, u[0].z, u[0].w, u[1].x, u[1].y, u[1].z, u[1].w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float2 f = unpack_bf16x2(w[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+    attention_decode_reg_kernel(AttnDecodeArgs a, int chunk, int outer) {
+  __shared__ RegSmem sm;
+  cg::cluster_group cluster = cg::this_cluster();
   const int G = a.n_heads / a.n_kv_heads;
   const int QV = a.M * G;
-  const int S = gridDim.x / outer;          // CTAs of one cluster
-  const int split = blockIdx.x % S;         // rank within the cluster
-  const int cidx = blockIdx.x / S;          // cluster index of this kv head
+  const int S = gridDim.x / outer;
+  const int split = blockIdx.x % S;
+  const int cidx = blockIdx.x / S;
   const int kvh = blockIdx.y;
+  const int qv0 = blockIdx.z * kRQ;
+  const int nq = min(kRQ, QV - qv0);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // *pos and the cache rows [0, *pos) were written at least two launches
-  // back (the LM-head kernel of the previous step and earlier QKV kernels),
-  // so they are read before the programmatic wait; q and the M new rows come
-  // from the QKV kernel right before this one and are read after it.
-  const int n_keys = a.n_virtual != nullptr ? *a.n_virtual : *a.pos + a.M;
-  const int pos0 = n_keys - a.M;  // virtual index of query row 0
-  const int page_mask = (1 << a.page_shift) - 1;
-  auto phys = [&](int v) -> int {
-    return a.page_table != nullptr ? (a.page_table[v >> a.page_shift] << a.page_shift) + (v & page_mask) : v;
-  };
-  const int k_begin = blockIdx.x * chunk;  // global split index over all clusters
-  const int k_end = min(n_keys, k_begin + chunk);
+  const int sub = lane & 7, grp = lane >> 3;
   const float sl2 = a.scale * 1.4426950408889634f;
-  const __nv_bfloat16* kb = a.k_cache + (size_t)kvh * a.cache_cap * 128;
-  const __nv_bfloat16* vb = a.v_cache + (size_t)kvh * a.cache_cap * 128;
-  const uint32_t sk0 = smem_u32(sm.k[0]), sv0 = smem_u32(sm.v[0]);
-  constexpr uint32_t kBufBytes = kSub * kRow;
-  // stage rows [base, base + nk) whose key index lies in [lo, hi) into buffer
-  // buf; rows past nk are zero-filled when zero_tail is set
-  auto stage = [&](int buf, int base, int nk, int lo, int hi, bool zero_tail) {
-    const uint32_t sk = sk0 + buf * kBufBytes, sv = sv0 + buf * kBufBytes;
-    for (int i = tid; i < kSub * 16; i += kThreads) {
-      const int r = i >> 4, c = i & 15;
-      const int key = base + r;
-      const bool in = r < nk;
-      if (in ? (key < lo || key >= hi) : !zero_tail) continue;
-      const size_t off = (size_t)(in ? phys(key) : 0) * 128 + c * 8;
-      cp_async16(sk + r * kRow + c * 16, kb + off, in);
-      cp_async16(sv + r * kRow + c * 16, vb + off, in);
-    }
-  };
-  if (k_begin < k_end) stage(0, k_begin, min(kSub, k_end - k_begin), 0, pos0, true);
-  for (int i = tid; i < QV * 128; i += kThreads) sm.o[i / 128][i % 128] = 0.f;
-  if (tid < QV) sm.m[tid] = -INFINITY, sm.l[tid] = 0.f;
-  pdl_wait();
+  const __nv_bfloat16* kb = a.k_cache + (size_t)kvh * a.cache_cap * 128 + sub * 16;
+  const __nv_bfloat16* vb = a.v_cache + (size_t)kvh * a.cache_cap * 128 + sub * 16;
+  const int page_mask = (1 << a.page_shift) - 1;
+  pdl_wait();  // q and the new rows come from the QKV kernel right before
   pdl_launch_dependents();
+  const int n_keys = a.n_virtual != nullptr ? *a.n_virtual : *a.pos + a.M;
+  const int pos0 = n_keys - a.M;
+  const int k_begin = blockIdx.x * chunk;
+  const int k_end = min(n_keys, k_begin + chunk);
+  auto row_off = [&](int v) -> size_t {
+    const int p = a.page_table != nullptr ? (a.page_table[v >> a.page_shift] << a.page_shift) + (v & page_mask) : v;
+    return (size_t)p * 128;
+  };
 
-  // Scores use LPK lanes per key (LPK = 8 for small query blocks: 4 keys per
-  // warp step and a 3-level shuffle reduction); lane owns DPL dims of every
-  // query vector in registers.
-  constexpr int LPK = QVT <= 8 ? 8 : 32;
-  constexpr int DPL = 128 / LPK;
-  const int sub = lane % LPK;        // dim slice
-  const int kgrp = lane / LPK;       // key slot within the warp step
-  float q[QVT][DPL];
+  float q[kRQ][16];
+  int last[kRQ];  // last visible key of each vector (its row's position)
 #pragma unroll
-  for (int qv = 0; qv < QVT; ++qv) {
-    if (qv < QV) {
-      const int m = qv / G, gi = qv % G;
-      const __nv_bfloat16* qp = a.q + (size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + DPL * sub;
+  for (int i = 0; i < kRQ; ++i) {
+    const int qv = qv0 + (i < nq ? i : 0);
+    const int m = qv / G, gi = qv % G;
+    uint4 u[2];
+    reg_load16(a.q + (size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + sub * 16, u);
+    reg_unpack16(u, q[i]);
 #pragma unroll
-      for (int c = 0; c < DPL / 4; ++c) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(qp + 4 * c);
-        const float2 f0 = unpack_bf16x2(raw.x), f1 = unpack_bf16x2(raw.y);
-        q[qv][4 * c] = f0.x; q[qv][4 * c + 1] = f0.y; q[qv][4 * c + 2] = f1.x; q[qv][4 * c + 3] = f1.y;
+    for (int e = 0; e < 16; ++e) q[i][e] *= sl2;
+    last[i] = i < nq ? pos0 + m : -1;
+  }
+  float mx[kRQ], ls[kRQ], acc[kRQ][16];
+#pragma unroll
+  for (int i = 0; i < kRQ; ++i) {
+    mx[i] = -INFINITY;
+    ls[i] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) acc[i][e] = 0.f;
+  }
+
+  // key loop: warp-uniform trip count (the 8-lane shuffles need all 32 lanes)
+  uint4 ck0[2], cv0[2], ck1[2], cv1[2], nk0[2], nv0[2], nk1[2], nv1[2];
+  int base = k_begin + warp * 8;
+  auto fetch = [&](int b, uint4 (&k0)[2], uint4 (&v0)[2], uint4 (&k1)[2], uint4 (&v1)[2]) {
+    const int j0 = b + grp, j1 = j0 + 4;
+    const size_t o0 = row_off(j0 < k_end ? j0 : b), o1 = row_off(j1 < k_end ? j1 : b);
+    reg_load16(kb + o0, k0);
+    reg_load16(vb + o0, v0);
+    reg_load16(kb + o1, k1);
+    reg_load16(vb + o1, v1);
+  };
+  if (base < k_end) fetch(base, ck0, cv0, ck1, cv1);
+  for (; base < k_end; base += kWarps * 8) {
+    if (base + kWarps * 8 < k_end) fetch(base + kWarps * 8, nk0, nv0, nk1, nv1);
+    const int j0 = base + grp, j1 = j0 + 4;
+    float s0[kRQ], s1[kRQ];
+    {
+      float kf0[16], kf1[16];
+      reg_unpack16(ck0, kf0);
+      reg_unpack16(ck1, kf1);
+#pragma unroll
+      for (int i = 0; i < kRQ; ++i) {
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          a0 = fmaf(q[i][e], kf0[e], a0);
+          a1 = fmaf(q[i][e], kf1[e], a1);
+        }
+        s0[i] = a0;
+        s1[i] = a1;
       }
+    }
+#pragma unroll
+    for (int i = 0; i < kRQ; ++i) {
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) {
+        s0[i] += __shfl_xor_sync(0xffffffffu, s0[i], o);
+        s1[i] += __shfl_xor_sync(0xffffffffu, s1[i], o);
+      }
+      if (j0 >= k_end || j0 > last[i]) s0[i] = -INFINITY;
+      if (j1 >= k_end || j1 > last[i]) s1[i] = -INFINITY;
+    }
+    // online softmax: the (corr, p0, p1) of every vector, then one pass over the dims
+    float corr[kRQ], p0[kRQ], p1[kRQ];
+#pragma unroll
+    for (int i = 0; i < kRQ; ++i) {
+      const float mn = fmaxf(mx[i], fmaxf(s0[i], s1[i]));
+      if (mn == -INFINITY) {  // nothing visible yet for this vector
+        corr[i] = 1.f, p0[i] = 0.f, p1[i] = 0.f;
+      } else {
+        corr[i] = exp2f(mx[i] - mn);
+        p0[i] = exp2f(s0[i] - mn);
+        p1[i] = exp2f(s1[i] - mn);
+        mx[i] = mn;
+      }
+      ls[i] = ls[i] * corr[i] + p0[i] + p1[i];
+    }
+    {
+      const unsigned w0[8] = {cv0[0].x, cv0[0].y, cv0[0].z, cv0[0].w, cv0[1].x, cv0[1].y, cv0[1].z, cv0[1].w};
+      const unsigned w1[8] = {cv1[0].x, cv1[0].y, cv1[0].z, cv1[0].w, cv1[1].x, cv1[1].y, cv1[1].z, cv1[1].w};
+#pragma unroll
+      for (int h = 0; h < 8; ++h) {
+        const float2 va = unpack_bf16x2(w0[h]), vb = unpack_bf16x2(w1[h]);
+#pragma unroll
+        for (int i = 0; i < kRQ; ++i) {
+          acc[i][2 * h] = fmaf(acc[i][2 * h], corr[i], fmaf(p0[i], va.x, p1[i] * vb.x));
+          acc[i][2 * h + 1] = fmaf(acc[i][2 * h + 1], corr[i], fmaf(p0[i], va.y, p1[i] * vb.y));
+        }
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      ck0[c] = nk0[c]; cv0[c] = nv0[c]; ck1[c] = nk1[c]; cv1[c] = nv1[c];
     }
   }
-  int it = 0;
-  for (int base = k_begin; base < k_end; base += kSub, ++it) {
-    const int nk = min(kSub, k_end - base);
-    const int buf = it & 1;
-    if (it == 0) {
-      stage(0, base, nk, pos0, n_keys, false);  // the new rows, now visible
-      asm volatile("cp.async.commit_group;" ::: "memory");
-    }
-    // prefetch the next sub-chunk into the other buffer while this one runs
-    const int nbase = base + kSub;
-    if (nbase < k_end) stage(buf ^ 1, nbase, min(kSub, k_end - nbase), 0, n_keys, true);
-    asm volatile("cp.async.commit_group;\ncp.async.wait_group 1;" ::: "memory");
-    __syncthreads();
 
-    // scores: each warp step covers 32/LPK keys; LPK lanes split the dims
-    constexpr int KPW = 32 / LPK;
-    for (int j0 = warp * KPW; j0 < nk; j0 += kWarps * KPW) {
-      const int j = j0 + kgrp;
-      const bool valid = j < nk;
-      float kf[DPL];
-      {
-        const __nv_bfloat16* kr = sm.k[buf] + (valid ? j : 0) * 128 + DPL * sub;
+  // merge the 4 lane groups of the warp (lanes with the same dims: xor 8, 16)
 #pragma unroll
-        for (int c = 0; c < DPL / 4; ++c) {
-          const uint2 raw = *reinterpret_cast<const uint2*>(kr + 4 * c);
-          const float2 f0 = unpack_bf16x2(raw.x), f1 = unpack_bf16x2(raw.y);
-          kf[4 * c] = f0.x; kf[4 * c + 1] = f0.y; kf[4 * c + 2] = f1.x; kf[4 * c + 3] = f1.y;
-        }
-      }
-      const int key = base + j;
+  for (int i = 0; i < kRQ; ++i) {
+    float wm = mx[i];
+    wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, 8));
+    wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, 16));
+    const float w = (mx[i] == -INFINITY) ? 0.f : exp2f(mx[i] - wm);
+    float l = ls[i] * w;
+    l += __shfl_xor_sync(0xffffffffu, l, 8);
+    l += __shfl_xor_sync(0xffffffffu, l, 16);
 #pragma unroll
-      for (int qv = 0; qv < QVT; ++qv) {
-        if (qv < QV) {
-          float d = 0.f;
+    for (int e = 0; e < 16; ++e) {
+      float x = acc[i][e] * w;
+      x += __shfl_xor_sync(0xffffffffu, x, 8);
+      x += __shfl_xor_sync(0xffffffffu, x, 16);
+      if (grp == 0) sm.wo[warp][i][sub * 16 + e] = x;
+    }
+    if (lane == 0) {
+      sm.wm[warp][i] = wm;
+      sm.wl[warp][i] = l;
+    }
+  }
+  __syncthreads();
+  // merge the 8 warps (fixed order) into this CTA's partial
+  for (int idx = tid; idx < kRQ * 128; idx += kThreads) {
+    const int i = idx >> 7, d = idx & 127;
+    float gm = -INFINITY;
 #pragma unroll
-          for (int e = 0; e < DPL; ++e) d = fmaf(q[qv][e], kf[e], d);
+    for (int w = 0; w < kWarps; ++w) gm = fmaxf(gm, sm.wm[w][i]);
+    float o = 0.f, l = 0.f;
+    if (gm != -INFINITY) {
 #pragma unroll
-          for (int o = LPK / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-          if (valid && sub == (qv % LPK)) sm.s[qv][j] = (key <= pos0 + qv / G) ? d * sl2 : -INFINITY;
-        }
+      for (int w = 0; w < kWarps; ++w) {
+        const float c = sm.wm[w][i] == -INFINITY ? 0.f : exp2f(sm.wm[w][i] - gm);
+        o += sm.wo[w][i][d] * c;
+        l += sm.wl[w][i] * c;
       }
     }
-    __syncthreads();
-
-    // online softmax update, one warp per query vector
-    for (int qv = warp; qv < QV; qv += kWarps) {
-      float mx = -INFINITY;
-      for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sm.s[qv][j]);
-      mx = warp_max(mx);
-      const float m_old = sm.m[qv];
-      const float m_new = fmaxf(m_old, mx);
-      const float base_m = (m_new == -INFINITY) ? 0.f : m_new;
-      float sum = 0.f;
-      for (int j = lane; j < nk; j += 32) {
-        const float e = exp2f(sm.s[qv][j] - base_m);
-        sm.s[qv][j] = e;
-        sum += e;
-      }
-      sum = warp_sum(sum);
-      if (lane == 0) {
-        const float c = exp2f(m_old - base_m);
-        sm.corr[qv] = c;
-        sm.l[qv] = sm.l[qv] * c + sum;
-        sm.m[qv] = m_new;
-      }
+    sm.o[i][d] = o;
+    if (d == 0) {
+      sm.m[i] = gm;
+      sm.l[i] = l;
     }
-    __syncthreads();
-
-    // o[qv][d] = o * corr + sum_j p[qv][j] * v[j][d]; thread t owns dim
-    // d = t % 128 for the query vectors qv = t / 128 (mod 2)
-    {
-      constexpr int kHalf = (QVT + 1) / 2;
-      const int d = tid & 127;
-      const int q0 = tid >> 7;
-      float acc[kHalf];
-#pragma unroll
-      for (int i = 0; i < kHalf; ++i) acc[i] = 0.f;
-      float acc2[kHalf];
-#pragma unroll
-      for (int i = 0; i < kHalf; ++i) acc2[i] = 0.f;
-      int j = 0;
-      for (; j + 1 < nk; j += 2) {  // two keys per step: independent FMA chains
-        const float v0 = __bfloat162float(sm.v[buf][j * 128 + d]);
-        const float v1 = __bfloat162float(sm.v[buf][(j + 1) * 128 + d]);
-#pragma unroll
-        for (int i = 0; i < kHalf; ++i) {
-          const int qv = q0 + 2 * i;
-          if (qv < QV) {
-            acc[i] = fmaf(sm.s[qv][j], v0, acc[i]);
-            acc2[i] = fmaf(sm.s[qv][j + 1], v1, acc2[i]);
-          }
-        }
-      }
-      if (j < nk) {
-        const float v0 = __bfloat162float(sm.v[buf][j * 128 + d]);
-#pragma unroll
-        for (int i = 0; i < kHalf; ++i) {
-          const int qv = q0 + 2 * i;
-          if (qv < QV) acc[i] = fmaf(sm.s[qv][j], v0, acc[i]);
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < kHalf; ++i) acc[i] += acc2[i];
-#pragma unroll
-      for (int i = 0; i < kHalf; ++i) {
-        const int qv = q0 + 2 * i;
-        if (qv < QV) sm.o[qv][d] = sm.o[qv][d] * sm.corr[qv] + acc[i];
-      }
-    }
-    __syncthreads();  // buffer `buf` is refilled by the next iteration's prefetch
   }
 
   // ---- merge the S partials of this kv head through DSMEM ----
   cluster.sync();
-  for (int idx = split * kThreads + tid; idx < QV * 128; idx += S * kThreads) {
-    const int qv = idx >> 7, d = idx & 127;
-    // all peer loads are independent: issue them together (<= 16 peers)
+  for (int idx = split * kThreads + tid; idx < nq * 128; idx += S * kThreads) {
+    const int i = idx >> 7, d = idx & 127;
     float mr[16], lr[16], orr[16];
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
       if (r < S) {
-        const DecodeSmem* peer = cluster.map_shared_rank(&sm, r);
-        mr[r] = peer->m[qv];
-        lr[r] = peer->l[qv];
-        orr[r] = peer->o[qv][d];
+        const RegSmem* peer = cluster.map_shared_rank(&sm, r);
+        mr[r] = peer->m[i];
+        lr[r] = peer->l[i];
+        orr[r] = peer->o[i][d];
       }
     }
     float gmax = -INFINITY;
@@ -269,6 +274,7 @@ __global__ void __launch_bounds__(kThreads)
         }
       }
     }
+    const int qv = qv0 + i;
     if (outer == 1) {
       const int m = qv / G, gi = qv % G;
       a.out[(size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + d] =
@@ -284,23 +290,23 @@ __global__ void __launch_bounds__(kThreads)
   }
   cluster.sync();
   if (outer == 1) return;
-  // the last CTA of this kv head merges the clusters' partials in cluster order
   __shared__ unsigned s_ticket;
+  unsigned* counter = a.counters + kvh * (kMaxQV / kRQ) + blockIdx.z;
   __threadfence();
   __syncthreads();
-  if (tid == 0) s_ticket = atomicAdd(a.counters + kvh, 1u);
+  if (tid == 0) s_ticket = atomicAdd(counter, 1u);
   __syncthreads();
   if (s_ticket != (unsigned)(S * outer - 1)) return;
   __threadfence();
-  for (int idx = tid; idx < QV * 128; idx += kThreads) {
-    const int qv = idx >> 7, d = idx & 127;
-    const float* base = a.ws + ((size_t)kvh * kMaxOuter * kMaxQV + qv) * 130;
+  for (int idx = tid; idx < nq * 128; idx += kThreads) {
+    const int qv = qv0 + (idx >> 7), d = idx & 127;
+    const float* b0 = a.ws + ((size_t)kvh * kMaxOuter * kMaxQV + qv) * 130;
     float gmax = -INFINITY;
-    for (int c = 0; c < outer; ++c) gmax = fmaxf(gmax, __ldcg(base + (size_t)c * kMaxQV * 130));
+    for (int c = 0; c < outer; ++c) gmax = fmaxf(gmax, __ldcg(b0 + (size_t)c * kMaxQV * 130));
     float num = 0.f, den = 0.f;
     if (gmax != -INFINITY) {
       for (int c = 0; c < outer; ++c) {
-        const float* pc = base + (size_t)c * kMaxQV * 130;
+        const float* pc = b0 + (size_t)c * kMaxQV * 130;
         const float mc = __ldcg(pc);
         if (mc == -INFINITY) continue;
         const float w = exp2f(mc - gmax);
@@ -312,13 +318,14 @@ __global__ void __launch_bounds__(kThreads)
     a.out[(size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + d] =
         __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
   }
-  if (tid == 0) a.counters[kvh] = 0u;
+  if (tid == 0) *counter = 0u;
 }
 
-// Clusters per kv head: enough CTAs for about two per SM when the kv heads are
-// few (tensor parallelism) or the context long, at least 128 keys per CTA.
+// Clusters per kv head: about one CTA per SM (a CTA holds 255 registers a
+// thread, so one fits an SM) when the kv heads are few (tensor parallelism) or
+// the context long, with at least 128 keys per CTA.
 int attention_decode_outer(int cache_cap, int n_kv_heads, int cluster, int num_sms) {
-  int r = (2 * num_sms + cluster * n_kv_heads / 2) / (cluster * n_kv_heads);
+  int r = num_sms / (cluster * n_kv_heads);
   const int by_keys = cache_cap / (cluster * 128);
   if (r > by_keys) r = by_keys;
   if (r > kMaxOuter) r = kMaxOuter;
@@ -350,26 +357,19 @@ cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
   const int total = S * outer;
   int chunk = (a.cache_cap + kMaxRows + total - 1) / total;
   chunk = (chunk + 15) / 16 * 16;
-  const int smem = (int)sizeof(DecodeSmem);
   const int qv = a.M * G;
-  auto kern = qv <= 4 ? attention_decode_kernel<4>
-            : qv <= 8 ? attention_decode_kernel<8>
-            : qv <= 16 ? attention_decode_kernel<16> : attention_decode_kernel<32>;
-  ensure_smem_attr(kern, smem);
+  auto kern = attention_decode_reg_kernel;
   {
-    static const void* nonportable_done[8] = {nullptr};
-    bool done = false;
-    for (auto* p : nonportable_done) done |= (p == reinterpret_cast<const void*>(kern));
-    if (!done) {
+    static bool nonportable_done = false;
+    if (!nonportable_done) {
       cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-      for (auto*& p : nonportable_done)
-        if (p == nullptr) { p = reinterpret_cast<const void*>(kern); break; }
+      nonportable_done = true;
     }
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(S * outer, a.n_kv_heads, 1);
+  cfg.gridDim = dim3(S * outer, a.n_kv_heads, (qv + kRQ - 1) / kRQ);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -190,7 +190,7 @@ struct AttnDecodeArgs {
   // order.  R is chosen from the capacity and the head count only, so a row's
   // result does not depend on M.
   float* ws;           // [n_kv_heads][16][32][130] fp32 (null: one cluster per kv head)
-  unsigned* counters;  // [n_kv_heads], zero between launches
+  unsigned* counters;  // [n_kv_heads][8] (one per kv head and group of 4 query vectors), zero between launches
 };
 
 cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream);

@@ -107,7 +107,7 @@ def main() -> None:
                     t_s = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), s_try, out))
                     res[f"attn_decode_ctx{cap}_S{s_try}"] = {"us": t_s}
             ws = torch.zeros(Hkv * 16 * 32 * 130, device=dev)
-            cnt = torch.zeros(Hkv, device=dev, dtype=torch.int32)
+            cnt = torch.zeros(Hkv * 8, device=dev, dtype=torch.int32)
             R = int(ext.attention_decode_outer(cap, Hkv, S, ext.num_sms()))
             t = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), S, out, ws=ws,
                                                     counters=cnt))
@@ -126,7 +126,7 @@ def main() -> None:
         pos = torch.tensor([cap - 16], device=dev, dtype=torch.int32)
         out = torch.empty(1, H * 128, device=dev, dtype=bf)
         ws = torch.zeros(Hkv * 16 * 32 * 130, device=dev)
-        cnt = torch.zeros(Hkv, device=dev, dtype=torch.int32)
+        cnt = torch.zeros(Hkv * 8, device=dev, dtype=torch.int32)
         kv_bytes = 2 * Hkv * (cap - 15) * 128 * 2
         for name, kw in (("one_cluster", {}), ("two_level", {"ws": ws, "counters": cnt})):
             t = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), 16, out, **kw))

@@ -220,7 +220,7 @@ def test_attention_decode_two_level_split(cuda_device, M, hkv, cap):
     ref = _attn_reference(q, kc[:, :n], vc[:, :n], pos0 + torch.arange(M, device=cuda_device),
                           torch.arange(n, device=cuda_device), H)
     ws = torch.zeros(hkv * 16 * 32 * 130, device=cuda_device)
-    cnt = torch.zeros(hkv, device=cuda_device, dtype=torch.int32)
+    cnt = torch.zeros(hkv * 8, device=cuda_device, dtype=torch.int32)
     outer = _ext().attention_decode_outer(cap, hkv, 16, _ext().num_sms())
     assert outer > 1
     for _ in range(2):
