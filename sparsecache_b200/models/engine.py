@@ -454,7 +454,7 @@ class B200Engine:
 
     def _decode_splits(self, capacity: int) -> int:
         """CTAs per kv head (= thread-block cluster size) of the decode attention."""
-        return int(self.ext.attention_decode_cluster(capacity))
+        return int(self.ext.attention_decode_cluster(capacity, self.cfg.n_kv_heads))
 
     def set_decode_state(self, *, position: int, slot: int | None = None, n_virtual: int | None = None) -> None:
         """Host-side set of the device scalars (stream-ordered, before a step)."""

@@ -321,21 +321,24 @@ __global__ void __launch_bounds__(kThreads)
   if (tid == 0) *counter = 0u;
 }
 
-// Clusters per kv head: about one CTA per SM (a CTA holds 255 registers a
-// thread, so one fits an SM) when the kv heads are few (tensor parallelism) or
-// the context long, with at least 128 keys per CTA.
+// Launch geometry (measured on B200, one query row, 8/4/1 kv heads, 2k-18k
+// keys): up to ~512 keys per CTA a single cluster per kv head is fastest (8
+// CTAs with 8 kv heads, 16 with fewer); beyond that, 4-CTA clusters with
+// several clusters per kv head (about 128 CTAs in all, at least 128 keys a
+// CTA) beat larger clusters, which schedule poorly at one CTA per SM.  Both
+// depend on the capacity and the head count only, never on M.
+int attention_decode_cluster(int cache_cap, int n_kv_heads) {
+  const int s1 = n_kv_heads >= 8 ? 8 : 16;
+  return cache_cap / s1 <= 512 ? s1 : 4;
+}
+
 int attention_decode_outer(int cache_cap, int n_kv_heads, int cluster, int num_sms) {
-  int r = num_sms / (cluster * n_kv_heads);
+  if (cluster != 4) return 1;
+  int r = (num_sms < 128 ? num_sms : 128) / (cluster * n_kv_heads);
   const int by_keys = cache_cap / (cluster * 128);
   if (r > by_keys) r = by_keys;
   if (r > kMaxOuter) r = kMaxOuter;
   return r < 1 ? 1 : r;
-}
-
-int attention_decode_cluster(int cache_cap) {
-  // 16-CTA clusters (non-portable, supported by B200) when the context is long
-  // enough to give each CTA at least a sub-chunk; 8 otherwise.
-  return cache_cap > 8 * kSub ? 16 : 8;
 }
 
 cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {

@@ -907,7 +907,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_decode_outer", [](int64_t cap, int64_t kvh, int64_t cluster, int64_t sms) {
     return sc::attention_decode_outer((int)cap, (int)kvh, (int)cluster, (int)sms);
   });
-  m.def("attention_decode_cluster", [](int64_t cap) { return sc::attention_decode_cluster((int)cap); });
+  m.def("attention_decode_cluster", [](int64_t cap, int64_t n_kv_heads) {
+    return sc::attention_decode_cluster((int)cap, (int)n_kv_heads);
+  }, py::arg("cache_cap"), py::arg("n_kv_heads") = 8);
   m.def("rmsnorm", &rmsnorm);
   m.def("embedding", &embedding);
   m.def("gather_rows", &gather_rows);

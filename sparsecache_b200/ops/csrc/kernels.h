@@ -194,7 +194,7 @@ struct AttnDecodeArgs {
 };
 
 cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream);
-int attention_decode_cluster(int cache_cap);
+int attention_decode_cluster(int cache_cap, int n_kv_heads);
 int attention_decode_outer(int cache_cap, int n_kv_heads, int cluster, int num_sms);
 
 // ------------------------------------------------------------ pointwise ----

@@ -101,7 +101,7 @@ def main() -> None:
             q = torch.randn(1, H * 128, device=dev).to(bf)
             pos = torch.tensor([cap - 16], device=dev, dtype=torch.int32)
             out = torch.empty(1, H * 128, device=dev, dtype=bf)
-            S = int(ext.attention_decode_cluster(cap))
+            S = int(ext.attention_decode_cluster(cap, Hkv))
             if "attn_decode_sweep" in only:  # cluster-size sweep
                 for s_try in (4, 8, 16):
                     t_s = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), s_try, out))
@@ -117,6 +117,23 @@ def main() -> None:
                                             "cluster": S, "clusters_per_kv_head": R,
                                             "l2_resident": kv_bytes < 126e6}
 
+    if "attn_decode_grid" in only:
+        # cluster size x (one / several clusters per kv head) for the decode shapes that matter
+        for H, Hkv, cap in ((32, 8, 2048), (32, 8, 18000), (8, 1, 16384), (16, 4, 4096)):
+            kc = torch.randn(Hkv, cap, 128, device=dev).to(bf)
+            vc = torch.randn(Hkv, cap, 128, device=dev).to(bf)
+            q = torch.randn(1, H * 128, device=dev).to(bf)
+            pos = torch.tensor([cap - 16], device=dev, dtype=torch.int32)
+            out = torch.empty(1, H * 128, device=dev, dtype=bf)
+            ws = torch.zeros(Hkv * 16 * 32 * 130, device=dev)
+            cnt = torch.zeros(Hkv * 8, device=dev, dtype=torch.int32)
+            for S in (4, 8, 16):
+                for two in (False, True):
+                    kw = {"ws": ws, "counters": cnt} if two else {}
+                    R = int(ext.attention_decode_outer(cap, Hkv, S, ext.num_sms())) if two else 1
+                    t = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), S, out, **kw))
+                    res[f"grid_H{H}_kv{Hkv}_ctx{cap}_S{S}_R{R}"] = {"us": t}
+
     if "attn_decode_tp" in only:
         # one kv head per GPU (70B at TP8), 16k context: one cluster vs several clusters per kv head
         H, Hkv, cap = 8, 1, 16384
@@ -128,8 +145,9 @@ def main() -> None:
         ws = torch.zeros(Hkv * 16 * 32 * 130, device=dev)
         cnt = torch.zeros(Hkv * 8, device=dev, dtype=torch.int32)
         kv_bytes = 2 * Hkv * (cap - 15) * 128 * 2
-        for name, kw in (("one_cluster", {}), ("two_level", {"ws": ws, "counters": cnt})):
-            t = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), 16, out, **kw))
+        for name, S, kw in (("one_cluster", 16, {}), ("two_level", int(ext.attention_decode_cluster(cap, Hkv)),
+                                                          {"ws": ws, "counters": cnt})):
+            t = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), S, out, **kw))
             res[f"attn_decode_tp8_70b_ctx{cap}_{name}"] = {"us": t, "GBps": kv_bytes / (t * 1e-6) / 1e9}
 
     if "attn_prefill" in only:

@@ -204,7 +204,7 @@ def test_attention_decode(cuda_device, M):
 
 
 @pytest.mark.parametrize("M", [1, 4])
-@pytest.mark.parametrize("hkv,cap", [(1, 16384), (2, 6000), (8, 18000)])
+@pytest.mark.parametrize("hkv,cap", [(1, 16384), (2, 6000), (4, 18000)])
 def test_attention_decode_two_level_split(cuda_device, M, hkv, cap):
     """Several clusters per kv head (few kv heads / long contexts): the ticketed
     cross-cluster merge equals the reference, twice in a row (the tickets reset)."""
@@ -221,11 +221,12 @@ def test_attention_decode_two_level_split(cuda_device, M, hkv, cap):
                           torch.arange(n, device=cuda_device), H)
     ws = torch.zeros(hkv * 16 * 32 * 130, device=cuda_device)
     cnt = torch.zeros(hkv * 8, device=cuda_device, dtype=torch.int32)
-    outer = _ext().attention_decode_outer(cap, hkv, 16, _ext().num_sms())
-    assert outer > 1
+    S = _ext().attention_decode_cluster(cap, hkv)
+    outer = _ext().attention_decode_outer(cap, hkv, S, _ext().num_sms())
+    assert S == 4 and outer > 1
     for _ in range(2):
         out = torch.empty(M, H * 128, device=cuda_device, dtype=torch.bfloat16)
-        _ext().attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), 16, out, ws=ws, counters=cnt)
+        _ext().attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), S, out, ws=ws, counters=cnt)
         torch.cuda.synchronize()
         torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
         assert int(cnt.sum()) == 0
