@@ -231,9 +231,16 @@ sc::GemmArgs sharded_gemm(const std::vector<int64_t>& shard_ptrs, int64_t rows, 
 
 void gemm_ag_qkv(std::vector<int64_t> shard_ptrs, int64_t rows, int64_t own, Tensor ready, int64_t epoch,
                  int64_t K, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_cache, Tensor rope_pos,
-                 Tensor cache_slot, Tensor rope_table, int64_t n_q_heads, int64_t n_kv_heads, int64_t bn) {
+                 Tensor cache_slot, Tensor rope_table, int64_t n_q_heads, int64_t n_kv_heads, int64_t bn,
+                 c10::optional<Tensor> dev_part, int64_t dev_mode) {
   const c10::cuda::CUDAGuard guard(w_qkv.device());
   auto g = sharded_gemm(shard_ptrs, rows, own, ready, epoch, K, w_qkv, sc::EPI_QKV, bn);
+  if (dev_part.has_value() && dev_part->defined()) {
+    CHECK_F32(*dev_part);
+    TORCH_CHECK(dev_part->numel() >= (int64_t)g.M * 2 * n_kv_heads, "dev_part size");
+    g.ep.dev_part = dev_part->data_ptr<float>();
+    g.ep.dev_mode = (int)dev_mode;
+  }
   check_matrix(q_out, "q_out");
   TORCH_CHECK(w_qkv.size(0) == (n_q_heads + 2 * n_kv_heads) * 128, "w_qkv rows");
   TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(0) == n_kv_heads && k_cache.is_contiguous(), "k_cache");
@@ -653,7 +660,7 @@ void compose_relocate(Tensor docs, Tensor offsets, int64_t total_tokens, int64_t
 void cacheblend_select(Tensor dev_part, int64_t n_kv_heads, int64_t dev_mode, int64_t total_rows,
                        int64_t doc_begin, int64_t doc_end, int64_t k, bool keep_prefix,
                        Tensor active, Tensor n_active, Tensor scores,
-                       c10::optional<Tensor> checksum) {
+                       c10::optional<Tensor> checksum, int64_t n_parts, int64_t part_stride) {
   const c10::cuda::CUDAGuard guard(dev_part.device());
   CHECK_F32(dev_part); CHECK_I32(active); CHECK_I32(n_active); CHECK_F32(scores);
   TORCH_CHECK(scores.numel() >= std::max<int64_t>(1, doc_end - doc_begin), "scores scratch");
@@ -669,6 +676,10 @@ void cacheblend_select(Tensor dev_part, int64_t n_kv_heads, int64_t dev_mode, in
   a.active = active.data_ptr<int>();
   a.n_active = n_active.data_ptr<int>();
   a.scores = scores.data_ptr<float>();
+  TORCH_CHECK(n_parts >= 1 && (n_parts == 1 || part_stride >= total_rows * 2 * n_kv_heads), "partial layout");
+  TORCH_CHECK(dev_part.numel() >= (n_parts - 1) * part_stride + total_rows * 2 * n_kv_heads, "dev_part size");
+  a.n_parts = (int)n_parts;
+  a.part_stride = part_stride;
   if (checksum.has_value() && checksum->defined()) {
     TORCH_CHECK(checksum->scalar_type() == torch::kInt64, "checksum int64");
     a.checksum = reinterpret_cast<long long*>(checksum->data_ptr<int64_t>());
@@ -874,7 +885,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                                cudaMemcpyDefault, cur_stream()),
                "memcpy_async");
   });
-  m.def("gemm_ag_qkv", &gemm_ag_qkv);
+  m.def("gemm_ag_qkv", &gemm_ag_qkv, py::arg("shard_ptrs"), py::arg("rows"), py::arg("own"), py::arg("ready"),
+        py::arg("epoch"), py::arg("K"), py::arg("w_qkv"), py::arg("q_out"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("rope_pos"), py::arg("cache_slot"), py::arg("rope_table"), py::arg("n_q_heads"),
+        py::arg("n_kv_heads"), py::arg("bn"), py::arg("dev_part") = py::none(), py::arg("dev_mode") = 0);
   m.def("gemm_ag_swiglu", &gemm_ag_swiglu);
   m.def("gemm_rs", &gemm_rs);
   m.def("rs_reduce", &rs_reduce, py::arg("recv"), py::arg("flags"), py::arg("epoch"), py::arg("timeout_ns"),
@@ -914,7 +928,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding", &embedding);
   m.def("gather_rows", &gather_rows);
   m.def("compose_relocate", &compose_relocate);
-  m.def("cacheblend_select", &cacheblend_select);
+  m.def("cacheblend_select", &cacheblend_select, py::arg("dev_part"), py::arg("n_kv_heads"), py::arg("dev_mode"),
+        py::arg("total_rows"), py::arg("doc_begin"), py::arg("doc_end"), py::arg("k"), py::arg("keep_prefix"),
+        py::arg("active"), py::arg("n_active"), py::arg("scores"), py::arg("checksum") = py::none(),
+        py::arg("n_parts") = 1, py::arg("part_stride") = 0);
   m.def("arange_i32", &arange_i32);
   m.def("index_i32", &index_i32);
   m.def("status", &status);

@@ -243,6 +243,10 @@ struct SelectArgs {
   int* n_active;    // out scalar
   float* scores;    // scratch [T]
   long long* checksum;  // optional out: sum over sorted selected doc positions * rank
+  // tensor parallel: the partials of n_parts ranks (each [T][2 * n_kv_heads]
+  // over its own kv heads) lie part_stride floats apart; scores sum them all
+  int n_parts;
+  long long part_stride;
 };
 cudaError_t cacheblend_select(const SelectArgs& a, cudaStream_t stream);
 

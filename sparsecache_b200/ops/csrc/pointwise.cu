@@ -214,12 +214,14 @@ __global__ void __launch_bounds__(kSelThreads) cacheblend_select_kernel(SelectAr
 
   // 1. scores (fixed reduction order over kv heads; key part then value part)
   for (int i = tid; i < n_doc; i += kSelThreads) {
-    const float* p = a.dev_part + (size_t)(a.doc_begin + i) * 2 * H;
     float s = 0.f;
-    if (a.dev_mode & DEV_KEY)
-      for (int h = 0; h < H; ++h) s += p[h];
-    if (a.dev_mode & DEV_VALUE)
-      for (int h = 0; h < H; ++h) s += p[H + h];
+    for (int part = 0; part < max(1, a.n_parts); ++part) {
+      const float* p = a.dev_part + part * a.part_stride + (size_t)(a.doc_begin + i) * 2 * H;
+      if (a.dev_mode & DEV_KEY)
+        for (int h = 0; h < H; ++h) s += p[h];
+      if (a.dev_mode & DEV_VALUE)
+        for (int h = 0; h < H; ++h) s += p[H + h];
+    }
     a.scores[i] = s;
   }
   __syncthreads();

@@ -26,6 +26,22 @@ Epoch-numbered flags only ever increase, so one flag word per (kind, sender)
 serves every layer; buffer reuse is safe because each rank reaches the next
 write of a buffer only after consuming data every peer produced after its
 last read of it.
+
+CacheBlend (``cacheblend``): the layers before the check layer and the check
+layer run over every prompt row as in prefill; the check layer's QKV
+epilogue also writes each row's deviation from the composed cache for the
+local kv heads, every rank pushes those partials to every peer (copy engine)
+and all ranks run the same top-k over the sum, so the active set is
+identical everywhere.  The residual rows are then all-gathered once and each
+rank keeps its share of the active rows, which run the later layers with the
+same fused AG/RS layer body (K/V written at their own slots, keys = the whole
+composed prompt).
+
+Decode, verify and drafting steps (single-row GEMVs with a fused all-reduce)
+share one device step counter ``pos[3]``: the all-reduce number k of a step
+uses epoch ``step * ar_stride + k``, each step advances the counter once,
+and every step (and every captured graph) holds an even number of
+all-reduces so that the two receive buffers strictly alternate.
 """
 from __future__ import annotations
 
@@ -43,7 +59,8 @@ from ..models.weights import GATE_UP_BLOCK
 FLAG_X, FLAG_X2, FLAG_RS_O, FLAG_RS_D = 0, 1, 2, 3
 FLAG_AR_O, FLAG_AR_D, FLAG_TOKEN, FLAG_TOKEN_EPOCH = 4, 5, 6, 7
 FLAG_STAGE_X, FLAG_STAGE_X2 = 8, 9  # local: a peer shard has landed in the staging buffer
-N_FLAG_KINDS = 10
+FLAG_DEV, FLAG_H, FLAG_STAGE_H = 10, 11, 12  # CacheBlend: deviation partials, residual all-gather
+N_FLAG_KINDS = 13
 TIMEOUT_NS = int(20e9)
 
 
@@ -128,6 +145,10 @@ class TPEngine:
         # bf16 partials of the row-parallel GEMMs, one slot per sender
         self.recv_o_buf, self.recv_o_ptrs = group.shared(self.tp * R * d * 2)
         self.recv_d_buf, self.recv_d_ptrs = group.shared(self.tp * R * d * 2)
+        self.h_buf, self.h_ptrs = group.shared(R * d * 2)  # residual shard (all-gathered by CacheBlend)
+        # deviation partials of every rank: [tp][tp * R rows][2 * local kv heads] fp32
+        self.dev_stride = self.tp * R * 2 * self.lcfg.n_kv_heads
+        self.dev_buf, self.dev_ptrs = group.shared(self.tp * self.dev_stride * 4)
         self.flag_buf, self.flag_ptrs = group.shared(N_FLAG_KINDS * self.tp * 4)
         self.flags = self.flag_buf.view(torch.int32).view(N_FLAG_KINDS, self.tp)
         # decode all-reduce receive slots [tp, 8 rows, d] fp32 (O and down)
@@ -142,6 +163,11 @@ class TPEngine:
         self.stage_x = torch.empty(self.tp * R, d, device=group.device, dtype=torch.bfloat16)
         self.stage_x2 = torch.empty(self.tp * R, d, device=group.device, dtype=torch.bfloat16)
         self.side = torch.cuda.Stream(device=group.device)
+        # epochs per device step: >= the all-reduces of any step kind (decode /
+        # verify: 2 per layer; a drafting graph: 3 per draft token)
+        self.ar_stride = 2 * cfg.n_layers + 64
+        L = cfg.n_layers
+        self.seed_layers = tuple(sorted({min(2, L - 1), L // 2, max(0, L - 3)})) if L >= 3 else tuple(range(L))
 
     @classmethod
     def from_full(cls, cfg: ModelConfig, full: EngineWeights, group: TPGroup, **kw) -> "TPEngine":
@@ -184,14 +210,56 @@ class TPEngine:
         return bases
 
     # ------------------------------------------------------------ prefill
-    def prefill(self, ids: torch.Tensor, slot: KVSlot) -> tuple[torch.Tensor, int, int]:
-        """Prefill ids (all ranks pass the same int32 device ids).
+    def _views(self, rows: int):
+        d, tp = self.full_cfg.d_model, self.tp
+        bf = torch.bfloat16
+        return (self.x_buf.view(bf)[: rows * d].view(rows, d), self.x2_buf.view(bf)[: rows * d].view(rows, d),
+                self.recv_o_buf.view(bf)[: tp * rows * d].view(tp, rows, d),
+                self.recv_d_buf.view(bf)[: tp * rows * d].view(tp, rows, d))
 
-        Returns (this rank's final-normed hidden shard [rows, d], rows, padded
-        length).  The shard owning row T-1 holds the last prompt row.
+    def _layer(self, layer: int, rows: int, pos: torch.Tensor, slots: torch.Tensor, n_keys: int,
+               h: torch.Tensor, nxt_norm: torch.Tensor, slot: KVSlot, *, dev_part: torch.Tensor | None = None,
+               dev_mode: int = 0) -> int:
+        """One fused TP layer over tp * rows rows (this rank's residual shard ``h`` [rows, d]).
+
+        The normed input shard must already be in ``x_buf``; on return the
+        next layer's normed input (``nxt_norm``) is there.  Rows write K/V at
+        cache ``slots`` with RoPE ``pos`` and attend causally (by position) to
+        keys [0, n_keys).  Returns the epoch used.
         """
         ext, eng, cfg, lc = self.ext, self.engine, self.full_cfg, self.lcfg
-        T = ids.numel()
+        d, n = cfg.d_model, rows * self.tp
+        x, x2, recv_o, recv_d = self._views(rows)
+        q = eng.ws.get("q", (n, lc.q_size), torch.bfloat16)
+        attn = eng.ws.get("attn", (n, lc.q_size), torch.bfloat16)
+        act = eng.ws.get("act", (n, lc.ffn), torch.bfloat16)
+        lw = eng.w.layers[layer]
+        bn = eng.bn
+        self.epoch += 1
+        e = self.epoch
+        self._signal_all(FLAG_X, e)
+        bases = self._pull_shards(FLAG_X, FLAG_STAGE_X, self.x_ptrs, self.stage_x, rows, e)
+        ext.gemm_ag_qkv(bases, rows, self.rank, self.flags[FLAG_STAGE_X], e, d, lw.w_qkv, q, slot.k(layer),
+                        slot.v(layer), pos, slots, eng.rope, lc.n_heads, lc.n_kv_heads, bn, dev_part, dev_mode)
+        ext.attention_prefill(q, None, pos, slot.k(layer), slot.v(layer), None, n_keys, lc.n_heads, eng.scale, attn)
+        ext.gemm_rs(attn, lw.w_o, self.recv_o_ptrs, rows, self.rank, bn)
+        self._signal_all(FLAG_RS_O, e)
+        ext.rs_reduce(recv_o, self.flags[FLAG_RS_O], e, TIMEOUT_NS, self.status, h, h, lw.ln2, x2, cfg.rms_eps)
+        self._signal_all(FLAG_X2, e)
+        bases = self._pull_shards(FLAG_X2, FLAG_STAGE_X2, self.x2_ptrs, self.stage_x2, rows, e)
+        ext.gemm_ag_swiglu(bases, rows, self.rank, self.flags[FLAG_STAGE_X2], e, d, lw.w_gu, act, bn)
+        ext.gemm_rs(act, lw.w_down, self.recv_d_ptrs, rows, self.rank, bn)
+        self._signal_all(FLAG_RS_D, e)
+        ext.rs_reduce(recv_d, self.flags[FLAG_RS_D], e, TIMEOUT_NS, self.status, h, h, nxt_norm, x, cfg.rms_eps)
+        return e
+
+    def _next_norm(self, layer: int) -> torch.Tensor:
+        w = self.engine.w
+        return w.layers[layer + 1].ln1 if layer + 1 < len(w.layers) else w.norm
+
+    def _embed_shard(self, ids: torch.Tensor, T: int, slot: KVSlot) -> tuple[torch.Tensor, int, int, torch.Tensor]:
+        """Pad the prompt to tp * rows (rows a multiple of 128), embed this rank's rows, norm into x_buf."""
+        eng, cfg = self.engine, self.full_cfg
         rows = int(math.ceil(T / (self.tp * 128)) * 128)
         if rows > self.max_rows:
             raise ValueError("prompt exceeds the TP buffers")
@@ -199,50 +267,117 @@ class TPEngine:
         if Tp > slot.capacity:
             raise ValueError("slot capacity below the padded prompt")
         d = cfg.d_model
-        ids_p = torch.zeros(Tp, dtype=torch.int32, device=ids.device)
+        ids_p = eng.ws.get("tp_ids", (Tp,), torch.int32)
+        ids_p.zero_()
         ids_p[:T] = ids
         own = slice(self.rank * rows, (self.rank + 1) * rows)
-        h = eng.ws.get("tp_h", (rows, d), torch.bfloat16)
-        ext.embedding(ids_p[own], eng.w.embed, h)
-        x = self.x_buf.view(torch.bfloat16)[: rows * d].view(rows, d)
-        x2 = self.x2_buf.view(torch.bfloat16)[: rows * d].view(rows, d)
-        recv_o = self.recv_o_buf.view(torch.bfloat16)[: self.tp * rows * d].view(self.tp, rows, d)
-        recv_d = self.recv_d_buf.view(torch.bfloat16)[: self.tp * rows * d].view(self.tp, rows, d)
-        ext.rmsnorm(h, None, eng.w.layers[0].ln1, cfg.rms_eps, x)
-        pos = eng._arange("pos", Tp)
-        q = eng.ws.get("q", (Tp, lc.q_size), torch.bfloat16)
-        attn = eng.ws.get("attn", (Tp, lc.q_size), torch.bfloat16)
-        act = eng.ws.get("act", (Tp, lc.ffn), torch.bfloat16)
-        bn = eng.bn
-        for layer, lw in enumerate(eng.w.layers):
-            self.epoch += 1
-            e = self.epoch
-            self._signal_all(FLAG_X, e)
-            bases = self._pull_shards(FLAG_X, FLAG_STAGE_X, self.x_ptrs, self.stage_x, rows, e)
-            ext.gemm_ag_qkv(bases, rows, self.rank, self.flags[FLAG_STAGE_X], e, d, lw.w_qkv, q, slot.k(layer),
-                            slot.v(layer), pos, pos, eng.rope, lc.n_heads, lc.n_kv_heads, bn)
-            ext.attention_prefill(q, None, pos, slot.k(layer), slot.v(layer), None, Tp, lc.n_heads, eng.scale, attn)
-            ext.gemm_rs(attn, lw.w_o, self.recv_o_ptrs, rows, self.rank, bn)
-            self._signal_all(FLAG_RS_O, e)
-            ext.rs_reduce(recv_o, self.flags[FLAG_RS_O], e, TIMEOUT_NS, self.status, h, h, lw.ln2, x2, cfg.rms_eps)
-            self._signal_all(FLAG_X2, e)
-            bases = self._pull_shards(FLAG_X2, FLAG_STAGE_X2, self.x2_ptrs, self.stage_x2, rows, e)
-            ext.gemm_ag_swiglu(bases, rows, self.rank, self.flags[FLAG_STAGE_X2], e, d, lw.w_gu, act, bn)
-            ext.gemm_rs(act, lw.w_down, self.recv_d_ptrs, rows, self.rank, bn)
-            self._signal_all(FLAG_RS_D, e)
-            nxt = eng.w.layers[layer + 1].ln1 if layer + 1 < len(eng.w.layers) else eng.w.norm
-            ext.rs_reduce(recv_d, self.flags[FLAG_RS_D], e, TIMEOUT_NS, self.status, h, h, nxt, x, cfg.rms_eps)
-        return x, rows, Tp
+        h = self.h_buf.view(torch.bfloat16)[: rows * d].view(rows, d)
+        self.ext.embedding(ids_p[own], eng.w.embed, h)
+        x = self._views(rows)[0]
+        self.ext.rmsnorm(h, None, eng.w.layers[0].ln1, cfg.rms_eps, x)
+        return h, rows, Tp, eng._arange("pos", Tp)
+
+    def prefill(self, ids: torch.Tensor, slot: KVSlot) -> tuple[torch.Tensor, int, int]:
+        """Prefill ids (all ranks pass the same int32 device ids).
+
+        Returns (this rank's final-normed hidden shard [rows, d], rows, padded
+        length).  The shard owning row T-1 holds the last prompt row.
+        """
+        T = ids.numel()
+        h, rows, Tp, pos = self._embed_shard(ids, T, slot)
+        for layer in range(self.full_cfg.n_layers):
+            self._layer(layer, rows, pos, pos, Tp, h, self._next_norm(layer), slot)
+        return self._views(rows)[0], rows, Tp
+
+    def cacheblend(self, ids: torch.Tensor, slot: KVSlot, *, prefix_tokens: int, suffix_tokens: int,
+                   blend) -> tuple[torch.Tensor, int, int, dict]:
+        """Tensor-parallel CacheBlend over the composed cache already in ``slot`` (local kv heads).
+
+        Same protocol as ``B200Engine.cacheblend`` (full recompute below the
+        check layer, deviation top-k at the check layer, active rows only
+        above it).  Returns (this rank's final-normed shard of the active rows
+        [rows_a, d], rows_a, A, metadata); active row A-1 is the last prompt row.
+        """
+        from ..cacheblend import recompute_count
+
+        ext, eng, cfg, lc = self.ext, self.engine, self.full_cfg, self.lcfg
+        T = ids.numel()
+        raw_len = T - suffix_tokens
+        n_doc = raw_len - prefix_tokens
+        check = blend.check_layer
+        if not 0 <= check < cfg.n_layers:
+            raise ValueError("check_layer lies outside the model")
+        k_sel = recompute_count(n_doc, blend.recompute_ratio)
+        A = (prefix_tokens if blend.keep_prefix else 0) + k_sel + suffix_tokens
+        h, rows, Tp, pos = self._embed_shard(ids, T, slot)
+        d = cfg.d_model
+        for layer in range(check):
+            self._layer(layer, rows, pos, pos, Tp, h, self._next_norm(layer), slot)
+        # ---- check layer over every row, with the deviation partials of the local kv heads
+        dev_part = eng.ws.get("tp_dev", (Tp, 2 * lc.n_kv_heads), torch.float32)
+        e = self._layer(check, rows, pos, pos, Tp, h, self._next_norm(check), slot, dev_part=dev_part,
+                        dev_mode=blend.dev_mode)
+        # push the partials to every rank (copy engine over NVLink), then one flag per sender
+        nbytes = Tp * 2 * lc.n_kv_heads * 4
+        for r in range(self.tp):
+            ext.memcpy_async(self.dev_ptrs[r] + self.rank * self.dev_stride * 4, dev_part.data_ptr(), nbytes)
+        self._signal_all(FLAG_DEV, e)
+        # all-gather the residual rows while the selection runs
+        self._signal_all(FLAG_H, e)
+        main = torch.cuda.current_stream()
+        self._pull_shards(FLAG_H, FLAG_STAGE_H, self.h_ptrs, self.stage_x, rows, e)
+        with torch.cuda.stream(self.side):
+            ext.memcpy_async(self.stage_x[self.rank * rows:].data_ptr(), h.data_ptr(), rows * d * 2)
+        for r in range(self.tp):
+            ext.wait_flag(self.flags[FLAG_DEV], r, e, TIMEOUT_NS, self.status)
+        dev_all = self.dev_buf.view(torch.float32)
+        active = eng._i32("active", Tp)
+        n_active = eng._i32("n_active", 1)
+        scores = eng.ws.get("scores", (max(1, n_doc),), torch.float32)
+        checksum = eng.ws.get("checksum", (1,), torch.int64)
+        ext.cacheblend_select(dev_all, lc.n_kv_heads, blend.dev_mode, T, prefix_tokens, raw_len, k_sel,
+                              blend.keep_prefix, active, n_active, scores, checksum, n_parts=self.tp,
+                              part_stride=self.dev_stride)
+        # ---- active rows: rows_a per rank; padding rows write K/V past the prompt
+        rows_a = int(math.ceil(A / (self.tp * 128)) * 128)
+        Ap = rows_a * self.tp
+        if rows_a > self.max_rows or T + (Ap - A) > slot.capacity:
+            raise ValueError("active rows exceed the TP buffers / slot capacity")
+        act = active[:A]
+        slots_a = eng._i32("tp_slots_a", Ap)
+        slots_a[:A].copy_(act)
+        if Ap > A:
+            ext.arange_i32(slots_a[A:], T)
+        src = eng._i32("tp_src_a", rows_a)
+        own = slice(self.rank * rows_a, (self.rank + 1) * rows_a)
+        src.copy_(torch.where(slots_a[own] < T, slots_a[own], torch.zeros_like(slots_a[own])))
+        h_a = eng.ws.get("tp_ha", (rows_a, d), torch.bfloat16)
+        main.wait_stream(self.side)
+        ext.gather_rows(self.stage_x[:Tp], src, h_a)
+        x_a = self._views(rows_a)[0]
+        ext.rmsnorm(h_a, None, self._next_norm(check), cfg.rms_eps, x_a)
+        for layer in range(check + 1, cfg.n_layers):
+            self._layer(layer, rows_a, slots_a, slots_a, T, h_a, self._next_norm(layer), slot)
+        meta = {"active": act, "n_active": n_active, "checksum": checksum, "k_selected": k_sel,
+                "document_tokens": n_doc, "active_rows": A, "rows_per_rank": rows_a}
+        return x_a, rows_a, A, meta
 
     # ------------------------------------------------------------- decode
-    def first_token(self, x_shard: torch.Tensor, rows: int, T: int, *, max_new: int) -> None:
-        """The owner of prompt row T-1 runs the LM head and sends the token to every rank."""
+    def first_token(self, x_shard: torch.Tensor, rows: int, T: int, *, max_new: int,
+                    last_row: int | None = None) -> None:
+        """The owner of the last prompt row runs the LM head and sends the token to every rank.
+
+        ``last_row`` is that row's index in the sharded layout (default T-1;
+        after CacheBlend it is the last active row, A-1); the next token is at
+        position T.
+        """
         eng, ext = self.engine, self.ext
-        owner = (T - 1) // rows
+        last = T - 1 if last_row is None else int(last_row)
+        owner = last // rows
         self.token_epoch += 1
         b = eng._decode_buffers(max_new)
         if self.rank == owner:
-            lr = (T - 1) - owner * rows
+            lr = last - owner * rows
             b["counter"].zero_()
             ext.gemv_argmax(x_shard[lr:lr + 1], eng.w.lm_head, None, self.full_cfg.rms_eps, b["pv"], b["pi"],
                             b["counter"], b["tok"], None, None, None, None, None)
@@ -259,32 +394,95 @@ class TPEngine:
         # keep the monotonic step counter pos[3]; reset position / slot / view
         b["pos"][:3].fill_(T)
 
-    def _decode_step(self, slot: KVSlot, splits: int) -> None:
+    def allreduce(self, x: torch.Tensor, w: torch.Tensor, k: int, residual: torch.Tensor,
+                  norm_w: torch.Tensor | None = None) -> None:
+        """residual += sum over ranks of x @ w^T (row-parallel GEMV, M <= 8 rows), fused over peer memory.
+
+        ``k`` numbers the all-reduce inside the current device step (epoch
+        ``pos[3] * ar_stride + k``); odd k use the O receive buffer and flags,
+        even k the down buffer, so consecutive all-reduces alternate.
+        """
+        eng, ext, cfg = self.engine, self.ext, self.full_cfg
+        b = eng._decode_buffers()
+        M, d = x.shape[0], residual.shape[1]
+        step = b["pos"][3:4]
+        odd = k % 2 == 1
+        buf, ptrs = (self.ar_o_buf, self.ar_o_ptrs) if odd else (self.ar_d_buf, self.ar_d_ptrs)
+        kind = FLAG_AR_O if odd else FLAG_AR_D
+        flags = [self._flag_addr(r, kind, self.rank) for r in range(self.tp)]
+        ext.gemv_allreduce(x, w, norm_w, cfg.rms_eps, ptrs, flags, self.rank, k, step, self.ar_stride,
+                           self.ar_counters[0:1] if odd else self.ar_counters[1:2])
+        recv = buf.view(torch.float32)[: self.tp * M * d].view(self.tp, M, d)
+        ext.rs_reduce(recv, self.flags[kind], k, TIMEOUT_NS, self.status, residual, residual, None, None,
+                      cfg.rms_eps, step, self.ar_stride)
+
+    def _decode_step(self, slot: KVSlot, splits: int, M: int = 1, *, verify: bool = False) -> None:
+        """One target step over the M rows in h (decode: M = 1 with token feedback; verify: M rows).
+
+        A verify step writes the M rows' K/V at positions pos[0].., leaves the
+        argmax after every row in tok[:M], copies the residual rows after the
+        seed layers into ``feat`` and advances only the step counter.
+        """
         eng, ext, cfg, lc = self.engine, self.ext, self.full_cfg, self.lcfg
         b = eng._decode_buffers()
-        h, pos = b["h"][:1], b["pos"]
-        step = pos[3:4]
-        mul = 2 * lc.n_layers
-        ar_o = self.ar_o_buf.view(torch.float32)[: self.tp * cfg.d_model].view(self.tp, 1, cfg.d_model)
-        ar_d = self.ar_d_buf.view(torch.float32)[: self.tp * cfg.d_model].view(self.tp, 1, cfg.d_model)
-        fo = [self._flag_addr(r, FLAG_AR_O, self.rank) for r in range(self.tp)]
-        fd = [self._flag_addr(r, FLAG_AR_D, self.rank) for r in range(self.tp)]
+        h, pos = b["h"][:M], b["pos"]
+        feat = eng.ws.get("tp_feat", (len(self.seed_layers), eng.MAX_ROWS, cfg.d_model), torch.bfloat16)
         for layer, lw in enumerate(eng.w.layers):
-            ext.gemv_qkv(h, lw.w_qkv, lw.ln1, cfg.rms_eps, b["q"][:1], slot.k(layer), slot.v(layer), pos[0:1],
+            ext.gemv_qkv(h, lw.w_qkv, lw.ln1, cfg.rms_eps, b["q"][:M], slot.k(layer), slot.v(layer), pos[0:1],
                          eng.rope, lc.n_heads, lc.n_kv_heads, slot=pos[1:2])
-            ext.attention_decode(b["q"][:1], slot.k(layer), slot.v(layer), pos[0:1], lc.n_heads, eng.scale, splits,
-                                 b["attn"][:1], ws=b["attn_ws"], counters=b["attn_cnt"])
-            ext.gemv_allreduce(b["attn"][:1], lw.w_o, None, cfg.rms_eps, self.ar_o_ptrs, fo, self.rank,
-                               2 * layer + 1, step, mul, self.ar_counters[0:1])
-            ext.rs_reduce(ar_o, self.flags[FLAG_AR_O], 2 * layer + 1, TIMEOUT_NS, self.status, h, h, None, None,
-                          cfg.rms_eps, step, mul)
-            ext.gemv_swiglu(h, lw.w_gu, lw.ln2, cfg.rms_eps, b["act"][:1])
-            ext.gemv_allreduce(b["act"][:1], lw.w_down, None, cfg.rms_eps, self.ar_d_ptrs, fd, self.rank,
-                               2 * layer + 2, step, mul, self.ar_counters[1:2])
-            ext.rs_reduce(ar_d, self.flags[FLAG_AR_D], 2 * layer + 2, TIMEOUT_NS, self.status, h, h, None, None,
-                          cfg.rms_eps, step, mul)
-        ext.gemv_argmax(h, eng.w.lm_head, eng.w.norm, cfg.rms_eps, b["pv"], b["pi"], b["counter"], b["tok"],
-                        b["log"], b["gen"], eng.w.embed, h, pos, 4)
+            ext.attention_decode(b["q"][:M], slot.k(layer), slot.v(layer), pos[0:1], lc.n_heads, eng.scale, splits,
+                                 b["attn"][:M], ws=b["attn_ws"], counters=b["attn_cnt"])
+            self.allreduce(b["attn"][:M], lw.w_o, 2 * layer + 1, h)
+            ext.gemv_swiglu(h, lw.w_gu, lw.ln2, cfg.rms_eps, b["act"][:M])
+            self.allreduce(b["act"][:M], lw.w_down, 2 * layer + 2, h)
+            if verify and layer in self.seed_layers:
+                feat[self.seed_layers.index(layer), :M].copy_(h)
+        if verify:
+            ext.gemv_argmax(h, eng.w.lm_head, eng.w.norm, cfg.rms_eps, b["pv"], b["pi"], b["counter"], b["tok"],
+                            None, None, None, None, None)
+            ext.bump_counter(pos[3:4])
+        else:
+            ext.gemv_argmax(h, eng.w.lm_head, eng.w.norm, cfg.rms_eps, b["pv"], b["pi"], b["counter"], b["tok"],
+                            b["log"], b["gen"], eng.w.embed, h, pos, 4)
+
+    def set_rows_state(self, position: int) -> None:
+        """Host write of the next rows' position / slot / key count (the step counter pos[3] is kept)."""
+        self.engine._decode_buffers()["pos"][:3].fill_(int(position))
+
+    def verify(self, slot: KVSlot, tokens: torch.Tensor, position: int, *, use_graph: bool = True) -> torch.Tensor:
+        """Forward M <= 8 tokens (device int32, same on every rank) at positions position.. as one step.
+
+        Returns the device argmax after every row; the residual rows after
+        the seed layers are left in the ``tp_feat`` workspace for a drafter.
+        """
+        eng, ext = self.engine, self.ext
+        M = int(tokens.numel())
+        if not 1 <= M <= eng.MAX_ROWS:
+            raise ValueError("verify handles 1..8 rows")
+        b = eng._decode_buffers()
+        splits = eng._decode_splits(slot.capacity)
+        b["ids"][:M].copy_(tokens, non_blocking=True)
+        ext.embedding(b["ids"][:M], eng.w.embed, b["h"][:M])
+        self.set_rows_state(position)
+        if not use_graph:
+            self._decode_step(slot, splits, M, verify=True)
+            return b["tok"][:M]
+        key = ("tpv", id(slot), splits, M)
+        graph = eng._graphs.get(key)
+        if graph is None:
+            # a real warm step (its K/V rows are rewritten by the next verify at
+            # the same positions), then capture; the step counter keeps increasing
+            saved = b["h"][:M].clone()
+            self._decode_step(slot, splits, M, verify=True)
+            b["h"][:M].copy_(saved)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self._decode_step(slot, splits, M, verify=True)
+            eng._graphs[key] = graph
+        graph.replay()
+        ext.launches += 7 * len(eng.w.layers) + 2
+        return b["tok"][:M]
 
     def decode_breakdown(self, slot: KVSlot, reps: int = 3) -> dict[str, float]:
         """Per-op device time of one eager decode step (ms, summed over layers, mean of ``reps``).

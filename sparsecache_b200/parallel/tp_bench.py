@@ -16,6 +16,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import zlib
 from datetime import timedelta
 
 import torch
@@ -30,6 +31,11 @@ BF16_TFLOPS = 1676.9
 NVLINK_GBS = 770.0
 
 
+def stable_seed(*parts) -> int:
+    """Seed from a tuple, identical in every process (``hash`` of a str is salted per process)."""
+    return zlib.crc32(repr(parts).encode()) & 0x7FFFFFFF
+
+
 def random_shard(cfg, rank: int, tp: int, seed: int, device) -> EngineWeights:
     """Seeded random weight shard of ``rank`` (the full model is the concatenation)."""
     lc = local_config(cfg, tp)
@@ -37,12 +43,12 @@ def random_shard(cfg, rank: int, tp: int, seed: int, device) -> EngineWeights:
     gen = torch.Generator(device=device)
 
     def mat(rows, cols, tag):
-        gen.manual_seed(hash((seed, tag, rank)) & 0x7FFFFFFF)
+        gen.manual_seed(stable_seed(seed, tag, rank))
         w = torch.empty(rows, cols, device=device, dtype=bf)
         return w.normal_(0.0, 0.02, generator=gen)
 
     def rep(rows, cols, tag):  # replicated tensors: same on every rank
-        gen.manual_seed(hash((seed, tag)) & 0x7FFFFFFF)
+        gen.manual_seed(stable_seed(seed, tag))
         w = torch.empty(rows, cols, device=device, dtype=bf)
         return w.normal_(0.0, 0.02, generator=gen)
 
