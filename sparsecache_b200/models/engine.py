@@ -435,6 +435,10 @@ class B200Engine:
         grid = self.ext.gemv_argmax_grid(cfg.vocab)
         if "dec_attn_cnt" not in ws.bufs:  # tickets of the cross-cluster merge: zero between launches
             ws.bufs["dec_attn_cnt"] = torch.zeros(cfg.n_kv_heads * 8, device=self.device, dtype=torch.int32)
+        if "dec_pos" not in ws.bufs:
+            # pos[3] is a step counter that tensor-parallel ranks turn into flag
+            # epochs: it must start equal (zero) on every rank
+            ws.bufs["dec_pos"] = torch.zeros(4, device=self.device, dtype=torch.int32)
         return {
             "attn_ws": ws.get("dec_attn_ws", (cfg.n_kv_heads * 16 * 32 * 130,), torch.float32),
             "attn_cnt": ws.bufs["dec_attn_cnt"],

@@ -282,6 +282,7 @@ __device__ __forceinline__ bool wait_shard_ready(const int* flag, int epoch, int
       report_status(status, kStatusTimeoutPeerFlag);
       return false;
     }
+    if (status != nullptr && *((volatile int*)status) != 0) return false;  // another wait failed
     __nanosleep(64);
   }
 }

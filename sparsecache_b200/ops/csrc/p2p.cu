@@ -38,6 +38,9 @@ __global__ void peer_signal_kernel(int* flag, int value, const int* value_src,
 __global__ void wait_flag_kernel(const int* flag, int target, long long timeout_ns, int* status,
                                  unsigned long long* stamp) {
   if (threadIdx.x != 0) return;
+  // an earlier wait on this status already failed: fail fast instead of
+  // spending another full time-out (the host raises at its next check)
+  if (status != nullptr && *((volatile int*)status) != 0) return;
   const unsigned long long start = global_ns();
   while (true) {
     int v;
@@ -100,7 +103,7 @@ __global__ void __launch_bounds__(kRsThreads) rs_reduce_kernel(RsReduceArgs a) {
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
   if (tid == 0) {
-    s_fail = 0;
+    s_fail = (a.status != nullptr && *((volatile int*)a.status) != 0) ? 1 : 0;  // fail fast
     const int epoch = a.epoch_ptr ? *a.epoch_ptr * a.epoch_mul + a.epoch : a.epoch;
     const unsigned long long start = global_ns();
     for (int s = 0; s < a.tp && !s_fail; ++s) {

@@ -35,7 +35,7 @@ __device__ __forceinline__ void st_release(int* p, int v) {
 __device__ bool block_wait_all(const int* flags, int n, int target, long long timeout_ns, int* status) {
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
-    s_ok = 1;
+    s_ok = (status != nullptr && *((volatile int*)status) != 0) ? 0 : 1;  // fail fast after a time-out
     const unsigned long long t0 = now_ns();
     for (int s = 0; s < n && s_ok; ++s) {
       while (ld_acquire(flags + s) < target) {

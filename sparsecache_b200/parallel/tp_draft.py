@@ -320,6 +320,7 @@ def speculative_generate(tpe: TPEngine, drafter: TPEagleDrafter | None, slot, *,
             new = d[:n_acc] + [pred[n_acc]]
             accepted.append(n_acc)
         verifies += 1
+        tpe.check_status()  # the host read above synchronised: a timed-out wait surfaces here
         tokens.extend(new)
         P += len(new)
     return {"tokens": tokens[:max_new], "accepted": accepted, "verify_steps": verifies,

@@ -392,3 +392,25 @@ def test_cacheblend_select(cuda_device, keep_prefix):
     assert torch.equal(active[:n].long(), expect)
     ss = sel.sort().values
     assert int(ck.item()) == int((ss * torch.arange(1, k + 1, device=cuda_device)).sum())
+
+
+def test_bounded_wait_times_out_then_fails_fast(cuda_device):
+    """A flag nothing sets: the wait records a time-out and returns; later waits on the
+    same status return at once; the context stays usable (no GPU fault involved)."""
+    import time
+
+    ext = _ext()
+    flags = torch.zeros(4, dtype=torch.int32, device=cuda_device)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    ext.wait_flag(flags, 1, 1, int(2e6), status)  # 2 ms limit
+    torch.cuda.synchronize()
+    assert int(status.item()) != 0
+    t0 = time.perf_counter()
+    ext.wait_flag(flags, 2, 1, int(10e9), status)  # would wait 10 s without fail-fast
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 1.0
+    status.zero_()
+    flags[2] = 5
+    ext.wait_flag(flags, 2, 5, int(1e9), status)  # satisfied flag, clean status
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
