@@ -62,13 +62,16 @@ class TPRAGServer:
 
     def __init__(self, tpe: TPEngine, *, capacity: int, blend: CacheBlendConfig | None = None,
                  drafter: TPEagleDrafter | None = None, sink: int = 64, recent: int = 512, chunk: int = 64,
-                 budget: int = 2048) -> None:
+                 budget: int = 2048, document_capacity: int | None = None) -> None:
         self.tpe = tpe
         self.blend = blend or CacheBlendConfig()
         self.drafter = drafter
         self.slot = tpe.new_slot(capacity)
         self.store = DocumentKVStore(tpe.lcfg, tier="hbm", device=tpe.engine.device)
-        self._scratch = tpe.new_slot(tpe.max_rows * tpe.tp)
+        # producer slot: one document at a time (padded to the TP row multiple)
+        doc_cap = tpe.max_rows * tpe.tp if document_capacity is None else \
+            -(-int(document_capacity) // (tpe.tp * 128)) * tpe.tp * 128
+        self._scratch = tpe.new_slot(doc_cap)
         self.view_args = dict(sink=sink, recent=recent, chunk=chunk, budget=budget)
 
     # ---------------------------------------------------------- producer
@@ -172,7 +175,7 @@ def main(argv=None) -> None:
                                      view_capacity=4096 + a.new_tokens)
         server = TPRAGServer(tpe, capacity=T_max + a.new_tokens + tp * 128 + 64,
                              blend=CacheBlendConfig(check_layer=a.check_layer, recompute_ratio=a.ratio),
-                             drafter=drafter)
+                             drafter=drafter, document_capacity=doc_max)
         prod = server.produce(reqs)
         torch.cuda.synchronize()
         res = {"ttft_blend": [], "ttft_full": [], "tpot_greedy": [], "tpot_spec": [], "accepted": [],
