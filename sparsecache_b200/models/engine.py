@@ -166,6 +166,12 @@ class PushTarget:
         return self.flags + 4 * index
 
 
+# decode attention cross-cluster merge scratch per kv head: [16 clusters][64 query
+# vectors][max, sum, o[128]] fp32, and one ticket counter per 4-vector z-block
+ATTN_WS_PER_KVH = 16 * 64 * 130
+ATTN_CNT_PER_KVH = 16
+
+
 class _Workspace:
     """Grow-only device scratch buffers, reused across calls (no per-call allocation)."""
 
@@ -434,13 +440,14 @@ class B200Engine:
         cfg, ws, R = self.cfg, self.ws, self.MAX_ROWS
         grid = self.ext.gemv_argmax_grid(cfg.vocab)
         if "dec_attn_cnt" not in ws.bufs:  # tickets of the cross-cluster merge: zero between launches
-            ws.bufs["dec_attn_cnt"] = torch.zeros(cfg.n_kv_heads * 8, device=self.device, dtype=torch.int32)
+            ws.bufs["dec_attn_cnt"] = torch.zeros(cfg.n_kv_heads * ATTN_CNT_PER_KVH, device=self.device,
+                                                  dtype=torch.int32)
         if "dec_pos" not in ws.bufs:
             # pos[3] is a step counter that tensor-parallel ranks turn into flag
             # epochs: it must start equal (zero) on every rank
             ws.bufs["dec_pos"] = torch.zeros(4, device=self.device, dtype=torch.int32)
         return {
-            "attn_ws": ws.get("dec_attn_ws", (cfg.n_kv_heads * 16 * 32 * 130,), torch.float32),
+            "attn_ws": ws.get("dec_attn_ws", (cfg.n_kv_heads * ATTN_WS_PER_KVH,), torch.float32),
             "attn_cnt": ws.bufs["dec_attn_cnt"],
             "h": ws.get("dec_h", (R, cfg.d_model), torch.bfloat16),
             "q": ws.get("dec_q", (R, cfg.q_size), torch.bfloat16),

@@ -30,7 +30,7 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kSub = 64;      // minimum keys per CTA for 16-CTA clusters
-constexpr int kMaxQV = 32;    // M * G
+constexpr int kMaxQV = 64;    // M * G (M <= 8 rows, G <= 8 query heads per kv head)
 constexpr int kMaxRows = 8;   // largest query block M
 constexpr int kMaxOuter = 16; // clusters per kv head (second split level)
 

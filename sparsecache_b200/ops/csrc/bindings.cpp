@@ -582,8 +582,8 @@ void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int6
   if (ws.has_value() && ws->defined()) {
     TORCH_CHECK(counters.has_value() && counters->defined(), "counters required with ws");
     CHECK_F32(*ws); CHECK_I32(*counters);
-    TORCH_CHECK(ws->numel() >= (int64_t)a.n_kv_heads * 16 * 32 * 130, "ws too small");
-    TORCH_CHECK(counters->numel() >= (int64_t)a.n_kv_heads * 8, "8 counters per kv head");
+    TORCH_CHECK(ws->numel() >= (int64_t)a.n_kv_heads * 16 * 64 * 130, "ws too small");
+    TORCH_CHECK(counters->numel() >= (int64_t)a.n_kv_heads * 16, "16 counters per kv head");
     a.ws = ws->data_ptr<float>();
     a.counters = reinterpret_cast<unsigned*>(counters->data_ptr<int>());
   }

@@ -79,7 +79,11 @@ __device__ __forceinline__ void load_batch(const uint4* w0, const uint4* w1, int
 
 }  // namespace
 
-template <int MR>
+// kXG: x is read from global memory (L1/L2-resident) instead of being staged
+// in shared memory; used when M * K * 2 bytes exceed the shared-memory budget
+// (the batched verifier's down projection at large FFN widths).  No prologue
+// RMSNorm in that mode.
+template <int MR, bool kXG = false>
 __global__ void __launch_bounds__(kThreads)
     gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
@@ -111,7 +115,9 @@ __global__ void __launch_bounds__(kThreads)
   pdl_launch_dependents();
 
   // ---- stage x (optionally RMS-normalised) into shared memory ----
-  if (a.norm_w == nullptr) {
+  if (kXG) {
+    // x stays in global memory
+  } else if (a.norm_w == nullptr) {
     for (int m = 0; m < M; ++m) {
       const uint4* src = reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx);
       uint4* dst = reinterpret_cast<uint4*>(xs + (size_t)m * K);
@@ -165,7 +171,7 @@ __global__ void __launch_bounds__(kThreads)
   }
   __syncthreads();
 
-  const uint4* xs4 = reinterpret_cast<const uint4*>(xs);
+  const uint4* xs4 = kXG ? reinterpret_cast<const uint4*>(a.x) : reinterpret_cast<const uint4*>(xs);
   const int pos0 = (a.epi == GEMV_QKV) ? *a.pos : 0;
   const int slot0 = (a.epi == GEMV_QKV) ? (a.slot != nullptr ? *a.slot : pos0) : 0;
 
@@ -193,7 +199,7 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
           for (int m = 0; m < MR; ++m) {
             if (m < M) {
-              const uint4 xv = xs4[m * nchunk + c];
+              const uint4 xv = kXG ? __ldg(xs4 + m * nchunk + c) : xs4[m * nchunk + c];
               acc0[m] += dot8(wa[u], xv);
               acc1[m] += dot8(wb[u], xv);
             }
@@ -361,7 +367,8 @@ __global__ void __launch_bounds__(kThreads)
 cudaError_t gemv_bf16(const GemvArgs& a, cudaStream_t stream) {
   if (a.M < 1 || a.M > 8 || (a.K % 8) != 0 || (a.N % 2) != 0) return cudaErrorInvalidValue;
   const size_t smem = (size_t)a.M * a.K * 2;
-  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  const bool xg = smem > 200 * 1024;
+  if (xg && (a.norm_w != nullptr || a.ldx != a.K || a.M <= 2)) return cudaErrorInvalidValue;
   const int n_pairs = a.N / 2;
   int grid = (n_pairs + kWarps - 1) / kWarps;
   const int cap = (a.num_sms > 0 ? a.num_sms : 148) * 8;
@@ -369,7 +376,7 @@ cudaError_t gemv_bf16(const GemvArgs& a, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = xg ? 0 : smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -380,6 +387,10 @@ cudaError_t gemv_bf16(const GemvArgs& a, cudaStream_t stream) {
   {                                                                \
     ensure_smem_attr(gemv_kernel<MRV>, 200 * 1024);                \
     return cudaLaunchKernelEx(&cfg, gemv_kernel<MRV>, a);          \
+  }
+  if (xg) {
+    if (a.M <= 4) return cudaLaunchKernelEx(&cfg, gemv_kernel<4, true>, a);
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<8, true>, a);
   }
   if (a.M == 1) SC_LAUNCH_GEMV(1)
   else if (a.M <= 2) SC_LAUNCH_GEMV(2)

@@ -17,6 +17,8 @@ import math
 
 import torch
 
+from ..models.engine import ATTN_CNT_PER_KVH, ATTN_WS_PER_KVH
+
 HBM_GBS = 6456.5
 BF16_TFLOPS = 1676.9
 
@@ -106,8 +108,8 @@ def main() -> None:
                 for s_try in (4, 8, 16):
                     t_s = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), s_try, out))
                     res[f"attn_decode_ctx{cap}_S{s_try}"] = {"us": t_s}
-            ws = torch.zeros(Hkv * 16 * 32 * 130, device=dev)
-            cnt = torch.zeros(Hkv * 8, device=dev, dtype=torch.int32)
+            ws = torch.zeros(Hkv * ATTN_WS_PER_KVH, device=dev)
+            cnt = torch.zeros(Hkv * ATTN_CNT_PER_KVH, device=dev, dtype=torch.int32)
             R = int(ext.attention_decode_outer(cap, Hkv, S, ext.num_sms()))
             t = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), S, out, ws=ws,
                                                     counters=cnt))
@@ -125,8 +127,8 @@ def main() -> None:
             q = torch.randn(1, H * 128, device=dev).to(bf)
             pos = torch.tensor([cap - 16], device=dev, dtype=torch.int32)
             out = torch.empty(1, H * 128, device=dev, dtype=bf)
-            ws = torch.zeros(Hkv * 16 * 32 * 130, device=dev)
-            cnt = torch.zeros(Hkv * 8, device=dev, dtype=torch.int32)
+            ws = torch.zeros(Hkv * ATTN_WS_PER_KVH, device=dev)
+            cnt = torch.zeros(Hkv * ATTN_CNT_PER_KVH, device=dev, dtype=torch.int32)
             for S in (4, 8, 16):
                 for two in (False, True):
                     kw = {"ws": ws, "counters": cnt} if two else {}
@@ -142,8 +144,8 @@ def main() -> None:
         q = torch.randn(1, H * 128, device=dev).to(bf)
         pos = torch.tensor([cap - 16], device=dev, dtype=torch.int32)
         out = torch.empty(1, H * 128, device=dev, dtype=bf)
-        ws = torch.zeros(Hkv * 16 * 32 * 130, device=dev)
-        cnt = torch.zeros(Hkv * 8, device=dev, dtype=torch.int32)
+        ws = torch.zeros(Hkv * ATTN_WS_PER_KVH, device=dev)
+        cnt = torch.zeros(Hkv * ATTN_CNT_PER_KVH, device=dev, dtype=torch.int32)
         kv_bytes = 2 * Hkv * (cap - 15) * 128 * 2
         for name, S, kw in (("one_cluster", 16, {}), ("two_level", int(ext.attention_decode_cluster(cap, Hkv)),
                                                           {"ws": ws, "counters": cnt})):

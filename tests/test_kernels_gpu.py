@@ -219,8 +219,8 @@ def test_attention_decode_two_level_split(cuda_device, M, hkv, cap):
     n = pos0 + M
     ref = _attn_reference(q, kc[:, :n], vc[:, :n], pos0 + torch.arange(M, device=cuda_device),
                           torch.arange(n, device=cuda_device), H)
-    ws = torch.zeros(hkv * 16 * 32 * 130, device=cuda_device)
-    cnt = torch.zeros(hkv * 8, device=cuda_device, dtype=torch.int32)
+    ws = torch.zeros(hkv * 16 * 64 * 130, device=cuda_device)
+    cnt = torch.zeros(hkv * 16, device=cuda_device, dtype=torch.int32)
     S = _ext().attention_decode_cluster(cap, hkv)
     outer = _ext().attention_decode_outer(cap, hkv, S, _ext().num_sms())
     assert S == 4 and outer > 1
@@ -414,3 +414,23 @@ def test_bounded_wait_times_out_then_fails_fast(cuda_device):
     ext.wait_flag(flags, 2, 5, int(1e9), status)  # satisfied flag, clean status
     torch.cuda.synchronize()
     assert int(status.item()) == 0
+
+
+@pytest.mark.parametrize("M", [3, 5, 8])
+def test_gemv_wide_k_reads_x_from_global(cuda_device, M):
+    """M * K * 2 bytes above the shared-memory budget (verify rows x a 28672-wide FFN):
+    x is read from global memory; rows are independent of M."""
+    K, N = 28672, 1024
+    x = (torch.randn(M, K, device=cuda_device) * 0.1).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda_device) * 0.02).to(torch.bfloat16)
+    res = torch.randn(M, N, device=cuda_device).to(torch.bfloat16)
+    out = res.clone()
+    ext = _ext()
+    ext.gemv_residual(x, w, None, 1e-5, out, out)
+    one = res[:1].clone()
+    ext.gemv_residual(x[:1].contiguous(), w, None, 1e-5, one, one)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    ref = res.float() + (x.float() @ w.float().T).to(torch.bfloat16).float()
+    assert _rel_err(out, ref) < 1e-2
+    assert torch.equal(out[:1], one)  # the row does not depend on how many rows share the launch
