@@ -46,6 +46,19 @@ __device__ __forceinline__ float dot8(const uint4 w, const uint4 x) {
   return s;
 }
 
+__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
+  const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y), c = unpack_bf16x2(v.z), d = unpack_bf16x2(v.w);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+
+// Same product order as dot8 (one rounding chain per 8 elements).
+__device__ __forceinline__ float dot8f(const float (&w)[8], const float (&x)[8]) {
+  float s = w[0] * x[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) s = fmaf(w[i], x[i], s);
+  return s;
+}
+
 // Pair p -> the two weight rows it reads.
 __device__ __forceinline__ void pair_rows(int epi, int p, int& r0, int& r1) {
   if (epi == GEMV_QKV) {
@@ -196,12 +209,23 @@ __global__ void __launch_bounds__(kThreads)
       for (int u = 0; u < kUnroll; ++u) {
         const int c = c0 + u * 32;
         if (c < nchunk) {
+          if (MR == 1) {
+            const uint4 xv = kXG ? __ldg(xs4 + c) : xs4[c];
+            acc0[0] += dot8(wa[u], xv);
+            acc1[0] += dot8(wb[u], xv);
+          } else {
+            // several rows: unpack the weight pair once, each row's x once
+            float w0[8], w1[8];
+            unpack8(wa[u], w0);
+            unpack8(wb[u], w1);
 #pragma unroll
-          for (int m = 0; m < MR; ++m) {
-            if (m < M) {
-              const uint4 xv = kXG ? __ldg(xs4 + m * nchunk + c) : xs4[m * nchunk + c];
-              acc0[m] += dot8(wa[u], xv);
-              acc1[m] += dot8(wb[u], xv);
+            for (int m = 0; m < MR; ++m) {
+              if (m < M) {
+                float xf[8];
+                unpack8(kXG ? __ldg(xs4 + m * nchunk + c) : xs4[m * nchunk + c], xf);
+                acc0[m] += dot8f(w0, xf);
+                acc1[m] += dot8f(w1, xf);
+              }
             }
           }
         }

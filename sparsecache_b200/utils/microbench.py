@@ -48,6 +48,23 @@ def main() -> None:
     res: dict[str, dict] = {}
     bf = torch.bfloat16
 
+    if "gemv_rows" in only:
+        # batched-verify rows at 70B widths (one GPU): weight bytes per launch / time
+        for name, N, K in (("qkv", 10240, 8192), ("down", 8192, 28672), ("gate_up", 57344, 8192)):
+            w = (torch.randn(N, K, device=dev) * 0.02).to(bf)
+            for M in (1, 2, 5, 8):
+                x = torch.randn(M, K, device=dev).to(bf)
+                if name == "gate_up":
+                    o = torch.empty(M, N // 2, device=dev, dtype=bf)
+                    fn = lambda: ext.gemv_swiglu(x, w, None, 1e-5, o)  # noqa: E731
+                else:
+                    o = torch.empty(M, N, device=dev, dtype=bf)
+                    fn = lambda: ext.gemv_residual(x, w, None, 1e-5, o, o)  # noqa: E731
+                t = timeit(fn, n=20, warm=5)
+                gbs = N * K * 2 / (t * 1e-6) / 1e9
+                res[f"gemv_rows_{name}_M{M}"] = {"us": t, "GBps": gbs, "frac_of_measured_hbm": gbs / HBM_GBS}
+            del w
+
     if "gemv" in only:
         for name, N, K in (("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 28672, 4096),
                            ("down", 4096, 14336), ("lm_head", 128256, 4096)):
