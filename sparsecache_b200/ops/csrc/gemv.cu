@@ -30,33 +30,26 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kUnroll = 8;
 
-__device__ __forceinline__ float dot8(const uint4 w, const uint4 x) {
-  float2 w0 = unpack_bf16x2(w.x), w1 = unpack_bf16x2(w.y), w2 = unpack_bf16x2(w.z),
-         w3 = unpack_bf16x2(w.w);
-  float2 x0 = unpack_bf16x2(x.x), x1 = unpack_bf16x2(x.y), x2 = unpack_bf16x2(x.z),
-         x3 = unpack_bf16x2(x.w);
-  float s = w0.x * x0.x;
-  s = fmaf(w0.y, x0.y, s);
-  s = fmaf(w1.x, x1.x, s);
-  s = fmaf(w1.y, x1.y, s);
-  s = fmaf(w2.x, x2.x, s);
-  s = fmaf(w2.y, x2.y, s);
-  s = fmaf(w3.x, x3.x, s);
-  s = fmaf(w3.y, x3.y, s);
-  return s;
+// Inner product: bf16 pairs widened into packed fp32x2 registers and
+// multiplied with the sm_100 two-lane FMA (fma.rn.f32x2), which halves the
+// FMA instructions per weight; each row keeps two interleaved fp32 chains
+// (even / odd elements) that are added at the end.
+typedef unsigned long long f32x2;
+
+__device__ __forceinline__ f32x2 widen_bf16x2(uint32_t v) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(v << 16), "r"(v & 0xffff0000u));
+  return r;
 }
 
-__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
-  const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y), c = unpack_bf16x2(v.z), d = unpack_bf16x2(v.w);
-  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+__device__ __forceinline__ void fma2(f32x2& acc, f32x2 a, f32x2 b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
 }
 
-// Same product order as dot8 (one rounding chain per 8 elements).
-__device__ __forceinline__ float dot8f(const float (&w)[8], const float (&x)[8]) {
-  float s = w[0] * x[0];
-#pragma unroll
-  for (int i = 1; i < 8; ++i) s = fmaf(w[i], x[i], s);
-  return s;
+__device__ __forceinline__ float sum2(f32x2 v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo + hi;
 }
 
 // Pair p -> the two weight rows it reads.
@@ -200,8 +193,9 @@ __global__ void __launch_bounds__(kThreads)
     const uint4* w0 = reinterpret_cast<const uint4*>(a.w + (size_t)r0 * K);
     const uint4* w1 = reinterpret_cast<const uint4*>(a.w + (size_t)r1 * K);
     float acc0[MR], acc1[MR];
+    f32x2 pacc0[MR], pacc1[MR];  // multi-row accumulators (packed even / odd chains)
 #pragma unroll
-    for (int m = 0; m < MR; ++m) acc0[m] = acc1[m] = 0.f;
+    for (int m = 0; m < MR; ++m) acc0[m] = acc1[m] = 0.f, pacc0[m] = pacc1[m] = 0ull;
     for (int c0 = lane; c0 < nchunk; c0 += 32 * kUnroll) {
       if (!preloaded) load_batch(w0, w1, c0, nchunk, wa, wb);
       preloaded = false;
@@ -209,28 +203,32 @@ __global__ void __launch_bounds__(kThreads)
       for (int u = 0; u < kUnroll; ++u) {
         const int c = c0 + u * 32;
         if (c < nchunk) {
-          if (MR == 1) {
-            const uint4 xv = kXG ? __ldg(xs4 + c) : xs4[c];
-            acc0[0] += dot8(wa[u], xv);
-            acc1[0] += dot8(wb[u], xv);
-          } else {
-            // several rows: unpack the weight pair once, each row's x once
-            float w0[8], w1[8];
-            unpack8(wa[u], w0);
-            unpack8(wb[u], w1);
+          {
+            // widen the weight pair once and each row's x once; the same
+            // arithmetic for every M keeps a row's result independent of M
+            const f32x2 w0[4] = {widen_bf16x2(wa[u].x), widen_bf16x2(wa[u].y), widen_bf16x2(wa[u].z),
+                                 widen_bf16x2(wa[u].w)};
+            const f32x2 w1[4] = {widen_bf16x2(wb[u].x), widen_bf16x2(wb[u].y), widen_bf16x2(wb[u].z),
+                                 widen_bf16x2(wb[u].w)};
 #pragma unroll
             for (int m = 0; m < MR; ++m) {
               if (m < M) {
-                float xf[8];
-                unpack8(kXG ? __ldg(xs4 + m * nchunk + c) : xs4[m * nchunk + c], xf);
-                acc0[m] += dot8f(w0, xf);
-                acc1[m] += dot8f(w1, xf);
+                const uint4 xv = kXG ? __ldg(xs4 + m * nchunk + c) : xs4[m * nchunk + c];
+                const f32x2 xf[4] = {widen_bf16x2(xv.x), widen_bf16x2(xv.y), widen_bf16x2(xv.z),
+                                     widen_bf16x2(xv.w)};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  fma2(pacc0[m], w0[i], xf[i]);
+                  fma2(pacc1[m], w1[i], xf[i]);
+                }
               }
             }
           }
         }
       }
     }
+#pragma unroll
+    for (int m = 0; m < MR; ++m) acc0[m] = sum2(pacc0[m]), acc1[m] = sum2(pacc1[m]);
 #pragma unroll
     for (int m = 0; m < MR; ++m) {
       acc0[m] = warp_sum(acc0[m]);
