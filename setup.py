@@ -25,7 +25,7 @@ NVCC_FLAGS = [
 ext = CUDAExtension(
     name="sparsecache_b200.ops._C",
     sources=[str(p.relative_to(ROOT)) for p in sorted(CSRC.glob("*.cu"))]
-    + [str((CSRC / "bindings.cpp").relative_to(ROOT))],
+    + [str(p.relative_to(ROOT)) for p in sorted(CSRC.glob("*.cpp"))],
     include_dirs=[str(CSRC)],
     extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
 )

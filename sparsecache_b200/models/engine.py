@@ -304,16 +304,24 @@ class B200Engine:
 
     # ----------------------------------------------------------- compose
     def compose(self, slot: KVSlot, blocks, *, first_slot: int, layer_begin: int = 0,
-                source_positions=None, target_positions=None) -> None:
+                source_positions=None, target_positions=None, layer_end: int | None = None) -> None:
         """Gather document K/V blocks into ``slot`` after ``first_slot`` and re-rotate keys.
 
         ``blocks`` are [L, 2, H_kv, n, D] tensors in HBM or pinned host memory
         (the kernel reads mapped host memory directly).  Document i lands at
         slots cursor..cursor+n-1; its keys move from source position
         ``source_positions[i]`` (0 for independently produced documents) to
-        ``target_positions[i]`` (default: its slot).  Layers below
-        ``layer_begin`` are skipped: CacheBlend recomputes them fully.
+        ``target_positions[i]`` (default: its slot).  Layers outside
+        [layer_begin, layer_end) are skipped: CacheBlend recomputes the layers
+        below the check layer fully.
         """
+        table = self.compose_table(slot, blocks, first_slot=first_slot, source_positions=source_positions,
+                                   target_positions=target_positions)
+        self.compose_layers(slot, table, layer_begin, self.cfg.n_layers if layer_end is None else layer_end)
+
+    def compose_table(self, slot: KVSlot, blocks, *, first_slot: int, source_positions=None,
+                      target_positions=None) -> tuple[torch.Tensor, torch.Tensor, int]:
+        """Device table of the composer: (docs [n, 6] int32, token offsets [n + 1], total tokens)."""
         rows, offsets, cursor = [], [0], first_slot
         for i, block in enumerate(blocks):
             n = int(block.shape[3])
@@ -332,10 +340,13 @@ class B200Engine:
         host[len(rows) * 6 :] = torch.tensor(offsets, dtype=torch.int32)
         dev = self.ws.get("compose_meta", (host.numel(),), torch.int32)
         dev.copy_(host, non_blocking=True)
-        docs = dev[: len(rows) * 6].view(len(rows), 6)
-        offs = dev[len(rows) * 6 :]
-        self.ext.compose_relocate(docs, offs, offsets[-1], layer_begin, self.cfg.n_layers, self.cfg.n_layers,
-                                  slot.data, self.cfg.n_kv_heads, self.rope)
+        return dev[: len(rows) * 6].view(len(rows), 6), dev[len(rows) * 6 :], offsets[-1]
+
+    def compose_layers(self, slot: KVSlot, table, layer_begin: int, layer_end: int) -> None:
+        """Run the composer over layers [layer_begin, layer_end) of a ``compose_table``."""
+        docs, offs, total = table
+        self.ext.compose_relocate(docs, offs, total, layer_begin, layer_end, self.cfg.n_layers, slot.data,
+                                  self.cfg.n_kv_heads, self.rope)
 
     # ------------------------------------------------------------ passes
     def embed(self, ids: torch.Tensor, name: str = "h") -> torch.Tensor:
@@ -375,12 +386,15 @@ class B200Engine:
         suffix_tokens: int,
         blend: CacheBlendConfig,
         global_positions: torch.Tensor | None = None,
+        before_layer=None,
     ) -> tuple[torch.Tensor, int, dict]:
         """Selective recompute over the composed cache already in ``slot``.
 
         Returns (hidden of the active rows [A, d], A, device-side metadata).
         The number of active rows A is known on the host (no sync):
         prefix (strict protocol) + ceil(ratio * N_doc) + suffix.
+        ``before_layer(layer)`` runs before each layer's kernels are issued
+        (layer-wise cache arrival: wait for the layer, compose it).
         """
         cfg, ext = self.cfg, self.ext
         T = ids.numel()
@@ -400,9 +414,13 @@ class B200Engine:
         gpos = rows if global_positions is None else global_positions
         kpos = global_positions  # None -> key position == slot
         for layer in range(check):
+            if before_layer is not None:
+                before_layer(layer)
             q = self._full_layer(layer, h, slot, gpos, rows, T, kpos)
             self._attn_mlp(layer, h, q, slot, q_rows=None, qpos=gpos, n_keys=T, kpos=kpos, n_rows=T)
         # ---- check layer ----
+        if before_layer is not None:
+            before_layer(check)
         dev_part = self.ws.get("dev", (T, 2 * cfg.n_kv_heads), torch.float32)
         q = self._full_layer(check, h, slot, gpos, rows, T, kpos, dev_part, blend.dev_mode)
         active = self._i32("active", T)
@@ -419,6 +437,8 @@ class B200Engine:
         self._attn_mlp(check, h_a, q, slot, q_rows=act_rows, qpos=qpos_a, n_keys=T, kpos=kpos, n_rows=A)
         # ---- later layers: active rows only ----
         for layer in range(check + 1, cfg.n_layers):
+            if before_layer is not None:
+                before_layer(layer)
             qa = self._full_layer(layer, h_a, slot, qpos_a, act_rows, T, kpos)
             self._attn_mlp(layer, h_a, qa, slot, q_rows=None, qpos=qpos_a, n_keys=T, kpos=kpos, n_rows=A)
         meta = {"active": act_rows, "n_active": n_active, "checksum": checksum, "k_selected": k_sel,
