@@ -687,6 +687,53 @@ void cacheblend_select(Tensor dev_part, int64_t n_kv_heads, int64_t dev_mode, in
   check_cuda(sc::cacheblend_select(a, cur_stream()), "cacheblend_select");
 }
 
+sc::LseGatherArgs lse_args(const Tensor& logits, const Tensor& ids, const Tensor& lse) {
+  check_matrix(logits, "logits");
+  CHECK_I32(ids); CHECK_F32(lse);
+  TORCH_CHECK(ids.dim() == 2 && ids.size(0) == logits.size(0) && ids.is_contiguous(), "ids [R, G]");
+  TORCH_CHECK(lse.numel() == logits.size(0) && lse.is_contiguous(), "lse [R]");
+  TORCH_CHECK(logits.size(1) % 8 == 0, "vocabulary must be a multiple of 8");
+  sc::LseGatherArgs a{};
+  a.logits = reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr());
+  a.ld = (int)logits.stride(0);
+  a.R = (int)logits.size(0);
+  a.V = (int)logits.size(1);
+  a.ids = ids.data_ptr<int>();
+  a.G = (int)ids.size(1);
+  a.lse = lse.data_ptr<float>();
+  return a;
+}
+
+void lse_gather(Tensor logits, Tensor ids, Tensor lse, Tensor z) {
+  const c10::cuda::CUDAGuard guard(logits.device());
+  auto a = lse_args(logits, ids, lse);
+  CHECK_F32(z);
+  TORCH_CHECK(z.sizes() == ids.sizes() && z.is_contiguous(), "z [R, G]");
+  a.z = z.data_ptr<float>();
+  check_cuda(sc::lse_gather(a, cur_stream()), "lse_gather");
+}
+
+void lse_gather_backward(Tensor logits, Tensor ids, Tensor lse, c10::optional<Tensor> g_lse,
+                         c10::optional<Tensor> g_z, Tensor dlogits) {
+  const c10::cuda::CUDAGuard guard(logits.device());
+  auto a = lse_args(logits, ids, lse);
+  check_matrix(dlogits, "dlogits");
+  TORCH_CHECK(dlogits.sizes() == logits.sizes(), "dlogits shape");
+  if (g_lse.has_value() && g_lse->defined()) {
+    CHECK_F32(*g_lse);
+    TORCH_CHECK(g_lse->numel() == a.R && g_lse->is_contiguous(), "g_lse [R]");
+    a.g_lse = g_lse->data_ptr<float>();
+  }
+  if (g_z.has_value() && g_z->defined()) {
+    CHECK_F32(*g_z);
+    TORCH_CHECK(g_z->sizes() == ids.sizes() && g_z->is_contiguous(), "g_z [R, G]");
+    a.g_z = g_z->data_ptr<float>();
+  }
+  a.dlogits = reinterpret_cast<__nv_bfloat16*>(dlogits.data_ptr());
+  a.ldd = (int)dlogits.stride(0);
+  check_cuda(sc::lse_gather_backward(a, cur_stream()), "lse_gather_backward");
+}
+
 void arange_i32(Tensor out, int64_t start) {
   const c10::cuda::CUDAGuard guard(out.device());
   CHECK_I32(out);
@@ -938,6 +985,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("active"), py::arg("n_active"), py::arg("scores"), py::arg("checksum") = py::none(),
         py::arg("n_parts") = 1, py::arg("part_stride") = 0);
   m.def("arange_i32", &arange_i32);
+  m.def("lse_gather", &lse_gather);
+  m.def("lse_gather_backward", &lse_gather_backward, py::arg("logits"), py::arg("ids"), py::arg("lse"),
+        py::arg("g_lse"), py::arg("g_z"), py::arg("dlogits"));
   m.def("index_i32", &index_i32);
   m.def("status", &status);
   m.def("num_sms", &num_sms);

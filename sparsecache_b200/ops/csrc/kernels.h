@@ -250,6 +250,23 @@ struct SelectArgs {
 };
 cudaError_t cacheblend_select(const SelectArgs& a, cudaStream_t stream);
 
+// Row log-sum-exp + logit gathers (forward) and the logits gradient
+// g_lse * softmax + sum_j g_z[j] * onehot(ids[j]) (backward), lm_loss.cu.
+struct LseGatherArgs {
+  const __nv_bfloat16* logits;  // [R, V] row stride ld
+  int ld, R, V;
+  const int* ids;  // [R, G], -1 = no id
+  int G;
+  float* lse;      // [R]
+  float* z;        // [R, G]
+  const float* g_lse;  // backward inputs (g_lse may be null)
+  const float* g_z;
+  __nv_bfloat16* dlogits;  // [R, V] row stride ldd (may alias logits)
+  int ldd;
+};
+cudaError_t lse_gather(const LseGatherArgs& a, cudaStream_t stream);
+cudaError_t lse_gather_backward(const LseGatherArgs& a, cudaStream_t stream);
+
 cudaError_t fill_arange_i32(int* out, int n, int start, cudaStream_t stream);
 
 // Owner-side reduction of GEMM -> reduce-scatter partials: waits (bounded)

@@ -48,7 +48,8 @@ from .. import ops
 from ..models.sparse_kv_draft import accepted_prefix_length
 from ..models.sparse_kv_eagle import SparseKVEagleConfig, SparseKVEagleDrafter
 from ..ops.sparse_attention import MemoryBatch
-from .losses import compressed_distillation_loss, compressed_target_score, feature_distillation_loss
+from .losses import (compressed_distillation_from_lse, compressed_distillation_loss, compressed_id_table,
+                     compressed_target_score, compressed_target_score_from_lse, feature_distillation_loss)
 from .teacher import DeviceTeacherBank, pick_mismatched
 
 ADAPTER_FORMAT = "sparsecache.sparse-kv-eagle-adapter.v2"
@@ -353,6 +354,13 @@ class EagleDrafterTrainer:
         if self.device.type == "cuda":
             self._pinned = self._pinned.pin_memory()
         self.launches_per_step: int | None = None
+        # frozen LM head: logits go through the fused log-sum-exp / gather path
+        # (no fp32 [rows, vocab] tensors); a trainable head keeps plain logits
+        self.head = None
+        if not model.lm_head.weight.requires_grad:
+            from ..ops.lm_loss import FrozenLMHead
+
+            self.head = FrozenLMHead(model.lm_head.weight)
 
     # ------------------------------------------------------------ batching
     def batch_indices(self, step: int) -> tuple[list[int], list[int]]:
@@ -388,11 +396,29 @@ class EagleDrafterTrainer:
         B = idx.shape[0]
         with torch.autocast("cuda", dtype=torch.bfloat16, enabled=self.device.type == "cuda"):
             feats = model.recurrent_forward(two(ids), two(seeds), mem, None, two(cos), two(sin), two(stage))
-            logits = model.lm_head(feats)
-            pos_logits, neg_logits = logits[:B], logits[B:]
-            loss, comps = compressed_distillation_loss(
-                model, pos_logits, labels, top_ids, top_lp, prefix_decay=cfg.prefix_decay,
-                hard_weight=cfg.hard_weight, soft_weight=cfg.soft_weight, check_coverage=False)
+            if self.head is not None:
+                # positive rows: label + teacher top-k; contrast rows: label only (-1 padded)
+                table = compressed_id_table(model, labels, top_ids)
+                neg_table = torch.full_like(table, -1)
+                neg_table[..., 0] = table[..., 0]
+                t_all = torch.cat((table, neg_table))
+                lse, z = self.head.lse_gather(feats.reshape(-1, feats.shape[-1]), t_all.reshape(2 * B * t, -1))
+                lse, z = lse.view(2 * B, t), z.view(2 * B, t, -1)
+                loss, comps = compressed_distillation_from_lse(
+                    lse[:B], z[:B], table, top_lp, prefix_decay=cfg.prefix_decay, hard_weight=cfg.hard_weight,
+                    soft_weight=cfg.soft_weight, check_coverage=False)
+                pos_score = compressed_target_score_from_lse(lse[:B], z[:B, :, 0], table[..., 0],
+                                                             prefix_decay=cfg.prefix_decay)
+                neg_score = compressed_target_score_from_lse(lse[B:], z[B:, :, 0], table[..., 0],
+                                                             prefix_decay=cfg.prefix_decay)
+            else:
+                logits = model.lm_head(feats)
+                pos_logits, neg_logits = logits[:B], logits[B:]
+                loss, comps = compressed_distillation_loss(
+                    model, pos_logits, labels, top_ids, top_lp, prefix_decay=cfg.prefix_decay,
+                    hard_weight=cfg.hard_weight, soft_weight=cfg.soft_weight, check_coverage=False)
+                pos_score = compressed_target_score(model, pos_logits, labels, prefix_decay=cfg.prefix_decay)
+                neg_score = compressed_target_score(model, neg_logits, labels, prefix_decay=cfg.prefix_decay)
             if cfg.feature_weight > 0.0:
                 if bank.teacher_hidden is None:
                     raise ValueError("feature loss requires teacher hidden states")
@@ -400,13 +426,18 @@ class EagleDrafterTrainer:
                 f_loss = feature_distillation_loss(feats[:B], th, prefix_decay=cfg.prefix_decay)
                 loss = loss + cfg.feature_weight * f_loss
                 comps["feature_loss"] = f_loss.detach()
-            pos_score = compressed_target_score(model, pos_logits, labels, prefix_decay=cfg.prefix_decay)
-            neg_score = compressed_target_score(model, neg_logits, labels, prefix_decay=cfg.prefix_decay)
             contrast = F.relu(cfg.contrast_margin - pos_score + neg_score).mean()
             with torch.no_grad():
                 base_feats = model.recurrent_forward(ids, seeds, None, None, cos, sin, stage, use_memory=False)
-                base_score = compressed_target_score(model, model.lm_head(base_feats), labels,
-                                                     prefix_decay=cfg.prefix_decay)
+                if self.head is not None:
+                    d_lab = model.draft_ids(labels)
+                    b_lse, b_z = self.head.lse_gather(base_feats.reshape(-1, base_feats.shape[-1]),
+                                                      d_lab.reshape(-1, 1))
+                    base_score = compressed_target_score_from_lse(b_lse.view(B, t), b_z.view(B, t), d_lab,
+                                                                  prefix_decay=cfg.prefix_decay)
+                else:
+                    base_score = compressed_target_score(model, model.lm_head(base_feats), labels,
+                                                         prefix_decay=cfg.prefix_decay)
             base_contrast = F.relu(cfg.contrast_margin / 2 - pos_score + base_score).mean()
             loss = loss + cfg.contrast_weight * contrast + cfg.base_contrast_weight * base_contrast
         loss.backward()

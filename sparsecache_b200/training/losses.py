@@ -11,6 +11,9 @@ Same definitions as the reference trainers:
   * ``compressed_distillation_loss`` / ``compressed_target_score``: the same
     losses in EAGLE's compressed draft vocabulary, skipping labels and
     teacher ids that have no draft id (experiments/train_sparse_kv_eagle.py:97-175).
+    They are written on (row log-sum-exp, logits at the label / top-k ids):
+    logp[id] = z[id] - lse, so the ``*_from_lse`` forms take the output of
+    the fused LM-head path (``ops.lm_loss``) and never need [B, t, V].
 
 Every function accepts a leading batch dimension (``[B, t, V]`` logits and
 ``[B, t]`` labels) in addition to the reference's batch-1 shapes; the batch
@@ -99,6 +102,70 @@ def target_sequence_score(logits: torch.Tensor, labels: torch.Tensor, *, prefix_
     return score if batched else score[0]
 
 
+def compressed_id_table(model, labels: torch.Tensor, teacher_ids: torch.Tensor | None) -> torch.Tensor:
+    """Draft-vocabulary id table [B, t, 1 + K]: the label, then the teacher top-k (-1 = unmapped)."""
+    d_lab = model.draft_ids(labels).unsqueeze(-1)
+    if teacher_ids is None:
+        return d_lab
+    ids = teacher_ids if teacher_ids.ndim == 3 else teacher_ids.unsqueeze(0)
+    return torch.cat((d_lab, model.draft_ids(ids)), dim=-1)
+
+
+def compressed_distillation_from_lse(
+    lse: torch.Tensor,
+    z: torch.Tensor,
+    table: torch.Tensor,
+    teacher_logprobs: torch.Tensor,
+    *,
+    prefix_decay: float,
+    hard_weight: float,
+    soft_weight: float,
+    check_coverage: bool = True,
+):
+    """``compressed_distillation_loss`` from the row log-sum-exp and the logits at ``table``.
+
+    ``lse`` [B, t]; ``z`` / ``table`` [B, t, 1 + K] (label column first, ids
+    < 0 unmapped).  logp[id] = z - lse, so the loss needs no [B, t, V] tensor.
+    """
+    lps = teacher_logprobs if teacher_logprobs.ndim == 3 else teacher_logprobs.unsqueeze(0)
+    B, t = lse.shape
+    w = prefix_weights(t, prefix_decay=prefix_decay, device=lse.device)
+    d_lab, d_ids = table[..., 0], table[..., 1:]
+    ok_hard = d_lab >= 0
+    hw = w * ok_hard.float()
+    hard = -(z[..., 0] - lse)
+    h_den = hw.sum(-1)
+    hard_loss = torch.where(h_den > 0, (hard * hw).sum(-1) / h_den.clamp_min(1.0), torch.zeros_like(h_den))
+    ok_soft = d_ids >= 0
+    ok_rows = ok_soft.any(-1)
+    t_logits = lps.float().masked_fill(~ok_soft, float("-inf"))
+    t_logits = torch.where(ok_rows.unsqueeze(-1), t_logits, torch.zeros_like(t_logits))
+    probs = t_logits.softmax(-1)
+    soft = -(probs * (z[..., 1:] - lse.unsqueeze(-1))).sum(-1)
+    sw = w * ok_rows.float()
+    s_den = sw.sum(-1)
+    soft_loss = torch.where(s_den > 0, (soft * sw).sum(-1) / s_den.clamp_min(1.0), torch.zeros_like(s_den))
+    if check_coverage and bool(((h_den == 0) & (s_den == 0)).any()):
+        raise ValueError("teacher labels and top-k are outside EAGLE vocabulary")
+    hard_loss, soft_loss = hard_loss.mean(), soft_loss.mean()
+    loss = hard_weight * hard_loss + soft_weight * soft_loss
+    return loss, {
+        "hard_loss": hard_loss.detach(),
+        "soft_loss": soft_loss.detach(),
+        "label_coverage": ok_hard.float().mean().detach(),
+        "topk_coverage": ok_soft.float().mean().detach(),
+    }
+
+
+def compressed_target_score_from_lse(lse: torch.Tensor, z_label: torch.Tensor, d_label: torch.Tensor, *,
+                                     prefix_decay: float) -> torch.Tensor:
+    """``compressed_target_score`` ([B]) from lse [B, t] and the label logits [B, t]."""
+    w = prefix_weights(lse.shape[1], prefix_decay=prefix_decay, device=lse.device) * (d_label >= 0).float()
+    sel = z_label - lse
+    den = w.sum(-1)
+    return torch.where(den > 0, (w * sel).sum(-1) / den.clamp_min(1.0), lse.sum(-1) * 0.0)
+
+
 def compressed_distillation_loss(
     model,
     logits: torch.Tensor,
@@ -119,49 +186,27 @@ def compressed_distillation_loss(
     and top-k all fall outside the draft vocabulary raises (this reads one
     device scalar; the graph-captured trainer passes False).
     """
+    from ..ops.lm_loss import lse_gather
+
     logits, labels = _batched(logits, labels)
-    ids = teacher_ids if teacher_ids.ndim == 3 else teacher_ids.unsqueeze(0)
-    lps = teacher_logprobs if teacher_logprobs.ndim == 3 else teacher_logprobs.unsqueeze(0)
-    w = prefix_weights(labels.shape[1], prefix_decay=prefix_decay, device=logits.device)
-    logp = logits.float().log_softmax(-1)
-    d_lab = model.draft_ids(labels)
-    ok_hard = d_lab >= 0
-    hw = w * ok_hard.float()
-    hard = -logp.gather(-1, d_lab.clamp_min(0).unsqueeze(-1)).squeeze(-1)
-    h_den = hw.sum(-1)
-    hard_loss = torch.where(h_den > 0, (hard * hw).sum(-1) / h_den.clamp_min(1.0), torch.zeros_like(h_den))
-    d_ids = model.draft_ids(ids)
-    ok_soft = d_ids >= 0
-    ok_rows = ok_soft.any(-1)
-    t_logits = lps.float().masked_fill(~ok_soft, float("-inf"))
-    t_logits = torch.where(ok_rows.unsqueeze(-1), t_logits, torch.zeros_like(t_logits))
-    probs = t_logits.softmax(-1)
-    soft = -(probs * logp.gather(-1, d_ids.clamp_min(0))).sum(-1)
-    sw = w * ok_rows.float()
-    s_den = sw.sum(-1)
-    soft_loss = torch.where(s_den > 0, (soft * sw).sum(-1) / s_den.clamp_min(1.0), torch.zeros_like(s_den))
-    if check_coverage and bool(((h_den == 0) & (s_den == 0)).any()):
-        raise ValueError("teacher labels and top-k are outside EAGLE vocabulary")
-    hard_loss, soft_loss = hard_loss.mean(), soft_loss.mean()
-    loss = hard_weight * hard_loss + soft_weight * soft_loss
-    return loss, {
-        "hard_loss": hard_loss.detach(),
-        "soft_loss": soft_loss.detach(),
-        "label_coverage": ok_hard.float().mean().detach(),
-        "topk_coverage": ok_soft.float().mean().detach(),
-    }
+    table = compressed_id_table(model, labels, teacher_ids)
+    B, t, V = logits.shape
+    lse, z = lse_gather(logits.reshape(B * t, V), table.reshape(B * t, -1))
+    return compressed_distillation_from_lse(lse.view(B, t), z.view(B, t, -1), table, teacher_logprobs,
+                                            prefix_decay=prefix_decay, hard_weight=hard_weight,
+                                            soft_weight=soft_weight, check_coverage=check_coverage)
 
 
 def compressed_target_score(model, logits: torch.Tensor, labels: torch.Tensor, *, prefix_decay: float):
     """Prefix-weighted draft-vocabulary log-probability of the mapped labels."""
+    from ..ops.lm_loss import lse_gather
+
     batched = labels.ndim == 2
     logits, labels = _batched(logits, labels)
-    d_lab = model.draft_ids(labels)
-    w = prefix_weights(labels.shape[1], prefix_decay=prefix_decay, device=logits.device) * (d_lab >= 0).float()
-    lp = logits.float().log_softmax(-1)
-    sel = lp.gather(-1, d_lab.clamp_min(0).unsqueeze(-1)).squeeze(-1)
-    den = w.sum(-1)
-    score = torch.where(den > 0, (w * sel).sum(-1) / den.clamp_min(1.0), lp.sum((-1, -2)) * 0.0)
+    table = compressed_id_table(model, labels, None)
+    B, t, V = logits.shape
+    lse, z = lse_gather(logits.reshape(B * t, V), table.reshape(B * t, 1))
+    score = compressed_target_score_from_lse(lse.view(B, t), z.view(B, t), table[..., 0], prefix_decay=prefix_decay)
     return score if batched else score[0]
 
 

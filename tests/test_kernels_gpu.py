@@ -434,3 +434,40 @@ def test_gemv_wide_k_reads_x_from_global(cuda_device, M):
     ref = res.float() + (x.float() @ w.float().T).to(torch.bfloat16).float()
     assert _rel_err(out, ref) < 1e-2
     assert torch.equal(out[:1], one)  # the row does not depend on how many rows share the launch
+
+
+def test_lse_gather_forward_backward(cuda_device):
+    """Row log-sum-exp + logit gathers and the logits gradient against fp32 autograd."""
+    from sparsecache_b200.ops.lm_loss import FrozenLMHead, lse_gather, lse_gather_reference
+
+    torch.manual_seed(0)
+    R, V, G = 300, 32000, 65
+    logits = (torch.randn(R, V, device=cuda_device) * 3).to(torch.bfloat16)
+    ids = torch.randint(0, V, (R, G), device=cuda_device, dtype=torch.int32)
+    ids[::7, 5:9] = -1
+    ids[:, 3] = ids[:, 0]  # duplicate ids add up
+    a = torch.randn(R, device=cuda_device)
+    b = torch.randn(R, G, device=cuda_device)
+    x = logits.clone().requires_grad_(True)
+    lse, z = lse_gather(x, ids)
+    ((a * lse).sum() + (b * z).sum()).backward()
+    xr = logits.float().clone().requires_grad_(True)
+    lse_r, z_r = lse_gather_reference(xr, ids)
+    ((a * lse_r).sum() + (b * z_r).sum()).backward()
+    torch.cuda.synchronize()
+    assert _rel_err(lse, lse_r) < 1e-5 and torch.equal(z, z_r.detach())
+    assert _rel_err(x.grad, xr.grad) < 2e-2
+    # fused LM head: feats -> (lse, z), gradient into feats through the frozen head
+    d = 512
+    w = (torch.randn(4096, d, device=cuda_device) * 0.05).to(torch.bfloat16)
+    head = FrozenLMHead(w)
+    f = torch.randn(R, d, device=cuda_device).to(torch.bfloat16).requires_grad_(True)
+    ids2 = ids.clamp_max(4095)
+    lse2, z2 = head.lse_gather(f, ids2)
+    ((a * lse2).sum() + (b * z2).sum()).backward()
+    fr = f.detach().float().clone().requires_grad_(True)
+    lse2r, z2r = lse_gather_reference(fr @ w.float().t(), ids2)
+    ((a * lse2r).sum() + (b * z2r).sum()).backward()
+    torch.cuda.synchronize()
+    assert _rel_err(lse2, lse2r) < 1e-2 and _rel_err(z2, z2r) < 2e-2
+    assert _rel_err(f.grad, fr.grad) < 3e-2
