@@ -16,6 +16,11 @@ Parity with the reference's experiments/pd_progressive_kv_pipeline.py:
     transfer, draft and verification breakdown.
   * ``aggregate`` (experiments/aggregate_pd_progressive_kv_pipeline.py):
     token equality, accepted drafts, TTFT/response distributions, paired gains.
+Result rows follow the reference's layout (pd_progressive_kv_pipeline.py:1560-1700):
+``schedules[name] = {ranking, stage_document_counts, full_target, chains}``,
+``chains[window] = {timing_token_ids, pipeline: {response_ms, first_committed_ms,
+terminated_stage, trace, ...}, paired_fixed_control, measurement_order}`` and a
+``protocol`` block, so ``pipelines.analysis`` and the latency-cell validator read them.
 The transport is the pinned-host tranche stager with an optional paced link
 (``TrancheStager``); the prefill producer is this package's engine.
 """
@@ -64,29 +69,42 @@ def run_full_target(engine, stager: TrancheStager, *, seed_token: int, prompt_to
     engine.decode(stager.slot, max_new_tokens - 1, max_new=max_new_tokens)
     tokens = engine.generated_tokens(max_new_tokens).tolist()
     torch.cuda.current_stream(engine.device).synchronize()
-    return {"tokens": tokens, "first_ready_ms": ready, "response_ms": (clock() - t0) * 1e3,
-            "transfer": stager.finish()}
+    response = (clock() - t0) * 1e3
+    return {"tokens": tokens, "first_ready_ms": ready, "response_ms": response, "seed_forward_ms": 0.0,
+            "decode_ms": response - ready, "transfer": stager.finish()}
+
+
+def _schedule_cells(rows: Sequence[dict]):
+    """(full_target, chain) pairs of every row (first schedule and commit window of the protocol)."""
+    for r in rows:
+        if "schedules" not in r:  # compact rows: {"full_target": ..., "chain": ...}
+            yield r["full_target"], r["chain"], r.get("tokens_equal")
+            continue
+        proto = r["protocol"]
+        sched = r["schedules"][proto["schedules"][0]]
+        chain = sched["chains"][str(proto["commit_windows"][0])]
+        pipe = dict(chain["pipeline"])
+        pipe.setdefault("first_ready_ms", pipe.get("first_committed_ms"))
+        yield sched["full_target"], pipe, chain.get("timing_token_match_target")
 
 
 def aggregate(rows: Sequence[dict]) -> dict[str, Any]:
-    def col(arm, key):
-        return [r[arm][key] for r in rows if r.get(arm) and r[arm].get(key) is not None]
-
+    """Token equality, accepted drafts, response / first-ready distributions and paired gains."""
     def stats(x):
+        x = sorted(v for v in x if v is not None)
         if not x:
             return None
-        x = sorted(x)
         return {"mean": statistics.fmean(x), "p50": x[len(x) // 2], "p99": x[min(len(x) - 1, int(0.99 * len(x)))]}
 
-    gains = [r["full_target"]["response_ms"] - r["chain"]["response_ms"] for r in rows]
-    return {"requests": len(rows),
-            "token_equality_rate": statistics.fmean(r["tokens_equal"] for r in rows) if rows else None,
-            "accepted_draft_tokens": stats([r["chain"]["accepted"] for r in rows]),
-            "full_target_response_ms": stats(col("full_target", "response_ms")),
-            "chain_response_ms": stats(col("chain", "response_ms")),
-            "full_target_first_ready_ms": stats(col("full_target", "first_ready_ms")),
-            "chain_first_ready_ms": stats(col("chain", "first_ready_ms")),
-            "response_gain_ms": stats(gains)}
+    cells = list(_schedule_cells(rows))
+    return {"requests": len(cells),
+            "token_equality_rate": statistics.fmean(bool(e) for _, _, e in cells) if cells else None,
+            "accepted_draft_tokens": stats([c["accepted"] for _, c, _ in cells]),
+            "full_target_response_ms": stats([t["response_ms"] for t, _, _ in cells]),
+            "chain_response_ms": stats([c["response_ms"] for _, c, _ in cells]),
+            "full_target_first_ready_ms": stats([t.get("first_ready_ms") for t, _, _ in cells]),
+            "chain_first_ready_ms": stats([c.get("first_ready_ms") for _, c, _ in cells]),
+            "response_gain_ms": stats([t["response_ms"] - c["response_ms"] for t, c, _ in cells])}
 
 
 def main(argv=None) -> None:
@@ -105,6 +123,8 @@ def main(argv=None) -> None:
     p.add_argument("--transport-gbps", type=float, default=100.0)
     p.add_argument("--auto-draft-tpot-ms", type=float, default=None)
     p.add_argument("--auto-draft-utilization", type=float, default=1.0)
+    p.add_argument("--paired-fixed-control", action="store_true",
+                   help="also run the fixed first-stage-view chain on the same staged request")
     p.add_argument("--output", type=Path, required=True)
     a = p.parse_args(argv)
     cfg = get_model_config(a.model)
@@ -113,9 +133,12 @@ def main(argv=None) -> None:
     fractions = tuple(float(x) for x in a.stage_fractions.split(","))
     bytes_per_token = cfg.n_layers * 2 * cfg.n_kv_heads * cfg.head_dim * 2
     rows = []
+    window = "inf"
+    protocol = {"schedules": [a.schedule], "commit_windows": [window], "transport_gbps": a.transport_gbps,
+                "draft_tokens": a.draft_tokens, "max_new_tokens": a.max_new_tokens,
+                "stage_fractions": list(fractions), "fixed_token_horizon": True, "paired_measurement": True,
+                "paired_fixed_control": a.paired_fixed_control, "model": a.model, "workload": a.workload}
     with open(a.output, "w") as f:
-        f.write(json.dumps({"protocol": {**vars(a), "output": str(a.output), "fixed_token_horizon": True,
-                                         "paired_measurement": True}}) + "\n")
         for i, r in enumerate(reqs):
             T = r.prompt_tokens
             docs = [Document(tuple(d), " ".join(map(str, d[:64])), start=b, end=e)
@@ -134,27 +157,53 @@ def main(argv=None) -> None:
             # producer: prefill the whole prompt once; its slot is the tranches' source
             src = eng.new_slot(T + a.max_new_tokens + 64)
             ids = torch.tensor(r.prompt, dtype=torch.int32, device=eng.device)
+            p0 = time.perf_counter()
             h = eng.prefill(ids, src)
             seed = int(eng.first_token(h[T - 1:T], position=T, max_new=1)["tok"][0].item())
+            prefill_ms = (time.perf_counter() - p0) * 1e3
             host = src.data[:, :, :, :T].cpu().pin_memory()
-            arms = ("full_target", "chain") if i % 2 == 0 else ("chain", "full_target")
-            row: dict[str, Any] = {"request_index": i, "prompt_tokens": T, "draft_tokens": gamma,
-                                   "residual_wire_ms": residual, "measurement_order": "->".join(arms)}
+            arms = ["full_target", "chain"] + (["fixed"] if a.paired_fixed_control else [])
+            if i % 2:
+                arms = arms[::-1]
+            out: dict[str, Any] = {}
             for arm in arms:
                 dst = eng.new_slot(T + a.max_new_tokens + 64)
                 stager = TrancheStager(host, dst, prefix_tokens=len(r.prefix), documents=docs,
                                        suffix_tokens=len(r.suffix), ranking=ranking, selected_sets=sets,
                                        transport_gbps=a.transport_gbps)
                 if arm == "full_target":
-                    row[arm] = run_full_target(eng, stager, seed_token=seed, prompt_tokens=T,
+                    out[arm] = run_full_target(eng, stager, seed_token=seed, prompt_tokens=T,
                                                max_new_tokens=a.max_new_tokens)
                 else:
-                    res = continuous_graft_chain(eng, stager, seed_token=seed, prompt_tokens=T,
-                                                 max_draft_tokens=gamma, max_new_tokens=a.max_new_tokens)
-                    row[arm] = {"tokens": list(res.token_ids), "first_ready_ms": res.first_token_ready_ms,
-                                "response_ms": res.response_ms, "accepted": res.accepted,
-                                "drafts": list(res.draft_tokens), "transfer": res.transfer}
-            row["tokens_equal"] = row["full_target"]["tokens"] == row["chain"]["tokens"]
+                    out[arm] = continuous_graft_chain(eng, stager, seed_token=seed, prompt_tokens=T,
+                                                      max_draft_tokens=gamma, max_new_tokens=a.max_new_tokens,
+                                                      grow_view=(arm == "chain"))
+            target = out["full_target"]
+            target_ids = target.pop("tokens")
+
+            def chain_cell(res, configured):
+                return {"timing_token_ids": list(res.token_ids), "configured_draft_tokens": configured,
+                        "timing_token_match_target": list(res.token_ids) == target_ids,
+                        "speedup_vs_full_target": target["response_ms"] / res.response_ms,
+                        **res.pipeline_record()}
+
+            pipe = out["chain"]
+            chains = {window: {
+                "timing_token_ids": list(pipe.token_ids), "configured_draft_tokens": gamma,
+                "estimated_residual_wire_ms": residual,
+                "timing_token_match_target": list(pipe.token_ids) == target_ids,
+                "pipeline": pipe.pipeline_record(),
+                "pipeline_speedup_vs_full_target": target["response_ms"] / pipe.response_ms,
+                "paired_fixed_control": chain_cell(out["fixed"], gamma) if "fixed" in out else None,
+                "measurement_order": "->".join(arms)}}
+            row = {"dataset_index": i, "prompt_tokens": T, "anchor_tokens": len(r.prefix) + len(r.suffix),
+                   "document_tokens": sum(len(d) for d in r.documents), "document_pages": len(docs),
+                   "logical_bf16_kv_bytes": T * bytes_per_token, "producer": {"prefill_ms": prefill_ms},
+                   "schedules": {a.schedule: {"ranking": list(ranking),
+                                              "stage_document_counts": [len(x) for x in sets],
+                                              "full_target": {"timing_token_ids": target_ids, **target},
+                                              "chains": chains}},
+                   "protocol": protocol}
             rows.append(row)
             f.write(json.dumps(row, default=str) + "\n")
     print(json.dumps(aggregate(rows), indent=2))

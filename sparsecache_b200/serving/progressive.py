@@ -434,12 +434,31 @@ class ChainResult:
     verifier_calls: int
     visible_fraction_per_draft: tuple[float, ...]
     transfer: dict[str, Any]
+    # per-stage trace in the reference pipeline's layout: draft entries
+    # {"stage", "drafted", "draft_token_ids"} (consecutive drafts on the same
+    # visible stage grouped), then {"stage", "verified", "accepted_pending",
+    # "rejected_pending"} for the final verifier
+    trace: tuple[dict, ...] = ()
+    draft_decode_ms: float = 0.0
+    terminated_stage: int = 0
+
+    def pipeline_record(self) -> dict[str, Any]:
+        """The ``pipeline`` block of a P/D result row."""
+        return {"response_ms": self.response_ms, "first_committed_ms": self.first_token_ready_ms,
+                "terminated_stage": self.terminated_stage, "trace": [dict(t) for t in self.trace],
+                "draft_prefill_ms": 0.0, "draft_decode_ms": self.draft_decode_ms, "transfer": self.transfer,
+                "verifier_calls": self.verifier_calls, "accepted": self.accepted,
+                "visible_fraction_per_draft": list(self.visible_fraction_per_draft)}
 
 
 def continuous_graft_chain(engine, stager: TrancheStager, *, seed_token: int, prompt_tokens: int,
                            max_draft_tokens: int, max_new_tokens: int, anchor_stages: int = 1,
-                           clock=time.perf_counter) -> ChainResult:
-    """Draft while tranches arrive, verify once on full KV, then decode normally."""
+                           grow_view: bool = True, clock=time.perf_counter) -> ChainResult:
+    """Draft while tranches arrive, verify once on full KV, then decode normally.
+
+    ``grow_view`` False is the fixed first-stage control: every draft reads
+    only the anchor stage's view however many tranches have landed.
+    """
     dev = engine.device
     T = prompt_tokens
     slot = stager.slot
@@ -464,6 +483,9 @@ def continuous_graft_chain(engine, stager: TrancheStager, *, seed_token: int, pr
 
     token = int(seed_token)
     drafts, fractions = [], []
+    trace: list[dict] = []
+    draft_ms = 0.0
+    view_stage = 0
     b = engine._decode_buffers(max_new_tokens + max_draft_tokens)
     while state.phase == ProgressivePDPhase.DRAFT_WHILE_LOADING and len(drafts) < max_draft_tokens:
         stager.poll_ready_copies()
@@ -471,18 +493,28 @@ def continuous_graft_chain(engine, stager: TrancheStager, *, seed_token: int, pr
         if newly:
             state.record_page_completion(newly)
             completed |= newly
-            visible = state.visible_priority_pages
-            arrived_tokens = stager.stages[visible[-1]].destination_end
+            if grow_view:
+                visible = state.visible_priority_pages
+                view_stage = visible[-1]
+                arrived_tokens = stager.stages[view_stage].destination_end
         if state.phase != ProgressivePDPhase.DRAFT_WHILE_LOADING:
             break
         # draft one token: row at position T + len(drafts), tail slot, visible view
+        t0 = clock()
         refresh_view(arrived_tokens)
         pred = engine.verify(slot, torch.tensor([token], dtype=torch.int32), position=T + len(drafts),
                              slot_start=tail[len(drafts)], view=view, n_visible=arrived_tokens + len(drafts))
         token = int(pred[0].item())
+        draft_ms += (clock() - t0) * 1000
         state.record_draft_token(token)
         drafts.append(token)
         fractions.append(state.visible_fraction)
+        if trace and trace[-1]["stage"] == view_stage and "verified" not in trace[-1]:
+            trace[-1]["drafted"] += 1
+            trace[-1]["draft_token_ids"].append(token)
+        else:
+            trace.append({"stage": view_stage, "drafted": 1, "draft_token_ids": [token]})
+    terminated = len(completed) - 1
     # full KV: wait for every tranche, then ONE verifier over [seed, d1..dk]
     for i in range(n_stages):
         stager.wait_on_compute_stream(i)
@@ -502,6 +534,8 @@ def continuous_graft_chain(engine, stager: TrancheStager, *, seed_token: int, pr
     accepted = accepted_prefix_length(drafts, preds)
     correction = preds[accepted] if accepted < len(preds) else preds[-1]
     state.record_final_verification(accepted, correction)
+    trace.append({"stage": n_stages - 1, "verified": True, "accepted_pending": accepted,
+                  "rejected_pending": len(drafts) - accepted, "drafted": 0})
     out.extend(state.external_token_ids)
     first_ready = (clock() - started) * 1000
     # continue greedy decode after seed + accepted + correction (KV crop = metadata)
@@ -517,4 +551,5 @@ def continuous_graft_chain(engine, stager: TrancheStager, *, seed_token: int, pr
     state.finish()
     torch.cuda.current_stream(dev).synchronize()
     return ChainResult(tuple(out[:max_new_tokens]), tuple(drafts), accepted, first_ready,
-                       (clock() - started) * 1000, state.verifier_calls, tuple(fractions), stager.finish())
+                       (clock() - started) * 1000, state.verifier_calls, tuple(fractions), stager.finish(),
+                       tuple(trace), draft_ms, max(0, terminated))

@@ -180,3 +180,49 @@ def test_pd_pipeline_auto_draft_and_aggregate():
              "chain": {"response_ms": 90.0, "first_ready_ms": 30.0, "accepted": 3}}]
     agg = aggregate(rows)
     assert agg["token_equality_rate"] == 1.0 and agg["response_gain_ms"]["mean"] == 10.0
+
+
+def _pd_row(i, *, target_ms, pipe_ms, fixed_ms, graft_batches, fixed_batch, acc, fixed_acc, match=True):
+    def pipe(batches, accepted, ms):
+        trace = [{"stage": s, "drafted": len(b), "draft_token_ids": b} for s, b in enumerate(batches)]
+        trace.append({"stage": 3, "verified": True, "accepted_pending": accepted,
+                      "rejected_pending": sum(map(len, batches)) - accepted, "drafted": 0})
+        return {"response_ms": ms, "first_committed_ms": ms / 2, "terminated_stage": len(batches) - 1,
+                "trace": trace, "draft_prefill_ms": 0.0, "draft_decode_ms": 2.0,
+                "visible_fraction_per_draft": [0.25] * len(batches[0]) + [0.5] * sum(map(len, batches[1:])),
+                "transfer": {"stage_wire_ms": [1.0, 2.0, 3.0], "total_h2d_ms": 0.5, "stage_wire_wait_ms": [0.1]}}
+
+    graft = pipe(graft_batches, acc, pipe_ms)
+    fixed = pipe([fixed_batch], fixed_acc, fixed_ms)
+    return {"dataset_index": i, "protocol": {"schedules": ["query"], "commit_windows": ["inf"],
+                                             "transport_gbps": 50.0, "draft_tokens": 6},
+            "schedules": {"query": {"full_target": {"response_ms": target_ms, "decode_ms": 5.0, "seed_forward_ms": 0.0,
+                                                    "transfer": {"total_h2d_ms": 1.0}},
+                                    "chains": {"inf": {"configured_draft_tokens": 6, "timing_token_match_target": match,
+                                                       "pipeline": graft, "paired_fixed_control": fixed}}}}}
+
+
+def test_pd_run_summary_and_graft_triggers():
+    from sparsecache_b200.pipelines.analysis import analyze_graft_triggers, paired_delta, summarize_run
+
+    rows = [_pd_row(0, target_ms=30.0, pipe_ms=20.0, fixed_ms=24.0, graft_batches=[[1, 2], [3, 4]],
+                    fixed_batch=[1, 2, 9, 9, 9, 9], acc=3, fixed_acc=2),
+            _pd_row(1, target_ms=40.0, pipe_ms=35.0, fixed_ms=33.0, graft_batches=[[5, 6], [7, 8, 1]],
+                    fixed_batch=[5, 6, 7, 8, 1, 0], acc=2, fixed_acc=2)]
+    s = summarize_run(rows)
+    assert s["cases"] == 2 and s["latency"]["saved_vs_full_target_ms"]["mean"] == 7.5
+    assert s["drafts"]["accepted_at_final_verifier"]["mean"] == 2.5 and s["drafts"]["proposed"]["max"] == 5
+    assert s["terminated_stage_counts"] == {"2": 2}
+    assert s["residual_wire_ms"]["mean"] == 5.0
+    pf = s["paired_fixed_control"]
+    assert pf["latency_saved_by_method_ms"]["mean"] == 1.0 and pf["accepted_token_delta_method_minus_fixed"]["positive"] == 1
+    t = analyze_graft_triggers(rows)
+    assert t["cases"] == 2 and t["triggers"]["margin_trigger"] is None
+    by = {c["dataset_index"]: c for c in t["rows"]}
+    # request 0: the second batch differs from the fixed proposals -> instability fires, gain 1
+    assert by[0]["s2_first_token_instability"] and by[0]["acceptance_gain"] == 1
+    # request 1: the graft proposals equal the fixed ones -> no trigger, no gain
+    assert not by[1]["s2_batch_instability"] and by[1]["acceptance_gain"] == 0
+    trig = t["triggers"]["s2_batch_instability"]
+    assert trig["triggered"] == 1 and trig["true_positive"] == 1 and trig["missed_positive"] == 0
+    assert paired_delta([3, 1], [1, 1])["positive"] == 1

@@ -105,3 +105,33 @@ def test_continuous_chain_is_exact(engine_setup):
     engine.decode(slot_f, 11, max_new=16, use_graph=False)
     full = [seed] + engine.generated_tokens(11).tolist()
     assert list(res.token_ids) == full
+
+
+def test_fixed_view_control_is_exact_and_traced(engine_setup):
+    """The fixed first-stage control drafts on the anchor view only; output stays exact."""
+    cfg, engine = engine_setup
+    dev = engine.device
+    req = make_requests("tiny_plumbing", cfg)[1]
+    T, P, S = req.prompt_tokens, len(req.prefix), len(req.suffix)
+    slot_p = engine.new_slot(T + 64)
+    h = engine.prefill(torch.tensor(req.prompt, dtype=torch.int32, device=dev), slot_p)
+    engine.first_token(h[T - 1:T], position=T, max_new=16)
+    seed = int(engine.generated_tokens(1).item())
+    source = slot_p.data[:, :, :, :T].cpu().pin_memory()
+    docs = [Document(d, start=b, end=e) for d, (b, e) in zip(req.documents, req.document_ranges())]
+    ranking = list(range(len(docs)))
+    stages = stage_document_sets(ranking, docs, (0.2, 0.6, 1.0))
+    outs = []
+    for grow in (True, False):
+        stager = TrancheStager(source, engine.new_slot(T + 64), prefix_tokens=P, documents=docs, suffix_tokens=S,
+                               ranking=ranking, selected_sets=stages, transport_gbps=0.5, device=dev)
+        stager.pack()
+        res = continuous_graft_chain(engine, stager, seed_token=seed, prompt_tokens=T, max_draft_tokens=4,
+                                     max_new_tokens=12, grow_view=grow)
+        rec = res.pipeline_record()
+        assert rec["trace"][-1]["verified"] and rec["trace"][-1]["accepted_pending"] == res.accepted
+        assert sum(t["drafted"] for t in rec["trace"]) == len(res.draft_tokens)
+        if not grow:
+            assert all(t["stage"] == 0 for t in rec["trace"][:-1])
+        outs.append(list(res.token_ids))
+    assert outs[0] == outs[1]  # both verified on the full KV: identical greedy output
