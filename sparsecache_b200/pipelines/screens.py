@@ -8,6 +8,9 @@ backends, the drafts run on this package's engine.
   * ``layer_draft_screen``: greedy drafts computed with a subset of the target's layers (the
     first N, or a frozen pattern; skipped layers are identity) against the full model's greedy
     continuation: accepted prefix and per-token draft time (CUDA graph per subset).
+  * layer patterns: uniform and sandwich subsets (``standard_patterns``) or a
+    schema-1 pattern file (configs/layer_subset_patterns_*.json, the layout
+    of the reference's configs/layer_subset_patterns_llama32.json);
   * ``sparse_page_crossover``: per-token cost of a draft step whose attention reads a page view
     (64 sink + 512 recent + evenly spaced 64-token pages up to the visible fraction) against a
     full-context step, over fractions and context lengths: where sparse drafting stops paying.
@@ -56,6 +59,49 @@ def layer_draft_screen(engine, prompt: Sequence[int], patterns: dict[str, Sequen
         out.append({"pattern": name, "layers": len(layers),
                     "accepted_prefix": accepted_prefix_length(toks[1:], ref[1:]), "ms_per_token": ms,
                     "relative_cost": ms / full_ms})
+    return out
+
+
+def uniform_layers(n_layers: int, k: int) -> list[int]:
+    """k layer indices spread evenly over [0, n_layers - 1] (both ends included)."""
+    if not 1 <= k <= n_layers:
+        raise ValueError("pattern size outside the model")
+    if k == 1:
+        return [0]
+    return sorted({int(i * (n_layers - 1) / (k - 1) + 0.5) for i in range(k)})
+
+
+def sandwich_layers(n_layers: int, k: int) -> list[int]:
+    """The first k/2 and the last k/2 layers."""
+    if k % 2 or not 2 <= k <= n_layers:
+        raise ValueError("sandwich patterns take an even size within the model")
+    return list(range(k // 2)) + list(range(n_layers - k // 2, n_layers))
+
+
+def standard_patterns(n_layers: int, sizes=(8, 16, 24)) -> dict:
+    """Pattern file content (schema 1): uniform and sandwich subsets of each size."""
+    pats = []
+    for k in sizes:
+        if k >= n_layers:
+            continue
+        pats.append({"id": f"uniform{k}", "layer_indices": uniform_layers(n_layers, k),
+                     "description": f"{k} layers spread evenly over the network"})
+        pats.append({"id": f"sandwich{k}", "layer_indices": sandwich_layers(n_layers, k),
+                     "description": f"first {k // 2} and last {k // 2} layers"})
+    return {"schema_version": 1, "n_layers": n_layers, "patterns": pats}
+
+
+def load_patterns(path, n_layers: int) -> dict[str, list[int]]:
+    """{id: layer indices} of a schema-1 pattern file; indices are checked against the model."""
+    data = json.loads(open(path).read())
+    if data.get("schema_version") != 1:
+        raise ValueError("unsupported layer-pattern schema")
+    out = {}
+    for p in data["patterns"]:
+        idx = [int(i) for i in p["layer_indices"]]
+        if idx != sorted(set(idx)) or not idx or idx[0] < 0 or idx[-1] >= n_layers:
+            raise ValueError(f"pattern {p['id']}: indices must be sorted, unique and inside the model")
+        out[p["id"]] = idx
     return out
 
 
@@ -118,6 +164,7 @@ def main(argv=None) -> None:
     p.add_argument("--draft-tokens", type=int, default=8)
     p.add_argument("--contexts", default="8192,32768")
     p.add_argument("--fractions", default="0.05,0.1,0.2,0.5")
+    p.add_argument("--patterns", default=None, help="schema-1 layer-pattern JSON (default: generated)")
     a = p.parse_args(argv)
     cfg = get_model_config(a.model)
     ctxs = [int(x) for x in a.contexts.split(",")]
@@ -127,6 +174,10 @@ def main(argv=None) -> None:
     prompt = torch.randint(0, cfg.vocab, (a.prompt_tokens,), generator=g).tolist()
     patterns = {f"first_{n}": list(range(n)) for n in (L // 4, L // 2, 3 * L // 4)}
     patterns["every_other"] = list(range(0, L, 2))
+    if a.patterns:
+        patterns.update(load_patterns(a.patterns, L))
+    else:
+        patterns.update({p["id"]: p["layer_indices"] for p in standard_patterns(L)["patterns"]})
     print(json.dumps({"layer_draft": layer_draft_screen(eng, prompt, patterns, draft_tokens=a.draft_tokens),
                       "sparse_page_crossover": sparse_page_crossover(
                           eng, ctxs, [float(x) for x in a.fractions.split(",")])}, indent=1))

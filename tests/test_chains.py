@@ -56,3 +56,23 @@ def test_reuse_pipeline_helpers():
     assert agg["arms"]["progressive"]["token_equal_rate"] == 0.0
     assert agg["arms"]["progressive"]["mean_agreeing_prefix"] == 2.0
     assert agg["arms"]["progressive"]["ttft_gain_vs_reference_ms"]["mean"] == 5.0
+
+
+def test_layer_subset_patterns(tmp_path):
+    import json
+    from pathlib import Path
+
+    import pytest
+
+    from sparsecache_b200.pipelines.screens import load_patterns, sandwich_layers, standard_patterns, uniform_layers
+
+    assert uniform_layers(32, 8) == [0, 4, 9, 13, 18, 22, 27, 31]
+    assert sandwich_layers(32, 8) == [0, 1, 2, 3, 28, 29, 30, 31]
+    assert len(uniform_layers(32, 24)) == 24 and uniform_layers(80, 16)[-1] == 79
+    root = Path(__file__).resolve().parents[1] / "configs"
+    pats = load_patterns(root / "layer_subset_patterns_llama31_8b.json", 32)
+    assert pats["uniform16"] == uniform_layers(32, 16) and set(pats) == {p["id"] for p in standard_patterns(32)["patterns"]}
+    bad = tmp_path / "bad.json"
+    bad.write_text(json.dumps({"schema_version": 1, "patterns": [{"id": "x", "layer_indices": [3, 1]}]}))
+    with pytest.raises(ValueError):
+        load_patterns(bad, 32)
