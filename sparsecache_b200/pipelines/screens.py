@@ -185,3 +185,84 @@ def main(argv=None) -> None:
 
 if __name__ == "__main__":
     main()
+
+
+# --------------------------------------------------------------------------
+# Frozen crossover jobs (reference: experiments/build_sparse_draft_crossover_queue.py,
+# experiments/run_sparse_draft_crossover_job.py): a queue pins each job's exact
+# command, the queue carries a sha256 over its jobs, and the runner refuses a
+# job that is not "ready", an edited queue, or GPUs that are not exclusive,
+# then runs the frozen command and writes a run record next to its output.
+# --------------------------------------------------------------------------
+CROSSOVER_QUEUE_FORMAT = "sparsecache.crossover-job-queue.v1"
+
+
+def build_crossover_queue(*, model: str, contexts: Sequence[int], fractions: Sequence[float], run_root: str,
+                          prompt_tokens: int = 4096, draft_tokens: int = 8, patterns: str | None = None) -> dict:
+    from ..serving.live.queue import canonical_sha256
+
+    jobs = []
+    for T in contexts:
+        job_id = f"crossover_{model}_ctx{T}"
+        out_dir = f"{run_root}/{job_id}"
+        cmd = ["python", "-m", "sparsecache_b200.pipelines.screens", "--model", model, "--contexts", str(T),
+               "--fractions", ",".join(str(f) for f in fractions), "--prompt-tokens", str(prompt_tokens),
+               "--draft-tokens", str(draft_tokens)]
+        if patterns:
+            cmd += ["--patterns", patterns]
+        jobs.append({"id": job_id, "status": "ready", "command": cmd, "output_dir": out_dir,
+                     "context_tokens": T, "fractions": list(fractions)})
+    if len({j["id"] for j in jobs}) != len(jobs):
+        raise ValueError("duplicate job ids")
+    return {"format": CROSSOVER_QUEUE_FORMAT, "jobs": jobs, "jobs_sha256": canonical_sha256(jobs)}
+
+
+def run_crossover_job(queue_path, job_id: str, *, gpus: Sequence[int] = (0,), gate=None, runner=None,
+                      max_used_memory_mib: float = 1024.0) -> dict:
+    """Run one frozen job fail-closed; returns (and writes) its run record."""
+    import hashlib
+    import subprocess
+    import time
+    from pathlib import Path
+
+    from ..serving.live.queue import canonical_sha256
+
+    queue_path = Path(queue_path)
+    raw = queue_path.read_bytes()
+    queue = json.loads(raw)
+    if queue.get("format") != CROSSOVER_QUEUE_FORMAT:
+        raise ValueError("not a crossover job queue")
+    if canonical_sha256(queue["jobs"]) != queue.get("jobs_sha256"):
+        raise ValueError("queue jobs were edited after registration")
+    matches = [j for j in queue["jobs"] if j["id"] == job_id]
+    if len(matches) != 1:
+        raise ValueError(f"expected exactly one job named {job_id!r}")
+    job = matches[0]
+    if job["status"] != "ready":
+        raise ValueError(f"job is not executable: {job['status']!r}")
+    if gate is None:
+        from ..serving.live.gate import evaluate_exclusivity, inspect_gpus
+
+        def gate():
+            v = evaluate_exclusivity(inspect_gpus(), list(gpus), max_used_memory_mib=max_used_memory_mib,
+                                     max_utilization_pct=5.0)
+            return {**v, "passed": v["status"] == "passed"}
+    verdict = gate()
+    if not verdict.get("passed", False):
+        raise RuntimeError(f"GPUs are not exclusive: {verdict}")
+    out_dir = Path(job["output_dir"])
+    out_dir.mkdir(parents=True, exist_ok=True)
+    result_path = out_dir / "result.json"
+    t0 = time.time()
+    if runner is None:
+        with open(result_path, "w") as f:
+            rc = subprocess.run(job["command"], stdout=f, check=False).returncode
+    else:
+        rc = runner(job["command"], result_path)
+    record = {"job_id": job_id, "queue_sha256": hashlib.sha256(raw).hexdigest(),
+              "jobs_sha256": queue["jobs_sha256"], "command": job["command"], "exit_code": int(rc),
+              "wall_s": time.time() - t0, "gate": verdict, "result": str(result_path)}
+    (out_dir / "run_record.json").write_text(json.dumps(record, indent=2) + "\n")
+    if rc != 0:
+        raise RuntimeError(f"{job_id} exited with {rc}")
+    return record

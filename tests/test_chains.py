@@ -76,3 +76,33 @@ def test_layer_subset_patterns(tmp_path):
     bad.write_text(json.dumps({"schema_version": 1, "patterns": [{"id": "x", "layer_indices": [3, 1]}]}))
     with pytest.raises(ValueError):
         load_patterns(bad, 32)
+
+
+def test_crossover_queue_is_fail_closed(tmp_path):
+    import json
+
+    import pytest
+
+    from sparsecache_b200.pipelines.screens import build_crossover_queue, run_crossover_job
+
+    q = build_crossover_queue(model="llama3-8b", contexts=[8192, 32768], fractions=[0.05, 0.2],
+                              run_root=str(tmp_path / "runs"))
+    qp = tmp_path / "queue.json"
+    qp.write_text(json.dumps(q))
+    calls = []
+
+    def runner(cmd, out):
+        calls.append(cmd)
+        out.write_text("{}")
+        return 0
+
+    rec = run_crossover_job(qp, "crossover_llama3-8b_ctx8192", gate=lambda: {"passed": True}, runner=runner)
+    assert rec["exit_code"] == 0 and calls[0][:3] == ["python", "-m", "sparsecache_b200.pipelines.screens"]
+    assert (tmp_path / "runs" / "crossover_llama3-8b_ctx8192" / "run_record.json").exists()
+    with pytest.raises(RuntimeError):  # GPUs busy
+        run_crossover_job(qp, "crossover_llama3-8b_ctx32768", gate=lambda: {"passed": False}, runner=runner)
+    q["jobs"][1]["command"].append("--extra")  # edited after registration
+    qp.write_text(json.dumps(q))
+    with pytest.raises(ValueError):
+        run_crossover_job(qp, "crossover_llama3-8b_ctx32768", gate=lambda: {"passed": True}, runner=runner)
+    assert len(calls) == 1
