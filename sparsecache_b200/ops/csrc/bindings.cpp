@@ -687,6 +687,44 @@ void cacheblend_select(Tensor dev_part, int64_t n_kv_heads, int64_t dev_mode, in
   check_cuda(sc::cacheblend_select(a, cur_stream()), "cacheblend_select");
 }
 
+// out = epilogue(x @ w^T) for M <= 16 rows on the tensor cores; returns kernels launched.
+int64_t skinny_gemm(Tensor x, Tensor w, int64_t epi, Tensor out, c10::optional<Tensor> residual, Tensor ws,
+                    int64_t splits) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_matrix(x, "x");
+  check_matrix(w, "w");
+  check_matrix(out, "out");
+  TORCH_CHECK(x.size(1) == w.size(1), "K mismatch");
+  CHECK_F32(ws);
+  sc::SkinnyArgs a{};
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  a.M = (int)x.size(0);
+  a.N = (int)w.size(0);
+  a.K = (int)w.size(1);
+  a.ldx = (int)x.stride(0);
+  a.ldw = (int)w.stride(0);
+  a.epi = (int)epi;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.ldo = (int)out.stride(0);
+  TORCH_CHECK(out.size(0) >= a.M && out.size(1) == (epi == sc::SKINNY_SWIGLU ? a.N / 2 : a.N), "out shape");
+  if (epi == sc::SKINNY_RESIDUAL) {
+    TORCH_CHECK(residual.has_value() && residual->defined(), "residual required");
+    check_matrix(*residual, "residual");
+    a.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    a.ldr = (int)residual->stride(0);
+  }
+  a.num_sms = num_sms();
+  a.splits = splits > 0 ? (int)splits : sc::skinny_splits(a.N, a.K, a.num_sms);
+  TORCH_CHECK(ws.numel() >= (int64_t)a.splits * a.N * 16, "workspace [splits][N][16] too small");
+  a.ws = ws.data_ptr<float>();
+  a.status = status_tensor(w).data_ptr<int>();
+  check_cuda(sc::skinny_gemm(a, cur_stream()), "skinny_gemm");
+  return 2;
+}
+
+int64_t skinny_splits(int64_t N, int64_t K) { return sc::skinny_splits((int)N, (int)K, num_sms()); }
+
 sc::LseGatherArgs lse_args(const Tensor& logits, const Tensor& ids, const Tensor& lse) {
   check_matrix(logits, "logits");
   CHECK_I32(ids); CHECK_F32(lse);
@@ -986,6 +1024,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("n_parts") = 1, py::arg("part_stride") = 0);
   m.def("arange_i32", &arange_i32);
   m.def("lse_gather", &lse_gather);
+  m.def("skinny_gemm", &skinny_gemm, py::arg("x"), py::arg("w"), py::arg("epi"), py::arg("out"),
+        py::arg("residual") = py::none(), py::arg("ws"), py::arg("splits") = -1);
+  m.def("skinny_splits", &skinny_splits);
   m.def("lse_gather_backward", &lse_gather_backward, py::arg("logits"), py::arg("ids"), py::arg("lse"),
         py::arg("g_lse"), py::arg("g_z"), py::arg("dlogits"));
   m.def("index_i32", &index_i32);

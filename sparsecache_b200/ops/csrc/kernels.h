@@ -250,6 +250,25 @@ struct SelectArgs {
 };
 cudaError_t cacheblend_select(const SelectArgs& a, cudaStream_t stream);
 
+// Skinny tensor-core GEMM for M <= 16 token rows (skinny_tc.cu).
+enum SkinnyEpi { SKINNY_STORE = 0, SKINNY_RESIDUAL = 1, SKINNY_SWIGLU = 2 };
+struct SkinnyArgs {
+  const __nv_bfloat16* x;  // [M, K] row stride ldx
+  const __nv_bfloat16* w;  // [N, K] row stride ldw
+  int M, N, K, ldx, ldw;
+  int epi;
+  __nv_bfloat16* out;      // [M, N] (SwiGLU: [M, N / 2]) row stride ldo
+  int ldo;
+  const __nv_bfloat16* residual;  // [M, N] row stride ldr (SKINNY_RESIDUAL; may alias out)
+  int ldr;
+  float* ws;               // [splits][N][16] fp32
+  int splits;
+  int num_sms;
+  int* status;
+};
+int skinny_splits(int N, int K, int num_sms);
+cudaError_t skinny_gemm(const SkinnyArgs& a, cudaStream_t stream);
+
 // Row log-sum-exp + logit gathers (forward) and the logits gradient
 // g_lse * softmax + sum_j g_z[j] * onehot(ids[j]) (backward), lm_loss.cu.
 struct LseGatherArgs {

@@ -1,0 +1,270 @@
+// Skinny GEMM on the tensor cores for a few token rows (batched verification,
+// small decode batches): out[m, n] = sum_k x[m, k] * w[n, k], M <= 16.
+//
+// At M <= 16 the work is a weight stream; the CUDA-core GEMV (gemv.cu) keeps
+// up with HBM only at M = 1-2 because every extra row costs an unpack and
+// FMAs per weight.  Here the roles are swapped so the tensor core does the
+// rows: the weight tile is the 128-row A operand (TMA, 128-byte swizzle,
+// `tcgen05.mma.cta_group::1.kind::f16` with M = 128), the token rows padded to
+// N = 16 are the B operand (TMA zero-fills rows >= M), and the 128 x 16 fp32
+// accumulator lives in TMEM (two buffers = 32 columns).  Work units are
+// (128-row weight tile, K slice) so that ~one unit per SM streams its slice
+// with a deep (10-stage) TMA pipeline; each unit writes its fp32 partial tile
+// [128 rows][16] to a workspace, and a small reduce kernel sums the K slices
+// in a fixed order and applies the epilogue (store, residual add with the
+// HF rounding order, SwiGLU over 128-row interleaved gate/up blocks).  The
+// result of a row m does not depend on M (columns never mix in the MMA and
+// the K split depends on N and K only).
+//
+// Warp roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer (one
+// elected lane), warps 2-5 epilogue (TMEM lane quarter = warp % 4).  Every
+// wait is bounded (mbar_wait) and reports through the status word.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace sc {
+
+namespace {
+constexpr int kSkBM = 128;  // weight rows per tile (MMA M)
+constexpr int kSkBN = 16;   // token rows (MMA N)
+constexpr int kSkBK = 64;   // 128 bytes of bf16 per row
+constexpr int kSkStages = 10;
+constexpr int kSkABytes = kSkBM * kSkBK * 2;  // 16 KB
+constexpr int kSkBBytes = kSkBN * kSkBK * 2;  // 2 KB
+constexpr int kSkStageBytes = kSkABytes + kSkBBytes;
+constexpr int kSkSmem = kSkStages * kSkStageBytes + 1024 + 256;
+constexpr int kSkThreads = 192;
+
+struct alignas(8) SkBars {
+  uint64_t full[kSkStages];
+  uint64_t empty[kSkStages];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+}  // namespace
+
+__global__ void __launch_bounds__(kSkThreads, 1)
+    skinny_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                      int N, int K, int splits, float* ws, int* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  SkBars* bars = reinterpret_cast<SkBars*>(smem + kSkStages * kSkStageBytes);
+  const int warp = warp_id(), lane = lane_id();
+  const int tiles = (N + kSkBM - 1) / kSkBM;
+  const int num_kb = (K + kSkBK - 1) / kSkBK;
+  const int units = tiles * splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSkStages; ++s) mbar_init(&bars->full[s], 1), mbar_init(&bars->empty[s], 1);
+    for (int b = 0; b < 2; ++b) mbar_init(&bars->tmem_full[b], 1), mbar_init(&bars->tmem_empty[b], 4);
+    mbar_init(&bars->drain, 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, 32);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+  pdl_wait();  // x comes from the previous kernel
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool issued[kSkStages];
+      uint32_t issued_phase[kSkStages];
+      for (int s = 0; s < kSkStages; ++s) issued[s] = false, issued_phase[s] = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int tile = u / splits, ks = u % splits;
+        const int kb0 = ks * num_kb / splits, kb1 = (ks + 1) * num_kb / splits;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&bars->empty[stage], phase ^ 1, status, kStatusTimeoutSmemEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * kSkStageBytes;
+          mbar_arrive_expect_tx(&bars->full[stage], kSkStageBytes);
+          tma_load_2d(sa, &tmap_w, &bars->full[stage], kb * kSkBK, tile * kSkBM);
+          tma_load_2d(sa + kSkABytes, &tmap_x, &bars->full[stage], kb * kSkBK, 0);
+          issued[stage] = true;
+          issued_phase[stage] = phase;
+          if (++stage == kSkStages) stage = 0, phase ^= 1;
+        }
+      }
+      for (int s = 0; s < kSkStages; ++s)
+        if (issued[s]) mbar_wait(&bars->full[s], issued_phase[s], status, kStatusTimeoutDrain);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(kSkBM, kSkBN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true, any = false;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
+        const int ks = u % splits;
+        const int kb0 = ks * num_kb / splits, kb1 = (ks + 1) * num_kb / splits;
+        const int buf = local & 1;
+        const uint32_t tphase = (local >> 1) & 1;
+        if (!mbar_wait(&bars->tmem_empty[buf], tphase ^ 1, status, kStatusTimeoutTmemEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tacc = tmem_base + buf * kSkBN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&bars->full[stage], phase, status, kStatusTimeoutTmaFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kSkStageBytes);
+          const uint32_t sb = sa + kSkABytes;
+#pragma unroll
+          for (int k = 0; k < kSkBK / 16; ++k)
+            tc_mma_f16(tacc, make_desc_kmajor_sw128(sa + k * 32), make_desc_kmajor_sw128(sb + k * 32), idesc,
+                       (kb != kb0 || k != 0) ? 1u : 0u);
+          any = true;
+          tc_commit(&bars->empty[stage]);
+          if (++stage == kSkStages) stage = 0, phase ^= 1;
+        }
+        if (!ok) break;
+        tc_commit(&bars->tmem_full[buf]);
+      }
+      if (any) {
+        tc_commit(&bars->drain);
+        mbar_wait(&bars->drain, 0, status, kStatusTimeoutDrain);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    int local = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      const int tile = u / splits, ks = u % splits;
+      const int buf = local & 1;
+      const uint32_t tphase = (local >> 1) & 1;
+      if (!mbar_wait(&bars->tmem_full[buf], tphase, status, kStatusTimeoutTmemFull)) break;
+      tc_fence_after();
+      uint32_t r[16];
+      tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * kSkBN, r);
+      tmem_ld_wait();
+      const int row = tile * kSkBM + quarter * 32 + lane;
+      if (row < N) {
+        float4* d = reinterpret_cast<float4*>(ws + ((size_t)ks * N + row) * kSkBN);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          d[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]), __uint_as_float(r[4 * i + 2]),
+                             __uint_as_float(r[4 * i + 3]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->tmem_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, 32);
+}
+
+// Sum the K slices in order and apply the epilogue; one thread per (row m, output j).
+__global__ void skinny_reduce_kernel(SkinnyArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int outs = a.epi == SKINNY_SWIGLU ? a.N / 2 : a.N;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= outs * a.M) return;
+  const int m = idx / outs, j = idx % outs;
+  auto sum_row = [&](int n) {
+    float v = 0.f;
+    for (int s = 0; s < a.splits; ++s) v += a.ws[((size_t)s * a.N + n) * kSkBN + m];
+    return v;
+  };
+  float out;
+  if (a.epi == SKINNY_SWIGLU) {
+    const int blk = j >> 7, i = j & 127;
+    const float g = bf16_round(sum_row(blk * 256 + i)), u = bf16_round(sum_row(blk * 256 + 128 + i));
+    out = bf16_round(silu_f(g)) * u;
+  } else {
+    out = sum_row(j);
+    if (a.epi == SKINNY_RESIDUAL) out = __bfloat162float(a.residual[(size_t)m * a.ldr + j]) + bf16_round(out);
+  }
+  a.out[(size_t)m * a.ldo + j] = __float2bfloat16_rn(out);
+}
+
+// K slices per tile: the smallest split whose units fill the persistent CTAs'
+// rounds to >= 90% (units / (rounds * SMs)), at least 4 k-blocks per unit;
+// else the best filling found.
+int skinny_splits(int N, int K, int num_sms) {
+  const int tiles = (N + kSkBM - 1) / kSkBM;
+  const int num_kb = (K + kSkBK - 1) / kSkBK;
+  const int max_s = num_kb / 4 < 1 ? 1 : (num_kb / 4 > 32 ? 32 : num_kb / 4);
+  int best = 1;
+  double best_eff = 0.0;
+  for (int s = 1; s <= max_s; ++s) {
+    const int units = tiles * s;
+    const int rounds = (units + num_sms - 1) / num_sms;
+    const double eff = (double)units / ((double)rounds * num_sms);
+    if (eff >= 0.9) return s;
+    if (eff > best_eff + 1e-9) best_eff = eff, best = s;
+  }
+  return best;
+}
+
+cudaError_t skinny_gemm(const SkinnyArgs& a, cudaStream_t stream) {
+  if (a.M < 1 || a.M > kSkBN || a.K % kSkBK != 0 || a.N % 2 != 0) return cudaErrorInvalidValue;
+  if (a.epi == SKINNY_SWIGLU && a.N % 256 != 0) return cudaErrorInvalidValue;
+  CUtensorMap tw, tx;
+  if (!make_tmap_2d_bf16(&tw, a.w, a.K, a.N, a.ldw, kSkBK, kSkBM, true)) return cudaErrorInvalidValue;
+  if (!make_tmap_2d_bf16(&tx, a.x, a.K, a.M, a.ldx, kSkBK, kSkBN, true)) return cudaErrorInvalidValue;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaFuncSetAttribute(skinny_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSkSmem);
+    attr_done = true;
+  }
+  const int tiles = (a.N + kSkBM - 1) / kSkBM;
+  const int units = tiles * a.splits;
+  const int grid = units < a.num_sms ? units : a.num_sms;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kSkThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSkSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_mma_kernel, tw, tx, a.N, a.K, a.splits, a.ws, a.status);
+  if (e != cudaSuccess) return e;
+  const int outs = (a.epi == SKINNY_SWIGLU ? a.N / 2 : a.N) * a.M;
+  cfg.gridDim = dim3((outs + 255) / 256, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  return cudaLaunchKernelEx(&cfg, skinny_reduce_kernel, a);
+}
+
+}  // namespace sc

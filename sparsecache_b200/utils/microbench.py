@@ -65,6 +65,22 @@ def main() -> None:
                 res[f"gemv_rows_{name}_M{M}"] = {"us": t, "GBps": gbs, "frac_of_measured_hbm": gbs / HBM_GBS}
             del w
 
+    if "skinny" in only:
+        # tensor-core skinny GEMM vs the CUDA-core GEMV at batched-verify row counts (70B widths)
+        for name, N, K in (("qkv", 10240, 8192), ("down", 8192, 28672), ("gate_up", 57344, 8192)):
+            w = (torch.randn(N, K, device=dev) * 0.02).to(bf)
+            splits = int(ext.skinny_splits(N, K))
+            ws = torch.empty(splits * N * 16, device=dev)
+            for M in (1, 2, 5, 8, 16):
+                x = torch.randn(M, K, device=dev).to(bf)
+                epi = 2 if name == "gate_up" else 1
+                o = torch.empty(M, N // 2 if epi == 2 else N, device=dev, dtype=bf)
+                t = timeit(lambda: ext.skinny_gemm(x, w, epi, o, o if epi == 1 else None, ws), n=20, warm=5)
+                gbs = N * K * 2 / (t * 1e-6) / 1e9
+                res[f"skinny_{name}_M{M}"] = {"us": t, "GBps": gbs, "frac_of_measured_hbm": gbs / HBM_GBS,
+                                               "splits": splits}
+            del w
+
     if "gemv" in only:
         for name, N, K in (("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 28672, 4096),
                            ("down", 4096, 14336), ("lm_head", 128256, 4096)):

@@ -471,3 +471,31 @@ def test_lse_gather_forward_backward(cuda_device):
     torch.cuda.synchronize()
     assert _rel_err(lse2, lse2r) < 1e-2 and _rel_err(z2, z2r) < 2e-2
     assert _rel_err(f.grad, fr.grad) < 3e-2
+
+
+@pytest.mark.parametrize("M", [1, 5, 16])
+def test_skinny_tensor_core_gemm(cuda_device, M):
+    """Swap-AB tcgen05 GEMM for a few rows: store / residual / SwiGLU against fp32, rows independent of M."""
+    ext = _ext()
+    K, N = 4096, 1536
+    x = (torch.randn(M, K, device=cuda_device) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda_device) * 0.02).to(torch.bfloat16)
+    splits = int(ext.skinny_splits(N, K))
+    ws = torch.empty(splits * N * 16, device=cuda_device)
+    out = torch.empty(M, N, device=cuda_device, dtype=torch.bfloat16)
+    ext.skinny_gemm(x, w, 0, out, None, ws)
+    ref = x.float() @ w.float().T
+    res = torch.randn(M, N, device=cuda_device).to(torch.bfloat16)
+    out_r = res.clone()
+    ext.skinny_gemm(x, w, 1, out_r, out_r, ws)
+    act = torch.empty(M, N // 2, device=cuda_device, dtype=torch.bfloat16)
+    ext.skinny_gemm(x, w, 2, act, None, ws)
+    one = torch.empty(1, N, device=cuda_device, dtype=torch.bfloat16)
+    ext.skinny_gemm(x[:1].contiguous(), w, 0, one, None, ws)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    assert _rel_err(out, ref) < 1e-2
+    assert _rel_err(out_r, res.float() + ref.to(torch.bfloat16).float()) < 1e-2
+    g, u = ref.view(M, N // 256, 2, 128)[:, :, 0].reshape(M, -1), ref.view(M, N // 256, 2, 128)[:, :, 1].reshape(M, -1)
+    assert _rel_err(act, torch.nn.functional.silu(g) * u) < 2e-2
+    assert torch.equal(out[:1], one)
