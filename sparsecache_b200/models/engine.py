@@ -192,9 +192,10 @@ class _CountingExt:
     """Proxy over the extension that counts kernel launches issued from the host."""
 
     _NOT_KERNELS = {"status", "num_sms", "gemv_argmax_grid", "attention_decode_cluster", "attention_decode_outer",
+                    "skinny_splits",
                     "shared_empty",
                     "shared_open", "shared_close"}
-    _MULTI = {"gemm_store", "gemm_residual"}
+    _MULTI = {"gemm_store", "gemm_residual", "skinny_gemm", "skinny_qkv", "skinny_allreduce"}
 
     def __init__(self, ext) -> None:
         self._ext = ext

@@ -687,13 +687,9 @@ void cacheblend_select(Tensor dev_part, int64_t n_kv_heads, int64_t dev_mode, in
   check_cuda(sc::cacheblend_select(a, cur_stream()), "cacheblend_select");
 }
 
-// out = epilogue(x @ w^T) for M <= 16 rows on the tensor cores; returns kernels launched.
-int64_t skinny_gemm(Tensor x, Tensor w, int64_t epi, Tensor out, c10::optional<Tensor> residual, Tensor ws,
-                    int64_t splits) {
-  const c10::cuda::CUDAGuard guard(x.device());
+sc::SkinnyArgs skinny_base(const Tensor& x, const Tensor& w, int64_t epi, const Tensor& ws, int64_t splits) {
   check_matrix(x, "x");
   check_matrix(w, "w");
-  check_matrix(out, "out");
   TORCH_CHECK(x.size(1) == w.size(1), "K mismatch");
   CHECK_F32(ws);
   sc::SkinnyArgs a{};
@@ -705,6 +701,21 @@ int64_t skinny_gemm(Tensor x, Tensor w, int64_t epi, Tensor out, c10::optional<T
   a.ldx = (int)x.stride(0);
   a.ldw = (int)w.stride(0);
   a.epi = (int)epi;
+  a.num_sms = num_sms();
+  a.splits = splits > 0 ? (int)splits : sc::skinny_splits(a.N, a.K, a.num_sms);
+  TORCH_CHECK(ws.numel() >= (int64_t)a.splits * a.N * 16, "workspace [splits][N][16] too small");
+  a.ws = ws.data_ptr<float>();
+  a.status = status_tensor(w).data_ptr<int>();
+  return a;
+}
+
+// out = epilogue(x @ w^T) for M <= 16 rows on the tensor cores; returns kernels launched.
+int64_t skinny_gemm(Tensor x, Tensor w, int64_t epi, Tensor out, c10::optional<Tensor> residual, Tensor ws,
+                    int64_t splits) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(epi == sc::SKINNY_STORE || epi == sc::SKINNY_RESIDUAL || epi == sc::SKINNY_SWIGLU, "epilogue");
+  auto a = skinny_base(x, w, epi, ws, splits);
+  check_matrix(out, "out");
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   a.ldo = (int)out.stride(0);
   TORCH_CHECK(out.size(0) >= a.M && out.size(1) == (epi == sc::SKINNY_SWIGLU ? a.N / 2 : a.N), "out shape");
@@ -714,13 +725,65 @@ int64_t skinny_gemm(Tensor x, Tensor w, int64_t epi, Tensor out, c10::optional<T
     a.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
     a.ldr = (int)residual->stride(0);
   }
-  a.num_sms = num_sms();
-  a.splits = splits > 0 ? (int)splits : sc::skinny_splits(a.N, a.K, a.num_sms);
-  TORCH_CHECK(ws.numel() >= (int64_t)a.splits * a.N * 16, "workspace [splits][N][16] too small");
-  a.ws = ws.data_ptr<float>();
-  a.status = status_tensor(w).data_ptr<int>();
   check_cuda(sc::skinny_gemm(a, cur_stream()), "skinny_gemm");
   return 2;
+}
+
+// Fused QKV (RoPE + K/V cache write) for M <= 16 rows on the tensor cores.
+int64_t skinny_qkv(Tensor x, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_cache, Tensor pos,
+                   Tensor rope_table, int64_t n_q_heads, int64_t n_kv_heads, Tensor ws, c10::optional<Tensor> slot) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto a = skinny_base(x, w_qkv, sc::SKINNY_QKV, ws, -1);
+  TORCH_CHECK(w_qkv.size(0) == (n_q_heads + 2 * n_kv_heads) * 128, "w_qkv rows");
+  TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(2) == 128 && k_cache.is_contiguous(), "k_cache");
+  CHECK_I32(pos); CHECK_F32(rope_table);
+  a.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
+  a.ldq = (int)q_out.stride(0);
+  a.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr());
+  a.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
+  a.cache_cap = (int)k_cache.size(1);
+  a.pos = pos.data_ptr<int>();
+  if (slot.has_value() && slot->defined()) { CHECK_I32(*slot); a.slot = slot->data_ptr<int>(); }
+  a.rope_table = reinterpret_cast<const float2*>(rope_table.data_ptr<float>());
+  a.n_q_heads = (int)n_q_heads;
+  a.n_kv_heads = (int)n_kv_heads;
+  check_cuda(sc::skinny_gemm(a, cur_stream()), "skinny_qkv");
+  return 2;
+}
+
+// Row-parallel projection whose fp32 partial rows go to every rank's receive slot (tensor parallel).
+int64_t skinny_allreduce(Tensor x, Tensor w, std::vector<int64_t> dst_ptrs, std::vector<int64_t> flag_ptrs,
+                         int64_t sender, int64_t epoch, c10::optional<Tensor> epoch_ptr, int64_t epoch_mul,
+                         Tensor counter, Tensor ws) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto a = skinny_base(x, w, sc::SKINNY_ALLREDUCE, ws, -1);
+  TORCH_CHECK(dst_ptrs.size() == flag_ptrs.size() && !dst_ptrs.empty() && dst_ptrs.size() <= 8, "1..8 ranks");
+  for (size_t r = 0; r < dst_ptrs.size(); ++r) {
+    a.ar_dst[r] = reinterpret_cast<float*>(dst_ptrs[r]);
+    a.ar_flag[r] = reinterpret_cast<int*>(flag_ptrs[r]);
+  }
+  a.ar_tp = (int)dst_ptrs.size();
+  a.ar_sender = (int)sender;
+  a.ar_epoch = (int)epoch;
+  if (epoch_ptr.has_value() && epoch_ptr->defined()) {
+    CHECK_I32(*epoch_ptr);
+    a.ar_epoch_ptr = epoch_ptr->data_ptr<int>();
+    a.ar_epoch_mul = (int)epoch_mul;
+  }
+  CHECK_I32(counter);
+  a.counter = reinterpret_cast<unsigned int*>(counter.data_ptr<int>());
+  check_cuda(sc::skinny_gemm(a, cur_stream()), "skinny_allreduce");
+  return 2;
+}
+
+void row_argmax(Tensor logits, Tensor out_token) {
+  const c10::cuda::CUDAGuard guard(logits.device());
+  check_matrix(logits, "logits");
+  CHECK_I32(out_token);
+  TORCH_CHECK(out_token.numel() >= logits.size(0), "out_token [M]");
+  check_cuda(sc::row_argmax_bf16(reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), (int)logits.stride(0),
+                                 (int)logits.size(0), (int)logits.size(1), out_token.data_ptr<int>(), cur_stream()),
+             "row_argmax");
 }
 
 int64_t skinny_splits(int64_t N, int64_t K) { return sc::skinny_splits((int)N, (int)K, num_sms()); }
@@ -1027,6 +1090,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("skinny_gemm", &skinny_gemm, py::arg("x"), py::arg("w"), py::arg("epi"), py::arg("out"),
         py::arg("residual") = py::none(), py::arg("ws"), py::arg("splits") = -1);
   m.def("skinny_splits", &skinny_splits);
+  m.def("skinny_qkv", &skinny_qkv, py::arg("x"), py::arg("w_qkv"), py::arg("q_out"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("pos"), py::arg("rope_table"), py::arg("n_q_heads"), py::arg("n_kv_heads"),
+        py::arg("ws"), py::arg("slot") = py::none());
+  m.def("skinny_allreduce", &skinny_allreduce);
+  m.def("row_argmax", &row_argmax);
   m.def("lse_gather_backward", &lse_gather_backward, py::arg("logits"), py::arg("ids"), py::arg("lse"),
         py::arg("g_lse"), py::arg("g_z"), py::arg("dlogits"));
   m.def("index_i32", &index_i32);

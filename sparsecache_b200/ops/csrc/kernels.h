@@ -251,7 +251,7 @@ struct SelectArgs {
 cudaError_t cacheblend_select(const SelectArgs& a, cudaStream_t stream);
 
 // Skinny tensor-core GEMM for M <= 16 token rows (skinny_tc.cu).
-enum SkinnyEpi { SKINNY_STORE = 0, SKINNY_RESIDUAL = 1, SKINNY_SWIGLU = 2 };
+enum SkinnyEpi { SKINNY_STORE = 0, SKINNY_RESIDUAL = 1, SKINNY_SWIGLU = 2, SKINNY_QKV = 3, SKINNY_ALLREDUCE = 4 };
 struct SkinnyArgs {
   const __nv_bfloat16* x;  // [M, K] row stride ldx
   const __nv_bfloat16* w;  // [N, K] row stride ldw
@@ -265,9 +265,31 @@ struct SkinnyArgs {
   int splits;
   int num_sms;
   int* status;
+  // SKINNY_QKV: fused QKV rows (q heads, k heads, v heads of 128): RoPE on
+  // q/k at position *pos + m, q to q_out, k/v to the cache at slot (*slot or
+  // *pos) + m -- the GEMV_QKV epilogue
+  __nv_bfloat16* q_out;
+  int ldq;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  int cache_cap;
+  const int* pos;
+  const int* slot;
+  const float2* rope_table;
+  int n_q_heads, n_kv_heads;
+  // SKINNY_ALLREDUCE: fp32 partial rows to every rank's receive slot
+  // ar_dst[r][sender][m][N], then the last CTA releases ar_flag[r] = epoch
+  float* ar_dst[8];
+  int* ar_flag[8];
+  int ar_tp, ar_sender, ar_epoch;
+  const int* ar_epoch_ptr;
+  int ar_epoch_mul;
+  unsigned int* counter;
 };
 int skinny_splits(int N, int K, int num_sms);
 cudaError_t skinny_gemm(const SkinnyArgs& a, cudaStream_t stream);
+// Row argmax over bf16 logits [M, V] (first index on ties) -> out_token[M].
+cudaError_t row_argmax_bf16(const __nv_bfloat16* logits, int ld, int M, int V, int* out_token, cudaStream_t stream);
 
 // Row log-sum-exp + logit gathers (forward) and the logits gradient
 // g_lse * softmax + sum_j g_z[j] * onehot(ids[j]) (backward), lm_loss.cu.

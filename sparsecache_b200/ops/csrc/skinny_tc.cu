@@ -190,29 +190,123 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, 32);
 }
 
-// Sum the K slices in order and apply the epilogue; one thread per (row m, output j).
+// Sum the K slices in order and apply the epilogue; one thread per (row m, output j)
+// (QKV: per (row, rotation pair)).  No thread leaves before the block barrier of
+// the all-reduce publication.
 __global__ void skinny_reduce_kernel(SkinnyArgs a) {
+  __shared__ int s_last;
   pdl_wait();
   pdl_launch_dependents();
-  const int outs = a.epi == SKINNY_SWIGLU ? a.N / 2 : a.N;
+  const int outs = (a.epi == SKINNY_SWIGLU || a.epi == SKINNY_QKV) ? a.N / 2 : a.N;
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= outs * a.M) return;
-  const int m = idx / outs, j = idx % outs;
+  const bool active = idx < outs * a.M;
+  const int m = active ? idx / outs : 0, j = active ? idx % outs : 0;
   auto sum_row = [&](int n) {
     float v = 0.f;
     for (int s = 0; s < a.splits; ++s) v += a.ws[((size_t)s * a.N + n) * kSkBN + m];
     return v;
   };
-  float out;
-  if (a.epi == SKINNY_SWIGLU) {
-    const int blk = j >> 7, i = j & 127;
-    const float g = bf16_round(sum_row(blk * 256 + i)), u = bf16_round(sum_row(blk * 256 + 128 + i));
-    out = bf16_round(silu_f(g)) * u;
-  } else {
-    out = sum_row(j);
-    if (a.epi == SKINNY_RESIDUAL) out = __bfloat162float(a.residual[(size_t)m * a.ldr + j]) + bf16_round(out);
+  if (active) {
+    if (a.epi == SKINNY_SWIGLU) {
+      const int blk = j >> 7, i = j & 127;
+      const float g = bf16_round(sum_row(blk * 256 + i)), u = bf16_round(sum_row(blk * 256 + 128 + i));
+      a.out[(size_t)m * a.ldo + j] = __float2bfloat16_rn(bf16_round(silu_f(g)) * u);
+    } else if (a.epi == SKINNY_QKV) {
+      const int head = j >> 6, i = j & 63;
+      const int r0 = head * 128 + i;
+      const float v0 = sum_row(r0), v1 = sum_row(r0 + 64);
+      const int pos0 = *a.pos;
+      const int slot0 = a.slot != nullptr ? *a.slot : pos0;
+      const bool is_q = head < a.n_q_heads;
+      const bool is_k = !is_q && head < a.n_q_heads + a.n_kv_heads;
+      float o0 = v0, o1 = v1;
+      if (is_q || is_k) {
+        const float2 cs = a.rope_table[(size_t)(pos0 + m) * 64 + i];
+        o0 = v0 * cs.x - v1 * cs.y;
+        o1 = v1 * cs.x + v0 * cs.y;
+      }
+      __nv_bfloat16* dst;
+      if (is_q) {
+        dst = a.q_out + (size_t)m * a.ldq + head * 128;
+      } else {
+        const int kvh = is_k ? head - a.n_q_heads : head - a.n_q_heads - a.n_kv_heads;
+        dst = (is_k ? a.k_cache : a.v_cache) + ((size_t)kvh * a.cache_cap + slot0 + m) * 128;
+      }
+      dst[i] = __float2bfloat16_rn(o0);
+      dst[i + 64] = __float2bfloat16_rn(o1);
+    } else if (a.epi == SKINNY_ALLREDUCE) {
+      const float v = sum_row(j);
+      for (int r = 0; r < a.ar_tp; ++r) a.ar_dst[r][((size_t)a.ar_sender * a.M + m) * a.N + j] = v;
+    } else {
+      float out = sum_row(j);
+      if (a.epi == SKINNY_RESIDUAL) out = __bfloat162float(a.residual[(size_t)m * a.ldr + j]) + bf16_round(out);
+      a.out[(size_t)m * a.ldo + j] = __float2bfloat16_rn(out);
+    }
   }
-  a.out[(size_t)m * a.ldo + j] = __float2bfloat16_rn(out);
+  if (a.epi != SKINNY_ALLREDUCE) return;
+  // the last block to finish publishes this rank's partial to every rank
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(a.counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (s_last) {
+    __threadfence_system();
+    const int epoch = a.ar_epoch_ptr ? *a.ar_epoch_ptr * a.ar_epoch_mul + a.ar_epoch : a.ar_epoch;
+    if ((int)threadIdx.x < a.ar_tp)
+      asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(a.ar_flag[threadIdx.x]), "r"(epoch) : "memory");
+    if (threadIdx.x == 0) *a.counter = 0u;
+  }
+}
+
+// One block per row: argmax over bf16 logits, first index on ties (the GEMV
+// LM head's rule).
+__global__ void row_argmax_kernel(const __nv_bfloat16* logits, int ld, int V, int* out) {
+  __shared__ float sv[8];
+  __shared__ int si[8];
+  pdl_wait();
+  pdl_launch_dependents();
+  const __nv_bfloat16* row = logits + (size_t)blockIdx.x * ld;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int c = threadIdx.x; c < V / 8; c += blockDim.x) {
+    const uint4 u = reinterpret_cast<const uint4*>(row)[c];
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = unpack_bf16x2(w[q]);
+      const int i0 = c * 8 + 2 * q;
+      if (f.x > bv || (f.x == bv && i0 < bi)) bv = f.x, bi = i0;
+      if (f.y > bv || (f.y == bv && i0 + 1 < bi)) bv = f.y, bi = i0 + 1;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
+  }
+  if ((threadIdx.x & 31) == 0) sv[threadIdx.x >> 5] = bv, si[threadIdx.x >> 5] = bi;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    bv = sv[0], bi = si[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) bv = sv[w], bi = si[w];
+    out[blockIdx.x] = bi;
+  }
+}
+
+cudaError_t row_argmax_bf16(const __nv_bfloat16* logits, int ld, int M, int V, int* out_token, cudaStream_t stream) {
+  if (M < 1 || V % 8 != 0 || ld % 8 != 0) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, row_argmax_kernel, logits, ld, V, out_token);
 }
 
 // K slices per tile: the smallest split whose units fill the persistent CTAs'
@@ -237,6 +331,9 @@ int skinny_splits(int N, int K, int num_sms) {
 cudaError_t skinny_gemm(const SkinnyArgs& a, cudaStream_t stream) {
   if (a.M < 1 || a.M > kSkBN || a.K % kSkBK != 0 || a.N % 2 != 0) return cudaErrorInvalidValue;
   if (a.epi == SKINNY_SWIGLU && a.N % 256 != 0) return cudaErrorInvalidValue;
+  if (a.epi == SKINNY_QKV && (a.N % 128 != 0 || a.N != (a.n_q_heads + 2 * a.n_kv_heads) * 128))
+    return cudaErrorInvalidValue;
+  if (a.epi == SKINNY_ALLREDUCE && (a.ar_tp < 1 || a.ar_tp > 8 || a.counter == nullptr)) return cudaErrorInvalidValue;
   CUtensorMap tw, tx;
   if (!make_tmap_2d_bf16(&tw, a.w, a.K, a.N, a.ldw, kSkBK, kSkBM, true)) return cudaErrorInvalidValue;
   if (!make_tmap_2d_bf16(&tx, a.x, a.K, a.M, a.ldx, kSkBK, kSkBN, true)) return cudaErrorInvalidValue;
@@ -260,7 +357,7 @@ cudaError_t skinny_gemm(const SkinnyArgs& a, cudaStream_t stream) {
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_mma_kernel, tw, tx, a.N, a.K, a.splits, a.ws, a.status);
   if (e != cudaSuccess) return e;
-  const int outs = (a.epi == SKINNY_SWIGLU ? a.N / 2 : a.N) * a.M;
+  const int outs = ((a.epi == SKINNY_SWIGLU || a.epi == SKINNY_QKV) ? a.N / 2 : a.N) * a.M;
   cfg.gridDim = dim3((outs + 255) / 256, 1, 1);
   cfg.blockDim = dim3(256, 1, 1);
   cfg.dynamicSmemBytes = 0;

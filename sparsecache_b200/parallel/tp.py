@@ -128,7 +128,7 @@ class TPEngine:
     """Sequence/tensor-parallel prefill over a TP group with fused collectives."""
 
     def __init__(self, cfg: ModelConfig, weights: EngineWeights, group: TPGroup, *, max_rows: int,
-                 max_positions: int = 65536) -> None:
+                 max_positions: int = 65536, verify_backend: str = "skinny") -> None:
         self.full_cfg = cfg
         self.tp = group.size
         self.rank = group.rank
@@ -168,6 +168,18 @@ class TPEngine:
         self.ar_stride = 2 * cfg.n_layers + 64
         L = cfg.n_layers
         self.seed_layers = tuple(sorted({min(2, L - 1), L // 2, max(0, L - 3)})) if L >= 3 else tuple(range(L))
+        # verify rows (M <= 8) on the tensor-core skinny GEMM ("skinny") or the
+        # CUDA-core multi-row GEMV ("gemv"); every verify call uses the same one,
+        # so a row's result never depends on how many rows were verified with it
+        if verify_backend not in ("skinny", "gemv"):
+            raise ValueError("verify_backend is skinny or gemv")
+        self.verify_backend = verify_backend
+        if verify_backend == "skinny":
+            lc, w0 = self.lcfg, weights.layers[0]
+            shapes = [tuple(w0.w_qkv.shape), tuple(w0.w_o.shape), tuple(w0.w_gu.shape), tuple(w0.w_down.shape),
+                      tuple(weights.lm_head.shape)]
+            need = max(int(self.ext.skinny_splits(n, k)) * n * 16 for n, k in shapes)
+            self.skinny_ws = torch.empty(need, device=group.device, dtype=torch.float32)
 
     @classmethod
     def from_full(cls, cfg: ModelConfig, full: EngineWeights, group: TPGroup, **kw) -> "TPEngine":
@@ -395,7 +407,7 @@ class TPEngine:
         b["pos"][:3].fill_(T)
 
     def allreduce(self, x: torch.Tensor, w: torch.Tensor, k: int, residual: torch.Tensor,
-                  norm_w: torch.Tensor | None = None) -> None:
+                  norm_w: torch.Tensor | None = None, skinny: bool = False) -> None:
         """residual += sum over ranks of x @ w^T (row-parallel GEMV, M <= 8 rows), fused over peer memory.
 
         ``k`` numbers the all-reduce inside the current device step (epoch
@@ -410,8 +422,13 @@ class TPEngine:
         buf, ptrs = (self.ar_o_buf, self.ar_o_ptrs) if odd else (self.ar_d_buf, self.ar_d_ptrs)
         kind = FLAG_AR_O if odd else FLAG_AR_D
         flags = [self._flag_addr(r, kind, self.rank) for r in range(self.tp)]
-        ext.gemv_allreduce(x, w, norm_w, cfg.rms_eps, ptrs, flags, self.rank, k, step, self.ar_stride,
-                           self.ar_counters[0:1] if odd else self.ar_counters[1:2])
+        counter = self.ar_counters[0:1] if odd else self.ar_counters[1:2]
+        if skinny:
+            if norm_w is not None:
+                raise ValueError("the skinny all-reduce takes normalised rows")
+            ext.skinny_allreduce(x, w, ptrs, flags, self.rank, k, step, self.ar_stride, counter, self.skinny_ws)
+        else:
+            ext.gemv_allreduce(x, w, norm_w, cfg.rms_eps, ptrs, flags, self.rank, k, step, self.ar_stride, counter)
         recv = buf.view(torch.float32)[: self.tp * M * d].view(self.tp, M, d)
         ext.rs_reduce(recv, self.flags[kind], k, TIMEOUT_NS, self.status, residual, residual, None, None,
                       cfg.rms_eps, step, self.ar_stride)
@@ -427,6 +444,9 @@ class TPEngine:
         b = eng._decode_buffers()
         h, pos = b["h"][:M], b["pos"]
         feat = eng.ws.get("tp_feat", (len(self.seed_layers), eng.MAX_ROWS, cfg.d_model), torch.bfloat16)
+        if verify and self.verify_backend == "skinny":
+            self._verify_rows_skinny(slot, splits, M, feat)
+            return
         for layer, lw in enumerate(eng.w.layers):
             ext.gemv_qkv(h, lw.w_qkv, lw.ln1, cfg.rms_eps, b["q"][:M], slot.k(layer), slot.v(layer), pos[0:1],
                          eng.rope, lc.n_heads, lc.n_kv_heads, slot=pos[1:2])
@@ -444,6 +464,32 @@ class TPEngine:
         else:
             ext.gemv_argmax(h, eng.w.lm_head, eng.w.norm, cfg.rms_eps, b["pv"], b["pi"], b["counter"], b["tok"],
                             b["log"], b["gen"], eng.w.embed, h, pos, 4)
+
+    def _verify_rows_skinny(self, slot: KVSlot, splits: int, M: int, feat: torch.Tensor) -> None:
+        """A verify step on the tensor-core skinny GEMM: norm, QKV (RoPE + cache), attention,
+        o + all-reduce, norm, gate/up SwiGLU, down + all-reduce per layer; final norm, logits, argmax."""
+        eng, ext, cfg, lc = self.engine, self.ext, self.full_cfg, self.lcfg
+        b = eng._decode_buffers()
+        h, pos = b["h"][:M], b["pos"]
+        x = eng.ws.get("sk_x", (eng.MAX_ROWS, cfg.d_model), torch.bfloat16)[:M]
+        ws = self.skinny_ws
+        for layer, lw in enumerate(eng.w.layers):
+            ext.rmsnorm(h, None, lw.ln1, cfg.rms_eps, x)
+            ext.skinny_qkv(x, lw.w_qkv, b["q"][:M], slot.k(layer), slot.v(layer), pos[0:1], eng.rope, lc.n_heads,
+                           lc.n_kv_heads, ws, slot=pos[1:2])
+            ext.attention_decode(b["q"][:M], slot.k(layer), slot.v(layer), pos[0:1], lc.n_heads, eng.scale, splits,
+                                 b["attn"][:M], ws=b["attn_ws"], counters=b["attn_cnt"])
+            self.allreduce(b["attn"][:M], lw.w_o, 2 * layer + 1, h, skinny=True)
+            ext.rmsnorm(h, None, lw.ln2, cfg.rms_eps, x)
+            ext.skinny_gemm(x, lw.w_gu, 2, b["act"][:M], None, ws)
+            self.allreduce(b["act"][:M], lw.w_down, 2 * layer + 2, h, skinny=True)
+            if layer in self.seed_layers:
+                feat[self.seed_layers.index(layer), :M].copy_(h)
+        ext.rmsnorm(h, None, eng.w.norm, cfg.rms_eps, x)
+        logits = eng.ws.get("sk_logits", (eng.MAX_ROWS, cfg.vocab), torch.bfloat16)[:M]
+        ext.skinny_gemm(x, eng.w.lm_head, 0, logits, None, ws)
+        ext.row_argmax(logits, b["tok"])
+        ext.bump_counter(pos[3:4])
 
     def set_rows_state(self, position: int) -> None:
         """Host write of the next rows' position / slot / key count (the step counter pos[3] is kept)."""
@@ -467,7 +513,7 @@ class TPEngine:
         if not use_graph:
             self._decode_step(slot, splits, M, verify=True)
             return b["tok"][:M]
-        key = ("tpv", id(slot), splits, M)
+        key = ("tpv", id(slot), splits, M, self.verify_backend)
         graph = eng._graphs.get(key)
         if graph is None:
             # a real warm step (its K/V rows are rewritten by the next verify at
@@ -481,7 +527,8 @@ class TPEngine:
                 self._decode_step(slot, splits, M, verify=True)
             eng._graphs[key] = graph
         graph.replay()
-        ext.launches += 7 * len(eng.w.layers) + 2
+        per_layer = 12 if self.verify_backend == "skinny" else 7
+        ext.launches += per_layer * len(eng.w.layers) + (5 if self.verify_backend == "skinny" else 2)
         return b["tok"][:M]
 
     def decode_breakdown(self, slot: KVSlot, reps: int = 3) -> dict[str, float]:

@@ -499,3 +499,47 @@ def test_skinny_tensor_core_gemm(cuda_device, M):
     g, u = ref.view(M, N // 256, 2, 128)[:, :, 0].reshape(M, -1), ref.view(M, N // 256, 2, 128)[:, :, 1].reshape(M, -1)
     assert _rel_err(act, torch.nn.functional.silu(g) * u) < 2e-2
     assert torch.equal(out[:1], one)
+
+
+def test_skinny_qkv_allreduce_and_row_argmax(cuda_device):
+    """Skinny QKV (RoPE + cache) against the GEMV QKV, the all-reduce epilogue on one rank, row argmax."""
+    cfg = get_model_config("tiny128")
+    ext = _ext()
+    nq, nkv, K, cap, M = 4, 2, 512, 300, 5
+    x = torch.randn(M, K, device=cuda_device).to(torch.bfloat16)
+    w = (torch.randn((nq + 2 * nkv) * 128, K, device=cuda_device) * 0.05).to(torch.bfloat16)
+    table = rope_table(cfg, 1024, cuda_device)
+    pos = torch.tensor([123], device=cuda_device, dtype=torch.int32)
+    ws = torch.empty(64 * 4096 * 16, device=cuda_device)
+    outs = []
+    for fn in ("gemv", "skinny"):
+        kc = torch.zeros(nkv, cap, 128, device=cuda_device, dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        q = torch.empty(M, nq * 128, device=cuda_device, dtype=torch.bfloat16)
+        if fn == "gemv":
+            ext.gemv_qkv(x, w, None, 1e-5, q, kc, vc, pos, table, nq, nkv)
+        else:
+            ext.skinny_qkv(x, w, q, kc, vc, pos, table, nq, nkv, ws)
+        outs.append((q, kc, vc))
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    for a, b in zip(outs[0], outs[1]):
+        assert _rel_err(b, a.float()) < 2e-2
+    assert outs[1][1][:, 123:123 + M].abs().sum() > 0 and outs[1][1][:, 123 + M:].abs().sum() == 0
+    # all-reduce epilogue, one rank: the partial rows land in the receive slot and the flag is released
+    N = 1024
+    w2 = (torch.randn(N, K, device=cuda_device) * 0.05).to(torch.bfloat16)
+    recv = torch.zeros(1, M, N, device=cuda_device)
+    flags = torch.zeros(2, device=cuda_device, dtype=torch.int32)
+    counter = torch.zeros(1, device=cuda_device, dtype=torch.int32)
+    ext.skinny_allreduce(x, w2, [recv.data_ptr()], [flags.data_ptr()], 0, 7, None, 0, counter, ws)
+    torch.cuda.synchronize()
+    assert _rel_err(recv[0], x.float() @ w2.float().T) < 1e-2
+    assert int(flags[0]) == 7 and int(counter[0]) == 0
+    # row argmax: first index on ties, as torch.argmax
+    logits = torch.randn(M, 128256, device=cuda_device).to(torch.bfloat16)
+    logits[2, 100] = logits[2, 5000] = 50.0
+    tok = torch.empty(M, device=cuda_device, dtype=torch.int32)
+    ext.row_argmax(logits, tok)
+    torch.cuda.synchronize()
+    assert tok.tolist() == logits.float().argmax(-1).tolist() and int(tok[2]) == 100
