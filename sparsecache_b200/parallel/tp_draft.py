@@ -280,7 +280,7 @@ class TPEagleDrafter:
 
 
 def speculative_generate(tpe: TPEngine, drafter: TPEagleDrafter | None, slot, *, prompt_tokens: int, max_new: int,
-                         use_graph: bool = True) -> dict:
+                         use_graph: bool = True, proposal_trace=None) -> dict:
     """Greedy generation from the state ``first_token`` left (token 0 in the log, position T).
 
     With a drafter: verify [last token] once (seed features), then repeat
@@ -289,7 +289,13 @@ def speculative_generate(tpe: TPEngine, drafter: TPEagleDrafter | None, slot, *,
     host read per iteration.  Without a drafter every step verifies one row
     (plain greedy decoding through the verify path).  Returns the tokens
     (first token included), accepted drafts per iteration and step counts.
+    ``proposal_trace``: a path that receives the first proposal (seed and
+    draft ids, atomically, first writer wins) for trace verification.
     """
+    import time
+
+    from ..serving.live.trace import publish_proposal_trace
+
     eng = tpe.engine
     b = eng._decode_buffers()
     feat = eng.ws.get("tp_feat", (len(tpe.seed_layers), eng.MAX_ROWS, tpe.full_cfg.d_model), torch.bfloat16)
@@ -310,10 +316,14 @@ def speculative_generate(tpe: TPEngine, drafter: TPEagleDrafter | None, slot, *,
             new = [pred[0]]
         else:
             g = drafter.gamma
+            started_ns = time.time_ns()
             drafts = drafter.propose(slot, rows[0:1], feat[:, n_acc], P, use_graph=use_graph)
             rows[1:1 + g].copy_(drafts)
             pred = tpe.verify(slot, rows[:1 + g], P, use_graph=use_graph).tolist()
             d = rows[1:1 + g].tolist()
+            if proposal_trace is not None and not accepted:
+                publish_proposal_trace(proposal_trace, method="eagle3", proposal_started_at_ns=started_ns,
+                                       seed_token_ids=[tokens[-1]], draft_token_ids=d)
             n_acc = 0
             while n_acc < g and d[n_acc] == pred[n_acc]:
                 n_acc += 1

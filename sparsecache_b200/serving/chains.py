@@ -22,7 +22,7 @@ its reuse-pipeline variant experiments/reuse_cacheblend_pipeline.py:896-1141)
 ``grafted_draft_batch`` / ``progressive_graft_chain`` (reference: :985-1310)
     zero-replay variants: the tokens drafted on a smaller view are carried
     over ("grafted") when the view grows, and only the final full-KV verifier
-    judges them, once.
+    checks them, once.
 """
 from __future__ import annotations
 

@@ -20,6 +20,49 @@ from pathlib import Path
 from typing import Any, Sequence
 
 
+def publish_proposal_trace(destination: str | Path, *, method: str, proposal_started_at_ns: int,
+                           seed_token_ids, draft_token_ids, methods: Sequence[str] = ("eagle3",)) -> dict | None:
+    """Write one drafter proposal record atomically; the first writer wins.
+
+    The record (state "ready", seed token, draft token ids, start and
+    creation timestamps in ns) is written to a temporary file and linked into
+    place with ``os.link``, which fails if the destination exists, so a later
+    proposal for the same destination is dropped (returns None) and readers
+    never see a partial file.  Methods outside ``methods`` publish nothing.
+    Counterpart of the proposal trace the reference's EAGLE-3 screens read
+    (tests/test_eagle_proposal_trace.py).
+    """
+    import os
+    import tempfile
+    import time
+
+    if method not in methods:
+        return None
+    dest = Path(destination)
+    if dest.exists():
+        return None
+
+    def ids(x) -> list[int]:
+        return [int(v) for v in (x.reshape(-1).tolist() if hasattr(x, "reshape") else x)]
+
+    seed = ids(seed_token_ids)
+    payload = {"state": "ready", "method": method, "proposal_started_at_ns": int(proposal_started_at_ns),
+               "created_at_ns": max(time.time_ns(), int(proposal_started_at_ns)),
+               "seed_token_id": seed[-1] if seed else None, "draft_token_ids": ids(draft_token_ids)}
+    dest.parent.mkdir(parents=True, exist_ok=True)
+    fd, tmp = tempfile.mkstemp(dir=dest.parent, prefix=dest.name, suffix=".tmp")
+    try:
+        with os.fdopen(fd, "w") as f:
+            json.dump(payload, f)
+        try:
+            os.link(tmp, dest)
+        except FileExistsError:
+            return None
+    finally:
+        os.unlink(tmp)
+    return payload
+
+
 def load_jsonl(path: Path) -> list[dict[str, Any]]:
     if not Path(path).is_file():
         raise FileNotFoundError(path)

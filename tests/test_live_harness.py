@@ -246,3 +246,26 @@ def test_latency_cell_validator():
     bad = validate_latency_cell([row(0, "full_target_then_pipeline"), row(0, "full_target_then_pipeline"),
                                  row(2, "full_target_then_pipeline")], expected_count=2, max_unattributed_ms=5.0)
     assert not bad["passed"] and len(bad["failures"]) >= 3
+
+
+def test_proposal_trace_is_atomic_and_first_writer_wins(tmp_path):
+    import json
+
+    import torch
+
+    from sparsecache_b200.serving.live.trace import publish_proposal_trace
+
+    dest = tmp_path / "proposal.json"
+    rec = publish_proposal_trace(dest, method="eagle3", proposal_started_at_ns=1,
+                                 seed_token_ids=torch.tensor([17], dtype=torch.int32),
+                                 draft_token_ids=torch.tensor([[18, 19, 20]], dtype=torch.int32))
+    stored = json.loads(dest.read_text())
+    assert rec == stored and stored["state"] == "ready" and stored["seed_token_id"] == 17
+    assert stored["draft_token_ids"] == [18, 19, 20] and stored["created_at_ns"] >= stored["proposal_started_at_ns"]
+    assert not list(tmp_path.glob("*.tmp"))
+    assert publish_proposal_trace(dest, method="eagle3", proposal_started_at_ns=2, seed_token_ids=[99],
+                                  draft_token_ids=[[100]]) is None
+    assert json.loads(dest.read_text()) == stored
+    other = tmp_path / "other.json"
+    assert publish_proposal_trace(other, method="eagle", proposal_started_at_ns=1, seed_token_ids=[1],
+                                  draft_token_ids=[[2]]) is None and not other.exists()
