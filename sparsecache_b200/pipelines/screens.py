@@ -152,6 +152,60 @@ def sparse_page_crossover(engine, context_lengths: Sequence[int], fractions: Seq
     return rows
 
 
+def parse_fractions(text: str) -> tuple[float, ...]:
+    """Comma-separated visible fractions in (0, 1]; the full view (1.0) must be among them."""
+    vals = tuple(float(x) for x in text.split(",") if x.strip())
+    if not vals or any(not 0.0 < v <= 1.0 for v in vals) or len(set(vals)) != len(vals):
+        raise ValueError("fractions must be unique values in (0, 1]")
+    if 1.0 not in vals:
+        raise ValueError("the fractions must include the full view 1.0 (the paired reference)")
+    return vals
+
+
+def balanced_fraction_schedule(fractions: Sequence[float], repeats: int) -> list[tuple[int, int, float]]:
+    """(repeat, order index, fraction): every repeat measures every fraction once, the order
+    rotated by one position per repeat so no fraction always runs first (warm-state bias)."""
+    n = len(fractions)
+    return [(r, i, fractions[(i + r) % n]) for r in range(repeats) for i in range(n)]
+
+
+def measurement_seed_token(vocab: int, repeat: int) -> int:
+    """A fixed ordinary-text seed token per repeat (clear of the low special ids)."""
+    return (1024 + repeat) % vocab
+
+
+def aggregate_crossover(rows: Sequence[dict]) -> dict[str, Any]:
+    """Per context length: draft-step time per visible fraction, speedup over the full view
+    paired by repeat, and the crossover (the largest fraction still faster than full).
+
+    Fails closed: every repeat must have measured every fraction of the context.
+    """
+    import statistics
+
+    out = {}
+    for T in sorted({r["context_tokens"] for r in rows}):
+        sub = [r for r in rows if r["context_tokens"] == T]
+        fracs = sorted({r["requested_fraction"] for r in sub})
+        reps = sorted({r.get("repeat", 0) for r in sub})
+        cell = {(r.get("repeat", 0), r["requested_fraction"]): r for r in sub}
+        missing = [(rp, f) for rp in reps for f in fracs if (rp, f) not in cell]
+        if missing:
+            raise ValueError(f"context {T}: incomplete fraction x repeat matrix, missing {missing[:4]}")
+        if 1.0 not in fracs:
+            raise ValueError(f"context {T}: no full-view reference")
+        per = {}
+        for f in fracs:
+            ms = [cell[(rp, f)]["draft_step_ms"] for rp in reps]
+            sp = [cell[(rp, 1.0)]["draft_step_ms"] / cell[(rp, f)]["draft_step_ms"] for rp in reps]
+            per[str(f)] = {"draft_step_ms_mean": statistics.fmean(ms), "speedup_vs_full_mean": statistics.fmean(sp),
+                           "speedup_vs_full_min": min(sp),
+                           "visible_fraction": statistics.fmean(cell[(rp, f)]["visible_fraction"] for rp in reps)}
+        faster = [f for f in fracs if f < 1.0 and per[str(f)]["speedup_vs_full_min"] > 1.0]
+        out[str(T)] = {"repeats": len(reps), "fractions": per,
+                       "crossover_fraction": max(faster) if faster else None}
+    return out
+
+
 def main(argv=None) -> None:
     import argparse
 
@@ -165,6 +219,7 @@ def main(argv=None) -> None:
     p.add_argument("--contexts", default="8192,32768")
     p.add_argument("--fractions", default="0.05,0.1,0.2,0.5")
     p.add_argument("--patterns", default=None, help="schema-1 layer-pattern JSON (default: generated)")
+    p.add_argument("--repeats", type=int, default=3, help="crossover repeats, fraction order rotated per repeat")
     a = p.parse_args(argv)
     cfg = get_model_config(a.model)
     ctxs = [int(x) for x in a.contexts.split(",")]
@@ -178,9 +233,17 @@ def main(argv=None) -> None:
         patterns.update(load_patterns(a.patterns, L))
     else:
         patterns.update({p["id"]: p["layer_indices"] for p in standard_patterns(L)["patterns"]})
+    vals = [float(x) for x in a.fractions.split(",") if x.strip()]
+    fractions = list(parse_fractions(",".join(map(str, vals + ([] if 1.0 in vals else [1.0])))))
+    cross = []
+    for T in ctxs:
+        for rep in range(a.repeats):
+            order = [f for r, _, f in balanced_fraction_schedule(fractions, a.repeats) if r == rep]
+            for i, row in enumerate(sparse_page_crossover(eng, [T], order, seed=rep)):
+                row.update(repeat=rep, order_index=i)
+                cross.append(row)
     print(json.dumps({"layer_draft": layer_draft_screen(eng, prompt, patterns, draft_tokens=a.draft_tokens),
-                      "sparse_page_crossover": sparse_page_crossover(
-                          eng, ctxs, [float(x) for x in a.fractions.split(",")])}, indent=1))
+                      "sparse_page_crossover": cross, "crossover_summary": aggregate_crossover(cross)}, indent=1))
 
 
 if __name__ == "__main__":

@@ -106,3 +106,27 @@ def test_crossover_queue_is_fail_closed(tmp_path):
     with pytest.raises(ValueError):
         run_crossover_job(qp, "crossover_llama3-8b_ctx32768", gate=lambda: {"passed": True}, runner=runner)
     assert len(calls) == 1
+
+
+def test_crossover_schedule_and_aggregate():
+    import pytest
+
+    from sparsecache_b200.pipelines.screens import (aggregate_crossover, balanced_fraction_schedule,
+                                                    measurement_seed_token, parse_fractions)
+
+    fr = parse_fractions("1,.1,.02")
+    sched = balanced_fraction_schedule(fr, 4)
+    assert len(sched) == 12
+    for r in range(4):
+        assert {f for rr, _, f in sched if rr == r} == set(fr)
+    assert [x[2] for x in sched[:3]] != [x[2] for x in sched[3:6]]
+    with pytest.raises(ValueError, match="include"):
+        parse_fractions(".02,.1")
+    assert measurement_seed_token(128256, 0) == 1024 and measurement_seed_token(128256, 1) == 1025
+    rows = [{"context_tokens": 1024, "requested_fraction": f, "visible_fraction": f, "repeat": r,
+             "draft_step_ms": 8.0 if f == 0.1 else (13.0 if f == 0.5 else 12.0)}
+            for r in range(3) for f in (0.1, 0.5, 1.0)]
+    agg = aggregate_crossover(rows)["1024"]
+    assert agg["crossover_fraction"] == 0.1 and agg["fractions"]["0.1"]["speedup_vs_full_mean"] == 1.5
+    with pytest.raises(ValueError, match="incomplete"):
+        aggregate_crossover(rows[:-1])
