@@ -40,6 +40,36 @@ from ..serving.progressive import (Document, TrancheStager, continuous_graft_cha
                                    stage_document_sets)
 
 
+def parse_bandwidths(text: str) -> tuple[float, ...]:
+    """Comma-separated link rates in Gbit/s: positive, unique, returned ascending."""
+    vals = [float(x) for x in text.split(",") if x.strip()]
+    if not vals or any(v <= 0 for v in vals) or len(set(vals)) != len(vals):
+        raise ValueError("bandwidths must be unique positive values")
+    return tuple(sorted(vals))
+
+
+def common_prefix_length(a: Sequence[int], b: Sequence[int]) -> int:
+    n = 0
+    for x, y in zip(a, b):
+        if x != y:
+            break
+        n += 1
+    return n
+
+
+def target_kv_bytes_per_token(model_dir: str | Path) -> int:
+    """bf16 K+V bytes per token of an HF Llama-style config.json (all layers)."""
+    cfg = json.loads((Path(model_dir) / "config.json").read_text())
+    head_dim = cfg.get("head_dim") or cfg["hidden_size"] // cfg["num_attention_heads"]
+    kv = cfg.get("num_key_value_heads", cfg["num_attention_heads"])
+    return int(cfg["num_hidden_layers"] * 2 * kv * head_dim * 2)
+
+
+def transfer_ms(nbytes: float, gbps: float) -> float:
+    """Wire time of ``nbytes`` at ``gbps`` Gbit/s."""
+    return nbytes * 8 / (gbps * 1e6)
+
+
 def auto_draft_tokens(*, prompt_tokens: int, first_stage_tokens: int, bytes_per_token: float, transport_gbps: float,
                       tpot_ms: float, max_draft_tokens: int, utilization: float = 1.0) -> tuple[int, float]:
     """(draft horizon, residual wire ms) of one request."""

@@ -226,3 +226,18 @@ def test_pd_run_summary_and_graft_triggers():
     trig = t["triggers"]["s2_batch_instability"]
     assert trig["triggered"] == 1 and trig["true_positive"] == 1 and trig["missed_positive"] == 0
     assert paired_delta([3, 1], [1, 1])["positive"] == 1
+
+
+def test_pd_link_helpers(tmp_path):
+    from sparsecache_b200.pipelines.pd import (common_prefix_length, parse_bandwidths, target_kv_bytes_per_token,
+                                               transfer_ms)
+
+    assert parse_bandwidths("100,25,50") == (25.0, 50.0, 100.0)
+    assert common_prefix_length([1, 2, 3], [1, 2, 9]) == 2
+    for bad in ("25,25", "0"):
+        with pytest.raises(ValueError):
+            parse_bandwidths(bad)
+    (tmp_path / "config.json").write_text(json.dumps({"num_hidden_layers": 32, "num_attention_heads": 32,
+                                                      "num_key_value_heads": 8, "hidden_size": 4096}))
+    assert target_kv_bytes_per_token(tmp_path) == 131072
+    assert transfer_ms(8_000_000_000, 100.0) == pytest.approx(640.0)
