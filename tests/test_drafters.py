@@ -200,3 +200,42 @@ def test_propose_matches_reference_style_prefix_rerun():
                                                        sin[:len(prefix)], stage))
         prefix.append(int(model.target_ids(logits[0, -1].argmax())))
     assert prop == prefix[1:]
+
+
+def test_tp_drafter_shards_reassemble_the_module():
+    """Every rank's shard of the EAGLE drafter (heads, 128-row gate/up blocks, memory heads)
+    concatenates back to the module's weights; replicated parts are identical."""
+    import torch
+
+    from sparsecache_b200.models.sparse_kv_eagle import SparseKVEagleConfig, SparseKVEagleDrafter
+    from sparsecache_b200.models.weights import split_gate_up
+    from sparsecache_b200.parallel.tp_draft import TPDraftWeights
+
+    cfg = SparseKVEagleConfig(target_hidden_size=512, hidden_size=512, intermediate_size=1024, head_dim=128,
+                              num_attention_heads=4, num_key_value_heads=2, num_memory_heads=2, num_memory_layers=3,
+                              num_seed_layers=3, target_vocab_size=4096, draft_vocab_size=1024)
+    torch.manual_seed(0)
+    m = SparseKVEagleDrafter(cfg)
+    tp = 2
+    shards = [TPDraftWeights.from_module(m, r, tp, "cpu") for r in range(tp)]
+    at, mlp = m.midlayer.self_attn, m.midlayer.mlp
+    bf = lambda t: t.detach().to(torch.bfloat16)  # noqa: E731
+    q = torch.cat([s.w_qkv[:2 * 128] for s in shards])
+    k = torch.cat([s.w_qkv[2 * 128:3 * 128] for s in shards])
+    v = torch.cat([s.w_qkv[3 * 128:] for s in shards])
+    assert torch.equal(q, bf(at.q_proj.weight)) and torch.equal(k, bf(at.k_proj.weight))
+    assert torch.equal(v, bf(at.v_proj.weight))
+    assert torch.equal(torch.cat([s.w_o for s in shards], 1), bf(at.o_proj.weight))
+    gates, ups = zip(*(split_gate_up(s.w_gu) for s in shards))
+    assert torch.equal(torch.cat(gates), bf(mlp.gate_proj.weight)) and torch.equal(torch.cat(ups), bf(mlp.up_proj.weight))
+    assert torch.equal(torch.cat([s.w_down for s in shards], 1), bf(mlp.down_proj.weight))
+    for i in range(3):
+        qi = torch.cat([s.w_memq[i * 128:(i + 1) * 128] for s in shards])
+        assert torch.equal(qi, bf(m.memory_attention.query[i].weight))
+        assert torch.equal(torch.cat([s.w_memo[i] for s in shards], 1), bf(m.memory_attention.output[i].weight))
+    assert all(torch.equal(s.lm_head, shards[0].lm_head) and torch.equal(s.fc, shards[0].fc) for s in shards)
+    assert shards[0].d2t.dtype == torch.int32 and abs(shards[0].adapter_scale - torch.sigmoid(torch.tensor(-4.0)).item()) < 1e-6
+    import pytest
+
+    with pytest.raises(ValueError):
+        TPDraftWeights.from_module(m, 0, 3, "cpu")
