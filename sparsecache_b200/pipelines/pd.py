@@ -137,6 +137,44 @@ def aggregate(rows: Sequence[dict]) -> dict[str, Any]:
             "response_gain_ms": stats([t["response_ms"] - c["response_ms"] for t, c, _ in cells])}
 
 
+def build_result_row(index: int, request, schedule: str, ranking, sets, out: dict, *, arms: Sequence[str],
+                     gamma: int, residual: float | None, bytes_per_token: int, prefill_ms: float,
+                     protocol: dict, window: str = "inf") -> dict[str, Any]:
+    """One request's result row in the reference layout from the arms' results.
+
+    ``out`` maps "full_target" (``run_full_target``'s dict), "chain" and
+    optionally "fixed" (``ChainResult``) to their results; ``arms`` is the
+    order they ran in.
+    """
+    target = dict(out["full_target"])
+    target_ids = target.pop("tokens")
+
+    def chain_cell(res, configured):
+        return {"timing_token_ids": list(res.token_ids), "configured_draft_tokens": configured,
+                "timing_token_match_target": list(res.token_ids) == target_ids,
+                "speedup_vs_full_target": target["response_ms"] / res.response_ms, **res.pipeline_record()}
+
+    pipe = out["chain"]
+    order = ("full_target_then_pipeline" if list(arms).index("full_target") < list(arms).index("chain")
+             else "pipeline_then_full_target")
+    chains = {window: {
+        "timing_token_ids": list(pipe.token_ids), "configured_draft_tokens": gamma,
+        "estimated_residual_wire_ms": residual,
+        "timing_token_match_target": list(pipe.token_ids) == target_ids,
+        "pipeline": pipe.pipeline_record(),
+        "pipeline_speedup_vs_full_target": target["response_ms"] / pipe.response_ms,
+        "paired_fixed_control": chain_cell(out["fixed"], gamma) if "fixed" in out else None,
+        "measurement_order": order, "arm_order": "->".join(arms)}}
+    T = request.prompt_tokens
+    return {"dataset_index": index, "prompt_tokens": T, "anchor_tokens": len(request.prefix) + len(request.suffix),
+            "document_tokens": sum(len(d) for d in request.documents), "document_pages": len(request.documents),
+            "logical_bf16_kv_bytes": T * bytes_per_token, "producer": {"prefill_ms": prefill_ms},
+            "schedules": {schedule: {"ranking": list(ranking), "stage_document_counts": [len(x) for x in sets],
+                                     "full_target": {"timing_token_ids": target_ids, **target},
+                                     "chains": chains}},
+            "protocol": protocol}
+
+
 def main(argv=None) -> None:
     from ..config import get_model_config
     from ..models.engine import B200Engine
@@ -157,6 +195,7 @@ def main(argv=None) -> None:
                    help="also run the fixed first-stage-view chain on the same staged request")
     p.add_argument("--output", type=Path, required=True)
     a = p.parse_args(argv)
+    free, total = torch.cuda.mem_get_info()
     cfg = get_model_config(a.model)
     eng = B200Engine.random(cfg, seed=0, device="cuda", max_positions=65536)
     reqs = make_requests(a.workload, cfg)[: a.requests]
@@ -167,7 +206,8 @@ def main(argv=None) -> None:
     protocol = {"schedules": [a.schedule], "commit_windows": [window], "transport_gbps": a.transport_gbps,
                 "draft_tokens": a.draft_tokens, "max_new_tokens": a.max_new_tokens,
                 "stage_fractions": list(fractions), "fixed_token_horizon": True, "paired_measurement": True,
-                "paired_fixed_control": a.paired_fixed_control, "model": a.model, "workload": a.workload}
+                "paired_fixed_control": a.paired_fixed_control, "model": a.model, "workload": a.workload,
+                "require_exclusive_gpu": True, "initial_gpu_used_bytes": int(total - free)}
     with open(a.output, "w") as f:
         for i, r in enumerate(reqs):
             T = r.prompt_tokens
@@ -208,32 +248,8 @@ def main(argv=None) -> None:
                     out[arm] = continuous_graft_chain(eng, stager, seed_token=seed, prompt_tokens=T,
                                                       max_draft_tokens=gamma, max_new_tokens=a.max_new_tokens,
                                                       grow_view=(arm == "chain"))
-            target = out["full_target"]
-            target_ids = target.pop("tokens")
-
-            def chain_cell(res, configured):
-                return {"timing_token_ids": list(res.token_ids), "configured_draft_tokens": configured,
-                        "timing_token_match_target": list(res.token_ids) == target_ids,
-                        "speedup_vs_full_target": target["response_ms"] / res.response_ms,
-                        **res.pipeline_record()}
-
-            pipe = out["chain"]
-            chains = {window: {
-                "timing_token_ids": list(pipe.token_ids), "configured_draft_tokens": gamma,
-                "estimated_residual_wire_ms": residual,
-                "timing_token_match_target": list(pipe.token_ids) == target_ids,
-                "pipeline": pipe.pipeline_record(),
-                "pipeline_speedup_vs_full_target": target["response_ms"] / pipe.response_ms,
-                "paired_fixed_control": chain_cell(out["fixed"], gamma) if "fixed" in out else None,
-                "measurement_order": "->".join(arms)}}
-            row = {"dataset_index": i, "prompt_tokens": T, "anchor_tokens": len(r.prefix) + len(r.suffix),
-                   "document_tokens": sum(len(d) for d in r.documents), "document_pages": len(docs),
-                   "logical_bf16_kv_bytes": T * bytes_per_token, "producer": {"prefill_ms": prefill_ms},
-                   "schedules": {a.schedule: {"ranking": list(ranking),
-                                              "stage_document_counts": [len(x) for x in sets],
-                                              "full_target": {"timing_token_ids": target_ids, **target},
-                                              "chains": chains}},
-                   "protocol": protocol}
+            row = build_result_row(i, r, a.schedule, ranking, sets, out, arms=arms, gamma=gamma, residual=residual,
+                                   bytes_per_token=bytes_per_token, prefill_ms=prefill_ms, protocol=protocol)
             rows.append(row)
             f.write(json.dumps(row, default=str) + "\n")
     print(json.dumps(aggregate(rows), indent=2))

@@ -241,3 +241,37 @@ def test_pd_link_helpers(tmp_path):
                                                       "num_key_value_heads": 8, "hidden_size": 4096}))
     assert target_kv_bytes_per_token(tmp_path) == 131072
     assert transfer_ms(8_000_000_000, 100.0) == pytest.approx(640.0)
+
+
+def test_pd_rows_feed_validator_summary_and_aggregate():
+    from types import SimpleNamespace
+
+    from sparsecache_b200.pipelines.analysis import summarize_run
+    from sparsecache_b200.pipelines.pd import aggregate, build_result_row
+    from sparsecache_b200.serving.live.validate import validate_latency_cell
+    from sparsecache_b200.serving.progressive import ChainResult
+
+    proto = {"schedules": ["query"], "commit_windows": ["inf"], "transport_gbps": 50.0, "draft_tokens": 4,
+             "fixed_token_horizon": True, "paired_measurement": True, "require_exclusive_gpu": True,
+             "initial_gpu_used_bytes": 0}
+    rows = []
+    for i in range(4):
+        req = SimpleNamespace(prompt_tokens=100, prefix=[1] * 4, suffix=[2] * 6, documents=[[3] * 45, [4] * 45])
+        toks = (7, 8, 9, 10)
+        trace = ({"stage": 0, "drafted": 2, "draft_token_ids": [8, 9]},
+                 {"stage": 1, "verified": True, "accepted_pending": 2, "rejected_pending": 0, "drafted": 0})
+        chain = ChainResult(toks, (8, 9), 2, 5.0, 20.0, 1, (0.5, 0.5),
+                            {"total_h2d_ms": 1.0, "stage_wire_ms": [2.0, 3.0], "stage_wire_wait_ms": [0.5]},
+                            trace, 4.0, 1)
+        out = {"full_target": {"tokens": list(toks), "first_ready_ms": 10.0, "response_ms": 30.0,
+                               "seed_forward_ms": 0.0, "decode_ms": 20.0, "transfer": {"total_h2d_ms": 1.0}},
+               "chain": chain, "fixed": chain}
+        arms = ["full_target", "chain", "fixed"] if i % 2 == 0 else ["fixed", "chain", "full_target"]
+        rows.append(build_result_row(i, req, "query", [0, 1], [{0}, {0, 1}], out, arms=arms, gamma=4,
+                                     residual=None, bytes_per_token=128, prefill_ms=3.0, protocol=proto))
+    v = validate_latency_cell(rows, expected_count=4, max_unattributed_ms=100.0)
+    assert v["passed"], v
+    s = summarize_run(rows)
+    assert s["latency"]["saved_vs_full_target_ms"]["mean"] == 10.0 and s["paired_fixed_control"] is not None
+    agg = aggregate(rows)
+    assert agg["token_equality_rate"] == 1.0 and agg["response_gain_ms"]["mean"] == 10.0
