@@ -731,7 +731,8 @@ int64_t skinny_gemm(Tensor x, Tensor w, int64_t epi, Tensor out, c10::optional<T
 
 // Fused QKV (RoPE + K/V cache write) for M <= 16 rows on the tensor cores.
 int64_t skinny_qkv(Tensor x, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_cache, Tensor pos,
-                   Tensor rope_table, int64_t n_q_heads, int64_t n_kv_heads, Tensor ws, c10::optional<Tensor> slot) {
+                   Tensor rope_table, int64_t n_q_heads, int64_t n_kv_heads, Tensor ws, c10::optional<Tensor> slot,
+                   c10::optional<Tensor> pos_rows, int64_t seq_stride) {
   const c10::cuda::CUDAGuard guard(x.device());
   auto a = skinny_base(x, w_qkv, sc::SKINNY_QKV, ws, -1);
   TORCH_CHECK(w_qkv.size(0) == (n_q_heads + 2 * n_kv_heads) * 128, "w_qkv rows");
@@ -744,6 +745,12 @@ int64_t skinny_qkv(Tensor x, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor 
   a.cache_cap = (int)k_cache.size(1);
   a.pos = pos.data_ptr<int>();
   if (slot.has_value() && slot->defined()) { CHECK_I32(*slot); a.slot = slot->data_ptr<int>(); }
+  if (pos_rows.has_value() && pos_rows->defined()) {
+    CHECK_I32(*pos_rows);
+    TORCH_CHECK(pos_rows->numel() >= a.M && seq_stride >= 0, "pos_rows [M] and a sequence stride");
+    a.pos_rows = pos_rows->data_ptr<int>();
+    a.seq_stride = seq_stride;
+  }
   a.rope_table = reinterpret_cast<const float2*>(rope_table.data_ptr<float>());
   a.n_q_heads = (int)n_q_heads;
   a.n_kv_heads = (int)n_kv_heads;
@@ -1092,7 +1099,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("skinny_splits", &skinny_splits);
   m.def("skinny_qkv", &skinny_qkv, py::arg("x"), py::arg("w_qkv"), py::arg("q_out"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("pos"), py::arg("rope_table"), py::arg("n_q_heads"), py::arg("n_kv_heads"),
-        py::arg("ws"), py::arg("slot") = py::none());
+        py::arg("ws"), py::arg("slot") = py::none(), py::arg("pos_rows") = py::none(), py::arg("seq_stride") = 0);
   m.def("skinny_allreduce", &skinny_allreduce);
   m.def("row_argmax", &row_argmax);
   m.def("lse_gather_backward", &lse_gather_backward, py::arg("logits"), py::arg("ids"), py::arg("lse"),

@@ -277,6 +277,10 @@ struct SkinnyArgs {
   const int* slot;
   const float2* rope_table;
   int n_q_heads, n_kv_heads;
+  // batched decode: row m belongs to sequence m, at position pos_rows[m], and
+  // its cache starts seq_stride elements after row m-1's (null: one sequence)
+  const int* pos_rows;
+  long long seq_stride;
   // SKINNY_ALLREDUCE: fp32 partial rows to every rank's receive slot
   // ar_dst[r][sender][m][N], then the last CTA releases ar_flag[r] = epoch
   float* ar_dst[8];

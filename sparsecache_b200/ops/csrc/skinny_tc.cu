@@ -215,13 +215,20 @@ __global__ void skinny_reduce_kernel(SkinnyArgs a) {
       const int head = j >> 6, i = j & 63;
       const int r0 = head * 128 + i;
       const float v0 = sum_row(r0), v1 = sum_row(r0 + 64);
-      const int pos0 = *a.pos;
-      const int slot0 = a.slot != nullptr ? *a.slot : pos0;
+      int pos, slot;
+      size_t seq_off = 0;
+      if (a.pos_rows != nullptr) {  // batched decode: one sequence per row
+        pos = slot = a.pos_rows[m];
+        seq_off = (size_t)m * (size_t)a.seq_stride;
+      } else {
+        pos = *a.pos + m;
+        slot = (a.slot != nullptr ? *a.slot : *a.pos) + m;
+      }
       const bool is_q = head < a.n_q_heads;
       const bool is_k = !is_q && head < a.n_q_heads + a.n_kv_heads;
       float o0 = v0, o1 = v1;
       if (is_q || is_k) {
-        const float2 cs = a.rope_table[(size_t)(pos0 + m) * 64 + i];
+        const float2 cs = a.rope_table[(size_t)pos * 64 + i];
         o0 = v0 * cs.x - v1 * cs.y;
         o1 = v1 * cs.x + v0 * cs.y;
       }
@@ -230,7 +237,7 @@ __global__ void skinny_reduce_kernel(SkinnyArgs a) {
         dst = a.q_out + (size_t)m * a.ldq + head * 128;
       } else {
         const int kvh = is_k ? head - a.n_q_heads : head - a.n_q_heads - a.n_kv_heads;
-        dst = (is_k ? a.k_cache : a.v_cache) + ((size_t)kvh * a.cache_cap + slot0 + m) * 128;
+        dst = (is_k ? a.k_cache : a.v_cache) + seq_off + ((size_t)kvh * a.cache_cap + slot) * 128;
       }
       dst[i] = __float2bfloat16_rn(o0);
       dst[i + 64] = __float2bfloat16_rn(o1);

@@ -20,7 +20,8 @@ Per rank (one process per GPU, TP group = the whole world):
 
 Reported (rank 0, one JSON line; device time, max over ranks): TTFT p50/p99
 of CacheBlend vs full prefill, TPOT and decode tokens/s for greedy and
-speculative decoding, mean accepted drafts.  Batch 1 per TP group.
+speculative decoding, mean accepted drafts, and batched greedy decode
+(B sequences per step on the skinny tensor-core GEMMs, B <= 16).
 """
 from __future__ import annotations
 
@@ -150,6 +151,7 @@ def main(argv=None) -> None:
     p.add_argument("--ratio", type=float, default=0.15)
     p.add_argument("--check-layer", type=int, default=1)
     p.add_argument("--no-spec", action="store_true")
+    p.add_argument("--batches", default="8,16", help="batched greedy decode sizes (<= 16 sequences)")
     a = p.parse_args(argv)
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -221,6 +223,36 @@ def main(argv=None) -> None:
                 res["accepted"].append(out_s["mean_accepted"])
                 diff = next((k for k, (x, y) in enumerate(zip(out_s["tokens"], out_g["tokens"])) if x != y), None)
                 res["spec_equals_greedy"].append(diff)
+        # batched greedy decode: B requests prefilled (CacheBlend) into one batch of slots
+        batch_out = {}
+        cap = T_max + a.new_tokens + tp * 128 + 64
+        for B in [int(x) for x in a.batches.split(",") if x.strip()]:
+            if B > len(reqs) or B > tpe.MAX_BATCH:
+                continue
+            bslots = tpe.batch_slots(B, cap)
+            firsts, positions = [], []
+            own_slot = server.slot
+            for r, sl in zip(reqs[:B], bslots):
+                server.slot = sl
+                server.prefill_request(r, mode="cacheblend", max_new=a.new_tokens)
+                firsts.append(int(tpe.engine.generated_tokens(1)[0]))
+                positions.append(r.prompt_tokens)
+            server.slot = own_slot
+            tpe.start_batch(bslots, firsts, positions, max_new=a.new_tokens)
+            tpe.decode_batch(bslots, 2)  # capture + warm
+            tpe.start_batch(bslots, firsts, positions, max_new=a.new_tokens)
+            dist.barrier()
+            torch.cuda.synchronize()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+            ev[0].record()
+            tpe.decode_batch(bslots, a.new_tokens - 1)
+            ev[1].record()
+            torch.cuda.synchronize()
+            ms = _max_over_ranks(ev[0].elapsed_time(ev[1])) / (a.new_tokens - 1)
+            tpe.check_status()
+            batch_out[str(B)] = {"step_ms": ms, "decode_tokens_per_s": B * 1e3 / ms}
+            del bslots
+            tpe.engine.release_graphs()
         tpe.engine.release_graphs()
         if drafter is not None:
             drafter._graph = None
@@ -234,7 +266,8 @@ def main(argv=None) -> None:
                    "ttft_cacheblend_ms": {"p50": _pct(res["ttft_blend"], 0.5), "p99": _pct(res["ttft_blend"], 0.99)},
                    "ttft_full_prefill_ms": {"p50": _pct(res["ttft_full"], 0.5), "p99": _pct(res["ttft_full"], 0.99)},
                    "tpot_greedy_ms": statistics.fmean(res["tpot_greedy"]),
-                   "decode_tokens_per_s_greedy": 1e3 / statistics.fmean(res["tpot_greedy"])}
+                   "decode_tokens_per_s_greedy": 1e3 / statistics.fmean(res["tpot_greedy"]),
+                   "batched_greedy_decode": batch_out}
             if res["tpot_spec"]:
                 out.update(tpot_spec_ms=statistics.fmean(res["tpot_spec"]),
                            decode_tokens_per_s_spec=1e3 / statistics.fmean(res["tpot_spec"]),

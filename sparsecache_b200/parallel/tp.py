@@ -127,6 +127,8 @@ def local_config(cfg: ModelConfig, tp: int) -> ModelConfig:
 class TPEngine:
     """Sequence/tensor-parallel prefill over a TP group with fused collectives."""
 
+    MAX_BATCH = 16  # rows of a batched decode step (skinny tensor-core GEMM limit)
+
     def __init__(self, cfg: ModelConfig, weights: EngineWeights, group: TPGroup, *, max_rows: int,
                  max_positions: int = 65536, verify_backend: str = "skinny") -> None:
         self.full_cfg = cfg
@@ -151,9 +153,9 @@ class TPEngine:
         self.dev_buf, self.dev_ptrs = group.shared(self.tp * self.dev_stride * 4)
         self.flag_buf, self.flag_ptrs = group.shared(N_FLAG_KINDS * self.tp * 4)
         self.flags = self.flag_buf.view(torch.int32).view(N_FLAG_KINDS, self.tp)
-        # decode all-reduce receive slots [tp, 8 rows, d] fp32 (O and down)
-        self.ar_o_buf, self.ar_o_ptrs = group.shared(self.tp * 8 * d * 4)
-        self.ar_d_buf, self.ar_d_ptrs = group.shared(self.tp * 8 * d * 4)
+        # decode all-reduce receive slots [tp, MAX_BATCH rows, d] fp32 (O and down)
+        self.ar_o_buf, self.ar_o_ptrs = group.shared(self.tp * self.MAX_BATCH * d * 4)
+        self.ar_d_buf, self.ar_d_ptrs = group.shared(self.tp * self.MAX_BATCH * d * 4)
         self.ar_counters = torch.zeros(2, dtype=torch.int32, device=group.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=group.device)
         self.epoch = 0
@@ -611,6 +613,111 @@ class TPEngine:
             eng._graphs[key] = graph
         for _ in range(n_steps):
             graph.replay()
+
+    # ------------------------------------------------------ batched decode
+    def batch_slots(self, n_seq: int, capacity: int) -> list[KVSlot]:
+        """``n_seq`` slots back to back in one buffer (a batched step addresses them by stride)."""
+        if not 1 <= n_seq <= self.MAX_BATCH:
+            raise ValueError(f"1..{self.MAX_BATCH} sequences per batched step")
+        lc = self.lcfg
+        per = lc.n_layers * 2 * lc.n_kv_heads * capacity * lc.head_dim
+        buf = torch.empty(n_seq * per, dtype=torch.bfloat16, device=self.group.device)
+        return [KVSlot.from_buffer(lc, capacity, buf[i * per:(i + 1) * per]) for i in range(n_seq)]
+
+    def _batch_buffers(self) -> dict:
+        eng, cfg, lc, B = self.engine, self.full_cfg, self.lcfg, self.MAX_BATCH
+        ws = eng.ws
+        if "bt_gen" not in ws.bufs:
+            ws.bufs["bt_gen"] = torch.zeros(1, device=eng.device, dtype=torch.int64)
+        steps = eng.MAX_DECODE_TOKENS
+        return {"h": ws.get("bt_h", (B, cfg.d_model), torch.bfloat16),
+                "x": ws.get("bt_x", (B, cfg.d_model), torch.bfloat16),
+                "q": ws.get("bt_q", (B, lc.q_size), torch.bfloat16),
+                "attn": ws.get("bt_attn", (B, lc.q_size), torch.bfloat16),
+                "act": ws.get("bt_act", (B, lc.ffn), torch.bfloat16),
+                "logits": ws.get("bt_logits", (B, cfg.vocab), torch.bfloat16),
+                "tok": ws.get("bt_tok", (B,), torch.int32),
+                "pos": ws.get("bt_pos", (B,), torch.int32),
+                "gen": ws.bufs["bt_gen"],
+                "log": ws.get("bt_log", (steps, B), torch.int32)}
+
+    def start_batch(self, slots: list[KVSlot], first_tokens, positions, *, max_new: int) -> None:
+        """Seed a batched decode: sequence b has produced ``first_tokens[b]`` at ``positions[b]``."""
+        B = len(slots)
+        if self.verify_backend != "skinny":
+            raise ValueError("batched decode runs on the skinny tensor-core GEMM")
+        if len(first_tokens) != B or len(positions) != B:
+            raise ValueError("one first token and one position per sequence")
+        bb = self._batch_buffers()
+        if max_new > bb["log"].shape[0]:
+            raise ValueError("max_new exceeds the batched token log")
+        bb["tok"][:B].copy_(torch.as_tensor(list(first_tokens), dtype=torch.int32))
+        bb["pos"][:B].copy_(torch.as_tensor(list(positions), dtype=torch.int32))
+        bb["log"][0, :B].copy_(bb["tok"][:B])
+        bb["gen"].fill_(1)
+        self.ext.embedding(bb["tok"][:B], self.engine.w.embed, bb["h"][:B])
+
+    def _batch_step(self, slots: list[KVSlot], splits: int) -> None:
+        """One greedy step for every sequence (row b = sequence b, its own position and slot)."""
+        eng, ext, cfg, lc = self.engine, self.ext, self.full_cfg, self.lcfg
+        B = len(slots)
+        bb = self._batch_buffers()
+        h, x, pos_rows = bb["h"][:B], bb["x"][:B], bb["pos"][:B]
+        stride = (slots[1].data.data_ptr() - slots[0].data.data_ptr()) // 2 if B > 1 else 0
+        ws = self.skinny_ws
+        b = eng._decode_buffers()
+        for layer, lw in enumerate(eng.w.layers):
+            ext.rmsnorm(h, None, lw.ln1, cfg.rms_eps, x)
+            ext.skinny_qkv(x, lw.w_qkv, bb["q"][:B], slots[0].k(layer), slots[0].v(layer), pos_rows, eng.rope,
+                           lc.n_heads, lc.n_kv_heads, ws, pos_rows=pos_rows, seq_stride=stride)
+            for i, sl in enumerate(slots):
+                ext.attention_decode(bb["q"][i:i + 1], sl.k(layer), sl.v(layer), pos_rows[i:i + 1], lc.n_heads,
+                                     eng.scale, splits, bb["attn"][i:i + 1], ws=b["attn_ws"], counters=b["attn_cnt"])
+            self.allreduce(bb["attn"][:B], lw.w_o, 2 * layer + 1, h, skinny=True)
+            ext.rmsnorm(h, None, lw.ln2, cfg.rms_eps, x)
+            ext.skinny_gemm(x, lw.w_gu, 2, bb["act"][:B], None, ws)
+            self.allreduce(bb["act"][:B], lw.w_down, 2 * layer + 2, h, skinny=True)
+        ext.rmsnorm(h, None, eng.w.norm, cfg.rms_eps, x)
+        ext.skinny_gemm(x, eng.w.lm_head, 0, bb["logits"][:B], None, ws)
+        ext.row_argmax(bb["logits"][:B], bb["tok"])
+        bb["log"][:, :B].index_copy_(0, bb["gen"], bb["tok"][:B].view(1, B))
+        bb["gen"].add_(1)
+        pos_rows.add_(1)
+        ext.embedding(bb["tok"][:B], eng.w.embed, h)
+        ext.bump_counter(b["pos"][3:4])
+
+    def decode_batch(self, slots: list[KVSlot], n_steps: int, *, use_graph: bool = True) -> None:
+        """``n_steps`` batched greedy steps from the state ``start_batch`` (or earlier steps) left."""
+        eng = self.engine
+        if len({s.capacity for s in slots}) != 1:
+            raise ValueError("batched slots share one capacity")
+        splits = eng._decode_splits(slots[0].capacity)
+        if not use_graph:
+            for _ in range(n_steps):
+                self._batch_step(slots, splits)
+            return
+        key = ("tpb", tuple(id(s) for s in slots), splits)
+        graph = eng._graphs.get(key)
+        if graph is None:
+            bb = self._batch_buffers()
+            saved = {k: bb[k].clone() for k in ("h", "tok", "pos", "gen", "log")}
+            self._batch_step(slots, splits)  # warm step; the group's step counter keeps increasing
+            for k, v in saved.items():
+                bb[k].copy_(v)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self._batch_step(slots, splits)
+            eng._graphs[key] = graph
+        for _ in range(n_steps):
+            graph.replay()
+        per_layer = 10 + len(slots)
+        self.ext.launches += n_steps * (per_layer * len(eng.w.layers) + 6)
+
+    def batch_tokens(self, n_seq: int, n_tokens: int) -> list[list[int]]:
+        """Host copy of the batched token log: tokens[b] = sequence b's first ``n_tokens`` tokens."""
+        log = self._batch_buffers()["log"][:n_tokens, :n_seq].cpu()
+        return [log[:, b].tolist() for b in range(n_seq)]
 
     def check_status(self) -> None:
         st = int(self.status.item())

@@ -243,6 +243,21 @@ def _spec_worker(rank, world, port, out_dir):
         server.prefill_request(req, mode="cacheblend", max_new=n_new)
         out = server.decode(req, meta, max_new=n_new, speculative=True)
         result.update(drafter_equal=out["tokens"] == plain, drafter_accepted=out["accepted"])
+        # batched decode of 3 sequences == each sequence through the verifier on its own
+        reqs3 = make_requests("tiny_plumbing", cfg)[:3]
+        server.produce(reqs3)
+        bslots = tpe.batch_slots(3, 4096)
+        own_slot, firsts, alone = server.slot, [], []
+        for r3, sl in zip(reqs3, bslots):
+            server.slot = sl
+            server.prefill_request(r3, mode="cacheblend", max_new=n_new)
+            firsts.append(int(tpe.engine.generated_tokens(1)[0]))
+            alone.append(speculative_generate(tpe, None, sl, prompt_tokens=r3.prompt_tokens, max_new=n_new)["tokens"])
+        server.slot = own_slot
+        for use_graph in (False, True):
+            tpe.start_batch(bslots, firsts, [r3.prompt_tokens for r3 in reqs3], max_new=n_new)
+            tpe.decode_batch(bslots, n_new - 1, use_graph=use_graph)
+            result[f"batch_equal_graph{int(use_graph)}"] = tpe.batch_tokens(3, n_new) == alone
         tpe.check_status()
         tpe.engine.release_graphs()
         drafter._graph = None
@@ -278,3 +293,4 @@ def test_tp_cacheblend_and_speculative_decoding(tmp_path, world):
         assert all(res["draft_near_argmax"]), res
         assert res["draft_hidden_rel_err"] < 5e-2, res
         assert res["drafter_equal"], res
+        assert res["batch_equal_graph0"] and res["batch_equal_graph1"], res
