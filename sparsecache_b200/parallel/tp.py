@@ -62,6 +62,11 @@ FLAG_STAGE_X, FLAG_STAGE_X2 = 8, 9  # local: a peer shard has landed in the stag
 FLAG_DEV, FLAG_H, FLAG_STAGE_H = 10, 11, 12  # CacheBlend: deviation partials, residual all-gather
 N_FLAG_KINDS = 13
 TIMEOUT_NS = int(20e9)
+# Guard bands around every peer-mapped buffer: peers write into these buffers
+# from their kernels (partial tiles, all-reduce rows, flags), so an index bug
+# shows up as a changed guard band, checked by ``TPGroup.check_canaries``.
+CANARY_BYTES = 4096  # keeps the buffer start 4 KiB-aligned (TMA needs 16 B)
+CANARY_VALUE = 0xA5
 
 
 class TPGroup:
@@ -74,12 +79,22 @@ class TPGroup:
         self.device = torch.device("cuda", torch.cuda.current_device())
         self._opened: list[int] = []
         self._keep: list[torch.Tensor] = []
+        self._guards: list[tuple[torch.Tensor, int]] = []
 
     def shared(self, nbytes: int) -> tuple[torch.Tensor, list[int]]:
-        """Allocate nbytes on every rank; return (local buffer, device address of each rank's buffer)."""
+        """Allocate nbytes on every rank; return (local buffer, device address of each rank's buffer).
+
+        Each allocation carries ``CANARY_BYTES`` of guard band on both sides;
+        the returned buffer and addresses point past the leading band.
+        """
         ext = ops.ext()
-        buf, handle = ext.shared_empty(int(nbytes), self.device.index)
-        self._keep.append(buf)
+        nbytes, pad = int(nbytes), CANARY_BYTES
+        raw, handle = ext.shared_empty(nbytes + 2 * pad, self.device.index)
+        raw[:pad].fill_(CANARY_VALUE)
+        raw[pad + nbytes:].fill_(CANARY_VALUE)
+        self._keep.append(raw)
+        self._guards.append((raw, nbytes))
+        buf = raw[pad:pad + nbytes]
         handles = [None] * self.size
         dist.all_gather_object(handles, handle, group=self.group)
         ptrs = []
@@ -89,8 +104,14 @@ class TPGroup:
             else:
                 p = ext.shared_open(h)
                 self._opened.append(p)
-                ptrs.append(p)
+                ptrs.append(p + pad)
         return buf, ptrs
+
+    def check_canaries(self) -> list[int]:
+        """Indices (allocation order) of shared buffers whose guard bands were overwritten."""
+        pad = CANARY_BYTES
+        return [i for i, (raw, n) in enumerate(self._guards)
+                if not (bool((raw[:pad] == CANARY_VALUE).all()) and bool((raw[pad + n:] == CANARY_VALUE).all()))]
 
     def close(self) -> None:
         ext = ops.ext()

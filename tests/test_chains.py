@@ -130,3 +130,36 @@ def test_crossover_schedule_and_aggregate():
     assert agg["crossover_fraction"] == 0.1 and agg["fractions"]["0.1"]["speedup_vs_full_mean"] == 1.5
     with pytest.raises(ValueError, match="incomplete"):
         aggregate_crossover(rows[:-1])
+
+
+def test_tp_shared_buffers_carry_guard_bands(monkeypatch, tmp_path):
+    """Peer-mapped buffers sit between guard bands; an overrun into a band is reported
+    (host logic with a fake extension and one gloo rank)."""
+    import torch
+    import torch.distributed as dist
+
+    from sparsecache_b200 import ops
+    from sparsecache_b200.parallel import tp
+
+    class FakeExt:
+        def shared_empty(self, nbytes, device):
+            return torch.zeros(nbytes, dtype=torch.uint8), b"handle"
+
+        def shared_open(self, handle):  # pragma: no cover - one rank opens nothing
+            raise AssertionError
+
+    monkeypatch.setattr(ops, "ext", lambda: FakeExt())
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 0)
+    dist.init_process_group("gloo", init_method=f"file://{tmp_path / 'store'}", rank=0, world_size=1)
+    try:
+        g = tp.TPGroup()
+        buf, ptrs = g.shared(100)
+        buf2, _ = g.shared(64)
+        assert buf.numel() == 100 and ptrs == [buf.data_ptr()] and buf.data_ptr() % 16 == 0
+        buf.fill_(7)
+        buf2.fill_(9)
+        assert g.check_canaries() == []
+        g._guards[1][0][tp.CANARY_BYTES + 64] = 0  # one byte past the second buffer
+        assert g.check_canaries() == [1]
+    finally:
+        dist.destroy_process_group()

@@ -57,7 +57,7 @@ def _worker(rank, world, port, out_dir):
             a = slot.k(layer)[:, :T].float()
             b = rslot.k(layer)[rank * hkv:(rank + 1) * hkv, :T].float()
             kv_err = max(kv_err, float(((a - b).abs().max() / b.abs().max()).item()))
-        result.update(hidden_rel_err=err, kv_rel_err=kv_err, rows=rows, padded=Tp)
+        result.update(hidden_rel_err=err, kv_rel_err=kv_err, rows=rows, padded=Tp, canaries=group.check_canaries())
         # TP decode (fused all-reduce GEMVs) vs single-GPU greedy decode
         n_new = 8
         for use_graph in (False, True):
@@ -89,6 +89,7 @@ def test_tp2_prefill_matches_single_gpu(tmp_path):
         res = json.loads((tmp_path / f"r{r}.json").read_text())
         assert "error" not in res, res
         assert res["hidden_rel_err"] < 3e-2, res
+        assert res["canaries"] == [], res
         assert res["kv_rel_err"] < 3e-2, res
         # graph replay and eager steps agree exactly; the first tokens match the
         # single-GPU engine (partial sums are added in a different order, so
@@ -259,6 +260,8 @@ def _spec_worker(rank, world, port, out_dir):
             tpe.decode_batch(bslots, n_new - 1, use_graph=use_graph)
             result[f"batch_equal_graph{int(use_graph)}"] = tpe.batch_tokens(3, n_new) == alone
         tpe.check_status()
+        torch.cuda.synchronize()
+        result["canaries"] = group.check_canaries()
         tpe.engine.release_graphs()
         drafter._graph = None
         dist.barrier()
@@ -294,3 +297,4 @@ def test_tp_cacheblend_and_speculative_decoding(tmp_path, world):
         assert res["draft_hidden_rel_err"] < 5e-2, res
         assert res["drafter_equal"], res
         assert res["batch_equal_graph0"] and res["batch_equal_graph1"], res
+        assert res["canaries"] == [], res
