@@ -163,3 +163,69 @@ def test_tp_shared_buffers_carry_guard_bands(monkeypatch, tmp_path):
         assert g.check_canaries() == [1]
     finally:
         dist.destroy_process_group()
+
+
+def test_speculative_loop_host_logic():
+    """speculative_generate with a fake verifier (the greedy sequence is known) and a drafter
+    that is right for the first k drafts: the output is the greedy sequence and the accepted
+    counts / positions follow the accept-longest-prefix rule."""
+    from types import SimpleNamespace
+
+    import torch
+
+    from sparsecache_b200.models.engine import _Workspace
+    from sparsecache_b200.parallel.tp_draft import speculative_generate
+
+    truth = [(7 * i + 3) % 50 for i in range(40)]  # token at position T + i
+    T = 100
+
+    class Eng:
+        MAX_ROWS = 8
+
+        def __init__(self):
+            self.ws = _Workspace("cpu")
+            self.bufs = {"log": torch.zeros(64, dtype=torch.int32), "tok": torch.zeros(8, dtype=torch.int32)}
+
+        def _decode_buffers(self, *a):
+            return self.bufs
+
+    calls = []
+
+    class TPE:
+        engine = Eng()
+        seed_layers = (0, 1, 2)
+        full_cfg = SimpleNamespace(d_model=4)
+
+        def verify(self, slot, rows, position, use_graph=True):
+            rows = rows.tolist()
+            calls.append((position, rows))
+            assert rows[0] == truth[position - T]  # row 0 is the token at ``position``
+            out = torch.tensor([truth[position - T + 1 + i] for i in range(len(rows))], dtype=torch.int32)
+            self.engine.bufs["tok"][:len(rows)] = out
+            return out
+
+        def check_status(self):
+            pass
+
+    class Drafter:
+        gamma = 4
+
+        def __init__(self, right):
+            self.right = right
+
+        def propose(self, slot, first, seed_row, position, use_graph=True):
+            assert int(first[0]) == truth[position - T]
+            d = [truth[position - T + 1 + i] for i in range(4)]
+            for i in range(self.right, 4):
+                d[i] = (d[i] + 1) % 50
+            return torch.tensor(d, dtype=torch.int32)
+
+    tpe = TPE()
+    tpe.engine.bufs["log"][0] = truth[0]
+    for right in (0, 2, 4):
+        calls.clear()
+        out = speculative_generate(tpe, Drafter(right), None, prompt_tokens=T, max_new=20)
+        assert out["tokens"] == truth[:20]
+        assert all(a == right for a in out["accepted"][:-1])
+        # every verify after the first starts right after the previously committed tokens
+        assert [p for p, _ in calls][:3] == [T, T + 1, T + 2 + right]
