@@ -161,15 +161,24 @@ def cacheblend_prefill_oracle(
     blend: CacheBlendConfig,
     global_positions: torch.Tensor | None = None,
 ) -> BlendOutput:
-    """CacheBlend prefill of ``ids`` against ``composed`` (prefix + documents)."""
+    """CacheBlend prefill of ``ids`` against ``composed`` (prefix + documents).
+
+    With a gradual schedule (several check layers) every later check layer
+    projects the rows still active, writes their fresh K/V, ranks the active
+    document rows by deviation from the composed cache and keeps the top
+    ``ratio * N_doc`` of them (ratios relative to the original document count).
+    """
     device = model.device
     ids = torch.as_tensor(ids, dtype=torch.long, device=device).view(1, -1)
     total = ids.shape[1]
     raw_len = total - suffix_tokens
     if composed[0][0].shape[2] != raw_len:
         raise ValueError("composed cache and prompt lengths disagree")
-    if not 0 <= blend.check_layer < len(model.layers):
+    sched = blend.schedule
+    if sched[-1][0] >= len(model.layers):
         raise ValueError("check_layer lies outside the model")
+    first = sched[0][0]
+    ratio_at = dict(sched)
     local = torch.arange(total, device=device)
     gpos = local if global_positions is None else global_positions.to(device)
     hidden = model.embed_tokens(ids)
@@ -177,50 +186,42 @@ def cacheblend_prefill_oracle(
     active = local
     selected = None
     cache = []
+    work = 0  # rows projected, summed over layers
     for index, layer in enumerate(model.layers):
         residual = hidden
         normed = layer.input_layernorm(hidden)
-        if index <= blend.check_layer:
-            layer_cos, layer_sin = cos, sin
-        else:
-            layer_cos, layer_sin = cos.index_select(0, active), sin.index_select(0, active)
-        q, k, v = model.project_qkv(layer, normed, layer_cos, layer_sin)
-        if index < blend.check_layer:
+        work += int(active.numel())
+        q, k, v = model.project_qkv(layer, normed, cos.index_select(0, active), sin.index_select(0, active))
+        if index < first:
             attended = model.attention(q, k, v, query_positions=gpos, key_positions=gpos)
             cache_k, cache_v = k, v
-        elif index == blend.check_layer:
-            old_k, old_v = composed[index]
-            scores = deviation_scores(
-                k[:, :, prefix_tokens:raw_len],
-                v[:, :, prefix_tokens:raw_len],
-                old_k[:, :, prefix_tokens:raw_len],
-                old_v[:, :, prefix_tokens:raw_len],
-                blend.deviation_metric,
-            )
-            active, selected = select_active(
-                scores,
-                doc_begin=prefix_tokens,
-                doc_end=raw_len,
-                total=total,
-                ratio=blend.recompute_ratio,
-                keep_prefix=blend.keep_prefix,
-            )
-            q = q.index_select(2, active)
-            attended = model.attention(
-                q, k, v, query_positions=gpos.index_select(0, active), key_positions=gpos
-            )
-            residual = residual.index_select(1, active)
-            cache_k, cache_v = k, v
         else:
-            old_k, old_v = composed[index]
-            pad = total - old_k.shape[2]
-            cache_k = torch.nn.functional.pad(old_k, (0, 0, 0, pad)).clone()
-            cache_v = torch.nn.functional.pad(old_v, (0, 0, 0, pad)).clone()
-            cache_k[:, :, active] = k.to(cache_k.dtype)
-            cache_v[:, :, active] = v.to(cache_v.dtype)
-            attended = model.attention(
-                q, cache_k, cache_v, query_positions=gpos.index_select(0, active), key_positions=gpos
-            )
+            if index == first:
+                cache_k, cache_v = k, v
+            else:
+                old_k, old_v = composed[index]
+                pad = total - old_k.shape[2]
+                cache_k = torch.nn.functional.pad(old_k, (0, 0, 0, pad)).clone()
+                cache_v = torch.nn.functional.pad(old_v, (0, 0, 0, pad)).clone()
+                cache_k[:, :, active] = k.to(cache_k.dtype)
+                cache_v[:, :, active] = v.to(cache_v.dtype)
+            if index in ratio_at:
+                old_k, old_v = composed[index]
+                doc = slice(prefix_tokens, raw_len)
+                scores = deviation_scores(cache_k[:, :, doc], cache_v[:, :, doc], old_k[:, :, doc], old_v[:, :, doc],
+                                          blend.deviation_metric)
+                if index != first:  # only rows still active compete
+                    live = torch.zeros(raw_len - prefix_tokens, dtype=torch.bool, device=device)
+                    live[(selected - prefix_tokens)] = True
+                    scores = torch.where(live, scores, torch.full_like(scores, float("-inf")))
+                new_active, selected = select_active(scores, doc_begin=prefix_tokens, doc_end=raw_len, total=total,
+                                                     ratio=ratio_at[index], keep_prefix=blend.keep_prefix)
+                keep = torch.searchsorted(active, new_active)  # rows of ``hidden`` that stay
+                q = q.index_select(2, keep)
+                residual = residual.index_select(1, keep)
+                active = new_active
+            attended = model.attention(q, cache_k, cache_v, query_positions=gpos.index_select(0, active),
+                                       key_positions=gpos)
         hidden = model.block_rest(layer, residual, attended)
         cache.append((cache_k, cache_v))
     last = (active == total - 1).nonzero()
@@ -229,8 +230,7 @@ def cacheblend_prefill_oracle(
     logits = model.logits(hidden[:, int(last[0, 0])])[0]
     assert selected is not None
     n_doc = raw_len - prefix_tokens
-    post = len(model.layers) - blend.check_layer - 1
-    work = blend.check_layer * total + total + post * active.numel()
+    trace = blend.layer_document_trace(len(model.layers))
     return BlendOutput(
         cache=tuple(cache),
         logits=logits,
@@ -245,6 +245,10 @@ def cacheblend_prefill_oracle(
             "selected_document_fraction": int(selected.numel()) / max(1, n_doc),
             "active_rows": int(active.numel()),
             "approximate_layer_token_fraction": work / (len(model.layers) * total),
+            "check_layers": [c for c, _ in blend.schedule],
+            "recompute_ratios": [r for _, r in blend.schedule],
+            "layer_document_trace": trace,
+            "layer_document_mean": blend.check_target(len(model.layers)),
             "selection_checksum": selection_checksum(selected),
         },
     )

@@ -182,6 +182,17 @@ class CacheBlendConfig:
     deviation_metric: str = "value"
     keep_prefix: bool = True
     max_new_tokens: int = 24
+    # gradual filtering (the reference runner's --blend-check-layers /
+    # --recompute-ratios): several ascending check layers with non-increasing
+    # ratios, each relative to the ORIGINAL document token count; empty means
+    # the single (check_layer, recompute_ratio)
+    check_layers: tuple[int, ...] = ()
+    recompute_ratios: tuple[float, ...] = ()
+    # --target-average-recompute-ratio: the layer-average document fraction
+    # must match within TARGET_TOLERANCE
+    target_average_recompute_ratio: float | None = None
+
+    TARGET_TOLERANCE = 0.002
 
     def __post_init__(self) -> None:
         if not 0 < self.recompute_ratio <= 1:
@@ -190,6 +201,48 @@ class CacheBlendConfig:
             raise ValueError(f"deviation_metric must be one of {DEVIATION_METRICS}")
         if self.check_layer < 0:
             raise ValueError("check_layer must be non-negative")
+        if self.check_layers or self.recompute_ratios:
+            layers, ratios = tuple(self.check_layers), tuple(self.recompute_ratios)
+            if len(layers) != len(ratios) or not layers:
+                raise ValueError("check_layers and recompute_ratios must have the same non-zero length")
+            if any(b <= a for a, b in zip(layers, layers[1:])) or layers[0] < 0:
+                raise ValueError("check_layers must be ascending and non-negative")
+            if any(not 0 < r <= 1 for r in ratios) or any(b > a for a, b in zip(ratios, ratios[1:])):
+                raise ValueError("recompute_ratios must lie in (0, 1] and not increase")
+            object.__setattr__(self, "check_layers", layers)
+            object.__setattr__(self, "recompute_ratios", ratios)
+            object.__setattr__(self, "check_layer", layers[0])
+            object.__setattr__(self, "recompute_ratio", ratios[-1])
+
+    @property
+    def schedule(self) -> tuple[tuple[int, float], ...]:
+        """(check layer, retained document ratio) pairs in layer order."""
+        if self.check_layers:
+            return tuple(zip(self.check_layers, self.recompute_ratios))
+        return ((self.check_layer, self.recompute_ratio),)
+
+    def layer_document_trace(self, n_layers: int) -> list[float]:
+        """Fraction of the document tokens each layer processes (1.0 up to the first check layer)."""
+        sched = self.schedule
+        if sched[-1][0] >= n_layers:
+            raise ValueError("a check layer lies outside the model")
+        trace, frac = [], 1.0
+        for layer in range(n_layers):
+            trace.append(frac)
+            for c, r in sched:
+                if c == layer:
+                    frac = r
+        return trace
+
+    def check_target(self, n_layers: int) -> float:
+        """Mean of the layer trace; raises if a target average is set and missed by > 0.002."""
+        trace = self.layer_document_trace(n_layers)
+        mean = sum(trace) / len(trace)
+        t = self.target_average_recompute_ratio
+        if t is not None and abs(mean - t) > self.TARGET_TOLERANCE:
+            raise ValueError(f"layer-average document ratio {mean:.6f} misses the target {t} by more than "
+                             f"{self.TARGET_TOLERANCE}")
+        return mean
 
     @property
     def dev_mode(self) -> int:

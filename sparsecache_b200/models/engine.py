@@ -397,6 +397,11 @@ class B200Engine:
         ``before_layer(layer)`` runs before each layer's kernels are issued
         (layer-wise cache arrival: wait for the layer, compose it).
         """
+        if len(blend.schedule) > 1:
+            if before_layer is not None:
+                raise ValueError("layer hooks are not supported with gradual filtering")
+            return self._cacheblend_gradual(ids, slot, prefix_tokens=prefix_tokens, suffix_tokens=suffix_tokens,
+                                            blend=blend, global_positions=global_positions)
         cfg, ext = self.cfg, self.ext
         T = ids.numel()
         raw_len = T - suffix_tokens
@@ -444,6 +449,86 @@ class B200Engine:
             self._attn_mlp(layer, h_a, qa, slot, q_rows=None, qpos=qpos_a, n_keys=T, kpos=kpos, n_rows=A)
         meta = {"active": act_rows, "n_active": n_active, "checksum": checksum, "k_selected": k_sel,
                 "document_tokens": n_doc, "active_rows": A}
+        return h_a, A, meta
+
+    def _cacheblend_gradual(self, ids: torch.Tensor, slot: KVSlot, *, prefix_tokens: int, suffix_tokens: int,
+                            blend: CacheBlendConfig, global_positions: torch.Tensor | None):
+        """CacheBlend with several check layers (``blend.schedule``).
+
+        The first check layer runs as in ``cacheblend``.  Each later check
+        layer projects the rows still active (fresh K/V written at their slots,
+        deviation partials against the composed cache in the QKV epilogue),
+        selects the top ``ratio * N_doc`` active document rows (the active
+        list is sorted, so its document rows are a contiguous local range),
+        and only those rows attend and continue.
+        """
+        from ..cacheblend import recompute_count
+
+        cfg, ext = self.cfg, self.ext
+        H = cfg.n_kv_heads
+        T = ids.numel()
+        raw_len = T - suffix_tokens
+        n_doc = raw_len - prefix_tokens
+        if T > slot.capacity:
+            raise ValueError("prompt exceeds slot capacity")
+        sched = blend.schedule
+        first = sched[0][0]
+        if sched[-1][0] >= cfg.n_layers:
+            raise ValueError("check_layer lies outside the model")
+        n_pre = prefix_tokens if blend.keep_prefix else 0
+        h = self.embed(ids)
+        rows = self._arange("rows", T)
+        gpos = rows if global_positions is None else global_positions
+        kpos = global_positions
+        for layer in range(first):
+            q = self._full_layer(layer, h, slot, gpos, rows, T, kpos)
+            self._attn_mlp(layer, h, q, slot, q_rows=None, qpos=gpos, n_keys=T, kpos=kpos, n_rows=T)
+        k_sel = recompute_count(n_doc, sched[0][1])
+        A = n_pre + k_sel + suffix_tokens
+        dev = self.ws.get("dev", (T, 2 * H), torch.float32)
+        q = self._full_layer(first, h, slot, gpos, rows, T, kpos, dev, blend.dev_mode)
+        active = self._i32("active", T)
+        n_active = self._i32("n_active", 1)
+        scores = self.ws.get("scores", (max(1, n_doc),), torch.float32)
+        ext.cacheblend_select(dev, H, blend.dev_mode, T, prefix_tokens, raw_len, k_sel, blend.keep_prefix, active,
+                              n_active, scores, None)
+        act = active[:A]
+        qpos_a = self._i32("qpos_a", A)
+        ext.index_i32(gpos, act, qpos_a)
+        h_a = self.ws.get("h_a", (A, cfg.d_model), torch.bfloat16)
+        ext.gather_rows(h, act, h_a)
+        self._attn_mlp(first, h_a, q, slot, q_rows=act, qpos=qpos_a, n_keys=T, kpos=kpos, n_rows=A)
+        later = dict(sched[1:])
+        pp = 0
+        for layer in range(first + 1, cfg.n_layers):
+            if layer not in later:
+                qa = self._full_layer(layer, h_a, slot, qpos_a, act, T, kpos)
+                self._attn_mlp(layer, h_a, qa, slot, q_rows=None, qpos=qpos_a, n_keys=T, kpos=kpos, n_rows=A)
+                continue
+            dev2 = self.ws.get("dev_g", (A, 2 * H), torch.float32)
+            qa = self._full_layer(layer, h_a, slot, qpos_a, act, T, kpos, dev2, blend.dev_mode)
+            k2 = min(recompute_count(n_doc, later[layer]), A - n_pre - suffix_tokens)
+            A2 = n_pre + k2 + suffix_tokens
+            local = self._i32("g_local", A)
+            n_loc = self._i32("g_nloc", 1)
+            sc2 = self.ws.get("g_scores", (max(1, A),), torch.float32)
+            ext.cacheblend_select(dev2, H, blend.dev_mode, A, n_pre, A - suffix_tokens, k2, blend.keep_prefix,
+                                  local, n_loc, sc2, None)
+            loc = local[:A2]
+            act2 = self._i32(f"g_act{pp}", A2)
+            ext.index_i32(act, loc, act2)
+            qpos2 = self._i32(f"g_qpos{pp}", A2)
+            ext.index_i32(qpos_a, loc, qpos2)
+            h2 = self.ws.get(f"g_h{pp}", (A2, cfg.d_model), torch.bfloat16)
+            ext.gather_rows(h_a, loc, h2)
+            self._attn_mlp(layer, h2, qa, slot, q_rows=loc, qpos=qpos2, n_keys=T, kpos=kpos, n_rows=A2)
+            act, qpos_a, h_a, A = act2, qpos2, h2, A2
+            pp ^= 1
+        meta = {"active": act, "n_active": None, "checksum": None, "k_selected": A - n_pre - suffix_tokens,
+                "document_tokens": n_doc, "active_rows": A, "check_layers": [c for c, _ in sched],
+                "recompute_ratios": [r for _, r in sched],
+                "layer_document_trace": blend.layer_document_trace(cfg.n_layers),
+                "layer_document_mean": blend.check_target(cfg.n_layers)}
         return h_a, A, meta
 
     # ------------------------------------------------------------ decode

@@ -335,6 +335,8 @@ class TPEngine:
         """
         from ..cacheblend import recompute_count
 
+        if len(blend.schedule) > 1:
+            raise NotImplementedError("gradual filtering (several check layers) runs on the single-GPU engine")
         ext, eng, cfg, lc = self.ext, self.engine, self.full_cfg, self.lcfg
         T = ids.numel()
         raw_len = T - suffix_tokens

@@ -36,6 +36,7 @@ from typing import Any, Sequence
 import torch
 
 from ..cacheblend import recompute_count
+from ..config import DEVIATION_METRICS
 from ..serving.chains import progressive_commit_chain
 from ..serving.progressive import Document, ranked_document_indices, stage_document_sets
 from ..synthetic import RAGRequest
@@ -234,8 +235,23 @@ def aggregate(rows: Sequence[dict], *, reference: str = "full", bootstrap_sample
     return out
 
 
+def blend_config_from_args(a) -> "CacheBlendConfig":
+    """CacheBlendConfig of the runner flags (single check layer, or the gradual schedule)."""
+    from ..config import CacheBlendConfig
+
+    common = dict(deviation_metric=a.deviation_metric, max_new_tokens=a.max_new_tokens,
+                  target_average_recompute_ratio=a.target_average_recompute_ratio)
+    if a.blend_check_layers or a.recompute_ratios:
+        if not (a.blend_check_layers and a.recompute_ratios):
+            raise SystemExit("--blend-check-layers and --recompute-ratios go together")
+        layers = tuple(int(x) for x in a.blend_check_layers.split(","))
+        ratios = tuple(float(x) for x in a.recompute_ratios.split(","))
+        return CacheBlendConfig(check_layers=layers, recompute_ratios=ratios, **common)
+    return CacheBlendConfig(check_layer=a.check_layer, recompute_ratio=a.recompute_ratio, **common)
+
+
 def main(argv=None) -> None:
-    from ..config import CacheBlendConfig, get_model_config
+    from ..config import get_model_config
     from ..models.engine import B200Engine
     from ..serving.server import RAGServer
     from ..store import DocumentKVStore
@@ -251,16 +267,22 @@ def main(argv=None) -> None:
     p.add_argument("--fractions", default="0.25,0.5,1.0")
     p.add_argument("--schedule", default="query")
     p.add_argument("--recompute-ratio", type=float, default=0.15)
-    p.add_argument("--check-layer", type=int, default=1)
+    p.add_argument("--check-layer", "--blend-check-layer", dest="check_layer", type=int, default=1)
+    p.add_argument("--blend-check-layers", default=None, help="gradual filtering: ascending check layers, e.g. 0,1,2")
+    p.add_argument("--recompute-ratios", default=None, help="retained document ratio at each check layer")
+    p.add_argument("--target-average-recompute-ratio", type=float, default=None,
+                   help="fail unless the layer-average document ratio is within 0.002 of this")
+    p.add_argument("--deviation-metric", default="value", choices=DEVIATION_METRICS)
     p.add_argument("--output", type=Path, required=True)
     a = p.parse_args(argv)
+    blend = blend_config_from_args(a)
     cfg = get_model_config(a.model)
+    blend.check_target(cfg.n_layers)  # fail before any work when the target is missed
     eng = B200Engine.random(cfg, seed=0, device="cuda")
     reqs = make_requests(a.workload, cfg)[: a.requests + a.warmup]
     store = DocumentKVStore(cfg, tier="hbm", device=eng.device)
     server = RAGServer(eng, store, capacity=max(r.prompt_tokens for r in reqs) + a.max_new_tokens + 64,
-                       blend=CacheBlendConfig(check_layer=a.check_layer, recompute_ratio=a.recompute_ratio,
-                                              max_new_tokens=a.max_new_tokens))
+                       blend=blend)
     server.produce(reqs)
     fractions = tuple(float(x) for x in a.fractions.split(","))
     rows = []
@@ -268,6 +290,10 @@ def main(argv=None) -> None:
         f.write(json.dumps({"protocol": {"model": a.model, "workload": a.workload, "fractions": fractions,
                                          "schedule": a.schedule, "recompute_ratio": a.recompute_ratio,
                                          "check_layer": a.check_layer, "draft_tokens": a.draft_tokens,
+                                         "blend_schedule": [list(x) for x in blend.schedule],
+                                         "layer_document_trace": blend.layer_document_trace(cfg.n_layers),
+                                         "layer_document_mean": blend.check_target(cfg.n_layers),
+                                         "deviation_metric": blend.deviation_metric,
                                          "max_new_tokens": a.max_new_tokens, "commit_window": 1}}) + "\n")
         for i, r in enumerate(reqs):
             prep = prepare_request(r, schedule=a.schedule, fractions=fractions, seed=i)

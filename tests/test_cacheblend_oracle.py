@@ -98,3 +98,53 @@ def test_deviation_and_select_helpers():
     with pytest.raises(ValueError):
         CacheBlendConfig(deviation_metric="cosine")
     assert CacheBlendConfig(deviation_metric="kv_l1").dev_mode == 7
+
+
+def test_gradual_filtering_schedule(tiny):
+    """Several check layers with non-increasing ratios (relative to the original document count)."""
+    cfg, model, reqs = tiny
+    req = reqs[2]
+    comp = _composed(cfg, model, req)
+    kw = dict(prefix_tokens=len(req.prefix), suffix_tokens=len(req.suffix))
+    full_logits, _ = model.prefill(req.prompt)
+    ones = cacheblend_prefill_oracle(model, req.prompt, comp, **kw,
+                                     blend=CacheBlendConfig(check_layers=(0, 1), recompute_ratios=(1.0, 1.0)))
+    assert torch.equal(ones.logits, full_logits)
+    first = cacheblend_prefill_oracle(model, req.prompt, comp, **kw,
+                                      blend=CacheBlendConfig(check_layer=0, recompute_ratio=0.5))
+    grad = cacheblend_prefill_oracle(model, req.prompt, comp, **kw,
+                                     blend=CacheBlendConfig(check_layers=(0, 1), recompute_ratios=(0.5, 0.15)))
+    n_doc = req.document_tokens
+    assert grad.selected_positions.numel() == recompute_count(n_doc, 0.15)
+    assert set(grad.selected_positions.tolist()) <= set(first.selected_positions.tolist())
+    assert grad.metadata["layer_document_trace"] == [1.0, 0.5]
+    assert grad.metadata["check_layers"] == [0, 1] and grad.metadata["recompute_ratios"] == [0.5, 0.15]
+    with pytest.raises(ValueError, match="misses the target"):
+        CacheBlendConfig(check_layers=(0, 1), recompute_ratios=(0.5, 0.15),
+                         target_average_recompute_ratio=0.5).check_target(2)
+    with pytest.raises(ValueError):
+        CacheBlendConfig(check_layers=(1, 0), recompute_ratios=(0.3, 0.2))
+    with pytest.raises(ValueError):
+        CacheBlendConfig(check_layers=(0, 1), recompute_ratios=(0.2, 0.3))
+    # the reference runner's example: 15% true layer-average over 32 layers
+    ex = CacheBlendConfig(check_layers=(0, 1, 2), recompute_ratios=(0.30, 0.20, 0.11379310344827587),
+                          target_average_recompute_ratio=0.15)
+    assert abs(ex.check_target(32) - 0.15) < 1e-9
+    assert abs(CacheBlendConfig().check_target(32) - 0.203125) < 1e-12
+
+
+def test_runner_flags_build_the_schedule():
+    import argparse
+
+    from sparsecache_b200.pipelines.reuse import blend_config_from_args
+
+    base = dict(deviation_metric="kv_l1", max_new_tokens=16, check_layer=1, recompute_ratio=0.15,
+                blend_check_layers=None, recompute_ratios=None, target_average_recompute_ratio=None)
+    b = blend_config_from_args(argparse.Namespace(**base))
+    assert b.schedule == ((1, 0.15),) and b.deviation_metric == "kv_l1" and b.dev_mode == 1 | 2 | 4
+    g = blend_config_from_args(argparse.Namespace(**{**base, "blend_check_layers": "0,1,2",
+                                                     "recompute_ratios": "0.30,0.20,0.11379310344827587",
+                                                     "target_average_recompute_ratio": 0.15}))
+    assert g.schedule[0] == (0, 0.30) and abs(g.check_target(32) - 0.15) < 1e-9
+    with pytest.raises(SystemExit):
+        blend_config_from_args(argparse.Namespace(**{**base, "blend_check_layers": "0,1"}))
