@@ -29,13 +29,12 @@ import json
 import math
 import statistics
 import time
-from dataclasses import asdict, dataclass
+from dataclasses import dataclass
 from pathlib import Path
 from typing import Any, Sequence
 
 import torch
 
-from ..cacheblend import recompute_count
 from ..config import DEVIATION_METRICS
 from ..serving.chains import progressive_commit_chain
 from ..serving.progressive import Document, ranked_document_indices, stage_document_sets

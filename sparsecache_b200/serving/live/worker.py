@@ -24,7 +24,7 @@ import threading
 import time
 from dataclasses import dataclass, field
 from pathlib import Path
-from typing import Any, Callable, Iterator, Protocol, Sequence
+from typing import Callable, Iterator, Protocol, Sequence
 
 from fastapi import Request  # module level: FastAPI resolves handler annotations here
 
