@@ -70,6 +70,39 @@ def transfer_ms(nbytes: float, gbps: float) -> float:
     return nbytes * 8 / (gbps * 1e6)
 
 
+def question_attention_document_scores(cfg, layer_inputs: dict, layer_weights: dict, layer_keys: dict,
+                                       positions: torch.Tensor, n_tokens: int,
+                                       document_ranges: Sequence[tuple[int, int]]) -> list[float]:
+    """Producer-side attention mass of the question on every document (the ``p_attention`` schedule).
+
+    For each scored layer: the question rows' residual inputs ``layer_inputs[l]``
+    [q, d] are RMS-normalised with the layer's input norm, projected to query
+    heads (``layer_weights[l] = (ln1, w_qkv)``), rotated at ``positions``;
+    softmax(q K^T / sqrt(D)) over the prompt keys ``layer_keys[l]`` [H_kv, T, D]
+    (query heads of a GQA group share a key head) is averaged over heads and
+    question rows and summed over each document's token range; the scores are
+    averaged over layers (reference: pd_progressive_kv_pipeline.py:117-141).
+    """
+    from ..rope import apply_rope, rope_cos_sin
+
+    D, H = cfg.head_dim, cfg.n_heads
+    cos, sin = rope_cos_sin(cfg, positions.cpu(), device=next(iter(layer_inputs.values())).device)
+    per_layer = []
+    for l, x in layer_inputs.items():
+        ln1, w_qkv = layer_weights[l]
+        xf = x.float()
+        xn = (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + cfg.rms_eps)).to(torch.bfloat16) * ln1
+        q = (xn.float() @ w_qkv[: cfg.q_size].float().t()).view(-1, H, D).transpose(0, 1)  # [H, q, D]
+        q = apply_rope(q, cos, sin, sequence_dim=1)
+        k = layer_keys[l][:, :n_tokens].float()  # [Hkv, T, D]
+        hkv = k.shape[0]
+        qg = q.reshape(hkv, H // hkv, -1, D)
+        probs = torch.einsum("gqrd,gkd->gqrk", qg, k).mul(D ** -0.5).softmax(-1)
+        tok = probs.mean(dim=(0, 1, 2))  # [T]
+        per_layer.append(torch.stack([tok[b:e].sum() for b, e in document_ranges]))
+    return torch.stack(per_layer).mean(0).tolist()
+
+
 def auto_draft_tokens(*, prompt_tokens: int, first_stage_tokens: int, bytes_per_token: float, transport_gbps: float,
                       tpot_ms: float, max_draft_tokens: int, utilization: float = 1.0) -> tuple[int, float]:
     """(draft horizon, residual wire ms) of one request."""
@@ -184,7 +217,8 @@ def main(argv=None) -> None:
     p.add_argument("--model", default="llama3-8b")
     p.add_argument("--workload", default="pd_long")
     p.add_argument("--requests", type=int, default=8)
-    p.add_argument("--schedule", default="query")
+    p.add_argument("--schedule", default="query",
+                   choices=("sequential", "uniform", "query", "p_attention", "oracle", "support_last", "random"))
     p.add_argument("--stage-fractions", default="0.25,0.5,0.75,1.0")
     p.add_argument("--max-new-tokens", type=int, default=32)
     p.add_argument("--draft-tokens", type=int, default=7)
@@ -213,8 +247,28 @@ def main(argv=None) -> None:
             T = r.prompt_tokens
             docs = [Document(tuple(d), " ".join(map(str, d[:64])), start=b, end=e)
                     for d, (b, e) in zip(r.documents, r.document_ranges())]
+            # producer: prefill the whole prompt once; its slot is the tranches' source
+            src = eng.new_slot(T + a.max_new_tokens + 64)
+            ids = torch.tensor(r.prompt, dtype=torch.int32, device=eng.device)
+            q_rows = slice(T - min(16, len(r.suffix)), T)  # question rows scored by p_attention
+            score_layers = sorted({round(j * (cfg.n_layers - 1) / 3) for j in range(4)})
+            captured: dict[int, torch.Tensor] = {}
+
+            def hook(layer, hh):
+                if layer in score_layers:
+                    captured[layer] = hh[q_rows].clone()
+
+            p0 = time.perf_counter()
+            h = eng.prefill(ids, src, layer_hook=hook if a.schedule == "p_attention" else None)
+            seed = int(eng.first_token(h[T - 1:T], position=T, max_new=1)["tok"][0].item())
+            prefill_ms = (time.perf_counter() - p0) * 1e3
+            att = None
+            if a.schedule == "p_attention":
+                att = question_attention_document_scores(
+                    cfg, captured, {l: (eng.w.layers[l].ln1, eng.w.layers[l].w_qkv) for l in captured},
+                    {l: src.k(l) for l in captured}, torch.arange(T)[q_rows], T, r.document_ranges())
             ranking = ranked_document_indices(a.schedule, question=" ".join(map(str, r.suffix)), documents=docs,
-                                              random_seed=i)
+                                              random_seed=i, attention_scores=att)
             sets = stage_document_sets(ranking, docs, fractions)
             first = len(r.prefix) + len(r.suffix) + sum(len(docs[j].token_ids) for j in sets[0])
             gamma, residual = (a.draft_tokens, None)
@@ -224,13 +278,6 @@ def main(argv=None) -> None:
                                                     transport_gbps=a.transport_gbps, tpot_ms=a.auto_draft_tpot_ms,
                                                     max_draft_tokens=a.draft_tokens,
                                                     utilization=a.auto_draft_utilization)
-            # producer: prefill the whole prompt once; its slot is the tranches' source
-            src = eng.new_slot(T + a.max_new_tokens + 64)
-            ids = torch.tensor(r.prompt, dtype=torch.int32, device=eng.device)
-            p0 = time.perf_counter()
-            h = eng.prefill(ids, src)
-            seed = int(eng.first_token(h[T - 1:T], position=T, max_new=1)["tok"][0].item())
-            prefill_ms = (time.perf_counter() - p0) * 1e3
             host = src.data[:, :, :, :T].cpu().pin_memory()
             arms = ["full_target", "chain"] + (["fixed"] if a.paired_fixed_control else [])
             if i % 2:

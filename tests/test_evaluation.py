@@ -275,3 +275,35 @@ def test_pd_rows_feed_validator_summary_and_aggregate():
     assert s["latency"]["saved_vs_full_target_ms"]["mean"] == 10.0 and s["paired_fixed_control"] is not None
     agg = aggregate(rows)
     assert agg["token_equality_rate"] == 1.0 and agg["response_gain_ms"]["mean"] == 10.0
+
+
+def test_question_attention_document_scores_match_direct_attention():
+    import torch
+
+    from sparsecache_b200.config import get_model_config
+    from sparsecache_b200.pipelines.pd import question_attention_document_scores
+    from sparsecache_b200.rope import apply_rope, rope_cos_sin
+
+    cfg = get_model_config("tiny")
+    g = torch.Generator().manual_seed(0)
+    T, d, D, H, Hkv = 40, cfg.d_model, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
+    ln1 = torch.ones(d, dtype=torch.bfloat16)
+    w = (torch.randn(cfg.qkv_rows, d, generator=g) * 0.05).to(torch.bfloat16)
+    keys = torch.randn(Hkv, T, D, generator=g).to(torch.bfloat16)
+    x = torch.randn(3, d, generator=g).to(torch.bfloat16)
+    pos = torch.arange(T - 3, T)
+    ranges = [(0, 10), (10, 25), (25, 37)]
+    got = question_attention_document_scores(cfg, {0: x}, {0: (ln1, w)}, {0: keys}, pos, T, ranges)
+    # direct: per head and row softmax over the keys of its kv head, mean over heads and rows
+    xn = (x.float() * torch.rsqrt(x.float().square().mean(-1, keepdim=True) + cfg.rms_eps)).to(torch.bfloat16) * ln1
+    q = (xn.float() @ w[: cfg.q_size].float().t()).view(3, H, D).transpose(0, 1)
+    cos, sin = rope_cos_sin(cfg, pos)
+    q = apply_rope(q, cos, sin, sequence_dim=1)
+    tok = torch.zeros(T)
+    for hh in range(H):
+        s = (q[hh] @ keys[hh // (H // Hkv)].float().t()) / D ** 0.5
+        tok += s.softmax(-1).sum(0)
+    tok /= H * 3
+    want = [float(tok[b:e].sum()) for b, e in ranges]
+    assert max(abs(a - b) for a, b in zip(got, want)) < 1e-5
+    assert sum(got) < 1.0 + 1e-5  # the rest of the mass sits on prefix / question tokens
