@@ -86,3 +86,39 @@ def test_corpus_builder(tmp_path):
     assert man["source_manifests"]["a"]["selected_source_indices"] == [1, 5, 8]
     corpus.write_corpus(tmp_path / "out", reqs, meta, man)
     assert json.loads((tmp_path / "out" / "manifest.json").read_text())["format"].endswith("corpus.v1")
+
+
+def test_training_clis_end_to_end_on_cpu(tmp_path):
+    """train-eagle (with snapshot + resume) and train-drafter over a written teacher dataset."""
+    from sparsecache_b200.training import cli
+
+    samples = [_sample(i, g=f"ds{i % 2}") for i in range(6)]
+    man = write_teacher_dataset(samples, tmp_path / "teacher", target_fingerprint="fp", kv_layers=(0, 1),
+                                seed_layers=(0, 1), head_dim=D, kv_heads=H, target_hidden_size=HT, vocab_size=V,
+                                with_boundaries=True)
+    g = torch.Generator().manual_seed(3)
+    torch.save({"embed": torch.randn(V, HT, generator=g), "lm_head": torch.randn(V, HT, generator=g)},
+               tmp_path / "target.pt")
+    (tmp_path / "eagle.json").write_text(json.dumps(dict(
+        target_hidden_size=HT, hidden_size=16, intermediate_size=32, head_dim=D, num_attention_heads=4,
+        num_key_value_heads=2, num_memory_heads=H, num_memory_layers=L, num_seed_layers=2, target_vocab_size=V,
+        draft_vocab_size=24)))
+    common = ["--teacher-manifest", str(man), "--device", "cpu", "--target-model", "tiny",
+              "--target-embedding", str(tmp_path / "target.pt"), "--eval-modulus", "3", "--log-every", "1"]
+    out = tmp_path / "eagle"
+    s = cli.main(["train-eagle", *common, "--output-dir", str(out), "--drafter-config", str(tmp_path / "eagle.json"),
+                  "--steps", "3", "--save-every", "2", "--global-batch", "2", "--adapter-scale-init", "0"])
+    assert s["completed_steps"] == 3 and s["train_samples"] == 4 and s["eval_samples"] == 2
+    assert (out / "adapter.pt").exists() and (out / "adapter_step000002.pt").exists()
+    assert set(s["evaluation"]) == {"exact", "disabled"} and len(s["history"]) == 2
+    s2 = cli.main(["train-eagle", *common, "--output-dir", str(tmp_path / "eagle2"), "--drafter-config",
+                   str(tmp_path / "eagle.json"), "--steps", "2", "--global-batch", "2",
+                   "--resume-adapter", str(out / "adapter.pt")])
+    assert s2["resumed_from_step"] == 3 and s2["completed_steps"] == 5
+    d = cli.main(["train-drafter", *common, "--output-dir", str(tmp_path / "drafter"), "--steps", "4",
+                  "--draft-hidden-size", "8", "--mlp-ratio", "2", "--visibility-fractions", "0.5",
+                  "--training-window-tokens", "3", "--max-eval-tokens", "3"])
+    assert (tmp_path / "drafter" / "checkpoint.pt").exists() and "exact" in d["ablation"]
+    assert cli.split_indices({0, 1, 2, 3}, train="0-2", evaluate=None, eval_modulus=0, eval_remainder=0) == ([0, 1, 2], [3])
+    with pytest.raises(ValueError):
+        cli.split_indices({0, 1}, train="0-1", evaluate="1", eval_modulus=0, eval_remainder=0)
