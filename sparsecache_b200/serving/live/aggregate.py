@@ -316,3 +316,42 @@ def write_artifacts(out_dir: Path, summary: dict, rows: Sequence[dict]) -> None:
             g = c["decode_completion_gain_ms"]
             w.writerow([k, c["token_equality_rate"], g["mean"], *g["mean_bootstrap_ci95"],
                         c["decode_ttft_gain_ms"]["mean"]])
+
+
+def main(argv=None) -> int:
+    """Aggregate one live run directory (results / metadata / scheduler / link JSONL) into gated artifacts.
+
+    Counterpart of the reference's experiments/aggregate_progressive_pd_live.py CLI;
+    exits 1 when a validity gate fails (the artifacts are written either way).
+    """
+    import argparse
+
+    from .trace import load_jsonl
+
+    p = argparse.ArgumentParser()
+    p.add_argument("--results", type=Path, required=True)
+    p.add_argument("--metadata", type=Path, required=True)
+    p.add_argument("--scheduler-trace", type=Path, required=True)
+    p.add_argument("--link-trace", type=Path, required=True)
+    p.add_argument("--arms", default="baseline,fixed_s1,continuous")
+    p.add_argument("--expected-requests", type=int, required=True)
+    p.add_argument("--fixed-output-tokens", type=int, default=None)
+    p.add_argument("--bootstrap-samples", type=int, default=10000)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--priority-jsonl", type=Path, default=None)
+    p.add_argument("--protected-chunks", type=int, default=0)
+    p.add_argument("--output-dir", type=Path, required=True)
+    a = p.parse_args(argv)
+    summary, rows = aggregate_live_run(
+        load_jsonl(a.results), load_jsonl(a.metadata), load_jsonl(a.scheduler_trace), load_jsonl(a.link_trace),
+        arms=a.arms.split(","), expected_requests=a.expected_requests, fixed_output_tokens=a.fixed_output_tokens,
+        bootstrap_samples=a.bootstrap_samples, seed=a.seed,
+        priority_rows=load_jsonl(a.priority_jsonl) if a.priority_jsonl else None,
+        protected_chunks=a.protected_chunks)
+    write_artifacts(a.output_dir, summary, rows)
+    print(json.dumps({"status": summary["status"], "output_dir": str(a.output_dir)}))
+    return 0 if summary["status"] == "passed" else 1
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -101,3 +101,31 @@ def validate_pack_hashes(job: dict) -> dict[str, str]:
     if "priority_jsonl" in job and sha256_file(Path(job["priority_jsonl"])) != job["priority_sha256"]:
         raise ValueError(f"priority sidecar of {job['job_id']} differs from the registered queue")
     return got
+
+
+def main(argv=None) -> int:
+    """Build a preregistered live-job queue from a packs JSON (``[{"name", "pack_dir", "core"}]``)."""
+    import argparse
+
+    p = argparse.ArgumentParser()
+    p.add_argument("--packs", type=Path, required=True)
+    p.add_argument("--run-root", type=Path, required=True)
+    p.add_argument("--bandwidths", default="25,50")
+    p.add_argument("--core-requests", type=int, default=64)
+    p.add_argument("--confirmation-requests", type=int, default=192)
+    p.add_argument("--warmup-requests", type=int, default=2)
+    p.add_argument("--max-draft-tokens", type=int, default=8)
+    p.add_argument("--output", type=Path, required=True)
+    a = p.parse_args(argv)
+    queue = build_queue(json.loads(a.packs.read_text()), a.run_root,
+                        bandwidths=[int(x) for x in a.bandwidths.split(",")], core_requests=a.core_requests,
+                        confirmation_requests=a.confirmation_requests, warmup_requests=a.warmup_requests,
+                        max_draft_tokens=a.max_draft_tokens)
+    a.output.parent.mkdir(parents=True, exist_ok=True)
+    a.output.write_text(json.dumps(queue, indent=2) + "\n")
+    print(json.dumps({"jobs": len(queue["jobs"]), "jobs_sha256": queue["jobs_sha256"]}))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -127,3 +127,51 @@ def aggregate_scheduling(records: Sequence[dict], *, schedules: Sequence[str] = 
                                                      bootstrap_samples=bootstrap_samples, seed=seed),
                     "decode_ttft_ms": statistics.fmean(r["decode_ttft_ms"] for r in rows)}
     return {"status": "passed" if gates["overall"]["passed"] else "failed_gates", "gates": gates, "cells": by_cell}
+
+
+def main(argv=None) -> int:
+    """``latency-cell ROWS.jsonl --expected N`` or ``scheduling RECORDS.jsonl --expected-requests N``.
+
+    Counterparts of the reference's experiments/validate_pd_latency_cell.py and
+    aggregate_progressive_pd_scheduling_live.py CLIs; exit code 1 on a failed check.
+    """
+    import argparse
+    import json
+    from pathlib import Path
+
+    from .trace import load_jsonl
+
+    p = argparse.ArgumentParser()
+    sub = p.add_subparsers(dest="cmd", required=True)
+    c = sub.add_parser("latency-cell")
+    c.add_argument("rows", type=Path)
+    c.add_argument("--expected", type=int, required=True)
+    c.add_argument("--max-unattributed-ms", type=float, default=100.0)
+    c.add_argument("--max-initial-gpu-bytes", type=int, default=1 << 30)
+    s = sub.add_parser("scheduling")
+    s.add_argument("records", type=Path)
+    s.add_argument("--expected-requests", type=int, required=True)
+    s.add_argument("--schedules", default=",".join(SCHEDULES))
+    s.add_argument("--arms", default="fixed_s1,continuous")
+    s.add_argument("--bootstrap-samples", type=int, default=2000)
+    for q in (c, s):
+        q.add_argument("--output", type=Path, default=None)
+    a = p.parse_args(argv)
+    if a.cmd == "latency-cell":
+        rows = [r for r in load_jsonl(a.rows) if "schedules" in r]
+        out = validate_latency_cell(rows, expected_count=a.expected, max_unattributed_ms=a.max_unattributed_ms,
+                                    max_initial_gpu_bytes=a.max_initial_gpu_bytes)
+        ok = out["passed"]
+    else:
+        out = aggregate_scheduling(load_jsonl(a.records), schedules=a.schedules.split(","), arms=a.arms.split(","),
+                                   expected_requests=a.expected_requests, bootstrap_samples=a.bootstrap_samples)
+        ok = out["status"] == "passed"
+    text = json.dumps(out, indent=2, default=str)
+    if a.output is not None:
+        a.output.write_text(text + "\n")
+    print(text)
+    return 0 if ok else 1
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -271,6 +271,16 @@ def test_pd_rows_feed_validator_summary_and_aggregate():
                                      residual=None, bytes_per_token=128, prefill_ms=3.0, protocol=proto))
     v = validate_latency_cell(rows, expected_count=4, max_unattributed_ms=100.0)
     assert v["passed"], v
+    import tempfile
+    from pathlib import Path
+
+    from sparsecache_b200.serving.live import validate as validate_mod
+
+    with tempfile.TemporaryDirectory() as d:
+        path = Path(d) / "rows.jsonl"
+        path.write_text("".join(json.dumps(r) + "\n" for r in rows))
+        assert validate_mod.main(["latency-cell", str(path), "--expected", "4"]) == 0
+        assert validate_mod.main(["latency-cell", str(path), "--expected", "5"]) == 1
     s = summarize_run(rows)
     assert s["latency"]["saved_vs_full_target_ms"]["mean"] == 10.0 and s["paired_fixed_control"] is not None
     agg = aggregate(rows)

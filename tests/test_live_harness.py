@@ -104,6 +104,15 @@ def test_full_chain_paired_run_aggregate_and_trace(tmp_path):
     assert not failed, failed
     aggregate.write_artifacts(tmp_path / "agg", summary, rows)
     assert (tmp_path / "agg" / "paper_table.csv").exists()
+    # the same run through the aggregator's command line
+    for name, recs in (("meta", meta), ("sched", sink.records["scheduler"]), ("link", sink.records["link"])):
+        (tmp_path / f"{name}.jsonl").write_text("".join(json.dumps(r) + "\n" for r in recs))
+    rc = aggregate.main(["--results", str(tmp_path / "results.jsonl"), "--metadata", str(tmp_path / "meta.jsonl"),
+                         "--scheduler-trace", str(tmp_path / "sched.jsonl"), "--link-trace",
+                         str(tmp_path / "link.jsonl"), "--expected-requests", "4", "--fixed-output-tokens", "12",
+                         "--bootstrap-samples", "200", "--protected-chunks", "1", "--output-dir",
+                         str(tmp_path / "agg_cli")])
+    assert rc == 0 and (tmp_path / "agg_cli" / "summary.md").exists()
     # input-trace audit of every progressive request
     n_prog = len(sink.records["scheduler"])
     rep = trace.verify_input_trace(sink.records["scheduler"], sink.records["input_trace"], expected_requests=n_prog)
@@ -178,6 +187,11 @@ def test_queue_registration_and_hash_checks(tmp_path):
     qp.write_text(json.dumps(q))
     job, _ = queue.load_job(qp, "confirm_ruler16k_bw25_n4_offset6")
     assert job["request_offset"] == 6 and queue.validate_pack_hashes(job)
+    (tmp_path / "packs.json").write_text(json.dumps([{"name": "ruler16k", "pack_dir": str(pack)}]))
+    assert queue.main(["--packs", str(tmp_path / "packs.json"), "--run-root", str(tmp_path / "runs"),
+                       "--bandwidths", "25,100", "--core-requests", "6", "--confirmation-requests", "4",
+                       "--warmup-requests", "1", "--output", str(tmp_path / "q2.json")]) == 0
+    assert json.loads((tmp_path / "q2.json").read_text())["jobs_sha256"] == q["jobs_sha256"]
     (pack / "metadata.jsonl").write_text("changed\n")
     with pytest.raises(ValueError):
         queue.validate_pack_hashes(job)
