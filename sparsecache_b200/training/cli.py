@@ -4,6 +4,10 @@
         --output-dir runs/eagle --steps 2000 --global-batch 32
     python -m sparsecache_b200.training.cli train-drafter --teacher-manifest T/manifest.json \\
         --output-dir runs/drafter --steps 2000
+    python -m sparsecache_b200.training.cli extract-teacher --model M --requests-jsonl C/requests.jsonl \\
+        --output-dir T --request-indices 0-255 --continuation-tokens 8
+    python -m sparsecache_b200.training.cli extend-teacher --base-manifest T/manifest.json \\
+        --output-dir T5 --continuation-tokens 64
 
 Counterparts of the reference's experiments/train_sparse_kv_eagle.py (flags
 :384-436) and experiments/train_sparse_kv_drafter.py (flags :536-572) with the
@@ -23,11 +27,26 @@ exact and disabled (4-token draft acceptance, teacher-forced top-1).
 over visibility fractions, then the five-cell ablation on held-out samples.
 The target's embedding / LM head come from ``--target-embedding`` (a tensor
 file) or the seeded random-init weights of ``--target-model``.
+
+``extract-teacher`` (reference: experiments/extract_sparse_kv_teacher.py,
+flags :326-341, manifest :393-431): the v3 teacher records of the chosen
+rows of a corpus ``requests.jsonl`` from a model directory (``config.json``
++ ``model.safetensors``), one ``sample_XXXXX.safetensors`` per request and a
+manifest that records the corpus hash, the model fingerprint, each prompt's
+hash and its seed token.  ``extend-teacher`` (reference:
+experiments/extend_sparse_kv_teacher.py:138-260): a longer greedy
+continuation per request with the seed-layer hidden state after every token,
+written as ``trace_XXXXX.safetensors`` + a v5 manifest chained to the v3
+base; it refuses a changed corpus, a changed model, a changed prompt or a
+seed token that does not reproduce.  On a CUDA device the B200 engine does
+the extraction (prefill hooks, CUDA-graph greedy decode); on the CPU the
+plain-PyTorch oracle model does.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import time
 from dataclasses import replace
 from pathlib import Path
 
@@ -214,6 +233,200 @@ def cmd_train_drafter(a) -> dict:
     return summary
 
 
+def parse_layer_list(raw: str, *, name: str) -> tuple[int, ...]:
+    """``"8,20,31"`` -> (8, 20, 31); empty, negative or duplicate entries are rejected."""
+    values = tuple(int(x) for x in raw.split(",") if x.strip())
+    if not values or min(values) < 0 or len(set(values)) != len(values):
+        raise ValueError(f"{name} must be distinct non-negative integers")
+    return values
+
+
+def load_request_rows(path: Path, indices, max_context_tokens: int) -> list[dict]:
+    """Rows ``indices`` of a corpus ``requests.jsonl`` (prompt token ids), sorted by index."""
+    wanted = set(int(i) for i in indices)
+    rows = []
+    with Path(path).open(encoding="utf-8") as f:
+        for index, line in enumerate(f):
+            if index not in wanted:
+                continue
+            row = json.loads(line)
+            prompt = row.get("prompt")
+            if not isinstance(prompt, list) or not prompt or any(type(t) is not int for t in prompt):
+                raise ValueError(f"request {index} has invalid prompt token ids")
+            if len(prompt) > max_context_tokens:
+                raise ValueError(f"request {index} has {len(prompt)} prompt tokens, above the "
+                                 f"{max_context_tokens}-token cap")
+            rows.append({"request_index": index, "prompt": prompt, "source_dataset": row.get("source_dataset"),
+                         "source_index": row.get("source_index")})
+    missing = wanted - {r["request_index"] for r in rows}
+    if missing:
+        raise ValueError(f"missing request indices: {sorted(missing)}")
+    return sorted(rows, key=lambda r: r["request_index"])
+
+
+class _TeacherModel:
+    """The target of a model directory: the B200 engine on a CUDA device, the fp32 oracle on the CPU."""
+
+    def __init__(self, model_dir: str, device: torch.device, max_positions: int) -> None:
+        from ..models.checkpoint import load_oracle
+
+        self.device = device
+        if device.type == "cuda":
+            from ..models.engine import B200Engine
+
+            oracle = load_oracle(model_dir, dtype=torch.bfloat16, device="cpu")
+            self.engine, self.oracle = B200Engine.from_oracle(oracle, device=device,
+                                                              max_positions=max_positions), None
+            del oracle
+        else:
+            self.engine, self.oracle = None, load_oracle(model_dir, dtype=torch.float32, device="cpu")
+        self.config = self.engine.cfg if self.engine is not None else self.oracle.config
+
+    def extract(self, prompt: list[int], **kw) -> dict[str, torch.Tensor]:
+        from .teacher import extract_teacher, extract_teacher_oracle
+
+        ids = torch.tensor(prompt, dtype=torch.int32)
+        if self.engine is not None:
+            return extract_teacher(self.engine, [ids], keep_full_memory=True, **kw)[0].tensors
+        return extract_teacher_oracle(self.oracle, [ids], **kw)[0].tensors
+
+
+def _eos_ids(model_dir: str, config) -> set[int]:
+    """End-of-sequence ids: the model config's, else a Hugging Face ``eos_token_id`` entry."""
+    if config.eos_token_ids:
+        return {int(x) for x in config.eos_token_ids}
+    raw = json.loads((Path(model_dir) / "config.json").read_text()).get("eos_token_id")
+    if raw is None:
+        return set()
+    return {int(raw)} if isinstance(raw, int) else {int(x) for x in raw}
+
+
+def _save_record(tensors: dict[str, torch.Tensor], path: Path) -> tuple[str, int]:
+    from .teacher import _atomic_save, sha256_file
+
+    _atomic_save(tensors, path)
+    return sha256_file(path), sum(t.numel() * t.element_size() for t in tensors.values())
+
+
+def cmd_extract_teacher(a) -> dict:
+    from ..store import model_fingerprint
+    from .teacher import TEACHER_FORMATS, prompt_sha256, required_fields, sha256_file, truncate_at_eos
+
+    indices = sorted(parse_indices(a.request_indices) or ())
+    kv_layers = parse_layer_list(a.kv_layers, name="KV layers")
+    seed_layers = parse_layer_list(a.seed_layers, name="seed layers")
+    if min(a.max_context_tokens, a.continuation_tokens, a.teacher_topk, a.priority_page_size) <= 0:
+        raise ValueError("context, continuation and top-k sizes must be positive")
+    requests = Path(a.requests_jsonl)
+    rows = load_request_rows(requests, indices, a.max_context_tokens)
+    out = Path(a.output_dir)
+    out.mkdir(parents=True, exist_ok=False)
+    dev = torch.device(a.device)
+    target = _TeacherModel(a.model, dev, a.max_context_tokens + a.continuation_tokens + 128)
+    cfg = target.config
+    if max(kv_layers + seed_layers) >= cfg.n_layers:
+        raise ValueError("a requested target layer is out of range")
+    eos = _eos_ids(a.model, cfg)
+    v3 = required_fields(3)
+    sample_rows = []
+    for row in rows:
+        t0 = time.perf_counter()
+        tensors = truncate_at_eos(target.extract(row["prompt"], kv_layers=kv_layers, seed_layers=seed_layers,
+                                                 continuation_tokens=a.continuation_tokens,
+                                                 teacher_topk=a.teacher_topk, page_size=a.priority_page_size),
+                                  eos)
+        i = row["request_index"]
+        f = out / f"sample_{i:05d}.safetensors"
+        digest, nbytes = _save_record({k: tensors[k] for k in v3}, f)
+        sample = {"request_index": i, "file": f.name, "prompt_tokens": len(row["prompt"]),
+                  "draft_training_tokens": int(tensors["labels"].numel()),
+                  "seed_token_id": int(tensors["input_ids"][0]), "prompt_sha256": prompt_sha256(row["prompt"]),
+                  "logical_bytes": nbytes, "file_sha256": digest,
+                  "elapsed_ms": (time.perf_counter() - t0) * 1000.0,
+                  "source_dataset": row["source_dataset"], "source_index": row["source_index"]}
+        sample_rows.append(sample)
+        print(json.dumps({"event": "teacher_sample", **sample}), flush=True)
+    manifest = {"schema_version": 3, "format": TEACHER_FORMATS[2], "created_at_ns": time.time_ns(),
+                "target_model": str(Path(a.model).resolve()), "target_fingerprint": model_fingerprint(a.model),
+                "requests_jsonl": str(requests.resolve()), "requests_sha256": sha256_file(requests),
+                "request_indices": indices, "max_context_tokens": a.max_context_tokens,
+                "continuation_tokens": a.continuation_tokens, "teacher_topk": a.teacher_topk,
+                "priority_page_size": a.priority_page_size, "kv_layers": list(kv_layers),
+                "seed_layers": list(seed_layers), "dtype": "bfloat16", "head_dim": cfg.head_dim,
+                "kv_heads": cfg.n_kv_heads, "target_hidden_size": cfg.d_model, "vocab_size": cfg.vocab,
+                "samples": sample_rows, "extractor": "sparsecache_b200.training.cli extract-teacher",
+                "extractor_backend": "b200-engine" if target.engine is not None else "oracle-cpu"}
+    (out / "manifest.json").write_text(json.dumps(manifest, indent=2, sort_keys=True) + "\n", encoding="utf-8")
+    print(json.dumps({"event": "teacher_manifest", "samples": len(sample_rows)}), flush=True)
+    return manifest
+
+
+_BASE_KEYS = ("target_model", "target_fingerprint", "requests_jsonl", "requests_sha256", "max_context_tokens",
+              "priority_page_size", "kv_layers", "seed_layers", "dtype", "head_dim", "kv_heads",
+              "target_hidden_size", "vocab_size")
+
+
+def cmd_extend_teacher(a) -> dict:
+    from ..store import model_fingerprint
+    from .teacher import TEACHER_FORMATS, _TRACE_FIELDS, prompt_sha256, sha256_file, truncate_at_eos
+
+    if min(a.continuation_tokens, a.teacher_topk) <= 0:
+        raise ValueError("continuation length and teacher top-k must be positive")
+    base_path = Path(a.base_manifest).resolve()
+    base = json.loads(base_path.read_text(encoding="utf-8"))
+    if base.get("format") != TEACHER_FORMATS[2]:
+        raise ValueError("trace extension requires a v3 base teacher manifest")
+    base_rows = {int(r["request_index"]): r for r in base["samples"]}
+    indices = sorted(parse_indices(a.request_indices) or base_rows)
+    missing = set(indices) - set(base_rows)
+    if missing:
+        raise ValueError(f"base teacher data is missing {sorted(missing)}")
+    requests = Path(base["requests_jsonl"])
+    if sha256_file(requests) != base["requests_sha256"]:
+        raise ValueError("request corpus hash differs from the base manifest")
+    rows = load_request_rows(requests, indices, int(base["max_context_tokens"]))
+    model_dir = str(base["target_model"])
+    if model_fingerprint(model_dir) != base["target_fingerprint"]:
+        raise ValueError("target model fingerprint differs from the base manifest")
+    out = Path(a.output_dir)
+    out.mkdir(parents=True, exist_ok=False)
+    dev = torch.device(a.device)
+    target = _TeacherModel(model_dir, dev, int(base["max_context_tokens"]) + a.continuation_tokens + 128)
+    eos = _eos_ids(model_dir, target.config)
+    sample_rows = []
+    for row in rows:
+        t0 = time.perf_counter()
+        i = row["request_index"]
+        brow = base_rows[i]
+        if prompt_sha256(row["prompt"]) != brow["prompt_sha256"]:
+            raise ValueError(f"request {i} prompt hash differs")
+        tensors = truncate_at_eos(target.extract(row["prompt"], kv_layers=tuple(base["kv_layers"]),
+                                                 seed_layers=tuple(base["seed_layers"]),
+                                                 continuation_tokens=a.continuation_tokens,
+                                                 teacher_topk=a.teacher_topk,
+                                                 page_size=int(base["priority_page_size"])), eos)
+        if int(tensors["input_ids"][0]) != int(brow["seed_token_id"]):
+            raise ValueError(f"request {i} seed token is not reproducible")
+        f = out / f"trace_{i:05d}.safetensors"
+        digest, nbytes = _save_record({k: tensors[k] for k in _TRACE_FIELDS}, f)
+        sample = {"request_index": i, "file": f.name, "file_sha256": digest,
+                  "draft_training_tokens": int(tensors["labels"].numel()), "seed_token_id": int(brow["seed_token_id"]),
+                  "prompt_tokens": len(row["prompt"]), "prompt_sha256": brow["prompt_sha256"],
+                  "logical_bytes": nbytes, "elapsed_ms": (time.perf_counter() - t0) * 1000.0,
+                  "source_dataset": brow.get("source_dataset"), "source_index": brow.get("source_index")}
+        sample_rows.append(sample)
+        print(json.dumps({"event": "teacher_trace", **sample}), flush=True)
+    manifest = {k: base[k] for k in _BASE_KEYS}
+    manifest.update({"schema_version": 5, "format": TEACHER_FORMATS[4], "created_at_ns": time.time_ns(),
+                     "base_manifest": str(base_path), "request_indices": indices,
+                     "continuation_tokens": a.continuation_tokens, "teacher_topk": a.teacher_topk,
+                     "samples": sample_rows, "extractor": "sparsecache_b200.training.cli extend-teacher"})
+    (out / "manifest.json").write_text(json.dumps(manifest, indent=2, sort_keys=True) + "\n", encoding="utf-8")
+    print(json.dumps({"event": "teacher_trace_manifest", "samples": len(sample_rows),
+                      "tokens": sum(r["draft_training_tokens"] for r in sample_rows)}), flush=True)
+    return manifest
+
+
 def _common(p: argparse.ArgumentParser) -> None:
     p.add_argument("--teacher-manifest", required=True)
     p.add_argument("--output-dir", required=True)
@@ -262,8 +475,28 @@ def main(argv=None) -> dict:
     d.add_argument("--draft-hidden-size", type=int, default=512)
     d.add_argument("--num-blocks", type=int, default=1)
     d.add_argument("--mlp-ratio", type=int, default=4)
+    x = sub.add_parser("extract-teacher")
+    x.add_argument("--model", required=True, help="model directory (config.json + model.safetensors)")
+    x.add_argument("--requests-jsonl", required=True)
+    x.add_argument("--output-dir", required=True)
+    x.add_argument("--request-indices", default="0,1,5,8")
+    x.add_argument("--max-context-tokens", type=int, default=16384)
+    x.add_argument("--continuation-tokens", type=int, default=8)
+    x.add_argument("--kv-layers", default="8,20,31")
+    x.add_argument("--seed-layers", default="2,16,29")
+    x.add_argument("--teacher-topk", type=int, default=64)
+    x.add_argument("--priority-page-size", type=int, default=64)
+    x.add_argument("--device", default="cuda")
+    t = sub.add_parser("extend-teacher")
+    t.add_argument("--base-manifest", required=True)
+    t.add_argument("--output-dir", required=True)
+    t.add_argument("--request-indices", default=None)
+    t.add_argument("--continuation-tokens", type=int, default=64)
+    t.add_argument("--teacher-topk", type=int, default=64)
+    t.add_argument("--device", default="cuda")
     a = p.parse_args(argv)
-    return cmd_train_eagle(a) if a.cmd == "train-eagle" else cmd_train_drafter(a)
+    return {"train-eagle": cmd_train_eagle, "train-drafter": cmd_train_drafter,
+            "extract-teacher": cmd_extract_teacher, "extend-teacher": cmd_extend_teacher}[a.cmd](a)
 
 
 if __name__ == "__main__":

@@ -417,6 +417,107 @@ def extract_teacher(engine, prompts: Sequence[torch.Tensor], *, kv_layers: Seque
     return samples
 
 
+def _oracle_layers(model, ids: torch.Tensor, positions: torch.Tensor, past=None):
+    """Oracle layer loop -> (hidden entering every layer + final hidden, [T, d] each; new cache)."""
+    hidden = model.embed_tokens(ids.to(model.device).view(1, -1))
+    positions = positions.to(model.device)
+    cos, sin = model.rope(positions)
+    key_pos = positions if past is None else torch.cat(
+        (torch.arange(past[0][0].shape[2], device=model.device), positions))
+    entering, cache = [], []
+    for index, layer in enumerate(model.layers):
+        entering.append(hidden[0])
+        q, k, v = model.project_qkv(layer, layer.input_layernorm(hidden), cos, sin)
+        if past is not None:
+            k = torch.cat((past[index][0], k), dim=2)
+            v = torch.cat((past[index][1], v), dim=2)
+        attended = model.attention(q, k, v, query_positions=positions, key_positions=key_pos)
+        hidden = model.block_rest(layer, hidden, attended)
+        cache.append((k, v))
+    entering.append(hidden[0])
+    return entering, tuple(cache)
+
+
+@torch.no_grad()
+def extract_teacher_oracle(model, prompts: Sequence[torch.Tensor], *, kv_layers: Sequence[int],
+                           seed_layers: Sequence[int], continuation_tokens: int, teacher_topk: int = 64,
+                           page_size: int = 64,
+                           continuation_ids: Sequence[torch.Tensor] | None = None) -> list[TeacherSample]:
+    """``extract_teacher`` restated on the plain-PyTorch oracle model (``models.llama.LlamaOracle``).
+
+    Same fields and storage dtypes as the engine path with the full prompt
+    memory (reference: experiments/extract_sparse_kv_teacher.py:97-323 for
+    the v3 fields, experiments/extend_sparse_kv_teacher.py:28-136 for
+    ``continuation_seed_hidden``): the numerics oracle of the GPU extractor
+    and the CPU path of the extraction command line.  ``continuation_ids``
+    (one token tensor per prompt) replaces the greedy continuation, so the
+    teacher fields can be compared along another extractor's tokens.
+    """
+    from ..rope import apply_rope
+
+    cfg = model.config
+    bf = torch.bfloat16
+    samples = []
+    for i, prompt in enumerate(prompts):
+        ids = prompt.to(torch.long).cpu()
+        T = ids.numel()
+        entering, cache = _oracle_layers(model, ids, torch.arange(T))
+        seed_hidden = torch.stack([entering[s + 1][T - 1] for s in seed_layers])
+        cos, sin = model.rope(torch.tensor([T - 1]))
+        page_probs = []
+        for l in kv_layers:
+            layer = model.layers[l]
+            q = layer.q_proj(layer.input_layernorm(entering[l][T - 1:T])).view(cfg.n_heads, 1, cfg.head_dim)
+            q = apply_rope(q, cos, sin, sequence_dim=1).squeeze(1)
+            page_probs.append(page_scores_from_queries(q, cache[l][0][0], T, page_size))
+        scores = torch.stack(page_probs).mean(0)
+        # greedy continuation token by token, then one pass over it for the teacher fields
+        if continuation_ids is not None:
+            input_ids = continuation_ids[i].to(torch.long).cpu()
+        else:
+            tokens = [int(model.logits(entering[-1][T - 1:T]).float().argmax())]
+            past = cache
+            for step in range(continuation_tokens - 1):
+                hid, past = model.forward_tokens(torch.tensor([tokens[-1]]), torch.tensor([T + step]), past=past)
+                tokens.append(int(model.logits(hid[:, -1]).float().argmax()))
+            input_ids = torch.tensor(tokens, dtype=torch.long)
+        n = input_ids.numel()
+        cont, _ = _oracle_layers(model, input_ids, torch.arange(T, T + n), past=cache)
+        normed = model.norm(cont[-1])
+        logits = model.lm_head(normed).float()
+        lp = logits.log_softmax(-1)
+        top_lp, top_ids = lp.topk(teacher_topk, dim=-1)
+        qc, qs = model.rope(torch.arange(T, T + n))
+        tensors = {
+            "memory_keys": torch.stack([cache[l][0][0] for l in kv_layers]).to(bf),
+            "memory_values": torch.stack([cache[l][1][0] for l in kv_layers]).to(bf),
+            "seed_hidden": seed_hidden.to(bf), "input_ids": input_ids, "labels": logits.argmax(-1),
+            "teacher_topk_ids": top_ids.long(), "teacher_topk_logprobs": top_lp.float(),
+            "teacher_hidden": normed.to(bf), "priority_page_scores": scores.float(),
+            "query_cos": qc.to(bf), "query_sin": qs.to(bf), "prompt_ids": ids.to(torch.int32),
+            "continuation_seed_hidden": torch.stack([cont[s + 1] for s in seed_layers], dim=1).to(bf)}
+        samples.append(TeacherSample(i, T, tensors, None))
+    return samples
+
+
+_TRACE_FIELDS = ("input_ids", "labels", "teacher_topk_ids", "teacher_topk_logprobs", "teacher_hidden",
+                 "query_cos", "query_sin", "continuation_seed_hidden")
+
+
+def truncate_at_eos(tensors: dict[str, torch.Tensor], eos: set[int]) -> dict[str, torch.Tensor]:
+    """Cut the continuation after the first label in ``eos`` (kept), as a greedy teacher that stops there."""
+    labels = tensors["labels"].tolist()
+    stop = next((j + 1 for j, t in enumerate(labels) if t in eos), len(labels))
+    if stop == len(labels):
+        return tensors
+    return {k: (v[:stop] if k in _TRACE_FIELDS else v) for k, v in tensors.items()}
+
+
+def prompt_sha256(prompt_ids: Sequence[int]) -> str:
+    """sha256 of the compact JSON list of prompt ids (the reference's per-sample prompt hash)."""
+    return hashlib.sha256(json.dumps([int(t) for t in prompt_ids], separators=(",", ":")).encode()).hexdigest()
+
+
 def bank_from_extracted(samples: Sequence[TeacherSample], device) -> DeviceTeacherBank:
     """Bank of ``extract_teacher`` output whose memory is already cut to its view."""
     views = [(s.tensors["memory_keys"], s.tensors["memory_values"]) for s in samples]

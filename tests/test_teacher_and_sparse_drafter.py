@@ -122,3 +122,49 @@ def test_training_clis_end_to_end_on_cpu(tmp_path):
     assert cli.split_indices({0, 1, 2, 3}, train="0-2", evaluate=None, eval_modulus=0, eval_remainder=0) == ([0, 1, 2], [3])
     with pytest.raises(ValueError):
         cli.split_indices({0, 1}, train="0-1", evaluate="1", eval_modulus=0, eval_remainder=0)
+
+
+def test_teacher_extraction_and_extension_clis_on_cpu(tmp_path):
+    """extract-teacher (v3) then extend-teacher (v5 chained to it) from a model directory on the CPU oracle,
+    re-read through the trainer's loader; the extender refuses a changed corpus."""
+    from sparsecache_b200.models.checkpoint import load_oracle, random_checkpoint
+    from sparsecache_b200.training import cli
+    from sparsecache_b200.training.teacher import prompt_sha256
+
+    model_dir = random_checkpoint(tmp_path / "model", "tiny", seed=1, std=0.05)
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(4, 1024, (n,), generator=g).tolist() for n in (70, 130, 90)]
+    corpus = tmp_path / "requests.jsonl"
+    corpus.write_text("".join(json.dumps({"prompt": p, "source_dataset": f"ds{i}", "source_index": i}) + "\n"
+                              for i, p in enumerate(prompts)))
+    m3 = cli.main(["extract-teacher", "--model", str(model_dir), "--requests-jsonl", str(corpus),
+                   "--output-dir", str(tmp_path / "t3"), "--request-indices", "0,2", "--continuation-tokens", "4",
+                   "--kv-layers", "0,1", "--seed-layers", "0,1", "--teacher-topk", "8", "--device", "cpu"])
+    assert m3["format"].endswith(".v3") and [r["request_index"] for r in m3["samples"]] == [0, 2]
+    assert m3["samples"][1]["prompt_sha256"] == prompt_sha256(prompts[2])
+    _, loaded = load_teacher_dataset(tmp_path / "t3" / "manifest.json")
+    s = loaded[2].tensors
+    oracle = load_oracle(model_dir)
+    _, cache = oracle.prefill(prompts[2])
+    assert s["memory_keys"].shape == (2, 2, 90, 64) and s["priority_page_scores"].shape == (2,)
+    assert torch.allclose(s["memory_keys"][1].float(), cache[1][0][0], atol=2e-2, rtol=2e-2)
+    assert torch.allclose(s["priority_page_scores"].sum(), torch.tensor(1.0), atol=1e-4)
+    n = s["labels"].numel()
+    assert 1 <= n <= 4 and torch.equal(s["labels"][:-1], s["input_ids"][1:])
+    assert torch.equal(s["teacher_topk_ids"][:, 0], s["labels"])
+    m5 = cli.main(["extend-teacher", "--base-manifest", str(tmp_path / "t3" / "manifest.json"),
+                   "--output-dir", str(tmp_path / "t5"), "--continuation-tokens", "7", "--teacher-topk", "8",
+                   "--device", "cpu"])
+    assert m5["format"].endswith(".v5") and m5["kv_layers"] == [0, 1]
+    man, loaded5 = load_teacher_dataset(tmp_path / "t5" / "manifest.json")
+    t = loaded5[2].tensors
+    assert torch.equal(t["memory_keys"], s["memory_keys"]) and t["continuation_seed_hidden"].shape[1:] == (2, 256)
+    assert torch.equal(t["input_ids"][:n], s["input_ids"]) and torch.equal(t["initial_labels"], s["labels"])
+    # the seed layer's hidden at continuation token j is its output at that row of one oracle pass
+    full = torch.tensor(prompts[2] + t["input_ids"].tolist())
+    hid, _ = oracle.forward_tokens(full, torch.arange(full.numel()))
+    assert torch.allclose(t["teacher_hidden"][-1].float(), oracle.norm(hid[0, -1]), atol=3e-2, rtol=3e-2)
+    corpus.write_text(corpus.read_text() + "\n")
+    with pytest.raises(ValueError, match="corpus hash"):
+        cli.main(["extend-teacher", "--base-manifest", str(tmp_path / "t3" / "manifest.json"),
+                  "--output-dir", str(tmp_path / "t5b"), "--device", "cpu"])
