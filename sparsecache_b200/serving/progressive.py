@@ -11,6 +11,11 @@ Components (reference behaviour cited per item):
     per-request BM25 and the schedules sequential, uniform (van der Corput
     bit reversal), query, p_attention, oracle, support_last, random; cumulative
     stage sets reaching ceil(fraction * tokens) (progressive_kv_feasibility.py:211-313).
+  * ``prefix_visibility_mask`` / ``pd_visibility_mask`` / ``encode_contiguous_cache``
+    / ``encode_independent_cache``: the whole-cache view model of the
+    feasibility runners (progressive_kv_feasibility.py:374-447;
+    pd_progressive_kv_feasibility.py:80-91), with ``visible_slot_map``
+    turning a mask into the slot map the engine reads.
   * ``TrancheStager``: each stage's disjoint token ranges packed into one
     pinned host block; stage 0 always carries the system prefix and the
     question suffix; tranches are appended to a compact device cache on a copy
@@ -233,6 +238,79 @@ def stage_document_sets(ranking: Sequence[int], documents: Sequence[Document],
     if any(not a <= b for a, b in zip(stages, stages[1:])):
         raise RuntimeError("stage document sets are not cumulative")
     return stages
+
+
+# --------------------------------------------------------------------------
+# Whole-cache encoders and visibility masks (the feasibility runners' view model)
+# --------------------------------------------------------------------------
+def prefix_visibility_mask(prefix_tokens: int, documents: Sequence[Document], selected,
+                           device=None) -> torch.Tensor:
+    """[1, prefix + documents] int64 mask: the prefix and the selected documents' spans are 1.
+
+    Reference: experiments/progressive_kv_feasibility.py:432-447.  Documents
+    carry their ``start``/``end`` in the concatenated prompt.
+    """
+    total = prefix_tokens + sum(len(d.token_ids) for d in documents)
+    mask = torch.zeros((1, total), dtype=torch.long, device=device)
+    mask[:, :prefix_tokens] = 1
+    for i in selected:
+        mask[:, documents[i].start:documents[i].end] = 1
+    return mask
+
+
+def pd_visibility_mask(prefix_tokens: int, documents: Sequence[Document], suffix_tokens: int, selected,
+                       device=None) -> torch.Tensor:
+    """As ``prefix_visibility_mask`` plus the question suffix, always visible (the P/D anchor).
+
+    Reference: experiments/pd_progressive_kv_feasibility.py:80-91.
+    """
+    doc_mask = prefix_visibility_mask(prefix_tokens, documents, selected, device)
+    tail = torch.ones((1, suffix_tokens), dtype=torch.long, device=doc_mask.device)
+    return torch.cat((doc_mask, tail), dim=1)
+
+
+def visible_slot_map(mask: torch.Tensor) -> torch.Tensor:
+    """int32 indices of the visible tokens of a [1, T] mask.
+
+    The engine's draft attention reads a view through such a slot map, so a
+    masked view costs no mask tensor and no K/V copy.
+    """
+    return mask.reshape(-1).nonzero().reshape(-1).to(torch.int32)
+
+
+@torch.no_grad()
+def encode_contiguous_cache(model, token_ids: Sequence[int]):
+    """One causal prefill of the whole prompt at positions 0..T-1 (oracle model) -> legacy cache.
+
+    Reference: experiments/progressive_kv_feasibility.py:416-429.
+    """
+    _, cache = model.prefill(list(token_ids), start=0)
+    return cache
+
+
+@torch.no_grad()
+def encode_independent_cache(model, prefix: Sequence[int], documents: Sequence[Document]):
+    """Prefix and every document prefilled alone at local positions, keys relocated to ``document.start``.
+
+    The result is the concatenated cache a reuse system composes from
+    independently produced entries (reference:
+    experiments/progressive_kv_feasibility.py:374-413); the engine path is the
+    document producer plus the ``compose_relocate`` kernel.
+    """
+    from ..rope import relocate_key
+
+    cfg = model.config
+    segments = [(tuple(prefix), 0)] + [(d.token_ids, d.start) for d in documents]
+    keys: list[list[torch.Tensor]] = [[] for _ in range(cfg.n_layers)]
+    values: list[list[torch.Tensor]] = [[] for _ in range(cfg.n_layers)]
+    for ids, start in segments:
+        if not ids:
+            continue
+        _, cache = model.prefill(list(ids), start=0)
+        for layer, (k, v) in enumerate(cache):
+            keys[layer].append(relocate_key(cfg, k, source_start=0, target_start=start))
+            values[layer].append(v)
+    return tuple((torch.cat(keys[l], dim=2), torch.cat(values[l], dim=2)) for l in range(cfg.n_layers))
 
 
 def accepted_prefix_length(draft_tokens: Sequence[int], target_tokens: Sequence[int]) -> int:

@@ -129,3 +129,37 @@ def test_stager_layout_and_paced_wire():
         TrancheStager(source, Slot(), prefix_tokens=4, documents=docs, suffix_tokens=3, ranking=ranking,
                       selected_sets=stages, transport_gbps=1.0, eager_serial_wire=True,
                       clock=clock, sleep=sleep).launch(1)
+
+
+def test_whole_cache_encoders_and_visibility_masks():
+    """Independent encoding equals each segment prefilled alone at its target offset (RoPE attention
+    depends on relative positions only); masks open the prefix, the chosen documents and the suffix."""
+    from sparsecache_b200.config import get_model_config
+    from sparsecache_b200.models.llama import LlamaOracle
+    from sparsecache_b200.serving.progressive import (Document, encode_contiguous_cache, encode_independent_cache,
+                                                      pd_visibility_mask, prefix_visibility_mask, visible_slot_map)
+
+    model = LlamaOracle.random_init(get_model_config("tiny"), seed=2, std=0.05)
+    g = torch.Generator().manual_seed(0)
+    prefix = torch.randint(4, 1024, (5,), generator=g).tolist()
+    docs, start = [], len(prefix)
+    for n in (7, 4, 9):
+        ids = tuple(torch.randint(4, 1024, (n,), generator=g).tolist())
+        docs.append(Document(ids, start=start, end=start + n))
+        start += n
+    cache = encode_independent_cache(model, prefix, docs)
+    assert cache[1][0].shape == (1, 2, start, 64)
+    d = docs[2]
+    _, alone = model.prefill(list(d.token_ids), start=d.start)
+    for layer in range(2):
+        assert torch.allclose(cache[layer][0][:, :, d.start:d.end], alone[layer][0], atol=1e-4, rtol=1e-4)
+        assert torch.allclose(cache[layer][1][:, :, d.start:d.end], alone[layer][1], atol=1e-4, rtol=1e-4)
+    full = encode_contiguous_cache(model, prefix + [t for x in docs for t in x.token_ids])
+    assert torch.allclose(full[0][0][:, :, :5], cache[0][0][:, :, :5], atol=1e-5)  # the prefix is the same prefill
+    m = prefix_visibility_mask(len(prefix), docs, {1})
+    assert m.shape == (1, start) and m[0, :5].all() and m[0, docs[1].start:docs[1].end].all()
+    assert int(m.sum()) == 5 + 4
+    pm = pd_visibility_mask(len(prefix), docs, 3, {0, 2})
+    assert pm.shape == (1, start + 3) and pm[0, -3:].all() and int(pm.sum()) == 5 + 7 + 9 + 3
+    sm = visible_slot_map(m)
+    assert sm.dtype == torch.int32 and sm.tolist() == list(range(5)) + list(range(docs[1].start, docs[1].end))
