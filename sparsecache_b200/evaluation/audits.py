@@ -96,3 +96,89 @@ def quality_audit(records: Sequence[dict], metadata: Sequence[dict], decode: Cal
                      "score": score})
     return {"overall": statistics.fmean(x["score"] for x in rows) if rows else None,
             "per_dataset": {k: statistics.fmean(v) for k, v in per_ds.items()}, "rows": rows}
+
+
+def _percentile_rank(values: Sequence[int], q: float) -> float:
+    import math
+
+    if not values:
+        return 0.0
+    xs = sorted(values)
+    return float(xs[min(len(xs) - 1, math.ceil(q * len(xs)) - 1)])
+
+
+def _coverage_summary(rows: Sequence[dict]) -> dict[str, Any]:
+    if not rows:
+        raise ValueError("cannot summarise an empty coverage split")
+    return {"requests": len(rows),
+            "any_support_chunk_rate": statistics.fmean(float(r["selected_support_chunks"] > 0) for r in rows),
+            "all_support_chunks_rate": statistics.fmean(float(r["support_chunk_recall"] == 1.0) for r in rows),
+            "mean_support_chunk_recall": statistics.fmean(r["support_chunk_recall"] for r in rows),
+            "all_support_documents_touched_rate": statistics.fmean(float(r["support_document_recall"] == 1.0)
+                                                                  for r in rows),
+            "mean_support_document_recall": statistics.fmean(r["support_document_recall"] for r in rows),
+            "all_support_chunks_rank_p50": _percentile_rank([r["all_support_chunks_rank"] for r in rows], 0.5),
+            "all_support_chunks_rank_p95": _percentile_rank([r["all_support_chunks_rank"] for r in rows], 0.95)}
+
+
+def analyze_priority_coverage(schedule_root: Path, *, fractions: Sequence[float],
+                              selection_requests: int) -> dict[str, Any]:
+    """Evidence coverage of every priority mode at chunk budgets, split into selection / confirmation rows.
+
+    Reference: experiments/analyze_ruler_priority_coverage.py.  For each
+    fraction f the first ceil(f * chunks) chunks of the order are "arrived":
+    supporting-chunk recall, supporting-document touch rate and the rank at
+    which the last supporting chunk arrives.
+    """
+    import math
+
+    if not fractions or len(set(fractions)) != len(fractions) or any(not 0 < f <= 1 for f in fractions):
+        raise ValueError("fractions must be unique and lie in (0, 1]")
+    root = Path(schedule_root)
+    audit = json.loads((root / "audit.json").read_text(encoding="utf-8"))
+    if audit.get("status") != "passed":
+        raise ValueError("the priority schedule audit has not passed")
+    n = int(audit["requests"])
+    if not 0 < selection_requests < n:
+        raise ValueError("the selection split must leave a non-empty confirmation split")
+    chunk = int(audit["chunk_tokens"])
+    total = int(audit["prompt_tokens"]) // chunk
+    spans = _jsonl(root / "document_spans.jsonl")
+    if len(spans) != n:
+        raise ValueError("document span row count differs from the audit")
+    modes = {}
+    for mode in audit["modes"]:
+        prio = _jsonl(root / f"priority_{mode}.jsonl")
+        if len(prio) != n:
+            raise ValueError("priority row count differs from the audit")
+        per_fraction = {}
+        for f in fractions:
+            budget = math.ceil(total * f)
+            rows = []
+            for i, (srow, prow) in enumerate(zip(spans, prio)):
+                if int(srow.get("request_index", -1)) != i or int(prow.get("request_index", -1)) != i:
+                    raise ValueError("request order differs across scheduling files")
+                order = prow.get("priority_chunks")
+                if not isinstance(order, list) or sorted(order) != list(range(total)):
+                    raise ValueError("priority row is not a complete permutation")
+                docs = [set(range(int(s["start_token"]) // chunk, math.ceil(int(s["end_token"]) / chunk)))
+                        for s in srow["document_spans"] if s.get("supporting") is True]
+                if not docs:
+                    raise ValueError("request has no supporting document span")
+                support = set().union(*docs)
+                rank = {c: k + 1 for k, c in enumerate(order)}
+                chosen = set(order[:budget])
+                rows.append({"request_index": i, "support_chunks": len(support),
+                             "selected_support_chunks": len(chosen & support),
+                             "support_chunk_recall": len(chosen & support) / len(support),
+                             "support_document_recall": sum(bool(chosen & d) for d in docs) / len(docs),
+                             "all_support_chunks_rank": max(rank[c] for c in support)})
+            per_fraction[str(f)] = {"fraction": f, "budget_chunks": budget, "budget_tokens": budget * chunk,
+                                    "all": _coverage_summary(rows),
+                                    "selection": _coverage_summary(rows[:selection_requests]),
+                                    "confirmation": _coverage_summary(rows[selection_requests:])}
+        modes[mode] = per_fraction
+    return {"schema_version": 1, "status": "passed", "schedule_root": str(root), "requests": n,
+            "selection_rows": [0, selection_requests], "confirmation_rows": [selection_requests, n],
+            "prompt_tokens": int(audit["prompt_tokens"]), "chunk_tokens": chunk, "total_chunks": total,
+            "fractions": list(fractions), "modes": modes}

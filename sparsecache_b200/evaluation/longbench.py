@@ -266,15 +266,124 @@ def encode_parts(tokenizer, rendered: str, placeholder: str, context: str):
 
 
 def build_longbench_request(tokenizer, dataset: str, row: dict[str, Any], *, max_prompt_tokens: int,
-                            chunk_tokens: int = 256, disable_thinking: bool = False) -> dict[str, Any]:
+                            chunk_tokens: int = 256, disable_thinking: bool = False,
+                            padding_token_id: int = 198) -> dict[str, Any]:
     """One P/D request row: chunk-aligned prompt ids plus its scoring metadata."""
     rendered, ph = render_longbench(tokenizer, dataset, row, disable_thinking=disable_thinking)
-    prefix, ctx, suffix = encode_parts(tokenizer, rendered, ph, row["context"])
+    prefix, ctx, suffix = encode_parts(tokenizer, rendered, ph, str(row["context"]))
     prompt, cap_removed, align_removed, pad = align_context_to_chunk(
-        prefix, ctx, suffix, max_prompt_tokens=max_prompt_tokens, chunk_tokens=chunk_tokens)
+        prefix, ctx, suffix, max_prompt_tokens=max_prompt_tokens, chunk_tokens=chunk_tokens,
+        padding_token_id=padding_token_id)
     cap = LONG_BENCH_V2_MAX_NEW_TOKENS if dataset == "longbench_v2" else LONG_BENCH_MAX_NEW_TOKENS.get(dataset, 32)
     answers = row.get("answers") or [row.get("answer", "")]
     return {"prompt": prompt, "max_tokens": cap, "dataset": dataset, "answers": list(answers),
             "all_classes": row.get("all_classes"), "cap_removed_tokens": cap_removed,
             "alignment_removed_tokens": align_removed, "padding_tokens": pad, "prefix_tokens": len(prefix),
             "suffix_tokens": len(suffix)}
+
+
+def iter_dataset_rows(path):
+    """Rows of a JSON list or a JSONL file (objects only)."""
+    import json
+    from pathlib import Path
+
+    path = Path(path)
+    if path.suffix == ".json":
+        rows = json.loads(path.read_text(encoding="utf-8"))
+        if not isinstance(rows, list):
+            raise TypeError("a JSON dataset must hold a list of request objects")
+    else:
+        rows = (json.loads(x) for x in path.read_text(encoding="utf-8").splitlines() if x.strip())
+    for row in rows:
+        if not isinstance(row, dict):
+            raise TypeError("dataset rows must be objects")
+        yield row
+
+
+def build_longbench_pack(tokenizer, dataset_path, dataset: str, output_dir, *, fmt: str = "longbench",
+                         served_model_name: str = "sparsecache-llama31-8b", num_requests: int | None = None,
+                         max_prompt_tokens: int = 32768, chunk_tokens: int = 256,
+                         fixed_output_tokens: int | None = None, disable_thinking: bool = False,
+                         tokenizer_name: str = "") -> dict[str, Any]:
+    """Write a chunk-aligned LongBench / LongBench-v2 P/D pack; returns its manifest.
+
+    Reference: experiments/build_longbench_pd_pack.py:182-344.  The context is
+    middle-truncated to the length cap and then down to whole transfer chunks;
+    one newline token pads a prompt only when aligning would remove the whole
+    context.  ``requests.jsonl`` holds completion requests (prompt ids),
+    ``metadata.jsonl`` the scoring fields, ``manifest.json`` the hashes.
+    """
+    import json
+    from pathlib import Path
+
+    from .audits import _sha256
+
+    if chunk_tokens <= 0 or max_prompt_tokens <= 0 or max_prompt_tokens % chunk_tokens:
+        raise ValueError("max_prompt_tokens must be a positive multiple of chunk_tokens")
+    if num_requests is not None and num_requests <= 0:
+        raise ValueError("num_requests must be positive")
+    if fixed_output_tokens is not None and fixed_output_tokens <= 0:
+        raise ValueError("fixed_output_tokens must be positive")
+    if fmt not in ("longbench", "longbench_v2"):
+        raise ValueError(f"unknown pack format {fmt}")
+    output_dir = Path(output_dir)
+    if output_dir.exists():
+        raise FileExistsError(f"refusing to overwrite {output_dir}")
+    newline = tokenizer.encode("\n", add_special_tokens=False)
+    if len(newline) != 1:
+        raise ValueError("the tokenizer must encode a newline as one alignment token")
+    output_dir.mkdir(parents=True)
+    req_path, meta_path = output_dir / "requests.jsonl", output_dir / "metadata.jsonl"
+    lengths, cap_rm, align_rm, pads = [], [], [], []
+    name = "longbench_v2" if fmt == "longbench_v2" else dataset
+    with req_path.open("w", encoding="utf-8") as rq, meta_path.open("w", encoding="utf-8") as md:
+        for source_index, row in enumerate(iter_dataset_rows(dataset_path)):
+            r = build_longbench_request(tokenizer, name, row, max_prompt_tokens=max_prompt_tokens,
+                                        chunk_tokens=chunk_tokens, disable_thinking=disable_thinking,
+                                        padding_token_id=int(newline[0]))
+            out_tokens = fixed_output_tokens or r["max_tokens"]
+            rq.write(json.dumps({"model": served_model_name, "prompt": r["prompt"], "max_tokens": out_tokens,
+                                 "temperature": 0, "ignore_eos": fixed_output_tokens is not None,
+                                 "stream": True, "return_token_ids": True}) + "\n")
+            answers = r["answers"] if fmt == "longbench" else (
+                list(row["answer"]) if isinstance(row.get("answer"), list) else [str(row.get("answer", ""))])
+            md.write(json.dumps({"request_index": len(lengths), "source_index": source_index,
+                                 "id": str(row.get("_id", row.get("id", source_index))), "dataset": dataset,
+                                 "format": fmt, "answers": answers, "all_classes": row.get("all_classes"),
+                                 "prompt_tokens": len(r["prompt"]),
+                                 "cap_removed_context_tokens": r["cap_removed_tokens"],
+                                 "alignment_removed_context_tokens": r["alignment_removed_tokens"],
+                                 "alignment_added_newline_tokens": r["padding_tokens"],
+                                 "prefix_tokens": r["prefix_tokens"], "suffix_tokens": r["suffix_tokens"],
+                                 "output_tokens": out_tokens,
+                                 "fixed_output_horizon": fixed_output_tokens is not None},
+                                ensure_ascii=False) + "\n")
+            lengths.append(len(r["prompt"]))
+            cap_rm.append(r["cap_removed_tokens"])
+            align_rm.append(r["alignment_removed_tokens"])
+            pads.append(r["padding_tokens"])
+            if num_requests is not None and len(lengths) == num_requests:
+                break
+    if not lengths:
+        raise ValueError("the dataset produced no requests")
+    if num_requests is not None and len(lengths) != num_requests:
+        raise ValueError(f"the dataset produced {len(lengths)} requests, expected {num_requests}")
+    n = len(lengths)
+    manifest = {"schema_version": 1, "status": "deterministic P/D request pack; no experiment result",
+                "dataset": dataset, "format": fmt, "source": str(Path(dataset_path).resolve()),
+                "tokenizer": tokenizer_name, "served_model_name": served_model_name, "prompt_mode": "official_chat",
+                "thinking_mode": "disabled" if disable_thinking else "template_default",
+                "context_truncation": "middle",
+                "transport_alignment": "context trimmed down to whole chunks; padded only when trimming would "
+                                       "remove the whole context",
+                "alignment_padding_token_id": int(newline[0]), "chunk_tokens": chunk_tokens,
+                "max_prompt_tokens": max_prompt_tokens, "fixed_output_tokens": fixed_output_tokens, "requests": n,
+                "prompt_tokens": {"min": min(lengths), "max": max(lengths), "mean": sum(lengths) / n},
+                "alignment_removed_context_tokens": {"max": max(align_rm), "mean": sum(align_rm) / n},
+                "alignment_added_newline_tokens": {"max": max(pads), "mean": sum(pads) / n,
+                                                   "affected_requests": sum(x > 0 for x in pads)},
+                "cap_removed_context_tokens": {"max": max(cap_rm), "mean": sum(cap_rm) / n},
+                "requests_sha256": _sha256(req_path), "metadata_sha256": _sha256(meta_path)}
+    (output_dir / "manifest.json").write_text(json.dumps(manifest, indent=2, ensure_ascii=False) + "\n",
+                                              encoding="utf-8")
+    return manifest

@@ -6,15 +6,18 @@ uniform bisection order (:56-71), per-request BM25 with k1 = 1.2, b = 0.75
 spans (:120-132), prompt-marker span recovery (:145-182) and the five modes
 sequential / uniform / random (hashed seed) / bm25 / oracle (:185-235).
 Every order returned is a complete permutation of the chunk indices with the
-protected prefix and suffix chunks first.
+protected prefix and suffix chunks first.  ``build_priority_sidecars`` writes a
+pack's per-mode sidecars, its document spans and the passing audit (:236-400).
 """
 from __future__ import annotations
 
 import hashlib
+import json
 import math
 import random
 import re
 from collections import Counter
+from pathlib import Path
 from typing import Any, Sequence
 
 MODES = ("sequential", "uniform", "random", "bm25", "oracle")
@@ -150,3 +153,89 @@ def coverage_curve(order: Sequence[int], spans: Sequence[dict[str, Any]], chunk_
         seen += sum(1 for t in range(c * chunk_tokens, (c + 1) * chunk_tokens) if t in support)
         out.append(seen / len(support))
     return out
+
+
+def _read_jsonl(path) -> list[dict]:
+    rows = [json.loads(x) for x in Path(path).read_text(encoding="utf-8").splitlines() if x.strip()]
+    if not rows:
+        raise ValueError(f"{path} contains no rows")
+    return rows
+
+
+def build_priority_sidecars(pack_dir, output_dir, *, modes: Sequence[str] = MODES, chunk_tokens: int = 256,
+                            protected_prefix_tokens: int = 256, protected_suffix_tokens: int = 512,
+                            seed: int = 20260827, tokenizer=None) -> dict[str, Any]:
+    """Write ``priority_<mode>.jsonl`` sidecars, ``document_spans.jsonl`` and ``audit.json`` for a RULER pack.
+
+    Reference: experiments/build_ruler_chunk_priorities.py:236-400.  Document
+    spans come from the pack metadata when the pack builder recorded them
+    (``pack_metadata_spans``); otherwise they are recovered from the
+    "Document i:" markers of the immutable prompt ids (``exact_token_marker_scan``,
+    which needs ``tokenizer``).  Every row of every mode is a full permutation of
+    the prompt's chunks with the protected prefix / suffix chunks first.
+    """
+    from .audits import _sha256
+
+    modes = tuple(modes)
+    if not modes or len(set(modes)) != len(modes) or any(m not in MODES for m in modes):
+        raise ValueError(f"modes must be unique values from {MODES}")
+    if min(chunk_tokens, protected_prefix_tokens, protected_suffix_tokens) <= 0:
+        raise ValueError("chunk and protected token counts must be positive")
+    pack_dir, output_dir = Path(pack_dir), Path(output_dir)
+    if output_dir.exists():
+        raise FileExistsError(f"refusing to overwrite {output_dir}")
+    manifest = json.loads((pack_dir / "manifest.json").read_text(encoding="utf-8"))
+    if manifest.get("dataset") != "ruler_qa2":
+        raise ValueError("chunk scheduling needs a RULER qa_2 pack")
+    prompt_tokens = int(manifest["prompt_tokens"])
+    if prompt_tokens % chunk_tokens:
+        raise ValueError("the prompt length must hold whole scheduling chunks")
+    sources = _read_jsonl(manifest["source"])
+    req_path, meta_path = pack_dir / "requests.jsonl", pack_dir / "metadata.jsonl"
+    requests, metadata = _read_jsonl(req_path), _read_jsonl(meta_path)
+    if len(requests) != len(metadata):
+        raise ValueError("request and metadata row counts differ")
+    total = prompt_tokens // chunk_tokens
+    pre, suf = math.ceil(protected_prefix_tokens / chunk_tokens), math.ceil(protected_suffix_tokens / chunk_tokens)
+    out_rows: dict[str, list[dict]] = {m: [] for m in modes}
+    span_rows, recon = [], Counter()
+    for index, (req, meta) in enumerate(zip(requests, metadata)):
+        source = sources[int(meta["source_index"])]
+        rid = str(meta.get("id", source.get("id", index)))
+        if meta.get("document_spans"):
+            spans = [dict(s) for s in meta["document_spans"]]
+            docs = [source["documents"][int(s["source_document_index"])] for s in spans]
+            how = "pack_metadata_spans"
+        else:
+            if tokenizer is None:
+                raise ValueError("the pack has no document spans; a tokenizer is needed to recover them")
+            spans, docs = document_spans_from_prompt_markers(tokenizer, req["prompt"], source, manifest["placement"],
+                                                             protected_suffix_tokens)
+            how = "exact_token_marker_scan"
+        recon[how] += 1
+        span_rows.append({"request_index": index, "id": rid, "prefix_tokens": int(spans[0]["start_token"]),
+                          "suffix_tokens": len(req["prompt"]) - int(spans[-1]["end_token"]),
+                          "coordinate_reconstruction": how, "document_spans": spans})
+        for mode in modes:
+            out_rows[mode].append({"request_index": index, "id": rid, "mode": mode, "priority_chunks": priority_for_mode(
+                mode, request_id=rid, question=str(source["question"]), documents=docs, spans=spans,
+                total_chunks=total, chunk_tokens=chunk_tokens, protected_prefix_chunks=pre,
+                protected_suffix_chunks=suf, seed=seed)})
+    output_dir.mkdir(parents=True)
+    spans_path = output_dir / "document_spans.jsonl"
+    spans_path.write_text("".join(json.dumps(r, ensure_ascii=False) + "\n" for r in span_rows), encoding="utf-8")
+    hashes = {}
+    for mode, rows in out_rows.items():
+        path = output_dir / f"priority_{mode}.jsonl"
+        path.write_text("".join(json.dumps(r) + "\n" for r in rows), encoding="utf-8")
+        hashes[mode] = _sha256(path)
+    audit = {"schema_version": 1, "status": "passed", "pack_dir": str(pack_dir), "requests": len(requests),
+             "prompt_tokens": prompt_tokens, "chunk_tokens": chunk_tokens,
+             "protected_prefix_tokens": protected_prefix_tokens, "protected_suffix_tokens": protected_suffix_tokens,
+             "modes": list(modes), "online_modes": [m for m in modes if m != "oracle"],
+             "analysis_upper_bound_modes": [m for m in modes if m == "oracle"],
+             "coordinate_reconstruction_modes": dict(recon), "requests_sha256": _sha256(req_path),
+             "metadata_sha256": _sha256(meta_path), "document_spans_sha256": _sha256(spans_path),
+             "priority_sha256": hashes}
+    (output_dir / "audit.json").write_text(json.dumps(audit, indent=2) + "\n", encoding="utf-8")
+    return audit

@@ -202,3 +202,30 @@ def build_pack(tokenizer, dataset_path: Path, placement: str, prompt_tokens: int
                 "tokenizer": getattr(tokenizer, "name_or_path", "")}
     (output_dir / "manifest.json").write_text(json.dumps(manifest, indent=2, sort_keys=True) + "\n")
     return manifest
+
+
+def normalize_tree(source_hotpot: Path, input_root: Path, output_root: Path,
+                   lengths: Sequence[int]) -> dict[str, Any]:
+    """Normalise ``<input_root>/<length>/qa_2/validation.jsonl`` for every length -> ``qa2_<length>.jsonl``.
+
+    Reference: experiments/normalize_ruler_qa2.py:68-125.  ``source_hotpot`` is
+    the HotpotQA JSON list the RULER rows index into (evidence titles and
+    questions are checked against it).  Returns and writes ``audit.json``.
+    """
+    source = json.loads(Path(source_hotpot).read_text(encoding="utf-8"))
+    output_root = Path(output_root)
+    output_root.mkdir(parents=True, exist_ok=True)
+    audit = {}
+    for length in lengths:
+        src = Path(input_root) / str(length) / "qa_2" / "validation.jsonl"
+        rows = [json.loads(x) for x in src.read_text(encoding="utf-8").splitlines() if x.strip()]
+        out = [normalize_row(r, source[r["index"]], int(length)) for r in rows]
+        dst = output_root / f"qa2_{length}.jsonl"
+        dst.write_text("".join(json.dumps(r, ensure_ascii=False) + "\n" for r in out), encoding="utf-8")
+        audit[str(length)] = {"input": str(src.resolve()), "output": str(dst.resolve()), "rows": len(out),
+                              "mean_documents": sum(len(r["documents"]) for r in out) / max(1, len(out)),
+                              "supporting_document_counts": sorted({sum(d["supporting"] for d in r["documents"])
+                                                                    for r in out}),
+                              "placements": sorted(out[0]["placements"]) if out else []}
+    (output_root / "audit.json").write_text(json.dumps(audit, indent=2) + "\n", encoding="utf-8")
+    return audit

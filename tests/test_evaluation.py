@@ -317,3 +317,119 @@ def test_question_attention_document_scores_match_direct_attention():
     want = [float(tok[b:e].sum()) for b, e in ranges]
     assert max(abs(a - b) for a, b in zip(got, want)) < 1e-5
     assert sum(got) < 1.0 + 1e-5  # the rest of the mass sits on prefix / question tokens
+
+
+def _ruler_raw(tmp_path, n=3, length=2048):
+    """A HotpotQA source list and RULER qa_2 rows built from it (two supporting titles per row)."""
+    import random as _r
+
+    rng = _r.Random(0)
+    words = "river city king museum year born league album river tower".split()
+    source, rows = [], []
+    for i in range(n):
+        titles = [f"Title{i}_{j}" for j in range(5)]
+        source.append({"question": f"Which city is {i}?", "supporting_facts": [[titles[1], 0], [titles[3], 0]]})
+        body = "\n\n".join(f"Document {j + 1}:\n{t}\n" + " ".join(rng.choice(words) for _ in range(60))
+                           for j, t in enumerate(titles))
+        prompt = ("<|begin_of_text|>sys " + ruler.CONTEXT_START + body + ruler.CONTEXT_END + source[-1]["question"]
+                  + "<|eot_id|>")
+        rows.append({"index": i, "input": prompt, "outputs": [f"city{i}"], "length": 900})
+    (tmp_path / "hotpot.json").write_text(json.dumps(source))
+    d = tmp_path / "raw" / str(length) / "qa_2"
+    d.mkdir(parents=True)
+    (d / "validation.jsonl").write_text("".join(json.dumps(r) + "\n" for r in rows))
+
+
+def test_evaluation_clis_end_to_end(tmp_path):
+    """normalize -> RULER pack -> priority sidecars -> coverage -> audits, LongBench pack -> audit -> quality."""
+    from sparsecache_b200.evaluation import cli
+    from sparsecache_b200.models.checkpoint import random_checkpoint
+
+    model = random_checkpoint(tmp_path / "model", "tiny", seed=0)
+    _ruler_raw(tmp_path)
+    norm = cli.main(["normalize-ruler", "--source-hotpot", str(tmp_path / "hotpot.json"), "--input-root",
+                     str(tmp_path / "raw"), "--output-root", str(tmp_path / "norm"), "--lengths", "2048"])
+    assert norm["2048"]["rows"] == 3 and norm["2048"]["supporting_document_counts"] == [2]
+    pack = tmp_path / "packs" / "2048" / "original"
+    man = cli.main(["ruler-pack", "--dataset", str(tmp_path / "norm" / "qa2_2048.jsonl"), "--placement", "original",
+                    "--tokenizer", str(model), "--prompt-tokens", "2048", "--output-dir", str(pack)])
+    assert man["requests"] == 3 and man["prompt_tokens"] == 2048
+    audit = cli.main(["priorities", "--pack-dir", str(pack), "--output-dir", str(tmp_path / "sched"),
+                      "--chunk-tokens", "128", "--protected-prefix-tokens", "128", "--protected-suffix-tokens", "128"])
+    assert audit["status"] == "passed" and audit["coordinate_reconstruction_modes"] == {"pack_metadata_spans": 3}
+    oracle = [json.loads(x) for x in (tmp_path / "sched" / "priority_oracle.jsonl").read_text().splitlines()]
+    assert all(sorted(r["priority_chunks"]) == list(range(16)) for r in oracle)
+    cov = cli.main(["priority-coverage", "--schedule-root", str(tmp_path / "sched"), "--output",
+                    str(tmp_path / "cov.json"), "--fractions", "0.25,0.5", "--selection-requests", "2"])
+    o, s = cov["modes"]["oracle"]["0.5"]["all"], cov["modes"]["sequential"]["0.5"]["all"]
+    assert o["mean_support_chunk_recall"] >= s["mean_support_chunk_recall"] and o["requests"] == 3
+    assert cov["modes"]["oracle"]["0.25"]["confirmation"]["requests"] == 1
+    ar = cli.main(["audit-ruler", "--root", str(tmp_path / "packs"), "--output", str(tmp_path / "ar.json"),
+                   "--lengths", "2048", "--placements", "original", "--requests-per-cell", "3"])
+    assert ar["status"] == "passed"
+    ar2 = cli.main(["audit-ruler", "--root", str(tmp_path / "packs"), "--output", str(tmp_path / "ar2.json"),
+                    "--lengths", "2048", "--placements", "original,evidence_last", "--requests-per-cell", "3"])
+    assert ar2["status"] == "failed" and ar2["failures"][0].startswith("2048/evidence_last")
+    # LongBench pack, audit and the token-id quality scorer
+    rows = [{"_id": f"h{i}", "input": f"Who is {i}?", "context": "Passage text. " * (40 + 30 * i),
+             "answers": [f"answer {i}"]} for i in range(3)]
+    (tmp_path / "hotpotqa.jsonl").write_text("".join(json.dumps(r) + "\n" for r in rows))
+    lb = cli.main(["longbench-pack", "--dataset", str(tmp_path / "hotpotqa.jsonl"), "--dataset-name", "hotpotqa",
+                   "--tokenizer", str(model), "--output-dir", str(tmp_path / "lb" / "hotpotqa"),
+                   "--max-prompt-tokens", "1024", "--chunk-tokens", "256", "--fixed-output-tokens", "8"])
+    assert lb["requests"] == 3 and lb["prompt_tokens"]["max"] <= 1024
+    assert cli.main(["audit-packs", "--root", str(tmp_path / "lb"), "--datasets", "hotpotqa", "--output",
+                     str(tmp_path / "ap.json")])["status"] == "passed"
+    from sparsecache_b200.tokenizer import ByteTokenizer
+
+    tok = ByteTokenizer(1024)
+    (tmp_path / "run").mkdir()
+    (tmp_path / "run" / "results.jsonl").write_text("".join(
+        json.dumps({"request_index": i, "token_ids": tok.encode(t, add_special_tokens=False)}) + "\n"
+        for i, t in enumerate(["answer 0", "wrong", "answer 2"])))
+    q = cli.main(["quality", "--result-dir", str(tmp_path / "run"), "--metadata-jsonl",
+                  str(tmp_path / "lb" / "hotpotqa" / "metadata.jsonl"), "--model", str(model),
+                  "--bootstrap-samples", "200"])
+    assert abs(q["overall"] - 2 / 3) < 1e-9 and q["requests"] == 3
+
+
+def test_live_requests_and_scheduling_queue(tmp_path):
+    """Fixed-length live requests (supports whole, distractors trimmed) and the paired scheduling queue that
+    pins every priority sidecar; an edited sidecar is refused."""
+    from sparsecache_b200.evaluation import cli
+    from sparsecache_b200.models.checkpoint import random_checkpoint
+    from sparsecache_b200.serving.live import queue as q
+    from sparsecache_b200.serving.live import requests as lr
+
+    model = random_checkpoint(tmp_path / "model", "tiny", seed=0)
+    _ruler_raw(tmp_path, n=4)
+    cli.main(["normalize-ruler", "--source-hotpot", str(tmp_path / "hotpot.json"), "--input-root",
+              str(tmp_path / "raw"), "--output-root", str(tmp_path / "norm"), "--lengths", "2048"])
+    norm = tmp_path / "norm" / "qa2_2048.jsonl"
+    s = lr.main(["--dataset", str(norm), "--tokenizer", str(model), "--output", str(tmp_path / "live.jsonl"),
+                 "--prompt-tokens", "2048", "--num-requests", "3"])
+    reqs = [json.loads(x) for x in (tmp_path / "live.jsonl").read_text().splitlines()]
+    assert s["requests"] == 3 and all(len(r["prompt"]) == 2048 and r["ignore_eos"] for r in reqs)
+    with pytest.raises(ValueError, match="fit exactly"):  # no row is long enough to be trimmed to 4096
+        lr.main(["--dataset", str(norm), "--tokenizer", str(model), "--output", str(tmp_path / "x.jsonl"),
+                 "--prompt-tokens", "4096", "--num-requests", "1"])
+    pack = tmp_path / "pack"
+    cli.main(["ruler-pack", "--dataset", str(norm), "--placement", "original", "--tokenizer", str(model),
+              "--prompt-tokens", "2048", "--output-dir", str(pack)])
+    cli.main(["priorities", "--pack-dir", str(pack), "--output-dir", str(tmp_path / "sched"), "--chunk-tokens", "128",
+              "--protected-prefix-tokens", "128", "--protected-suffix-tokens", "128"])
+    assert q.main(["scheduling", "--pack-dir", str(pack), "--schedule-dir", str(tmp_path / "sched"), "--run-root",
+                   str(tmp_path / "runs"), "--output", str(tmp_path / "queue.json"), "--selection-requests", "2",
+                   "--confirmation-requests", "2", "--warmup-requests", "0", "--tranche-fraction", "0.25",
+                   "--start-fraction", "0.25"]) == 0
+    queue = json.loads((tmp_path / "queue.json").read_text())
+    assert len(queue["jobs"]) == 4 and queue["jobs"][0]["retrieve_fractions"] == [0.25, 0.5, 0.75, 1.0]
+    job, _ = q.load_job(tmp_path / "queue.json", queue["jobs"][2]["job_id"])
+    assert job["status"].startswith("blocked") and job["request_offset"] == 2
+    assert set(job["priority_sidecars"]) == set(q.SCHEDULING_MODES)
+    q.validate_pack_hashes(job)
+    (tmp_path / "sched" / "priority_bm25.jsonl").write_text("{}\n")
+    with pytest.raises(ValueError, match="bm25"):
+        q.validate_pack_hashes(job)
+    with pytest.raises(ValueError):
+        q.fraction_schedule(0.3)
