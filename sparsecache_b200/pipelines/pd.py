@@ -9,6 +9,8 @@ Parity with the reference's experiments/pd_progressive_kv_pipeline.py:
     decodes greedily from the full KV;
   * ``run_chain`` (:1120-1243): the continuous draft-while-loading chain with
     one final verifier (``serving.progressive.continuous_graft_chain``);
+  * ``requests_from_pack``: requests of a RULER pack (document spans) or a
+    LongBench pack (context pages) for ``main --pack``;
   * ``evaluate_request`` / ``main`` (:1246-1699): rank documents by a schedule,
     stage them into tranches (anchor = prefix + first ranked documents +
     suffix), run both arms in alternating order on the same staged request,
@@ -208,6 +210,51 @@ def build_result_row(index: int, request, schedule: str, ranking, sets, out: dic
             "protocol": protocol}
 
 
+def requests_from_pack(pack_dir: str | Path, *, page_tokens: int = 256, offset: int = 0,
+                       limit: int | None = None) -> list[tuple[Any, list[bool | None]]]:
+    """(request, supporting flag per document) of the rows of a P/D pack.
+
+    A RULER pack records the document spans of every prompt: each span is one
+    document (contiguous spans required) and carries its supporting flag.  A
+    LongBench pack records the prefix and suffix lengths: its context region is
+    cut into pages of ``page_tokens`` (the last page may be short), the
+    documents of the schedule (reference: pd_progressive_kv_pipeline.py's
+    ``--context-page-tokens``).
+    """
+    from ..synthetic import RAGRequest
+
+    pack_dir = Path(pack_dir)
+    reqs = [json.loads(x) for x in (pack_dir / "requests.jsonl").read_text().splitlines() if x.strip()]
+    meta = [json.loads(x) for x in (pack_dir / "metadata.jsonl").read_text().splitlines() if x.strip()]
+    if len(reqs) != len(meta):
+        raise ValueError("request and metadata row counts differ")
+    if page_tokens <= 0:
+        raise ValueError("page_tokens must be positive")
+    end = len(reqs) if limit is None else min(len(reqs), offset + limit)
+    out = []
+    for i in range(offset, end):
+        prompt, m = [int(t) for t in reqs[i]["prompt"]], meta[i]
+        if m.get("document_spans"):
+            spans = m["document_spans"]
+            for a, b in zip(spans, spans[1:]):
+                if int(a["end_token"]) != int(b["start_token"]):
+                    raise ValueError(f"row {i}: document spans are not contiguous")
+            docs = tuple(tuple(prompt[int(s["start_token"]):int(s["end_token"])]) for s in spans)
+            flags = [bool(s.get("supporting")) for s in spans]
+            head, tail = int(spans[0]["start_token"]), int(spans[-1]["end_token"])
+        else:
+            head, tail = int(m["prefix_tokens"]), len(prompt) - int(m["suffix_tokens"])
+            if not 0 < head < tail <= len(prompt):
+                raise ValueError(f"row {i}: prefix / suffix lengths leave no context")
+            docs = tuple(tuple(prompt[a:min(a + page_tokens, tail)]) for a in range(head, tail, page_tokens))
+            flags = [None] * len(docs)
+        out.append((RAGRequest(index=i, prefix=tuple(prompt[:head]), documents=docs, suffix=tuple(prompt[tail:])),
+                    flags))
+    if not out:
+        raise ValueError("the pack window holds no requests")
+    return out
+
+
 def main(argv=None) -> None:
     from ..config import get_model_config
     from ..models.engine import B200Engine
@@ -227,12 +274,32 @@ def main(argv=None) -> None:
     p.add_argument("--auto-draft-utilization", type=float, default=1.0)
     p.add_argument("--paired-fixed-control", action="store_true",
                    help="also run the fixed first-stage-view chain on the same staged request")
+    p.add_argument("--pack", type=Path, default=None, help="P/D request pack (replaces --workload)")
+    p.add_argument("--request-offset", type=int, default=0)
+    p.add_argument("--context-page-tokens", type=int, default=256)
+    p.add_argument("--model-dir", type=Path, default=None,
+                   help="model directory (config.json + model.safetensors) instead of random-init --model")
     p.add_argument("--output", type=Path, required=True)
     a = p.parse_args(argv)
     free, total = torch.cuda.mem_get_info()
-    cfg = get_model_config(a.model)
-    eng = B200Engine.random(cfg, seed=0, device="cuda", max_positions=65536)
-    reqs = make_requests(a.workload, cfg)[: a.requests]
+    if a.model_dir is not None:
+        from ..models.checkpoint import load_oracle
+
+        eng = B200Engine.from_oracle(load_oracle(a.model_dir, dtype=torch.bfloat16), device="cuda",
+                                     max_positions=65536)
+        cfg = eng.cfg
+        a.model = str(a.model_dir)
+    else:
+        cfg = get_model_config(a.model)
+        eng = B200Engine.random(cfg, seed=0, device="cuda", max_positions=65536)
+    if a.pack is not None:
+        packed = requests_from_pack(a.pack, page_tokens=a.context_page_tokens, offset=a.request_offset,
+                                    limit=a.requests)
+        reqs, flags = [r for r, _ in packed], [f for _, f in packed]
+        a.workload = str(a.pack)
+    else:
+        reqs = make_requests(a.workload, cfg)[a.request_offset:a.request_offset + a.requests]
+        flags = [[None] * len(r.documents) for r in reqs]
     fractions = tuple(float(x) for x in a.stage_fractions.split(","))
     bytes_per_token = cfg.n_layers * 2 * cfg.n_kv_heads * cfg.head_dim * 2
     rows = []
@@ -245,8 +312,8 @@ def main(argv=None) -> None:
     with open(a.output, "w") as f:
         for i, r in enumerate(reqs):
             T = r.prompt_tokens
-            docs = [Document(tuple(d), " ".join(map(str, d[:64])), start=b, end=e)
-                    for d, (b, e) in zip(r.documents, r.document_ranges())]
+            docs = [Document(tuple(d), " ".join(map(str, d[:64])), supporting=sup, start=b, end=e)
+                    for d, (b, e), sup in zip(r.documents, r.document_ranges(), flags[i])]
             # producer: prefill the whole prompt once; its slot is the tranches' source
             src = eng.new_slot(T + a.max_new_tokens + 64)
             ids = torch.tensor(r.prompt, dtype=torch.int32, device=eng.device)
@@ -295,7 +362,7 @@ def main(argv=None) -> None:
                     out[arm] = continuous_graft_chain(eng, stager, seed_token=seed, prompt_tokens=T,
                                                       max_draft_tokens=gamma, max_new_tokens=a.max_new_tokens,
                                                       grow_view=(arm == "chain"))
-            row = build_result_row(i, r, a.schedule, ranking, sets, out, arms=arms, gamma=gamma, residual=residual,
+            row = build_result_row(r.index, r, a.schedule, ranking, sets, out, arms=arms, gamma=gamma, residual=residual,
                                    bytes_per_token=bytes_per_token, prefill_ms=prefill_ms, protocol=protocol)
             rows.append(row)
             f.write(json.dumps(row, default=str) + "\n")

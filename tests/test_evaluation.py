@@ -433,3 +433,33 @@ def test_live_requests_and_scheduling_queue(tmp_path):
         q.validate_pack_hashes(job)
     with pytest.raises(ValueError):
         q.fraction_schedule(0.3)
+
+
+def test_pd_requests_from_packs(tmp_path):
+    """P/D pipeline inputs from a RULER pack (document spans, supporting flags) and a LongBench pack
+    (context pages between the recorded prefix and suffix)."""
+    from sparsecache_b200.evaluation import cli
+    from sparsecache_b200.models.checkpoint import random_checkpoint
+    from sparsecache_b200.pipelines.pd import requests_from_pack
+
+    model = random_checkpoint(tmp_path / "model", "tiny", seed=0)
+    _ruler_raw(tmp_path, n=3)
+    cli.main(["normalize-ruler", "--source-hotpot", str(tmp_path / "hotpot.json"), "--input-root",
+              str(tmp_path / "raw"), "--output-root", str(tmp_path / "norm"), "--lengths", "2048"])
+    pack = tmp_path / "pack"
+    cli.main(["ruler-pack", "--dataset", str(tmp_path / "norm" / "qa2_2048.jsonl"), "--placement", "evidence_last",
+              "--tokenizer", str(model), "--prompt-tokens", "2048", "--output-dir", str(pack)])
+    rows = requests_from_pack(pack, offset=1, limit=5)
+    assert [r.index for r, _ in rows] == [1, 2]
+    r, flags = rows[0]
+    prompt = json.loads((pack / "requests.jsonl").read_text().splitlines()[1])["prompt"]
+    assert list(r.prompt) == prompt and len(r.documents) == 5 and flags == [False, False, False, True, True]
+    lb_rows = [{"_id": "h0", "input": "Who?", "context": "Passage text. " * 120, "answers": ["x"]}]
+    (tmp_path / "hotpotqa.jsonl").write_text(json.dumps(lb_rows[0]) + "\n")
+    cli.main(["longbench-pack", "--dataset", str(tmp_path / "hotpotqa.jsonl"), "--dataset-name", "hotpotqa",
+              "--tokenizer", str(model), "--output-dir", str(tmp_path / "lb"), "--max-prompt-tokens", "2048"])
+    (r, flags), = requests_from_pack(tmp_path / "lb", page_tokens=256)
+    meta = json.loads((tmp_path / "lb" / "metadata.jsonl").read_text())
+    assert len(r.prefix) == meta["prefix_tokens"] and len(r.suffix) == meta["suffix_tokens"]
+    assert all(len(d) == 256 for d in r.documents[:-1]) and 0 < len(r.documents[-1]) <= 256
+    assert flags == [None] * len(r.documents) and r.prompt_tokens % 256 == 0
