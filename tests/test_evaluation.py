@@ -463,3 +463,32 @@ def test_pd_requests_from_packs(tmp_path):
     assert len(r.prefix) == meta["prefix_tokens"] and len(r.suffix) == meta["suffix_tokens"]
     assert all(len(d) == 256 for d in r.documents[:-1]) and 0 < len(r.documents[-1]) <= 256
     assert flags == [None] * len(r.documents) and r.prompt_tokens % 256 == 0
+
+
+def test_matrix_queue_separates_selection_from_confirmation(tmp_path):
+    from sparsecache_b200.pipelines import matrix_queue as mq
+
+    matrix = {"datasets": [{"name": "qmsum", "path": "d/qmsum.jsonl", "available": 200},
+                           {"name": "hotpotqa", "path": "d/hotpotqa.jsonl", "available": 200}],
+              "models": [{"name": "Llama-3.1-8B-Instruct", "path": "m/llama"}, {"name": "Qwen3-8B", "path": "m/qwen"}],
+              "selection_split": {"progressive_focus_cells": {"transport_gbps": [25, 50], "draft_tokens": [16],
+                                                              "arrival_bundles": [4, 8]}},
+              "controlled_context": {"paths": {"16000": "r/qa2_16384.jsonl"}, "evidence_placement": ["first", "last"],
+                                     "requests_per_cell": 200, "primary_model_max_prompt_tokens": 131040},
+              "longbench_v2": {"path": "d/lb2.json", "available": 503, "llama31_8b_max_context_tokens": 120000}}
+    (tmp_path / "m.json").write_text(json.dumps(matrix))
+    q = mq.main(["--matrix", str(tmp_path / "m.json"), "--run-root", str(tmp_path / "runs"),
+                 "--output", str(tmp_path / "q.json")])
+    assert q["counts"] == {"ready": 10, "measurement_integrity": 1, "continuous_policy_selection": 8,
+                           "sparse_kernel_mechanism": 1, "confirmation_templates": 7}
+    sel = [j for j in q["ready_jobs"] if j["phase"] == "continuous_policy_selection"]
+    assert sel[0]["id"] == "select_llama_31_8b_instruct_qmsum_n30_bw25_g16_b4"
+    cmd = sel[1]["command"]
+    assert cmd[cmd.index("--stage-fractions") + 1] == mq.fractions_for_bundles(0.02, 8)
+    assert "--paired-fixed-control" in cmd and cmd[cmd.index("--pack") + 1].endswith("qmsum_n30")
+    assert mq.fractions_for_bundles(0.02, 4).split(",")[-1] == "1.000000"
+    gate = q["ready_jobs"][0]
+    assert gate["validator"][3] == "latency-cell" and "--paired-fixed-control" not in gate["command"]
+    assert q["confirmation_policy"]["status"].startswith("blocked")
+    assert {t["ruler_placement"] for t in q["confirmation_policy"]["templates"] if "ruler_placement" in t} == {
+        "evidence_first", "evidence_last"}
