@@ -46,7 +46,7 @@ all-reduces so that the two receive buffers strictly alternate.
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass, replace
+from dataclasses import replace
 
 import torch
 import torch.distributed as dist

@@ -22,7 +22,6 @@ from datetime import timedelta
 import torch
 import torch.distributed as dist
 
-from .. import ops
 from ..config import get_model_config
 from ..models.engine import EngineWeights, LayerWeights
 from .tp import FLAG_RS_O, FLAG_STAGE_X, FLAG_X, TIMEOUT_NS, TPEngine, TPGroup, local_config
