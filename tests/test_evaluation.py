@@ -492,3 +492,28 @@ def test_matrix_queue_separates_selection_from_confirmation(tmp_path):
     assert q["confirmation_policy"]["status"].startswith("blocked")
     assert {t["ruler_placement"] for t in q["confirmation_policy"]["templates"] if "ruler_placement" in t} == {
         "evidence_first", "evidence_last"}
+
+
+def test_pd_source_aggregation_pairs_arms_and_models_the_link():
+    from sparsecache_b200.pipelines import pd_source as ps
+
+    dense = [{"request_index": i, "prompt_tokens": 8192, "prompt_sha256": f"h{i}", "seed_token_id": 5,
+              "elapsed_ms": 100.0 + i} for i in range(4)]
+    eagle = [{"request_index": i, "prompt_tokens": 8192, "prompt_sha256": f"h{i}", "seed_token_id": 5 + (i == 3),
+              "proposal_ready_ms": 104.0 + 3 * i, "proposal_token_ids": [1, 2, 3, 4],
+              "first_proposal_accepted_prefix": i} for i in range(4)]
+    out = ps.aggregate_source(dense, eagle, bandwidths=(25.0, 1e6), kv_bytes_per_token=131072,
+                              bootstrap_samples=200)
+    assert out["samples"] == 4 and out["seed_match_fraction"] == 0.75
+    assert out["source_extra_ms"]["min"] == 4.0 and out["source_extra_ms"]["max"] == 10.0
+    # 8192 tokens x 128 KiB at 25 Gbit/s = 343.6 ms of transfer: every proposal is ready first
+    slow = out["bandwidths"]["25"]
+    assert slow["proposal_ready_before_full_kv_fraction"] == 1.0
+    assert abs(slow["full_target_kv_transfer_ms"]["mean"] - 8192 * 131072 * 8 / 25e6) < 1e-6
+    assert out["bandwidths"]["1e+06"]["proposal_ready_before_full_kv_fraction"] == 0.0
+    assert ps.accepted_prefix([1, 2, 9], [1, 2, 3]) == 2
+    eagle[0]["prompt_sha256"] = "other"
+    with pytest.raises(ValueError, match="hashes"):
+        ps.aggregate_source(dense, eagle, bandwidths=(25.0,), kv_bytes_per_token=1)
+    with pytest.raises(ValueError, match="different requests"):
+        ps.aggregate_source(dense, eagle[:3], bandwidths=(25.0,), kv_bytes_per_token=1)
