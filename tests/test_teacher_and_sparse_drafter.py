@@ -168,3 +168,24 @@ def test_teacher_extraction_and_extension_clis_on_cpu(tmp_path):
     with pytest.raises(ValueError, match="corpus hash"):
         cli.main(["extend-teacher", "--base-manifest", str(tmp_path / "t3" / "manifest.json"),
                   "--output-dir", str(tmp_path / "t5b"), "--device", "cpu"])
+
+
+def test_teacher_request_rows_are_exact_and_bounded(tmp_path):
+    from sparsecache_b200.training import cli
+
+    path = tmp_path / "r.jsonl"
+    path.write_text("".join(json.dumps(r) + "\n" for r in (
+        {"prompt": [5, 6, 7], "source_dataset": "a", "source_index": 3}, {"prompt": [1] * 9},
+        {"prompt": [1, "x"]}, {"prompt": [8, 9]})))
+    rows = cli.load_request_rows(path, [3, 0], 8)
+    assert [r["request_index"] for r in rows] == [0, 3] and rows[0]["source_index"] == 3
+    with pytest.raises(ValueError, match="cap"):
+        cli.load_request_rows(path, [1], 8)
+    with pytest.raises(ValueError, match="invalid prompt"):
+        cli.load_request_rows(path, [2], 8)
+    with pytest.raises(ValueError, match="missing"):
+        cli.load_request_rows(path, [0, 7], 8)
+    assert cli.parse_layer_list("8,20,31", name="KV layers") == (8, 20, 31)
+    for bad in ("", "1,1", "-1"):
+        with pytest.raises(ValueError):
+            cli.parse_layer_list(bad, name="KV layers")
