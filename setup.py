@@ -41,6 +41,10 @@ setup(
             "sparsecache-prepare=sparsecache_b200.data:main",
             "sparsecache-precompute=sparsecache_b200.precompute:main",
             "sparsecache-qa=sparsecache_b200.qa:main",
+            "sparsecache-train=sparsecache_b200.training.cli:main",
+            "sparsecache-eval=sparsecache_b200.evaluation.cli:main",
+            "sparsecache-feasibility=sparsecache_b200.pipelines.feasibility:main",
+            "sparsecache-pd=sparsecache_b200.pipelines.pd:main",
         ]
     },
 )
