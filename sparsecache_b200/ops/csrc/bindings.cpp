@@ -1020,10 +1020,12 @@ void wait_all(Tensor flags, int64_t n, Tensor epoch, int64_t offset, int64_t tim
 
 namespace sc {
 void register_disk_loader(py::module& m);
+void register_host_pack(py::module& m);
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   sc::register_disk_loader(m);
+  sc::register_host_pack(m);
   m.doc() = "sm_100a kernels of sparsecache_b200";
   m.def("gemm_store", &gemm_store, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("bn"),
         py::arg("splits") = -1);

@@ -392,15 +392,26 @@ class TrancheStager:
         self._stream = None
 
     # ------------------------------------------------------------- setup
-    def pack(self) -> None:
-        """Pack each stage's ranges into one contiguous pinned block."""
+    def pack(self, n_threads: int = 8) -> None:
+        """Pack each stage's ranges into one contiguous pinned block.
+
+        One threaded native gather per stage (``pack_token_ranges``) writes the
+        ranges straight into the pinned block (no intermediate concatenation).
+        """
+        from .. import ops
+
+        ext = ops.ext()
+        src = self.source if self.source.is_contiguous() else self.source.contiguous()
+        L, two, H, T, D = src.shape
+        rows = src.view(L * two * H, T, D)
+        pin = torch.cuda.is_available()
         packed = []
         for st in self.stages:
-            parts = [self.source[:, :, :, b:e] for b, e in st.ranges]
-            block = torch.cat(parts, dim=3) if parts else self.source[:, :, :, :0]
-            pinned = torch.empty(block.shape, dtype=block.dtype, pin_memory=True)
-            pinned.copy_(block)
-            packed.append(pinned)
+            width = st.destination_end - st.destination_start
+            block = torch.empty((L, two, H, width, D), dtype=src.dtype, pin_memory=pin)
+            ext.pack_token_ranges(rows, [b for b, _ in st.ranges], [e for _, e in st.ranges],
+                                  block.view(L * two * H, width, D), n_threads)
+            packed.append(block)
         self._packed = packed
         if torch.cuda.is_available():
             self._stream = torch.cuda.Stream(device=self.device)

@@ -163,3 +163,29 @@ def test_whole_cache_encoders_and_visibility_masks():
     assert pm.shape == (1, start + 3) and pm[0, -3:].all() and int(pm.sum()) == 5 + 7 + 9 + 3
     sm = visible_slot_map(m)
     assert sm.dtype == torch.int32 and sm.tolist() == list(range(5)) + list(range(docs[1].start, docs[1].end))
+
+
+def test_native_tranche_packing_matches_concatenation():
+    """Each stage's pinned block holds its token ranges back to back, as a concatenation along tokens."""
+    from sparsecache_b200 import ops
+    from sparsecache_b200.serving.progressive import Document, TrancheStager
+
+    g = torch.Generator().manual_seed(0)
+    src = torch.randn(3, 2, 2, 100, 8, generator=g).to(torch.bfloat16)
+    docs, at = [], 4
+    for n in (20, 30, 36):
+        docs.append(Document(tuple(range(n)), start=at, end=at + n))
+        at += n
+    st = TrancheStager(src, None, prefix_tokens=4, documents=docs, suffix_tokens=10, ranking=[2, 0, 1],
+                       selected_sets=[{2}, {2, 0}, {0, 1, 2}])
+    st.pack(n_threads=3)
+    for stage, block in zip(st.stages, st._packed):
+        want = torch.cat([src[:, :, :, b:e] for b, e in stage.ranges], dim=3)
+        assert torch.equal(block, want)
+    ext = ops.ext()
+    rows = src.view(-1, 100, 8)
+    out = torch.empty(rows.shape[0], 5, 8, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        ext.pack_token_ranges(rows, [98], [103], out, 2)  # range past the tokens
+    with pytest.raises(RuntimeError):
+        ext.pack_token_ranges(rows, [0], [4], out, 2)  # width differs from the destination
