@@ -8,7 +8,9 @@ sender's flag reached the epoch.  Writes are safe only if a rank never writes a 
 before the peer has consumed the previous content of that slot.  The emulation checks that
 invariant for the schedules the engine uses (steps with an even number of all-reduces) and
 shows the race the even-count rule prevents (an odd count lets two consecutive all-reduces
-hit the same buffer).
+hit the same buffer).  The same is done for the slot reuse of open-loop prefill/decode serving
+(``parallel.pd``): request i goes to decode slot i mod S, and the prefill rank waits on the
+slot's free flag (released by the decoder after request i - S) before pushing.
 """
 import threading
 import time
@@ -110,3 +112,78 @@ def test_odd_all_reduce_count_races():
     # the same slow reduce with an even count (10) is safe: the next step starts on the other buffer
     assert emulate(2, [10, 2], lambda r, s, k: 0.0,
                    lambda r, s, k: 0.05 if (r == 1 and s == 0 and k == 10) else 0.0) == []
+
+
+class PDSlots:
+    """Decode-side slots and flags of one prefill/decode pair (``parallel.pd`` open-loop serving)."""
+
+    def __init__(self, n_slots):
+        self.lock = threading.Lock()
+        self.content = {s: (0, True) for s in range(n_slots)}  # slot -> (request epoch, consumed)
+        self.ready = {s: 0 for s in range(n_slots)}            # completion flag (epoch)
+        self.free = {s: 0 for s in range(n_slots)}             # prefill-side free flag (epoch)
+        self.violations = []
+
+    def _wait(self, cond, deadline=5.0):
+        t0 = time.time()
+        while True:
+            with self.lock:
+                if cond():
+                    return
+            if time.time() - t0 > deadline:
+                raise TimeoutError("bounded wait gave up")
+            time.sleep(0.0002)
+
+
+def _serve_pair(n_requests, n_slots, *, wait_free=True, seed=0):
+    import random
+
+    dev = PDSlots(n_slots)
+    rng = random.Random(seed)
+    pre_delay = [rng.random() * 0.002 for _ in range(n_requests)]
+    dec_delay = [0.002 + rng.random() * 0.004 for _ in range(n_requests)]
+
+    def prefill():
+        for i in range(n_requests):
+            s, e = i % n_slots, i + 1
+            if wait_free and i >= n_slots:  # the decoder released the slot's previous request
+                dev._wait(lambda: dev.free[s] >= e - n_slots)
+            time.sleep(pre_delay[i])
+            with dev.lock:
+                old, consumed = dev.content[s]
+                if not consumed:
+                    dev.violations.append(("overwrite", s, old, e))
+                dev.content[s] = (e, False)
+                dev.ready[s] = e
+
+    def decode():
+        for i in range(n_requests):
+            s, e = i % n_slots, i + 1
+            dev._wait(lambda: dev.ready[s] >= e)
+            time.sleep(dec_delay[i])  # the decode reads the slot for a while
+            with dev.lock:
+                got, _ = dev.content[s]
+                if got != e:
+                    dev.violations.append(("read", s, got, e))
+                dev.content[s] = (got, True)
+                dev.free[s] = e
+
+    threads = [threading.Thread(target=prefill), threading.Thread(target=decode)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(10)
+    return dev.violations
+
+
+@pytest.mark.parametrize("n_slots", [1, 2, 3])
+def test_pd_slot_reuse_waits_for_the_decoder(n_slots):
+    """Request i of a prefill/decode pair goes to slot i mod S; the prefill rank pushes into a slot only
+    after the decoder released the slot's previous request, so no pushed K/V is overwritten unread."""
+    for seed in range(3):
+        assert _serve_pair(24, n_slots, seed=seed) == []
+
+
+def test_pd_slot_reuse_without_the_free_flag_races():
+    """Dropping the free-flag wait lets a fast prefill overwrite a slot the decoder is still reading."""
+    assert any(_serve_pair(24, 2, wait_free=False, seed=s) for s in range(3))
