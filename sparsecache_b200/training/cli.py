@@ -8,6 +8,10 @@
         --output-dir T --request-indices 0-255 --continuation-tokens 8
     python -m sparsecache_b200.training.cli extend-teacher --base-manifest T/manifest.json \\
         --output-dir T5 --continuation-tokens 64
+    python -m sparsecache_b200.training.cli eval-drafter --checkpoint runs/drafter/checkpoint.pt \\
+        --teacher-manifest T/manifest.json --output runs/drafter/eval.json
+    python -m sparsecache_b200.training.cli eval-boundaries --checkpoint runs/drafter/checkpoint.pt \\
+        --teacher-manifest T5/manifest.json --output runs/drafter/boundaries.json
 
 Counterparts of the reference's experiments/train_sparse_kv_eagle.py (flags
 :384-436) and experiments/train_sparse_kv_drafter.py (flags :536-572) with the
@@ -427,6 +431,84 @@ def cmd_extend_teacher(a) -> dict:
     return manifest
 
 
+def _eval_setup(a):
+    """(manifest, samples, held-out ids, drafter with the target embedding / LM head bound, device)."""
+    from . import sparse_drafter
+    from .teacher import load_teacher_dataset
+
+    dev = torch.device(a.device)
+    manifest, samples = load_teacher_dataset(a.teacher_manifest)
+    _, eval_ids = split_indices(samples, train=None, evaluate=a.eval_indices, eval_modulus=a.eval_modulus,
+                                eval_remainder=a.eval_remainder)
+    if not eval_ids:
+        raise ValueError("no evaluation samples")
+    model, _ = sparse_drafter.load_checkpoint(a.checkpoint, target_fingerprint=manifest.get("target_fingerprint"))
+    cfg = model.config
+    vocab = int(manifest.get("vocab_size", 0)) or int(max(int(s.tensors["labels"].max()) for s in samples.values())) + 1
+    emb, head = _target_tensors(a, vocab, cfg.target_hidden_size, dev)
+    model.to(dev)
+    model.bind_target_weights(emb.float() if dev.type == "cpu" else emb, head.float() if dev.type == "cpu" else head)
+    return manifest, samples, eval_ids, model, dev
+
+
+def cmd_eval_drafter(a) -> dict:
+    """Five-cell ablation (memory x seed) of a drafter checkpoint on held-out samples.
+
+    Reference: experiments/eval_sparse_kv_drafter.py:45-171.
+    """
+    from . import sparse_drafter
+
+    manifest, samples, eval_ids, model, dev = _eval_setup(a)
+    fractions = tuple(float(x) for x in a.visibility_fractions.split(","))
+    cells = sparse_drafter.five_cell_ablation(model, [samples[i] for i in eval_ids], fractions, device=dev,
+                                              page_size=a.page_size, selection_seed=a.selection_seed,
+                                              selection_mode=a.selection_mode, max_proposal_tokens=a.max_eval_tokens)
+    out = {"checkpoint": str(a.checkpoint), "teacher_format": manifest.get("format"), "eval_indices": eval_ids,
+           "visibility_fractions": list(fractions), "selection_mode": a.selection_mode, "cells": cells}
+    Path(a.output).parent.mkdir(parents=True, exist_ok=True)
+    Path(a.output).write_text(json.dumps(out, indent=2, default=float) + "\n")
+    return out
+
+
+def cmd_eval_boundaries(a) -> dict:
+    """Drafts that start after a verification boundary (v5 teacher data), by source group, for exact /
+    zero / shuffled memory.  Reference: experiments/eval_sparse_kv_boundaries.py:30-178."""
+    from . import sparse_drafter
+
+    manifest, samples, eval_ids, model, dev = _eval_setup(a)
+    if not str(manifest.get("format", "")).endswith(".v5"):
+        raise ValueError("boundary evaluation needs v5 teacher data (continuation_seed_hidden)")
+    fractions = tuple(float(x) for x in a.visibility_fractions.split(","))
+    held = [samples[i] for i in eval_ids]
+    modes = {m: sparse_drafter.evaluate_boundaries(model, held, fractions, device=dev, page_size=a.page_size,
+                                                   selection_seed=a.selection_seed, selection_mode=a.selection_mode,
+                                                   memory_mode=m, window_tokens=a.window_tokens,
+                                                   maximum_windows_per_sample=a.max_windows_per_sample)
+             for m in ("exact", "zero", "shuffled")}
+    out = {"checkpoint": str(a.checkpoint), "eval_indices": eval_ids, "visibility_fractions": list(fractions),
+           "window_tokens": a.window_tokens, "memory_modes": modes}
+    Path(a.output).parent.mkdir(parents=True, exist_ok=True)
+    Path(a.output).write_text(json.dumps(out, indent=2, default=float) + "\n")
+    return out
+
+
+def _eval_common(p: argparse.ArgumentParser, fractions: str) -> None:
+    p.add_argument("--checkpoint", required=True)
+    p.add_argument("--teacher-manifest", required=True)
+    p.add_argument("--output", required=True)
+    p.add_argument("--eval-indices", default=None)
+    p.add_argument("--eval-modulus", type=int, default=5)
+    p.add_argument("--eval-remainder", type=int, default=0)
+    p.add_argument("--visibility-fractions", default=fractions)
+    p.add_argument("--page-size", type=int, default=64)
+    p.add_argument("--selection-mode", choices=("random", "priority", "strided"), default="priority")
+    p.add_argument("--selection-seed", type=int, default=20960827)
+    p.add_argument("--device", default="cuda")
+    p.add_argument("--target-model", default="llama3-8b", help="random-init target preset (embedding, LM head)")
+    p.add_argument("--target-seed", type=int, default=0)
+    p.add_argument("--target-embedding", default=None, help="tensor file: embedding or {embed, lm_head}")
+
+
 def _common(p: argparse.ArgumentParser) -> None:
     p.add_argument("--teacher-manifest", required=True)
     p.add_argument("--output-dir", required=True)
@@ -494,9 +576,17 @@ def main(argv=None) -> dict:
     t.add_argument("--continuation-tokens", type=int, default=64)
     t.add_argument("--teacher-topk", type=int, default=64)
     t.add_argument("--device", default="cuda")
+    ed = sub.add_parser("eval-drafter")
+    _eval_common(ed, "0.05,0.10,0.20,1.0")
+    ed.add_argument("--max-eval-tokens", type=int, default=8)
+    eb = sub.add_parser("eval-boundaries")
+    _eval_common(eb, "0.05,0.10,0.20")
+    eb.add_argument("--window-tokens", type=int, default=8)
+    eb.add_argument("--max-windows-per-sample", type=int, default=8)
     a = p.parse_args(argv)
     return {"train-eagle": cmd_train_eagle, "train-drafter": cmd_train_drafter,
-            "extract-teacher": cmd_extract_teacher, "extend-teacher": cmd_extend_teacher}[a.cmd](a)
+            "extract-teacher": cmd_extract_teacher, "extend-teacher": cmd_extend_teacher,
+            "eval-drafter": cmd_eval_drafter, "eval-boundaries": cmd_eval_boundaries}[a.cmd](a)
 
 
 if __name__ == "__main__":

@@ -119,6 +119,17 @@ def test_training_clis_end_to_end_on_cpu(tmp_path):
                   "--draft-hidden-size", "8", "--mlp-ratio", "2", "--visibility-fractions", "0.5",
                   "--training-window-tokens", "3", "--max-eval-tokens", "3"])
     assert (tmp_path / "drafter" / "checkpoint.pt").exists() and "exact" in d["ablation"]
+    ev_common = ["--checkpoint", str(tmp_path / "drafter" / "checkpoint.pt"), "--teacher-manifest", str(man),
+                 "--device", "cpu", "--target-embedding", str(tmp_path / "target.pt"), "--eval-indices", "0,3",
+                 "--visibility-fractions", "0.5,1.0"]
+    ev = cli.main(["eval-drafter", *ev_common, "--output", str(tmp_path / "eval.json"), "--max-eval-tokens", "3"])
+    assert ev["eval_indices"] == [0, 3] and set(ev["cells"]) == {"exact", "zero_memory", "shuffled_memory",
+                                                                 "zero_seed", "zero_memory_zero_seed"}
+    assert len(ev["cells"]["exact"]) == 2 and (tmp_path / "eval.json").exists()
+    bd = cli.main(["eval-boundaries", *ev_common, "--output", str(tmp_path / "bd.json"), "--window-tokens", "2",
+                   "--max-windows-per-sample", "2"])
+    row = bd["memory_modes"]["exact"][0]
+    assert row["overall"]["windows"] == 4 and set(row["by_source_group"]) == {"ds0", "ds1"}
     assert cli.split_indices({0, 1, 2, 3}, train="0-2", evaluate=None, eval_modulus=0, eval_remainder=0) == ([0, 1, 2], [3])
     with pytest.raises(ValueError):
         cli.split_indices({0, 1}, train="0-1", evaluate="1", eval_modulus=0, eval_remainder=0)
