@@ -193,7 +193,24 @@ async def run_benchmark(client, endpoint: str, requests: Sequence[dict], arms: S
     return records, summary(records, arms)
 
 
+def parse_sidecars(values: Sequence[str]) -> dict[str, Path]:
+    """``MODE=PATH`` values -> {mode: path}; at least two unique modes."""
+    out: dict[str, Path] = {}
+    for v in values:
+        mode, sep, path = v.partition("=")
+        mode, path = mode.strip(), path.strip()
+        if not sep or not mode or not path or mode in out:
+            raise ValueError("priority sidecars must be unique non-empty MODE=PATH values")
+        out[mode] = Path(path)
+    if len(out) < 2:
+        raise ValueError("a scheduling run needs at least two modes")
+    return out
+
+
 def main(argv=None) -> None:
+    """Paired arms over a request file; with ``--priority-sidecar MODE=PATH`` (two or more) every request
+    runs under every schedule x arm on one shared prefill (reference:
+    experiments/benchmark_progressive_pd_scheduling_live.py)."""
     import httpx
 
     p = argparse.ArgumentParser()
@@ -206,8 +223,12 @@ def main(argv=None) -> None:
     p.add_argument("--warmup-requests", type=int, default=4)
     p.add_argument("--fixed-output-tokens", type=int)
     p.add_argument("--priority-jsonl", type=Path)
-    p.add_argument("--arms", type=parse_arms, default=("baseline", "continuous"))
+    p.add_argument("--arms", type=parse_arms, default=None)
+    p.add_argument("--priority-sidecar", action="append", default=[], metavar="MODE=PATH")
     a = p.parse_args(argv)
+    if a.priority_sidecar:
+        return _scheduling_main(a)
+    a.arms = a.arms or ("baseline", "continuous")
     pri = read_priority_rows(a.priority_jsonl) if a.priority_jsonl else None
     reqs = read_requests(a.requests_jsonl, a.num_requests, a.request_offset, pri)
     if a.fixed_output_tokens:
@@ -222,6 +243,50 @@ def main(argv=None) -> None:
 
     _, summ = asyncio.run(go())
     print(json.dumps(summ, indent=2))
+
+
+
+def _scheduling_main(a) -> dict:
+    import httpx
+
+    from .validate import run_scheduling_benchmark
+
+    if a.output_jsonl.exists():
+        raise FileExistsError(f"refusing to overwrite {a.output_jsonl}")
+    arms = a.arms or ("fixed_s1", "continuous")
+    sidecars = parse_sidecars(a.priority_sidecar)
+    rows = {m: read_priority_rows(path) for m, path in sidecars.items()}
+    reqs = read_requests(a.requests_jsonl, a.num_requests, a.request_offset)
+    horizon = a.fixed_output_tokens or 32
+    for r in reqs:
+        r["max_tokens"], r["ignore_eos"] = horizon, True
+    local = {}
+    for m, by_source in rows.items():
+        missing = [a.request_offset + i for i in range(len(reqs)) if a.request_offset + i not in by_source]
+        if missing:
+            raise ValueError(f"{m} sidecar has no source request {missing[0]}")
+        local[m] = {i: by_source[a.request_offset + i] for i in range(len(reqs))}
+
+    async def go():
+        async with httpx.AsyncClient(base_url=a.url, timeout=None, trust_env=False) as c:
+            return await run_scheduling_benchmark(c, a.endpoint, reqs, local, arms=arms, schedules=tuple(sidecars),
+                                                  run_id=uuid.uuid4().hex[:8])
+
+    recs = asyncio.run(go())
+    a.output_jsonl.parent.mkdir(parents=True, exist_ok=True)
+    with open(a.output_jsonl, "w", encoding="utf-8") as f:
+        for r in recs:
+            r["source_request_index"] = a.request_offset + r["request_index"]
+            f.write(json.dumps(r) + "\n")
+    summ = {"schema_version": 1, "status": "raw live measurements; aggregation gates not yet applied",
+            "modes": list(sidecars), "arms": list(arms), "requests": len(reqs), "request_offset": a.request_offset,
+            "fixed_output_tokens": horizon, "measured_records": len(recs),
+            "expected_records": len(reqs) * len(sidecars) * len(arms),
+            "priority_sidecars": {m: str(pth) for m, pth in sidecars.items()},
+            "prefill_pairing": "one exact producer prefill per request, reused by every schedule x arm"}
+    a.output_jsonl.with_suffix(".summary.json").write_text(json.dumps(summ, indent=2) + "\n")
+    print(json.dumps(summ, indent=2))
+    return summ
 
 
 if __name__ == "__main__":

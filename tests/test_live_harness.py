@@ -283,3 +283,21 @@ def test_proposal_trace_is_atomic_and_first_writer_wins(tmp_path):
     other = tmp_path / "other.json"
     assert publish_proposal_trace(other, method="eagle", proposal_started_at_ns=1, seed_token_ids=[1],
                                   draft_token_ids=[[2]]) is None and not other.exists()
+
+
+def test_scheduling_cli_sidecar_parsing_and_source_rows(tmp_path):
+    """``--priority-sidecar MODE=PATH`` needs two or more unique modes and a row for every source request."""
+    with pytest.raises(ValueError):
+        client.parse_sidecars(["uniform=a.jsonl"])
+    with pytest.raises(ValueError):
+        client.parse_sidecars(["uniform=a.jsonl", "uniform=b.jsonl"])
+    assert set(client.parse_sidecars(["uniform=a", "bm25=b"])) == {"uniform", "bm25"}
+    (tmp_path / "r.jsonl").write_text("".join(json.dumps({"model": "toy", "prompt": [1, 2, 3]}) + "\n"
+                                              for _ in range(3)))
+    for mode in ("uniform", "bm25"):
+        (tmp_path / f"{mode}.jsonl").write_text("".join(
+            json.dumps({"request_index": i, "priority_chunks": [0, 1]}) + "\n" for i in range(2)))
+    with pytest.raises(ValueError, match="no source request 2"):
+        client.main(["--requests-jsonl", str(tmp_path / "r.jsonl"), "--output-jsonl", str(tmp_path / "o.jsonl"),
+                     "--num-requests", "2", "--request-offset", "1", "--priority-sidecar",
+                     f"uniform={tmp_path / 'uniform.jsonl'}", "--priority-sidecar", f"bm25={tmp_path / 'bm25.jsonl'}"])
