@@ -140,6 +140,22 @@ PRESETS: dict[str, ModelConfig] = {
         eos_token_ids=LLAMA3_EOS,
         n_special=0,
     ),
+    # Mistral-7B-Instruct-v0.2 geometry (Llama architecture, no sliding window)
+    "mistral-7b": ModelConfig(
+        name="mistral-7b",
+        n_layers=32,
+        d_model=4096,
+        n_heads=32,
+        n_kv_heads=8,
+        head_dim=128,
+        ffn=14336,
+        vocab=32000,
+        rope_theta=1000000.0,
+        max_positions=32768,
+        bos_token_id=1,
+        eos_token_ids=(2,),
+        n_special=3,
+    ),
     "llama3-70b": ModelConfig(
         name="llama3-70b",
         n_layers=80,

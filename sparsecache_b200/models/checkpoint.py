@@ -4,6 +4,12 @@ Parameter names follow the usual Llama naming (``model.layers.N.self_attn.q_proj
 ...) so the directory is self-describing; ``model_fingerprint`` of the store
 hashes ``config.json`` and ``model.safetensors.index.json`` exactly as the
 reference does for HF checkpoints (store.py:19-27).
+
+Hugging Face Llama / Mistral directories load as they are: a ``config.json``
+with ``num_hidden_layers`` is read as an HF config (GQA head counts,
+``head_dim``, ``rope_theta``, the "llama3" ``rope_scaling`` block, EOS ids,
+tied embeddings), and weights come from ``model.safetensors`` or from the
+shards named by ``model.safetensors.index.json``.
 """
 from __future__ import annotations
 
@@ -13,7 +19,7 @@ from pathlib import Path
 import torch
 from safetensors.torch import load_file, save_file
 
-from ..config import ModelConfig, get_model_config
+from ..config import ModelConfig, RopeScaling, get_model_config
 from .llama import LlamaOracle
 
 
@@ -46,18 +52,74 @@ def save_checkpoint(directory: str | Path, model: LlamaOracle, *, dtype: torch.d
     return root
 
 
+def config_from_hf(data: dict, name: str = "hf") -> ModelConfig:
+    """ModelConfig of a Hugging Face Llama-family ``config.json``."""
+    arch = set(data.get("architectures") or ())
+    if arch and not arch & {"LlamaForCausalLM", "MistralForCausalLM"}:
+        raise ValueError(f"unsupported architecture {sorted(arch)}: the engine implements the Llama geometry")
+    if data.get("sliding_window") not in (None, 0) and int(data["sliding_window"]) < int(
+            data.get("max_position_embeddings", 0)):
+        raise ValueError("sliding-window attention is not implemented")
+    heads = int(data["num_attention_heads"])
+    # transformers < 5 writes rope_theta + rope_scaling; >= 5 one rope_parameters block
+    params = data.get("rope_parameters") or {}
+    scaling = data.get("rope_scaling") or params
+    theta = float(data.get("rope_theta") or params.get("rope_theta") or 10000.0)
+    rope = None
+    kind = scaling.get("rope_type", scaling.get("type")) if scaling else None
+    if kind not in (None, "default"):
+        if kind != "llama3":
+            raise ValueError(f"unsupported rope scaling {kind!r}")
+        rope = RopeScaling(factor=float(scaling["factor"]), low_freq_factor=float(scaling["low_freq_factor"]),
+                           high_freq_factor=float(scaling["high_freq_factor"]),
+                           original_max_position_embeddings=int(scaling["original_max_position_embeddings"]))
+    eos = data.get("eos_token_id")
+    eos_ids = () if eos is None else ((int(eos),) if isinstance(eos, int) else tuple(int(x) for x in eos))
+    return ModelConfig(name=name, n_layers=int(data["num_hidden_layers"]), d_model=int(data["hidden_size"]),
+                       n_heads=heads, n_kv_heads=int(data.get("num_key_value_heads", heads)),
+                       head_dim=int(data.get("head_dim") or int(data["hidden_size"]) // heads),
+                       ffn=int(data["intermediate_size"]), vocab=int(data["vocab_size"]),
+                       rms_eps=float(data.get("rms_norm_eps", 1e-5)), rope_theta=theta,
+                       rope_scaling=rope, max_positions=int(data.get("max_position_embeddings", 131072)),
+                       bos_token_id=int(data.get("bos_token_id", 1) or 1), eos_token_ids=eos_ids)
+
+
 def load_config(directory: str | Path) -> ModelConfig:
-    return ModelConfig.from_dict(json.loads((Path(directory) / "config.json").read_text(encoding="utf-8")))
+    data = json.loads((Path(directory) / "config.json").read_text(encoding="utf-8"))
+    if "num_hidden_layers" in data:
+        return config_from_hf(data, name=Path(directory).name)
+    return ModelConfig.from_dict(data)
+
+
+def _weights(directory: Path) -> dict[str, torch.Tensor]:
+    single = directory / "model.safetensors"
+    index = directory / "model.safetensors.index.json"
+    if index.exists():
+        shards = sorted(set(json.loads(index.read_text(encoding="utf-8"))["weight_map"].values()))
+        out: dict[str, torch.Tensor] = {}
+        for shard in shards:
+            out.update(load_file(str(directory / shard), device="cpu"))
+        return out
+    return load_file(str(single), device="cpu")
 
 
 def load_oracle(directory: str | Path, *, dtype: torch.dtype = torch.float32, device="cpu") -> LlamaOracle:
+    directory = Path(directory)
     cfg = load_config(directory)
     model = LlamaOracle(cfg)
-    tensors = load_file(str(Path(directory) / "model.safetensors"), device="cpu")
+    tensors = _weights(directory)
+    if "lm_head.weight" not in tensors:  # tied embeddings
+        tensors["lm_head.weight"] = tensors["model.embed_tokens.weight"]
     params = dict(model.named_parameters())
+    missing = [n for n, _ in _names(cfg) if n not in tensors]
+    if missing:
+        raise ValueError(f"checkpoint lacks {len(missing)} tensors, e.g. {missing[:3]}")
     with torch.no_grad():
         for name, (module, attr) in _names(cfg):
-            params[f"{module}.{attr}"].copy_(tensors[name])
+            t = tensors[name]
+            if tuple(t.shape) != tuple(params[f"{module}.{attr}"].shape):
+                raise ValueError(f"{name}: shape {tuple(t.shape)} differs from the config's")
+            params[f"{module}.{attr}"].copy_(t)
     return model.to(device=device, dtype=dtype).eval()
 
 

@@ -1,0 +1,55 @@
+"""Hugging Face Llama / Mistral checkpoint directories load into the oracle (and so the engine) with the
+same logits as the transformers model: HF config mapping (GQA, head_dim, rope_theta, llama3 rope scaling,
+EOS ids), sharded safetensors through the index, tied embeddings."""
+import pytest
+import torch
+
+transformers = pytest.importorskip("transformers")
+
+
+def _check(model, tmp_path, *, shard="100KB"):
+    from sparsecache_b200.models.checkpoint import load_config, load_oracle
+
+    model.save_pretrained(tmp_path, max_shard_size=shard, safe_serialization=True)
+    assert (tmp_path / "model.safetensors.index.json").exists()  # sharded
+    oracle = load_oracle(tmp_path)
+    ids = torch.randint(3, model.config.vocab_size, (1, 150), generator=torch.Generator().manual_seed(0))
+    with torch.no_grad():
+        want = model(ids).logits[0, -1].float()
+    got, _ = oracle.prefill(ids[0].tolist())
+    assert torch.allclose(got.float(), want, atol=2e-4, rtol=2e-4), (got - want).abs().max()
+    return load_config(tmp_path)
+
+
+def test_llama_with_llama3_rope_scaling(tmp_path):
+    cfg = transformers.LlamaConfig(vocab_size=512, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                                   num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=256,
+                                   rope_theta=500000.0, eos_token_id=[7, 9], bos_token_id=1,
+                                   rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                                 "high_freq_factor": 4.0, "original_max_position_embeddings": 64})
+    torch.manual_seed(0)
+    mc = _check(transformers.LlamaForCausalLM(cfg).eval(), tmp_path)
+    assert (mc.n_kv_heads, mc.head_dim, mc.eos_token_ids) == (2, 32, (7, 9))
+    assert mc.rope_scaling is not None and mc.rope_scaling.original_max_position_embeddings == 64
+
+
+def test_mistral_with_tied_embeddings(tmp_path):
+    cfg = transformers.MistralConfig(vocab_size=512, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                                     num_attention_heads=4, num_key_value_heads=1, rope_theta=1e6,
+                                     sliding_window=None, tie_word_embeddings=True)
+    torch.manual_seed(1)
+    mc = _check(transformers.MistralForCausalLM(cfg).eval(), tmp_path)
+    assert mc.n_kv_heads == 1 and mc.rope_theta == 1e6
+
+
+def test_unsupported_families_are_refused():
+    from sparsecache_b200.models.checkpoint import config_from_hf
+
+    base = {"num_hidden_layers": 2, "hidden_size": 64, "num_attention_heads": 4, "intermediate_size": 128,
+            "vocab_size": 100}
+    with pytest.raises(ValueError, match="architecture"):
+        config_from_hf({**base, "architectures": ["Qwen3ForCausalLM"]})
+    with pytest.raises(ValueError, match="sliding"):
+        config_from_hf({**base, "sliding_window": 16, "max_position_embeddings": 4096})
+    with pytest.raises(ValueError, match="rope scaling"):
+        config_from_hf({**base, "rope_scaling": {"rope_type": "yarn", "factor": 4.0}})
