@@ -255,6 +255,28 @@ def requests_from_pack(pack_dir: str | Path, *, page_tokens: int = 256, offset: 
     return out
 
 
+def exclusive_gpu_or_exit(*, command_runner=None, max_used_memory_mib: float = 1024.0,
+                          max_utilization_pct: float = 5.0) -> dict[str, Any]:
+    """Fail closed unless the GPU this process uses has no compute process and is idle.
+
+    The physical index is the first entry of CUDA_VISIBLE_DEVICES when that is
+    set, else the current CUDA device (reference: the P/D pipeline's
+    ``--require-exclusive-gpu`` check).
+    """
+    import os
+
+    from ..serving.live import gate
+
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")[0].strip()
+    index = int(vis) if vis.isdecimal() else int(torch.cuda.current_device())
+    states = gate.inspect_gpus(**({"command_runner": command_runner} if command_runner else {}))
+    res = gate.evaluate_exclusivity(states, [index], max_used_memory_mib=max_used_memory_mib,
+                                    max_utilization_pct=max_utilization_pct)
+    if res["status"] != "passed":
+        raise SystemExit(f"GPU {index} is not exclusive: {json.dumps(res['failures'])}")
+    return res
+
+
 def main(argv=None) -> None:
     from ..config import get_model_config
     from ..models.engine import B200Engine
@@ -279,8 +301,14 @@ def main(argv=None) -> None:
     p.add_argument("--context-page-tokens", type=int, default=256)
     p.add_argument("--model-dir", type=Path, default=None,
                    help="model directory (config.json + model.safetensors) instead of random-init --model")
+    p.add_argument("--eager-serial-wire", action="store_true",
+                   help="tranches leave on one serial wire as soon as the request starts (cumulative deadlines)")
+    p.add_argument("--require-exclusive-gpu", action="store_true",
+                   help="refuse to run unless the GPU has no other compute process and is idle")
     p.add_argument("--output", type=Path, required=True)
     a = p.parse_args(argv)
+    if a.require_exclusive_gpu:
+        exclusive_gpu_or_exit()
     free, total = torch.cuda.mem_get_info()
     if a.model_dir is not None:
         from ..models.checkpoint import load_oracle
@@ -308,7 +336,8 @@ def main(argv=None) -> None:
                 "draft_tokens": a.draft_tokens, "max_new_tokens": a.max_new_tokens,
                 "stage_fractions": list(fractions), "fixed_token_horizon": True, "paired_measurement": True,
                 "paired_fixed_control": a.paired_fixed_control, "model": a.model, "workload": a.workload,
-                "require_exclusive_gpu": True, "initial_gpu_used_bytes": int(total - free)}
+                "require_exclusive_gpu": bool(a.require_exclusive_gpu), "eager_serial_wire": bool(a.eager_serial_wire),
+                "initial_gpu_used_bytes": int(total - free)}
     with open(a.output, "w") as f:
         for i, r in enumerate(reqs):
             T = r.prompt_tokens
@@ -354,7 +383,7 @@ def main(argv=None) -> None:
                 dst = eng.new_slot(T + a.max_new_tokens + 64)
                 stager = TrancheStager(host, dst, prefix_tokens=len(r.prefix), documents=docs,
                                        suffix_tokens=len(r.suffix), ranking=ranking, selected_sets=sets,
-                                       transport_gbps=a.transport_gbps)
+                                       transport_gbps=a.transport_gbps, eager_serial_wire=a.eager_serial_wire)
                 if arm == "full_target":
                     out[arm] = run_full_target(eng, stager, seed_token=seed, prompt_tokens=T,
                                                max_new_tokens=a.max_new_tokens)

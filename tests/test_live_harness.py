@@ -301,3 +301,17 @@ def test_scheduling_cli_sidecar_parsing_and_source_rows(tmp_path):
         client.main(["--requests-jsonl", str(tmp_path / "r.jsonl"), "--output-jsonl", str(tmp_path / "o.jsonl"),
                      "--num-requests", "2", "--request-offset", "1", "--priority-sidecar",
                      f"uniform={tmp_path / 'uniform.jsonl'}", "--priority-sidecar", f"bm25={tmp_path / 'bm25.jsonl'}"])
+
+
+def test_pd_pipeline_exclusive_gpu_check(monkeypatch):
+    """``pipelines.pd --require-exclusive-gpu`` maps CUDA_VISIBLE_DEVICES to the physical GPU and fails closed."""
+    from sparsecache_b200.pipelines.pd import exclusive_gpu_or_exit
+
+    def runner(cmd):
+        return GPU_QUERY if cmd[1].startswith("--query-gpu=") else PROC_QUERY
+
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "0")
+    assert exclusive_gpu_or_exit(command_runner=runner)["status"] == "passed"
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "1,0")
+    with pytest.raises(SystemExit, match="GPU 1 is not exclusive"):
+        exclusive_gpu_or_exit(command_runner=runner)
