@@ -68,7 +68,7 @@ def _pd_command(pack_dir: Path, model: dict, output: Path, *, requests: int, fra
     cmd = [PY, "-m", "sparsecache_b200.pipelines.pd", "--pack", str(pack_dir), "--model-dir", str(model["path"]),
            "--requests", str(requests), "--max-new-tokens", "64", "--context-page-tokens", "256",
            "--stage-fractions", fractions, "--draft-tokens", str(drafts), "--transport-gbps", str(bandwidth),
-           "--schedule", "query", "--output", str(output)]
+           "--schedule", "query", "--eager-serial-wire", "--require-exclusive-gpu", "--output", str(output)]
     if paired_fixed_control:
         cmd.append("--paired-fixed-control")
     return cmd
