@@ -69,9 +69,11 @@ class PreparedRequest:
 
 def prepare_request(request: RAGRequest, *, question: str = "", schedule: str = "query",
                     fractions: Sequence[float] = (0.25, 0.5, 1.0), seed: int = 0,
-                    texts: Sequence[str] | None = None) -> PreparedRequest:
+                    texts: Sequence[str] | None = None,
+                    supporting: Sequence[bool | None] | None = None) -> PreparedRequest:
     """Rank the request's documents, re-lay them in ranked order, stage them cumulatively."""
-    docs = [Document(tuple(d), texts[i] if texts else " ".join(map(str, d[:64])))
+    docs = [Document(tuple(d), texts[i] if texts else " ".join(map(str, d[:64])),
+                     supporting=supporting[i] if supporting else None)
             for i, d in enumerate(request.documents)]
     ranking = ranked_document_indices(schedule, question=question or " ".join(map(str, request.suffix)),
                                       documents=docs, random_seed=seed)
@@ -231,6 +233,10 @@ def aggregate(rows: Sequence[dict], *, reference: str = "full", bootstrap_sample
             "ttft_gain_vs_reference_ms": {"mean": statistics.fmean(d_ttft) if d_ttft else math.nan,
                                           "ci95": _boot(d_ttft, bootstrap_samples)},
         }
+        scored = [r["arms"][a] for r in rr if "f1" in r["arms"][a]]
+        if scored:  # dataset runs: short-answer quality
+            out["arms"][a].update(em=statistics.fmean(x["em"] for x in scored),
+                                  f1=statistics.fmean(x["f1"] for x in scored))
     return out
 
 
@@ -247,6 +253,55 @@ def blend_config_from_args(a) -> "CacheBlendConfig":
         ratios = tuple(float(x) for x in a.recompute_ratios.split(","))
         return CacheBlendConfig(check_layers=layers, recompute_ratios=ratios, **common)
     return CacheBlendConfig(check_layer=a.check_layer, recompute_ratio=a.recompute_ratio, **common)
+
+
+def dataset_requests(path: Path, cfg, *, model_dir=None, sample_count: int | None = None, seed: int = 0,
+                     answer_word_limit: int = 5, limit: int | None = None) -> tuple[list[RAGRequest], list[dict]]:
+    """Requests (prefix, one document per paragraph, question suffix) of a MuSiQue-style JSONL.
+
+    Rows are a hop-stratified seeded sample (``sample_count``; all rows when
+    None); the prompt is rendered with the model directory's tokenizer (the
+    byte tokenizer of this package for random-init presets).  The metadata
+    keeps the question, the paragraph texts and supporting flags (for the
+    query and oracle schedules), the gold answers and a decoder.
+    """
+    from ..tokenizer import ByteTokenizer, load_tokenizer
+    from .feasibility import stratified_indices, tokenize_prompt
+
+    rows = [json.loads(x) for x in Path(path).read_text(encoding="utf-8").splitlines() if x.strip()]
+    order = stratified_indices(rows, sample_count, seed) if sample_count else list(range(len(rows)))
+    if limit is not None:
+        order = order[:limit]
+    if model_dir is not None:
+        tok = load_tokenizer(model_dir, cfg.vocab, max(cfg.n_special, 4), cfg.eos_token_ids)
+    else:
+        tok = ByteTokenizer(cfg.vocab, n_special=max(cfg.n_special, 4),
+                            eos_token_id=cfg.eos_token_ids[0] if cfg.eos_token_ids else 2)
+    reqs, meta = [], []
+    for index in order:
+        row = rows[index]
+        prefix, docs, suffix = tokenize_prompt(tok, row, answer_word_limit)
+        reqs.append(RAGRequest(index, tuple(prefix), tuple(tuple(d.token_ids) for d in docs), tuple(suffix)))
+        meta.append({"question": row["question"], "texts": [d.text for d in docs],
+                     "supporting": [bool(d.supporting) for d in docs],
+                     "golds": [row["answer"], *row.get("answer_aliases", [])],
+                     "decode": lambda ids, _t=tok: _t.decode(ids, skip_special_tokens=True)})
+    return reqs, meta
+
+
+def score_row(row: dict[str, Any], meta: dict, eos_ids) -> None:
+    """Short-answer EM / F1 of every arm's tokens against the row's gold answers (in place)."""
+    from ..metrics import answer_em, answer_f1, clean_short_answer
+
+    row["gold_answers"] = meta["golds"]
+    for arm in row["arms"].values():
+        toks = [t for t in arm["tokens"]]
+        for k, t in enumerate(toks):
+            if t in eos_ids:
+                toks = toks[:k]
+                break
+        ans = clean_short_answer(meta["decode"](toks))
+        arm.update(answer=ans, em=answer_em(ans, meta["golds"]), f1=answer_f1(ans, meta["golds"]))
 
 
 def main(argv=None) -> None:
@@ -272,13 +327,33 @@ def main(argv=None) -> None:
     p.add_argument("--target-average-recompute-ratio", type=float, default=None,
                    help="fail unless the layer-average document ratio is within 0.002 of this")
     p.add_argument("--deviation-metric", default="value", choices=DEVIATION_METRICS)
+    p.add_argument("--dataset", type=Path, default=None,
+                   help="MuSiQue-style JSONL (question, answer, paragraphs) instead of --workload")
+    p.add_argument("--sample-count", type=int, default=None, help="stratified sample size of --dataset")
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--answer-word-limit", type=int, default=5)
+    p.add_argument("--model-dir", type=Path, default=None,
+                   help="model directory (HF Llama / Mistral or this package's) instead of random-init --model")
     p.add_argument("--output", type=Path, required=True)
     a = p.parse_args(argv)
     blend = blend_config_from_args(a)
-    cfg = get_model_config(a.model)
+    if a.model_dir is not None:
+        from ..models.checkpoint import load_oracle
+
+        eng = B200Engine.from_oracle(load_oracle(a.model_dir, dtype=torch.bfloat16), "cuda")
+        cfg, a.model = eng.cfg, str(a.model_dir)
+    else:
+        cfg = get_model_config(a.model)
+        eng = B200Engine.random(cfg, seed=0, device="cuda")
     blend.check_target(cfg.n_layers)  # fail before any work when the target is missed
-    eng = B200Engine.random(cfg, seed=0, device="cuda")
-    reqs = make_requests(a.workload, cfg)[: a.requests + a.warmup]
+    meta: list[dict] = []
+    if a.dataset is not None:
+        reqs, meta = dataset_requests(a.dataset, cfg, model_dir=a.model_dir, sample_count=a.sample_count,
+                                      seed=a.seed, answer_word_limit=a.answer_word_limit,
+                                      limit=a.requests + a.warmup)
+        a.workload = str(a.dataset)
+    else:
+        reqs = make_requests(a.workload, cfg)[: a.requests + a.warmup]
     store = DocumentKVStore(cfg, tier="hbm", device=eng.device)
     server = RAGServer(eng, store, capacity=max(r.prompt_tokens for r in reqs) + a.max_new_tokens + 64,
                        blend=blend)
@@ -295,8 +370,13 @@ def main(argv=None) -> None:
                                          "deviation_metric": blend.deviation_metric,
                                          "max_new_tokens": a.max_new_tokens, "commit_window": 1}}) + "\n")
         for i, r in enumerate(reqs):
-            prep = prepare_request(r, schedule=a.schedule, fractions=fractions, seed=i)
+            m = meta[i] if meta else {}
+            prep = prepare_request(r, schedule=a.schedule, fractions=fractions, seed=i,
+                                   question=m.get("question", ""), texts=m.get("texts"),
+                                   supporting=m.get("supporting"))
             row = evaluate_request(server, prep, max_new_tokens=a.max_new_tokens, draft_tokens=a.draft_tokens)
+            if m:
+                score_row(row, m, server.eos)
             if i >= a.warmup:
                 rows.append(row)
                 f.write(json.dumps(row) + "\n")

@@ -517,3 +517,31 @@ def test_pd_source_aggregation_pairs_arms_and_models_the_link():
         ps.aggregate_source(dense, eagle, bandwidths=(25.0,), kv_bytes_per_token=1)
     with pytest.raises(ValueError, match="different requests"):
         ps.aggregate_source(dense, eagle[:3], bandwidths=(25.0,), kv_bytes_per_token=1)
+
+
+def test_reuse_pipeline_dataset_requests_and_scoring(tmp_path):
+    """MuSiQue rows become prefix / one document per paragraph / question requests with texts and supporting
+    flags for the schedules; arms are scored against the gold answers."""
+    from sparsecache_b200.config import get_model_config
+    from sparsecache_b200.pipelines import reuse
+
+    rows = [{"id": f"q{i}", "question": f"Where is {i}?", "answer": f"place {i}", "answer_aliases": ["p"],
+             "question_decomposition": [{}] * 2,
+             "paragraphs": [{"title": f"T{j}", "paragraph_text": f"text {i} {j}", "is_supporting": j == 1}
+                            for j in range(3)]} for i in range(4)]
+    (tmp_path / "m.jsonl").write_text("".join(json.dumps(r) + "\n" for r in rows))
+    cfg = get_model_config("tiny")
+    reqs, meta = reuse.dataset_requests(tmp_path / "m.jsonl", cfg, sample_count=3, seed=0, limit=2)
+    assert len(reqs) == 2 and len(reqs[0].documents) == 3 and meta[0]["supporting"] == [False, True, False]
+    r, m = reqs[0], meta[0]
+    assert meta[0]["decode"](list(r.documents[1])).endswith(m["texts"][1].split("\n")[-1])
+    prep = reuse.prepare_request(r, schedule="oracle", fractions=(0.34, 1.0), question=m["question"],
+                                 texts=m["texts"], supporting=m["supporting"])
+    assert prep.ranking[0] == 1  # the supporting paragraph first
+    from sparsecache_b200.tokenizer import ByteTokenizer
+
+    tok = ByteTokenizer(cfg.vocab)
+    row = {"arms": {"full": {"tokens": tok.encode("place 7", add_special_tokens=False) + [2, 50]},
+                    "cacheblend": {"tokens": tok.encode("nowhere", add_special_tokens=False)}}}
+    reuse.score_row(row, {**m, "golds": ["place 7"]}, {2})
+    assert row["arms"]["full"]["em"] == 1.0 and row["arms"]["cacheblend"]["f1"] == 0.0
