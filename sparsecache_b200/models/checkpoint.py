@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import json
 from pathlib import Path
+from typing import Any
 
 import torch
 from safetensors.torch import load_file, save_file
@@ -127,3 +128,64 @@ def random_checkpoint(directory: str | Path, preset: str, *, seed: int = 0, std:
     """Write a seeded random-init model directory for ``preset`` (no download)."""
     model = LlamaOracle.random_init(get_model_config(preset), seed=seed, std=std)
     return save_checkpoint(directory, model)
+
+
+def checkpoint_shard(directory: str | Path, rank: int, tp: int, device="cpu"):
+    """Engine weights of tensor-parallel ``rank`` read straight from a model directory.
+
+    Only this rank's rows / columns are read from the safetensors files
+    (column-parallel q/k/v heads and gate/up rows, row-parallel o / down
+    columns; norms, embedding and LM head replicated), so a 70B checkpoint
+    never has to fit one host whole.  The result equals slicing the full
+    engine weights with ``parallel.tp.shard_weights``.
+    """
+    from safetensors import safe_open
+
+    from .engine import EngineWeights, LayerWeights
+    from .weights import GATE_UP_BLOCK, fuse_qkv, interleave_gate_up
+
+    directory = Path(directory)
+    cfg = load_config(directory)
+    if cfg.n_heads % tp or cfg.n_kv_heads % tp or cfg.ffn % (tp * GATE_UP_BLOCK):
+        raise ValueError("heads, kv heads and ffn / 128 must divide by the TP size")
+    index = directory / "model.safetensors.index.json"
+    where = (json.loads(index.read_text(encoding="utf-8"))["weight_map"] if index.exists() else None)
+    handles: dict[str, Any] = {}
+
+    def sl(name: str):
+        if where is not None and name not in where:
+            raise KeyError(name)
+        fname = where[name] if where is not None else "model.safetensors"
+        if fname not in handles:
+            handles[fname] = safe_open(str(directory / fname), framework="pt", device="cpu")
+        if name not in handles[fname].keys():
+            raise KeyError(name)
+        return handles[fname].get_slice(name)
+
+    bf = torch.bfloat16
+    dev = torch.device(device)
+
+    def t(x):
+        return x.to(device=dev, dtype=bf).contiguous()
+
+    D = cfg.head_dim
+    hq, hkv, f = cfg.n_heads // tp, cfg.n_kv_heads // tp, cfg.ffn // tp
+    layers = []
+    for i in range(cfg.n_layers):
+        b = f"model.layers.{i}."
+        q = sl(b + "self_attn.q_proj.weight")[rank * hq * D:(rank + 1) * hq * D]
+        k = sl(b + "self_attn.k_proj.weight")[rank * hkv * D:(rank + 1) * hkv * D]
+        v = sl(b + "self_attn.v_proj.weight")[rank * hkv * D:(rank + 1) * hkv * D]
+        gate = sl(b + "mlp.gate_proj.weight")[rank * f:(rank + 1) * f]
+        up = sl(b + "mlp.up_proj.weight")[rank * f:(rank + 1) * f]
+        layers.append(LayerWeights(
+            ln1=t(sl(b + "input_layernorm.weight")[:]), w_qkv=t(fuse_qkv(q, k, v)),
+            w_o=t(sl(b + "self_attn.o_proj.weight")[:, rank * hq * D:(rank + 1) * hq * D]),
+            ln2=t(sl(b + "post_attention_layernorm.weight")[:]), w_gu=t(interleave_gate_up(gate, up)),
+            w_down=t(sl(b + "mlp.down_proj.weight")[:, rank * f:(rank + 1) * f])))
+    embed = t(sl("model.embed_tokens.weight")[:])
+    try:
+        head = t(sl("lm_head.weight")[:])
+    except KeyError:  # tied embeddings
+        head = embed
+    return cfg, EngineWeights(embed=embed, layers=layers, norm=t(sl("model.norm.weight")[:]), lm_head=head)

@@ -152,22 +152,31 @@ def main(argv=None) -> None:
     p.add_argument("--check-layer", type=int, default=1)
     p.add_argument("--no-spec", action="store_true")
     p.add_argument("--batches", default="8,16", help="batched greedy decode sizes (<= 16 sequences)")
+    p.add_argument("--model-dir", default=None,
+                   help="model directory (HF Llama or this package's): each rank reads only its shard")
     a = p.parse_args(argv)
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
     try:
-        cfg = get_model_config(a.model)
-        if a.layers:
-            cfg = cfg.with_layers(a.layers)
         group = TPGroup()
         tp, rank = group.size, group.rank
+        shard = None
+        if a.model_dir:
+            from ..models.checkpoint import checkpoint_shard
+
+            cfg, shard = checkpoint_shard(a.model_dir, rank, tp, dev)
+        else:
+            cfg = get_model_config(a.model)
+            if a.layers:
+                cfg = cfg.with_layers(a.layers)
         reqs = make_requests(a.workload, cfg)[: a.warmup + a.requests]
         T_max = max(r.prompt_tokens for r in reqs)
         doc_max = max(len(d) for r in reqs for d in r.documents)
         rows = (max(T_max, doc_max) + tp * 128) // tp + 128
-        tpe = TPEngine(cfg, random_shard(cfg, rank, tp, 0, dev), group, max_rows=rows,
+        weights = shard if shard is not None else random_shard(cfg, rank, tp, 0, dev)
+        tpe = TPEngine(cfg, weights, group, max_rows=rows,
                        max_positions=T_max + a.new_tokens + tp * 128 + 1024)
         dcfg = drafter_config_for(cfg)
         drafter = None

@@ -53,3 +53,24 @@ def test_unsupported_families_are_refused():
         config_from_hf({**base, "sliding_window": 16, "max_position_embeddings": 4096})
     with pytest.raises(ValueError, match="rope scaling"):
         config_from_hf({**base, "rope_scaling": {"rope_type": "yarn", "factor": 4.0}})
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_tensor_parallel_shards_read_from_the_checkpoint(tmp_path, tp):
+    """Each rank's shard read with safetensors slices equals slicing the full engine weights."""
+    from sparsecache_b200.models.checkpoint import checkpoint_shard, load_oracle
+    from sparsecache_b200.models.engine import EngineWeights
+    from sparsecache_b200.parallel.tp import shard_weights
+
+    cfg = transformers.LlamaConfig(vocab_size=256, hidden_size=128, intermediate_size=512, num_hidden_layers=2,
+                                   num_attention_heads=4, num_key_value_heads=2, tie_word_embeddings=True)
+    torch.manual_seed(2)
+    transformers.LlamaForCausalLM(cfg).save_pretrained(tmp_path, max_shard_size="100KB")
+    full = EngineWeights.from_oracle(load_oracle(tmp_path), "cpu")
+    for rank in range(tp):
+        mc, got = checkpoint_shard(tmp_path, rank, tp)
+        want = shard_weights(full, mc, rank, tp)
+        assert torch.equal(got.embed, want.embed) and torch.equal(got.lm_head, want.lm_head)
+        for a, b in zip(got.layers, want.layers):
+            for name in ("ln1", "w_qkv", "w_o", "ln2", "w_gu", "w_down"):
+                assert torch.equal(getattr(a, name), getattr(b, name)), name
