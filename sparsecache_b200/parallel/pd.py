@@ -187,6 +187,18 @@ def nccl_decode_request(eng: B200Engine, slot: KVSlot, T: int, max_new: int, pee
     eng.decode(slot, max_new - 1, max_new=max_new)
 
 
+def build_engine(args, dev) -> B200Engine:
+    """The serving engine of a rank: a model directory's weights, else the seeded random-init preset."""
+    if getattr(args, "model_dir", None):
+        from ..models.checkpoint import load_oracle
+
+        return B200Engine.from_oracle(load_oracle(args.model_dir, dtype=torch.bfloat16), dev, max_positions=65536)
+    cfg = get_model_config(args.model)
+    if args.layers:
+        cfg = cfg.with_layers(args.layers)
+    return B200Engine.random(cfg, seed=0, device=dev, max_positions=65536)
+
+
 def run(args) -> dict | None:
     rank, world = dist.get_rank(), dist.get_world_size()
     if world % 2:
@@ -194,11 +206,9 @@ def run(args) -> dict | None:
     pairs = world // 2
     role = "prefill" if rank < pairs else "decode"
     peer = rank + pairs if role == "prefill" else rank - pairs
-    cfg = get_model_config(args.model)
-    if args.layers:
-        cfg = cfg.with_layers(args.layers)
     dev = torch.device("cuda", torch.cuda.current_device())
-    engine = B200Engine.random(cfg, seed=0, device=dev, max_positions=65536)
+    engine = build_engine(args, dev)
+    cfg = engine.cfg
     requests = make_requests("pd_long", cfg)
     mine = [r for r in requests if r.index % pairs == rank % pairs]
     need = args.warmup + args.steps
@@ -324,11 +334,9 @@ def serve_poisson(args) -> dict | None:
     pairs = world // 2
     role = "prefill" if rank < pairs else "decode"
     pair = rank % pairs
-    cfg = get_model_config(args.model)
-    if args.layers:
-        cfg = cfg.with_layers(args.layers)
     dev = torch.device("cuda", torch.cuda.current_device())
-    engine = B200Engine.random(cfg, seed=0, device=dev, max_positions=65536)
+    engine = build_engine(args, dev)
+    cfg = engine.cfg
     mine = [r for r in make_requests("pd_long", cfg) if r.index % pairs == pair]
     n = args.warmup + args.steps
     served = [mine[i % len(mine)] for i in range(n)]
@@ -415,6 +423,7 @@ def main() -> None:
     p = argparse.ArgumentParser(description="Prefill/decode disaggregation with the fused NVLink KV push")
     p.add_argument("--model", default="llama3-8b")
     p.add_argument("--layers", type=int, default=None)
+    p.add_argument("--model-dir", default=None, help="model directory (HF Llama / Mistral or this package's)")
     p.add_argument("--mode", choices=("push", "nccl"), default="push")
     p.add_argument("--steps", type=int, default=4)
     p.add_argument("--warmup", type=int, default=2)
