@@ -277,6 +277,32 @@ def exclusive_gpu_or_exit(*, command_runner=None, max_used_memory_mib: float = 1
     return res
 
 
+def score_pack_row(row: dict[str, Any], meta: dict[str, Any], decode) -> None:
+    """Score the full target's and every chain's timing tokens with the pack's task metric (in place).
+
+    ``meta`` is the request's pack metadata (``dataset``, ``answers``,
+    ``all_classes``); ``decode`` turns token ids into text.
+    """
+    from ..evaluation.longbench import score_prediction
+
+    answers = meta.get("answers") or []
+    dataset = meta.get("dataset", "")
+    if not answers or not dataset:
+        return
+
+    def score(cell: dict) -> None:
+        text = decode(list(cell["timing_token_ids"]))
+        metric, em, value = score_prediction(dataset, text, answers, meta.get("all_classes"))
+        cell.update(answer=text, metric=metric, exact_match=em, score=value)
+
+    for sched in row["schedules"].values():
+        score(sched["full_target"])
+        for chain in sched["chains"].values():
+            score(chain)
+            if chain.get("paired_fixed_control"):
+                score(chain["paired_fixed_control"])
+
+
 def main(argv=None) -> None:
     from ..config import get_model_config
     from ..models.engine import B200Engine
@@ -320,11 +346,21 @@ def main(argv=None) -> None:
     else:
         cfg = get_model_config(a.model)
         eng = B200Engine.random(cfg, seed=0, device="cuda", max_positions=65536)
+    pack_meta, decode = {}, None
     if a.pack is not None:
         packed = requests_from_pack(a.pack, page_tokens=a.context_page_tokens, offset=a.request_offset,
                                     limit=a.requests)
         reqs, flags = [r for r, _ in packed], [f for _, f in packed]
         a.workload = str(a.pack)
+        manifest = json.loads((a.pack / "manifest.json").read_text())
+        lines = (a.pack / "metadata.jsonl").read_text().splitlines()
+        pack_meta = {i: {"dataset": manifest.get("dataset", ""), **json.loads(x)} for i, x in enumerate(lines)
+                     if x.strip()}
+        if a.model_dir is not None:  # the pack's tokenizer ships with the model: score the answers
+            from ..tokenizer import load_tokenizer
+
+            tok = load_tokenizer(a.model_dir, cfg.vocab, max(cfg.n_special, 4), cfg.eos_token_ids)
+            decode = lambda ids: tok.decode(ids, skip_special_tokens=True)  # noqa: E731
     else:
         reqs = make_requests(a.workload, cfg)[a.request_offset:a.request_offset + a.requests]
         flags = [[None] * len(r.documents) for r in reqs]
@@ -393,6 +429,8 @@ def main(argv=None) -> None:
                                                       grow_view=(arm == "chain"))
             row = build_result_row(r.index, r, a.schedule, ranking, sets, out, arms=arms, gamma=gamma, residual=residual,
                                    bytes_per_token=bytes_per_token, prefill_ms=prefill_ms, protocol=protocol)
+            if decode is not None and r.index in pack_meta:
+                score_pack_row(row, pack_meta[r.index], decode)
             rows.append(row)
             f.write(json.dumps(row, default=str) + "\n")
     print(json.dumps(aggregate(rows), indent=2))

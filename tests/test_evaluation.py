@@ -545,3 +545,16 @@ def test_reuse_pipeline_dataset_requests_and_scoring(tmp_path):
                     "cacheblend": {"tokens": tok.encode("nowhere", add_special_tokens=False)}}}
     reuse.score_row(row, {**m, "golds": ["place 7"]}, {2})
     assert row["arms"]["full"]["em"] == 1.0 and row["arms"]["cacheblend"]["f1"] == 0.0
+
+
+def test_pd_rows_scored_with_the_pack_metric():
+    from sparsecache_b200.pipelines.pd import score_pack_row
+
+    row = {"schedules": {"query": {"full_target": {"timing_token_ids": [1, 2]},
+                                   "chains": {"inf": {"timing_token_ids": [3],
+                                                      "paired_fixed_control": {"timing_token_ids": [1, 2]}}}}}}
+    text = {(1, 2): "Paris", (3,): "Rome"}
+    score_pack_row(row, {"dataset": "hotpotqa", "answers": ["Paris"]}, lambda ids: text[tuple(ids)])
+    cell = row["schedules"]["query"]
+    assert cell["full_target"]["score"] == 1.0 and cell["full_target"]["metric"] == "qa_f1"
+    assert cell["chains"]["inf"]["score"] == 0.0 and cell["chains"]["inf"]["paired_fixed_control"]["score"] == 1.0
