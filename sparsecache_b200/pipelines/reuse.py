@@ -304,6 +304,37 @@ def score_row(row: dict[str, Any], meta: dict, eos_ids) -> None:
         arm.update(answer=ans, em=answer_em(ans, meta["golds"]), f1=answer_f1(ans, meta["golds"]))
 
 
+def aggregate_main(argv=None) -> dict[str, Any]:
+    """Aggregate run files (reference: experiments/aggregate_reuse_cacheblend_pipeline.py:46-229).
+
+    Protocol lines are skipped; a request index seen twice across shards is refused.
+    """
+    p = argparse.ArgumentParser(prog="reuse aggregate")
+    p.add_argument("inputs", nargs="+", type=Path)
+    p.add_argument("--output", type=Path, required=True)
+    p.add_argument("--reference-arm", default="full")
+    p.add_argument("--bootstrap-samples", type=int, default=10000)
+    a = p.parse_args(argv)
+    rows, protocols = [], []
+    for path in a.inputs:
+        for line in path.read_text(encoding="utf-8").splitlines():
+            if not line.strip():
+                continue
+            obj = json.loads(line)
+            (protocols if "protocol" in obj else rows).append(obj.get("protocol", obj))
+    if not rows:
+        raise ValueError("no result rows found")
+    idx = [r["request_index"] for r in rows]
+    if len(idx) != len(set(idx)):
+        raise ValueError("duplicate request indices across shards")
+    out = {"protocol": protocols[0] if protocols else None, "source_files": [str(x.resolve()) for x in a.inputs],
+           "summary": aggregate(rows, reference=a.reference_arm, bootstrap_samples=a.bootstrap_samples)}
+    a.output.parent.mkdir(parents=True, exist_ok=True)
+    a.output.write_text(json.dumps(out, indent=2, default=float) + "\n")
+    print(json.dumps(out["summary"], indent=2, default=float))
+    return out
+
+
 def main(argv=None) -> None:
     from ..config import get_model_config
     from ..models.engine import B200Engine
@@ -311,6 +342,12 @@ def main(argv=None) -> None:
     from ..store import DocumentKVStore
     from ..synthetic import make_requests
 
+    import sys
+
+    argv = list(sys.argv[1:] if argv is None else argv)
+    if argv and argv[0] == "aggregate":
+        aggregate_main(argv[1:])
+        return
     p = argparse.ArgumentParser()
     p.add_argument("--model", default="llama3-8b")
     p.add_argument("--workload", default="llama8b_rag")

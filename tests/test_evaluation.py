@@ -558,3 +558,26 @@ def test_pd_rows_scored_with_the_pack_metric():
     cell = row["schedules"]["query"]
     assert cell["full_target"]["score"] == 1.0 and cell["full_target"]["metric"] == "qa_f1"
     assert cell["chains"]["inf"]["score"] == 0.0 and cell["chains"]["inf"]["paired_fixed_control"]["score"] == 1.0
+
+
+def test_reuse_aggregate_command_over_shards(tmp_path):
+    from sparsecache_b200.pipelines import reuse
+
+    def row(i, same):
+        full = [5, 6, 7]
+        return {"request_index": i, "prompt_tokens": 100, "document_tokens": 80,
+                "arms": {"full": {"tokens": full, "ttft_ms": 20.0, "e2e_ms": 50.0, "em": 1.0, "f1": 1.0},
+                         "cacheblend": {"tokens": full if same else [5, 9, 7], "ttft_ms": 8.0, "e2e_ms": 40.0,
+                                        "em": float(same), "f1": float(same)}}}
+
+    (tmp_path / "a.jsonl").write_text(json.dumps({"protocol": {"model": "m"}}) + "\n"
+                                      + "".join(json.dumps(row(i, i % 2 == 0)) + "\n" for i in range(4)))
+    (tmp_path / "b.jsonl").write_text("".join(json.dumps(row(i, True)) + "\n" for i in range(4, 6)))
+    out = reuse.aggregate_main([str(tmp_path / "a.jsonl"), str(tmp_path / "b.jsonl"), "--output",
+                                str(tmp_path / "agg.json"), "--bootstrap-samples", "100"])
+    cb = out["summary"]["arms"]["cacheblend"]
+    assert out["summary"]["requests"] == 6 and out["protocol"] == {"model": "m"}
+    assert abs(cb["token_equal_rate"] - 4 / 6) < 1e-9 and abs(cb["em"] - 4 / 6) < 1e-9
+    assert cb["ttft_gain_vs_reference_ms"]["mean"] == 12.0
+    with pytest.raises(ValueError, match="duplicate"):
+        reuse.aggregate_main([str(tmp_path / "b.jsonl"), str(tmp_path / "b.jsonl"), "--output", str(tmp_path / "x")])
