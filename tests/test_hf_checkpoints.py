@@ -74,3 +74,15 @@ def test_tensor_parallel_shards_read_from_the_checkpoint(tmp_path, tp):
         for a, b in zip(got.layers, want.layers):
             for name in ("ln1", "w_qkv", "w_o", "ln2", "w_gu", "w_down"):
                 assert torch.equal(getattr(a, name), getattr(b, name)), name
+
+
+def test_shard_and_config_errors(tmp_path):
+    from sparsecache_b200.models.checkpoint import checkpoint_shard, save_checkpoint
+    from sparsecache_b200.config import get_model_config
+    from sparsecache_b200.models.llama import LlamaOracle
+
+    save_checkpoint(tmp_path, LlamaOracle.random_init(get_model_config("tiny"), seed=0))
+    with pytest.raises(ValueError, match="divide"):
+        checkpoint_shard(tmp_path, 0, 3)  # 4 heads / 2 kv heads do not split three ways
+    with pytest.raises(ValueError, match="divide"):
+        checkpoint_shard(tmp_path, 0, 2)  # FFN 688 is not a whole number of 128-row gate/up blocks per rank
