@@ -375,14 +375,15 @@ def main(argv=None) -> None:
     a = p.parse_args(argv)
     blend = blend_config_from_args(a)
     if a.model_dir is not None:
-        from ..models.checkpoint import load_oracle
+        from ..models.checkpoint import load_config, load_oracle
 
+        blend.check_target(load_config(a.model_dir).n_layers)  # fail before any work when the target is missed
         eng = B200Engine.from_oracle(load_oracle(a.model_dir, dtype=torch.bfloat16), "cuda")
         cfg, a.model = eng.cfg, str(a.model_dir)
     else:
         cfg = get_model_config(a.model)
+        blend.check_target(cfg.n_layers)
         eng = B200Engine.random(cfg, seed=0, device="cuda")
-    blend.check_target(cfg.n_layers)  # fail before any work when the target is missed
     meta: list[dict] = []
     if a.dataset is not None:
         reqs, meta = dataset_requests(a.dataset, cfg, model_dir=a.model_dir, sample_count=a.sample_count,
