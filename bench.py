@@ -30,7 +30,6 @@ from datetime import timedelta
 import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-PUBLISHED_CB15_TTFT_MS = 76.9  # reference README: CacheBlend 15%, 1x H200 (no tokens/s is published)
 METRIC = "p50/p99 TTFT and decode tokens/s, 8B/70B 10-doc RAG reuse, 1/2/4/8 B200"
 
 
@@ -190,6 +189,21 @@ def run_ours(args, world, rank, local):
     tokens = reduce_sum(my_tokens, world)
     value = tokens / (max_ms / 1000.0)
 
+    # ---------------- TTFT against full prefill and ratio 1.0 ----------------
+    # Same requests, same server; only the first token is needed, so these
+    # calls generate one token (TTFT is the event pair around the prefill).
+    gate = CacheBlendConfig(check_layer=1, recompute_ratio=1.0, deviation_metric="value", keep_prefix=True,
+                            max_new_tokens=1)
+    ttft_modes = {}
+    for name, kw in (("full_prefill", {"mode": "full"}), ("cacheblend_r1.0", {"blend": gate})):
+        for r in served[: args.warmup]:
+            server.serve(r, max_new_tokens=1, sync=True, **kw)
+        barrier(world)
+        vals = [server.serve(r, max_new_tokens=1, sync=True, **kw).ttft_ms for r in served[args.warmup:]]
+        vals = gather_list(vals, world)
+        ttft_modes[name] = {"p50_ms": percentile(vals, 0.5), "p99_ms": percentile(vals, 0.99)}
+    ttft_modes[f"cacheblend_r{args.ratio}"] = {"p50_ms": percentile(ttfts, 0.5), "p99_ms": percentile(ttfts, 0.99)}
+
     # ---------------- end-to-end through the public API ----------------
     # Documents served from the PINNED host tier (composer reads them over
     # PCIe), prompt ids copied H2D from pinned memory and the generated ids
@@ -233,7 +247,7 @@ def run_ours(args, world, rank, local):
         "ttft_p99_ms": percentile(ttfts, 0.99),
         "response_p50_ms": percentile(resp, 0.5),
         "tpot_ms": statistics.mean((r - t) / (args.new_tokens - 1) for r, t in zip(resp, ttfts)),
-        "ttft_vs_published_h200_cb15": PUBLISHED_CB15_TTFT_MS / percentile(ttfts, 0.5),
+        "ttft_by_mode": ttft_modes,
         "e2e": {"value": e2e_value, "unit": "generated tokens/s (all GPUs)",
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4 * args.new_tokens,
                 "ttft_p50_ms": percentile(e2e_ttft, 0.5), "ttft_p99_ms": percentile(e2e_ttft, 0.99),
@@ -275,16 +289,41 @@ def _install_cache_shims():
         DynamicCache.to_legacy_cache = lambda self: tuple((l.keys, l.values) for l in self.layers)
 
 
-def run_reference(args, world, rank, local):
+def _find_reference() -> tuple[str | None, str]:
+    """Directory that holds the installed reference package ``sparsecache``.
+
+    ``pip install --target baseline/_ref`` puts it at baseline/_ref/sparsecache;
+    a source copy keeps it at baseline/_ref/src/sparsecache.  Returns
+    (directory or None, reason when not found)."""
     ref_root = os.path.join(ROOT, "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref_root, "sparsecache")):
-        return {"impl": "reference", "unavailable": "baseline/_ref is not installed"}
-    sys.path.insert(0, ref_root)
+    if not os.path.isdir(ref_root):
+        return None, "baseline/_ref is not installed (pip install --target baseline/_ref of the reference tree)"
+    for cand in (ref_root, os.path.join(ref_root, "src")):
+        if os.path.isfile(os.path.join(cand, "sparsecache", "modeling.py")):
+            return cand, ""
+    return None, "baseline/_ref exists but holds no sparsecache/modeling.py (nor src/sparsecache/modeling.py)"
+
+
+def run_reference(args, world, rank, local):
+    """The unmodified reference through its public API (``sparsecache.modeling``).
+
+    Model: HF ``LlamaForCausalLM`` (sdpa) of the Llama-3.1-8B geometry with
+    random bf16 weights, one per GPU.  Each request's prefix cache is built the
+    reference's way: every document prefilled alone at positions 0.., its keys
+    moved to the request's positions with ``sparsecache.rope.relocate_key``,
+    the system prefix prefilled alone, all concatenated per layer; the caches
+    live in pinned host memory and the stock ``cacheblend_generate`` copies
+    them to the GPU inside each call (its own H2D, timed as part of its TTFT).
+    """
+    ref_dir, why = _find_reference()
+    if ref_dir is None:
+        return {"impl": "reference", "unavailable": why}
+    sys.path.insert(0, ref_dir)
     sys.path.insert(1, ROOT)
     _install_cache_shims()
     from transformers import LlamaConfig, LlamaForCausalLM
 
-    from sparsecache.modeling import cacheblend_generate  # the reference's public API
+    from sparsecache.modeling import baseline_generate, cacheblend_generate  # the reference's public API
     from sparsecache.rope import relocate_key
     from sparsecache_b200.config import get_model_config
     from sparsecache_b200.synthetic import make_requests, workload_summary
@@ -329,14 +368,17 @@ def run_reference(args, world, rank, local):
                 keys[i].append(relocate_key(model, k, source_start=0, target_start=cursor))
                 values[i].append(v)
             cursor += len(d)
-        prefix_caches.append(tuple((torch.cat(keys[i], 2), torch.cat(values[i], 2)) for i in range(cfg.n_layers)))
+        prefix_caches.append(tuple((torch.cat(keys[i], 2).pin_memory(), torch.cat(values[i], 2).pin_memory())
+                                   for i in range(cfg.n_layers)))
+    doc_cache.clear()
     eos = set(cfg.eos_token_ids)
 
-    def call(r, pc):
+    def call(r, pc, ratio=args.ratio, new_tokens=args.new_tokens):
         return cacheblend_generate(model, full_ids=r.prompt, prefix_cache=pc, system_tokens=len(r.prefix),
-                                   suffix_tokens=len(r.suffix), check_layer=1, recompute_ratio=args.ratio,
-                                   max_new_tokens=args.new_tokens, eos_token_ids=eos)
+                                   suffix_tokens=len(r.suffix), check_layer=1, recompute_ratio=ratio,
+                                   max_new_tokens=new_tokens, eos_token_ids=eos)
 
+    timed = list(zip(served[args.warmup:], prefix_caches[args.warmup:]))
     for r, pc in zip(served[: args.warmup], prefix_caches):
         call(r, pc)
     sampler = ClockSampler(local)
@@ -346,7 +388,7 @@ def run_reference(args, world, rank, local):
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
-    results = [call(r, pc) for r, pc in zip(served[args.warmup:], prefix_caches[args.warmup:])]
+    results = [call(r, pc) for r, pc in timed]
     t1.record()
     torch.cuda.synchronize()
     barrier(world)
@@ -357,8 +399,37 @@ def run_reference(args, world, rank, local):
     max_ms = reduce_max(elapsed_ms, world)
     tokens = reduce_sum(my_tokens, world)
     value = tokens / (max_ms / 1000.0)
+
+    # TTFT of full prefill (stock baseline_generate) and of the ratio-1.0 gate
+    ttft_modes = {f"cacheblend_r{args.ratio}": {"p50_ms": percentile(ttfts, 0.5), "p99_ms": percentile(ttfts, 0.99)}}
+    for name in ("full_prefill", "cacheblend_r1.0"):
+        def one(r, pc):
+            if name == "full_prefill":
+                x = baseline_generate(model, full_ids=r.prompt, max_new_tokens=1, eos_token_ids=eos)
+            else:
+                x = call(r, pc, ratio=1.0, new_tokens=1)
+            return x.prefill_ms + x.metadata.get("prefix_h2d_ms", 0.0)
+
+        for r, pc in zip(served[: args.warmup], prefix_caches):
+            one(r, pc)
+        barrier(world)
+        vals = gather_list([one(r, pc) for r, pc in timed], world)
+        ttft_modes[name] = {"p50_ms": percentile(vals, 0.5), "p99_ms": percentile(vals, 0.99)}
+
+    # End to end: host wall clock around each public call (prompt ids H2D and
+    # the pinned prefix cache H2D happen inside it; every token is read back
+    # to the host by its greedy loop).
+    barrier(world)
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    e2e_results = [call(r, pc) for r, pc in timed]
+    torch.cuda.synchronize()
+    e2e_s = reduce_max(time.perf_counter() - w0, world)
+    e2e_value = reduce_sum(sum(len(x.token_ids) for x in e2e_results), world) / e2e_s
+    e2e_ttft = gather_list([x.prefill_ms + x.metadata.get("prefix_h2d_ms", 0.0) for x in e2e_results], world)
+
     summary = workload_summary(requests)
-    h2d = statistics.mean(sum((k.numel() + v.numel()) * 2 for k, v in pc) for pc in prefix_caches[args.warmup:])
+    h2d = statistics.mean(sum((k.numel() + v.numel()) * 2 for k, v in pc) + 8 * len(r.prompt) for r, pc in timed)
     return {
         "impl": "reference",
         "metric": METRIC,
@@ -375,14 +446,20 @@ def run_reference(args, world, rank, local):
         "data": "synthetic (seeded token ids; random-init weights)",
         "ttft_p50_ms": percentile(ttfts, 0.5),
         "ttft_p99_ms": percentile(ttfts, 0.99),
-        "e2e": {"value": value, "unit": "generated tokens/s (all GPUs)", "h2d_bytes_per_step": int(h2d),
+        "tpot_ms": statistics.mean(x.decode_ms / max(1, len(x.token_ids) - 1) for x in results),
+        "ttft_by_mode": ttft_modes,
+        "e2e": {"value": e2e_value, "unit": "generated tokens/s (all GPUs)", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": 8 * args.new_tokens,
-                "note": "the reference API call is end to end (pageable H2D of the composed cache inside)"},
+                "ttft_p50_ms": percentile(e2e_ttft, 0.5), "ttft_p99_ms": percentile(e2e_ttft, 0.99),
+                "timing": "host wall clock around each cacheblend_generate call",
+                "store_tier": "pinned host (the reference copies the composed prefix cache H2D per call)"},
         "gpu_launches": None,
         "clocks": clocks,
         "config": {"model": f"{args.model} (random init, HF LlamaForCausalLM sdpa)", "global_batch": world,
                    "seq_len": round(summary["mean_prompt_tokens"]), "parallelism": f"dp{world}",
-                   "api": "sparsecache.modeling.cacheblend_generate (key deviation, suffix mandatory)",
+                   "api": "sparsecache.modeling.cacheblend_generate / baseline_generate "
+                          "(key deviation, suffix mandatory)",
+                   "reference_dir": os.path.relpath(ref_dir, ROOT),
                    "ratio": args.ratio, "check_layer": 1, "new_tokens": args.new_tokens,
                    "l2": "inputs larger than L2: every step streams the 16 GB of weights"},
     }

@@ -14,6 +14,8 @@
 #include <stdint.h>
 #include <stdlib.h>
 
+#include <mutex>
+
 namespace sc {
 
 // ----------------------------------------------------------------------------
@@ -346,6 +348,10 @@ inline void ensure_smem_attr(F* func, int bytes) {
   struct Entry { const void* fn; int dev; int bytes; };
   static Entry table[256];
   static int used = 0;
+  // host threads may launch concurrently (one per device, or a plugin's
+  // worker threads): the table is shared, so look-up and insert are locked
+  static std::mutex lock;
+  std::lock_guard<std::mutex> guard(lock);
   int dev = 0;
   cudaGetDevice(&dev);
   const void* key = reinterpret_cast<const void*>(func);

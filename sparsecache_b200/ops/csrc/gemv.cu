@@ -449,6 +449,7 @@ static __device__ __align__(256) NoAllocScratch g_noalloc_scratch;
 // code the symbol itself is only a host-side stand-in, never a device
 // address, so it is never passed to a kernel directly.
 NoAllocScratch* g_noalloc_ptr[64] = {nullptr};
+std::mutex g_noalloc_setup_lock;
 
 }  // namespace
 }  // namespace sc
@@ -461,6 +462,9 @@ extern "C" __attribute__((visibility("default"))) const char* sc_noalloc_error_s
     case SC_NOALLOC_ETOOLARGE: return "launch grid * M exceeds the fixed scratch (16384 partials)";
     case SC_NOALLOC_ESYMBOL: return "cudaGetSymbolAddress of the scratch array failed";
     case SC_NOALLOC_ELAUNCH: return "memset of the counter or kernel launch failed";
+    case SC_NOALLOC_EBADPOINTER:
+      return "x, w, norm_w must be 16-byte aligned device pointers (x, w non-NULL); out_token non-NULL, "
+             "4-byte aligned";
   }
   return "unknown error code";
 }
@@ -472,16 +476,28 @@ extern "C" __attribute__((visibility("default"))) int sc_lm_head_argmax_noalloc(
   if (M < 1 || M > SC_NOALLOC_MAX_ROWS || K < 8 || (K % 8) != 0 || N < 2 || (N % 2) != 0 ||
       (size_t)M * K * 2 > 200 * 1024)
     return SC_NOALLOC_EBADSHAPE;
+  // the kernel reads x, w and norm_w with 16-byte loads and writes int32 tokens
+  if (x == nullptr || w == nullptr || out_token == nullptr ||
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+        reinterpret_cast<uintptr_t>(norm_w)) & 15u) != 0 ||
+      (reinterpret_cast<uintptr_t>(out_token) & 3u) != 0)
+    return SC_NOALLOC_EBADPOINTER;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SC_NOALLOC_ESYMBOL;
-  // Set-up on the first call on this device (the device is current here).
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
-      return SC_NOALLOC_ESYMBOL;
-    g_noalloc_ptr[dev] = reinterpret_cast<NoAllocScratch*>(p);
+  // Set-up on the first call on this device (the device is current here),
+  // under a lock so that concurrent first calls from several host threads
+  // look the address up once.
+  NoAllocScratch* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> guard(g_noalloc_setup_lock);
+    if (g_noalloc_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
+        return SC_NOALLOC_ESYMBOL;
+      g_noalloc_ptr[dev] = reinterpret_cast<NoAllocScratch*>(p);
+    }
+    scratch = g_noalloc_ptr[dev];
   }
-  NoAllocScratch* scratch = g_noalloc_ptr[dev];
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
     sms = 148;

@@ -19,13 +19,22 @@
 //     norm_w [K] bf16 or NULL (then x is used without RMSNorm), eps.
 //     Output: out_token [M] int32 (device memory), the index of the largest
 //     bf16-rounded logit of each row, lowest index on ties.
+//   * Pointers: x, w and norm_w (when given) must be 16-byte aligned device
+//     addresses (the kernel reads them with 16-byte vector loads; a row-major
+//     view that starts at a multiple of 8 elements of an aligned buffer
+//     qualifies); out_token must be a non-NULL, 4-byte aligned device
+//     address.  A NULL or misaligned pointer returns SC_NOALLOC_EBADPOINTER
+//     before anything is launched.
 //   * Limits: 1 <= M <= SC_NOALLOC_MAX_ROWS, K a multiple of 8, N even,
 //     M * K * 2 <= 200 KiB (x is staged in shared memory), and the launch
 //     grid (<= 8 CTAs per SM) times M must fit SC_NOALLOC_MAX_PARTIALS.
 //     Violations return a non-zero code before anything is launched.
 //   * Set-up: the first call on a device (with that device current) looks up
 //     the device address of the scratch array with cudaGetSymbolAddress; do
-//     this first call before any CUDA stream capture.
+//     this first call before any CUDA stream capture.  The set-up runs once
+//     per device under a lock, so host threads may make their first calls at
+//     the same time; it is the GPU-side scratch, not the host state, that
+//     concurrent calls share (see below).
 //   * The scratch array is shared by every call on a device and keeps the
 //     last call's contents; the completion counter is cleared (memset on
 //     `stream`) at the start of every call.  Calls that overlap on the GPU
@@ -56,6 +65,7 @@ const char* sc_noalloc_error_string(int code);
 #define SC_NOALLOC_ETOOLARGE 2      // grid * M exceeds SC_NOALLOC_MAX_PARTIALS
 #define SC_NOALLOC_ESYMBOL 3        // cudaGetSymbolAddress failed
 #define SC_NOALLOC_ELAUNCH 4        // memset or kernel launch failed
+#define SC_NOALLOC_EBADPOINTER 5    // NULL or misaligned x / w / norm_w / out_token
 
 #ifdef __cplusplus
 }

@@ -97,12 +97,17 @@ class RAGServer:
         ids_host: torch.Tensor | None = None,
         store: DocumentKVStore | None = None,
         max_new_tokens: int | None = None,
+        blend: CacheBlendConfig | None = None,
         sync: bool = False,
     ) -> ServeHandle | ServeResult:
-        """Serve one request.  ``ids_host`` (pinned int32) is copied H2D inside the timed region."""
+        """Serve one request.  ``ids_host`` (pinned int32) is copied H2D inside the timed region.
+
+        ``blend`` overrides the server's CacheBlend parameters for this call
+        (e.g. recompute ratio 1.0 as the correctness gate against full prefill).
+        """
         eng = self.engine
         store = store or self.store
-        blend = self.blend
+        blend = blend or self.blend
         max_new = max_new_tokens or blend.max_new_tokens
         T = request.prompt_tokens
         if T + max_new > self.slot.capacity:

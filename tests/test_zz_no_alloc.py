@@ -62,6 +62,37 @@ def test_noalloc_entry_point_matches_regular(cuda_device):
         assert torch.equal(got, expect), (got.tolist(), expect.tolist())
 
 
+def test_noalloc_without_norm_and_ties(cuda_device):
+    """norm_w = NULL uses x as given; tied logits resolve to the lowest row index."""
+    fn, err = _symbol()
+    stream = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator(device="cpu").manual_seed(7)
+    M, N, K = 4, 4096, 512
+    x = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.05).to(cuda_device, torch.bfloat16)
+    for call in range(2):
+        expect = _regular(x, w, None, 1e-5)
+        got = torch.full((M,), -1, device=cuda_device, dtype=torch.int32)
+        rc = fn(x.data_ptr(), w.data_ptr(), None, 1e-5, M, N, K, got.data_ptr(), stream)
+        assert rc == 0, err(rc).decode()
+        torch.cuda.synchronize()
+        assert torch.equal(got, expect), (call, got.tolist(), expect.tolist())
+    # rows 17, 900 and 3000 become copies of row 0's winning row: their
+    # logits tie exactly, and the lowest index of the tied rows must win
+    w2 = w.clone()
+    logits = (x.float() @ w2.float().t())
+    best = int(logits[0].argmax())
+    for j in (17, 900, 3000):
+        w2[j] = w2[best]
+    got = torch.full((M,), -1, device=cuda_device, dtype=torch.int32)
+    rc = fn(x.data_ptr(), w2.data_ptr(), None, 1e-5, M, N, K, got.data_ptr(), stream)
+    assert rc == 0, err(rc).decode()
+    torch.cuda.synchronize()
+    expect = _regular(x, w2, None, 1e-5)
+    assert torch.equal(got, expect)
+    assert int(got[0]) == min(17, best)
+
+
 def test_noalloc_rejects_oversized_calls(cuda_device):
     fn, err = _symbol()
     stream = torch.cuda.current_stream().cuda_stream
@@ -72,3 +103,9 @@ def test_noalloc_rejects_oversized_calls(cuda_device):
     assert rc == 1 and b"M <= 8" in err(rc)
     rc = fn(x.data_ptr(), w.data_ptr(), None, 1e-5, 1, 64, 60, out.data_ptr(), stream)
     assert rc == 1
+    # misaligned x (a view starting 1 element into the buffer) and NULL x
+    xa = torch.zeros(2, 72, device=cuda_device, dtype=torch.bfloat16)
+    rc = fn(xa.data_ptr() + 2, w.data_ptr(), None, 1e-5, 1, 64, 64, out.data_ptr(), stream)
+    assert rc == 5 and b"16-byte aligned" in err(rc)
+    rc = fn(None, w.data_ptr(), None, 1e-5, 1, 64, 64, out.data_ptr(), stream)
+    assert rc == 5
