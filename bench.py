@@ -165,6 +165,11 @@ def run_ours(args, world, rank, local):
     # ---------------- device-timed region ----------------
     for r in served[: args.warmup]:
         server.serve(r, sync=True)
+    # one untimed call per timed request as well (both arms do this): every
+    # request shape has been seen once, so neither arm's allocator or
+    # autotuner state is measured, only its steady-state serving path
+    for r in served[args.warmup:]:
+        server.serve(r, sync=True)
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
     barrier(world)
@@ -265,6 +270,7 @@ def run_ours(args, world, rank, local):
             "store_tier": "hbm",
             "producer": prod,
             "l2": "inputs larger than L2: every step streams the 16 GB of weights",
+            "warm_pass": "every timed request served once untimed before the timed region",
         },
     }
     return out
@@ -381,6 +387,11 @@ def run_reference(args, world, rank, local):
     timed = list(zip(served[args.warmup:], prefix_caches[args.warmup:]))
     for r, pc in zip(served[: args.warmup], prefix_caches):
         call(r, pc)
+    # one untimed call per timed request (as in our arm): the first call of a
+    # new prompt length makes the CUDA caching allocator grow, which costs the
+    # HF path up to a second per call and is not its steady state
+    for r, pc in timed:
+        call(r, pc)
     sampler = ClockSampler(local)
     barrier(world)
     torch.cuda.synchronize()
@@ -461,7 +472,8 @@ def run_reference(args, world, rank, local):
                           "(key deviation, suffix mandatory)",
                    "reference_dir": os.path.relpath(ref_dir, ROOT),
                    "ratio": args.ratio, "check_layer": 1, "new_tokens": args.new_tokens,
-                   "l2": "inputs larger than L2: every step streams the 16 GB of weights"},
+                   "l2": "inputs larger than L2: every step streams the 16 GB of weights",
+                   "warm_pass": "every timed request served once untimed before the timed region"},
     }
 
 

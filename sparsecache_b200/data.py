@@ -1,21 +1,29 @@
-"""Dataset adapters and the ``sparsecache-prepare`` CLI.
+"""Dataset readers and the ``sparsecache-prepare`` command.
 
-Normalises one QA record into a ``QACase`` with an ordered list of
-independently reusable document chunks (reference src/sparsecache/data.py):
-  * HotpotQA-E / LongBench JSONL: the ``context`` field is split on lines of
-    the form ``Passage N:``; the first line of a passage is its title;
-  * official MuSiQue JSONL: ``paragraphs`` with ``idx``, ``title``,
-    ``paragraph_text`` and ``is_supporting``; gold answers are ``answer`` plus
-    ``answer_aliases``.
+A prepared case is one question with its gold answers and an ordered list of
+document chunks, each of which is prefilled and cached on its own.  Two
+source formats are read (behaviour of the reference's
+src/sparsecache/data.py, whose prepared-case JSON and chunk ids this module
+keeps so that caches and manifests stay interchangeable):
+
+* passage-context rows (HotpotQA-E / LongBench JSONL): the ``context``
+  string holds ``Passage N:`` header lines; each header opens a passage
+  whose first line is its title and whose remaining lines are its text;
+  chunk ids are ``passage-01`` ...;
+* MuSiQue rows: a ``paragraphs`` list with ``idx``, ``title``,
+  ``paragraph_text`` and ``is_supporting``; gold answers are ``answer``
+  followed by the ``answer_aliases`` not already listed; chunk ids are
+  ``paragraph-<idx>``.
 """
 from __future__ import annotations
 
 import argparse
+import itertools
 import json
 import re
 from dataclasses import asdict, dataclass
 from pathlib import Path
-from typing import Any
+from typing import Any, Callable, Iterator
 
 
 @dataclass(frozen=True)
@@ -35,83 +43,131 @@ class QACase:
     chunks: tuple[DocumentChunk, ...]
 
     def as_dict(self) -> dict[str, Any]:
-        out = asdict(self)
-        out["answers"] = list(self.answers)
-        out["chunks"] = [asdict(c) for c in self.chunks]
-        return out
+        """The prepared-case JSON object (lists, not tuples)."""
+        return {"case_id": self.case_id, "source": self.source, "question": self.question,
+                "answers": list(self.answers), "chunks": [asdict(c) for c in self.chunks]}
+
+    @classmethod
+    def from_dict(cls, obj: dict[str, Any]) -> "QACase":
+        return cls(case_id=str(obj["case_id"]), source=str(obj["source"]), question=str(obj["question"]),
+                   answers=tuple(map(str, obj["answers"])),
+                   chunks=tuple(DocumentChunk(**c) for c in obj["chunks"]))
 
 
 def load_prepared_case(path: str | Path) -> QACase:
-    row = json.loads(Path(path).read_text(encoding="utf-8"))
-    return QACase(
-        case_id=str(row["case_id"]),
-        source=str(row["source"]),
-        question=str(row["question"]),
-        answers=tuple(str(a) for a in row["answers"]),
-        chunks=tuple(DocumentChunk(**c) for c in row["chunks"]),
-    )
+    return QACase.from_dict(json.loads(Path(path).read_text(encoding="utf-8")))
 
 
-def _jsonl_row(path: str | Path, index: int) -> dict[str, Any]:
-    with Path(path).open(encoding="utf-8") as handle:
-        for i, line in enumerate(handle):
-            if i == index:
-                return json.loads(line)
-    raise ValueError(f"dataset does not contain row {index}")
+def read_jsonl_row(path: str | Path, index: int) -> dict[str, Any]:
+    """Row ``index`` (0-based) of a JSONL file, reading no further than it."""
+    with Path(path).open(encoding="utf-8") as lines:
+        hit = next(itertools.islice(lines, index, None), None)
+    if hit is None:
+        raise ValueError(f"dataset does not contain row {index}")
+    return json.loads(hit)
 
 
-_PASSAGE = re.compile(r"(?=^Passage \d+:\n)", flags=re.M)
+_HEADER = re.compile(r"Passage \d+:")
 
 
 def split_passages(context: str) -> list[str]:
-    parts = [p for p in _PASSAGE.split(context.strip()) if p.strip()]
-    return parts or [context]
+    """Cut a passage-context string into passages.
+
+    A line ``Passage N:`` that is followed by another line starts a new
+    passage (the header stays at the head of its passage); text before the
+    first header is a passage of its own; with no non-blank passage at all the
+    whole context is returned as one.
+    """
+    lines = context.strip().split("\n")
+    groups: list[list[str]] = [[]]
+    for pos, line in enumerate(lines):
+        if _HEADER.fullmatch(line) and pos + 1 < len(lines) and groups[-1]:
+            groups.append([])
+        groups[-1].append(line)
+    passages = ["\n".join(g) for g in groups]
+    kept = [p for p in passages if p.strip()]
+    return kept or [context]
 
 
-def load_hotpotqa_case(path: str | Path, *, index: int, max_chunks: int) -> QACase:
-    row = _jsonl_row(path, index)
-    chunks = []
-    for i, passage in enumerate(split_passages(str(row["context"]))[:max_chunks]):
-        lines = passage.strip().splitlines()
-        if lines and re.fullmatch(r"Passage \d+:", lines[0]):
-            lines = lines[1:]
-        title = lines[0].strip() if lines else f"Passage {i + 1}"
+def passage_chunk(position: int, passage: str) -> DocumentChunk:
+    """Chunk ``position`` (1-based) from one passage: header dropped, first line the title."""
+    lines = passage.strip().splitlines()
+    if lines and _HEADER.fullmatch(lines[0]):
+        lines = lines[1:]
+    if not lines:
+        title, text = f"Passage {position}", f"Passage {position}"
+    else:
+        title = lines[0].strip()
         text = "\n".join(lines[1:]).strip() if len(lines) > 1 else title
-        chunks.append(DocumentChunk(chunk_id=f"passage-{i + 1:02d}", title=title, text=text))
+    return DocumentChunk(chunk_id=f"passage-{position:02d}", title=title, text=text)
+
+
+def _passage_rows(row: dict[str, Any], index: int, max_chunks: int) -> QACase:
+    parts = split_passages(str(row["context"]))[:max_chunks]
     return QACase(
         case_id=str(row.get("_id", index)),
         source=str(row.get("dataset", "hotpotqa")),
         question=str(row["input"]),
-        answers=tuple(str(a) for a in row.get("answers", [])),
-        chunks=tuple(chunks),
+        answers=tuple(map(str, row.get("answers", []))),
+        chunks=tuple(passage_chunk(k, part) for k, part in enumerate(parts, 1)),
     )
 
 
-def load_musique_case(path: str | Path, *, index: int, max_chunks: int) -> QACase:
-    row = _jsonl_row(path, index)
-    chunks = tuple(
-        DocumentChunk(
-            chunk_id=f"paragraph-{int(p['idx']):02d}",
-            title=str(p["title"]),
-            text=str(p["paragraph_text"]),
-            supporting=bool(p.get("is_supporting", False)),
-        )
-        for p in row["paragraphs"][:max_chunks]
-    )
-    answers: list[str] = [str(row["answer"])] if row.get("answer") else []
-    answers.extend(str(a) for a in row.get("answer_aliases", []) if a not in answers)
+def _musique_answers(row: dict[str, Any]) -> tuple[str, ...]:
+    ordered: dict[str, None] = {}
+    if row.get("answer"):
+        ordered[str(row["answer"])] = None
+    for alias in row.get("answer_aliases", []):
+        ordered.setdefault(str(alias), None)
+    return tuple(ordered)
+
+
+def _musique_rows(row: dict[str, Any], index: int, max_chunks: int) -> QACase:
+    paragraphs = row["paragraphs"][:max_chunks]
     return QACase(
         case_id=str(row.get("id", index)),
         source="musique",
         question=str(row["question"]),
-        answers=tuple(answers),
-        chunks=chunks,
+        answers=_musique_answers(row),
+        chunks=tuple(DocumentChunk(chunk_id=f"paragraph-{int(p['idx']):02d}", title=str(p["title"]),
+                                   text=str(p["paragraph_text"]), supporting=bool(p.get("is_supporting", False)))
+                     for p in paragraphs),
     )
 
 
+# dataset name -> reader of one parsed JSONL row
+READERS: dict[str, Callable[[dict[str, Any], int, int], QACase]] = {
+    "hotpotqa": _passage_rows,
+    "musique": _musique_rows,
+}
+
+
+def load_case(dataset: str, path: str | Path, *, index: int, max_chunks: int) -> QACase:
+    if dataset not in READERS:
+        raise ValueError(f"unknown dataset {dataset!r}; known: {sorted(READERS)}")
+    return READERS[dataset](read_jsonl_row(path, index), index, max_chunks)
+
+
+def load_hotpotqa_case(path: str | Path, *, index: int, max_chunks: int) -> QACase:
+    return load_case("hotpotqa", path, index=index, max_chunks=max_chunks)
+
+
+def load_musique_case(path: str | Path, *, index: int, max_chunks: int) -> QACase:
+    return load_case("musique", path, index=index, max_chunks=max_chunks)
+
+
+def iter_cases(dataset: str, path: str | Path, *, max_chunks: int, start: int = 0,
+               count: int | None = None) -> Iterator[QACase]:
+    """Cases of a JSONL file in order (for batch preparation), one row per case."""
+    with Path(path).open(encoding="utf-8") as lines:
+        rows = itertools.islice(lines, start, None if count is None else start + count)
+        for offset, line in enumerate(rows):
+            yield READERS[dataset](json.loads(line), start + offset, max_chunks)
+
+
 def main(argv: list[str] | None = None) -> None:
-    parser = argparse.ArgumentParser(description="Prepare one normalised ten-chunk QA case")
-    parser.add_argument("--dataset", choices=("hotpotqa", "musique"), required=True)
+    parser = argparse.ArgumentParser(description="Prepare one normalised multi-chunk QA case")
+    parser.add_argument("--dataset", choices=tuple(READERS), required=True)
     parser.add_argument("--input", required=True)
     parser.add_argument("--output", required=True)
     parser.add_argument("--index", type=int, default=0)
@@ -119,15 +175,14 @@ def main(argv: list[str] | None = None) -> None:
     args = parser.parse_args(argv)
     if args.index < 0 or args.max_chunks < 1:
         parser.error("index must be non-negative and max-chunks positive")
-    loader = load_hotpotqa_case if args.dataset == "hotpotqa" else load_musique_case
-    case = loader(args.input, index=args.index, max_chunks=args.max_chunks)
+    case = load_case(args.dataset, args.input, index=args.index, max_chunks=args.max_chunks)
     if len(case.chunks) != args.max_chunks:
         raise ValueError(f"requested {args.max_chunks} chunks but case contains {len(case.chunks)}")
-    out = Path(args.output)
-    out.parent.mkdir(parents=True, exist_ok=True)
-    out.write_text(json.dumps(case.as_dict(), ensure_ascii=False, indent=2) + "\n", encoding="utf-8")
-    print(json.dumps({"event": "prepared", "output": str(out), "case_id": case.case_id,
-                      "chunks": len(case.chunks)}, ensure_ascii=False))
+    target = Path(args.output)
+    target.parent.mkdir(parents=True, exist_ok=True)
+    target.write_text(json.dumps(case.as_dict(), ensure_ascii=False, indent=2) + "\n", encoding="utf-8")
+    event = {"event": "prepared", "output": str(target), "case_id": case.case_id, "chunks": len(case.chunks)}
+    print(json.dumps(event, ensure_ascii=False))
 
 
 if __name__ == "__main__":

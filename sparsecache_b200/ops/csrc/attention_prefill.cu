@@ -1,23 +1,46 @@
-// Flash attention over a paged layer cache with per-row position vectors.
+// Flash attention over a layer cache with per-row position vectors, on the
+// 5th-generation tensor cores (tcgen05.mma, accumulators in TMEM, K/V tiles
+// by TMA).
 //
 //   out[r, h, :] = softmax_j( q[r,h,:] . k[j,kvh(h),:] * scale | kpos[j] <= qpos[r] ) v[j,kvh,:]
 //
 // One kernel covers both prefill flavours of the reference:
 //   * full causal prefill (qpos = kpos = arange) - HF SDPA is_causal=True
-//     (modeling.py:196-206, reuse_cacheblend_pipeline.py:557-567)
+//     (src/sparsecache/modeling.py:196-206, reuse_cacheblend_pipeline.py:557-567)
 //   * CacheBlend selective recompute: the query rows are an arbitrary sorted
 //     subset of positions and the keys are the whole composed cache; the
 //     reference materialises a dense [A, T] boolean mask
-//     (modeling.py:345-369, reuse_cacheblend_pipeline.py:464-488); here the
-//     predicate kpos[j] <= qpos[r] is evaluated per tile from two int vectors.
+//     (src/sparsecache/modeling.py:345-369, reuse_cacheblend_pipeline.py:464-488).
+//     Here kpos is non-decreasing (cache slots are in position order), so row
+//     r sees exactly the key prefix [0, nvis[r]) with nvis[r] = #{j : kpos[j]
+//     <= qpos[r]}: one binary search per row replaces the mask.
 // Query rows can be gathered through q_rows (row r reads q[q_rows[r]]), so
 // the check layer attends only its active rows without a separate gather.
-// kpos must be non-decreasing (it is: cache slots are laid out in position
-// order), which lets every CTA stop at the last key any of its rows can see.
 //
-// Tiles: 64 query rows x 64 keys, head_dim 128, 4 warps of 16 rows, bf16
-// m16n8k16 tensor-core MMAs with fp32 accumulation, online softmax in exp2
-// space, K/V double-buffered with cp.async into XOR-swizzled shared memory.
+// CTA = 128 query rows of one q head (the tcgen05 M), 192 threads:
+//   warp 0     TMA producer: K and V tiles of 128 keys (two 128-byte-swizzled
+//              boxes of 64 dims each) into a 2-deep ring; rows past n_keys
+//              are zero-filled by the tensor map, never read from the cache.
+//   warp 1     MMA issuer and TMEM owner:
+//                S_j = Q K_j^T   M=128 N=128 K=128 -> TMEM S[j & 1] (fp32)
+//                O  += P_j V_j   M=128 N=128 K=128 -> TMEM O       (fp32)
+//              Q and P_j are K-major operands in shared memory; V_j is the
+//              MN-major B operand straight from its [keys][dims] tile.  QK of
+//              tile j+1 is issued before PV of tile j, so the tensor core
+//              works on the next scores while the softmax of this tile runs.
+//   warps 2-5  softmax + epilogue, one query row per thread (the TMEM lane
+//              of that row): tcgen05.ld the 128 scores, mask by nvis, online
+//              softmax in exp2 space, P_j as bf16 into the swizzled K-major
+//              smem tile, then one arrive.  The running max is rescaled
+//              lazily: O in TMEM is rescaled (tcgen05.ld/st) only when a
+//              warp's max grows by more than 2^8, so P stays <= 256 and most
+//              tiles touch O not at all.  The epilogue reads O once, divides
+//              by the row sum and stores bf16.
+// TMEM: S[0] cols 0-127, S[1] cols 128-255, O cols 256-383 (512 allocated).
+// Shared memory: Q 32 KB + 2 x (K 32 KB + V 32 KB) + 2 x P 32 KB = 224 KB.
+// Every wait is bounded; an expired wait records a status code and the CTA
+// winds down (TMA loads in flight are drained, TMEM is freed).  No cluster,
+// no multicast: safe inside multi-GPU programs.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -25,289 +48,367 @@ namespace sc {
 
 namespace {
 
-constexpr int kBM = 64;
-constexpr int kBN = 64;
 constexpr int kD = 128;
-constexpr int kThreads = 128;
-constexpr int kRowBytes = kD * 2;  // 256 B = 16 chunks of 16 B
+constexpr int kBM = 128;
+constexpr int kBN = 128;
+constexpr int kStages = 2;
+constexpr int kThreads = 192;
+constexpr float kRescaleLog2 = 8.0f;
 
-__device__ __forceinline__ uint32_t swz(int row, int chunk) {
-  return row * kRowBytes + ((chunk ^ (row & 7)) << 4);
+constexpr int kQBytes = kBM * kD * 2;      // two 16 KB k-blocks (dims 0-63, 64-127)
+constexpr int kKVBytes = kBN * kD * 2;     // two 16 KB halves (dims 0-63, 64-127)
+constexpr int kHalfBytes = kBN * 128;      // one 128-key x 128-byte half
+constexpr int kPBytes = kBM * kBN * 2;     // two 16 KB k-blocks (keys 0-63, 64-127)
+constexpr int kPBlock = kBM * 128;
+constexpr int kOffK = kQBytes;
+constexpr int kOffV = kOffK + kStages * kKVBytes;
+constexpr int kOffP = kOffV + kStages * kKVBytes;
+constexpr int kOffBars = kOffP + 2 * kPBytes;
+constexpr int kSmemBytes = 1024 + kOffBars + 256;
+
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemO = 256;
+
+struct alignas(8) AttnBars {
+  uint64_t k_full[kStages];
+  uint64_t k_empty[kStages];
+  uint64_t v_full[kStages];
+  uint64_t v_empty[kStages];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_done;
+  uint64_t o_final;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int max_vis;
+};
+static_assert(sizeof(AttnBars) <= 256, "barrier block");
+
+// 2^x by the MUFU ex2 instruction (flush-to-zero; 2^-inf = +0)
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
-  const int sz = pred ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(sz)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                        uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                          uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// Load a [64 rows x 128] bf16 tile (rows row0.., clipped at nrows) into
-// swizzled smem.  Each of the 128 threads moves 8 chunks of 16 B.
-__device__ __forceinline__ void load_tile(uint32_t sbase, const __nv_bfloat16* g, size_t row_stride,
-                                          int row0, int nrows) {
-  const int tid = threadIdx.x;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int idx = tid + i * kThreads;  // 0..1023
-    const int r = idx >> 4, c = idx & 15;
-    const int grow = row0 + r;
-    const bool ok = grow < nrows;
-    const __nv_bfloat16* src = g + (size_t)(ok ? grow : 0) * row_stride + c * 8;
-    cp_async16(sbase + swz(r, c), src, ok);
-  }
+// byte offset of 16-byte chunk c of row r in a K-major, 128-byte-swizzled
+// block of 128-byte rows (the layout TMA SWIZZLE_128B writes)
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+  return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4));
 }
 
 }  // namespace
 
-__global__ void __launch_bounds__(kThreads, 2)
-    attention_prefill_kernel(AttnPrefillArgs p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const uint32_t sQ = smem_u32(smem);
-  const uint32_t sK = sQ + kBM * kRowBytes;       // 2 stages
-  const uint32_t sV = sK + 2 * kBN * kRowBytes;   // 2 stages
-  __shared__ int s_qpos[kBM];
-  __shared__ int s_qmin, s_qmax, s_nkeys;
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
+                                const __grid_constant__ CUtensorMap tm_v, AttnPrefillArgs p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  AttnBars* bars = reinterpret_cast<AttnBars*>(smem + kOffBars);
+  int* status = p.status;
 
-  const int h = blockIdx.y;
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int h = blockIdx.x;
   const int kvh = h / (p.n_heads / p.n_kv_heads);
-  const int r0 = blockIdx.x * kBM;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_row_tiles = gridDim.y;
+  const int r0 = (n_row_tiles - 1 - (int)blockIdx.y) * kBM;  // longest row tiles first
 
-  // ---- query positions of this tile; bound of visible keys ----
-  if (tid < kBM) {
-    const int r = r0 + tid;
-    s_qpos[tid] = (r < p.n_rows) ? p.qpos[r] : -1;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->s_full[b], 1);
+      mbar_init(&bars->p_full[b], 128);
+    }
+    mbar_init(&bars->o_done, 1);
+    mbar_init(&bars->o_final, 1);
+    mbar_init(&bars->drain, 1);
+    bars->max_vis = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
   }
   __syncthreads();
-  if (tid == 0) {
-    int mn = 0x7fffffff, mx = -1;
-    for (int i = 0; i < kBM; ++i) {
-      const int q = s_qpos[i];
-      if (q >= 0) { mn = min(mn, q); mx = max(mx, q); }
+
+  // ---- softmax warps: stage the (gathered) Q tile, find each row's visible prefix ----
+  const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+  const int row = quarter * 32 + lane;  // tile row == TMEM lane (softmax warps only)
+  int nvis = 0;
+  if (warp >= 2) {
+    const int g = r0 + row;
+    uint8_t* sq = smem;
+    int qp = -1;
+    if (g < p.n_rows) {
+      qp = p.qpos[g];
+      const int src = p.q_rows ? p.q_rows[g] : g;
+      const uint4* qsrc = reinterpret_cast<const uint4*>(p.q + (size_t)src * p.ldq + (size_t)h * kD);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint4 v = qsrc[c];
+        *reinterpret_cast<uint4*>(sq + (c >> 3) * (kBM * 128) + sw128(row, c & 7)) = v;
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < 16; ++c)
+        *reinterpret_cast<uint4*>(sq + (c >> 3) * (kBM * 128) + sw128(row, c & 7)) = make_uint4(0, 0, 0, 0);
     }
-    // number of keys with kpos <= mx (kpos non-decreasing)
-    int lo = 0, hi = p.n_keys;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      const int kp = p.kpos ? p.kpos[mid] : mid;
-      if (kp <= mx) lo = mid + 1; else hi = mid;
-    }
-    s_qmin = mn; s_qmax = mx; s_nkeys = (mx < 0) ? 0 : lo;
-  }
-
-  // ---- Q tile (gathered rows) ----
-  {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int idx = tid + i * kThreads;
-      const int r = idx >> 4, c = idx & 15;
-      const int grow = r0 + r;
-      const bool ok = grow < p.n_rows;
-      const int src_row = ok ? (p.q_rows ? p.q_rows[grow] : grow) : 0;
-      const __nv_bfloat16* src = p.q + (size_t)src_row * p.ldq + h * kD + c * 8;
-      cp_async16(sQ + swz(r, c), src, ok);
-    }
-    cp_async_commit();
-  }
-  __syncthreads();
-  const int n_keys = s_nkeys;
-  const int qmin = s_qmin;
-  const int n_tiles = (n_keys + kBN - 1) / kBN;
-
-  const __nv_bfloat16* kbase = p.k_cache + (size_t)kvh * p.cache_cap * kD;
-  const __nv_bfloat16* vbase = p.v_cache + (size_t)kvh * p.cache_cap * kD;
-  if (n_tiles > 0) {
-    load_tile(sK, kbase, kD, 0, n_keys);
-    load_tile(sV, vbase, kD, 0, n_keys);
-  }
-  cp_async_commit();
-
-  // Q fragments
-  cp_async_wait<1>();
-  __syncthreads();
-  uint32_t qf[8][4];
-  {
-    const int mi = lane >> 3, rr = lane & 7;
-    const int row = warp * 16 + (mi & 1) * 8 + rr;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const int chunk = kk * 2 + (mi >> 1);
-      ldsm_x4(sQ + swz(row, chunk), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
-    }
-  }
-
-  const int g = lane >> 2, t4 = lane & 3;
-  const int my_row0 = warp * 16 + g;  // tile-local rows my_row0 and my_row0 + 8
-  const int qp0 = s_qpos[my_row0], qp1 = s_qpos[my_row0 + 8];
-  const float sl2 = p.scale * 1.4426950408889634f;
-
-  float o[16][4];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-
-  for (int it = 0; it < n_tiles; ++it) {
-    const int stage = it & 1;
-    if (it + 1 < n_tiles) {
-      const int ns = stage ^ 1;
-      load_tile(sK + ns * kBN * kRowBytes, kbase, kD, (it + 1) * kBN, n_keys);
-      load_tile(sV + ns * kBN * kRowBytes, vbase, kD, (it + 1) * kBN, n_keys);
-    }
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    const uint32_t k_s = sK + stage * kBN * kRowBytes;
-    const uint32_t v_s = sV + stage * kBN * kRowBytes;
-
-    // S = Q K^T : 16 x 64 per warp -> 8 n-tiles of 8 keys
-    float s[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-#pragma unroll
-      for (int jp = 0; jp < 4; ++jp) {
-        // two n-tiles (16 keys) x 16 dims per ldmatrix.x4
-        const int mi = lane >> 3, rr = lane & 7;
-        const int key = jp * 16 + (mi >> 1) * 8 + rr;
-        const int chunk = kk * 2 + (mi & 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(k_s + swz(key, chunk), b0, b1, b2, b3);
-        mma_bf16(s[2 * jp], qf[kk], b0, b1);
-        mma_bf16(s[2 * jp + 1], qf[kk], b2, b3);
+    if (qp >= 0) {
+      if (p.kpos == nullptr) {
+        nvis = qp + 1 < p.n_keys ? qp + 1 : p.n_keys;
+      } else {
+        int lo = 0, hi = p.n_keys;  // first key with kpos > qp
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (p.kpos[mid] <= qp) lo = mid + 1; else hi = mid;
+        }
+        nvis = lo;
       }
     }
+    fence_proxy_async_smem();  // Q written by threads, read by the tensor core
+    const int wmax = __reduce_max_sync(0xffffffffu, nvis);
+    if (lane == 0) atomicMax(&bars->max_vis, wmax);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+  const int n_tiles = (bars->max_vis + kBN - 1) / kBN;
 
-    // masking
-    const int key0 = it * kBN;
-    const int last_key = min(key0 + kBN, n_keys) - 1;
-    const int last_kpos = p.kpos ? p.kpos[last_key] : last_key;
-    const bool need_mask = (key0 + kBN > n_keys) || (last_kpos > qmin);
-    if (need_mask) {
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int k_last[kStages], v_last[kStages];
+      for (int s = 0; s < kStages; ++s) k_last[s] = v_last[s] = -1;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int s = j % kStages;
+        const uint32_t ph = (uint32_t)(j / kStages) & 1u;
+        uint8_t* sk = smem + kOffK + s * kKVBytes;
+        uint8_t* sv = smem + kOffV + s * kKVBytes;
+        if (!mbar_wait(&bars->k_empty[s], ph ^ 1u, status, kStatusTimeoutSmemEmpty)) break;
+        mbar_arrive_expect_tx(&bars->k_full[s], kKVBytes);
+        tma_load_3d(sk, &tm_k, &bars->k_full[s], 0, j * kBN, kvh);
+        tma_load_3d(sk + kHalfBytes, &tm_k, &bars->k_full[s], 64, j * kBN, kvh);
+        k_last[s] = (int)ph;
+        if (!mbar_wait(&bars->v_empty[s], ph ^ 1u, status, kStatusTimeoutSmemEmpty)) break;
+        mbar_arrive_expect_tx(&bars->v_full[s], kKVBytes);
+        tma_load_3d(sv, &tm_v, &bars->v_full[s], 0, j * kBN, kvh);
+        tma_load_3d(sv + kHalfBytes, &tm_v, &bars->v_full[s], 64, j * kBN, kvh);
+        v_last[s] = (int)ph;
+      }
+      // every TMA load issued must land before the CTA exits
+      for (int s = 0; s < kStages; ++s) {
+        if (k_last[s] >= 0) mbar_wait(&bars->k_full[s], (uint32_t)k_last[s], status, kStatusTimeoutDrain);
+        if (v_last[s] >= 0) mbar_wait(&bars->v_full[s], (uint32_t)v_last[s], status, kStatusTimeoutDrain);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && n_tiles > 0) {
+      constexpr uint32_t idesc_qk = make_idesc_bf16(kBM, kBN);
+      constexpr uint32_t idesc_pv = make_idesc_bf16(kBM, kD, /*b_mn_major=*/true);
+      const uint32_t sq = smem_u32(smem);
+      bool ok = true;
+      auto issue_qk = [&](int j) -> bool {
+        const int s = j % kStages;
+        if (!mbar_wait(&bars->k_full[s], (uint32_t)(j / kStages) & 1u, status, kStatusTimeoutTmaFull))
+          return false;
+        tc_fence_after();
+        const uint32_t sk = smem_u32(smem + kOffK + s * kKVBytes);
+        const uint32_t d = tmem_base + (uint32_t)(j & 1) * kBN;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+        for (int t = 0; t < kD / 16; ++t) {
+          const uint64_t ad = make_desc_kmajor_sw128(sq + (t >> 2) * (kBM * 128) + (t & 3) * 32);
+          const uint64_t bd = make_desc_kmajor_sw128(sk + (t >> 2) * kHalfBytes + (t & 3) * 32);
+          tc_mma_f16(d, ad, bd, idesc_qk, t > 0 ? 1u : 0u);
+        }
+        tc_commit(&bars->s_full[j & 1]);
+        tc_commit(&bars->k_empty[s]);
+        return true;
+      };
+      ok = issue_qk(0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (j + 1 < n_tiles && !(ok = issue_qk(j + 1))) break;
+        const int s = j % kStages;
+        if (!mbar_wait(&bars->p_full[j & 1], (uint32_t)(j >> 1) & 1u, status, kStatusTimeoutTmemFull)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(&bars->v_full[s], (uint32_t)(j / kStages) & 1u, status, kStatusTimeoutTmaFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sp = smem_u32(smem + kOffP + (j & 1) * kPBytes);
+        const uint32_t sv = smem_u32(smem + kOffV + s * kKVBytes);
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int key = key0 + j * 8 + 2 * t4 + e;
-          int kp = 0x7fffffff;
-          if (key < n_keys) kp = p.kpos ? p.kpos[key] : key;
-          if (kp > qp0) s[j][e] = -INFINITY;
-          if (kp > qp1) s[j][2 + e] = -INFINITY;
+        for (int t = 0; t < kBN / 16; ++t) {
+          const uint64_t ad = make_desc_kmajor_sw128(sp + (t >> 2) * kPBlock + (t & 3) * 32);
+          const uint64_t bd = make_desc_mnmajor_sw128(sv + t * 2048, kHalfBytes);
+          tc_mma_f16(tmem_base + kTmemO, ad, bd, idesc_pv, (j > 0 || t > 0) ? 1u : 0u);
+        }
+        tc_commit(&bars->o_done);
+        tc_commit(&bars->v_empty[s]);
+      }
+      // o_final completes once every MMA above has completed (also on the
+      // error path, so the epilogue and the teardown never read a live TMEM)
+      tc_commit(&bars->o_final);
+    }
+  } else {
+    // ---------------- softmax (warps 2-5) ----------------
+    const float c = p.scale * 1.4426950408889634f;
+    const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    float m_ref = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int b = j & 1;
+      // exits stay warp-uniform: the tcgen05 loads below are warp-collective
+      const bool got = mbar_wait(&bars->s_full[b], (uint32_t)(j >> 1) & 1u, status, kStatusTimeoutTmemFull);
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[kBN];
+#pragma unroll
+      for (int q4 = 0; q4 < kBN / 32; ++q4)
+        tmem_ld_32x32b_x32(lane_base + b * kBN + q4 * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[q4 * 32]));
+      tmem_ld_wait();
+      const int vis = nvis - j * kBN;  // keys [0, vis) of this tile are visible to my row
+      if (!__all_sync(0xffffffffu, vis >= kBN)) {
+#pragma unroll
+        for (int i = 0; i < kBN; ++i)
+          if (i >= vis) sv[i] = 0xff800000u;  // -inf
+      }
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kBN; i += 4) {
+        mx0 = fmaxf(mx0, __uint_as_float(sv[i]));
+        mx1 = fmaxf(mx1, __uint_as_float(sv[i + 1]));
+        mx2 = fmaxf(mx2, __uint_as_float(sv[i + 2]));
+        mx3 = fmaxf(mx3, __uint_as_float(sv[i + 3]));
+      }
+      const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;
+      const bool need = m_tile > m_ref + kRescaleLog2;  // false when the tile is fully masked
+      float f = 1.f;
+      if (need) {
+        f = exp2_approx(m_ref - m_tile);  // 0 while nothing was visible (m_ref = -inf)
+        m_ref = m_tile;
+        l *= f;
+      }
+      // O holds P_0..P_{j-1} V: rescale it (warp-uniformly, tcgen05 ld/st are
+      // warp-collective) once PV(j-1) has completed.  s_full(j) implies PV(j-2)
+      // completed, so waiting on o_done's phase j-1 is unambiguous.
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        const bool done = mbar_wait(&bars->o_done, (uint32_t)(j - 1) & 1u, status, kStatusTimeoutTmemFull);
+        if (!__all_sync(0xffffffffu, done)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int cc = 0; cc < kD / 32; ++cc) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(lane_base + kTmemO + cc * 32, o);
+          tmem_ld_wait();
+          uint32_t lo[16], hi[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            lo[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+            hi[i] = __float_as_uint(__uint_as_float(o[16 + i]) * f);
+          }
+          tmem_st_32x32b_x16(lane_base + kTmemO + cc * 32, lo);
+          tmem_st_32x32b_x16(lane_base + kTmemO + cc * 32 + 16, hi);
+        }
+        tmem_st_wait();
+      }
+      const float base = (m_ref == -INFINITY) ? 0.f : m_ref;
+      float sum0 = 0.f, sum1 = 0.f;
+      uint8_t* sp = smem + kOffP + b * kPBytes;
+#pragma unroll
+      for (int cc = 0; cc < kBN / 8; ++cc) {  // 8 keys = one 16-byte chunk of the P row
+        float e[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) e[i] = exp2_approx(fmaf(__uint_as_float(sv[8 * cc + i]), c, -base));
+        sum0 += (e[0] + e[1]) + (e[2] + e[3]);
+        sum1 += (e[4] + e[5]) + (e[6] + e[7]);
+        *reinterpret_cast<uint4*>(sp + (cc >> 3) * kPBlock + sw128(row, cc & 7)) =
+            make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
+                       pack_bf16x2(e[6], e[7]));
+      }
+      l += sum0 + sum1;
+      fence_proxy_async_smem();  // P written by threads, read by the tensor core
+      tc_fence_before();
+      mbar_arrive(&bars->p_full[b]);
+    }
+    // ---- epilogue: O / l -> bf16 ----
+    const int g = r0 + row;
+    if (n_tiles > 0 && ok) ok = mbar_wait(&bars->o_final, 0, status, kStatusTimeoutTmemFull);
+    __nv_bfloat16* dst = p.out + (size_t)g * p.ldo + (size_t)h * kD;
+    if (n_tiles > 0 && __all_sync(0xffffffffu, ok)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll 1
+      for (int cc = 0; cc < kD / 32; ++cc) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(lane_base + kTmemO + cc * 32, o);
+        tmem_ld_wait();
+        if (g < p.n_rows) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            d4[i] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * i]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
+                               pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
+                               pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
+                               pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
         }
       }
-    }
-
-    // online softmax (rows g and g+8 of this warp; each row shared by 4 lanes)
-    float mx0 = -INFINITY, mx1 = -INFINITY;
+    } else if (g < p.n_rows && n_tiles == 0) {
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
-      mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
+      for (int i = 0; i < 16; ++i) d4[i] = make_uint4(0, 0, 0, 0);
     }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float mn0 = fmaxf(m0, mx0 * sl2), mn1 = fmaxf(m1, mx1 * sl2);
-    const float base0 = (mn0 == -INFINITY) ? 0.f : mn0;
-    const float base1 = (mn1 == -INFINITY) ? 0.f : mn1;
-    const float c0 = exp2f(m0 - base0), c1 = exp2f(m1 - base1);
-    m0 = mn0; m1 = mn1;
-    float rs0 = 0.f, rs1 = 0.f;
-    uint32_t pf[4][4];  // P as A fragments for 4 k-steps of 16 keys
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float p0 = exp2f(s[j][0] * sl2 - base0);
-      const float p1 = exp2f(s[j][1] * sl2 - base0);
-      const float p2 = exp2f(s[j][2] * sl2 - base1);
-      const float p3 = exp2f(s[j][3] * sl2 - base1);
-      rs0 += p0 + p1;
-      rs1 += p2 + p3;
-      const int kk = j >> 1, hi = j & 1;
-      pf[kk][hi * 2 + 0] = pack_bf16x2(p0, p1);
-      pf[kk][hi * 2 + 1] = pack_bf16x2(p2, p3);
-    }
-    l0 = l0 * c0 + rs0;
-    l1 = l1 * c1 + rs1;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      o[i][0] *= c0; o[i][1] *= c0;
-      o[i][2] *= c1; o[i][3] *= c1;
-    }
-
-    // O += P V : V tile [64 keys x 128 dims], B fragments via ldmatrix.trans
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-      for (int dp = 0; dp < 8; ++dp) {
-        // two n-tiles of 8 dims (16 dims) x 16 keys
-        const int mi = lane >> 3, rr = lane & 7;
-        const int key = kk * 16 + (mi & 1) * 8 + rr;
-        const int chunk = dp * 2 + (mi >> 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(v_s + swz(key, chunk), b0, b1, b2, b3);
-        mma_bf16(o[2 * dp], pf[kk], b0, b1);
-        mma_bf16(o[2 * dp + 1], pf[kk], b2, b3);
-      }
-    }
-    __syncthreads();
   }
 
-  // finalize: reduce row sums across the 4 lanes sharing a row
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
-  const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
-  const int row_a = r0 + my_row0, row_b = row_a + 8;
-#pragma unroll
-  for (int dn = 0; dn < 16; ++dn) {
-    const int d = dn * 8 + 2 * t4;
-    if (row_a < p.n_rows) {
-      *reinterpret_cast<uint32_t*>(p.out + (size_t)row_a * p.ldo + h * kD + d) =
-          pack_bf16x2(o[dn][0] * inv0, o[dn][1] * inv0);
-    }
-    if (row_b < p.n_rows) {
-      *reinterpret_cast<uint32_t*>(p.out + (size_t)row_b * p.ldo + h * kD + d) =
-          pack_bf16x2(o[dn][2] * inv1, o[dn][3] * inv1);
-    }
-  }
+  // teardown: the MMA thread's o_final commit covers every MMA it issued; a
+  // CTA that failed early still waits (bounded) for it before freeing TMEM
+  if (warp == 1 && lane == 0 && n_tiles > 0) mbar_wait(&bars->o_final, 0, status, kStatusTimeoutDrain);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
 }
 
 cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream) {
-  if (p.head_dim != kD || p.n_rows <= 0) return p.n_rows == 0 ? cudaSuccess : cudaErrorInvalidValue;
-  const int smem = kBM * kRowBytes + 4 * kBN * kRowBytes;  // 80 KB
-  ensure_smem_attr(attention_prefill_kernel, smem);
-  dim3 grid((p.n_rows + kBM - 1) / kBM, p.n_heads);
-  attention_prefill_kernel<<<grid, kThreads, smem, stream>>>(p);
+  if (p.head_dim != kD || p.n_rows < 0 || p.n_kv_heads <= 0 || p.n_heads % p.n_kv_heads != 0)
+    return cudaErrorInvalidValue;
+  if (p.n_rows == 0) return cudaSuccess;
+  if (p.n_keys < 0 || p.n_keys > p.cache_cap) return cudaErrorInvalidValue;
+  // [n_kv_heads][n_keys][128] view of the layer cache: rows past n_keys are
+  // outside the tensor and arrive as zeros
+  const uint64_t rows = p.n_keys > 0 ? (uint64_t)p.n_keys : 1;
+  CUtensorMap tk, tv;
+  if (!make_tmap_3d_bf16(&tk, p.k_cache, kD, rows, (uint64_t)p.n_kv_heads, kD, (uint64_t)p.cache_cap * kD, 64,
+                         kBN))
+    return cudaErrorInvalidValue;
+  if (!make_tmap_3d_bf16(&tv, p.v_cache, kD, rows, (uint64_t)p.n_kv_heads, kD, (uint64_t)p.cache_cap * kD, 64,
+                         kBN))
+    return cudaErrorInvalidValue;
+  ensure_smem_attr(attention_prefill_tc_kernel, kSmemBytes);
+  dim3 grid(p.n_heads, (p.n_rows + kBM - 1) / kBM);
+  attention_prefill_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tk, tv, p);
   return cudaGetLastError();
 }
 

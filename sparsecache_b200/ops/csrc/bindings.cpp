@@ -513,9 +513,9 @@ void gemv_argmax(Tensor x, Tensor w, c10::optional<Tensor> norm_w, double eps, T
 }
 
 // ----------------------------------------------------------- attention
-void attention_prefill(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tensor k_cache,
-                       Tensor v_cache, c10::optional<Tensor> kpos, int64_t n_keys,
-                       int64_t n_heads, double scale, Tensor out) {
+void attention_prefill_impl(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tensor k_cache,
+                            Tensor v_cache, c10::optional<Tensor> kpos, int64_t n_keys,
+                            int64_t n_heads, double scale, Tensor out, bool legacy) {
   const c10::cuda::CUDAGuard guard(q.device());
   check_matrix(q, "q");
   check_matrix(out, "out");
@@ -548,7 +548,29 @@ void attention_prefill(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tens
   p.scale = (float)scale;
   p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   p.ldo = (int)out.stride(0);
-  check_cuda(sc::attention_prefill(p, cur_stream()), "attention_prefill");
+  p.status = status_tensor(q).data_ptr<int>();
+  TORCH_CHECK(k_cache.is_cuda() && v_cache.is_cuda(), "caches must be CUDA tensors");
+  CHECK_BF16(k_cache); CHECK_BF16(v_cache);
+  CHECK_ALIGN16(k_cache); CHECK_ALIGN16(v_cache);
+  TORCH_CHECK(n_heads % k_cache.size(0) == 0, "n_heads must be a multiple of the kv heads");
+  TORCH_CHECK(q.size(1) >= n_heads * 128 && out.size(1) >= n_heads * 128, "q / out narrower than n_heads * 128");
+  if (legacy) {
+    check_cuda(sc::attention_prefill_mma(p, cur_stream()), "attention_prefill_mma");
+  } else {
+    check_cuda(sc::attention_prefill(p, cur_stream()), "attention_prefill");
+  }
+}
+
+void attention_prefill(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tensor k_cache,
+                       Tensor v_cache, c10::optional<Tensor> kpos, int64_t n_keys,
+                       int64_t n_heads, double scale, Tensor out) {
+  attention_prefill_impl(q, q_rows, qpos, k_cache, v_cache, kpos, n_keys, n_heads, scale, out, false);
+}
+
+void attention_prefill_mma(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tensor k_cache,
+                           Tensor v_cache, c10::optional<Tensor> kpos, int64_t n_keys,
+                           int64_t n_heads, double scale, Tensor out) {
+  attention_prefill_impl(q, q_rows, qpos, k_cache, v_cache, kpos, n_keys, n_heads, scale, out, true);
 }
 
 void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int64_t n_heads,
@@ -1076,6 +1098,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("pos_advance"), py::arg("n_advance") = 1);
   m.def("gemv_argmax_grid", &gemv_argmax_grid);
   m.def("attention_prefill", &attention_prefill);
+  m.def("attention_prefill_mma", &attention_prefill_mma);
   m.def("attention_decode", &attention_decode, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("pos"), py::arg("n_heads"), py::arg("scale"), py::arg("splits"), py::arg("out"),
         py::arg("page_table") = py::none(), py::arg("page_shift") = 6, py::arg("n_virtual") = py::none(),

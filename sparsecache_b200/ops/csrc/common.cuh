@@ -100,19 +100,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait: returns false (after recording `code`) if the phase with the
 // given parity did not complete within kSpinLimitCycles.
+// try_wait suspends the thread until the phase completes or a hardware time
+// limit passes, so the loop wakes as soon as the phase flips; the deadline
+// and the shared status word (a global load) are looked at only every 32nd
+// round, keeping them off the wake-up path of a handoff.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           int* status, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
-  while (true) {
+  for (uint32_t round = 1;; ++round) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - start > kSpinLimitCycles) {
-      report_status(status, code);
-      return false;
-    }
-    if (status != nullptr && *((volatile int*)status) != 0) {
-      // Another role already failed: stop waiting so the kernel can drain.
-      return false;
+    if ((round & 31u) == 0) {
+      if (clock64() - start > kSpinLimitCycles) {
+        report_status(status, code);
+        return false;
+      }
+      if (status != nullptr && *((volatile int*)status) != 0) {
+        // Another role already failed: stop waiting so the kernel can drain.
+        return false;
+      }
     }
   }
 }

@@ -16,6 +16,11 @@ typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_
 bool make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                        uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
                        bool swizzle128);
+// 3-D [outer][mid][inner] bf16 view, 128-byte swizzle, box {box_inner, box_mid, 1};
+// coordinates past mid / outer load as zeros
+bool make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t mid, uint64_t outer,
+                       uint64_t mid_stride_elems, uint64_t outer_stride_elems, uint32_t box_inner,
+                       uint32_t box_mid);
 
 // ---------------------------------------------------------------- GEMM ----
 enum Epi : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_RS = 4, EPI_PARTIAL = 5 };
@@ -160,9 +165,12 @@ struct AttnPrefillArgs {
   float scale;
   __nv_bfloat16* out;  // [n_rows, n_heads*128]
   int ldo;
+  int* status;  // bounded-wait status word
 };
 
 cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream);
+// the mma.sync kernel the tcgen05 one replaced, kept for A/B measurement only
+cudaError_t attention_prefill_mma(const AttnPrefillArgs& p, cudaStream_t stream);
 
 struct AttnDecodeArgs {
   const __nv_bfloat16* q;  // [M, n_heads*128]

@@ -7,7 +7,9 @@ uses; every port must be free; the prefill worker, decode worker and proxy
 start in their own process groups with logs in the run directory; the
 launcher waits for their health endpoints (and stops at the first fatal
 startup log line); then it runs the paired benchmark client, aggregates,
-verifies the input trace and writes a run manifest.  Any failure stops all
+verifies the input trace and writes a run manifest.  While the services run,
+an optional exclusive-GPU monitor polls the GPUs and stops the cell at the
+first compute process that is not one of the launched services' own.  Any failure stops all
 the launched process groups (by the group ids this launcher created) and
 leaves a manifest with the failure reason.
 """
@@ -133,13 +135,22 @@ def launch_spec(job: dict, *, host: str = "127.0.0.1", ports: dict | None = None
 
 def execute(job: dict, run_dir: Path, *, gate: Callable[[], dict] | None = None, host: str = "127.0.0.1",
             ports: dict | None = None, startup_timeout_s: float = 600.0,
-            run_client: Callable[[], Any] | None = None) -> dict[str, Any]:
-    """Run one job fail-closed; returns (and writes) the run manifest."""
+            run_client: Callable[[], Any] | None = None,
+            monitor: Callable[[Sequence[int]], Any] | None = None,
+            spec: list[dict] | None = None) -> dict[str, Any]:
+    """Run one job fail-closed; returns (and writes) the run manifest.
+
+    ``monitor(service_pids)`` builds the runtime exclusive-GPU watch (a
+    ``gate.ExclusivityMonitor``) once the services run; the first foreign
+    compute process it sees stops every launched process group and fails
+    the run (reference run_progressive_pd_live_job.py:524-560).
+    """
     from .queue import validate_pack_hashes
 
     run_dir.mkdir(parents=True, exist_ok=True)
     manifest: dict[str, Any] = {"job_id": job["job_id"], "started_at": time.time(), "status": "failed"}
     procs: list[ManagedProcess] = []
+    watch = None
     try:
         manifest["pack_hashes"] = validate_pack_hashes(job)
         if gate is not None:
@@ -147,18 +158,32 @@ def execute(job: dict, run_dir: Path, *, gate: Callable[[], dict] | None = None,
             manifest["resource_gate"] = res
             if res.get("status") != "passed":
                 raise RuntimeError("exclusive-GPU gate failed")
-        spec = launch_spec(job, host=host, ports=ports)
-        assert_ports_free(host, [int(a.rsplit(":", 1)[1].split("/")[0]) for a in (s["health"] for s in spec)])
+        spec = spec if spec is not None else launch_spec(job, host=host, ports=ports)
+        health = [s["health"] for s in spec if s.get("health")]
+        assert_ports_free(host, [int(a.rsplit(":", 1)[1].split("/")[0]) for a in health])
         for s in spec:
             procs.append(spawn(s["name"], s["argv"], run_dir / "logs", s["env"]))
+        if monitor is not None:
+            watch = monitor([mp.popen.pid for mp in procs])
+            watch.start(lambda finding: stop(procs, timeout_s=10.0))
         for s in spec:
-            wait_http(s["health"], procs, startup_timeout_s)
+            if s.get("health"):
+                wait_http(s["health"], procs, startup_timeout_s)
         if run_client is not None:
             manifest["client"] = run_client()
+        if watch is not None and watch.finding is not None:
+            raise RuntimeError("interference")
         manifest["status"] = "completed"
     except Exception as exc:  # noqa: BLE001
         manifest["error"] = f"{type(exc).__name__}: {exc}"
     finally:
+        if watch is not None:
+            watch.stop()
+            manifest["runtime_monitor"] = {"samples": watch.samples, "finding": watch.finding}
+            if watch.finding is not None:
+                manifest["status"] = "failed"
+                manifest["error"] = ("runtime exclusive-GPU monitor detected interference: "
+                                     + json.dumps(watch.finding, default=str))
         stop(procs)
         manifest["finished_at"] = time.time()
         (run_dir / "run_manifest.json").write_text(json.dumps(manifest, indent=2, default=str) + "\n")

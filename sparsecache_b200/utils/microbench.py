@@ -6,8 +6,8 @@ CUDA events on the launching stream, 10 warm-up launches, mean over N timed
 launches; every case uses tensors that are re-read each launch, so the
 bandwidth figures of the GEMV / decode-attention rows are HBM figures when
 the operand exceeds L2 (126 MB) and L2-assisted otherwise (noted per row).
-Fractions are against the measured copy bandwidth and cuBLAS bf16 rate of
-this machine class (6.46 TB/s, 1.68 PFLOP/s burst).
+Fractions are against the measured copy bandwidth and cuBLAS bf16 burst rate
+of this machine class (``_measured_peaks``).
 """
 from __future__ import annotations
 
@@ -19,8 +19,24 @@ import torch
 
 from ..models.engine import ATTN_CNT_PER_KVH, ATTN_WS_PER_KVH
 
-HBM_GBS = 6456.5
-BF16_TFLOPS = 1676.9
+
+def _measured_peaks() -> tuple[float, float]:
+    """Copy bandwidth (GB/s) and cuBLAS bf16 burst rate (TFLOP/s) measured on
+    this machine class (MEASURED_PEAKS.json at the repository root when it is
+    there; otherwise an earlier measurement of the same B200 pool)."""
+    import os
+
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                        "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        return 6558.7, 1661.6
+
+
+HBM_GBS, BF16_TFLOPS = _measured_peaks()
 
 
 def timeit(fn, n: int = 50, warm: int = 10) -> float:
@@ -185,6 +201,27 @@ def main() -> None:
             t = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), S, out, **kw))
             res[f"attn_decode_tp8_70b_ctx{cap}_{name}"] = {"us": t, "GBps": kv_bytes / (t * 1e-6) / 1e9}
 
+    if "attn_prefill" in only or "attn_prefill_ab" in only:
+        # CacheBlend shapes of the 8B serving case: the full layers (every row,
+        # causal) and the selective layers (300 active rows over 1676 keys);
+        # the tcgen05 kernel against the mma.sync kernel it replaced
+        H, Hkv, T = 32, 8, 1676
+        kc = torch.randn(Hkv, T, 128, device=dev).to(bf)
+        vc = torch.randn(Hkv, T, 128, device=dev).to(bf)
+        q = torch.randn(T, H * 128, device=dev).to(bf)
+        allpos = torch.arange(T, device=dev, dtype=torch.int32)
+        sel = torch.sort(torch.randperm(T - 40, device=dev)[:260]).values.to(torch.int32)
+        sel = torch.cat([sel, allpos[-40:]]).sort().values
+        for name, rows in (("causal", None), ("selective300", sel)):
+            R = T if rows is None else rows.numel()
+            qpos = allpos if rows is None else rows
+            out = torch.empty(R, H * 128, device=dev, dtype=bf)
+            flops = 4 * 128 * H * float(sum(int(x) + 1 for x in qpos.tolist()))
+            for kern in ("attention_prefill", "attention_prefill_mma"):
+                fn = getattr(ext, kern)
+                t = timeit(lambda: fn(q, rows, qpos, kc, vc, None, T, H, 1 / math.sqrt(128), out), n=20)
+                tf = flops / (t * 1e-6) / 1e12
+                res[f"{kern}_{name}_T{T}"] = {"us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS}
     if "attn_prefill" in only:
         H, Hkv = 32, 8
         for T in (2048, 16384):

@@ -157,29 +157,42 @@ def _attn_reference(q, kc, vc, qpos, kpos, n_heads):
     return (p @ v).transpose(0, 1).reshape(R, n_heads * 128)
 
 
-@pytest.mark.parametrize("case", ["causal", "selective", "staged"])
-def test_attention_prefill(cuda_device, case):
-    H, Hkv, T = 8, 2, 777
-    cap = 1000
-    kc = torch.randn(Hkv, cap, 128, device=cuda_device).to(torch.bfloat16)
-    vc = torch.randn(Hkv, cap, 128, device=cuda_device).to(torch.bfloat16)
+@pytest.mark.parametrize("T,R", [(777, 150), (1676, 300), (65, 1), (129, 3)])
+@pytest.mark.parametrize("case", ["causal", "selective", "staged", "growing"])
+def test_attention_prefill(cuda_device, case, T, R):
+    """tcgen05 flash attention vs the fp32 reference: full causal rows, a sorted
+    subset of rows over the whole cache (CacheBlend), staged key positions (a
+    suffix at later global positions), and scores that grow along the keys so
+    the lazily rescaled running max moves many times (the O-in-TMEM rescale)."""
+    H, Hkv = 8, 2
+    cap = T + 223
+    g = torch.Generator(device="cpu").manual_seed(T * 7 + R + len(case))
+    kc = torch.randn(Hkv, cap, 128, generator=g)
+    vc = torch.randn(Hkv, cap, 128, generator=g)
+    if case == "growing":
+        kc[:, :T] *= torch.linspace(0.2, 3.0, T)[None, :, None]
+    kc = kc.to(cuda_device, torch.bfloat16)
+    vc = vc.to(cuda_device, torch.bfloat16)
     kpos = torch.arange(T, device=cuda_device, dtype=torch.int32)
-    if case == "causal":
+    if case in ("causal", "growing"):
         rows = torch.arange(T, device=cuda_device, dtype=torch.int32)
         qpos = kpos.clone()
     else:
-        rows = torch.sort(torch.randperm(T)[:150]).values.to(torch.int32).to(cuda_device)
+        rows = torch.sort(torch.randperm(T, generator=g)[:R]).values.to(torch.int32).to(cuda_device)
         qpos = kpos[rows.long()]
         if case == "staged":  # suffix placed at a later global position
             kpos = kpos.clone()
-            kpos[-40:] += 300
+            kpos[-min(40, T // 2):] += 300
             qpos = kpos[rows.long()]
-    qfull = torch.randn(T, H * 128, device=cuda_device).to(torch.bfloat16)
+    qfull = torch.randn(T, H * 128, generator=g).to(cuda_device, torch.bfloat16)
+    if case == "growing":
+        qfull = (qfull.float() * 2.0).to(torch.bfloat16)
     out = torch.empty(rows.numel(), H * 128, device=cuda_device, dtype=torch.bfloat16)
     _ext().attention_prefill(
         qfull, rows, qpos, kc, vc, kpos if case == "staged" else None, T, H, 1 / math.sqrt(128), out
     )
     torch.cuda.synchronize()
+    assert int(_ext().status(out).item()) == 0
     ref = _attn_reference(qfull[rows.long()], kc[:, :T], vc[:, :T], qpos.long(), kpos.long(), H)
     torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
 

@@ -8,6 +8,8 @@ test_verify_progressive_pd_input_trace.py, test_progressive_pd_live_queue.py
 and test_run_progressive_pd_live_job.py)."""
 import asyncio
 import json
+import time
+import os
 import sys
 
 import httpx
@@ -37,6 +39,84 @@ def test_resource_gate():
     assert {f["reason"] for f in bad["failures"]} == {"compute_processes_present", "memory_used_above_threshold",
                                                        "utilization_above_threshold"}
     assert gate.parse_compute_query("No running processes found") == {}
+    assert gate.parse_compute_query("GPU-b, 7, x, [N/A]\n") == {"GPU-b": [
+        {"pid": 7, "process_name": "x", "used_gpu_memory_mib": None}]}
+    with pytest.raises(ValueError, match="unexpected nvidia-smi GPU row"):
+        gate.parse_gpu_query("0, GPU-a\n")
+    with pytest.raises(ValueError, match="no GPUs"):
+        gate.parse_gpu_query("")
+    with pytest.raises(ValueError, match="non-empty unique"):
+        gate.evaluate_exclusivity(states, (0, 0), max_used_memory_mib=1024, max_utilization_pct=5)
+    with pytest.raises(ValueError, match="do not exist"):
+        gate.evaluate_exclusivity(states, (0, 5), max_used_memory_mib=1024, max_utilization_pct=5)
+    # the thresholds are inclusive limits: exactly at the limit passes
+    edge = gate.evaluate_exclusivity(states, (0,), max_used_memory_mib=12, max_utilization_pct=0)
+    assert edge["status"] == "passed" and edge["requested_gpus"] == [0]
+
+
+def test_runtime_monitor_finds_foreign_processes():
+    """The runtime watch ignores the run's own service tree and reports the first
+    compute process outside it (or a GPU that vanished)."""
+    parents = {500: 400, 400: 300, 300: 1, 900: 1}
+    procs = {"text": ""}
+
+    def runner(cmd):
+        return GPU_QUERY if cmd[1].startswith("--query-gpu=") else procs["text"]
+
+    mon = gate.ExclusivityMonitor([0, 1], service_roots=[300], command_runner=runner, parent_of=parents.get)
+    assert mon.check() is None
+    procs["text"] = "GPU-a, 500, python, 100\n"  # grandchild of the service root: owned
+    assert mon.check() is None
+    procs["text"] = "GPU-a, 500, python, 100\nGPU-b, 900, intruder, 2000\n"
+    found = mon.check()
+    assert found["reason"] == "foreign_compute_process" and found["pid"] == 900 and found["gpu"] == 1
+    gone = gate.ExclusivityMonitor([3], service_roots=[300], command_runner=runner, parent_of=parents.get)
+    assert gone.check()["reason"] == "gpu_disappeared"
+    # the daemon thread reports once and stops
+    hits = []
+    mon2 = gate.ExclusivityMonitor([1], service_roots=[300], command_runner=runner, parent_of=parents.get,
+                                   interval_s=0.01)
+    mon2.start(hits.append)
+    deadline = time.time() + 5
+    while not hits and time.time() < deadline:
+        time.sleep(0.01)
+    mon2.stop()
+    assert len(hits) == 1 and hits[0]["pid"] == 900 and mon2.finding == hits[0]
+    assert gate.parent_pid(os.getpid()) == os.getppid()
+
+
+def test_launcher_stops_the_cell_on_interference(tmp_path):
+    """A foreign compute process during the run stops every launched process
+    group and fails the run with the monitor's finding."""
+    pack = tmp_path / "pack"
+    pack.mkdir()
+    (pack / "requests.jsonl").write_text('{"prompt": [1]}\n')
+    (pack / "metadata.jsonl").write_text('{}\n')
+    job = queue.build_job(job_id="j", phase="p", status="s", pack_dir=pack, run_dir=tmp_path / "run", requests=1,
+                          request_offset=0, warmups=0, bandwidth_gbps=25)
+    spec = [{"name": "svc", "argv": [sys.executable, "-c", "import time; time.sleep(60)"], "env": {}}]
+    intruder = {"on": False}
+
+    def runner(cmd):
+        if cmd[1].startswith("--query-gpu="):
+            return GPU_QUERY
+        return "GPU-a, 424242, intruder, 10\n" if intruder["on"] else ""
+
+    def make_monitor(pids):
+        return gate.ExclusivityMonitor([0], pids, command_runner=runner, parent_of=lambda p: 1, interval_s=0.02)
+
+    def client():
+        intruder["on"] = True
+        deadline = time.time() + 5
+        while time.time() < deadline:  # the cell keeps running until the monitor stops it
+            time.sleep(0.02)
+        return {"requests": 1}
+
+    t0 = time.time()
+    man = launcher.execute(job, tmp_path / "run", spec=spec, monitor=make_monitor, run_client=client)
+    assert man["status"] == "failed" and "interference" in man["error"] and "424242" in man["error"]
+    assert man["runtime_monitor"]["finding"]["reason"] == "foreign_compute_process"
+    assert time.time() - t0 < 30
 
 
 CFG = proxy.ProxyConfig()
