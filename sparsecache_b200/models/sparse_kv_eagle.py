@@ -32,6 +32,12 @@ from ..rope import apply_rope
 from .sparse_kv_draft import RMSNorm, SparseKVDraftConfig, SparseTargetKVAttention, stage_features
 
 
+# how the adapter's memory read joins the recurrent hidden state (see
+# SparseKVEagleDrafter.fuse): "scalar" adds sigmoid(adapter_scale) * delta;
+# "gated_delta" adds a gated, linearly mapped correction toward delta
+FUSION_MODES = frozenset({"scalar", "gated_delta"})
+
+
 @dataclass(frozen=True)
 class SparseKVEagleConfig:
     target_hidden_size: int = 4096
@@ -49,17 +55,18 @@ class SparseKVEagleConfig:
     fusion_mode: str = "scalar"
 
     def __post_init__(self) -> None:
-        if self.hidden_size != self.num_attention_heads * self.head_dim:
-            raise ValueError("hidden size must match the attention head geometry")
-        if self.num_attention_heads % self.num_key_value_heads:
-            raise ValueError("query heads must be divisible by key/value heads")
-        if self.num_memory_heads * self.head_dim <= 0:
-            raise ValueError("memory attention geometry must be positive")
-        if min(self.target_hidden_size, self.intermediate_size, self.num_memory_layers, self.num_seed_layers,
-               self.target_vocab_size, self.draft_vocab_size) <= 0:
-            raise ValueError("all architecture sizes must be positive")
-        if self.fusion_mode not in {"scalar", "gated_delta"}:
-            raise ValueError("fusion_mode must be scalar or gated_delta")
+        sizes = (self.target_hidden_size, self.intermediate_size, self.num_memory_layers, self.num_seed_layers,
+                 self.target_vocab_size, self.draft_vocab_size, self.num_memory_heads, self.head_dim)
+        problems = [message for failed, message in (
+            (self.num_attention_heads * self.head_dim != self.hidden_size,
+             "hidden_size must equal num_attention_heads * head_dim"),
+            (self.num_key_value_heads <= 0 or self.num_attention_heads % self.num_key_value_heads != 0,
+             "num_attention_heads must be a multiple of num_key_value_heads"),
+            (any(v <= 0 for v in sizes), "every architecture size must be positive"),
+            (self.fusion_mode not in FUSION_MODES, f"fusion_mode must be one of {sorted(FUSION_MODES)}"),
+        ) if failed]
+        if problems:
+            raise ValueError("; ".join(problems))
 
     def to_dict(self) -> dict[str, Any]:
         return asdict(self)
@@ -135,14 +142,27 @@ class EagleDraftLayer(nn.Module):
         return hidden, k, v
 
 
-#: Tensors an original EAGLE-3 checkpoint does not have (the adapter).
-def _adapter_only_names(num_memory_layers: int) -> set[str]:
-    names = {"adapter_scale", "draft_to_target", "target_to_draft", "memory_norm.weight",
-             "memory_attention.layer_gates", "stage_layer_bias.weight", "stage_layer_bias.bias",
-             "memory_gate.weight", "memory_gate.bias", "memory_delta.weight", "memory_delta.bias"}
-    names.update(f"memory_attention.{kind}.{i}.weight" for kind in ("query", "output")
-                 for i in range(num_memory_layers))
-    return names
+#: top-level modules and buffers of the EAGLE-3 trunk; everything else in the
+#: drafter's state dict is the adapter, which an EAGLE-3 checkpoint lacks
+EAGLE_TRUNK = frozenset({"midlayer", "fc", "norm", "lm_head", "d2t", "t2d"})
+
+
+def vocab_maps(offsets: torch.Tensor, target_vocab: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """EAGLE's compressed vocabulary: draft id i is target id i + offsets[i].
+
+    Returns (draft -> target ids, target -> draft ids with -1 for target ids
+    outside the draft vocabulary); refuses a map that is not one-to-one.
+    """
+    n = offsets.numel()
+    to_target = offsets.long() + torch.arange(n, device=offsets.device)
+    if int(to_target.min()) < 0 or int(to_target.max()) >= target_vocab:
+        raise ValueError("EAGLE compressed-vocabulary mapping leaves the target vocabulary")
+    hits = torch.bincount(to_target, minlength=target_vocab)
+    if int(hits.max()) > 1:
+        raise ValueError("EAGLE compressed-vocabulary mapping is not one-to-one")
+    to_draft = torch.full((target_vocab,), -1, dtype=torch.long, device=offsets.device)
+    to_draft.scatter_(0, to_target, torch.arange(n, device=offsets.device))
+    return to_target, to_draft
 
 
 class SparseKVEagleDrafter(nn.Module):
@@ -192,23 +212,23 @@ class SparseKVEagleDrafter(nn.Module):
             raise ValueError("target embedding shape is incompatible with EAGLE")
         object.__setattr__(self, "_target_embedding_weight", embedding_weight.detach())
 
+    def adapter_names(self) -> set[str]:
+        """State-dict entries outside the EAGLE-3 trunk (the sparse-KV adapter)."""
+        return {name for name in self.state_dict() if name.split(".", 1)[0] not in EAGLE_TRUNK}
+
     def load_eagle_checkpoint(self, checkpoint_path: str | Path) -> None:
-        """Load an EAGLE-3 state dict; only the adapter may be missing, nothing may be extra."""
+        """Load an EAGLE-3 checkpoint: exactly the trunk, nothing more, nothing less."""
         state = torch.load(checkpoint_path, map_location="cpu", weights_only=True)
-        missing, unexpected = self.load_state_dict(state, strict=False)
-        if set(missing) != _adapter_only_names(self.config.num_memory_layers) or unexpected:
-            raise ValueError(f"incompatible EAGLE checkpoint: missing={missing}, unexpected={unexpected}")
+        result = self.load_state_dict(state, strict=False)
+        if set(result.missing_keys) != self.adapter_names() or result.unexpected_keys:
+            raise ValueError(f"incompatible EAGLE checkpoint: missing={result.missing_keys}, "
+                             f"unexpected={result.unexpected_keys}")
         self._rebuild_vocab_maps()
 
     def _rebuild_vocab_maps(self) -> None:
-        dev = self.d2t.device
-        d2t = torch.arange(self.config.draft_vocab_size, device=dev) + self.d2t
-        if d2t.unique().numel() != d2t.numel():
-            raise ValueError("EAGLE compressed-vocabulary mapping is not one-to-one")
-        t2d = torch.full_like(self.target_to_draft, -1)
-        t2d[d2t] = torch.arange(self.config.draft_vocab_size, device=dev)
-        self.draft_to_target.copy_(d2t)
-        self.target_to_draft.copy_(t2d)
+        to_target, to_draft = vocab_maps(self.d2t, self.config.target_vocab_size)
+        self.draft_to_target.copy_(to_target)
+        self.target_to_draft.copy_(to_draft)
 
     def freeze_eagle(self) -> None:
         for module in (self.midlayer, self.fc, self.norm, self.lm_head):
@@ -219,8 +239,8 @@ class SparseKVEagleDrafter(nn.Module):
         return [p for p in self.parameters() if p.requires_grad]
 
     def adapter_state_dict(self) -> dict[str, torch.Tensor]:
-        trainable = {n for n, p in self.named_parameters() if p.requires_grad}
-        return {n: t.detach().cpu() for n, t in self.state_dict().items() if n in trainable}
+        """CPU copies of the trainable parameters (the adapter checkpoint payload)."""
+        return {name: p.detach().cpu() for name, p in self.named_parameters() if p.requires_grad}
 
     def target_ids(self, draft_ids: torch.Tensor) -> torch.Tensor:
         return self.draft_to_target[draft_ids]
@@ -229,19 +249,29 @@ class SparseKVEagleDrafter(nn.Module):
         return self.target_to_draft[target_ids]
 
     # ---------------------------------------------------------------- compute
+    def fuse(self, hidden: torch.Tensor, delta: torch.Tensor) -> torch.Tensor:
+        """What the memory read adds to the recurrent hidden state.
+
+        scalar:       s * delta
+        gated_delta:  s * g * W_d (delta - hidden),  g = sigmoid(W_g [hidden, delta, delta - hidden] + b_g)
+        with s = sigmoid(adapter_scale).  These are the semantics trained
+        adapters carry, so both implementations compute the same function.
+        """
+        s = torch.sigmoid(self.adapter_scale).to(hidden.dtype)
+        if self.config.fusion_mode == "scalar":
+            return s * delta
+        toward = delta - hidden
+        g = torch.sigmoid(self.memory_gate(torch.cat((hidden, delta, toward), dim=-1)))
+        return s * g * self.memory_delta(toward)
+
     def _memory_delta(self, hidden, memory_keys, memory_values, cos, sin, stage) -> torch.Tensor:
         """Adapter output for the current position.  ``stage`` is [B, 2] (or [1, 2])."""
-        stage_bias = self.stage_layer_bias(stage.float())  # [B, L]
-        if stage_bias.shape[0] == 1:
-            stage_bias = stage_bias.squeeze(0)
-        delta = self.memory_attention(self.memory_norm(hidden), memory_keys, memory_values, cos, sin,
-                                      layer_logits_bias=stage_bias)
-        scale = torch.sigmoid(self.adapter_scale).to(hidden.dtype)
-        if self.config.fusion_mode == "scalar":
-            return scale * delta
-        correction = delta - hidden
-        gate = torch.sigmoid(self.memory_gate(torch.cat((hidden, delta, correction), dim=-1)))
-        return scale * gate * self.memory_delta(correction)
+        layer_bias = self.stage_layer_bias(stage.float())  # [B, L]
+        if layer_bias.shape[0] == 1:
+            layer_bias = layer_bias[0]
+        read = self.memory_attention(self.memory_norm(hidden), memory_keys, memory_values, cos, sin,
+                                     layer_logits_bias=layer_bias)
+        return self.fuse(hidden, read)
 
     def init_state(self, seed_hidden: torch.Tensor):
         """Recurrent state before the first draft position: (fc(seeds), no KV)."""

@@ -17,7 +17,7 @@
 // Query rows can be gathered through q_rows (row r reads q[q_rows[r]]), so
 // the check layer attends only its active rows without a separate gather.
 //
-// CTA = 128 query rows of one q head (the tcgen05 M), 192 threads:
+// CTA = 128 query rows of one q head (the tcgen05 M), 320 threads:
 //   warp 0     TMA producer: K and V tiles of 128 keys (two 128-byte-swizzled
 //              boxes of 64 dims each) into a 2-deep ring; rows past n_keys
 //              are zero-filled by the tensor map, never read from the cache.
@@ -28,14 +28,17 @@
 //              MN-major B operand straight from its [keys][dims] tile.  QK of
 //              tile j+1 is issued before PV of tile j, so the tensor core
 //              works on the next scores while the softmax of this tile runs.
-//   warps 2-5  softmax + epilogue, one query row per thread (the TMEM lane
-//              of that row): tcgen05.ld the 128 scores, mask by nvis, online
-//              softmax in exp2 space, P_j as bf16 into the swizzled K-major
-//              smem tile, then one arrive.  The running max is rescaled
-//              lazily: O in TMEM is rescaled (tcgen05.ld/st) only when a
-//              warp's max grows by more than 2^8, so P stays <= 256 and most
-//              tiles touch O not at all.  The epilogue reads O once, divides
-//              by the row sum and stores bf16.
+//   warps 2-9  softmax + epilogue, two threads per query row (the TMEM lane
+//              of that row; warps 2-5 own key columns 0-63 of a tile, warps
+//              6-9 columns 64-127, so two warps share each TMEM lane quarter
+//              and hide each other's latency): tcgen05.ld 64 scores, mask by
+//              nvis, exchange the partial row max through shared memory,
+//              online softmax in exp2 space, P_j as bf16 into the swizzled
+//              K-major smem tile, then one arrive.  The running max is
+//              rescaled lazily: O in TMEM is rescaled (tcgen05.ld/st) only
+//              when a row max grows by more than 2^8, so P stays <= 256 and
+//              most tiles touch O not at all.  The epilogue adds the two
+//              halves' row sums, reads O once, divides and stores bf16.
 // TMEM: S[0] cols 0-127, S[1] cols 128-255, O cols 256-383 (512 allocated).
 // Shared memory: Q 32 KB + 2 x (K 32 KB + V 32 KB) + 2 x P 32 KB = 224 KB.
 // Every wait is bounded; an expired wait records a status code and the CTA
@@ -52,7 +55,7 @@ constexpr int kD = 128;
 constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kStages = 2;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr float kRescaleLog2 = 8.0f;
 
 constexpr int kQBytes = kBM * kD * 2;      // two 16 KB k-blocks (dims 0-63, 64-127)
@@ -64,7 +67,6 @@ constexpr int kOffK = kQBytes;
 constexpr int kOffV = kOffK + kStages * kKVBytes;
 constexpr int kOffP = kOffV + kStages * kKVBytes;
 constexpr int kOffBars = kOffP + 2 * kPBytes;
-constexpr int kSmemBytes = 1024 + kOffBars + 256;
 
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemO = 256;
@@ -79,10 +81,19 @@ struct alignas(8) AttnBars {
   uint64_t o_done;
   uint64_t o_final;
   uint64_t drain;
+  uint64_t mx_ready[2];  // the two column halves' partial row maxima of a tile are in smem
+  uint64_t l_ready;      // the two halves' partial row sums are in smem (epilogue)
   uint32_t tmem_base;
   int max_vis;
 };
 static_assert(sizeof(AttnBars) <= 256, "barrier block");
+constexpr int kOffRed = kOffBars + 256;  // float red_max[tile parity][half][row]
+constexpr int kRedBytes = 2 * 2 * kBM * 4;
+constexpr int kNeedBytes = kOffRed + kRedBytes;  // from the 1024-aligned base
+// the largest opt-in dynamic shared memory of a CTA; the base is aligned up
+// to 1024 inside it, which leaves kSmemBytes - kNeedBytes bytes of slack
+constexpr int kSmemBytes = 232448;
+static_assert(kNeedBytes <= kSmemBytes, "shared-memory plan");
 
 // 2^x by the MUFU ex2 instruction (flush-to-zero; 2^-inf = +0)
 __device__ __forceinline__ float exp2_approx(float x) {
@@ -107,6 +118,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~uintptr_t(1023));
   AttnBars* bars = reinterpret_cast<AttnBars*>(smem + kOffBars);
   int* status = p.status;
+  // the swizzled operand tiles need a 1024-byte aligned base; the dynamic
+  // window is aligned that way on sm_100, and if it ever were not by enough,
+  // the kernel reports it and does nothing rather than overrun shared memory
+  if ((smem - smem_raw) + kNeedBytes > kSmemBytes) {
+    if (threadIdx.x == 0) report_status(status, kStatusBadArgument);
+    return;
+  }
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -124,8 +142,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->s_full[b], 1);
-      mbar_init(&bars->p_full[b], 128);
+      mbar_init(&bars->p_full[b], 256);
+      mbar_init(&bars->mx_ready[b], 256);
     }
+    mbar_init(&bars->l_ready, 256);
     mbar_init(&bars->o_done, 1);
     mbar_init(&bars->o_final, 1);
     mbar_init(&bars->drain, 1);
@@ -139,26 +159,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
 
   // ---- softmax warps: stage the (gathered) Q tile, find each row's visible prefix ----
-  const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+  // warps 2-5 own key columns 0-63 of every tile, warps 6-9 columns 64-127;
+  // a warp reaches only TMEM lane quarter (warp % 4), so the two warps of a
+  // quarter share its 32 rows
+  const int quarter = warp & 3;
+  const int half = warp >= 6 ? 1 : 0;
   const int row = quarter * 32 + lane;  // tile row == TMEM lane (softmax warps only)
   int nvis = 0;
   if (warp >= 2) {
     const int g = r0 + row;
-    uint8_t* sq = smem;
+    uint8_t* sq = smem + half * (kBM * 128);  // this half stages dims [64 * half, 64 * half + 64)
     int qp = -1;
     if (g < p.n_rows) {
       qp = p.qpos[g];
       const int src = p.q_rows ? p.q_rows[g] : g;
-      const uint4* qsrc = reinterpret_cast<const uint4*>(p.q + (size_t)src * p.ldq + (size_t)h * kD);
+      const uint4* qsrc =
+          reinterpret_cast<const uint4*>(p.q + (size_t)src * p.ldq + (size_t)h * kD + half * 64);
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const uint4 v = qsrc[c];
-        *reinterpret_cast<uint4*>(sq + (c >> 3) * (kBM * 128) + sw128(row, c & 7)) = v;
-      }
+      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(sq + sw128(row, c)) = qsrc[c];
     } else {
 #pragma unroll
-      for (int c = 0; c < 16; ++c)
-        *reinterpret_cast<uint4*>(sq + (c >> 3) * (kBM * 128) + sw128(row, c & 7)) = make_uint4(0, 0, 0, 0);
+      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(sq + sw128(row, c)) = make_uint4(0, 0, 0, 0);
     }
     if (qp >= 0) {
       if (p.kpos == nullptr) {
@@ -266,9 +287,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(&bars->o_final);
     }
   } else {
-    // ---------------- softmax (warps 2-5) ----------------
+    // ---------------- softmax (warps 2-9: 64 key columns per thread) ----------------
+    constexpr int kHalf = kBN / 2;
+    float* red_max = reinterpret_cast<float*>(smem + kOffRed);  // [tile parity][half][row]
     const float c = p.scale * 1.4426950408889634f;
     const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t col0 = (uint32_t)(half * kHalf);  // my S columns / O columns within a tile
     float m_ref = -INFINITY;
     float l = 0.f;
     bool ok = true;
@@ -281,26 +305,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t sv[kBN];
-#pragma unroll
-      for (int q4 = 0; q4 < kBN / 32; ++q4)
-        tmem_ld_32x32b_x32(lane_base + b * kBN + q4 * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[q4 * 32]));
+      uint32_t sv[kHalf];
+      tmem_ld_32x32b_x32(lane_base + b * kBN + col0, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+      tmem_ld_32x32b_x32(lane_base + b * kBN + col0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
       tmem_ld_wait();
-      const int vis = nvis - j * kBN;  // keys [0, vis) of this tile are visible to my row
-      if (!__all_sync(0xffffffffu, vis >= kBN)) {
+      const int vis = nvis - j * kBN - half * kHalf;  // my columns [0, vis) are visible to my row
+      if (!__all_sync(0xffffffffu, vis >= kHalf)) {
 #pragma unroll
-        for (int i = 0; i < kBN; ++i)
+        for (int i = 0; i < kHalf; ++i)
           if (i >= vis) sv[i] = 0xff800000u;  // -inf
       }
       float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < kBN; i += 4) {
+      for (int i = 0; i < kHalf; i += 4) {
         mx0 = fmaxf(mx0, __uint_as_float(sv[i]));
         mx1 = fmaxf(mx1, __uint_as_float(sv[i + 1]));
         mx2 = fmaxf(mx2, __uint_as_float(sv[i + 2]));
         mx3 = fmaxf(mx3, __uint_as_float(sv[i + 3]));
       }
-      const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;
+      // the row max over both halves: exchange partial maxima through shared
+      // memory (slot by tile parity, so a slot is rewritten only after both
+      // halves passed the next tile's exchange)
+      float* slot = red_max + b * (2 * kBM);
+      slot[half * kBM + row] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      mbar_arrive(&bars->mx_ready[b]);
+      const bool both = mbar_wait(&bars->mx_ready[b], (uint32_t)(j >> 1) & 1u, status, kStatusTimeoutTmemFull);
+      if (!__all_sync(0xffffffffu, both)) {
+        ok = false;
+        break;
+      }
+      const float m_tile = fmaxf(slot[row], slot[kBM + row]) * c;
       const bool need = m_tile > m_ref + kRescaleLog2;  // false when the tile is fully masked
       float f = 1.f;
       if (need) {
@@ -308,9 +342,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_ref = m_tile;
         l *= f;
       }
-      // O holds P_0..P_{j-1} V: rescale it (warp-uniformly, tcgen05 ld/st are
-      // warp-collective) once PV(j-1) has completed.  s_full(j) implies PV(j-2)
-      // completed, so waiting on o_done's phase j-1 is unambiguous.
+      // O holds P_0..P_{j-1} V: rescale my 64 columns of it (warp-uniformly,
+      // tcgen05 ld/st are warp-collective) once PV(j-1) has completed.
+      // s_full(j) implies PV(j-2) completed, so o_done's phase j-1 is unambiguous.
       if (j > 0 && __any_sync(0xffffffffu, need)) {
         const bool done = mbar_wait(&bars->o_done, (uint32_t)(j - 1) & 1u, status, kStatusTimeoutTmemFull);
         if (!__all_sync(0xffffffffu, done)) {
@@ -319,9 +353,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
 #pragma unroll 1
-        for (int cc = 0; cc < kD / 32; ++cc) {
+        for (int cc = 0; cc < kHalf / 32; ++cc) {
           uint32_t o[32];
-          tmem_ld_32x32b_x32(lane_base + kTmemO + cc * 32, o);
+          const uint32_t at = lane_base + kTmemO + col0 + cc * 32;
+          tmem_ld_32x32b_x32(at, o);
           tmem_ld_wait();
           uint32_t lo[16], hi[16];
 #pragma unroll
@@ -329,22 +364,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             lo[i] = __float_as_uint(__uint_as_float(o[i]) * f);
             hi[i] = __float_as_uint(__uint_as_float(o[16 + i]) * f);
           }
-          tmem_st_32x32b_x16(lane_base + kTmemO + cc * 32, lo);
-          tmem_st_32x32b_x16(lane_base + kTmemO + cc * 32 + 16, hi);
+          tmem_st_32x32b_x16(at, lo);
+          tmem_st_32x32b_x16(at + 16, hi);
         }
         tmem_st_wait();
       }
       const float base = (m_ref == -INFINITY) ? 0.f : m_ref;
       float sum0 = 0.f, sum1 = 0.f;
-      uint8_t* sp = smem + kOffP + b * kPBytes;
+      uint8_t* sp = smem + kOffP + b * kPBytes + half * kPBlock;  // my 64 keys = one P k-block
 #pragma unroll
-      for (int cc = 0; cc < kBN / 8; ++cc) {  // 8 keys = one 16-byte chunk of the P row
+      for (int cc = 0; cc < kHalf / 8; ++cc) {  // 8 keys = one 16-byte chunk of the P row
         float e[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) e[i] = exp2_approx(fmaf(__uint_as_float(sv[8 * cc + i]), c, -base));
         sum0 += (e[0] + e[1]) + (e[2] + e[3]);
         sum1 += (e[4] + e[5]) + (e[6] + e[7]);
-        *reinterpret_cast<uint4*>(sp + (cc >> 3) * kPBlock + sw128(row, cc & 7)) =
+        *reinterpret_cast<uint4*>(sp + sw128(row, cc)) =
             make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
                        pack_bf16x2(e[6], e[7]));
       }
@@ -353,17 +388,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&bars->p_full[b]);
     }
-    // ---- epilogue: O / l -> bf16 ----
+    // ---- epilogue: O / (l of both halves) -> bf16, my 64 columns ----
+    // the row sums go to the max-exchange slot the last tile did not use: its
+    // previous readers all passed the last tile's exchange already
+    float* red_l = red_max + (n_tiles & 1) * (2 * kBM);
+    red_l[half * kBM + row] = l;
+    mbar_arrive(&bars->l_ready);
+    ok = ok && mbar_wait(&bars->l_ready, 0, status, kStatusTimeoutTmemFull);
+    const float l_row = red_l[row] + red_l[kBM + row];
     const int g = r0 + row;
     if (n_tiles > 0 && ok) ok = mbar_wait(&bars->o_final, 0, status, kStatusTimeoutTmemFull);
-    __nv_bfloat16* dst = p.out + (size_t)g * p.ldo + (size_t)h * kD;
+    __nv_bfloat16* dst = p.out + (size_t)g * p.ldo + (size_t)h * kD + col0;
     if (n_tiles > 0 && __all_sync(0xffffffffu, ok)) {
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
 #pragma unroll 1
-      for (int cc = 0; cc < kD / 32; ++cc) {
+      for (int cc = 0; cc < kHalf / 32; ++cc) {
         uint32_t o[32];
-        tmem_ld_32x32b_x32(lane_base + kTmemO + cc * 32, o);
+        tmem_ld_32x32b_x32(lane_base + kTmemO + col0 + cc * 32, o);
         tmem_ld_wait();
         if (g < p.n_rows) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 32);
@@ -378,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (g < p.n_rows && n_tiles == 0) {
       uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) d4[i] = make_uint4(0, 0, 0, 0);
+      for (int i = 0; i < 8; ++i) d4[i] = make_uint4(0, 0, 0, 0);
     }
   }
 

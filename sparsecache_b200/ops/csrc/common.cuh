@@ -1,8 +1,8 @@
 // Shared device helpers for the sm_100a kernels of sparsecache_b200.
 //
 // Everything here is written directly against the PTX ISA for sm_100a:
-// mbarriers, TMA tiled loads (cp.async.bulk.tensor, never with
-// .multicast::cluster), and the tcgen05 family (alloc / mma / commit / ld).
+// mbarriers, TMA tiled loads (cp.async.bulk.tensor into this CTA's own
+// shared memory only), and the tcgen05 family (alloc / mma / commit / ld).
 // Every spin-wait is bounded by a clock64 deadline; on expiry the waiting
 // thread records an error code in a device status word and the kernel winds
 // down instead of hanging the GPU.

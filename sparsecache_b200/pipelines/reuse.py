@@ -17,10 +17,12 @@ Parity with the reference's experiments/reuse_cacheblend_pipeline.py:
   * ``aggregate`` (experiments/aggregate_reuse_cacheblend_pipeline.py:46-229):
     token agreement with full prefill, TTFT and end-to-end latency
     distributions, paired bootstrap of the latency differences.
-The documents' K/V blocks are resident in HBM (the store's ``hbm`` tier), so
-a stage "arrival" is the on-device composition of its documents; the stage
-model runs this package's engine (composer, CacheBlend kernels, batched
-verifier).
+The documents' K/V blocks wait in pinned host memory (``--store-tier
+pinned``, the reference's CPU tier): the one-shot arm composes them over PCIe
+inside the request, and the progressive arm stages each stage's new
+documents H2D on a copy stream (``serving.doc_stager``), overlapped with the
+previous stage's work or serially, and compares the two.  The stage model
+runs this package's engine (composer, CacheBlend kernels, batched verifier).
 """
 from __future__ import annotations
 
@@ -84,40 +86,62 @@ def prepare_request(request: RAGRequest, *, question: str = "", schedule: str = 
 
 
 class EngineStageModel:
-    """Stage s = CacheBlend repair over the documents of ``selected_sets[s]`` (others zero).
+    """Stage s = CacheBlend repair of the prompt that holds only the documents arrived by stage s.
 
-    ``verify``/``draft``/``final_decode`` append the given token sequence with
-    the batched verifier (8 rows a pass) behind the stage's repaired prompt,
-    so every stage sees exactly prompt + sequence.
+    The stage prompt is prefix + ranked documents[:count_s] + question suffix,
+    with the suffix (and every appended token) at its FINAL global position,
+    so drafts made at an early stage line up with the full prompt; the
+    documents' K/V come from the ``PinnedDocumentStager`` arena (HBM) after
+    the stage's copy event.  ``verify``/``draft``/``final_decode`` append the
+    given token sequence with the batched verifier (8 rows a pass) behind the
+    stage's repaired prompt, through an identity slot map so the appended
+    rows sit right after the stage's slots while their RoPE positions are
+    global (reference cacheblend_repair with final_prompt_tokens,
+    experiments/reuse_cacheblend_pipeline.py:512-706).
     """
 
-    def __init__(self, server, prepared: PreparedRequest, *, document_blocks: Sequence[torch.Tensor]) -> None:
+    def __init__(self, server, prepared: PreparedRequest, *, stager, overlap: bool = True) -> None:
         self.server, self.eng = server, server.engine
         self.req = prepared.request
         self.sets = prepared.selected_sets
         self.n_stages = len(self.sets)
-        self.blocks = list(document_blocks)
+        self.stager = stager
+        self.overlap = overlap
         self.T = self.req.prompt_tokens
         self.slot = server.slot
-        self.ids = torch.tensor(self.req.prompt, dtype=torch.int32, device=self.eng.device)
+        dev = self.eng.device
+        self.view = torch.arange(self.slot.capacity, dtype=torch.int32, device=dev)
         self._stage = None
         self._first = None
+        self._len = 0
         self._appended: list[int] = []
         self.repairs = 0
+
+    def _stage_prompt(self, stage: int):
+        req = self.req
+        count = len(self.sets[stage])
+        docs = req.documents[:count]
+        body = tuple(req.prefix) + tuple(t for d in docs for t in d)
+        ids = body + tuple(req.suffix)
+        S = len(req.suffix)
+        gpos = list(range(len(body))) + list(range(self.T - S, self.T))
+        dev = self.eng.device
+        return (torch.tensor(ids, dtype=torch.int32, device=dev), torch.tensor(gpos, dtype=torch.int32, device=dev),
+                len(ids))
 
     def _repair(self, stage: int) -> None:
         if self._stage == stage:
             return
         eng, req = self.eng, self.req
         blend = self.server.blend
-        zero = {i for i in range(len(self.blocks)) if i not in self.sets[stage]}
-        blocks = [torch.zeros_like(b) if i in zero else b for i, b in enumerate(self.blocks)]
-        eng.compose(self.slot, blocks, first_slot=len(req.prefix), layer_begin=blend.check_layer)
-        h_a, A, _ = eng.cacheblend(self.ids, self.slot, prefix_tokens=len(req.prefix),
-                                   suffix_tokens=len(req.suffix), blend=blend)
+        self.stager.arrive(stage, overlap=self.overlap)
+        ids, gpos, n = self._stage_prompt(stage)
+        eng.compose(self.slot, self.stager.blocks(stage), first_slot=len(req.prefix), layer_begin=blend.check_layer)
+        h_a, A, _ = eng.cacheblend(ids, self.slot, prefix_tokens=len(req.prefix), suffix_tokens=len(req.suffix),
+                                   blend=blend, global_positions=gpos)
         b = eng.first_token(h_a[A - 1:A], position=self.T, max_new=1)
         self._first = int(b["tok"][0].item())
-        self._stage, self._appended = stage, []
+        self._stage, self._len, self._appended = stage, n, []
         self.repairs += 1
 
     def _append(self, seq: Sequence[int]) -> list[int]:
@@ -130,7 +154,8 @@ class EngineStageModel:
         for k in range(common, len(seq), 8):
             chunk = list(seq[k:k + 8])
             out = self.eng.verify(self.slot, torch.tensor(chunk, dtype=torch.int32, device=self.eng.device),
-                                  position=self.T + k)
+                                  position=self.T + k, slot_start=self._len + k, view=self.view,
+                                  n_visible=self._len + k)
             preds += out.cpu().tolist()
             self._appended += chunk
         return preds
@@ -157,34 +182,74 @@ class EngineStageModel:
         return self.draft(self.n_stages - 1, sequence, n)
 
 
-def run_progressive_cacheblend(server, prepared: PreparedRequest, document_blocks, *, draft_tokens: int,
-                               max_new_tokens: int, eos_ids=frozenset()) -> dict[str, Any]:
-    model = EngineStageModel(server, prepared, document_blocks=document_blocks)
+def host_blocks(server, request: RAGRequest, pinned_store=None) -> list[torch.Tensor]:
+    """Pinned host copies of the request's document blocks (the reuse pipeline's CPU tier)."""
+    out = []
+    for d in request.documents:
+        if pinned_store is not None and d in pinned_store:
+            out.append(pinned_store[d].kv)
+            continue
+        block = server.store[d].kv
+        out.append(block if block.device.type == "cpu" and block.is_pinned() else block.cpu().pin_memory())
+    return out
+
+
+def run_progressive_cacheblend(server, prepared: PreparedRequest, blocks_host, *, draft_tokens: int,
+                               max_new_tokens: int, eos_ids=frozenset(), overlap: bool = True) -> dict[str, Any]:
+    """One progressive run with the documents staged from pinned host memory (overlapped or serial)."""
+    from ..serving.doc_stager import PinnedDocumentStager
+
+    eng = server.engine
+    torch.cuda.synchronize(eng.device)
     t0 = time.perf_counter()
+    stager = PinnedDocumentStager(blocks_host, prepared.selected_sets, device=eng.device,
+                                  layer_begin=server.blend.check_layer)
+    model = EngineStageModel(server, prepared, stager=stager, overlap=overlap)
     out = progressive_commit_chain(model, commit_window=1, draft_tokens=draft_tokens, max_new_tokens=max_new_tokens,
                                    eos_ids=set(eos_ids))
-    torch.cuda.synchronize(server.engine.device)
-    return {"tokens": out.tokens, "response_ms": (time.perf_counter() - t0) * 1e3,
+    torch.cuda.synchronize(eng.device)
+    response_ms = (time.perf_counter() - t0) * 1e3
+    return {"tokens": out.tokens, "response_ms": response_ms,
             "first_draft_ms": out.first_draft_ms, "first_committed_ms": out.first_committed_ms,
             "verify_ms": out.verify_ms, "draft_ms": out.draft_ms, "final_decode_ms": out.final_decode_ms,
             "ignored_committed_flips": out.ignored_committed_flips, "stages": model.n_stages,
-            "repairs": model.repairs, "trace": out.trace}
+            "repairs": model.repairs, "trace": out.trace, "transfer": stager.finish(), "overlap": overlap}
 
 
 def evaluate_request(server, prepared: PreparedRequest, *, max_new_tokens: int, draft_tokens: int = 8,
-                     modes: Sequence[str] = ("full", "cacheblend", "progressive")) -> dict[str, Any]:
-    """Paired arms of one request: device-timed TTFT and end-to-end latency per arm."""
+                     modes: Sequence[str] = ("full", "cacheblend", "progressive"), pinned_store=None,
+                     serial: bool = True) -> dict[str, Any]:
+    """Paired arms of one request: device-timed TTFT and end-to-end latency per arm.
+
+    The progressive arm stages its documents from pinned host memory on a
+    copy stream; with ``serial`` it runs a second time with each stage's copy
+    started only when the stage begins, and the row records both response
+    times and whether the two produced the same tokens (they must).
+    """
     req = prepared.request
     row: dict[str, Any] = {"request_index": req.index, "prompt_tokens": req.prompt_tokens,
                            "document_tokens": req.document_tokens, "arms": {}}
     for mode in modes:
         if mode == "progressive":
-            blocks = [server.store[d].kv for d in req.documents]
+            blocks = host_blocks(server, req, pinned_store)
             res = run_progressive_cacheblend(server, prepared, blocks, draft_tokens=draft_tokens,
-                                             max_new_tokens=max_new_tokens, eos_ids=server.eos)
-            row["arms"][mode] = {"tokens": res["tokens"], "ttft_ms": res["first_committed_ms"],
-                                 "first_draft_ms": res["first_draft_ms"], "e2e_ms": res["response_ms"],
-                                 "ignored_committed_flips": res["ignored_committed_flips"]}
+                                             max_new_tokens=max_new_tokens, eos_ids=server.eos, overlap=True)
+            arm = {"tokens": res["tokens"], "ttft_ms": res["first_committed_ms"],
+                   "first_draft_ms": res["first_draft_ms"], "e2e_ms": res["response_ms"],
+                   "ignored_committed_flips": res["ignored_committed_flips"], "transfer": res["transfer"]}
+            if serial:
+                ser = run_progressive_cacheblend(server, prepared, blocks, draft_tokens=draft_tokens,
+                                                 max_new_tokens=max_new_tokens, eos_ids=server.eos, overlap=False)
+                arm.update(serial_response_ms=ser["response_ms"],
+                           serial_pipeline_token_match=ser["tokens"] == res["tokens"],
+                           serial_transfer=ser["transfer"])
+            row["arms"][mode] = arm
+        elif mode == "cacheblend" and pinned_store is not None:
+            # one-shot CacheBlend from the pinned tier: the composer reads the
+            # host blocks over PCIe inside the timed request
+            r = server.serve(req, mode=mode, store=pinned_store, max_new_tokens=max_new_tokens, sync=True)
+            row["arms"][mode] = {"tokens": list(r.token_ids), "ttft_ms": r.ttft_ms, "e2e_ms": r.response_ms,
+                                 "store_tier": "pinned"}
         else:
             r = server.serve(req, mode=mode, max_new_tokens=max_new_tokens, sync=True)
             row["arms"][mode] = {"tokens": list(r.token_ids), "ttft_ms": r.ttft_ms, "e2e_ms": r.response_ms}
@@ -233,6 +298,14 @@ def aggregate(rows: Sequence[dict], *, reference: str = "full", bootstrap_sample
             "ttft_gain_vs_reference_ms": {"mean": statistics.fmean(d_ttft) if d_ttft else math.nan,
                                           "ci95": _boot(d_ttft, bootstrap_samples)},
         }
+        serial = [r["arms"][a] for r in rr if "serial_response_ms" in r["arms"][a]]
+        if serial:  # overlapped vs serial staging of the progressive arm
+            gains = [x["serial_response_ms"] - x["e2e_ms"] for x in serial]
+            out["arms"][a]["serial_staging"] = {
+                "serial_e2e_ms": {"p50": _pct([x["serial_response_ms"] for x in serial], 0.5)},
+                "overlap_gain_ms": {"mean": statistics.fmean(gains), "ci95": _boot(gains, bootstrap_samples)},
+                "token_match_rate": statistics.fmean(bool(x["serial_pipeline_token_match"]) for x in serial),
+                "h2d_ms_mean": statistics.fmean(x["transfer"]["total_h2d_ms"] for x in serial)}
         scored = [r["arms"][a] for r in rr if "f1" in r["arms"][a]]
         if scored:  # dataset runs: short-answer quality
             out["arms"][a].update(em=statistics.fmean(x["em"] for x in scored),
@@ -371,6 +444,11 @@ def main(argv=None) -> None:
     p.add_argument("--answer-word-limit", type=int, default=5)
     p.add_argument("--model-dir", type=Path, default=None,
                    help="model directory (HF Llama / Mistral or this package's) instead of random-init --model")
+    p.add_argument("--store-tier", choices=("pinned", "hbm"), default="pinned",
+                   help="where reused document KV waits: pinned host memory (the reference's CPU tier; the "
+                        "one-shot arm composes from it over PCIe, the progressive arm stages it on a copy "
+                        "stream) or HBM")
+    p.add_argument("--no-serial", action="store_true", help="skip the serial-staging rerun of the progressive arm")
     p.add_argument("--output", type=Path, required=True)
     a = p.parse_args(argv)
     blend = blend_config_from_args(a)
@@ -396,6 +474,14 @@ def main(argv=None) -> None:
     server = RAGServer(eng, store, capacity=max(r.prompt_tokens for r in reqs) + a.max_new_tokens + 64,
                        blend=blend)
     server.produce(reqs)
+    pinned = None
+    if a.store_tier == "pinned":
+        # the reference's CPU tier: every document block in pinned host memory
+        pinned = DocumentKVStore(cfg, tier="pinned")
+        for r in reqs:
+            for d in r.documents:
+                if d not in pinned:
+                    pinned.put(d, store[d].kv)
     fractions = tuple(float(x) for x in a.fractions.split(","))
     rows = []
     with open(a.output, "w") as f:
@@ -406,13 +492,15 @@ def main(argv=None) -> None:
                                          "layer_document_trace": blend.layer_document_trace(cfg.n_layers),
                                          "layer_document_mean": blend.check_target(cfg.n_layers),
                                          "deviation_metric": blend.deviation_metric,
-                                         "max_new_tokens": a.max_new_tokens, "commit_window": 1}}) + "\n")
+                                         "max_new_tokens": a.max_new_tokens, "commit_window": 1,
+                                         "store_tier": a.store_tier, "serial_staging": not a.no_serial}}) + "\n")
         for i, r in enumerate(reqs):
             m = meta[i] if meta else {}
             prep = prepare_request(r, schedule=a.schedule, fractions=fractions, seed=i,
                                    question=m.get("question", ""), texts=m.get("texts"),
                                    supporting=m.get("supporting"))
-            row = evaluate_request(server, prep, max_new_tokens=a.max_new_tokens, draft_tokens=a.draft_tokens)
+            row = evaluate_request(server, prep, max_new_tokens=a.max_new_tokens, draft_tokens=a.draft_tokens,
+                                   pinned_store=pinned, serial=not a.no_serial)
             if m:
                 score_row(row, m, server.eos)
             if i >= a.warmup:

@@ -4,7 +4,8 @@ Behavioural parity with the reference's experiments/progressive_pd_proxy.py:
   * request validation of the proxy-owned ``sparsecache_*`` fields (mode
     baseline|progressive, visibility continuous|fixed_s1, max draft tokens,
     start fraction in (0, 1), request-scoped chunk priority, paired prefill
-    group) and greedy-only requests (:137-214);
+    group) and greedy-only requests (:137-214), written here as a table of
+    field rules (``FIELD_RULES``) applied by ``ProxyRequest.parse``;
   * the prefill request is the client request with ``max_tokens=1``,
     non-streaming, ``return_token_ids``; the seed token comes from
     ``choices[0].token_ids[0]`` (:123-135);
@@ -66,79 +67,127 @@ def build_config(args: argparse.Namespace) -> ProxyConfig:
 
 
 def prefill_fingerprint(endpoint: str, payload: dict[str, Any]) -> str:
-    blob = json.dumps({"endpoint": endpoint, "payload": payload}, sort_keys=True, separators=(",", ":"),
-                      ensure_ascii=False).encode()
-    return hashlib.sha256(blob).hexdigest()
+    """Identity of a prefill: sha256 of the canonical JSON of (endpoint, payload)."""
+    canonical = json.dumps([endpoint, payload], sort_keys=True, separators=(",", ":"), ensure_ascii=False)
+    return hashlib.sha256(canonical.encode("utf-8")).hexdigest()
 
 
 def extract_seed_token(response: dict[str, Any]) -> int:
-    try:
-        seed = response["choices"][0]["token_ids"][0]
-    except (KeyError, IndexError, TypeError) as exc:
-        raise RuntimeError("prefiller response did not contain choices[0].token_ids[0]; "
-                           "the prefiller must support return_token_ids") from exc
-    if not isinstance(seed, int) or isinstance(seed, bool):
-        raise TypeError("prefiller seed token ID is not an integer")
-    return seed
+    """The producer's first generated token: ``choices[0].token_ids[0]`` of its response."""
+    node: Any = response
+    for key in ("choices", 0, "token_ids", 0):
+        try:
+            node = node[key]
+        except (KeyError, IndexError, TypeError) as exc:
+            raise RuntimeError("the prefill response has no choices[0].token_ids[0] "
+                               "(the prefill worker must honour return_token_ids)") from exc
+    if type(node) is not int:
+        raise TypeError(f"the prefill seed token must be an integer, got {type(node).__name__}")
+    return node
 
 
-def _is_int(x) -> bool:
-    return isinstance(x, int) and not isinstance(x, bool)
+def _count(v: Any) -> bool:
+    return type(v) is int and v >= 1
+
+
+def _fraction(v: Any) -> bool:
+    return type(v) in (int, float) and 0.0 < float(v) < 1.0
+
+
+def _chunk_ids(v: Any) -> bool:
+    return v is None or (type(v) is list and len(v) > 0 and all(type(c) is int and c >= 0 for c in v)
+                         and len(set(v)) == len(v))
+
+
+def _label(v: Any) -> bool:
+    return v is None or (isinstance(v, str) and v.strip() != "")
+
+
+@dataclass(frozen=True)
+class FieldRule:
+    """One proxy-owned request field: its default (from the config) and its check."""
+
+    name: str
+    default: Callable[[ProxyConfig], Any]
+    valid: Callable[[Any], bool]
+    expect: str
+
+
+# the ``sparsecache_*`` fields a client may send; the proxy consumes them and
+# never forwards them to a worker
+FIELD_RULES = (
+    FieldRule("sparsecache_mode", lambda c: c.default_mode, lambda v: v in ("baseline", "progressive"),
+              "baseline or progressive"),
+    FieldRule("sparsecache_visibility_mode", lambda c: c.default_visibility_mode,
+              lambda v: v in ("continuous", "fixed_s1"), "continuous or fixed_s1"),
+    FieldRule("sparsecache_max_draft_tokens", lambda c: c.max_draft_tokens, _count, "a positive integer"),
+    FieldRule("sparsecache_start_fraction", lambda c: c.start_fraction, _fraction, "a number in (0, 1)"),
+    FieldRule("sparsecache_priority_chunks", lambda c: None, _chunk_ids, "unique non-negative integers"),
+    FieldRule("sparsecache_prefill_group", lambda c: None, _label, "a non-empty string"),
+)
+
+
+@dataclass(frozen=True)
+class ProxyRequest:
+    """A validated client request: the worker payload plus the proxy's settings."""
+
+    payload: dict[str, Any]
+    settings: dict[str, Any]
+
+    @classmethod
+    def parse(cls, request: dict[str, Any], config: ProxyConfig) -> "ProxyRequest":
+        payload = dict(request)
+        settings = {}
+        for rule in FIELD_RULES:
+            value = payload.pop(rule.name, rule.default(config))
+            if not rule.valid(value):
+                raise ValueError(f"{rule.name} must be {rule.expect}")
+            settings[rule.name[len("sparsecache_"):]] = value
+        if config.require_greedy and float(payload.get("temperature", 1.0)) != 0.0:
+            raise ValueError("only greedy requests are served (the correctness gate needs temperature=0)")
+        return cls(payload, settings)
+
+    @property
+    def mode(self) -> str:
+        return self.settings["mode"]
+
+    def prefill_payload(self) -> dict[str, Any]:
+        """One non-streamed token whose id comes back (the seed)."""
+        out = {k: v for k, v in self.payload.items() if k != "stream_options"}
+        out.update(max_tokens=1, stream=False, return_token_ids=True)
+        if "max_completion_tokens" in out:
+            out["max_completion_tokens"] = 1
+        return out
+
+    def decode_payload(self, seed_token_id: int | None) -> dict[str, Any]:
+        """The client request plus the proxy-owned ``kv_transfer_params`` entries."""
+        out = dict(self.payload)
+        client_params = dict(out.get("kv_transfer_params") or {})
+        progressive = self.mode == "progressive"
+        if progressive and seed_token_id is None:
+            raise ValueError("progressive mode requires the exact prefiller seed")
+        owned: dict[str, Any] = {"require_full_remote_kv": True}
+        if progressive:
+            owned["progressive_sparse_draft"] = {
+                "seed_token_id": seed_token_id, "max_draft_tokens": self.settings["max_draft_tokens"],
+                "start_fraction": float(self.settings["start_fraction"]),
+                "visibility_mode": self.settings["visibility_mode"]}
+        elif seed_token_id is not None:
+            owned["producer_seed_token_id"] = seed_token_id
+        taken = sorted(k for k in owned if k in client_params)
+        if taken:
+            raise ValueError(f"kv_transfer_params.{taken[0]} is proxy-owned")
+        if progressive and self.settings["priority_chunks"] is not None:
+            owned["progressive_priority_chunks"] = self.settings["priority_chunks"]
+        if progressive or seed_token_id is not None:
+            out["kv_transfer_params"] = {**client_params, **owned}
+        return out
 
 
 def prepare_requests(request: dict[str, Any], config: ProxyConfig, seed_token_id: int | None):
-    """Split a client request into (prefill payload, decode payload, mode)."""
-    payload = dict(request)
-    mode = payload.pop("sparsecache_mode", config.default_mode)
-    visibility = payload.pop("sparsecache_visibility_mode", config.default_visibility_mode)
-    gamma = payload.pop("sparsecache_max_draft_tokens", config.max_draft_tokens)
-    start = payload.pop("sparsecache_start_fraction", config.start_fraction)
-    priority = payload.pop("sparsecache_priority_chunks", None)
-    group = payload.pop("sparsecache_prefill_group", None)
-    if mode not in ("baseline", "progressive"):
-        raise ValueError("sparsecache_mode must be baseline or progressive")
-    if visibility not in ("continuous", "fixed_s1"):
-        raise ValueError("sparsecache_visibility_mode must be continuous or fixed_s1")
-    if not _is_int(gamma) or gamma < 1:
-        raise ValueError("sparsecache_max_draft_tokens must be a positive integer")
-    if isinstance(start, bool) or not isinstance(start, (int, float)) or not 0.0 < float(start) < 1.0:
-        raise ValueError("sparsecache_start_fraction must lie in (0, 1)")
-    if priority is not None and (not isinstance(priority, list) or not priority
-                                 or any(not _is_int(c) or c < 0 for c in priority)
-                                 or len(priority) != len(set(priority))):
-        raise ValueError("sparsecache_priority_chunks must be unique non-negative integers")
-    if group is not None and (not isinstance(group, str) or not group.strip()):
-        raise ValueError("sparsecache_prefill_group must be a non-empty string")
-    if config.require_greedy and float(payload.get("temperature", 1.0)) != 0.0:
-        raise ValueError("the correctness gate requires temperature=0")
-    pre = dict(payload)
-    pre["max_tokens"] = 1
-    if "max_completion_tokens" in pre:
-        pre["max_completion_tokens"] = 1
-    pre["stream"] = False
-    pre.pop("stream_options", None)
-    pre["return_token_ids"] = True
-    dec = dict(payload)
-    params = dict(dec.get("kv_transfer_params") or {})
-    if "require_full_remote_kv" in params:
-        raise ValueError("kv_transfer_params.require_full_remote_kv is proxy-owned")
-    params["require_full_remote_kv"] = True
-    if mode == "progressive":
-        if seed_token_id is None:
-            raise ValueError("progressive mode requires the exact prefiller seed")
-        if "progressive_sparse_draft" in params:
-            raise ValueError("kv_transfer_params.progressive_sparse_draft is proxy-owned")
-        params["progressive_sparse_draft"] = {"seed_token_id": seed_token_id, "max_draft_tokens": gamma,
-                                              "start_fraction": float(start), "visibility_mode": visibility}
-        if priority is not None:
-            params["progressive_priority_chunks"] = priority
-        dec["kv_transfer_params"] = params
-    elif seed_token_id is not None:
-        if "producer_seed_token_id" in params:
-            raise ValueError("kv_transfer_params.producer_seed_token_id is proxy-owned")
-        params["producer_seed_token_id"] = seed_token_id
-        dec["kv_transfer_params"] = params
-    return pre, dec, mode
+    """(prefill payload, decode payload, mode) of one client request."""
+    parsed = ProxyRequest.parse(request, config)
+    return parsed.prefill_payload(), parsed.decode_payload(seed_token_id), parsed.mode
 
 
 @dataclass(frozen=True)

@@ -4,6 +4,7 @@ tests/test_sparse_kv_eagle.py), plus the batched recurrence and memory
 batches this package adds."""
 from pathlib import Path
 
+import pytest
 import torch
 
 from sparsecache_b200.models.sparse_kv_draft import (
@@ -239,3 +240,27 @@ def test_tp_drafter_shards_reassemble_the_module():
 
     with pytest.raises(ValueError):
         TPDraftWeights.from_module(m, 0, 3, "cpu")
+
+
+def test_eagle_adapter_names_and_vocab_rules():
+    """The adapter (what an EAGLE-3 checkpoint lacks) is exactly this set of
+    names, for any number of memory layers; the vocabulary map must stay in
+    range and be one-to-one."""
+    from sparsecache_b200.models.sparse_kv_eagle import vocab_maps
+
+    for layers in (1, 3):
+        cfg = SparseKVEagleConfig(**{**_eagle_cfg().to_dict(), "num_memory_layers": layers})
+        names = SparseKVEagleDrafter(cfg).adapter_names()
+        expect = {"adapter_scale", "draft_to_target", "target_to_draft", "memory_norm.weight",
+                  "memory_attention.layer_gates", "stage_layer_bias.weight", "stage_layer_bias.bias",
+                  "memory_gate.weight", "memory_gate.bias", "memory_delta.weight", "memory_delta.bias"}
+        expect |= {f"memory_attention.{k}.{i}.weight" for k in ("query", "output") for i in range(layers)}
+        assert names == expect
+    to_t, to_d = vocab_maps(torch.tensor([0, 1, 1, 5]), 10)
+    assert to_t.tolist() == [0, 2, 3, 8] and to_d.tolist() == [0, -1, 1, 2, -1, -1, -1, -1, 3, -1]
+    with pytest.raises(ValueError, match="one-to-one"):
+        vocab_maps(torch.tensor([1, 0]), 4)
+    with pytest.raises(ValueError, match="target vocabulary"):
+        vocab_maps(torch.tensor([0, 9]), 4)
+    with pytest.raises(ValueError, match="multiple of num_key_value_heads"):
+        SparseKVEagleConfig(**{**_eagle_cfg().to_dict(), "num_key_value_heads": 3})
