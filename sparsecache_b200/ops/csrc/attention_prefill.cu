@@ -95,6 +95,16 @@ constexpr int kNeedBytes = kOffRed + kRedBytes;  // from the 1024-aligned base
 constexpr int kSmemBytes = 232448;
 static_assert(kNeedBytes <= kSmemBytes, "shared-memory plan");
 
+// Optional debug timeline of one CTA (head 0, the first scheduled row tile):
+// trace[tile * 10 + event] = globaltimer ns; tile 63 holds kernel-level events.
+__device__ __forceinline__ void trace_at(const AttnPrefillArgs& p, int tile, int event) {
+  if (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && tile < 64) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    p.trace[tile * 10 + event] = t;
+  }
+}
+
 // 2^x by the MUFU ex2 instruction (flush-to-zero; 2^-inf = +0)
 __device__ __forceinline__ float exp2_approx(float x) {
   float y;
@@ -134,6 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int r0 = (n_row_tiles - 1 - (int)blockIdx.y) * kBM;  // longest row tiles first
 
   if (threadIdx.x == 0) {
+    trace_at(p, 63, 0);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);
@@ -206,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
   const int n_tiles = (bars->max_vis + kBN - 1) / kBN;
+  if (threadIdx.x == 0) trace_at(p, 63, 1);
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -221,11 +233,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&bars->k_full[s], kKVBytes);
         tma_load_3d(sk, &tm_k, &bars->k_full[s], 0, j * kBN, kvh);
         tma_load_3d(sk + kHalfBytes, &tm_k, &bars->k_full[s], 64, j * kBN, kvh);
+        trace_at(p, j, 0);
         k_last[s] = (int)ph;
         if (!mbar_wait(&bars->v_empty[s], ph ^ 1u, status, kStatusTimeoutSmemEmpty)) break;
         mbar_arrive_expect_tx(&bars->v_full[s], kKVBytes);
         tma_load_3d(sv, &tm_v, &bars->v_full[s], 0, j * kBN, kvh);
         tma_load_3d(sv + kHalfBytes, &tm_v, &bars->v_full[s], 64, j * kBN, kvh);
+        trace_at(p, j, 1);
         v_last[s] = (int)ph;
       }
       // every TMA load issued must land before the CTA exits
@@ -256,6 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_commit(&bars->s_full[j & 1]);
         tc_commit(&bars->k_empty[s]);
+        trace_at(p, j, 2);
         return true;
       };
       ok = issue_qk(0);
@@ -266,6 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        trace_at(p, j, 3);
         if (!mbar_wait(&bars->v_full[s], (uint32_t)(j / kStages) & 1u, status, kStatusTimeoutTmaFull)) {
           ok = false;
           break;
@@ -281,6 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_commit(&bars->o_done);
         tc_commit(&bars->v_empty[s]);
+        trace_at(p, j, 4);
       }
       // o_final completes once every MMA above has completed (also on the
       // error path, so the epilogue and the teardown never read a live TMEM)
@@ -304,11 +321,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
+      if (warp == 2 && lane == 0) trace_at(p, j, 5);
       tc_fence_after();
       uint32_t sv[kHalf];
       tmem_ld_32x32b_x32(lane_base + b * kBN + col0, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
       tmem_ld_32x32b_x32(lane_base + b * kBN + col0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
       tmem_ld_wait();
+      if (warp == 2 && lane == 0) trace_at(p, j, 6);
       const int vis = nvis - j * kBN - half * kHalf;  // my columns [0, vis) are visible to my row
       if (!__all_sync(0xffffffffu, vis >= kHalf)) {
 #pragma unroll
@@ -334,6 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
+      if (warp == 2 && lane == 0) trace_at(p, j, 7);
       const float m_tile = fmaxf(slot[row], slot[kBM + row]) * c;
       const bool need = m_tile > m_ref + kRescaleLog2;  // false when the tile is fully masked
       float f = 1.f;
@@ -384,9 +404,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                        pack_bf16x2(e[6], e[7]));
       }
       l += sum0 + sum1;
+      if (warp == 2 && lane == 0) trace_at(p, j, 8);
       fence_proxy_async_smem();  // P written by threads, read by the tensor core
       tc_fence_before();
       mbar_arrive(&bars->p_full[b]);
+      if (warp == 2 && lane == 0) trace_at(p, j, 9);
     }
     // ---- epilogue: O / (l of both halves) -> bf16, my 64 columns ----
     // the row sums go to the max-exchange slot the last tile did not use: its
@@ -398,6 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float l_row = red_l[row] + red_l[kBM + row];
     const int g = r0 + row;
     if (n_tiles > 0 && ok) ok = mbar_wait(&bars->o_final, 0, status, kStatusTimeoutTmemFull);
+    if (warp == 2 && lane == 0) trace_at(p, 63, 2);
     __nv_bfloat16* dst = p.out + (size_t)g * p.ldo + (size_t)h * kD + col0;
     if (n_tiles > 0 && __all_sync(0xffffffffu, ok)) {
       tc_fence_after();
@@ -431,6 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+  if (threadIdx.x == 0) trace_at(p, 63, 3);
 }
 
 cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream) {

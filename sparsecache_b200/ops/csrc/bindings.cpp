@@ -515,7 +515,8 @@ void gemv_argmax(Tensor x, Tensor w, c10::optional<Tensor> norm_w, double eps, T
 // ----------------------------------------------------------- attention
 void attention_prefill_impl(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tensor k_cache,
                             Tensor v_cache, c10::optional<Tensor> kpos, int64_t n_keys,
-                            int64_t n_heads, double scale, Tensor out, bool legacy) {
+                            int64_t n_heads, double scale, Tensor out, bool legacy,
+                            c10::optional<Tensor> trace = c10::nullopt) {
   const c10::cuda::CUDAGuard guard(q.device());
   check_matrix(q, "q");
   check_matrix(out, "out");
@@ -549,6 +550,11 @@ void attention_prefill_impl(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos,
   p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   p.ldo = (int)out.stride(0);
   p.status = status_tensor(q).data_ptr<int>();
+  if (trace.has_value() && trace->defined()) {
+    TORCH_CHECK(trace->scalar_type() == torch::kInt64 && trace->numel() >= 640 && trace->is_cuda(),
+                "trace must be a CUDA int64 tensor of >= 640 entries");
+    p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  }
   TORCH_CHECK(k_cache.is_cuda() && v_cache.is_cuda(), "caches must be CUDA tensors");
   CHECK_BF16(k_cache); CHECK_BF16(v_cache);
   CHECK_ALIGN16(k_cache); CHECK_ALIGN16(v_cache);
@@ -563,8 +569,8 @@ void attention_prefill_impl(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos,
 
 void attention_prefill(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tensor k_cache,
                        Tensor v_cache, c10::optional<Tensor> kpos, int64_t n_keys,
-                       int64_t n_heads, double scale, Tensor out) {
-  attention_prefill_impl(q, q_rows, qpos, k_cache, v_cache, kpos, n_keys, n_heads, scale, out, false);
+                       int64_t n_heads, double scale, Tensor out, c10::optional<Tensor> trace) {
+  attention_prefill_impl(q, q_rows, qpos, k_cache, v_cache, kpos, n_keys, n_heads, scale, out, false, trace);
 }
 
 void attention_prefill_mma(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tensor k_cache,
@@ -1097,7 +1103,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("token_log"), py::arg("gen_count"), py::arg("embed"), py::arg("next_hidden"),
         py::arg("pos_advance"), py::arg("n_advance") = 1);
   m.def("gemv_argmax_grid", &gemv_argmax_grid);
-  m.def("attention_prefill", &attention_prefill);
+  m.def("attention_prefill", &attention_prefill, py::arg("q"), py::arg("q_rows"), py::arg("qpos"),
+        py::arg("k_cache"), py::arg("v_cache"), py::arg("kpos"), py::arg("n_keys"), py::arg("n_heads"),
+        py::arg("scale"), py::arg("out"), py::arg("trace") = py::none());
   m.def("attention_prefill_mma", &attention_prefill_mma);
   m.def("attention_decode", &attention_decode, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("pos"), py::arg("n_heads"), py::arg("scale"), py::arg("splits"), py::arg("out"),

@@ -361,6 +361,9 @@ __global__ void __launch_bounds__(kThreads)
       if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
     }
     if (lane == 0) {
+      // no logit compared (all NaN): report token 0, never an index past the
+      // vocabulary (the token feeds the embedding load below)
+      if (bi < 0 || bi >= a.N) bi = 0;
       a.out_token[warp] = bi;
       s_bidx[0][warp] = bi;
     }

@@ -166,6 +166,7 @@ struct AttnPrefillArgs {
   __nv_bfloat16* out;  // [n_rows, n_heads*128]
   int ldo;
   int* status;  // bounded-wait status word
+  unsigned long long* trace;  // optional debug timeline (640 entries), null in production
 };
 
 cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream);

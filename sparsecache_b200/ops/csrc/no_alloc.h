@@ -18,7 +18,8 @@
 //   * Inputs: x [M, K] bf16 row-major (row stride K), w [N, K] bf16 row-major,
 //     norm_w [K] bf16 or NULL (then x is used without RMSNorm), eps.
 //     Output: out_token [M] int32 (device memory), the index of the largest
-//     bf16-rounded logit of each row, lowest index on ties.
+//     bf16-rounded logit of each row, lowest index on ties (0 for a row none
+//     of whose logits compares, i.e. all NaN).
 //   * Pointers: x, w and norm_w (when given) must be 16-byte aligned device
 //     addresses (the kernel reads them with 16-byte vector loads; a row-major
 //     view that starts at a multiple of 8 elements of an aligned buffer

@@ -298,7 +298,7 @@ __global__ void row_argmax_kernel(const __nv_bfloat16* logits, int ld, int V, in
     bv = sv[0], bi = si[0];
     for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
       if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) bv = sv[w], bi = si[w];
-    out[blockIdx.x] = bi;
+    out[blockIdx.x] = (bi < 0 || bi >= V) ? 0 : bi;  // all-NaN row: token 0, never out of range
   }
 }
 

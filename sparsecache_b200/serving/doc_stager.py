@@ -75,9 +75,16 @@ class PinnedDocumentStager:
         return sum(self.host[i][lb:].numel() * self.host[i].element_size() for i in self.stages[stage])
 
     def launch(self, stage: int) -> None:
-        """Queue the stage's new documents on the copy stream (idempotent)."""
+        """Queue the stage's new documents on the copy stream (idempotent).
+
+        Earlier stages that were never launched are queued first: a stage's
+        view is the whole ranked prefix, so its documents must all arrive.
+        """
         if self.launched[stage]:
             return
+        for earlier in range(stage):
+            if not self.launched[earlier]:
+                self.launch(earlier)
         # the arena may still be read by compute work queued before this
         # launch (an earlier request's stages): order the copies after it
         self.stream.wait_stream(torch.cuda.current_stream(self.device))
@@ -90,9 +97,10 @@ class PinnedDocumentStager:
         self.launched[stage] = True
 
     def wait(self, stage: int) -> None:
-        """Make the current (compute) stream wait for the stage's copies."""
+        """Make the current (compute) stream wait for the stage's copies (and the earlier stages')."""
         if not self.launched[stage]:
             raise RuntimeError(f"stage {stage} was not launched")
+        # one copy stream in launch order: the stage's end event follows every earlier copy
         torch.cuda.current_stream(self.device).wait_event(self.ends[stage])
 
     def arrive(self, stage: int, *, overlap: bool) -> None:

@@ -120,14 +120,14 @@ def main() -> None:
                 res[f"gemm_M{M}_{name}"] = {"us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS,
                                             "weight_GBps": N * K * 2 / (t * 1e-6) / 1e9}
 
-    if "gemm_small" in only or "gemm_down_splitk" in only:
+    if "gemm_small" in only or "gemm_down_splitk" in only or "gemm_gate_up" in only:
         # CacheBlend active rows (~15% of a 1.7k-token prompt): the layer's four
         # projections as the engine issues them (128-wide QKV tiles, split-K o/down)
         M = 300
         cases = (("qkv_bn128", 6144, 4096, "store", 128), ("o_splitk", 4096, 4096, "residual", 256),
                  ("gate_up", 28672, 4096, "swiglu", 256), ("down_splitk", 4096, 14336, "residual", 256))
         if "gemm_small" not in only:
-            cases = cases[3:]
+            cases = cases[3:] if "gemm_down_splitk" in only else cases[2:3]
         for name, N, K, kind, bn in cases:
             a = torch.randn(M, K, device=dev).to(bf)
             w = (torch.randn(N, K, device=dev) * 0.02).to(bf)
@@ -222,6 +222,29 @@ def main() -> None:
                 t = timeit(lambda: fn(q, rows, qpos, kc, vc, None, T, H, 1 / math.sqrt(128), out), n=20)
                 tf = flops / (t * 1e-6) / 1e12
                 res[f"{kern}_{name}_T{T}"] = {"us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS}
+    if "attn_trace" in only:
+        # timeline of one CTA (head 0, the longest row tile) of the causal case
+        H, Hkv, T = 32, 8, 1676
+        kc = torch.randn(Hkv, T, 128, device=dev).to(bf)
+        vc = torch.randn(Hkv, T, 128, device=dev).to(bf)
+        q = torch.randn(T, H * 128, device=dev).to(bf)
+        pos = torch.arange(T, device=dev, dtype=torch.int32)
+        out = torch.empty(T, H * 128, device=dev, dtype=bf)
+        tr = torch.zeros(640, device=dev, dtype=torch.int64)
+        for _ in range(3):
+            ext.attention_prefill(q, None, pos, kc, vc, None, T, H, 1 / math.sqrt(128), out, trace=tr)
+        torch.cuda.synchronize()
+        t = tr.view(64, 10).cpu()
+        t0 = int(t[63, 0])
+        names = ("K_issued", "V_issued", "QK_issued", "P_ready_seen", "PV_issued", "S_ready_seen", "S_in_regs",
+                 "max_exchanged", "P_written", "P_arrived")
+        rows = {}
+        for j in range(63):
+            if int(t[j].abs().sum()) == 0:
+                continue
+            rows[j] = {n: (int(t[j, e]) - t0) / 1000.0 for e, n in enumerate(names) if int(t[j, e])}
+        res["attn_trace_us_from_cta_start"] = {"tiles": rows, "kernel": {
+            n: (int(t[63, e]) - t0) / 1000.0 for e, n in enumerate(("start", "prologue_done", "o_final_seen", "end"))}}
     if "attn_prefill" in only:
         H, Hkv = 32, 8
         for T in (2048, 16384):
