@@ -17,7 +17,11 @@
 // Query rows can be gathered through q_rows (row r reads q[q_rows[r]]), so
 // the check layer attends only its active rows without a separate gather.
 //
-// CTA = 128 query rows of one q head (the tcgen05 M), 320 threads:
+// CTA = one kv head and 128 / G query positions, where G query heads share
+// the kv head: the 128 rows of the tcgen05 tile are (query head g, position
+// i) pairs, so every K/V tile is loaded once for the whole GQA group (a
+// kv-head-major packing; K/V traffic from L2 drops by G against one CTA per
+// query head).  192 threads:
 //   warp 0     TMA producer: K and V tiles of 128 keys (two 128-byte-swizzled
 //              boxes of 64 dims each) into a 2-deep ring; rows past n_keys
 //              are zero-filled by the tensor map, never read from the cache.
@@ -28,17 +32,14 @@
 //              MN-major B operand straight from its [keys][dims] tile.  QK of
 //              tile j+1 is issued before PV of tile j, so the tensor core
 //              works on the next scores while the softmax of this tile runs.
-//   warps 2-9  softmax + epilogue, two threads per query row (the TMEM lane
-//              of that row; warps 2-5 own key columns 0-63 of a tile, warps
-//              6-9 columns 64-127, so two warps share each TMEM lane quarter
-//              and hide each other's latency): tcgen05.ld 64 scores, mask by
-//              nvis, exchange the partial row max through shared memory,
-//              online softmax in exp2 space, P_j as bf16 into the swizzled
-//              K-major smem tile, then one arrive.  The running max is
-//              rescaled lazily: O in TMEM is rescaled (tcgen05.ld/st) only
-//              when a row max grows by more than 2^8, so P stays <= 256 and
-//              most tiles touch O not at all.  The epilogue adds the two
-//              halves' row sums, reads O once, divides and stores bf16.
+//   warps 2-5  softmax + epilogue, one tile row per thread (its TMEM lane):
+//              tcgen05.ld the 128 scores, mask by nvis, online softmax in
+//              exp2 space, P_j as bf16 into the swizzled K-major smem tile,
+//              then one arrive.  The running max is rescaled lazily: O in
+//              TMEM is rescaled (tcgen05.ld/st) only when a row max grows by
+//              more than 2^8, so P stays <= 256 and most tiles touch O not at
+//              all.  The epilogue reads O once, divides by the row sum and
+//              stores bf16.
 // TMEM: S[0] cols 0-127, S[1] cols 128-255, O cols 256-383 (512 allocated).
 // Shared memory: Q 32 KB + 2 x (K 32 KB + V 32 KB) + 2 x P 32 KB = 224 KB.
 // Every wait is bounded; an expired wait records a status code and the CTA
@@ -55,7 +56,7 @@ constexpr int kD = 128;
 constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kStages = 2;
-constexpr int kThreads = 320;
+constexpr int kThreads = 192;
 constexpr float kRescaleLog2 = 8.0f;
 
 constexpr int kQBytes = kBM * kD * 2;      // two 16 KB k-blocks (dims 0-63, 64-127)
@@ -81,21 +82,17 @@ struct alignas(8) AttnBars {
   uint64_t o_done;
   uint64_t o_final;
   uint64_t drain;
-  uint64_t mx_ready[2];  // the two column halves' partial row maxima of a tile are in smem
-  uint64_t l_ready;      // the two halves' partial row sums are in smem (epilogue)
   uint32_t tmem_base;
   int max_vis;
 };
 static_assert(sizeof(AttnBars) <= 256, "barrier block");
-constexpr int kOffRed = kOffBars + 256;  // float red_max[tile parity][half][row]
-constexpr int kRedBytes = 2 * 2 * kBM * 4;
-constexpr int kNeedBytes = kOffRed + kRedBytes;  // from the 1024-aligned base
+constexpr int kNeedBytes = kOffBars + 256;  // from the 1024-aligned base
 // the largest opt-in dynamic shared memory of a CTA; the base is aligned up
 // to 1024 inside it, which leaves kSmemBytes - kNeedBytes bytes of slack
 constexpr int kSmemBytes = 232448;
 static_assert(kNeedBytes <= kSmemBytes, "shared-memory plan");
 
-// Optional debug timeline of one CTA (head 0, the first scheduled row tile):
+// Optional debug timeline of one CTA (kv head 0, the first scheduled row tile):
 // trace[tile * 10 + event] = globaltimer ns; tile 63 holds kernel-level events.
 __device__ __forceinline__ void trace_at(const AttnPrefillArgs& p, int tile, int event) {
   if (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && tile < 64) {
@@ -138,10 +135,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = warp_id();
   const int lane = lane_id();
-  const int h = blockIdx.x;
-  const int kvh = h / (p.n_heads / p.n_kv_heads);
+  const int kvh = blockIdx.x;
+  const int G = p.n_heads / p.n_kv_heads;  // query heads per kv head (divides 128)
+  const int span = kBM / G;                // query positions per CTA
   const int n_row_tiles = gridDim.y;
-  const int r0 = (n_row_tiles - 1 - (int)blockIdx.y) * kBM;  // longest row tiles first
+  const int r0 = (n_row_tiles - 1 - (int)blockIdx.y) * span;  // longest row tiles first
 
   if (threadIdx.x == 0) {
     trace_at(p, 63, 0);
@@ -153,10 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->s_full[b], 1);
-      mbar_init(&bars->p_full[b], 256);
-      mbar_init(&bars->mx_ready[b], 256);
+      mbar_init(&bars->p_full[b], 128);
     }
-    mbar_init(&bars->l_ready, 256);
     mbar_init(&bars->o_done, 1);
     mbar_init(&bars->o_final, 1);
     mbar_init(&bars->drain, 1);
@@ -170,27 +166,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
 
   // ---- softmax warps: stage the (gathered) Q tile, find each row's visible prefix ----
-  // warps 2-5 own key columns 0-63 of every tile, warps 6-9 columns 64-127;
-  // a warp reaches only TMEM lane quarter (warp % 4), so the two warps of a
-  // quarter share its 32 rows
-  const int quarter = warp & 3;
-  const int half = warp >= 6 ? 1 : 0;
-  const int row = quarter * 32 + lane;  // tile row == TMEM lane (softmax warps only)
+  // tile row = TMEM lane = warp quarter * 32 + lane; row -> (query head
+  // kvh * G + row / span, position r0 + row % span)
+  const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+  const int row = quarter * 32 + lane;
+  const int head = kvh * G + row / span;
+  const int g = r0 + row % span;  // query row index of this tile row
   int nvis = 0;
   if (warp >= 2) {
-    const int g = r0 + row;
-    uint8_t* sq = smem + half * (kBM * 128);  // this half stages dims [64 * half, 64 * half + 64)
+    uint8_t* sq = smem;
     int qp = -1;
     if (g < p.n_rows) {
       qp = p.qpos[g];
       const int src = p.q_rows ? p.q_rows[g] : g;
-      const uint4* qsrc =
-          reinterpret_cast<const uint4*>(p.q + (size_t)src * p.ldq + (size_t)h * kD + half * 64);
+      const uint4* qsrc = reinterpret_cast<const uint4*>(p.q + (size_t)src * p.ldq + (size_t)head * kD);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(sq + sw128(row, c)) = qsrc[c];
+      for (int c = 0; c < 16; ++c)
+        *reinterpret_cast<uint4*>(sq + (c >> 3) * (kBM * 128) + sw128(row, c & 7)) = qsrc[c];
     } else {
 #pragma unroll
-      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(sq + sw128(row, c)) = make_uint4(0, 0, 0, 0);
+      for (int c = 0; c < 16; ++c)
+        *reinterpret_cast<uint4*>(sq + (c >> 3) * (kBM * 128) + sw128(row, c & 7)) = make_uint4(0, 0, 0, 0);
     }
     if (qp >= 0) {
       if (p.kpos == nullptr) {
@@ -304,12 +300,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(&bars->o_final);
     }
   } else {
-    // ---------------- softmax (warps 2-9: 64 key columns per thread) ----------------
-    constexpr int kHalf = kBN / 2;
-    float* red_max = reinterpret_cast<float*>(smem + kOffRed);  // [tile parity][half][row]
+    // ---------------- softmax (warps 2-5: one tile row per thread) ----------------
     const float c = p.scale * 1.4426950408889634f;
     const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
-    const uint32_t col0 = (uint32_t)(half * kHalf);  // my S columns / O columns within a tile
     float m_ref = -INFINITY;
     float l = 0.f;
     bool ok = true;
@@ -323,38 +316,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (warp == 2 && lane == 0) trace_at(p, j, 5);
       tc_fence_after();
-      uint32_t sv[kHalf];
-      tmem_ld_32x32b_x32(lane_base + b * kBN + col0, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-      tmem_ld_32x32b_x32(lane_base + b * kBN + col0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      uint32_t sv[kBN];
+#pragma unroll
+      for (int q4 = 0; q4 < kBN / 32; ++q4)
+        tmem_ld_32x32b_x32(lane_base + b * kBN + q4 * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[q4 * 32]));
       tmem_ld_wait();
       if (warp == 2 && lane == 0) trace_at(p, j, 6);
-      const int vis = nvis - j * kBN - half * kHalf;  // my columns [0, vis) are visible to my row
-      if (!__all_sync(0xffffffffu, vis >= kHalf)) {
+      const int vis = nvis - j * kBN;  // keys [0, vis) of this tile are visible to my row
+      if (!__all_sync(0xffffffffu, vis >= kBN)) {
 #pragma unroll
-        for (int i = 0; i < kHalf; ++i)
+        for (int i = 0; i < kBN; ++i)
           if (i >= vis) sv[i] = 0xff800000u;  // -inf
       }
       float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < kHalf; i += 4) {
+      for (int i = 0; i < kBN; i += 4) {
         mx0 = fmaxf(mx0, __uint_as_float(sv[i]));
         mx1 = fmaxf(mx1, __uint_as_float(sv[i + 1]));
         mx2 = fmaxf(mx2, __uint_as_float(sv[i + 2]));
         mx3 = fmaxf(mx3, __uint_as_float(sv[i + 3]));
       }
-      // the row max over both halves: exchange partial maxima through shared
-      // memory (slot by tile parity, so a slot is rewritten only after both
-      // halves passed the next tile's exchange)
-      float* slot = red_max + b * (2 * kBM);
-      slot[half * kBM + row] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-      mbar_arrive(&bars->mx_ready[b]);
-      const bool both = mbar_wait(&bars->mx_ready[b], (uint32_t)(j >> 1) & 1u, status, kStatusTimeoutTmemFull);
-      if (!__all_sync(0xffffffffu, both)) {
-        ok = false;
-        break;
-      }
       if (warp == 2 && lane == 0) trace_at(p, j, 7);
-      const float m_tile = fmaxf(slot[row], slot[kBM + row]) * c;
+      const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;
       const bool need = m_tile > m_ref + kRescaleLog2;  // false when the tile is fully masked
       float f = 1.f;
       if (need) {
@@ -362,9 +345,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_ref = m_tile;
         l *= f;
       }
-      // O holds P_0..P_{j-1} V: rescale my 64 columns of it (warp-uniformly,
-      // tcgen05 ld/st are warp-collective) once PV(j-1) has completed.
-      // s_full(j) implies PV(j-2) completed, so o_done's phase j-1 is unambiguous.
+      // O holds P_0..P_{j-1} V: rescale it (warp-uniformly, tcgen05 ld/st are
+      // warp-collective) once PV(j-1) has completed.  s_full(j) implies PV(j-2)
+      // completed, so waiting on o_done's phase j-1 is unambiguous.
       if (j > 0 && __any_sync(0xffffffffu, need)) {
         const bool done = mbar_wait(&bars->o_done, (uint32_t)(j - 1) & 1u, status, kStatusTimeoutTmemFull);
         if (!__all_sync(0xffffffffu, done)) {
@@ -373,9 +356,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
 #pragma unroll 1
-        for (int cc = 0; cc < kHalf / 32; ++cc) {
+        for (int cc = 0; cc < kD / 32; ++cc) {
           uint32_t o[32];
-          const uint32_t at = lane_base + kTmemO + col0 + cc * 32;
+          const uint32_t at = lane_base + kTmemO + cc * 32;
           tmem_ld_32x32b_x32(at, o);
           tmem_ld_wait();
           uint32_t lo[16], hi[16];
@@ -391,15 +374,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float base = (m_ref == -INFINITY) ? 0.f : m_ref;
       float sum0 = 0.f, sum1 = 0.f;
-      uint8_t* sp = smem + kOffP + b * kPBytes + half * kPBlock;  // my 64 keys = one P k-block
+      uint8_t* sp = smem + kOffP + b * kPBytes;
 #pragma unroll
-      for (int cc = 0; cc < kHalf / 8; ++cc) {  // 8 keys = one 16-byte chunk of the P row
+      for (int cc = 0; cc < kBN / 8; ++cc) {  // 8 keys = one 16-byte chunk of the P row
         float e[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) e[i] = exp2_approx(fmaf(__uint_as_float(sv[8 * cc + i]), c, -base));
         sum0 += (e[0] + e[1]) + (e[2] + e[3]);
         sum1 += (e[4] + e[5]) + (e[6] + e[7]);
-        *reinterpret_cast<uint4*>(sp + sw128(row, cc)) =
+        *reinterpret_cast<uint4*>(sp + (cc >> 3) * kPBlock + sw128(row, cc & 7)) =
             make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
                        pack_bf16x2(e[6], e[7]));
       }
@@ -410,25 +393,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&bars->p_full[b]);
       if (warp == 2 && lane == 0) trace_at(p, j, 9);
     }
-    // ---- epilogue: O / (l of both halves) -> bf16, my 64 columns ----
-    // the row sums go to the max-exchange slot the last tile did not use: its
-    // previous readers all passed the last tile's exchange already
-    float* red_l = red_max + (n_tiles & 1) * (2 * kBM);
-    red_l[half * kBM + row] = l;
-    mbar_arrive(&bars->l_ready);
-    ok = ok && mbar_wait(&bars->l_ready, 0, status, kStatusTimeoutTmemFull);
-    const float l_row = red_l[row] + red_l[kBM + row];
-    const int g = r0 + row;
+    // ---- epilogue: O / l -> bf16 ----
     if (n_tiles > 0 && ok) ok = mbar_wait(&bars->o_final, 0, status, kStatusTimeoutTmemFull);
     if (warp == 2 && lane == 0) trace_at(p, 63, 2);
-    __nv_bfloat16* dst = p.out + (size_t)g * p.ldo + (size_t)h * kD + col0;
+    __nv_bfloat16* dst = p.out + (size_t)g * p.ldo + (size_t)head * kD;
     if (n_tiles > 0 && __all_sync(0xffffffffu, ok)) {
       tc_fence_after();
-      const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
-      for (int cc = 0; cc < kHalf / 32; ++cc) {
+      for (int cc = 0; cc < kD / 32; ++cc) {
         uint32_t o[32];
-        tmem_ld_32x32b_x32(lane_base + kTmemO + col0 + cc * 32, o);
+        tmem_ld_32x32b_x32(lane_base + kTmemO + cc * 32, o);
         tmem_ld_wait();
         if (g < p.n_rows) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 32);
@@ -443,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (g < p.n_rows && n_tiles == 0) {
       uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) d4[i] = make_uint4(0, 0, 0, 0);
+      for (int i = 0; i < 16; ++i) d4[i] = make_uint4(0, 0, 0, 0);
     }
   }
 
@@ -458,7 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream) {
-  if (p.head_dim != kD || p.n_rows < 0 || p.n_kv_heads <= 0 || p.n_heads % p.n_kv_heads != 0)
+  if (p.head_dim != kD || p.n_rows < 0 || p.n_kv_heads <= 0 || p.n_heads % p.n_kv_heads != 0 ||
+      kBM % (p.n_heads / p.n_kv_heads) != 0)
     return cudaErrorInvalidValue;
   if (p.n_rows == 0) return cudaSuccess;
   if (p.n_keys < 0 || p.n_keys > p.cache_cap) return cudaErrorInvalidValue;
@@ -473,7 +449,8 @@ cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream) {
                          kBN))
     return cudaErrorInvalidValue;
   ensure_smem_attr(attention_prefill_tc_kernel, kSmemBytes);
-  dim3 grid(p.n_heads, (p.n_rows + kBM - 1) / kBM);
+  const int span = kBM / (p.n_heads / p.n_kv_heads);
+  dim3 grid(p.n_kv_heads, (p.n_rows + span - 1) / span);
   attention_prefill_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tk, tv, p);
   return cudaGetLastError();
 }

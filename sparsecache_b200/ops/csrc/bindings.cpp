@@ -343,6 +343,44 @@ void gemv_allreduce(Tensor x, Tensor w, c10::optional<Tensor> norm_w, double eps
   run_gemv(g);
 }
 
+// ------------------------------------------------------- page scores (K11)
+Tensor page_token_scores(Tensor q, std::vector<Tensor> keys, int64_t n_tokens, double scale) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  CHECK_CUDA(q); CHECK_F32(q);
+  TORCH_CHECK(q.dim() == 4 && q.size(3) == 128 && q.is_contiguous(), "q [layers, rows, q_heads, 128] fp32");
+  const int L = (int)q.size(0);
+  TORCH_CHECK(L >= 1 && L <= sc::kPsMaxLayers && (int)keys.size() == L, "1..8 layers, one key tensor each");
+  sc::PageScoreArgs a{};
+  a.q = q.data_ptr<float>();
+  for (int l = 0; l < L; ++l) {
+    const Tensor& k = keys[l];
+    CHECK_CUDA(k); CHECK_BF16(k); CHECK_ALIGN16(k);
+    TORCH_CHECK(k.dim() == 3 && k.size(2) == 128 && k.is_contiguous(), "keys [kv_heads, capacity, 128]");
+    TORCH_CHECK(k.sizes() == keys[0].sizes(), "every layer's keys have the same shape");
+    a.keys[l] = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  }
+  a.cache_cap = (int)keys[0].size(1);
+  a.n_layers = L;
+  a.n_rows = (int)q.size(1);
+  a.n_q_heads = (int)q.size(2);
+  a.n_kv_heads = (int)keys[0].size(0);
+  a.n_tokens = (int)n_tokens;
+  a.scale = (float)scale;
+  const int64_t n = (int64_t)L * a.n_rows * a.n_q_heads;
+  const int64_t chunks = (n_tokens + 255) / 256;
+  auto f32 = torch::TensorOptions().dtype(torch::kFloat32).device(q.device());
+  Tensor logits = torch::empty({n, std::max<int64_t>(n_tokens, 1)}, f32);
+  Tensor partials = torch::empty({n, std::max<int64_t>(chunks, 1), 2}, f32);
+  Tensor stats = torch::empty({n, 2}, f32);
+  Tensor out = torch::empty({std::max<int64_t>(n_tokens, 1)}, f32);
+  a.logits = logits.data_ptr<float>();
+  a.partials = reinterpret_cast<float2*>(partials.data_ptr<float>());
+  a.stats = reinterpret_cast<float2*>(stats.data_ptr<float>());
+  a.token_scores = out.data_ptr<float>();
+  check_cuda(sc::page_token_scores(a, cur_stream()), "page_token_scores");
+  return out;
+}
+
 // ---------------------------------------------------------------- p2p
 std::tuple<Tensor, py::bytes> shared_empty(int64_t nbytes, int64_t device) {
   const c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
@@ -1107,6 +1145,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("k_cache"), py::arg("v_cache"), py::arg("kpos"), py::arg("n_keys"), py::arg("n_heads"),
         py::arg("scale"), py::arg("out"), py::arg("trace") = py::none());
   m.def("attention_prefill_mma", &attention_prefill_mma);
+  m.def("page_token_scores", &page_token_scores, py::arg("q"), py::arg("keys"), py::arg("n_tokens"),
+        py::arg("scale"));
   m.def("attention_decode", &attention_decode, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("pos"), py::arg("n_heads"), py::arg("scale"), py::arg("splits"), py::arg("out"),
         py::arg("page_table") = py::none(), py::arg("page_shift") = 6, py::arg("n_virtual") = py::none(),

@@ -29,6 +29,7 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kUnroll = 8;
+constexpr int kArMaxPairs = 32;  // pairs per CTA of the all-reduce epilogue (launcher keeps it there)
 
 // Inner product: bf16 pairs widened into packed fp32x2 registers and
 // multiplied with the sm_100 two-lane FMA (fma.rn.f32x2), which halves the
@@ -98,6 +99,7 @@ __global__ void __launch_bounds__(kThreads)
   __shared__ float s_bval[kWarps][MR];
   __shared__ int s_bidx[kWarps][MR];
   __shared__ int s_last;
+  __shared__ __align__(16) float s_ar[MR][2 * kArMaxPairs];  // all-reduce chunk of this CTA
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = a.K;
@@ -105,11 +107,21 @@ __global__ void __launch_bounds__(kThreads)
   const int n_pairs = a.N / 2;
   const int nchunk = K / 8;
 
+  // Pair schedule.  The all-reduce epilogue gives every CTA a contiguous run
+  // of pairs (its outputs form one contiguous chunk, sent to the peers with
+  // vector stores); the other epilogues interleave pairs over all warps.
+  const bool ar = a.epi == GEMV_ALLREDUCE;
+  const int ar_ppc = ar ? (((n_pairs + (int)gridDim.x - 1) / (int)gridDim.x + 1) & ~1) : 0;
+  const int ar_p0 = ar ? (int)blockIdx.x * ar_ppc : 0;
+  const int ar_p1 = ar ? max(ar_p0, min(ar_p0 + ar_ppc, n_pairs)) : 0;  // empty for CTAs past the end
+  const int p_step = ar ? kWarps : (int)gridDim.x * kWarps;
+  const int p_end = ar ? ar_p1 : n_pairs;
+
   // Prefetch this warp's first weight batch before waiting on the previous
   // kernel: weights never depend on it, so the prologue below overlaps HBM.
   uint4 wa[kUnroll], wb[kUnroll];
-  const int first_p = blockIdx.x * kWarps + warp;
-  if (first_p < n_pairs) {
+  const int first_p = ar ? ar_p0 + warp : (int)blockIdx.x * kWarps + warp;
+  if (first_p < p_end) {
     int r0, r1;
     pair_rows(a.epi, first_p, r0, r1);
     load_batch(reinterpret_cast<const uint4*>(a.w + (size_t)r0 * K),
@@ -187,7 +199,7 @@ __global__ void __launch_bounds__(kThreads)
   for (int m = 0; m < MR; ++m) best_v[m] = -INFINITY, best_i[m] = 0x7fffffff;
 
   bool preloaded = true;
-  for (int p = first_p; p < n_pairs; p += gridDim.x * kWarps) {
+  for (int p = first_p; p < p_end; p += p_step) {
     int r0, r1;
     pair_rows(a.epi, p, r0, r1);
     const uint4* w0 = reinterpret_cast<const uint4*>(a.w + (size_t)r0 * K);
@@ -280,12 +292,9 @@ __global__ void __launch_bounds__(kThreads)
           break;
         }
         case GEMV_ALLREDUCE: {
-          // row-parallel partial -> every rank's receive slot for this sender
-          for (int r = 0; r < a.ar_tp; ++r) {
-            float* dst = a.ar_dst[r] + ((size_t)a.ar_sender * M + m) * a.N;
-            dst[r0] = v0;
-            dst[r1] = v1;
-          }
+          // staged: the CTA sends its whole contiguous chunk after the loop
+          s_ar[m][2 * (p - ar_p0)] = v0;
+          s_ar[m][2 * (p - ar_p0) + 1] = v1;
           break;
         }
         case GEMV_ARGMAX: {
@@ -300,6 +309,25 @@ __global__ void __launch_bounds__(kThreads)
   }
 
   if (a.epi == GEMV_ALLREDUCE) {
+    // this CTA's outputs [2 * ar_p0, 2 * ar_p1) of every row go to every
+    // rank's receive slot of this sender as 16-byte stores (NVLink for
+    // peers); the chunk start is 16-byte aligned because ar_ppc is even
+    __syncthreads();
+    const int n_vec = (ar_p1 - ar_p0) / 2;  // float4 per row (2 pairs = 4 outputs)
+    const int per_rank = M * n_vec;
+    for (int i = tid; i < a.ar_tp * per_rank; i += kThreads) {
+      const int r = i / per_rank, rem = i - r * per_rank;
+      const int m = rem / n_vec, v = rem - m * n_vec;
+      float4* dst = reinterpret_cast<float4*>(a.ar_dst[r] + ((size_t)a.ar_sender * M + m) * a.N + 2 * ar_p0);
+      dst[v] = *reinterpret_cast<const float4*>(&s_ar[m][4 * v]);
+    }
+    if ((ar_p1 - ar_p0) & 1) {  // odd tail pair (only the last CTA can have one)
+      for (int i = tid; i < a.ar_tp * M; i += kThreads) {
+        const int r = i / M, m = i - r * M;
+        float2* dst = reinterpret_cast<float2*>(a.ar_dst[r] + ((size_t)a.ar_sender * M + m) * a.N + 2 * (ar_p1 - 1));
+        *dst = make_float2(s_ar[m][2 * (ar_p1 - 1 - ar_p0)], s_ar[m][2 * (ar_p1 - 1 - ar_p0) + 1]);
+      }
+    }
     // the last CTA to finish publishes this rank's partial to every rank
     __threadfence_system();
     __syncthreads();
@@ -398,6 +426,12 @@ cudaError_t gemv_bf16(const GemvArgs& a, cudaStream_t stream) {
   int grid = (n_pairs + kWarps - 1) / kWarps;
   const int cap = (a.num_sms > 0 ? a.num_sms : 148) * 8;
   if (grid > cap) grid = cap;
+  if (a.epi == GEMV_ALLREDUCE) {
+    // at most kArMaxPairs (rounded to even) pairs per CTA
+    const int need = (n_pairs + kArMaxPairs - 2) / (kArMaxPairs - 1);
+    if (grid < need) grid = need;
+    if (a.N % 4 != 0) return cudaErrorInvalidValue;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);

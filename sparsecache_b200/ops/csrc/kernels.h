@@ -345,6 +345,22 @@ struct RsReduceArgs {
 };
 cudaError_t rs_reduce(const RsReduceArgs& a, cudaStream_t stream);
 
+// -------------------------------------------------------- page scores ----
+constexpr int kPsMaxLayers = 8;
+constexpr int kPsMaxRowsPerGroup = 64;
+struct PageScoreArgs {
+  const float* q;                       // [n_layers, n_rows, n_q_heads, 128] fp32 (RoPE applied)
+  const __nv_bfloat16* keys[kPsMaxLayers];  // per layer [n_kv_heads, cache_cap, 128]
+  int cache_cap;
+  int n_layers, n_rows, n_q_heads, n_kv_heads, n_tokens;
+  float scale;
+  float* logits;        // scratch [n_layers * n_rows * n_q_heads, n_tokens]
+  float2* partials;     // scratch [n_layers * n_rows * n_q_heads, ceil(n_tokens / 256)]
+  float2* stats;        // scratch [n_layers * n_rows * n_q_heads]
+  float* token_scores;  // [n_tokens]
+};
+cudaError_t page_token_scores(const PageScoreArgs& a, cudaStream_t stream);
+
 // ------------------------------------------------------------------- p2p ----
 cudaError_t peer_signal(int* flag, int value, const int* value_src, unsigned long long* stamp,
                         cudaStream_t stream);

@@ -122,12 +122,17 @@ __global__ void __launch_bounds__(kRsThreads) rs_reduce_kernel(RsReduceArgs a) {
   }
   __syncthreads();
   if (s_fail) return;
-  const int nvec = a.N / 4;
+  // column block of this CTA (several blocks per row only without the norm,
+  // which needs the whole row)
+  const int nvec_row = a.N / 4;
+  const int per_block = (nvec_row + gridDim.y - 1) / gridDim.y;
+  const int cbase = blockIdx.y * per_block;
+  const int nvec = min(nvec_row, cbase + per_block);
   float vals[kRsMaxVec][4];
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < kRsMaxVec; ++i) {
-    const int c = tid + i * kRsThreads;
+    const int c = cbase + tid + i * kRsThreads;
     if (c >= nvec) break;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int s = 0; s < a.tp; ++s) {
@@ -162,7 +167,7 @@ __global__ void __launch_bounds__(kRsThreads) rs_reduce_kernel(RsReduceArgs a) {
   const float rinv = rsqrtf(tot / (float)a.N + a.eps);
 #pragma unroll
   for (int i = 0; i < kRsMaxVec; ++i) {
-    const int c = tid + i * kRsThreads;
+    const int c = cbase + tid + i * kRsThreads;
     if (c >= nvec) break;
     const uint2 gw = *reinterpret_cast<const uint2*>(a.norm_w + 4 * c);
     const float2 g0 = unpack_bf16x2(gw.x), g1 = unpack_bf16x2(gw.y);
@@ -174,7 +179,12 @@ __global__ void __launch_bounds__(kRsThreads) rs_reduce_kernel(RsReduceArgs a) {
 
 cudaError_t rs_reduce(const RsReduceArgs& a, cudaStream_t stream) {
   if (a.N % 4 != 0 || a.N / 4 > kRsThreads * kRsMaxVec || a.tp < 1 || a.rows < 1) return cudaErrorInvalidValue;
-  rs_reduce_kernel<<<a.rows, kRsThreads, 0, stream>>>(a);
+  // few rows (decode, verify): spread each row over column blocks of 256
+  // float4 so the tp partials are summed by many SMs; the fused RMSNorm
+  // needs whole rows and keeps one CTA per row
+  int blocks = 1;
+  if (a.norm_w == nullptr && a.rows < 64) blocks = (a.N / 4 + kRsThreads - 1) / kRsThreads;
+  rs_reduce_kernel<<<dim3(a.rows, blocks), kRsThreads, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

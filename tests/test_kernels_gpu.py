@@ -556,3 +556,51 @@ def test_skinny_qkv_allreduce_and_row_argmax(cuda_device):
     ext.row_argmax(logits, tok)
     torch.cuda.synchronize()
     assert tok.tolist() == logits.float().argmax(-1).tolist() and int(tok[2]) == 100
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 8192, 1024), (3, 4096, 2048), (8, 4096, 512)])
+def test_gemv_allreduce_one_rank_matches_residual_gemv(cuda_device, M, N, K):
+    """The decode all-reduce epilogue at one rank: each CTA's contiguous chunk
+    of fp32 partials goes to the receive slot with vector stores, the flag is
+    released, and the column-split reduce adds it to the residual; equal to
+    the residual GEMV (same rounding order) twice in a row."""
+    ext = _ext()
+    g = torch.Generator(device="cpu").manual_seed(M * 1000 + N + K)
+    x = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(cuda_device, torch.bfloat16)
+    res = torch.randn(M, N, generator=g).to(cuda_device, torch.bfloat16)
+    recv = torch.zeros(1, M, N, device=cuda_device)
+    flag = torch.zeros(4, device=cuda_device, dtype=torch.int32)
+    counter = torch.zeros(1, device=cuda_device, dtype=torch.int32)
+    status = torch.zeros(1, device=cuda_device, dtype=torch.int32)
+    expect = torch.empty_like(res)
+    ext.gemv_residual(x, w, None, 1e-5, expect, res)
+    for epoch in (1, 2):
+        out = res.clone()
+        ext.gemv_allreduce(x, w, None, 1e-5, [recv.data_ptr()], [flag.data_ptr()], 0, epoch, None, 0, counter)
+        ext.rs_reduce(recv, flag, epoch, int(2e9), status, out, out, None, None, 1e-5, None, 0)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0 and int(flag[0].item()) == epoch
+        torch.testing.assert_close(out.float(), expect.float(), rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("L,R,H,Hkv,T", [(1, 1, 32, 8, 16000), (3, 1, 8, 2, 777), (2, 4, 8, 8, 300)])
+def test_page_token_scores_match_fp32_softmax(cuda_device, L, R, H, Hkv, T):
+    """K11: mean over layers, query rows and heads of softmax(q K^T / sqrt(d)),
+    per prompt token, against the fp32 einsum the reference uses."""
+    ext = _ext()
+    g = torch.Generator(device="cpu").manual_seed(L * 100 + T)
+    cap = T + 37
+    keys = [torch.randn(Hkv, cap, 128, generator=g).to(cuda_device, torch.bfloat16) for _ in range(L)]
+    q = (torch.randn(L, R, H, 128, generator=g) * 1.5).to(cuda_device)
+    got = ext.page_token_scores(q, keys, T, 128 ** -0.5)
+    torch.cuda.synchronize()
+    ref = torch.zeros(T, device=cuda_device)
+    G = H // Hkv
+    for l in range(L):
+        k = keys[l][:, :T].float().repeat_interleave(G, dim=0)  # [H, T, D]
+        logits = torch.einsum("rhd,htd->rht", q[l].float(), k) * 128 ** -0.5
+        ref += logits.softmax(-1).mean(dim=(0, 1))
+    ref /= L
+    torch.testing.assert_close(got, ref, rtol=2e-3, atol=1e-6)
+    assert abs(float(got.sum()) - 1.0) < 1e-3
