@@ -89,20 +89,39 @@ def question_attention_document_scores(cfg, layer_inputs: dict, layer_weights: d
 
     D, H = cfg.head_dim, cfg.n_heads
     cos, sin = rope_cos_sin(cfg, positions.cpu(), device=next(iter(layer_inputs.values())).device)
-    per_layer = []
+    queries, keys = [], []
     for l, x in layer_inputs.items():
         ln1, w_qkv = layer_weights[l]
         xf = x.float()
         xn = (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + cfg.rms_eps)).to(torch.bfloat16) * ln1
         q = (xn.float() @ w_qkv[: cfg.q_size].float().t()).view(-1, H, D).transpose(0, 1)  # [H, q, D]
-        q = apply_rope(q, cos, sin, sequence_dim=1)
-        k = layer_keys[l][:, :n_tokens].float()  # [Hkv, T, D]
-        hkv = k.shape[0]
-        qg = q.reshape(hkv, H // hkv, -1, D)
-        probs = torch.einsum("gqrd,gkd->gqrk", qg, k).mul(D ** -0.5).softmax(-1)
-        tok = probs.mean(dim=(0, 1, 2))  # [T]
-        per_layer.append(torch.stack([tok[b:e].sum() for b, e in document_ranges]))
-    return torch.stack(per_layer).mean(0).tolist()
+        queries.append(apply_rope(q, cos, sin, sequence_dim=1).transpose(0, 1).contiguous())  # [q, H, D]
+        keys.append(layer_keys[l])
+    tok = token_attention_scores(torch.stack(queries), keys, n_tokens)
+    return [float(tok[b:e].sum()) for b, e in document_ranges]
+
+
+def token_attention_scores(q: torch.Tensor, keys: Sequence[torch.Tensor], n_tokens: int) -> torch.Tensor:
+    """Mean over layers, query rows and heads of softmax(q K^T / sqrt(D)) per prompt token (K11).
+
+    ``q`` [L, R, H, D] fp32 (RoPE applied), ``keys[l]`` [H_kv, >= n_tokens, D].
+    On the GPU this is the sm_100a page-score kernel; CPU tensors (the fp32
+    oracle path) use the same formula in PyTorch.
+    """
+    D = q.shape[-1]
+    if q.is_cuda:
+        from .. import ops
+
+        return ops.ext().page_token_scores(q.float().contiguous(), [k.contiguous() for k in keys], n_tokens,
+                                           D ** -0.5)
+    L, R, H, _ = q.shape
+    out = torch.zeros(n_tokens, dtype=torch.float32)
+    for l in range(L):
+        k = keys[l][:, :n_tokens].float()
+        g = H // k.shape[0]
+        logits = torch.einsum("rhd,htd->rht", q[l].float(), k.repeat_interleave(g, dim=0)) * D ** -0.5
+        out += logits.softmax(-1).mean(dim=(0, 1))
+    return out / L
 
 
 def auto_draft_tokens(*, prompt_tokens: int, first_stage_tokens: int, bytes_per_token: float, transport_gbps: float,

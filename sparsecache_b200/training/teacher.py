@@ -35,6 +35,8 @@ from typing import Any, Sequence
 import torch
 import torch.nn.functional as F
 
+from .. import ops
+
 from ..models.sparse_kv_draft import select_visible_token_indices, sink_recent_topk_indices
 
 TEACHER_FORMATS = tuple(f"sparsecache.sparse-kv-draft-teacher.v{i}" for i in range(1, 6))
@@ -365,15 +367,18 @@ def extract_teacher(engine, prompts: Sequence[torch.Tensor], *, kv_layers: Seque
         seed_hidden = torch.stack([captured[l] for l in seed_layers])
         # K11 page scores: the last prompt token's queries of every memory layer
         cos, sin = rope_cos_sin(cfg, torch.tensor([T - 1]), device=dev)
-        page_probs = []
+        queries = []
         for l in kv_layers:
             x = captured[("q", l)].float()
             x = x * torch.rsqrt(x.square().mean() + cfg.rms_eps)
             x = (x.to(torch.bfloat16) * w.layers[l].ln1).float()
             q = (w.layers[l].w_qkv[: cfg.q_size].float() @ x).view(cfg.n_heads, cfg.head_dim)
-            q = apply_rope(q.unsqueeze(1), cos, sin, sequence_dim=1).squeeze(1)
-            page_probs.append(page_scores_from_queries(q, s.k(l), T, page_size))
-        scores = torch.stack(page_probs).mean(0)
+            queries.append(apply_rope(q.unsqueeze(1), cos, sin, sequence_dim=1).squeeze(1))
+        # K11 on the GPU: layer-mean token scores, then per-page sums
+        tok = ops.ext().page_token_scores(torch.stack(queries).unsqueeze(1).contiguous(),
+                                          [s.k(l) for l in kv_layers], T, cfg.head_dim ** -0.5)
+        pages = -(-T // page_size)
+        scores = F.pad(tok, (0, pages * page_size - T)).view(pages, page_size).sum(-1)
         # greedy continuation (CUDA-graph decode), then one prefill of it for the teacher logits
         engine.first_token(h[T - 1:T], position=T, max_new=continuation_tokens)
         engine.decode(s, continuation_tokens - 1, max_new=continuation_tokens)
