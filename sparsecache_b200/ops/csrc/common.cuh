@@ -142,6 +142,16 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Prefetch a 2D box of a tensor map into L2 (no shared memory, no barrier):
+// a later tiled load of the same box then hits L2 instead of DRAM.  Same
+// alignment rule on x as the loads.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 // 3D box: coordinates (x innermost, y, z).
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map,
                                             uint64_t* bar, int x, int y, int z) {

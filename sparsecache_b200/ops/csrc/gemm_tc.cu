@@ -39,6 +39,7 @@ namespace sc {
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
 constexpr int kGemmThreads = 192;
+constexpr int kPrefetchKb = 6;  // k-blocks of L2 prefetch ahead of the smem ring
 
 template <int BN>
 struct GemmCfg {
@@ -362,7 +363,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             confirmed |= 1u << map;
           }
         }
+        // L2 prefetch runs kPrefetchKb k-blocks ahead of the loads: the
+        // weight tiles stream from DRAM into L2 while earlier stages are
+        // consumed, so each tiled load waits on an L2 hit instead of DRAM
+        for (int kb = kb0; kb < kb0 + kPrefetchKb && kb < kb1; ++kb) {
+          tma_prefetch_l2_2d(&tmap_b, kb * kGemmBK, tn * BN);
+          tma_prefetch_l2_2d(&amaps.m[map], kb * kGemmBK, ay);
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
+          if (kb + kPrefetchKb < kb1) {
+            tma_prefetch_l2_2d(&tmap_b, (kb + kPrefetchKb) * kGemmBK, tn * BN);
+            tma_prefetch_l2_2d(&amaps.m[map], (kb + kPrefetchKb) * kGemmBK, ay);
+          }
           if (!mbar_wait(&bars->empty[stage], phase ^ 1, status, kStatusTimeoutSmemEmpty)) {
             ok = false;
             break;

@@ -41,7 +41,8 @@ def test_prefill_matches_oracle(setup):
     h = engine.prefill(ids, slot)
     torch.cuda.synchronize()
     hidden, cache = oracle.forward_tokens(torch.tensor(req.prompt), torch.arange(len(req.prompt)))
-    assert _rel(h.cpu(), hidden[0]) < 5e-2
+    err = _rel(h.cpu(), hidden[0])
+    assert err < 2e-2, err
     T = len(req.prompt)
     for layer in range(cfg.n_layers):
         assert _rel(slot.k(layer)[:, :T].cpu(), cache[layer][0][0]) < 5e-2
@@ -111,18 +112,48 @@ def test_graph_decode_equals_eager_decode(setup):
     assert tuple(toks[: len(a.token_ids)]) == a.token_ids
 
 
-def test_decode_matches_oracle_greedy_first_tokens(setup):
-    cfg, oracle, engine, store, requests, server = setup
-    req = requests[3]
-    full = server.serve(req, mode="full", sync=True)
-    logits, cache = oracle.prefill(req.prompt)
-    top2 = logits.topk(2).values
-    if float(top2[0] - top2[1]) > 0.05:
-        assert full.token_ids[0] == int(logits.argmax())
+def _assert_eps_argmax(oracle_logits, tokens, eps):
+    """Every generated token is an eps-argmax of the fp32 oracle's logits at its
+    step (teacher forcing on the engine's own tokens): bf16 kernels may pick
+    either side of a near-tie, never a token the oracle clearly ranks lower."""
+    assert oracle_logits.shape[0] == len(tokens)
+    for step, tok in enumerate(tokens):
+        row = oracle_logits[step].float()
+        gap = float(row.max() - row[tok])
+        assert gap <= eps, f"step {step}: token {tok} is {gap:.4f} below the oracle's best {int(row.argmax())}"
 
 
-def test_direct_mode_runs(setup):
+def test_greedy_decode_matches_oracle_multi_token(setup):
+    """Full prefill + 12 greedy CUDA-graph decode steps against the fp32 oracle."""
     cfg, oracle, engine, store, requests, server = setup
-    out = server.serve(requests[0], mode="direct", sync=True)
-    assert len(out.token_ids) >= 1
-    assert int(engine.ext.status(torch.empty(1, device=engine.device)).item()) == 0
+    n_match = 0
+    for req in requests:
+        out = server.serve(req, mode="full", max_new_tokens=12, sync=True)
+        toks = list(out.token_ids)
+        T = len(req.prompt)
+        seq = torch.tensor(list(req.prompt) + toks[:-1])
+        hidden, _ = oracle.forward_tokens(seq, torch.arange(seq.numel()))
+        logits = oracle.logits(hidden[0, T - 1:])  # the rows that predicted each generated token
+        _assert_eps_argmax(logits, toks, eps=0.08)
+        n_match += sum(int(logits[i].argmax()) == t for i, t in enumerate(toks))
+    # most steps are exact argmax agreements, not near-ties
+    assert n_match >= 0.9 * 12 * len(requests)
+
+
+def test_direct_mode_matches_oracle(setup):
+    """Direct reuse: the prefix prefilled, the documents' independently produced
+    KV composed as-is (keys re-rotated), only the question suffix prefilled;
+    12 tokens against the fp32 oracle doing the same composition."""
+    cfg, oracle, engine, store, requests, server = setup
+    for req in requests[:2]:
+        out = server.serve(req, mode="direct", max_new_tokens=12, sync=True)
+        assert int(engine.ext.status(torch.empty(1, device=engine.device)).item()) == 0
+        toks = list(out.token_ids)
+        P, S, T = len(req.prefix), len(req.suffix), len(req.prompt)
+        _, system = oracle.prefill(req.prefix)
+        docs = [oracle.encode_local(d) for d in req.documents]
+        past = compose_documents(cfg, docs, prefix_tokens=P, system_cache=system)
+        seq = torch.tensor(list(req.suffix) + toks[:-1])
+        hidden, _ = oracle.forward_tokens(seq, torch.arange(T - S, T - S + seq.numel()), past=past)
+        logits = oracle.logits(hidden[0, S - 1:])
+        _assert_eps_argmax(logits, toks, eps=0.08)
