@@ -192,10 +192,10 @@ class _CountingExt:
     """Proxy over the extension that counts kernel launches issued from the host."""
 
     _NOT_KERNELS = {"status", "num_sms", "gemv_argmax_grid", "attention_decode_cluster", "attention_decode_outer",
-                    "skinny_splits",
+                    "skinny_splits", "attention_prefill_splits",
                     "shared_empty",
                     "shared_open", "shared_close"}
-    _MULTI = {"gemm_store", "gemm_residual", "skinny_gemm", "skinny_qkv", "skinny_allreduce"}
+    _MULTI = {"gemm_store", "gemm_residual", "skinny_gemm", "skinny_qkv", "skinny_allreduce", "attention_prefill"}
 
     def __init__(self, ext) -> None:
         self._ext = ext
@@ -269,7 +269,12 @@ class B200Engine:
         """attention over the slot's keys, o_proj + residual, then the MLP block (in place on h)."""
         cfg, lw, ext = self.cfg, self.w.layers[layer], self.ext
         attn = self.ws.get("attn", (n_rows, cfg.q_size), torch.bfloat16)
-        ext.attention_prefill(q, q_rows, qpos, slot.k(layer), slot.v(layer), kpos, n_keys, cfg.n_heads, self.scale, attn)
+        # few query rows (CacheBlend's active set) leave SMs idle: the kernel
+        # splits the keys over several CTAs and merges fp32 partials from here
+        split_ws = (self.ws.get("attn_split", (4 * self.ATTN_SPLIT_ROWS * cfg.n_heads * 132,), torch.float32)
+                    if n_rows <= self.ATTN_SPLIT_ROWS else None)
+        ext.attention_prefill(q, q_rows, qpos, slot.k(layer), slot.v(layer), kpos, n_keys, cfg.n_heads, self.scale, attn,
+                              ws=split_ws)
         ext.gemm_residual(attn, lw.w_o, h, h, self.bn)
         x = self.ws.get("x", (n_rows, cfg.d_model), torch.bfloat16)
         ext.rmsnorm(h, None, lw.ln2, cfg.rms_eps, x)
@@ -534,6 +539,7 @@ class B200Engine:
     # ------------------------------------------------------------ decode
     MAX_DECODE_TOKENS = 8192
     MAX_ROWS = 8
+    ATTN_SPLIT_ROWS = 512  # query rows up to which prefill attention may split its keys
 
     def _decode_buffers(self, max_new: int = 0):
         """Fixed-size decode state (captured decode graphs hold these addresses).

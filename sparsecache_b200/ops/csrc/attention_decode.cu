@@ -83,17 +83,24 @@ __global__ void __launch_bounds__(kThreads)
   const int split = blockIdx.x % S;
   const int cidx = blockIdx.x / S;
   const int kvh = blockIdx.y;
-  const int qv0 = blockIdx.z * kRQ;
+  // batched sequences (pos_rows): z = sequence * z-blocks + z-block, one row
+  // per sequence, its own position and cache (seq_stride elements apart)
+  const int nzb = (QV + kRQ - 1) / kRQ;
+  const int seq = a.pos_rows != nullptr ? (int)blockIdx.z / nzb : 0;
+  const int qv0 = (a.pos_rows != nullptr ? (int)blockIdx.z % nzb : (int)blockIdx.z) * kRQ;
+  const __nv_bfloat16* qbase = a.q + (size_t)seq * a.n_heads * 128;
+  __nv_bfloat16* obase = a.out + (size_t)seq * a.n_heads * 128;
   const int nq = min(kRQ, QV - qv0);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int sub = lane & 7, grp = lane >> 3;
   const float sl2 = a.scale * 1.4426950408889634f;
-  const __nv_bfloat16* kb = a.k_cache + (size_t)kvh * a.cache_cap * 128 + sub * 16;
-  const __nv_bfloat16* vb = a.v_cache + (size_t)kvh * a.cache_cap * 128 + sub * 16;
+  const size_t seq_off = (size_t)seq * (size_t)a.seq_stride;
+  const __nv_bfloat16* kb = a.k_cache + seq_off + (size_t)kvh * a.cache_cap * 128 + sub * 16;
+  const __nv_bfloat16* vb = a.v_cache + seq_off + (size_t)kvh * a.cache_cap * 128 + sub * 16;
   const int page_mask = (1 << a.page_shift) - 1;
   pdl_wait();  // q and the new rows come from the QKV kernel right before
   pdl_launch_dependents();
-  const int n_keys = a.n_virtual != nullptr ? *a.n_virtual : *a.pos + a.M;
+  const int n_keys = a.pos_rows != nullptr ? a.pos_rows[seq] + 1 : (a.n_virtual != nullptr ? *a.n_virtual : *a.pos + a.M);
   const int pos0 = n_keys - a.M;
   const int k_begin = blockIdx.x * chunk;
   const int k_end = min(n_keys, k_begin + chunk);
@@ -109,7 +116,7 @@ __global__ void __launch_bounds__(kThreads)
     const int qv = qv0 + (i < nq ? i : 0);
     const int m = qv / G, gi = qv % G;
     uint4 u[2];
-    reg_load16(a.q + (size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + sub * 16, u);
+    reg_load16(qbase + (size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + sub * 16, u);
     reg_unpack16(u, q[i]);
 #pragma unroll
     for (int e = 0; e < 16; ++e) q[i][e] *= sl2;
@@ -277,7 +284,7 @@ __global__ void __launch_bounds__(kThreads)
     const int qv = qv0 + i;
     if (outer == 1) {
       const int m = qv / G, gi = qv % G;
-      a.out[(size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + d] =
+      obase[(size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + d] =
           __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
     } else {
       float* part = a.ws + (((size_t)kvh * kMaxOuter + cidx) * kMaxQV + qv) * 130;
@@ -315,7 +322,7 @@ __global__ void __launch_bounds__(kThreads)
       }
     }
     const int m = qv / G, gi = qv % G;
-    a.out[(size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + d] =
+    obase[(size_t)m * a.n_heads * 128 + (kvh * G + gi) * 128 + d] =
         __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
   }
   if (tid == 0) *counter = 0u;
@@ -346,12 +353,14 @@ cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
   if (a.M < 1 || a.M * G > kMaxQV) return cudaErrorInvalidValue;
   const int S = a.splits;
   if (S < 1 || S > 16) return cudaErrorInvalidValue;
+  if (a.pos_rows != nullptr && (a.M != 1 || a.n_seq < 1 || a.page_table != nullptr)) return cudaErrorInvalidValue;
   int outer = 1;
-  if (a.ws != nullptr && a.counters != nullptr) {
+  if (a.ws != nullptr && a.counters != nullptr && a.pos_rows == nullptr) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    outer = attention_decode_outer(a.cache_cap, a.n_kv_heads, S, sms);
+    outer = a.outer > 0 ? a.outer : attention_decode_outer(a.cache_cap, a.n_kv_heads, S, sms);
+    if (outer > kMaxOuter) return cudaErrorInvalidValue;
   }
   // keys per CTA: the cache capacity (+ the largest row block) split evenly
   // over all S * outer CTAs, rounded to 16 keys; independent of M so a row
@@ -370,7 +379,7 @@ cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
     }
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(S * outer, a.n_kv_heads, (qv + kRQ - 1) / kRQ);
+  cfg.gridDim = dim3(S * outer, a.n_kv_heads, ((qv + kRQ - 1) / kRQ) * (a.pos_rows != nullptr ? a.n_seq : 1));
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;

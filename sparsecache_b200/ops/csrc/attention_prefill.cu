@@ -212,7 +212,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
-  const int n_tiles = (bars->max_vis + kBN - 1) / kBN;
+  // key tiles of the row tile, and this CTA's share of them (key split z of
+  // gridDim.z); below, j counts this CTA's tiles and t0 + j is the key tile
+  const int n_tiles_all = (bars->max_vis + kBN - 1) / kBN;
+  const int t0 = (int)blockIdx.z * n_tiles_all / (int)gridDim.z;
+  const int n_tiles = ((int)blockIdx.z + 1) * n_tiles_all / (int)gridDim.z - t0;
   if (threadIdx.x == 0) trace_at(p, 63, 1);
 
   if (warp == 0) {
@@ -227,14 +231,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* sv = smem + kOffV + s * kKVBytes;
         if (!mbar_wait(&bars->k_empty[s], ph ^ 1u, status, kStatusTimeoutSmemEmpty)) break;
         mbar_arrive_expect_tx(&bars->k_full[s], kKVBytes);
-        tma_load_3d(sk, &tm_k, &bars->k_full[s], 0, j * kBN, kvh);
-        tma_load_3d(sk + kHalfBytes, &tm_k, &bars->k_full[s], 64, j * kBN, kvh);
+        tma_load_3d(sk, &tm_k, &bars->k_full[s], 0, (t0 + j) * kBN, kvh);
+        tma_load_3d(sk + kHalfBytes, &tm_k, &bars->k_full[s], 64, (t0 + j) * kBN, kvh);
         trace_at(p, j, 0);
         k_last[s] = (int)ph;
         if (!mbar_wait(&bars->v_empty[s], ph ^ 1u, status, kStatusTimeoutSmemEmpty)) break;
         mbar_arrive_expect_tx(&bars->v_full[s], kKVBytes);
-        tma_load_3d(sv, &tm_v, &bars->v_full[s], 0, j * kBN, kvh);
-        tma_load_3d(sv + kHalfBytes, &tm_v, &bars->v_full[s], 64, j * kBN, kvh);
+        tma_load_3d(sv, &tm_v, &bars->v_full[s], 0, (t0 + j) * kBN, kvh);
+        tma_load_3d(sv + kHalfBytes, &tm_v, &bars->v_full[s], 64, (t0 + j) * kBN, kvh);
         trace_at(p, j, 1);
         v_last[s] = (int)ph;
       }
@@ -322,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x32(lane_base + b * kBN + q4 * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[q4 * 32]));
       tmem_ld_wait();
       if (warp == 2 && lane == 0) trace_at(p, j, 6);
-      const int vis = nvis - j * kBN;  // keys [0, vis) of this tile are visible to my row
+      const int vis = nvis - (t0 + j) * kBN;  // keys [0, vis) of this tile are visible to my row
       if (!__all_sync(0xffffffffu, vis >= kBN)) {
 #pragma unroll
         for (int i = 0; i < kBN; ++i)
@@ -393,11 +397,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&bars->p_full[b]);
       if (warp == 2 && lane == 0) trace_at(p, j, 9);
     }
-    // ---- epilogue: O / l -> bf16 ----
+    // ---- epilogue: O / l -> bf16 (or the fp32 partial of a key split) ----
     if (n_tiles > 0 && ok) ok = mbar_wait(&bars->o_final, 0, status, kStatusTimeoutTmemFull);
     if (warp == 2 && lane == 0) trace_at(p, 63, 2);
     __nv_bfloat16* dst = p.out + (size_t)g * p.ldo + (size_t)head * kD;
-    if (n_tiles > 0 && __all_sync(0xffffffffu, ok)) {
+    if (gridDim.z > 1) {
+      // partial (O relative to m_ref, m_ref, l) of this split; rows whose keys
+      // all lie in other splits leave m = -inf, l = 0 and are ignored by the merge
+      float* part = p.ws + (((size_t)blockIdx.z * p.n_rows + (g < p.n_rows ? g : 0)) * p.n_heads + head) * 132;
+      const bool have = n_tiles > 0 && __all_sync(0xffffffffu, ok);
+      if (have) tc_fence_after();
+#pragma unroll 1
+      for (int cc = 0; cc < kD / 32; ++cc) {
+        uint32_t o[32];
+        if (have) {
+          tmem_ld_32x32b_x32(lane_base + kTmemO + cc * 32, o);
+          tmem_ld_wait();
+        }
+        if (g < p.n_rows) {
+          float4* d4 = reinterpret_cast<float4*>(part + cc * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            d4[i] = have ? make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                       __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      if (g < p.n_rows) {
+        part[128] = have ? m_ref : -INFINITY;
+        part[129] = have ? l : 0.f;
+      }
+    } else if (n_tiles > 0 && __all_sync(0xffffffffu, ok)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
@@ -432,6 +462,38 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) trace_at(p, 63, 3);
 }
 
+// Merge of the key-split partials: one warp per (row, head), 4 dims a lane,
+// splits combined in split order (deterministic).
+__global__ void __launch_bounds__(256) attention_prefill_merge_kernel(AttnPrefillArgs p) {
+  const long long pair = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (pair >= (long long)p.n_rows * p.n_heads) return;
+  const int lane = threadIdx.x & 31;
+  const int row = (int)(pair / p.n_heads), head = (int)(pair % p.n_heads);
+  const size_t stride = (size_t)p.n_rows * p.n_heads * 132;
+  const float* base = p.ws + (size_t)pair * 132;
+  float mx = -INFINITY;
+  for (int s = 0; s < p.splits; ++s) mx = fmaxf(mx, base[s * stride + 128]);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float den = 0.f;
+  if (mx != -INFINITY) {
+    for (int s = 0; s < p.splits; ++s) {
+      const float* part = base + s * stride;
+      const float m = part[128];
+      if (m == -INFINITY) continue;
+      const float w = exp2_approx(m - mx);
+      const float4 o = reinterpret_cast<const float4*>(part)[lane];
+      acc.x = fmaf(w, o.x, acc.x);
+      acc.y = fmaf(w, o.y, acc.y);
+      acc.z = fmaf(w, o.z, acc.z);
+      acc.w = fmaf(w, o.w, acc.w);
+      den = fmaf(w, part[129], den);
+    }
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  uint2 packed = make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
+  *reinterpret_cast<uint2*>(p.out + (size_t)row * p.ldo + (size_t)head * kD + lane * 4) = packed;
+}
+
 cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream) {
   if (p.head_dim != kD || p.n_rows < 0 || p.n_kv_heads <= 0 || p.n_heads % p.n_kv_heads != 0 ||
       kBM % (p.n_heads / p.n_kv_heads) != 0)
@@ -450,9 +512,32 @@ cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   ensure_smem_attr(attention_prefill_tc_kernel, kSmemBytes);
   const int span = kBM / (p.n_heads / p.n_kv_heads);
-  dim3 grid(p.n_kv_heads, (p.n_rows + span - 1) / span);
-  attention_prefill_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tk, tv, p);
+  int sms = 148, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  AttnPrefillArgs a = p;
+  a.splits = attention_prefill_splits(p, sms);
+  dim3 grid(p.n_kv_heads, (p.n_rows + span - 1) / span, a.splits);
+  attention_prefill_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tk, tv, a);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess || a.splits == 1) return err;
+  const long long pairs = (long long)p.n_rows * p.n_heads;
+  attention_prefill_merge_kernel<<<(unsigned)((pairs + 7) / 8), 256, 0, stream>>>(a);
   return cudaGetLastError();
+}
+
+// A grid of fewer CTAs than half the SMs (a few hundred selective rows) gets
+// its key tiles split over up to 4 CTAs per row tile, each split keeping at
+// least 2 key tiles; full prefills (many row tiles) never split.
+int attention_prefill_splits(const AttnPrefillArgs& p, int num_sms) {
+  if (p.ws == nullptr || p.n_rows <= 0 || p.n_kv_heads <= 0) return 1;
+  const int span = kBM / (p.n_heads / p.n_kv_heads);
+  const int ctas = p.n_kv_heads * ((p.n_rows + span - 1) / span);
+  const int key_tiles = (p.n_keys + kBN - 1) / kBN;
+  int s = 1;
+  while (s < 4 && ctas * (s + 1) <= num_sms && key_tiles >= 2 * (s + 1)) ++s;
+  if ((long long)s * p.n_rows * p.n_heads * 132 > p.ws_floats) return 1;
+  return s;
 }
 
 }  // namespace sc

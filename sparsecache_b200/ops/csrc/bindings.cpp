@@ -232,9 +232,15 @@ sc::GemmArgs sharded_gemm(const std::vector<int64_t>& shard_ptrs, int64_t rows, 
 void gemm_ag_qkv(std::vector<int64_t> shard_ptrs, int64_t rows, int64_t own, Tensor ready, int64_t epoch,
                  int64_t K, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_cache, Tensor rope_pos,
                  Tensor cache_slot, Tensor rope_table, int64_t n_q_heads, int64_t n_kv_heads, int64_t bn,
-                 c10::optional<Tensor> dev_part, int64_t dev_mode) {
+                 c10::optional<Tensor> dev_part, int64_t dev_mode, int64_t k_peer, int64_t v_peer) {
   const c10::cuda::CUDAGuard guard(w_qkv.device());
   auto g = sharded_gemm(shard_ptrs, rows, own, ready, epoch, K, w_qkv, sc::EPI_QKV, bn);
+  // optional push of this rank's K/V rows into a peer slot of the same
+  // local geometry (the decode rank with the same TP index); 0 disables it
+  TORCH_CHECK((k_peer == 0) == (v_peer == 0), "k_peer and v_peer go together");
+  TORCH_CHECK((k_peer & 15) == 0 && (v_peer & 15) == 0, "peer K/V bases must be 16-byte aligned");
+  g.ep.k_peer = reinterpret_cast<__nv_bfloat16*>(k_peer);
+  g.ep.v_peer = reinterpret_cast<__nv_bfloat16*>(v_peer);
   if (dev_part.has_value() && dev_part->defined()) {
     CHECK_F32(*dev_part);
     TORCH_CHECK(dev_part->numel() >= (int64_t)g.M * 2 * n_kv_heads, "dev_part size");
@@ -551,10 +557,11 @@ void gemv_argmax(Tensor x, Tensor w, c10::optional<Tensor> norm_w, double eps, T
 }
 
 // ----------------------------------------------------------- attention
-void attention_prefill_impl(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tensor k_cache,
+int64_t attention_prefill_impl(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tensor k_cache,
                             Tensor v_cache, c10::optional<Tensor> kpos, int64_t n_keys,
                             int64_t n_heads, double scale, Tensor out, bool legacy,
-                            c10::optional<Tensor> trace = c10::nullopt) {
+                            c10::optional<Tensor> trace = c10::nullopt,
+                            c10::optional<Tensor> ws = c10::nullopt) {
   const c10::cuda::CUDAGuard guard(q.device());
   check_matrix(q, "q");
   check_matrix(out, "out");
@@ -593,6 +600,12 @@ void attention_prefill_impl(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos,
                 "trace must be a CUDA int64 tensor of >= 640 entries");
     p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
   }
+  if (ws.has_value() && ws->defined()) {
+    CHECK_F32(*ws);
+    CHECK_ALIGN16(*ws);
+    p.ws = ws->data_ptr<float>();
+    p.ws_floats = ws->numel();
+  }
   TORCH_CHECK(k_cache.is_cuda() && v_cache.is_cuda(), "caches must be CUDA tensors");
   CHECK_BF16(k_cache); CHECK_BF16(v_cache);
   CHECK_ALIGN16(k_cache); CHECK_ALIGN16(v_cache);
@@ -600,27 +613,32 @@ void attention_prefill_impl(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos,
   TORCH_CHECK(q.size(1) >= n_heads * 128 && out.size(1) >= n_heads * 128, "q / out narrower than n_heads * 128");
   if (legacy) {
     check_cuda(sc::attention_prefill_mma(p, cur_stream()), "attention_prefill_mma");
+    return 1;
   } else {
     check_cuda(sc::attention_prefill(p, cur_stream()), "attention_prefill");
+    return sc::attention_prefill_splits(p, num_sms()) > 1 ? 2 : 1;  // + the merge kernel
   }
 }
 
-void attention_prefill(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tensor k_cache,
-                       Tensor v_cache, c10::optional<Tensor> kpos, int64_t n_keys,
-                       int64_t n_heads, double scale, Tensor out, c10::optional<Tensor> trace) {
-  attention_prefill_impl(q, q_rows, qpos, k_cache, v_cache, kpos, n_keys, n_heads, scale, out, false, trace);
+// returns the kernels launched (2 when the keys were split: + the merge)
+int64_t attention_prefill(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tensor k_cache,
+                          Tensor v_cache, c10::optional<Tensor> kpos, int64_t n_keys,
+                          int64_t n_heads, double scale, Tensor out, c10::optional<Tensor> trace,
+                          c10::optional<Tensor> ws) {
+  return attention_prefill_impl(q, q_rows, qpos, k_cache, v_cache, kpos, n_keys, n_heads, scale, out, false, trace, ws);
 }
 
-void attention_prefill_mma(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tensor k_cache,
-                           Tensor v_cache, c10::optional<Tensor> kpos, int64_t n_keys,
-                           int64_t n_heads, double scale, Tensor out) {
-  attention_prefill_impl(q, q_rows, qpos, k_cache, v_cache, kpos, n_keys, n_heads, scale, out, true);
+int64_t attention_prefill_mma(Tensor q, c10::optional<Tensor> q_rows, Tensor qpos, Tensor k_cache,
+                              Tensor v_cache, c10::optional<Tensor> kpos, int64_t n_keys,
+                              int64_t n_heads, double scale, Tensor out) {
+  return attention_prefill_impl(q, q_rows, qpos, k_cache, v_cache, kpos, n_keys, n_heads, scale, out, true);
 }
 
 void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int64_t n_heads,
                       double scale, int64_t splits, Tensor out, c10::optional<Tensor> page_table,
                       int64_t page_shift, c10::optional<Tensor> n_virtual, c10::optional<Tensor> ws,
-                      c10::optional<Tensor> counters) {
+                      c10::optional<Tensor> counters, int64_t outer, c10::optional<Tensor> pos_rows,
+                      int64_t seq_stride) {
   const c10::cuda::CUDAGuard guard(q.device());
   CHECK_BF16(q); CHECK_BF16(out); CHECK_I32(pos);
   TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(2) == 128 && k_cache.is_contiguous(), "k_cache");
@@ -652,6 +670,18 @@ void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int6
     TORCH_CHECK(counters->numel() >= (int64_t)a.n_kv_heads * 16, "16 counters per kv head");
     a.ws = ws->data_ptr<float>();
     a.counters = reinterpret_cast<unsigned*>(counters->data_ptr<int>());
+  }
+  TORCH_CHECK(outer >= 0 && outer <= 16, "outer: 0 (automatic) or 1..16 clusters per kv head");
+  a.outer = (int)outer;
+  if (pos_rows.has_value() && pos_rows->defined()) {
+    CHECK_I32(*pos_rows);
+    TORCH_CHECK(q.size(0) == pos_rows->numel() && out.size(0) == pos_rows->numel(),
+                "batched decode attention: one q / out row per sequence");
+    TORCH_CHECK(seq_stride >= 0 && seq_stride % 8 == 0, "seq_stride (elements) must keep rows 16-byte aligned");
+    a.pos_rows = pos_rows->data_ptr<int>();
+    a.seq_stride = seq_stride;
+    a.n_seq = (int)pos_rows->numel();
+    a.M = 1;
   }
   check_cuda(sc::attention_decode(a, cur_stream()), "attention_decode");
 }
@@ -769,13 +799,14 @@ sc::SkinnyArgs skinny_base(const Tensor& x, const Tensor& w, int64_t epi, const 
   a.epi = (int)epi;
   a.num_sms = num_sms();
   a.splits = splits > 0 ? (int)splits : sc::skinny_splits(a.N, a.K, a.num_sms);
-  TORCH_CHECK(ws.numel() >= (int64_t)a.splits * a.N * 16, "workspace [splits][N][16] too small");
+  TORCH_CHECK(a.M >= 1 && a.M <= 32, "the skinny GEMM takes 1..32 rows");
+  TORCH_CHECK(ws.numel() >= (int64_t)a.splits * a.N * sc::skinny_bn(a.M), "workspace [splits][N][bn] too small");
   a.ws = ws.data_ptr<float>();
   a.status = status_tensor(w).data_ptr<int>();
   return a;
 }
 
-// out = epilogue(x @ w^T) for M <= 16 rows on the tensor cores; returns kernels launched.
+// out = epilogue(x @ w^T) for M <= 32 rows on the tensor cores; returns kernels launched.
 int64_t skinny_gemm(Tensor x, Tensor w, int64_t epi, Tensor out, c10::optional<Tensor> residual, Tensor ws,
                     int64_t splits) {
   const c10::cuda::CUDAGuard guard(x.device());
@@ -795,7 +826,7 @@ int64_t skinny_gemm(Tensor x, Tensor w, int64_t epi, Tensor out, c10::optional<T
   return 2;
 }
 
-// Fused QKV (RoPE + K/V cache write) for M <= 16 rows on the tensor cores.
+// Fused QKV (RoPE + K/V cache write) for M <= 32 rows on the tensor cores.
 int64_t skinny_qkv(Tensor x, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_cache, Tensor pos,
                    Tensor rope_table, int64_t n_q_heads, int64_t n_kv_heads, Tensor ws, c10::optional<Tensor> slot,
                    c10::optional<Tensor> pos_rows, int64_t seq_stride) {
@@ -1116,7 +1147,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_ag_qkv", &gemm_ag_qkv, py::arg("shard_ptrs"), py::arg("rows"), py::arg("own"), py::arg("ready"),
         py::arg("epoch"), py::arg("K"), py::arg("w_qkv"), py::arg("q_out"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("rope_pos"), py::arg("cache_slot"), py::arg("rope_table"), py::arg("n_q_heads"),
-        py::arg("n_kv_heads"), py::arg("bn"), py::arg("dev_part") = py::none(), py::arg("dev_mode") = 0);
+        py::arg("n_kv_heads"), py::arg("bn"), py::arg("dev_part") = py::none(), py::arg("dev_mode") = 0,
+        py::arg("k_peer") = 0, py::arg("v_peer") = 0);
   m.def("gemm_ag_swiglu", &gemm_ag_swiglu);
   m.def("gemm_rs", &gemm_rs);
   m.def("rs_reduce", &rs_reduce, py::arg("recv"), py::arg("flags"), py::arg("epoch"), py::arg("timeout_ns"),
@@ -1143,14 +1175,26 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_argmax_grid", &gemv_argmax_grid);
   m.def("attention_prefill", &attention_prefill, py::arg("q"), py::arg("q_rows"), py::arg("qpos"),
         py::arg("k_cache"), py::arg("v_cache"), py::arg("kpos"), py::arg("n_keys"), py::arg("n_heads"),
-        py::arg("scale"), py::arg("out"), py::arg("trace") = py::none());
+        py::arg("scale"), py::arg("out"), py::arg("trace") = py::none(), py::arg("ws") = py::none());
+  m.def("attention_prefill_splits", [](int64_t n_rows, int64_t n_heads, int64_t n_kv_heads, int64_t n_keys,
+                                       int64_t ws_floats, int64_t num_sms) {
+    sc::AttnPrefillArgs p{};
+    p.n_rows = (int)n_rows;
+    p.n_heads = (int)n_heads;
+    p.n_kv_heads = (int)n_kv_heads;
+    p.n_keys = (int)n_keys;
+    p.ws = ws_floats > 0 ? reinterpret_cast<float*>(16) : nullptr;  // only tested for null
+    p.ws_floats = ws_floats;
+    return sc::attention_prefill_splits(p, (int)num_sms);
+  });
   m.def("attention_prefill_mma", &attention_prefill_mma);
   m.def("page_token_scores", &page_token_scores, py::arg("q"), py::arg("keys"), py::arg("n_tokens"),
         py::arg("scale"));
   m.def("attention_decode", &attention_decode, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("pos"), py::arg("n_heads"), py::arg("scale"), py::arg("splits"), py::arg("out"),
         py::arg("page_table") = py::none(), py::arg("page_shift") = 6, py::arg("n_virtual") = py::none(),
-        py::arg("ws") = py::none(), py::arg("counters") = py::none());
+        py::arg("ws") = py::none(), py::arg("counters") = py::none(), py::arg("outer") = 0,
+        py::arg("pos_rows") = py::none(), py::arg("seq_stride") = 0);
   m.def("attention_decode_outer", [](int64_t cap, int64_t kvh, int64_t cluster, int64_t sms) {
     return sc::attention_decode_outer((int)cap, (int)kvh, (int)cluster, (int)sms);
   });

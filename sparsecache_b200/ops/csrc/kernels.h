@@ -167,9 +167,18 @@ struct AttnPrefillArgs {
   int ldo;
   int* status;  // bounded-wait status word
   unsigned long long* trace;  // optional debug timeline (640 entries), null in production
+  // Optional key split for grids that leave SMs idle (few query rows): CTA z
+  // of `splits` streams its share of the row tile's key tiles and leaves
+  // fp32 (O, running max, sum) partials in ws[split][row][head][132]; a merge
+  // kernel combines them.  ws = null or ws_floats too small: no split.
+  float* ws;
+  long long ws_floats;
+  int splits;  // set by the launcher
 };
 
 cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream);
+// key splits the launcher would use for these arguments (1 = none)
+int attention_prefill_splits(const AttnPrefillArgs& p, int num_sms);
 // the mma.sync kernel the tcgen05 one replaced, kept for A/B measurement only
 cudaError_t attention_prefill_mma(const AttnPrefillArgs& p, cudaStream_t stream);
 
@@ -200,6 +209,14 @@ struct AttnDecodeArgs {
   // result does not depend on M.
   float* ws;           // [n_kv_heads][16][32][130] fp32 (null: one cluster per kv head)
   unsigned* counters;  // [n_kv_heads][8] (one per kv head and group of 4 query vectors), zero between launches
+  int outer;           // clusters per kv head; 0 = chosen from the capacity (attention_decode_outer)
+  // Batched sequences (null: one sequence): n_seq independent sequences of
+  // one query row each (M = 1); sequence s's row is q/out row s, it sits at
+  // position pos_rows[s] (keys [0, pos_rows[s]]) and its caches start
+  // s * seq_stride elements after k_cache / v_cache.  One cluster per kv head.
+  const int* pos_rows;
+  long long seq_stride;
+  int n_seq;
 };
 
 cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream);
@@ -270,8 +287,9 @@ struct SkinnyArgs {
   int ldo;
   const __nv_bfloat16* residual;  // [M, N] row stride ldr (SKINNY_RESIDUAL; may alias out)
   int ldr;
-  float* ws;               // [splits][N][16] fp32
+  float* ws;               // [splits][N][bn] fp32, bn = skinny_bn(M)
   int splits;
+  int bn;                  // token-row tile (16 or 32), set by the launcher
   int num_sms;
   int* status;
   // SKINNY_QKV: fused QKV rows (q heads, k heads, v heads of 128): RoPE on
@@ -300,6 +318,8 @@ struct SkinnyArgs {
   unsigned int* counter;
 };
 int skinny_splits(int N, int K, int num_sms);
+// token-row tile of the skinny GEMM for M rows: 16 (M <= 16) or 32 (M <= 32)
+int skinny_bn(int M);
 cudaError_t skinny_gemm(const SkinnyArgs& a, cudaStream_t stream);
 // Row argmax over bf16 logits [M, V] (first index on ties) -> out_token[M].
 cudaError_t row_argmax_bf16(const __nv_bfloat16* logits, int ld, int M, int V, int* out_token, cudaStream_t stream);

@@ -1,16 +1,16 @@
 // Skinny GEMM on the tensor cores for a few token rows (batched verification,
-// small decode batches): out[m, n] = sum_k x[m, k] * w[n, k], M <= 16.
+// small decode batches): out[m, n] = sum_k x[m, k] * w[n, k], M <= 32.
 //
 // At M <= 16 the work is a weight stream; the CUDA-core GEMV (gemv.cu) keeps
 // up with HBM only at M = 1-2 because every extra row costs an unpack and
 // FMAs per weight.  Here the roles are swapped so the tensor core does the
 // rows: the weight tile is the 128-row A operand (TMA, 128-byte swizzle,
 // `tcgen05.mma.cta_group::1.kind::f16` with M = 128), the token rows padded to
-// N = 16 are the B operand (TMA zero-fills rows >= M), and the 128 x 16 fp32
-// accumulator lives in TMEM (two buffers = 32 columns).  Work units are
-// (128-row weight tile, K slice) so that ~one unit per SM streams its slice
-// with a deep (10-stage) TMA pipeline; each unit writes its fp32 partial tile
-// [128 rows][16] to a workspace, and a small reduce kernel sums the K slices
+// N = 16 (M <= 16) or N = 32 (M <= 32) are the B operand (TMA zero-fills rows
+// >= M), and the 128 x N fp32 accumulator lives in TMEM (two buffers).  Work
+// units are (128-row weight tile, K slice) so that ~one unit per SM streams
+// its slice with a deep (10-stage) TMA pipeline; each unit writes its fp32
+// partial tile [128 rows][N] to a workspace, and a small reduce kernel sums the K slices
 // in a fixed order and applies the epilogue (store, residual add with the
 // HF rounding order, SwiGLU over 128-row interleaved gate/up blocks).  The
 // result of a row m does not depend on M (columns never mix in the MMA and
@@ -26,14 +26,19 @@ namespace sc {
 
 namespace {
 constexpr int kSkBM = 128;  // weight rows per tile (MMA M)
-constexpr int kSkBN = 16;   // token rows (MMA N)
 constexpr int kSkBK = 64;   // 128 bytes of bf16 per row
 constexpr int kSkStages = 10;
 constexpr int kSkABytes = kSkBM * kSkBK * 2;  // 16 KB
-constexpr int kSkBBytes = kSkBN * kSkBK * 2;  // 2 KB
-constexpr int kSkStageBytes = kSkABytes + kSkBBytes;
-constexpr int kSkSmem = kSkStages * kSkStageBytes + 1024 + 256;
 constexpr int kSkThreads = 192;
+
+// BN = token rows padded to the MMA N: 16 (M <= 16) or 32 (M <= 32)
+template <int BN>
+struct SkCfg {
+  static constexpr int kBBytes = BN * kSkBK * 2;  // 2 / 4 KB
+  static constexpr int kStageBytes = kSkABytes + kBBytes;
+  static constexpr int kSmem = kSkStages * kStageBytes + 1024 + 256;
+  static constexpr uint32_t kTmemCols = BN == 16 ? 32 : 64;  // two accumulators, power of two >= 32
+};
 
 struct alignas(8) SkBars {
   uint64_t full[kSkStages];
@@ -56,9 +61,12 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
 }
 }  // namespace
 
+template <int BN>
 __global__ void __launch_bounds__(kSkThreads, 1)
     skinny_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                       int N, int K, int splits, float* ws, int* status) {
+  using Cfg = SkCfg<BN>;
+  constexpr int kSkStageBytes = Cfg::kStageBytes;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   SkBars* bars = reinterpret_cast<SkBars*>(smem + kSkStages * kSkStageBytes);
@@ -79,7 +87,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     tma_prefetch_desc(&tmap_x);
   }
   if (warp == 1) {
-    tmem_alloc(&bars->tmem_base, 32);
+    tmem_alloc(&bars->tmem_base, Cfg::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -119,7 +127,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(kSkBM, kSkBN);
+      constexpr uint32_t idesc = make_idesc_bf16(kSkBM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -134,7 +142,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t tacc = tmem_base + buf * kSkBN;
+        const uint32_t tacc = tmem_base + buf * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&bars->full[stage], phase, status, kStatusTimeoutTmaFull)) {
             ok = false;
@@ -168,14 +176,19 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       const uint32_t tphase = (local >> 1) & 1;
       if (!mbar_wait(&bars->tmem_full[buf], tphase, status, kStatusTimeoutTmemFull)) break;
       tc_fence_after();
-      uint32_t r[16];
-      tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * kSkBN, r);
+      uint32_t r[BN];
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
+      if constexpr (BN == 16) {
+        tmem_ld_32x32b_x16(taddr, r);
+      } else {
+        tmem_ld_32x32b_x32(taddr, r);
+      }
       tmem_ld_wait();
       const int row = tile * kSkBM + quarter * 32 + lane;
       if (row < N) {
-        float4* d = reinterpret_cast<float4*>(ws + ((size_t)ks * N + row) * kSkBN);
+        float4* d = reinterpret_cast<float4*>(ws + ((size_t)ks * N + row) * BN);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < BN / 4; ++i)
           d[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]), __uint_as_float(r[4 * i + 2]),
                              __uint_as_float(r[4 * i + 3]));
       }
@@ -187,7 +200,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, 32);
+  if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
 }
 
 // Sum the K slices in order and apply the epilogue; one thread per (row m, output j)
@@ -203,7 +216,7 @@ __global__ void skinny_reduce_kernel(SkinnyArgs a) {
   const int m = active ? idx / outs : 0, j = active ? idx % outs : 0;
   auto sum_row = [&](int n) {
     float v = 0.f;
-    for (int s = 0; s < a.splits; ++s) v += a.ws[((size_t)s * a.N + n) * kSkBN + m];
+    for (int s = 0; s < a.splits; ++s) v += a.ws[((size_t)s * a.N + n) * a.bn + m];
     return v;
   };
   if (active) {
@@ -335,34 +348,37 @@ int skinny_splits(int N, int K, int num_sms) {
   return best;
 }
 
-cudaError_t skinny_gemm(const SkinnyArgs& a, cudaStream_t stream) {
-  if (a.M < 1 || a.M > kSkBN || a.K % kSkBK != 0 || a.N % 2 != 0) return cudaErrorInvalidValue;
+int skinny_bn(int M) { return M <= 16 ? 16 : 32; }
+
+cudaError_t skinny_gemm(const SkinnyArgs& args, cudaStream_t stream) {
+  SkinnyArgs a = args;
+  if (a.M < 1 || a.M > 32 || a.K % kSkBK != 0 || a.N % 2 != 0) return cudaErrorInvalidValue;
+  a.bn = skinny_bn(a.M);
   if (a.epi == SKINNY_SWIGLU && a.N % 256 != 0) return cudaErrorInvalidValue;
   if (a.epi == SKINNY_QKV && (a.N % 128 != 0 || a.N != (a.n_q_heads + 2 * a.n_kv_heads) * 128))
     return cudaErrorInvalidValue;
   if (a.epi == SKINNY_ALLREDUCE && (a.ar_tp < 1 || a.ar_tp > 8 || a.counter == nullptr)) return cudaErrorInvalidValue;
   CUtensorMap tw, tx;
   if (!make_tmap_2d_bf16(&tw, a.w, a.K, a.N, a.ldw, kSkBK, kSkBM, true)) return cudaErrorInvalidValue;
-  if (!make_tmap_2d_bf16(&tx, a.x, a.K, a.M, a.ldx, kSkBK, kSkBN, true)) return cudaErrorInvalidValue;
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaFuncSetAttribute(skinny_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSkSmem);
-    attr_done = true;
-  }
+  if (!make_tmap_2d_bf16(&tx, a.x, a.K, a.M, a.ldx, kSkBK, a.bn, true)) return cudaErrorInvalidValue;
+  ensure_smem_attr(skinny_mma_kernel<16>, SkCfg<16>::kSmem);
+  ensure_smem_attr(skinny_mma_kernel<32>, SkCfg<32>::kSmem);
   const int tiles = (a.N + kSkBM - 1) / kSkBM;
   const int units = tiles * a.splits;
   const int grid = units < a.num_sms ? units : a.num_sms;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kSkThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSkSmem;
+  cfg.dynamicSmemBytes = a.bn == 16 ? SkCfg<16>::kSmem : SkCfg<32>::kSmem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_mma_kernel, tw, tx, a.N, a.K, a.splits, a.ws, a.status);
+  cudaError_t e = a.bn == 16
+                      ? cudaLaunchKernelEx(&cfg, skinny_mma_kernel<16>, tw, tx, a.N, a.K, a.splits, a.ws, a.status)
+                      : cudaLaunchKernelEx(&cfg, skinny_mma_kernel<32>, tw, tx, a.N, a.K, a.splits, a.ws, a.status);
   if (e != cudaSuccess) return e;
   const int outs = ((a.epi == SKINNY_SWIGLU || a.epi == SKINNY_QKV) ? a.N / 2 : a.N) * a.M;
   cfg.gridDim = dim3((outs + 255) / 256, 1, 1);

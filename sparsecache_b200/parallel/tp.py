@@ -148,7 +148,7 @@ def local_config(cfg: ModelConfig, tp: int) -> ModelConfig:
 class TPEngine:
     """Sequence/tensor-parallel prefill over a TP group with fused collectives."""
 
-    MAX_BATCH = 16  # rows of a batched decode step (skinny tensor-core GEMM limit)
+    MAX_BATCH = 32  # rows of a batched decode step (skinny tensor-core GEMM limit)
 
     def __init__(self, cfg: ModelConfig, weights: EngineWeights, group: TPGroup, *, max_rows: int,
                  max_positions: int = 65536, verify_backend: str = "skinny") -> None:
@@ -201,7 +201,7 @@ class TPEngine:
             lc, w0 = self.lcfg, weights.layers[0]
             shapes = [tuple(w0.w_qkv.shape), tuple(w0.w_o.shape), tuple(w0.w_gu.shape), tuple(w0.w_down.shape),
                       tuple(weights.lm_head.shape)]
-            need = max(int(self.ext.skinny_splits(n, k)) * n * 16 for n, k in shapes)
+            need = max(int(self.ext.skinny_splits(n, k)) * n * 32 for n, k in shapes)
             self.skinny_ws = torch.empty(need, device=group.device, dtype=torch.float32)
 
     @classmethod
@@ -254,13 +254,16 @@ class TPEngine:
 
     def _layer(self, layer: int, rows: int, pos: torch.Tensor, slots: torch.Tensor, n_keys: int,
                h: torch.Tensor, nxt_norm: torch.Tensor, slot: KVSlot, *, dev_part: torch.Tensor | None = None,
-               dev_mode: int = 0) -> int:
+               dev_mode: int = 0, push=None) -> int:
         """One fused TP layer over tp * rows rows (this rank's residual shard ``h`` [rows, d]).
 
         The normed input shard must already be in ``x_buf``; on return the
         next layer's normed input (``nxt_norm``) is there.  Rows write K/V at
         cache ``slots`` with RoPE ``pos`` and attend causally (by position) to
-        keys [0, n_keys).  Returns the epoch used.
+        keys [0, n_keys).  With ``push`` (a ``PushTarget`` of a peer slot with
+        this rank's local geometry) the QKV epilogue also stores the local kv
+        heads' rows into it and the layer's flag is released right after the
+        GEMM.  Returns the epoch used.
         """
         ext, eng, cfg, lc = self.ext, self.engine, self.full_cfg, self.lcfg
         d, n = cfg.d_model, rows * self.tp
@@ -275,7 +278,10 @@ class TPEngine:
         self._signal_all(FLAG_X, e)
         bases = self._pull_shards(FLAG_X, FLAG_STAGE_X, self.x_ptrs, self.stage_x, rows, e)
         ext.gemm_ag_qkv(bases, rows, self.rank, self.flags[FLAG_STAGE_X], e, d, lw.w_qkv, q, slot.k(layer),
-                        slot.v(layer), pos, slots, eng.rope, lc.n_heads, lc.n_kv_heads, bn, dev_part, dev_mode)
+                        slot.v(layer), pos, slots, eng.rope, lc.n_heads, lc.n_kv_heads, bn, dev_part, dev_mode,
+                        push.k(layer) if push is not None else 0, push.v(layer) if push is not None else 0)
+        if push is not None:
+            ext.peer_signal(push.flag(layer), push.epoch)
         ext.attention_prefill(q, None, pos, slot.k(layer), slot.v(layer), None, n_keys, lc.n_heads, eng.scale, attn)
         ext.gemm_rs(attn, lw.w_o, self.recv_o_ptrs, rows, self.rank, bn)
         self._signal_all(FLAG_RS_O, e)
@@ -312,16 +318,20 @@ class TPEngine:
         self.ext.rmsnorm(h, None, eng.w.layers[0].ln1, cfg.rms_eps, x)
         return h, rows, Tp, eng._arange("pos", Tp)
 
-    def prefill(self, ids: torch.Tensor, slot: KVSlot) -> tuple[torch.Tensor, int, int]:
+    def prefill(self, ids: torch.Tensor, slot: KVSlot, *, push=None) -> tuple[torch.Tensor, int, int]:
         """Prefill ids (all ranks pass the same int32 device ids).
 
         Returns (this rank's final-normed hidden shard [rows, d], rows, padded
-        length).  The shard owning row T-1 holds the last prompt row.
+        length).  The shard owning row T-1 holds the last prompt row.  With
+        ``push`` every layer's local K/V rows (padded rows included, they sit
+        past the prompt) are stored into the peer slot as they are written.
         """
         T = ids.numel()
         h, rows, Tp, pos = self._embed_shard(ids, T, slot)
+        if push is not None and push.capacity != slot.capacity:
+            raise ValueError("the pushed slot must have the local slot's capacity")
         for layer in range(self.full_cfg.n_layers):
-            self._layer(layer, rows, pos, pos, Tp, h, self._next_norm(layer), slot)
+            self._layer(layer, rows, pos, pos, Tp, h, self._next_norm(layer), slot, push=push)
         return self._views(rows)[0], rows, Tp
 
     def cacheblend(self, ids: torch.Tensor, slot: KVSlot, *, prefix_tokens: int, suffix_tokens: int,
@@ -401,12 +411,13 @@ class TPEngine:
 
     # ------------------------------------------------------------- decode
     def first_token(self, x_shard: torch.Tensor, rows: int, T: int, *, max_new: int,
-                    last_row: int | None = None) -> None:
+                    last_row: int | None = None) -> torch.Tensor:
         """The owner of the last prompt row runs the LM head and sends the token to every rank.
 
         ``last_row`` is that row's index in the sharded layout (default T-1;
         after CacheBlend it is the last active row, A-1); the next token is at
-        position T.
+        position T.  Returns the token's device view (int32 [1], in this
+        rank's flag block).
         """
         eng, ext = self.engine, self.ext
         last = T - 1 if last_row is None else int(last_row)
@@ -424,6 +435,16 @@ class TPEngine:
                                  self.token_epoch)
         ext.wait_flag(self.flags[FLAG_TOKEN_EPOCH], owner, self.token_epoch, TIMEOUT_NS, self.status)
         tok = self.flags[FLAG_TOKEN, owner:owner + 1]
+        self.seed_decode(tok, T, max_new=max_new)
+        return tok
+
+    def seed_decode(self, tok: torch.Tensor, T: int, *, max_new: int) -> None:
+        """Start greedy decode from a first token (device int32 [1], same on every rank) at position T.
+
+        Used after ``first_token`` and by a decode group whose prompt K/V and
+        seed token were pushed by a prefill group."""
+        eng, ext = self.engine, self.ext
+        b = eng._decode_buffers(max_new)
         ext.embedding(tok, eng.w.embed, b["h"][:1])
         b["log"][0:1].copy_(tok)
         b["gen"].fill_(1)
@@ -693,9 +714,9 @@ class TPEngine:
             ext.rmsnorm(h, None, lw.ln1, cfg.rms_eps, x)
             ext.skinny_qkv(x, lw.w_qkv, bb["q"][:B], slots[0].k(layer), slots[0].v(layer), pos_rows, eng.rope,
                            lc.n_heads, lc.n_kv_heads, ws, pos_rows=pos_rows, seq_stride=stride)
-            for i, sl in enumerate(slots):
-                ext.attention_decode(bb["q"][i:i + 1], sl.k(layer), sl.v(layer), pos_rows[i:i + 1], lc.n_heads,
-                                     eng.scale, splits, bb["attn"][i:i + 1], ws=b["attn_ws"], counters=b["attn_cnt"])
+            # every sequence in one launch: row b reads its own slot (stride apart) at pos_rows[b]
+            ext.attention_decode(bb["q"][:B], slots[0].k(layer), slots[0].v(layer), pos_rows, lc.n_heads, eng.scale,
+                                 splits, bb["attn"][:B], pos_rows=pos_rows, seq_stride=stride)
             self.allreduce(bb["attn"][:B], lw.w_o, 2 * layer + 1, h, skinny=True)
             ext.rmsnorm(h, None, lw.ln2, cfg.rms_eps, x)
             ext.skinny_gemm(x, lw.w_gu, 2, bb["act"][:B], None, ws)
@@ -734,7 +755,7 @@ class TPEngine:
             eng._graphs[key] = graph
         for _ in range(n_steps):
             graph.replay()
-        per_layer = 10 + len(slots)
+        per_layer = 11
         self.ext.launches += n_steps * (per_layer * len(eng.w.layers) + 6)
 
     def batch_tokens(self, n_seq: int, n_tokens: int) -> list[list[int]]:

@@ -120,10 +120,11 @@ def main() -> None:
                 res[f"gemm_M{M}_{name}"] = {"us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS,
                                             "weight_GBps": N * K * 2 / (t * 1e-6) / 1e9}
 
-    if "gemm_small" in only or "gemm_down_splitk" in only or "gemm_gate_up" in only:
+    if "gemm_small" in only or "gemm_down_splitk" in only or "gemm_gate_up" in only or "gemm_gate_up_big" in only:
         # CacheBlend active rows (~15% of a 1.7k-token prompt): the layer's four
-        # projections as the engine issues them (128-wide QKV tiles, split-K o/down)
-        M = 300
+        # projections as the engine issues them (128-wide QKV tiles, split-K o/down);
+        # gemm_gate_up_big: the SwiGLU projection of a full 2048-row prefill
+        M = 2048 if "gemm_gate_up_big" in only else 300
         cases = (("qkv_bn128", 6144, 4096, "store", 128), ("o_splitk", 4096, 4096, "residual", 256),
                  ("gate_up", 28672, 4096, "swiglu", 256), ("down_splitk", 4096, 14336, "residual", 256))
         if "gemm_small" not in only:
@@ -167,6 +168,33 @@ def main() -> None:
             res[f"attn_decode_ctx{cap}"] = {"us": t, "GBps": gbs, "frac_of_measured_hbm": gbs / HBM_GBS,
                                             "cluster": S, "clusters_per_kv_head": R,
                                             "l2_resident": kv_bytes < 126e6}
+
+    if "attn_decode_serving" in only:
+        # the 8B serving shape: 32 layer caches of one slot (cycled, so K/V come
+        # from HBM as in a decode step) at the bench capacity, keys = a typical
+        # and a long prompt; cluster size x clusters per kv head
+        H, Hkv, cap, layers = 32, 8, 2768, 32
+        kcs = [torch.randn(Hkv, cap, 128, device=dev).to(bf) for _ in range(layers)]
+        vcs = [torch.randn(Hkv, cap, 128, device=dev).to(bf) for _ in range(layers)]
+        q = torch.randn(1, H * 128, device=dev).to(bf)
+        out = torch.empty(1, H * 128, device=dev, dtype=bf)
+        ws = torch.zeros(Hkv * ATTN_WS_PER_KVH, device=dev)
+        cnt = torch.zeros(Hkv * ATTN_CNT_PER_KVH, device=dev, dtype=torch.int32)
+        auto = (int(ext.attention_decode_cluster(cap, Hkv)),
+                int(ext.attention_decode_outer(cap, Hkv, int(ext.attention_decode_cluster(cap, Hkv)), ext.num_sms())))
+        for n_keys in (1676, 2600):
+            pos = torch.tensor([n_keys - 1], device=dev, dtype=torch.int32)
+            for S in (4, 8, 16):
+                for R in (1, 2, 3, 4, 6, 8):
+                    def run_all():
+                        for i in range(layers):
+                            ext.attention_decode(q, kcs[i], vcs[i], pos, H, 1 / math.sqrt(128), S, out, ws=ws,
+                                                 counters=cnt, outer=R)
+                    t = timeit(run_all, n=10, warm=3) / layers
+                    kv_bytes = 2 * Hkv * n_keys * 128 * 2
+                    res[f"attn_decode_serving_keys{n_keys}_S{S}_R{R}"] = {
+                        "us": t, "frac_of_measured_hbm": kv_bytes / (t * 1e-6) / 1e9 / HBM_GBS,
+                        "automatic": (S, R) == auto}
 
     if "attn_decode_grid" in only:
         # cluster size x (one / several clusters per kv head) for the decode shapes that matter

@@ -157,13 +157,16 @@ def _attn_reference(q, kc, vc, qpos, kpos, n_heads):
     return (p @ v).transpose(0, 1).reshape(R, n_heads * 128)
 
 
+@pytest.mark.parametrize("split", [False, True])
 @pytest.mark.parametrize("T,R", [(777, 150), (1676, 300), (65, 1), (129, 3)])
 @pytest.mark.parametrize("case", ["causal", "selective", "staged", "growing"])
-def test_attention_prefill(cuda_device, case, T, R):
+def test_attention_prefill(cuda_device, case, T, R, split):
     """tcgen05 flash attention vs the fp32 reference: full causal rows, a sorted
     subset of rows over the whole cache (CacheBlend), staged key positions (a
     suffix at later global positions), and scores that grow along the keys so
-    the lazily rescaled running max moves many times (the O-in-TMEM rescale)."""
+    the lazily rescaled running max moves many times (the O-in-TMEM rescale).
+    With ``split`` the kernel gets a workspace and splits the key tiles of
+    small grids over several CTAs (fp32 partials + merge kernel)."""
     H, Hkv = 8, 2
     cap = T + 223
     g = torch.Generator(device="cpu").manual_seed(T * 7 + R + len(case))
@@ -188,8 +191,14 @@ def test_attention_prefill(cuda_device, case, T, R):
     if case == "growing":
         qfull = (qfull.float() * 2.0).to(torch.bfloat16)
     out = torch.empty(rows.numel(), H * 128, device=cuda_device, dtype=torch.bfloat16)
+    ws = None
+    if split:
+        ws = torch.full((4 * rows.numel() * H * 132,), float("nan"), device=cuda_device)
+        n_split = _ext().attention_prefill_splits(rows.numel(), H, Hkv, T, ws.numel(), _ext().num_sms())
+        if T >= 777:
+            assert n_split > 1
     _ext().attention_prefill(
-        qfull, rows, qpos, kc, vc, kpos if case == "staged" else None, T, H, 1 / math.sqrt(128), out
+        qfull, rows, qpos, kc, vc, kpos if case == "staged" else None, T, H, 1 / math.sqrt(128), out, ws=ws
     )
     torch.cuda.synchronize()
     assert int(_ext().status(out).item()) == 0
@@ -214,6 +223,34 @@ def test_attention_decode(cuda_device, M):
         _ext().attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), splits, out)
         torch.cuda.synchronize()
         torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("hkv,G", [(2, 4), (1, 8)])
+def test_attention_decode_batched_sequences(cuda_device, hkv, G):
+    """One launch over B independent sequences (own position, own slot stride apart) equals one
+    launch per sequence bit for bit, and the fp32 reference."""
+    H, cap, B = hkv * G, 900, 5
+    g = torch.Generator(device="cpu").manual_seed(11 + hkv)
+    kc = torch.randn(B, hkv, cap, 128, generator=g).to(cuda_device, torch.bfloat16)
+    vc = torch.randn(B, hkv, cap, 128, generator=g).to(cuda_device, torch.bfloat16)
+    q = torch.randn(B, H * 128, generator=g).to(cuda_device, torch.bfloat16)
+    positions = [37, 899, 400, 0, 511]
+    pos_rows = torch.tensor(positions, device=cuda_device, dtype=torch.int32)
+    out = torch.empty(B, H * 128, device=cuda_device, dtype=torch.bfloat16)
+    stride = hkv * cap * 128
+    for splits in (4, 8):
+        _ext().attention_decode(q, kc[0], vc[0], pos_rows, H, 1 / math.sqrt(128), splits, out,
+                                pos_rows=pos_rows, seq_stride=stride)
+        torch.cuda.synchronize()
+        for b, p in enumerate(positions):
+            one = torch.empty(1, H * 128, device=cuda_device, dtype=torch.bfloat16)
+            pos = torch.tensor([p], device=cuda_device, dtype=torch.int32)
+            _ext().attention_decode(q[b:b + 1], kc[b], vc[b], pos, H, 1 / math.sqrt(128), splits, one)
+            torch.cuda.synchronize()
+            assert torch.equal(one, out[b:b + 1]), (splits, b)
+            ref = _attn_reference(q[b:b + 1], kc[b, :, :p + 1], vc[b, :, :p + 1],
+                                  torch.tensor([p], device=cuda_device), torch.arange(p + 1, device=cuda_device), H)
+            torch.testing.assert_close(out[b:b + 1].float(), ref, rtol=2e-2, atol=2e-2)
 
 
 @pytest.mark.parametrize("M", [1, 4])
@@ -486,15 +523,16 @@ def test_lse_gather_forward_backward(cuda_device):
     assert _rel_err(f.grad, fr.grad) < 3e-2
 
 
-@pytest.mark.parametrize("M", [1, 5, 16])
+@pytest.mark.parametrize("M", [1, 5, 16, 17, 32])
 def test_skinny_tensor_core_gemm(cuda_device, M):
-    """Swap-AB tcgen05 GEMM for a few rows: store / residual / SwiGLU against fp32, rows independent of M."""
+    """Swap-AB tcgen05 GEMM for a few rows: store / residual / SwiGLU against fp32, rows independent of M
+    (M <= 16 runs the 16-row token tile, 17..32 the 32-row tile; row 0 must match a 1-row call bitwise)."""
     ext = _ext()
     K, N = 4096, 1536
     x = (torch.randn(M, K, device=cuda_device) * 0.5).to(torch.bfloat16)
     w = (torch.randn(N, K, device=cuda_device) * 0.02).to(torch.bfloat16)
     splits = int(ext.skinny_splits(N, K))
-    ws = torch.empty(splits * N * 16, device=cuda_device)
+    ws = torch.empty(splits * N * 32, device=cuda_device)
     out = torch.empty(M, N, device=cuda_device, dtype=torch.bfloat16)
     ext.skinny_gemm(x, w, 0, out, None, ws)
     ref = x.float() @ w.float().T
