@@ -526,18 +526,29 @@ cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-// A grid of fewer CTAs than half the SMs (a few hundred selective rows) gets
-// its key tiles split over up to 4 CTAs per row tile, each split keeping at
-// least 2 key tiles; full prefills (many row tiles) never split.
+// A grid of fewer CTAs than SMs (a few hundred selective rows over a long
+// cache) gets its key tiles split over up to 4 CTAs per row tile, each split
+// keeping at least 16 key tiles (2048 keys: below that a CTA's fixed costs -
+// TMEM allocation, Q staging, pipeline fill - outweigh the shorter key loop;
+// 300 rows over 1676 keys ran 31.7 us whole and 41.5 us split three ways);
+// full prefills (a wave of row tiles or more) never split.
 int attention_prefill_splits(const AttnPrefillArgs& p, int num_sms) {
-  if (p.ws == nullptr || p.n_rows <= 0 || p.n_kv_heads <= 0) return 1;
+  if (p.ws == nullptr || p.n_rows <= 0 || p.n_kv_heads <= 0 || num_sms <= 0) return 1;
   const int span = kBM / (p.n_heads / p.n_kv_heads);
   const int ctas = p.n_kv_heads * ((p.n_rows + span - 1) / span);
+  if (ctas >= num_sms) return 1;
   const int key_tiles = (p.n_keys + kBN - 1) / kBN;
-  int s = 1;
-  while (s < 4 && ctas * (s + 1) <= num_sms && key_tiles >= 2 * (s + 1)) ++s;
-  if ((long long)s * p.n_rows * p.n_heads * 132 > p.ws_floats) return 1;
-  return s;
+  // one CTA per SM (224 KB of shared memory): s splits take ceil(ctas * s /
+  // SMs) waves of 1/s of the work each, plus a merge; pick the cheapest
+  int best_s = 1;
+  double best = 1.0;
+  for (int s = 2; s <= 4 && key_tiles >= 16 * s; ++s) {
+    const int waves = (ctas * s + num_sms - 1) / num_sms;
+    const double cost = (double)waves / s + 0.1;
+    if (cost < best) best = cost, best_s = s;
+  }
+  if ((long long)best_s * p.n_rows * p.n_heads * 132 > p.ws_floats) return 1;
+  return best_s;
 }
 
 }  // namespace sc

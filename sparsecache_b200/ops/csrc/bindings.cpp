@@ -79,8 +79,8 @@ void run_gemm(const sc::GemmArgs& g) {
 // Split-K for STORE/RESIDUAL GEMMs whose output has too few tiles to fill the
 // SMs (small M): K-slices write fp32 partials, an ordered reduce applies the
 // epilogue.  splits < 0 picks automatically; 1 disables.
-int auto_splits(const sc::GemmArgs& g) {
-  const int tiles = ((g.M + 127) / 128) * ((g.N + g.bn - 1) / g.bn);
+int auto_splits(const sc::GemmArgs& g, int rows_per_tile) {
+  const int tiles = ((g.M + rows_per_tile - 1) / rows_per_tile) * ((g.N + g.bn - 1) / g.bn);
   const int num_kb = (g.K + 63) / 64;
   if (2 * tiles > g.num_sms) return 1;
   int s = g.num_sms / tiles;
@@ -89,8 +89,38 @@ int auto_splits(const sc::GemmArgs& g) {
   return s < 2 ? 1 : s;
 }
 
-bool run_gemm_split(sc::GemmArgs g, int64_t splits, const Tensor& like) {
-  const int s = splits < 0 ? auto_splits(g) : (int)splits;
+// Tile rows forced for every GEMM (0: chosen per call); a test hook.
+static int g_rows_policy = 0;
+void set_gemm_rows_per_tile(int64_t rows) {
+  TORCH_CHECK(rows == 0 || rows == 128 || rows == 256, "rows per tile: 0 (automatic), 128 or 256");
+  g_rows_policy = (int)rows;
+}
+
+// Tile shape of an unsharded GEMM: 128-row tiles, or 256-row tiles (two TMEM
+// accumulators sharing each B k-block) when the cost model prefers them; with
+// `may_split`, the split-K count of each shape is priced in as well (partials
+// written and read back by the ordered reduce).  Returns the split count.
+int choose_shape(sc::GemmArgs& g, bool may_split, int64_t splits_req) {
+  // 256-row tiles pay off from ~3 full m-tiles on (B200, 8B shapes: o / gate-up / down 1.2-1.4x
+  // faster at 1676 rows, equal or slower at 300 rows where the k-loop is latency-bound)
+  const bool two_ok = g.bn == 256 && g.shards.n <= 1 && g.epi != sc::EPI_RS &&
+                      (g.M >= 768 || (g_rows_policy == 256 && g.M > 128));
+  double best = 0.0;
+  int best_rows = 128, best_s = 1;
+  bool have = false;
+  for (int rows : {128, 256}) {
+    if (rows == 256 && !two_ok) continue;
+    if (g_rows_policy != 0 && rows != g_rows_policy && !(rows == 128 && !two_ok)) continue;
+    const int s = !may_split ? 1 : (splits_req < 0 ? auto_splits(g, rows) : (int)splits_req);
+    double cost = sc::gemm_cost_estimate(g.M, g.N, g.K, g.bn, rows, s, g.num_sms);
+    if (s > 1) cost += ((double)g.M * g.N * 4.0 * (s + 1) + (double)g.M * g.N * 4.0) / (6.5e12 / 1.9e9);
+    if (!have || cost < best) best = cost, best_rows = rows, best_s = s, have = true;
+  }
+  g.rows_per_tile = best_rows;
+  return best_s;
+}
+
+bool run_gemm_split(sc::GemmArgs g, int s, const Tensor& like) {
   if (s <= 1 || g.M == 0) return false;
   Tensor ws = torch::empty({s, g.M, g.N}, like.options().dtype(torch::kFloat32));
   const __nv_bfloat16* residual = g.epi == sc::EPI_RESIDUAL ? g.ep.residual : nullptr;
@@ -114,7 +144,8 @@ int64_t gemm_store(Tensor a, Tensor w, Tensor out, int64_t bn, int64_t splits) {
   TORCH_CHECK(g.N % 32 == 0, "N must be a multiple of 32");
   g.ep.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   g.ep.ldo = (int)out.stride(0);
-  if (run_gemm_split(g, splits, a)) return 2;  // kernels launched
+  const int s = choose_shape(g, true, splits);
+  if (run_gemm_split(g, s, a)) return 2;  // kernels launched
   run_gemm(g);
   return 1;
 }
@@ -132,7 +163,8 @@ int64_t gemm_residual(Tensor a, Tensor w, Tensor out, Tensor residual, int64_t b
   g.ep.ldo = (int)out.stride(0);
   g.ep.residual = reinterpret_cast<const __nv_bfloat16*>(residual.data_ptr());
   g.ep.ldr = (int)residual.stride(0);
-  if (run_gemm_split(g, splits, a)) return 2;  // kernels launched
+  const int s = choose_shape(g, true, splits);
+  if (run_gemm_split(g, s, a)) return 2;  // kernels launched
   run_gemm(g);
   return 1;
 }
@@ -146,6 +178,7 @@ void gemm_swiglu(Tensor a, Tensor w_gu, Tensor out, int64_t bn) {
   TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == w_gu.size(0) / 2, "out shape");
   g.ep.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   g.ep.ldo = (int)out.stride(0);
+  choose_shape(g, false, 1);
   run_gemm(g);
 }
 
@@ -187,6 +220,7 @@ void gemm_qkv(Tensor a, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_cac
   g.ep.k_peer = reinterpret_cast<__nv_bfloat16*>(k_peer);
   g.ep.v_peer = reinterpret_cast<__nv_bfloat16*>(v_peer);
   TORCH_CHECK((k_peer == 0) == (v_peer == 0), "k_peer and v_peer go together");
+  choose_shape(g, false, 1);
   run_gemm(g);
 }
 
@@ -1150,6 +1184,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("n_kv_heads"), py::arg("bn"), py::arg("dev_part") = py::none(), py::arg("dev_mode") = 0,
         py::arg("k_peer") = 0, py::arg("v_peer") = 0);
   m.def("gemm_ag_swiglu", &gemm_ag_swiglu);
+  m.def("set_gemm_rows_per_tile", &set_gemm_rows_per_tile);
+  m.def("gemm_cost_estimate", [](int64_t M, int64_t N, int64_t K, int64_t bn, int64_t rows, int64_t splits,
+                                 int64_t sms) {
+    return sc::gemm_cost_estimate((int)M, (int)N, (int)K, (int)bn, (int)rows, (int)splits,
+                                  sms > 0 ? (int)sms : num_sms());
+  }, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("bn"), py::arg("rows"), py::arg("splits"),
+     py::arg("sms") = 0);
   m.def("gemm_rs", &gemm_rs);
   m.def("rs_reduce", &rs_reduce, py::arg("recv"), py::arg("flags"), py::arg("epoch"), py::arg("timeout_ns"),
         py::arg("status"), py::arg("residual"), py::arg("out"), py::arg("norm_w"), py::arg("norm_out"),

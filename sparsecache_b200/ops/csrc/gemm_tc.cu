@@ -6,11 +6,23 @@
 //   warp 0      TMA producer: 128B-swizzled A/B tiles into a STAGES-deep ring
 //   warp 1      MMA issuer: tcgen05.mma (M=128, N=BN, K=16) into TMEM,
 //               owns the TMEM allocation
-//   warps 2..5  epilogue: tcgen05.ld the fp32 accumulator (one row per
+//   warps 2..   epilogue: tcgen05.ld the fp32 accumulator (one row per
 //               thread), apply the fused epilogue and store bf16
-// The accumulator is double-buffered in TMEM so the epilogue of tile i
-// overlaps the MMAs of tile i+1.  No cluster multicast is used anywhere, so
-// the same kernel is safe inside multi-GPU programs.
+// Two tile shapes (ACC = accumulators per tile):
+//   ACC = 1   128 x BN tiles, the accumulator double-buffered in TMEM so the
+//             epilogue of tile i overlaps the MMAs of tile i+1; 4 epilogue warps.
+//   ACC = 2   256 x 256 tiles: every B k-block in shared memory feeds two
+//             M=128 MMAs (rows 0-127 and 128-255 of the A k-block) into two
+//             accumulators that fill the 512 TMEM columns (no double buffer;
+//             8 epilogue warps drain both halves at once).  Per k-block the
+//             CTA moves 64 KB from L2 for 256x256 outputs instead of 48 KB for
+//             128x256: the 128x256 shape is L2-bandwidth-bound on B200 (ncu:
+//             L2 throughput ~80 % with the tensor pipe ~55 % busy), this one
+//             a third less so.  A last m-tile with <= 128 valid rows runs one
+//             accumulator only.  Not used with row-sharded A (TP all-gather)
+//             or the reduce-scatter epilogue.
+// No cluster multicast is used anywhere, so the same kernel is safe inside
+// multi-GPU programs.
 //
 // Fused epilogues (the hot projections of a Llama layer):
 //   EPI_STORE     C = acc
@@ -31,6 +43,8 @@
 // apply_rope), modeling.py:257-264 (scatter of fresh K/V into the composed
 // cache), modeling.py:215-226 / reuse_cacheblend_pipeline.py:586-604
 // (squared deviation of fresh vs cached K or V), HF LlamaMLP SwiGLU.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -41,14 +55,19 @@ constexpr int kGemmBK = 64;
 constexpr int kGemmThreads = 192;
 constexpr int kPrefetchKb = 6;  // k-blocks of L2 prefetch ahead of the smem ring
 
-template <int BN>
+template <int BN, int ACC = 1>
 struct GemmCfg {
-  static constexpr int kStages = (BN == 256) ? 4 : 6;
-  static constexpr int kABytes = kGemmBM * kGemmBK * 2;
+  static_assert(ACC == 1 || (ACC == 2 && BN == 256), "two accumulators only with 256-column tiles");
+  static constexpr int kBM = kGemmBM * ACC;  // rows per tile
+  static constexpr int kStages = ACC == 2 ? 3 : ((BN == 256) ? 4 : 6);
+  static constexpr int kABytes = kBM * kGemmBK * 2;
   static constexpr int kBBytes = BN * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
-  static constexpr int kEpiStageBytes = 4 * 32 * 33 * 4;  // per-warp transpose tiles (EPI_RS)
+  static constexpr int kNumBuf = ACC == 2 ? 1 : 2;  // TMEM accumulator buffers
+  static constexpr int kTmemCols = kNumBuf * ACC * BN;  // 256 or 512 columns
+  static constexpr int kEpiWarps = 4 * ACC;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kEpiStageBytes = ACC == 1 ? 4 * 32 * 33 * 4 : 0;  // per-warp transpose tiles (EPI_RS)
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256 + kEpiStageBytes;
 };
 
@@ -264,12 +283,20 @@ struct AMaps {
   CUtensorMap m[kMaxShards];
 };
 
-// Tile t -> (m-tile, n-tile).  With a row-sharded A the m-tiles are rotated so
-// that every rank starts on its own shard while its peers finish theirs.
-__device__ __forceinline__ void tile_coords(int t, int num_m, const AShards& sh, int& tm, int& tn) {
+// Tile t -> (m-tile, n-tile).  The m-tiles of one n-tile are consecutive, so
+// CTAs working at the same time share B k-blocks through L2.  With a
+// row-sharded A the m-tiles are rotated so that every rank starts on its own
+// shard while its peers finish theirs.  With `round_rotate` (256-row tiles,
+// whose last m-tile may be half empty) the m-tile order is rotated by the
+// schedule round t / grid, so a CTA that took a full tile in one round takes
+// the short one in the next; grid % num_m == 0 keeps every n-tile's units
+// inside one round, which keeps the map one to one.
+__device__ __forceinline__ void tile_coords(int t, int num_m, const AShards& sh, int& tm, int& tn,
+                                            bool round_rotate = false, int grid = 1) {
   tm = t % num_m;
   tn = t / num_m;
   if (sh.n > 1) tm = (tm + sh.own * (sh.rows / kGemmBM)) % num_m;
+  if (round_rotate && grid > 0 && grid % num_m == 0) tm = (tm + t / grid) % num_m;
 }
 
 // Bounded acquire-poll of a peer shard's ready flag (written over NVLink).
@@ -288,13 +315,15 @@ __device__ __forceinline__ bool wait_shard_ready(const int* flag, int epoch, int
   }
 }
 
-template <int BN, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+template <int BN, int EPI, int ACC>
+__global__ void __launch_bounds__(GemmCfg<BN, ACC>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ AMaps amaps,
                    const __grid_constant__ CUtensorMap tmap_b, int M, int N, int K,
                    GemmEpilogue ep, AShards shards, int splits, int* status) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, ACC>;
   constexpr int S = Cfg::kStages;
+  constexpr int BM = Cfg::kBM;
+  constexpr int NB = Cfg::kNumBuf;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -303,7 +332,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int warp = warp_id();
   const int lane = lane_id();
-  const int num_m = (M + kGemmBM - 1) / kGemmBM;
+  const int num_m = (M + BM - 1) / BM;
   const int num_n = (N + BN - 1) / BN;
   const int num_kb = (K + kGemmBK - 1) / kGemmBK;
   // work unit u = (tile u / splits, K-slice u % splits); slice ks covers
@@ -315,9 +344,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NB; ++b) {
       mbar_init(&bars->tmem_full[b], 1);
-      mbar_init(&bars->tmem_empty[b], 4);
+      mbar_init(&bars->tmem_empty[b], Cfg::kEpiWarps);
     }
     mbar_init(&bars->drain, 1);
     fence_barrier_init();
@@ -348,10 +377,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       unsigned confirmed = 1u << shards.own;  // shards known to be ready
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         int tm, tn;
-        tile_coords(u / splits, num_m, shards, tm, tn);
+        tile_coords(u / splits, num_m, shards, tm, tn, ACC == 2, gridDim.x / splits);
         const int ks = u % splits;
         const int kb0 = ks * num_kb / splits, kb1 = (ks + 1) * num_kb / splits;
-        int map = 0, ay = tm * kGemmBM;
+        int map = 0, ay = tm * BM;
         if (shards.n > 1) {
           map = ay / shards.rows;
           ay -= map * shards.rows;
@@ -405,14 +434,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
         const int ks = u % splits;
         const int kb0 = ks * num_kb / splits, kb1 = (ks + 1) * num_kb / splits;
-        const int buf = local & 1;
-        const uint32_t tphase = (local >> 1) & 1;
+        const int buf = local % NB;
+        const uint32_t tphase = (uint32_t)(local / NB) & 1u;
+        // accumulators with valid rows in this tile (ACC = 2: the last m-tile may need one)
+        int n_acc = 1;
+        if constexpr (ACC == 2) {
+          int tm, tn;
+          tile_coords(u / splits, num_m, shards, tm, tn, true, gridDim.x / splits);
+          n_acc = M - tm * BM > kGemmBM ? 2 : 1;
+        }
         if (!mbar_wait(&bars->tmem_empty[buf], tphase ^ 1, status, kStatusTimeoutTmemEmpty)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t tacc = tmem_base + buf * BN;
+        const uint32_t tacc = tmem_base + buf * ACC * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&bars->full[stage], phase, status, kStatusTimeoutTmaFull)) {
             ok = false;
@@ -423,9 +459,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t sb = sa + Cfg::kABytes;
 #pragma unroll
           for (int k = 0; k < kGemmBK / 16; ++k) {
-            const uint64_t ad = make_desc_kmajor_sw128(sa + k * 32);
             const uint64_t bd = make_desc_kmajor_sw128(sb + k * 32);
-            tc_mma_f16(tacc, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+#pragma unroll
+            for (int a = 0; a < ACC; ++a) {
+              // rows 128a.. of the A k-block start 128a * 128 bytes in (a whole number of 8-row atoms)
+              if (a < n_acc) {
+                const uint64_t ad = make_desc_kmajor_sw128(sa + a * (kGemmBM * 128) + k * 32);
+                tc_mma_f16(tacc + a * BN, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+              }
+            }
           }
           any = true;
           tc_commit(&bars->empty[stage]);
@@ -441,19 +483,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ---------------- Epilogue (warps 2..5) ----------------
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    // ---------------- Epilogue (warps 2..) ----------------
+    const int quarter = warp & 3;     // TMEM lane quarter this warp may access
+    const int acc = (warp - 2) >> 2;  // accumulator this warp drains (ACC = 2: warps 6.. take the second)
     int local = 0;
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
       int tm, tn;
-      tile_coords(u / splits, num_m, shards, tm, tn);
-      const int buf = local & 1;
-      const uint32_t tphase = (local >> 1) & 1;
+      tile_coords(u / splits, num_m, shards, tm, tn, ACC == 2, gridDim.x / splits);
+      const int buf = local % NB;
+      const uint32_t tphase = (uint32_t)(local / NB) & 1u;
       if (!mbar_wait(&bars->tmem_full[buf], tphase, status, kStatusTimeoutTmemFull)) break;
       tc_fence_after();
-      const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
-      const int row = tm * kGemmBM + quarter * 32 + lane;
-      gemm_epilogue_tile<BN, EPI>(ep, tacc, row, tn, M, N, epi_stage + quarter * (32 * 33), u % splits);
+      const int row0 = tm * BM + acc * kGemmBM;
+      if (row0 < M) {  // the second accumulator of a short last m-tile holds nothing
+        const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + (buf * ACC + acc) * BN;
+        gemm_epilogue_tile<BN, EPI>(ep, tacc, row0 + quarter * 32 + lane, tn, M, N, epi_stage + quarter * (32 * 33),
+                                    u % splits);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->tmem_empty[buf]);
@@ -511,9 +557,9 @@ bool make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint6
   return r == CUDA_SUCCESS;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int ACC>
 static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, ACC>;
   AMaps maps;
   CUtensorMap tb;
   AShards sh = g.shards;
@@ -522,44 +568,84 @@ static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
     sh.rows = g.M;
     sh.own = 0;
     sh.ready = nullptr;
-    if (!make_tmap_2d_bf16(&maps.m[0], g.a, g.K, g.M, g.lda, kGemmBK, kGemmBM, true))
+    if (!make_tmap_2d_bf16(&maps.m[0], g.a, g.K, g.M, g.lda, kGemmBK, Cfg::kBM, true))
       return cudaErrorInvalidValue;
   } else {
+    if (ACC != 1) return cudaErrorInvalidValue;  // an m-tile must not span two shards
     if (sh.n > kMaxShards || sh.rows % kGemmBM != 0 || sh.rows * sh.n != g.M) return cudaErrorInvalidValue;
     for (int r = 0; r < sh.n; ++r)
       if (!make_tmap_2d_bf16(&maps.m[r], g.a_shards[r], g.K, sh.rows, g.lda, kGemmBK, kGemmBM, true))
         return cudaErrorInvalidValue;
   }
   if (!make_tmap_2d_bf16(&tb, g.b, g.K, g.N, g.ldb, kGemmBK, BN, true)) return cudaErrorInvalidValue;
-  auto kern = gemm_tc_kernel<BN, EPI>;
+  auto kern = gemm_tc_kernel<BN, EPI, ACC>;
   ensure_smem_attr(kern, Cfg::kSmemBytes);
   const int splits = EPI == EPI_PARTIAL ? (g.splits < 1 ? 1 : g.splits) : 1;
   if (splits > (g.K + kGemmBK - 1) / kGemmBK) return cudaErrorInvalidValue;  // every slice needs a k-block
-  const int num_units = ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + BN - 1) / BN) * splits;
+  const int num_units = ((g.M + Cfg::kBM - 1) / Cfg::kBM) * ((g.N + BN - 1) / BN) * splits;
   int grid = num_units < g.num_sms ? num_units : g.num_sms;
   if (grid < 1) grid = 1;
-  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(maps, tb, g.M, g.N, g.K, g.ep, sh, splits, g.status);
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(maps, tb, g.M, g.N, g.K, g.ep, sh, splits, g.status);
   return cudaGetLastError();
 }
 
+template <int EPI>
+static cudaError_t launch_gemm_bn(const GemmArgs& g, cudaStream_t stream) {
+  if (g.rows_per_tile == 256) {
+    if constexpr (EPI == EPI_RS) {
+      return cudaErrorInvalidValue;
+    } else {
+      return g.bn == 256 ? launch_gemm<256, EPI, 2>(g, stream) : cudaErrorInvalidValue;
+    }
+  }
+  return g.bn == 128 ? launch_gemm<128, EPI, 1>(g, stream) : launch_gemm<256, EPI, 1>(g, stream);
+}
+
 cudaError_t gemm_bf16_tc(const GemmArgs& g, cudaStream_t stream) {
-  const int bn = g.bn;
+  if (g.rows_per_tile != 128 && g.rows_per_tile != 256 && g.rows_per_tile != 0) return cudaErrorInvalidValue;
   switch (g.epi) {
-    case EPI_STORE:
-      return bn == 128 ? launch_gemm<128, EPI_STORE>(g, stream) : launch_gemm<256, EPI_STORE>(g, stream);
-    case EPI_RESIDUAL:
-      return bn == 128 ? launch_gemm<128, EPI_RESIDUAL>(g, stream)
-                       : launch_gemm<256, EPI_RESIDUAL>(g, stream);
-    case EPI_SWIGLU:
-      return bn == 128 ? launch_gemm<128, EPI_SWIGLU>(g, stream) : launch_gemm<256, EPI_SWIGLU>(g, stream);
-    case EPI_QKV:
-      return bn == 128 ? launch_gemm<128, EPI_QKV>(g, stream) : launch_gemm<256, EPI_QKV>(g, stream);
-    case EPI_RS:
-      return bn == 128 ? launch_gemm<128, EPI_RS>(g, stream) : launch_gemm<256, EPI_RS>(g, stream);
-    case EPI_PARTIAL:
-      return bn == 128 ? launch_gemm<128, EPI_PARTIAL>(g, stream) : launch_gemm<256, EPI_PARTIAL>(g, stream);
+    case EPI_STORE: return launch_gemm_bn<EPI_STORE>(g, stream);
+    case EPI_RESIDUAL: return launch_gemm_bn<EPI_RESIDUAL>(g, stream);
+    case EPI_SWIGLU: return launch_gemm_bn<EPI_SWIGLU>(g, stream);
+    case EPI_QKV: return launch_gemm_bn<EPI_QKV>(g, stream);
+    case EPI_RS: return launch_gemm_bn<EPI_RS>(g, stream);
+    case EPI_PARTIAL: return launch_gemm_bn<EPI_PARTIAL>(g, stream);
   }
   return cudaErrorInvalidValue;
+}
+
+// Estimated device cycles of a GEMM with the given tile shape: every CTA's
+// units summed (static round-robin schedule), a unit costing the larger of
+// its MMA cycles (512 per 128x256x64 k-block and accumulator) and its
+// L2->SM bytes at the CTAs' share of ~15 TB/s of L2 bandwidth.  Only the
+// ratio between shapes is used.
+double gemm_cost_estimate(int M, int N, int K, int bn, int rows_per_tile, int splits, int num_sms) {
+  const int acc = rows_per_tile / kGemmBM;
+  const int num_m = (M + rows_per_tile - 1) / rows_per_tile;
+  const int num_n = (N + bn - 1) / bn;
+  const int units = num_m * num_n * (splits < 1 ? 1 : splits);
+  const int grid = units < num_sms ? units : num_sms;
+  const double kb = (double)((K + kGemmBK - 1) / kGemmBK) / (splits < 1 ? 1 : splits);
+  const double share = std::min(128.0, 15.0e12 / (grid * 1.9e9));  // bytes per cycle per CTA
+  const int sp = splits < 1 ? 1 : splits;
+  const int tgrid = grid / sp;
+  auto unit_cost = [&](int u) {
+    const int t = u / sp;
+    int tm = t % num_m;
+    if (acc == 2 && tgrid > 0 && tgrid % num_m == 0) tm = (tm + t / tgrid) % num_m;
+    const int rows = std::min(rows_per_tile, M - tm * rows_per_tile);
+    const int n_acc = acc == 2 && rows <= kGemmBM ? 1 : acc;
+    const double mma = kb * 512.0 * n_acc * bn / 256.0;
+    const double l2 = kb * (double)(std::min(rows, rows_per_tile) + bn) * 128.0 / share;
+    return std::max(mma, l2);
+  };
+  double worst = 0.0;
+  for (int c = 0; c < grid; ++c) {
+    double t = 0.0;
+    for (int u = c; u < units; u += grid) t += unit_cost(u);
+    worst = std::max(worst, t);
+  }
+  return worst;
 }
 
 // Sum of the K-slice partials in slice order, then the STORE or RESIDUAL

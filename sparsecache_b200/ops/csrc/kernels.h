@@ -79,6 +79,7 @@ struct GemmArgs {
   int M, N, K, lda, ldb;
   int epi;
   int bn;  // 128 or 256
+  int rows_per_tile;  // 128 (one accumulator) or 256 (two; bn 256, unsharded, not EPI_RS); 0 = 128
   int splits;  // EPI_PARTIAL: number of K slices (>= 1)
   int num_sms;
   GemmEpilogue ep;
@@ -86,6 +87,8 @@ struct GemmArgs {
 };
 
 cudaError_t gemm_bf16_tc(const GemmArgs& g, cudaStream_t stream);
+// relative device-cycle estimate of a tile shape (used to pick rows_per_tile and split-K)
+double gemm_cost_estimate(int M, int N, int K, int bn, int rows_per_tile, int splits, int num_sms);
 cudaError_t splitk_reduce(const float* ws, int splits, int M, int N, const __nv_bfloat16* residual, int ldr,
                           __nv_bfloat16* out, int ldo, cudaStream_t stream);
 

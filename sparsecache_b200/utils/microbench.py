@@ -145,6 +145,30 @@ def main() -> None:
                                         "weight_GBps": N * K * 2 / (t * 1e-6) / 1e9,
                                         "weight_frac_of_measured_hbm": N * K * 2 / (t * 1e-6) / 1e9 / HBM_GBS}
 
+    if "gemm_shapes" in only:
+        # 128-row tiles (one accumulator) vs 256-row tiles (two accumulators sharing B)
+        # vs the automatic choice, for the CacheBlend active-row and full-prefill shapes
+        for M in (300, 1676):
+            for name, N, K, kind in (("qkv", 6144, 4096, "store"), ("o", 4096, 4096, "residual"),
+                                     ("gate_up", 28672, 4096, "swiglu"), ("down", 4096, 14336, "residual")):
+                a = torch.randn(M, K, device=dev).to(bf)
+                w = (torch.randn(N, K, device=dev) * 0.02).to(bf)
+                o = torch.empty(M, N // 2 if kind == "swiglu" else N, device=dev, dtype=bf)
+                for rows in (128, 256, 0):
+                    ext.set_gemm_rows_per_tile(rows)
+                    if kind == "store":
+                        fn = lambda: ext.gemm_store(a, w, o, 256, -1)  # noqa: E731
+                    elif kind == "residual":
+                        fn = lambda: ext.gemm_residual(a, w, o, o, 256, -1)  # noqa: E731
+                    else:
+                        fn = lambda: ext.gemm_swiglu(a, w, o, 256)  # noqa: E731
+                    t = timeit(fn, n=20)
+                    tf = 2 * M * N * K / (t * 1e-6) / 1e12
+                    res[f"gemm_M{M}_{name}_rows{rows or 'auto'}"] = {
+                        "us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS}
+                ext.set_gemm_rows_per_tile(0)
+                del a, w, o
+
     if "attn_decode" in only or "attn_decode_sweep" in only:
         H, Hkv = 32, 8
         for cap in (2048, 18000):
@@ -245,9 +269,15 @@ def main() -> None:
             qpos = allpos if rows is None else rows
             out = torch.empty(R, H * 128, device=dev, dtype=bf)
             flops = 4 * 128 * H * float(sum(int(x) + 1 for x in qpos.tolist()))
+            split_ws = torch.empty(4 * 512 * H * 132, device=dev)  # the engine's key-split workspace
             for kern in ("attention_prefill", "attention_prefill_mma"):
                 fn = getattr(ext, kern)
-                t = timeit(lambda: fn(q, rows, qpos, kc, vc, None, T, H, 1 / math.sqrt(128), out), n=20)
+                if kern == "attention_prefill":
+                    call = lambda: fn(q, rows, qpos, kc, vc, None, T, H, 1 / math.sqrt(128), out,  # noqa: E731
+                                      ws=split_ws if R <= 512 else None)
+                else:
+                    call = lambda: fn(q, rows, qpos, kc, vc, None, T, H, 1 / math.sqrt(128), out)  # noqa: E731
+                t = timeit(call, n=20)
                 tf = flops / (t * 1e-6) / 1e12
                 res[f"{kern}_{name}_T{T}"] = {"us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS}
     if "attn_trace" in only:

@@ -89,6 +89,62 @@ def test_gemm_residual_and_swiglu(cuda_device):
     assert _rel_err(act, ref) < 2e-2
 
 
+@pytest.mark.parametrize("M", [129, 300, 513, 1000])
+def test_gemm_two_accumulator_tiles(cuda_device, M):
+    """256-row tiles (two TMEM accumulators sharing each B k-block; a short last m-tile runs one)
+    give the same bits as 128-row tiles for every epilogue, and match the fp32 reference."""
+    ext = _ext()
+    cfg = get_model_config("tiny128")
+    g = torch.Generator(device="cpu").manual_seed(M)
+    K, N = 1024, 1536
+    a = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.03).to(cuda_device, torch.bfloat16)
+    res = torch.randn(M, N, generator=g).to(cuda_device, torch.bfloat16)
+    nq, nkv, cap = 8, 2, M + 64
+    wq = (torch.randn((nq + 2 * nkv) * 128, K, generator=g) * 0.03).to(cuda_device, torch.bfloat16)
+    pos = torch.arange(M, device=cuda_device, dtype=torch.int32) + 3
+    slot = torch.arange(M, device=cuda_device, dtype=torch.int32) + 5
+    table = rope_table(cfg, 2048, cuda_device)
+
+    def run_all():
+        outs = {}
+        o = torch.empty(M, N, device=cuda_device, dtype=torch.bfloat16)
+        ext.gemm_store(a, w, o, 256, 1)
+        outs["store"] = o
+        r = res.clone()
+        ext.gemm_residual(a, w, r, r, 256, 1)
+        outs["residual"] = r
+        r2 = res.clone()
+        ext.gemm_residual(a, w, r2, r2, 256, 3)
+        outs["residual_split3"] = r2
+        act = torch.empty(M, N // 2, device=cuda_device, dtype=torch.bfloat16)
+        ext.gemm_swiglu(a, w, act, 256)
+        outs["swiglu"] = act
+        kc = torch.zeros(nkv, cap, 128, device=cuda_device, dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        q = torch.empty(M, nq * 128, device=cuda_device, dtype=torch.bfloat16)
+        dev = torch.zeros(M, 2 * nkv, device=cuda_device)
+        ext.gemm_qkv(a, wq, q, kc, vc, pos, slot, table, nq, nkv, dev, 3, 256)
+        outs.update(q=q, k=kc, v=vc, dev=dev)
+        torch.cuda.synchronize()
+        _status_ok(cuda_device)
+        return outs
+
+    try:
+        ext.set_gemm_rows_per_tile(128)
+        ref128 = run_all()
+        ext.set_gemm_rows_per_tile(256)
+        got = run_all()
+    finally:
+        ext.set_gemm_rows_per_tile(0)
+    for name in ref128:
+        assert torch.equal(got[name], ref128[name]), name
+    y = a.float() @ w.float().T
+    assert _rel_err(got["store"], y) < 1e-2
+    assert _rel_err(got["residual"], res.float() + y.to(torch.bfloat16).float()) < 1e-2
+    assert _rel_err(got["residual_split3"], res.float() + y.to(torch.bfloat16).float()) < 1e-2
+
+
 def _qkv_reference(a, w, cfg, pos, nq, nkv):
     y = a.float() @ w.float().T
     D = 128
@@ -158,7 +214,7 @@ def _attn_reference(q, kc, vc, qpos, kpos, n_heads):
 
 
 @pytest.mark.parametrize("split", [False, True])
-@pytest.mark.parametrize("T,R", [(777, 150), (1676, 300), (65, 1), (129, 3)])
+@pytest.mark.parametrize("T,R", [(777, 150), (1676, 300), (65, 1), (129, 3), (4500, 120)])
 @pytest.mark.parametrize("case", ["causal", "selective", "staged", "growing"])
 def test_attention_prefill(cuda_device, case, T, R, split):
     """tcgen05 flash attention vs the fp32 reference: full causal rows, a sorted
@@ -195,7 +251,7 @@ def test_attention_prefill(cuda_device, case, T, R, split):
     if split:
         ws = torch.full((4 * rows.numel() * H * 132,), float("nan"), device=cuda_device)
         n_split = _ext().attention_prefill_splits(rows.numel(), H, Hkv, T, ws.numel(), _ext().num_sms())
-        if T >= 777:
+        if case not in ("causal", "growing") and (T, R) == (4500, 120):
             assert n_split > 1
     _ext().attention_prefill(
         qfull, rows, qpos, kc, vc, kpos if case == "staged" else None, T, H, 1 / math.sqrt(128), out, ws=ws
