@@ -689,5 +689,124 @@ class B200Engine:
         """Device view of the token log (first ``max_new`` entries)."""
         return self._decode_buffers(max_new)["log"][:max_new]
 
+    # ------------------------------------------------------ batched decode
+    MAX_BATCH = 32  # sequences per batched step (the skinny tensor-core GEMM takes 32 rows)
+
+    def batch_slots(self, n_seq: int, capacity: int) -> list[KVSlot]:
+        """``n_seq`` serving slots back to back in one buffer (a batched step addresses them by stride)."""
+        if not 1 <= n_seq <= self.MAX_BATCH:
+            raise ValueError(f"1..{self.MAX_BATCH} sequences per batched step")
+        per = KVSlot.nbytes_for(self.cfg, capacity) // 2
+        buf = torch.empty(n_seq * per, dtype=torch.bfloat16, device=self.device)
+        return [KVSlot.from_buffer(self.cfg, capacity, buf[i * per:(i + 1) * per]) for i in range(n_seq)]
+
+    def _batch_buffers(self) -> dict:
+        cfg, ws, B = self.cfg, self.ws, self.MAX_BATCH
+        if "bt_gen" not in ws.bufs:
+            ws.bufs["bt_gen"] = torch.zeros(1, device=self.device, dtype=torch.int64)
+        if "bt_skinny_ws" not in ws.bufs:
+            w0 = self.w.layers[0]
+            shapes = [tuple(w0.w_qkv.shape), tuple(w0.w_o.shape), tuple(w0.w_gu.shape), tuple(w0.w_down.shape),
+                      tuple(self.w.lm_head.shape)]
+            need = max(int(self.ext.skinny_splits(n, k)) * n * 32 for n, k in shapes)
+            ws.bufs["bt_skinny_ws"] = torch.empty(need, device=self.device, dtype=torch.float32)
+        return {"h": ws.get("bt_h", (B, cfg.d_model), torch.bfloat16),
+                "x": ws.get("bt_x", (B, cfg.d_model), torch.bfloat16),
+                "q": ws.get("bt_q", (B, cfg.q_size), torch.bfloat16),
+                "attn": ws.get("bt_attn", (B, cfg.q_size), torch.bfloat16),
+                "act": ws.get("bt_act", (B, cfg.ffn), torch.bfloat16),
+                "logits": ws.get("bt_logits", (B, cfg.vocab), torch.bfloat16),
+                "tok": ws.get("bt_tok", (B,), torch.int32),
+                "pos": ws.get("bt_pos", (B,), torch.int32),
+                "gen": ws.bufs["bt_gen"],
+                "log": ws.get("bt_log", (self.MAX_DECODE_TOKENS, B), torch.int32),
+                "skinny_ws": ws.bufs["bt_skinny_ws"]}
+
+    def batch_first_tokens(self, last_rows: torch.Tensor) -> torch.Tensor:
+        """Greedy first token of each sequence from its last prompt row (pre-norm hidden, [B, d]):
+        final RMSNorm, LM head on the tensor cores, row argmax.  Returns the device int32 [B]."""
+        B = last_rows.shape[0]
+        bb = self._batch_buffers()
+        x = bb["x"][:B]
+        self.ext.rmsnorm(last_rows, None, self.w.norm, self.cfg.rms_eps, x)
+        self.ext.skinny_gemm(x, self.w.lm_head, 0, bb["logits"][:B], None, bb["skinny_ws"])
+        self.ext.row_argmax(bb["logits"][:B], bb["tok"])
+        return bb["tok"][:B]
+
+    def start_batch(self, slots: list[KVSlot], first_tokens: torch.Tensor, positions, *, max_new: int) -> None:
+        """Seed a batched greedy decode: sequence b produced ``first_tokens[b]`` (device int32) at
+        position ``positions[b]`` (its prompt length)."""
+        B = len(slots)
+        if first_tokens.numel() != B or len(positions) != B:
+            raise ValueError("one first token and one position per sequence")
+        bb = self._batch_buffers()
+        if max_new > bb["log"].shape[0]:
+            raise ValueError("max_new exceeds the batched token log")
+        bb["tok"][:B].copy_(first_tokens.to(torch.int32), non_blocking=True)
+        bb["pos"][:B].copy_(torch.as_tensor(list(positions), dtype=torch.int32).pin_memory(), non_blocking=True)
+        bb["log"][0, :B].copy_(bb["tok"][:B])
+        bb["gen"].fill_(1)
+        self.ext.embedding(bb["tok"][:B], self.w.embed, bb["h"][:B])
+
+    def _batch_step(self, slots: list[KVSlot], splits: int) -> None:
+        """One greedy step of every sequence: row b is sequence b at its own position and slot."""
+        cfg, ext = self.cfg, self.ext
+        B = len(slots)
+        bb = self._batch_buffers()
+        h, x, pos_rows, ws = bb["h"][:B], bb["x"][:B], bb["pos"][:B], bb["skinny_ws"]
+        stride = (slots[1].data.data_ptr() - slots[0].data.data_ptr()) // 2 if B > 1 else 0
+        for layer, lw in enumerate(self.w.layers):
+            ext.rmsnorm(h, None, lw.ln1, cfg.rms_eps, x)
+            ext.skinny_qkv(x, lw.w_qkv, bb["q"][:B], slots[0].k(layer), slots[0].v(layer), pos_rows, self.rope,
+                           cfg.n_heads, cfg.n_kv_heads, ws, pos_rows=pos_rows, seq_stride=stride)
+            ext.attention_decode(bb["q"][:B], slots[0].k(layer), slots[0].v(layer), pos_rows, cfg.n_heads,
+                                 self.scale, splits, bb["attn"][:B], pos_rows=pos_rows, seq_stride=stride)
+            ext.skinny_gemm(bb["attn"][:B], lw.w_o, 1, h, h, ws)
+            ext.rmsnorm(h, None, lw.ln2, cfg.rms_eps, x)
+            ext.skinny_gemm(x, lw.w_gu, 2, bb["act"][:B], None, ws)
+            ext.skinny_gemm(bb["act"][:B], lw.w_down, 1, h, h, ws)
+        ext.rmsnorm(h, None, self.w.norm, cfg.rms_eps, x)
+        ext.skinny_gemm(x, self.w.lm_head, 0, bb["logits"][:B], None, ws)
+        ext.row_argmax(bb["logits"][:B], bb["tok"])
+        bb["log"][:, :B].index_copy_(0, bb["gen"], bb["tok"][:B].view(1, B))
+        bb["gen"].add_(1)
+        pos_rows.add_(1)
+        ext.embedding(bb["tok"][:B], self.w.embed, h)
+
+    def decode_batch(self, slots: list[KVSlot], n_steps: int, *, use_graph: bool = True) -> None:
+        """``n_steps`` batched greedy steps from the state ``start_batch`` (or earlier steps) left."""
+        if n_steps <= 0:
+            return
+        if len({s.capacity for s in slots}) != 1:
+            raise ValueError("batched slots share one capacity")
+        splits = self._decode_splits(slots[0].capacity)
+        if not use_graph:
+            for _ in range(n_steps):
+                self._batch_step(slots, splits)
+            return
+        key = ("batch", tuple(id(s) for s in slots), splits)
+        graph = self._graphs.get(key)
+        if graph is None:
+            bb = self._batch_buffers()
+            saved = {k: bb[k].clone() for k in ("h", "tok", "pos", "gen", "log")}
+            self._batch_step(slots, splits)  # warm step, then capture against the saved state
+            for k, v in saved.items():
+                bb[k].copy_(v)
+            torch.cuda.synchronize(self.device)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self._batch_step(slots, splits)
+            for k, v in saved.items():
+                bb[k].copy_(v)
+            self._graphs[key] = graph
+        for _ in range(n_steps):
+            graph.replay()
+        # per layer: 2 norms, QKV (GEMM + reduce), attention, 3 skinny GEMMs (GEMM + reduce each)
+        self.ext.launches += n_steps * (11 * self.cfg.n_layers + 7)
+
+    def batch_tokens(self, n_seq: int, n_tokens: int) -> torch.Tensor:
+        """Device view of the batched token log: [n_tokens, n_seq] (column b = sequence b)."""
+        return self._batch_buffers()["log"][:n_tokens, :n_seq]
+
     def release_graphs(self) -> None:
         self._graphs.clear()

@@ -28,6 +28,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from ..ops.linear import recurrent_attention
 from ..rope import apply_rope
 from .sparse_kv_draft import RMSNorm, SparseKVDraftConfig, SparseTargetKVAttention, stage_features
 
@@ -105,12 +106,9 @@ class EagleSelfAttention(nn.Module):
                 raise ValueError("EAGLE key/value cache is incomplete")
             k = torch.cat((past_key, k), dim=2)
             v = torch.cat((past_value, v), dim=2)
-        # grouped-query attention without materialising repeated K/V:
-        # fold the query heads of one KV group into the query-length axis.
-        g = self.num_heads // self.num_key_value_heads
-        qg = q.view(b, self.num_key_value_heads, g, self.head_dim)
-        out = F.scaled_dot_product_attention(qg, k, v)
-        out = out.reshape(b, 1, self.num_heads * self.head_dim)
+        # one new position over every past one (GQA without repeating K/V):
+        # this package's forward / backward kernels on CUDA, SDPA otherwise
+        out = recurrent_attention(q, k, v).reshape(b, 1, self.num_heads * self.head_dim)
         return self.o_proj(out), k, v
 
 

@@ -720,6 +720,58 @@ void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int6
   check_cuda(sc::attention_decode(a, cur_stream()), "attention_decode");
 }
 
+// ------------------------------------------------- recurrent attention (K14)
+static sc::RecurrentAttnArgs recurrent_args(const Tensor& q, const Tensor& k, const Tensor& v, double scale) {
+  CHECK_BF16(q); CHECK_BF16(k); CHECK_BF16(v);
+  TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda(), "CUDA tensors");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && q.is_contiguous(), "q [B, Hq, 128] contiguous");
+  TORCH_CHECK(k.dim() == 4 && k.size(3) == 128 && k.is_contiguous() && k.size(0) == q.size(0),
+              "k [B, Hkv, P, 128] contiguous");
+  TORCH_CHECK(v.sizes() == k.sizes() && v.is_contiguous(), "v like k");
+  TORCH_CHECK(q.size(1) % k.size(1) == 0 && q.size(1) / k.size(1) <= 8, "Hq = G * Hkv, G <= 8");
+  TORCH_CHECK(k.size(2) >= 1 && k.size(2) <= sc::kRecurrentAttnMaxKeys, "1..1024 keys");
+  sc::RecurrentAttnArgs a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  a.v = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  a.batch = (int)q.size(0);
+  a.n_heads = (int)q.size(1);
+  a.n_kv_heads = (int)k.size(1);
+  a.n_keys = (int)k.size(2);
+  a.scale = (float)scale;
+  return a;
+}
+
+std::vector<Tensor> recurrent_attention_fwd(Tensor q, Tensor k, Tensor v, double scale) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto a = recurrent_args(q, k, v, scale);
+  Tensor out = torch::empty_like(q);
+  Tensor lse = torch::empty({q.size(0), q.size(1)}, q.options().dtype(torch::kFloat32));
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.lse = lse.data_ptr<float>();
+  check_cuda(sc::recurrent_attention_fwd(a, cur_stream()), "recurrent_attention_fwd");
+  return {out, lse};
+}
+
+std::vector<Tensor> recurrent_attention_bwd(Tensor q, Tensor k, Tensor v, Tensor out, Tensor lse, Tensor dout,
+                                            double scale) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto a = recurrent_args(q, k, v, scale);
+  CHECK_BF16(out); CHECK_BF16(dout); CHECK_F32(lse);
+  TORCH_CHECK(out.sizes() == q.sizes() && dout.sizes() == q.sizes() && out.is_contiguous() &&
+                  dout.is_contiguous(), "out / dout like q");
+  TORCH_CHECK(lse.numel() == q.size(0) * q.size(1), "lse [B, Hq]");
+  Tensor dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.lse = lse.data_ptr<float>();
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  a.dq = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
+  a.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  a.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  check_cuda(sc::recurrent_attention_bwd(a, cur_stream()), "recurrent_attention_bwd");
+  return {dq, dk, dv};
+}
+
 // ------------------------------------------------------------ pointwise
 void rmsnorm(Tensor x, c10::optional<Tensor> rows, Tensor w, double eps, Tensor out) {
   const c10::cuda::CUDAGuard guard(x.device());
@@ -833,14 +885,14 @@ sc::SkinnyArgs skinny_base(const Tensor& x, const Tensor& w, int64_t epi, const 
   a.epi = (int)epi;
   a.num_sms = num_sms();
   a.splits = splits > 0 ? (int)splits : sc::skinny_splits(a.N, a.K, a.num_sms);
-  TORCH_CHECK(a.M >= 1 && a.M <= 32, "the skinny GEMM takes 1..32 rows");
+  TORCH_CHECK(a.M >= 1 && a.M <= 64, "the skinny GEMM takes 1..64 rows");
   TORCH_CHECK(ws.numel() >= (int64_t)a.splits * a.N * sc::skinny_bn(a.M), "workspace [splits][N][bn] too small");
   a.ws = ws.data_ptr<float>();
   a.status = status_tensor(w).data_ptr<int>();
   return a;
 }
 
-// out = epilogue(x @ w^T) for M <= 32 rows on the tensor cores; returns kernels launched.
+// out = epilogue(x @ w^T) for M <= 64 rows on the tensor cores; returns kernels launched.
 int64_t skinny_gemm(Tensor x, Tensor w, int64_t epi, Tensor out, c10::optional<Tensor> residual, Tensor ws,
                     int64_t splits) {
   const c10::cuda::CUDAGuard guard(x.device());
@@ -860,7 +912,7 @@ int64_t skinny_gemm(Tensor x, Tensor w, int64_t epi, Tensor out, c10::optional<T
   return 2;
 }
 
-// Fused QKV (RoPE + K/V cache write) for M <= 32 rows on the tensor cores.
+// Fused QKV (RoPE + K/V cache write) for M <= 64 rows on the tensor cores.
 int64_t skinny_qkv(Tensor x, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_cache, Tensor pos,
                    Tensor rope_table, int64_t n_q_heads, int64_t n_kv_heads, Tensor ws, c10::optional<Tensor> slot,
                    c10::optional<Tensor> pos_rows, int64_t seq_stride) {
@@ -1229,6 +1281,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     return sc::attention_prefill_splits(p, (int)num_sms);
   });
   m.def("attention_prefill_mma", &attention_prefill_mma);
+  m.def("recurrent_attention_fwd", &recurrent_attention_fwd);
+  m.def("recurrent_attention_bwd", &recurrent_attention_bwd);
   m.def("page_token_scores", &page_token_scores, py::arg("q"), py::arg("keys"), py::arg("n_tokens"),
         py::arg("scale"));
   m.def("attention_decode", &attention_decode, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),

@@ -180,6 +180,25 @@ struct AttnPrefillArgs {
 };
 
 cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream);
+
+// Attention of one new position over its past keys (recurrent drafter trunk,
+// K14): q [B, Hq, 128], k / v [B, Hkv, P, 128] bf16 contiguous, Hq / Hkv <= 8.
+constexpr int kRecurrentAttnMaxKeys = 1024;
+struct RecurrentAttnArgs {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  __nv_bfloat16* out;   // [B, Hq, 128]
+  float* lse;           // [B, Hq] (written by the forward, read by the backward)
+  const __nv_bfloat16* dout;  // backward: dO [B, Hq, 128]
+  __nv_bfloat16* dq;    // backward outputs
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  int batch, n_heads, n_kv_heads, n_keys;
+  float scale;
+};
+cudaError_t recurrent_attention_fwd(const RecurrentAttnArgs& a, cudaStream_t stream);
+cudaError_t recurrent_attention_bwd(const RecurrentAttnArgs& a, cudaStream_t stream);
 // key splits the launcher would use for these arguments (1 = none)
 int attention_prefill_splits(const AttnPrefillArgs& p, int num_sms);
 // the mma.sync kernel the tcgen05 one replaced, kept for A/B measurement only
@@ -292,7 +311,7 @@ struct SkinnyArgs {
   int ldr;
   float* ws;               // [splits][N][bn] fp32, bn = skinny_bn(M)
   int splits;
-  int bn;                  // token-row tile (16 or 32), set by the launcher
+  int bn;                  // token-row tile (16, 32 or 64), set by the launcher
   int num_sms;
   int* status;
   // SKINNY_QKV: fused QKV rows (q heads, k heads, v heads of 128): RoPE on
@@ -321,7 +340,7 @@ struct SkinnyArgs {
   unsigned int* counter;
 };
 int skinny_splits(int N, int K, int num_sms);
-// token-row tile of the skinny GEMM for M rows: 16 (M <= 16) or 32 (M <= 32)
+// token-row tile of the skinny GEMM for M rows: 16 (M <= 16), 32 (M <= 32) or 64 (M <= 64)
 int skinny_bn(int M);
 cudaError_t skinny_gemm(const SkinnyArgs& a, cudaStream_t stream);
 // Row argmax over bf16 logits [M, V] (first index on ties) -> out_token[M].

@@ -1,12 +1,12 @@
 // Skinny GEMM on the tensor cores for a few token rows (batched verification,
-// small decode batches): out[m, n] = sum_k x[m, k] * w[n, k], M <= 32.
+// small decode batches, drafter-trunk rows): out[m, n] = sum_k x[m, k] * w[n, k], M <= 64.
 //
 // At M <= 16 the work is a weight stream; the CUDA-core GEMV (gemv.cu) keeps
 // up with HBM only at M = 1-2 because every extra row costs an unpack and
 // FMAs per weight.  Here the roles are swapped so the tensor core does the
 // rows: the weight tile is the 128-row A operand (TMA, 128-byte swizzle,
 // `tcgen05.mma.cta_group::1.kind::f16` with M = 128), the token rows padded to
-// N = 16 (M <= 16) or N = 32 (M <= 32) are the B operand (TMA zero-fills rows
+// N = 16 (M <= 16), 32 (M <= 32) or 64 (M <= 64) are the B operand (TMA zero-fills rows
 // >= M), and the 128 x N fp32 accumulator lives in TMEM (two buffers).  Work
 // units are (128-row weight tile, K slice) so that ~one unit per SM streams
 // its slice with a deep (10-stage) TMA pipeline; each unit writes its fp32
@@ -31,13 +31,14 @@ constexpr int kSkStages = 10;
 constexpr int kSkABytes = kSkBM * kSkBK * 2;  // 16 KB
 constexpr int kSkThreads = 192;
 
-// BN = token rows padded to the MMA N: 16 (M <= 16) or 32 (M <= 32)
+// BN = token rows padded to the MMA N: 16 (M <= 16), 32 (M <= 32) or 64 (M <= 64)
 template <int BN>
 struct SkCfg {
-  static constexpr int kBBytes = BN * kSkBK * 2;  // 2 / 4 KB
+  static constexpr int kBBytes = BN * kSkBK * 2;  // 2 / 4 / 8 KB
   static constexpr int kStageBytes = kSkABytes + kBBytes;
-  static constexpr int kSmem = kSkStages * kStageBytes + 1024 + 256;
-  static constexpr uint32_t kTmemCols = BN == 16 ? 32 : 64;  // two accumulators, power of two >= 32
+  static constexpr int kStages = BN == 64 ? 8 : kSkStages;  // 8 x 24 KB fits shared memory
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
+  static constexpr uint32_t kTmemCols = BN == 16 ? 32 : 2 * BN;  // two accumulators, power of two >= 32
 };
 
 struct alignas(8) SkBars {
@@ -67,6 +68,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
                       int N, int K, int splits, float* ws, int* status) {
   using Cfg = SkCfg<BN>;
   constexpr int kSkStageBytes = Cfg::kStageBytes;
+  constexpr int kSkStages = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   SkBars* bars = reinterpret_cast<SkBars*>(smem + kSkStages * kSkStageBytes);
@@ -181,7 +183,9 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       if constexpr (BN == 16) {
         tmem_ld_32x32b_x16(taddr, r);
       } else {
-        tmem_ld_32x32b_x32(taddr, r);
+#pragma unroll
+        for (int h = 0; h < BN / 32; ++h)
+          tmem_ld_32x32b_x32(taddr + h * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[h * 32]));
       }
       tmem_ld_wait();
       const int row = tile * kSkBM + quarter * 32 + lane;
@@ -348,11 +352,11 @@ int skinny_splits(int N, int K, int num_sms) {
   return best;
 }
 
-int skinny_bn(int M) { return M <= 16 ? 16 : 32; }
+int skinny_bn(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
 cudaError_t skinny_gemm(const SkinnyArgs& args, cudaStream_t stream) {
   SkinnyArgs a = args;
-  if (a.M < 1 || a.M > 32 || a.K % kSkBK != 0 || a.N % 2 != 0) return cudaErrorInvalidValue;
+  if (a.M < 1 || a.M > 64 || a.K % kSkBK != 0 || a.N % 2 != 0) return cudaErrorInvalidValue;
   a.bn = skinny_bn(a.M);
   if (a.epi == SKINNY_SWIGLU && a.N % 256 != 0) return cudaErrorInvalidValue;
   if (a.epi == SKINNY_QKV && (a.N % 128 != 0 || a.N != (a.n_q_heads + 2 * a.n_kv_heads) * 128))
@@ -363,22 +367,24 @@ cudaError_t skinny_gemm(const SkinnyArgs& args, cudaStream_t stream) {
   if (!make_tmap_2d_bf16(&tx, a.x, a.K, a.M, a.ldx, kSkBK, a.bn, true)) return cudaErrorInvalidValue;
   ensure_smem_attr(skinny_mma_kernel<16>, SkCfg<16>::kSmem);
   ensure_smem_attr(skinny_mma_kernel<32>, SkCfg<32>::kSmem);
+  ensure_smem_attr(skinny_mma_kernel<64>, SkCfg<64>::kSmem);
   const int tiles = (a.N + kSkBM - 1) / kSkBM;
   const int units = tiles * a.splits;
   const int grid = units < a.num_sms ? units : a.num_sms;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kSkThreads, 1, 1);
-  cfg.dynamicSmemBytes = a.bn == 16 ? SkCfg<16>::kSmem : SkCfg<32>::kSmem;
+  cfg.dynamicSmemBytes = a.bn == 16 ? SkCfg<16>::kSmem : (a.bn == 32 ? SkCfg<32>::kSmem : SkCfg<64>::kSmem);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = a.bn == 16
-                      ? cudaLaunchKernelEx(&cfg, skinny_mma_kernel<16>, tw, tx, a.N, a.K, a.splits, a.ws, a.status)
-                      : cudaLaunchKernelEx(&cfg, skinny_mma_kernel<32>, tw, tx, a.N, a.K, a.splits, a.ws, a.status);
+  cudaError_t e =
+      a.bn == 16   ? cudaLaunchKernelEx(&cfg, skinny_mma_kernel<16>, tw, tx, a.N, a.K, a.splits, a.ws, a.status)
+      : a.bn == 32 ? cudaLaunchKernelEx(&cfg, skinny_mma_kernel<32>, tw, tx, a.N, a.K, a.splits, a.ws, a.status)
+                   : cudaLaunchKernelEx(&cfg, skinny_mma_kernel<64>, tw, tx, a.N, a.K, a.splits, a.ws, a.status);
   if (e != cudaSuccess) return e;
   const int outs = ((a.epi == SKINNY_SWIGLU || a.epi == SKINNY_QKV) ? a.N / 2 : a.N) * a.M;
   cfg.gridDim = dim3((outs + 255) / 256, 1, 1);

@@ -47,6 +47,9 @@ def main(argv=None) -> None:
     p.add_argument("--train-fc", action="store_true")
     p.add_argument("--train-midlayer", action="store_true")
     p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--tc-linears", action="store_true",
+                   help="frozen trunk projections on this package's tensor-core GEMMs instead of autograd's linears")
+    p.add_argument("--no-k14", action="store_true", help="trunk self-attention on SDPA instead of the K14 kernels")
     p.add_argument("--small", action="store_true", help="tiny geometry (smoke runs)")
     args = p.parse_args(argv)
 
@@ -58,6 +61,11 @@ def main(argv=None) -> None:
     from .drafter_trainer import (DrafterTrainConfig, EagleDrafterTrainer, configure_trainable_modules,
                                   evaluate_drafter, prepare_for_training, random_eagle_drafter)
     from .teacher import synthetic_bank
+
+    if args.no_k14:
+        from ..ops import linear as _linear
+
+        _linear.USE_RECURRENT_ATTENTION_KERNEL = False
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -94,7 +102,8 @@ def main(argv=None) -> None:
             bank = _extracted_bank(target, n_total, args, dev)
         cos, sin = rope_cos_sin(target, torch.arange(args.prompt_tokens + args.horizon + 8), device=dev)
         train_bank_rows = args.samples
-        tcfg = DrafterTrainConfig(global_batch=args.global_batch, use_graph=not args.no_graph)
+        tcfg = DrafterTrainConfig(global_batch=args.global_batch, use_graph=not args.no_graph,
+                                  tc_linears=args.tc_linears)
         trainer = EagleDrafterTrainer(model, _head(bank, train_bank_rows), cos, sin, tcfg, distributed=distributed)
         trainer.warmup_and_capture(warmup=max(1, args.warmup))
         if distributed:
@@ -119,6 +128,27 @@ def main(argv=None) -> None:
             for mode in ("exact", "disabled"):
                 evals[mode] = evaluate_drafter(model, bank, rows, cos, sin, memory_mode=mode, draft_tokens=4,
                                                batch=32)
+        # the optimizer phase on its own (eager, after the evaluation): with several ranks it is
+        # the peer-memory reduce-scatter + clip + AdamW + all-gather, which runs after the
+        # backward (every adapter weight is shared by all 256 positions of the recurrence),
+        # so its time is the exposed exchange of a step
+        if distributed:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        for _ in range(3):
+            if distributed:
+                trainer.opt.begin_step()
+            trainer.opt.step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        opt_ms = e0.elapsed_time(e1) / 3
+        if distributed:
+            trainer.opt.check()
+            mt = torch.tensor([opt_ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(mt, op=dist.ReduceOp.MAX)
+            opt_ms = float(mt.item())
         tokens = args.global_batch * trainer.horizon
         trainable = sum(p.numel() for p in model.adapter_parameters())
         if rank == 0:
@@ -132,8 +162,13 @@ def main(argv=None) -> None:
                            "visible_tokens": args.visible, "samples": args.samples,
                            "trainable_params": trainable, "fusion_mode": ecfg.fusion_mode,
                            "parallelism": f"dp{world}", "graph": not args.no_graph,
+                           "trunk_linears": "tcgen05 GEMM" if trainer.tc_linears else "autograd (library)",
+                           "trunk_self_attention": "SDPA (library)" if args.no_k14 else "K14 kernels",
                            "inputs": "bank resident in HBM (larger than L2)"},
                 "final_loss": row["loss"], "grad_norm": row["grad_norm"],
+                "optimizer_exchange_ms": opt_ms,
+                "optimizer_exchange": ("peer-memory reduce-scatter + clip + AdamW + all-gather, after backward "
+                                       "(exposed)" if distributed else "fused clip + AdamW"),
                 "acceptance_4tok": {k: v["mean_accepted_prefix"] for k, v in evals.items()},
                 "teacher_forced_top1": {k: v["teacher_forced_top1"] for k, v in evals.items()},
                 "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9,

@@ -29,7 +29,11 @@ What is different is how a step runs:
     phases.  No NCCL call is on the step path;
   * the whole step (gather of the batch from the bank, recurrent forward,
     loss, backward, optimizer, DP exchange) is captured once as a CUDA graph
-    and replayed; the host only writes the next batch's indices.
+    and replayed; the host only writes the next batch's indices;
+  * the trunk's self-attention runs forward and backward on the K14 kernels
+    (``ops.linear.recurrent_attention``), the LM head through the fused
+    LM-head/log-sum-exp kernels, the memory attention through K13; the frozen
+    projections can run on the tensor-core GEMMs (``tc_linears``).
 """
 from __future__ import annotations
 
@@ -74,6 +78,10 @@ class DrafterTrainConfig:
     global_batch: int = 32
     window_tokens: int = 0  # 0: the whole teacher horizon
     use_graph: bool = True
+    # frozen trunk projections forward/backward on this package's tensor-core GEMMs; off by
+    # default: at 64 rows per recurrent position the library's single-kernel small GEMMs are
+    # faster (8B width, B200: 570 vs 484 ms per step), see ops/linear.py
+    tc_linears: bool = False
     seed: int = 0
 
     def to_dict(self) -> dict[str, Any]:
@@ -354,6 +362,12 @@ class EagleDrafterTrainer:
         if self.device.type == "cuda":
             self._pinned = self._pinned.pin_memory()
         self.launches_per_step: int | None = None
+        # frozen trunk projections (fc, q/k/v/o, gate/up/down) on this package's GEMM, fwd + dX
+        self.tc_linears: list[str] = []
+        if cfg.tc_linears and self.device.type == "cuda" and ops.available():
+            from ..ops.linear import use_tc_for_frozen_linears
+
+            self.tc_linears = use_tc_for_frozen_linears(model)
         # frozen LM head: logits go through the fused log-sum-exp / gather path
         # (no fp32 [rows, vocab] tensors); a trainable head keeps plain logits
         self.head = None

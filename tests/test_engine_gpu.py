@@ -157,3 +157,23 @@ def test_direct_mode_matches_oracle(setup):
         hidden, _ = oracle.forward_tokens(seq, torch.arange(T - S, T - S + seq.numel()), past=past)
         logits = oracle.logits(hidden[0, S - 1:])
         _assert_eps_argmax(logits, toks, eps=0.08)
+
+
+def test_batched_serving_matches_oracle_and_is_row_independent(setup):
+    """serve_batch: per-request CacheBlend prefill into batch slots, one tensor-core LM head for the
+    first tokens, then batched greedy steps (skinny GEMMs, one attention launch for all sequences).
+    At ratio 1.0 (equal to full prefill) every request's tokens are eps-argmax tokens of the fp32
+    oracle, and a request's tokens do not depend on the batch it was served in."""
+    cfg, oracle, engine, store, requests, server = setup
+    blend = CacheBlendConfig(recompute_ratio=1.0, max_new_tokens=12)
+    batch = server.serve_batch(requests[:4], blend=blend)
+    assert int(engine.ext.status(torch.empty(1, device=engine.device)).item()) == 0
+    assert len(batch.token_ids) == 4 and batch.decode_step_ms > 0
+    for req, toks in zip(requests[:4], batch.token_ids):
+        toks = list(toks)
+        T = len(req.prompt)
+        seq = torch.tensor(list(req.prompt) + toks[:-1])
+        hidden, _ = oracle.forward_tokens(seq, torch.arange(seq.numel()))
+        _assert_eps_argmax(oracle.logits(hidden[0, T - 1:]), toks, eps=0.08)
+    alone = server.serve_batch([requests[2]], blend=blend)
+    assert alone.token_ids[0] == batch.token_ids[2]

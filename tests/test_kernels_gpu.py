@@ -579,16 +579,17 @@ def test_lse_gather_forward_backward(cuda_device):
     assert _rel_err(f.grad, fr.grad) < 3e-2
 
 
-@pytest.mark.parametrize("M", [1, 5, 16, 17, 32])
+@pytest.mark.parametrize("M", [1, 5, 16, 17, 32, 33, 64])
 def test_skinny_tensor_core_gemm(cuda_device, M):
     """Swap-AB tcgen05 GEMM for a few rows: store / residual / SwiGLU against fp32, rows independent of M
-    (M <= 16 runs the 16-row token tile, 17..32 the 32-row tile; row 0 must match a 1-row call bitwise)."""
+    (M <= 16 runs the 16-row token tile, 17..32 the 32-row tile, 33..64 the 64-row tile; row 0 must
+    match a 1-row call bitwise)."""
     ext = _ext()
     K, N = 4096, 1536
     x = (torch.randn(M, K, device=cuda_device) * 0.5).to(torch.bfloat16)
     w = (torch.randn(N, K, device=cuda_device) * 0.02).to(torch.bfloat16)
     splits = int(ext.skinny_splits(N, K))
-    ws = torch.empty(splits * N * 32, device=cuda_device)
+    ws = torch.empty(splits * N * 64, device=cuda_device)
     out = torch.empty(M, N, device=cuda_device, dtype=torch.bfloat16)
     ext.skinny_gemm(x, w, 0, out, None, ws)
     ref = x.float() @ w.float().T

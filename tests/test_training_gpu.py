@@ -86,7 +86,74 @@ def test_fused_adamw_matches_torch_adamw_with_clipping(cuda_device):
     assert float(opt.state[0]) == 4.0
 
 
-def _small_setup(dev, seed=0, global_batch=4, use_graph=True, distributed=False):
+def test_frozen_tc_linear_forward_and_input_grad(cuda_device):
+    """Frozen projection on the tcgen05 GEMM: Y = X W^T and dX = dY W against fp32."""
+    from sparsecache_b200.ops.linear import use_tc_for_frozen_linears
+
+    dev = cuda_device
+    lin = torch.nn.Linear(512, 768, bias=False).to(dev, torch.bfloat16)
+    lin.weight.requires_grad_(False)
+    assert use_tc_for_frozen_linears(torch.nn.Sequential(lin)) == ["0"]
+    x = torch.randn(3, 37, 512, device=dev).to(torch.bfloat16).requires_grad_(True)
+    y = lin(x)
+    g = torch.randn_like(y)
+    (y.float() * g.float()).sum().backward()
+    w = lin.weight.float()
+    ref = x.detach().float() @ w.T
+    assert y.shape == (3, 37, 768) and y.dtype == torch.bfloat16
+    assert ((y.float() - ref).abs().max() / ref.abs().max()).item() < 1e-2
+    dref = g.float() @ w
+    assert ((x.grad.float() - dref).abs().max() / dref.abs().max()).item() < 1e-2
+
+
+@pytest.mark.parametrize("G,P", [(4, 1), (4, 97), (8, 256), (1, 33)])
+def test_recurrent_attention_forward_backward_match_fp32(cuda_device, G, P):
+    """K14: one new position over P past keys (GQA group G), forward and q / k / v gradients
+    against fp32 SDPA on repeated K/V."""
+    from sparsecache_b200.ops.linear import recurrent_attention
+
+    dev = cuda_device
+    B, hkv = 3, 2
+    g = torch.Generator(device="cpu").manual_seed(G * 1000 + P)
+    q = torch.randn(B, hkv * G, 1, 128, generator=g).to(dev, torch.bfloat16).requires_grad_(True)
+    k = torch.randn(B, hkv, P, 128, generator=g).to(dev, torch.bfloat16).requires_grad_(True)
+    v = torch.randn(B, hkv, P, 128, generator=g).to(dev, torch.bfloat16).requires_grad_(True)
+    out = recurrent_attention(q, k, v)
+    dout = torch.randn(out.shape, generator=g).to(dev, torch.bfloat16)
+    (out.float() * dout.float()).sum().backward()
+    qr, kr, vr = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    ref = torch.nn.functional.scaled_dot_product_attention(qr, kr.repeat_interleave(G, 1), vr.repeat_interleave(G, 1))
+    (ref * dout.float()).sum().backward()
+    for name, a, b in (("out", out, ref), ("dq", q.grad, qr.grad), ("dk", k.grad, kr.grad), ("dv", v.grad, vr.grad)):
+        # a single key makes the softmax constant: dq is 0 up to rounding, so errors are taken
+        # relative to at least 1e-2
+        err = ((a.float() - b).abs().max() / b.abs().max().clamp_min(1e-2)).item()
+        assert err < 2e-2, (name, err)
+
+
+def test_trainer_with_tc_linears_matches_library_linears(cuda_device):
+    """The trainer with the frozen trunk on the tcgen05 GEMM tracks the one on autograd's linears
+    (bf16 rounding of the projections only)."""
+    dev = cuda_device
+    m1, t1 = _small_setup(dev, use_graph=True, tc_linears=True)
+    m2, t2 = _small_setup(dev, use_graph=True, tc_linears=False)
+    assert t1.tc_linears and not t2.tc_linears
+    t1.warmup_and_capture(warmup=2)
+    t2.warmup_and_capture(warmup=2)
+    for _ in range(3):
+        t1.train_step()
+        t2.train_step()
+        torch.cuda.synchronize()
+        a, b = float(t1.loss), float(t2.loss)
+        assert abs(a - b) <= 2e-2 * max(1.0, abs(b)), (a, b)
+    w1 = m1.memory_attention.query[0].weight
+    w2 = m2.memory_attention.query[0].weight
+    assert (w1 - w2).abs().max().item() < 5e-3
+    t1.release()
+    t2.release()
+
+
+def _small_setup(dev, seed=0, global_batch=4, use_graph=True, distributed=False, tc_linears=False):
     from sparsecache_b200.models.sparse_kv_eagle import SparseKVEagleConfig
     from sparsecache_b200.training.drafter_trainer import (DrafterTrainConfig, EagleDrafterTrainer,
                                                            prepare_for_training, random_eagle_drafter)
@@ -107,7 +174,7 @@ def _small_setup(dev, seed=0, global_batch=4, use_graph=True, distributed=False)
     pos = torch.arange(1024, dtype=torch.float32)[:, None] * torch.logspace(0, -4, 64)[None, :]
     cos = torch.cat((pos.cos(), pos.cos()), -1)
     sin = torch.cat((pos.sin(), pos.sin()), -1)
-    tcfg = DrafterTrainConfig(lr=1e-3, global_batch=global_batch, use_graph=use_graph)
+    tcfg = DrafterTrainConfig(lr=1e-3, global_batch=global_batch, use_graph=use_graph, tc_linears=tc_linears)
     return model, EagleDrafterTrainer(model, bank, cos, sin, tcfg, distributed=distributed)
 
 
