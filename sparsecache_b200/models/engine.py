@@ -265,8 +265,14 @@ class B200Engine:
         n_keys: int,
         kpos: torch.Tensor | None,
         n_rows: int,
+        next_norm: torch.Tensor | None = None,
     ) -> None:
-        """attention over the slot's keys, o_proj + residual, then the MLP block (in place on h)."""
+        """attention over the slot's keys, o_proj + residual, then the MLP block (in place on h).
+
+        The post-attention RMSNorm is produced by the o_proj call (fused into
+        its split-K reduce when it splits); with ``next_norm`` the down_proj
+        call also leaves RMSNorm(h) with that weight in the ``x`` workspace,
+        for the next layer's QKV (``_full_layer(..., x_ready=True)``)."""
         cfg, lw, ext = self.cfg, self.w.layers[layer], self.ext
         attn = self.ws.get("attn", (n_rows, cfg.q_size), torch.bfloat16)
         # few query rows (CacheBlend's active set) leave SMs idle: the kernel
@@ -275,21 +281,27 @@ class B200Engine:
                     if n_rows <= self.ATTN_SPLIT_ROWS else None)
         ext.attention_prefill(q, q_rows, qpos, slot.k(layer), slot.v(layer), kpos, n_keys, cfg.n_heads, self.scale, attn,
                               ws=split_ws)
-        ext.gemm_residual(attn, lw.w_o, h, h, self.bn)
         x = self.ws.get("x", (n_rows, cfg.d_model), torch.bfloat16)
-        ext.rmsnorm(h, None, lw.ln2, cfg.rms_eps, x)
+        ext.gemm_residual(attn, lw.w_o, h, h, self.bn, norm_w=lw.ln2, eps=cfg.rms_eps, norm_out=x)
         act = self.ws.get("act", (n_rows, cfg.ffn), torch.bfloat16)
         ext.gemm_swiglu(x, lw.w_gu, act, self.bn)
-        ext.gemm_residual(act, lw.w_down, h, h, self.bn)
+        if next_norm is None:
+            ext.gemm_residual(act, lw.w_down, h, h, self.bn)
+        else:
+            ext.gemm_residual(act, lw.w_down, h, h, self.bn, norm_w=next_norm, eps=cfg.rms_eps, norm_out=x)
 
     def _qkv_bn(self, rows: int) -> int:
         """128-column tiles when 256-column tiles would leave SMs idle (small M)."""
         tiles = -(-rows // 128) * -(-self.cfg.qkv_rows // 256)
         return 128 if tiles < self.num_sms else self.bn
 
+    def _next_ln1(self, layer: int) -> torch.Tensor | None:
+        """Input-norm weight of the layer after ``layer`` (None after the last layer)."""
+        return self.w.layers[layer + 1].ln1 if layer + 1 < len(self.w.layers) else None
+
     def _full_layer(self, layer: int, h: torch.Tensor, slot: KVSlot, pos: torch.Tensor, slots: torch.Tensor,
                     n_keys: int, kpos: torch.Tensor | None, dev_part=None, dev_mode: int = 0,
-                    push: PushTarget | None = None) -> torch.Tensor:
+                    push: PushTarget | None = None, x_ready: bool = False) -> torch.Tensor:
         """Norm + fused QKV/RoPE/scatter for every row of h; returns q.
 
         With ``push`` the QKV epilogue also stores every K/V row into the
@@ -299,7 +311,8 @@ class B200Engine:
         cfg, lw, ext = self.cfg, self.w.layers[layer], self.ext
         n = h.shape[0]
         x = self.ws.get("x", (n, cfg.d_model), torch.bfloat16)
-        ext.rmsnorm(h, None, lw.ln1, cfg.rms_eps, x)
+        if not x_ready:  # else the previous layer's down_proj left RMSNorm(h) in x
+            ext.rmsnorm(h, None, lw.ln1, cfg.rms_eps, x)
         q = self.ws.get("q", (n, cfg.q_size), torch.bfloat16)
         ext.gemm_qkv(x, lw.w_qkv, q, slot.k(layer), slot.v(layer), pos, slots, self.rope,
                      cfg.n_heads, cfg.n_kv_heads, dev_part, dev_mode, self._qkv_bn(n),
@@ -379,8 +392,9 @@ class B200Engine:
         for layer in range(self.cfg.n_layers):
             if layer_hook is not None:
                 layer_hook(layer, h)
-            q = self._full_layer(layer, h, slot, pos, pos, start + T, kpos, push=push)
-            self._attn_mlp(layer, h, q, slot, q_rows=None, qpos=pos, n_keys=start + T, kpos=kpos, n_rows=T)
+            q = self._full_layer(layer, h, slot, pos, pos, start + T, kpos, push=push, x_ready=layer > 0)
+            self._attn_mlp(layer, h, q, slot, q_rows=None, qpos=pos, n_keys=start + T, kpos=kpos, n_rows=T,
+                           next_norm=self._next_ln1(layer))
         return h
 
     def cacheblend(
@@ -427,13 +441,14 @@ class B200Engine:
         for layer in range(check):
             if before_layer is not None:
                 before_layer(layer)
-            q = self._full_layer(layer, h, slot, gpos, rows, T, kpos)
-            self._attn_mlp(layer, h, q, slot, q_rows=None, qpos=gpos, n_keys=T, kpos=kpos, n_rows=T)
+            q = self._full_layer(layer, h, slot, gpos, rows, T, kpos, x_ready=layer > 0)
+            self._attn_mlp(layer, h, q, slot, q_rows=None, qpos=gpos, n_keys=T, kpos=kpos, n_rows=T,
+                           next_norm=self._next_ln1(layer))
         # ---- check layer ----
         if before_layer is not None:
             before_layer(check)
         dev_part = self.ws.get("dev", (T, 2 * cfg.n_kv_heads), torch.float32)
-        q = self._full_layer(check, h, slot, gpos, rows, T, kpos, dev_part, blend.dev_mode)
+        q = self._full_layer(check, h, slot, gpos, rows, T, kpos, dev_part, blend.dev_mode, x_ready=check > 0)
         active = self._i32("active", T)
         n_active = self._i32("n_active", 1)
         scores = self.ws.get("scores", (max(1, n_doc),), torch.float32)
@@ -445,13 +460,15 @@ class B200Engine:
         ext.index_i32(gpos, act_rows, qpos_a)
         h_a = self.ws.get("h_a", (A, cfg.d_model), torch.bfloat16)
         ext.gather_rows(h, act_rows, h_a)
-        self._attn_mlp(check, h_a, q, slot, q_rows=act_rows, qpos=qpos_a, n_keys=T, kpos=kpos, n_rows=A)
+        self._attn_mlp(check, h_a, q, slot, q_rows=act_rows, qpos=qpos_a, n_keys=T, kpos=kpos, n_rows=A,
+                       next_norm=self._next_ln1(check))
         # ---- later layers: active rows only ----
         for layer in range(check + 1, cfg.n_layers):
             if before_layer is not None:
                 before_layer(layer)
-            qa = self._full_layer(layer, h_a, slot, qpos_a, act_rows, T, kpos)
-            self._attn_mlp(layer, h_a, qa, slot, q_rows=None, qpos=qpos_a, n_keys=T, kpos=kpos, n_rows=A)
+            qa = self._full_layer(layer, h_a, slot, qpos_a, act_rows, T, kpos, x_ready=True)
+            self._attn_mlp(layer, h_a, qa, slot, q_rows=None, qpos=qpos_a, n_keys=T, kpos=kpos, n_rows=A,
+                           next_norm=self._next_ln1(layer))
         meta = {"active": act_rows, "n_active": n_active, "checksum": checksum, "k_selected": k_sel,
                 "document_tokens": n_doc, "active_rows": A}
         return h_a, A, meta

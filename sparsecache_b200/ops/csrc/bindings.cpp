@@ -120,7 +120,14 @@ int choose_shape(sc::GemmArgs& g, bool may_split, int64_t splits_req) {
   return best_s;
 }
 
-bool run_gemm_split(sc::GemmArgs g, int s, const Tensor& like) {
+struct NormOut {  // optional RMSNorm of the finished rows (the next projection's input)
+  const __nv_bfloat16* w = nullptr;
+  float eps = 0.f;
+  __nv_bfloat16* out = nullptr;
+  int ld = 0;
+};
+
+bool run_gemm_split(sc::GemmArgs g, int s, const Tensor& like, const NormOut& norm = NormOut{}) {
   if (s <= 1 || g.M == 0) return false;
   Tensor ws = torch::empty({s, g.M, g.N}, like.options().dtype(torch::kFloat32));
   const __nv_bfloat16* residual = g.epi == sc::EPI_RESIDUAL ? g.ep.residual : nullptr;
@@ -131,7 +138,13 @@ bool run_gemm_split(sc::GemmArgs g, int s, const Tensor& like) {
   g.splits = s;
   g.ep.ws = ws.data_ptr<float>();
   check_cuda(sc::gemm_bf16_tc(g, cur_stream()), "gemm_bf16_tc (split-K)");
-  check_cuda(sc::splitk_reduce(g.ep.ws, s, g.M, g.N, residual, ldr, out, ldo, cur_stream()), "splitk_reduce");
+  if (norm.w != nullptr) {
+    check_cuda(sc::splitk_reduce_norm(g.ep.ws, s, g.M, g.N, residual, ldr, out, ldo, norm.w, norm.eps, norm.out,
+                                      norm.ld, cur_stream()),
+               "splitk_reduce_norm");
+  } else {
+    check_cuda(sc::splitk_reduce(g.ep.ws, s, g.M, g.N, residual, ldr, out, ldo, cur_stream()), "splitk_reduce");
+  }
   return true;
 }
 
@@ -150,8 +163,11 @@ int64_t gemm_store(Tensor a, Tensor w, Tensor out, int64_t bn, int64_t splits) {
   return 1;
 }
 
-// out = residual + bf16(a @ w^T)   (out may alias residual)
-int64_t gemm_residual(Tensor a, Tensor w, Tensor out, Tensor residual, int64_t bn, int64_t splits) {
+// out = residual + bf16(a @ w^T)   (out may alias residual); with norm_w also
+// norm_out = RMSNorm(out) (fused into the split-K reduce when split-K runs,
+// else the RMSNorm kernel after the GEMM).  Returns the kernels launched.
+int64_t gemm_residual(Tensor a, Tensor w, Tensor out, Tensor residual, int64_t bn, int64_t splits,
+                      c10::optional<Tensor> norm_w, double eps, c10::optional<Tensor> norm_out) {
   const c10::cuda::CUDAGuard guard(a.device());
   auto g = base_gemm(a, w, sc::EPI_RESIDUAL, (int)bn);
   check_matrix(out, "out");
@@ -163,10 +179,25 @@ int64_t gemm_residual(Tensor a, Tensor w, Tensor out, Tensor residual, int64_t b
   g.ep.ldo = (int)out.stride(0);
   g.ep.residual = reinterpret_cast<const __nv_bfloat16*>(residual.data_ptr());
   g.ep.ldr = (int)residual.stride(0);
+  NormOut norm;
+  if (norm_w.has_value() && norm_w->defined()) {
+    TORCH_CHECK(norm_out.has_value() && norm_out->defined(), "norm_out required with norm_w");
+    CHECK_BF16(*norm_w); check_matrix(*norm_out, "norm_out");
+    TORCH_CHECK(norm_w->numel() == g.N && norm_out->sizes() == out.sizes(), "norm shapes");
+    TORCH_CHECK(g.N % 8 == 0 && g.N <= 8192, "fused norm: N % 8 == 0, N <= 8192");
+    norm.w = reinterpret_cast<const __nv_bfloat16*>(norm_w->data_ptr());
+    norm.eps = (float)eps;
+    norm.out = reinterpret_cast<__nv_bfloat16*>(norm_out->data_ptr());
+    norm.ld = (int)norm_out->stride(0);
+  }
   const int s = choose_shape(g, true, splits);
-  if (run_gemm_split(g, s, a)) return 2;  // kernels launched
+  if (run_gemm_split(g, s, a, norm)) return 2;  // kernels launched (the norm is fused into the reduce)
   run_gemm(g);
-  return 1;
+  if (norm.w == nullptr) return 1;
+  check_cuda(sc::rmsnorm_bf16(g.ep.out, g.ep.ldo, nullptr, norm.w, norm.out, norm.ld, g.M, g.N, norm.eps,
+                              cur_stream()),
+             "rmsnorm");
+  return 2;
 }
 
 // out[:, j] = silu(gate_j) * up_j with w_gu rows interleaved in blocks of bn/2
@@ -1213,7 +1244,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_store", &gemm_store, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("bn"),
         py::arg("splits") = -1);
   m.def("gemm_residual", &gemm_residual, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("residual"),
-        py::arg("bn"), py::arg("splits") = -1);
+        py::arg("bn"), py::arg("splits") = -1, py::arg("norm_w") = py::none(), py::arg("eps") = 1e-5,
+        py::arg("norm_out") = py::none());
   m.def("gemm_swiglu", &gemm_swiglu);
   m.def("gemm_qkv", &gemm_qkv, py::arg("a"), py::arg("w_qkv"), py::arg("q_out"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("rope_pos"), py::arg("cache_slot"), py::arg("rope_table"),

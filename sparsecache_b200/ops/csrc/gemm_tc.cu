@@ -676,6 +676,88 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
   }
 }
 
+// Split-K reduce + RESIDUAL epilogue + the RMSNorm of each finished row (the
+// next projection's input), one CTA of 256 threads per row.  Thread t owns
+// the 8-column chunks t, t + 256, ...; the sum of squares runs over the
+// bf16-rounded outputs in exactly the order of rmsnorm_kernel (same chunk
+// ownership, same pair order, same warp / block reduction), so norm_out is
+// bit-identical to running rmsnorm_bf16 on the stored rows.
+constexpr int kRedNormMaxChunks = 4;  // N <= 256 threads * 4 chunks * 8 = 8192
+__global__ void __launch_bounds__(256) splitk_reduce_norm_kernel(const float* __restrict__ ws, int splits, int M,
+                                                                 int N, const __nv_bfloat16* residual, int ldr,
+                                                                 __nv_bfloat16* out, int ldo,
+                                                                 const __nv_bfloat16* norm_w, float eps,
+                                                                 __nv_bfloat16* norm_out, int ldn) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const int n8 = N / 8;
+  uint32_t keep[kRedNormMaxChunks][4];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kRedNormMaxChunks; ++k) {
+    const int c = threadIdx.x + k * 256;
+    if (c >= n8) break;
+    float acc[8];
+    {
+      const float4 a0 = __ldcs(reinterpret_cast<const float4*>(ws + (size_t)row * N + 8 * c));
+      const float4 a1 = __ldcs(reinterpret_cast<const float4*>(ws + (size_t)row * N + 8 * c) + 1);
+      acc[0] = a0.x; acc[1] = a0.y; acc[2] = a0.z; acc[3] = a0.w;
+      acc[4] = a1.x; acc[5] = a1.y; acc[6] = a1.z; acc[7] = a1.w;
+    }
+    for (int s = 1; s < splits; ++s) {
+      const float* src = ws + ((size_t)s * M + row) * N + 8 * c;
+      const float4 p0 = __ldcs(reinterpret_cast<const float4*>(src));
+      const float4 p1 = __ldcs(reinterpret_cast<const float4*>(src) + 1);
+      acc[0] += p0.x; acc[1] += p0.y; acc[2] += p0.z; acc[3] += p0.w;
+      acc[4] += p1.x; acc[5] += p1.y; acc[6] += p1.z; acc[7] += p1.w;
+    }
+    const uint4 rr = *reinterpret_cast<const uint4*>(residual + (size_t)row * ldr + 8 * c);
+    const uint32_t ri[4] = {rr.x, rr.y, rr.z, rr.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 r = unpack_bf16x2(ri[q]);
+      keep[k][q] = pack_bf16x2(r.x + bf16_round(acc[2 * q]), r.y + bf16_round(acc[2 * q + 1]));
+      const float2 f = unpack_bf16x2(keep[k][q]);
+      ss += f.x * f.x + f.y * f.y;
+    }
+    *reinterpret_cast<uint4*>(out + (size_t)row * ldo + 8 * c) = make_uint4(keep[k][0], keep[k][1], keep[k][2], keep[k][3]);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float rinv = rsqrtf(red[0] / (float)N + eps);
+#pragma unroll
+  for (int k = 0; k < kRedNormMaxChunks; ++k) {
+    const int c = threadIdx.x + k * 256;
+    if (c >= n8) break;
+    const uint4 g = *reinterpret_cast<const uint4*>(norm_w + 8 * c);
+    const uint32_t gi[4] = {g.x, g.y, g.z, g.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 xf = unpack_bf16x2(keep[k][q]), gf = unpack_bf16x2(gi[q]);
+      o[q] = pack_bf16x2(gf.x * bf16_round(xf.x * rinv), gf.y * bf16_round(xf.y * rinv));
+    }
+    *reinterpret_cast<uint4*>(norm_out + (size_t)row * ldn + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+cudaError_t splitk_reduce_norm(const float* ws, int splits, int M, int N, const __nv_bfloat16* residual, int ldr,
+                               __nv_bfloat16* out, int ldo, const __nv_bfloat16* norm_w, float eps,
+                               __nv_bfloat16* norm_out, int ldn, cudaStream_t stream) {
+  if (N % 8 != 0 || N / 8 > 256 * kRedNormMaxChunks || splits < 1 || residual == nullptr) return cudaErrorInvalidValue;
+  if (M <= 0) return cudaSuccess;
+  splitk_reduce_norm_kernel<<<M, 256, 0, stream>>>(ws, splits, M, N, residual, ldr, out, ldo, norm_w, eps, norm_out,
+                                                    ldn);
+  return cudaGetLastError();
+}
+
 cudaError_t splitk_reduce(const float* ws, int splits, int M, int N, const __nv_bfloat16* residual, int ldr,
                           __nv_bfloat16* out, int ldo, cudaStream_t stream) {
   if (N % 4 != 0 || splits < 1) return cudaErrorInvalidValue;

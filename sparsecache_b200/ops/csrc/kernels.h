@@ -91,6 +91,11 @@ cudaError_t gemm_bf16_tc(const GemmArgs& g, cudaStream_t stream);
 double gemm_cost_estimate(int M, int N, int K, int bn, int rows_per_tile, int splits, int num_sms);
 cudaError_t splitk_reduce(const float* ws, int splits, int M, int N, const __nv_bfloat16* residual, int ldr,
                           __nv_bfloat16* out, int ldo, cudaStream_t stream);
+// the same with the RESIDUAL epilogue and the RMSNorm of every finished row
+// (bit-identical to rmsnorm_bf16 on the stored rows); N % 8 == 0, N <= 8192
+cudaError_t splitk_reduce_norm(const float* ws, int splits, int M, int N, const __nv_bfloat16* residual, int ldr,
+                               __nv_bfloat16* out, int ldo, const __nv_bfloat16* norm_w, float eps,
+                               __nv_bfloat16* norm_out, int ldn, cudaStream_t stream);
 
 // ---------------------------------------------------------------- GEMV ----
 // Small-M (1..8 rows) weight-streaming kernel for decode / verify.
@@ -309,7 +314,7 @@ struct SkinnyArgs {
   int ldo;
   const __nv_bfloat16* residual;  // [M, N] row stride ldr (SKINNY_RESIDUAL; may alias out)
   int ldr;
-  float* ws;               // [splits][N][bn] fp32, bn = skinny_bn(M)
+  float* ws;               // [splits][M][N] fp32 (at least splits * N * bn floats, bn = skinny_bn(M))
   int splits;
   int bn;                  // token-row tile (16, 32 or 64), set by the launcher
   int num_sms;

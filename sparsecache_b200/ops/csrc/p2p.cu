@@ -102,6 +102,11 @@ __global__ void __launch_bounds__(kRsThreads) rs_reduce_kernel(RsReduceArgs a) {
   __shared__ float red[kRsThreads / 32];
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
+  // launched programmatically after the partial-sending kernel: the flags
+  // (acquire) order every partial, including this rank's own, so the CTAs
+  // can sit resident and poll while that kernel finishes; the next kernel
+  // may launch now and prefetch its weights (it waits before reading ours)
+  pdl_launch_dependents();
   if (tid == 0) {
     s_fail = (a.status != nullptr && *((volatile int*)a.status) != 0) ? 1 : 0;  // fail fast
     const int epoch = a.epoch_ptr ? *a.epoch_ptr * a.epoch_mul + a.epoch : a.epoch;
@@ -122,6 +127,7 @@ __global__ void __launch_bounds__(kRsThreads) rs_reduce_kernel(RsReduceArgs a) {
   }
   __syncthreads();
   if (s_fail) return;
+  pdl_wait();  // the residual row and the output buffers: the predecessor has completed
   // column block of this CTA (several blocks per row only without the norm,
   // which needs the whole row)
   const int nvec_row = a.N / 4;
@@ -184,8 +190,16 @@ cudaError_t rs_reduce(const RsReduceArgs& a, cudaStream_t stream) {
   // needs whole rows and keeps one CTA per row
   int blocks = 1;
   if (a.norm_w == nullptr && a.rows < 64) blocks = (a.N / 4 + kRsThreads - 1) / kRsThreads;
-  rs_reduce_kernel<<<dim3(a.rows, blocks), kRsThreads, 0, stream>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.rows, blocks, 1);
+  cfg.blockDim = dim3(kRsThreads, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, rs_reduce_kernel, a);
 }
 
 }  // namespace sc

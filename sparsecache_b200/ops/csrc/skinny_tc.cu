@@ -10,7 +10,7 @@
 // >= M), and the 128 x N fp32 accumulator lives in TMEM (two buffers).  Work
 // units are (128-row weight tile, K slice) so that ~one unit per SM streams
 // its slice with a deep (10-stage) TMA pipeline; each unit writes its fp32
-// partial tile [128 rows][N] to a workspace, and a small reduce kernel sums the K slices
+// partial tile to a workspace [slice][token row][weight row], and a small reduce kernel sums the K slices
 // in a fixed order and applies the epilogue (store, residual add with the
 // HF rounding order, SwiGLU over 128-row interleaved gate/up blocks).  The
 // result of a row m does not depend on M (columns never mix in the MMA and
@@ -65,7 +65,7 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
 template <int BN>
 __global__ void __launch_bounds__(kSkThreads, 1)
     skinny_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                      int N, int K, int splits, float* ws, int* status) {
+                      int M, int N, int K, int splits, float* ws, int* status) {
   using Cfg = SkCfg<BN>;
   constexpr int kSkStageBytes = Cfg::kStageBytes;
   constexpr int kSkStages = Cfg::kStages;
@@ -190,11 +190,13 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       tmem_ld_wait();
       const int row = tile * kSkBM + quarter * 32 + lane;
       if (row < N) {
-        float4* d = reinterpret_cast<float4*>(ws + ((size_t)ks * N + row) * BN);
+        // partials laid out [slice][token row m][weight row n]: a warp's 32
+        // weight rows are 128 contiguous bytes per token row, and the reduce
+        // kernel reads them back along n with coalesced loads
+        float* d = ws + (size_t)ks * M * N + row;
 #pragma unroll
-        for (int i = 0; i < BN / 4; ++i)
-          d[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]), __uint_as_float(r[4 * i + 2]),
-                             __uint_as_float(r[4 * i + 3]));
+        for (int m = 0; m < BN; ++m)
+          if (m < M) d[(size_t)m * N] = __uint_as_float(r[m]);
       }
       tc_fence_before();
       __syncwarp();
@@ -220,7 +222,7 @@ __global__ void skinny_reduce_kernel(SkinnyArgs a) {
   const int m = active ? idx / outs : 0, j = active ? idx % outs : 0;
   auto sum_row = [&](int n) {
     float v = 0.f;
-    for (int s = 0; s < a.splits; ++s) v += a.ws[((size_t)s * a.N + n) * a.bn + m];
+    for (int s = 0; s < a.splits; ++s) v += a.ws[((size_t)s * a.M + m) * a.N + n];
     return v;
   };
   if (active) {
@@ -382,9 +384,9 @@ cudaError_t skinny_gemm(const SkinnyArgs& args, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e =
-      a.bn == 16   ? cudaLaunchKernelEx(&cfg, skinny_mma_kernel<16>, tw, tx, a.N, a.K, a.splits, a.ws, a.status)
-      : a.bn == 32 ? cudaLaunchKernelEx(&cfg, skinny_mma_kernel<32>, tw, tx, a.N, a.K, a.splits, a.ws, a.status)
-                   : cudaLaunchKernelEx(&cfg, skinny_mma_kernel<64>, tw, tx, a.N, a.K, a.splits, a.ws, a.status);
+      a.bn == 16   ? cudaLaunchKernelEx(&cfg, skinny_mma_kernel<16>, tw, tx, a.M, a.N, a.K, a.splits, a.ws, a.status)
+      : a.bn == 32 ? cudaLaunchKernelEx(&cfg, skinny_mma_kernel<32>, tw, tx, a.M, a.N, a.K, a.splits, a.ws, a.status)
+                   : cudaLaunchKernelEx(&cfg, skinny_mma_kernel<64>, tw, tx, a.M, a.N, a.K, a.splits, a.ws, a.status);
   if (e != cudaSuccess) return e;
   const int outs = ((a.epi == SKINNY_SWIGLU || a.epi == SKINNY_QKV) ? a.N / 2 : a.N) * a.M;
   cfg.gridDim = dim3((outs + 255) / 256, 1, 1);

@@ -31,18 +31,33 @@ def main() -> None:
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--new-tokens", type=int, default=24)
     p.add_argument("--ratio", type=float, default=0.15)
+    p.add_argument("--batch", type=int, default=0, help="> 0: profile serve_batch of this many requests")
     args = p.parse_args()
     cfg = get_model_config(args.model)
     if args.layers:
         cfg = cfg.with_layers(args.layers)
     dev = torch.device("cuda:0")
     engine = B200Engine.random(cfg, seed=0, device=dev)
-    requests = make_requests("llama8b_rag", cfg)[: args.requests]
+    requests = make_requests("llama8b_rag", cfg)[: max(args.requests, args.batch)]
     store = DocumentKVStore(cfg, tier="hbm", device=dev)
     blend = CacheBlendConfig(recompute_ratio=args.ratio, max_new_tokens=args.new_tokens)
     server = RAGServer(engine, store, capacity=max(r.prompt_tokens for r in requests) + args.new_tokens + 64,
                        blend=blend)
     server.produce(requests)
+    if args.batch > 0:
+        batch = requests[: args.batch]
+        for _ in range(args.warmup):
+            server.serve_batch(batch)
+        torch.cuda.synchronize()
+        launches = engine.ext.launches
+        torch.cuda.nvtx.range_push("profile")
+        res = server.serve_batch(batch)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        print(json.dumps({"mode": "batch", "batch": args.batch, "batch_ms": res.response_ms,
+                          "decode_step_ms": res.decode_step_ms, "first_tokens_ms": res.metadata["first_tokens_ms"],
+                          "launches": engine.ext.launches - launches}))
+        return
     for _ in range(args.warmup):
         server.serve(requests[0], mode=args.mode, sync=True)
     torch.cuda.synchronize()

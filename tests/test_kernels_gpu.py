@@ -65,6 +65,30 @@ def test_gemm_split_k_residual(cuda_device, mnk):
     assert _rel_err(st, a.float() @ w.float().T) < 1e-2
 
 
+@pytest.mark.parametrize("M,K,splits", [(300, 4096, 3), (300, 14336, -1), (257, 512, 1), (1000, 4096, 1)])
+def test_gemm_residual_with_fused_norm(cuda_device, M, K, splits):
+    """gemm_residual(..., norm_w, norm_out): the RMSNorm of the new rows (fused into the split-K reduce
+    when it splits) is bit-identical to the RMSNorm kernel run on the stored rows."""
+    ext = _ext()
+    N = 4096
+    g = torch.Generator(device="cpu").manual_seed(M + K)
+    a = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(cuda_device, torch.bfloat16)
+    res = torch.randn(M, N, generator=g).to(cuda_device, torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(N, generator=g)).to(cuda_device, torch.bfloat16)
+    out, normed = res.clone(), torch.empty(M, N, device=cuda_device, dtype=torch.bfloat16)
+    launched = ext.gemm_residual(a, w, out, out, 256, splits, norm_w=nw, eps=1e-5, norm_out=normed)
+    assert launched == 2
+    plain = res.clone()
+    ext.gemm_residual(a, w, plain, plain, 256, splits)
+    ref_norm = torch.empty_like(normed)
+    ext.rmsnorm(plain, None, nw, 1e-5, ref_norm)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    assert torch.equal(out, plain)
+    assert torch.equal(normed, ref_norm)
+
+
 def test_gemm_residual_and_swiglu(cuda_device):
     M, K, F = 257, 512, 1024
     a = torch.randn(M, K, device=cuda_device).to(torch.bfloat16)

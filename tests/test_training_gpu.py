@@ -224,6 +224,16 @@ def _dp_worker(rank, world, port, out_dir):
         res["steps"] = tr.steps_done
         dist.barrier()
         tr.release()
+        # one eager step from a fresh start: the first moment of this rank's optimizer shard is
+        # (1 - beta1) * clip * (rank-averaged gradient), linear in the gradient
+        model2, tr2 = _small_setup(dev, global_batch=4, use_graph=False, distributed=True)
+        tr2.train_step()
+        torch.cuda.synchronize()
+        tr2.opt.check()
+        torch.save({"exp_avg": tr2.opt.exp_avg.cpu(), "numel": tr2.flat.numel, "shard": tr2.flat.shard(world)},
+                   os.path.join(out_dir, f"m1_rank{rank}.pt"))
+        dist.barrier()
+        tr2.release()
     except Exception as exc:  # noqa: BLE001
         res["error"] = repr(exc)
     finally:
@@ -248,9 +258,17 @@ def test_data_parallel_optimizer_matches_single_gpu(tmp_path, cuda_device):
     ref = model.memory_attention.query[1].weight.float().cpu().flatten()[:4096]
     got = torch.tensor(res[0]["weight"])
     # Adam normalises every element's step, so bf16 rounding differences between one 4-row and two
-    # 2-row batches can flip the sign of near-zero updates; compare the updates as a whole.
+    # 2-row batches flip the sign of near-zero updates: after five steps compare only the direction
     d_ref, d_got = ref - init, got - init
-    rel = ((d_got - d_ref).norm() / d_ref.norm()).item()
-    assert rel < 0.1, rel
-    assert torch.nn.functional.cosine_similarity(d_got, d_ref, dim=0).item() > 0.99
+    assert torch.nn.functional.cosine_similarity(d_got, d_ref, dim=0).item() > 0.9
+    # the exact check: after one step from the same start, the concatenated first-moment shards of
+    # the two ranks equal the single-GPU first moment (the gradient of the 4-row batch, averaged)
+    m1 = [torch.load(tmp_path / f"m1_rank{r}.pt") for r in range(2)]
+    m_dp = torch.cat([m["exp_avg"] for m in m1])[: m1[0]["numel"]]
+    model3, tr3 = _small_setup(cuda_device, global_batch=4, use_graph=False)
+    tr3.train_step()
+    torch.cuda.synchronize()
+    m_ref = tr3.opt.exp_avg[: tr3.flat.numel].cpu()
+    rel = ((m_dp - m_ref).norm() / m_ref.norm()).item()
+    assert rel < 2e-2, rel
 
