@@ -220,6 +220,27 @@ def main() -> None:
                         "us": t, "frac_of_measured_hbm": kv_bytes / (t * 1e-6) / 1e9 / HBM_GBS,
                         "automatic": (S, R) == auto}
 
+    if "attn_decode_batch" in only:
+        # batched decode attention: 32 sequences, each with its own slot (stride apart) at ~1676 keys,
+        # 4 layers' caches cycled so K/V come from HBM (32 x 6.9 MB per layer); one launch per layer
+        H, Hkv, cap, B, layers = 32, 8, 2768, 32, 4
+        per = Hkv * cap * 128
+        kbuf = [torch.randn(B * per, device=dev).to(bf) for _ in range(layers)]
+        vbuf = [torch.randn(B * per, device=dev).to(bf) for _ in range(layers)]
+        q = torch.randn(B, H * 128, device=dev).to(bf)
+        out = torch.empty(B, H * 128, device=dev, dtype=bf)
+        pos_rows = torch.full((B,), 1675, device=dev, dtype=torch.int32)
+        S = int(ext.attention_decode_cluster(cap, Hkv))
+
+        def run_layers():
+            for i in range(layers):
+                ext.attention_decode(q, kbuf[i][:per].view(Hkv, cap, 128), vbuf[i][:per].view(Hkv, cap, 128),
+                                     pos_rows, H, 1 / math.sqrt(128), S, out, pos_rows=pos_rows, seq_stride=per)
+        t = timeit(run_layers, n=10, warm=3) / layers
+        kv_bytes = B * 2 * Hkv * 1676 * 128 * 2
+        res["attn_decode_batch32_keys1676"] = {"us": t, "frac_of_measured_hbm": kv_bytes / (t * 1e-6) / 1e9 / HBM_GBS,
+                                               "cluster": S}
+
     if "attn_decode_grid" in only:
         # cluster size x (one / several clusters per kv head) for the decode shapes that matter
         for H, Hkv, cap in ((32, 8, 2048), (32, 8, 18000), (8, 1, 16384), (16, 4, 4096)):
