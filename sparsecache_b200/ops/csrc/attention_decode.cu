@@ -51,6 +51,15 @@ constexpr int kMaxOuter = 16; // clusters per kv head (second split level)
 // and the CTAs of the cluster through DSMEM.
 constexpr int kRQ = 4;  // query vectors per z-block
 
+// 2^x by the MUFU ex2 instruction (flush-to-zero; 2^-inf = +0): the key
+// loop's three exponentials per key pair and vector are its costliest
+// instructions, and a softmax weight needs no more than this precision
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 struct RegSmem {
   float wo[kWarps][kRQ][128];  // per-warp partial accumulators
   float wm[kWarps][kRQ], wl[kWarps][kRQ];
@@ -181,9 +190,9 @@ __global__ void __launch_bounds__(kThreads)
       if (mn == -INFINITY) {  // nothing visible yet for this vector
         corr[i] = 1.f, p0[i] = 0.f, p1[i] = 0.f;
       } else {
-        corr[i] = exp2f(mx[i] - mn);
-        p0[i] = exp2f(s0[i] - mn);
-        p1[i] = exp2f(s1[i] - mn);
+        corr[i] = ex2_fast(mx[i] - mn);
+        p0[i] = ex2_fast(s0[i] - mn);
+        p1[i] = ex2_fast(s1[i] - mn);
         mx[i] = mn;
       }
       ls[i] = ls[i] * corr[i] + p0[i] + p1[i];

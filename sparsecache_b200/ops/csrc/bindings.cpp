@@ -393,7 +393,8 @@ void rs_reduce(Tensor recv, Tensor flags, int64_t epoch, int64_t timeout_ns, Ten
 // Row-parallel decode projection with the all-reduce fused into the epilogue.
 void gemv_allreduce(Tensor x, Tensor w, c10::optional<Tensor> norm_w, double eps, std::vector<int64_t> dst_ptrs,
                     std::vector<int64_t> flag_ptrs, int64_t sender, int64_t epoch, c10::optional<Tensor> epoch_ptr,
-                    int64_t epoch_mul, Tensor counter) {
+                    int64_t epoch_mul, Tensor counter, c10::optional<Tensor> recv, c10::optional<Tensor> wait_flags,
+                    c10::optional<Tensor> residual, int64_t timeout_ns, c10::optional<Tensor> status) {
   const c10::cuda::CUDAGuard guard(x.device());
   auto g = base_gemv(x, w, norm_w, eps, sc::GEMV_ALLREDUCE);
   TORCH_CHECK(dst_ptrs.size() == flag_ptrs.size() && !dst_ptrs.empty() && dst_ptrs.size() <= 8, "1..8 ranks");
@@ -411,6 +412,23 @@ void gemv_allreduce(Tensor x, Tensor w, c10::optional<Tensor> norm_w, double eps
   }
   CHECK_I32(counter);
   g.counter = reinterpret_cast<unsigned int*>(counter.data_ptr<int>());
+  if (recv.has_value() && recv->defined()) {
+    // fused reduction: residual (in place) += sum over ranks of the partial rows
+    TORCH_CHECK(wait_flags.has_value() && residual.has_value() && status.has_value(),
+                "fused reduce needs wait_flags, residual and status");
+    CHECK_F32(*recv); CHECK_I32(*wait_flags); CHECK_BF16(*residual); CHECK_I32(*status);
+    TORCH_CHECK(recv->numel() >= (int64_t)g.ar_tp * g.M * g.N, "recv [tp, M, N]");
+    TORCH_CHECK(wait_flags->numel() >= g.ar_tp, "one wait flag per rank");
+    TORCH_CHECK(residual->dim() == 2 && residual->size(0) == g.M && residual->size(1) == g.N &&
+                    residual->is_contiguous(), "residual [M, N] contiguous");
+    TORCH_CHECK(g.N % 4 == 0, "N % 4");
+    g.ar_recv = recv->data_ptr<float>();
+    g.ar_wait_flags = wait_flags->data_ptr<int>();
+    g.ar_residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    g.ar_out = reinterpret_cast<__nv_bfloat16*>(residual->data_ptr());
+    g.ar_timeout_ns = timeout_ns;
+    g.status = status->data_ptr<int>();
+  }
   run_gemv(g);
 }
 
@@ -1279,7 +1297,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rs_reduce", &rs_reduce, py::arg("recv"), py::arg("flags"), py::arg("epoch"), py::arg("timeout_ns"),
         py::arg("status"), py::arg("residual"), py::arg("out"), py::arg("norm_w"), py::arg("norm_out"),
         py::arg("eps"), py::arg("epoch_ptr") = py::none(), py::arg("epoch_mul") = 0);
-  m.def("gemv_allreduce", &gemv_allreduce);
+  m.def("gemv_allreduce", &gemv_allreduce, py::arg("x"), py::arg("w"), py::arg("norm_w"), py::arg("eps"),
+        py::arg("dst_ptrs"), py::arg("flag_ptrs"), py::arg("sender"), py::arg("epoch"), py::arg("epoch_ptr"),
+        py::arg("epoch_mul"), py::arg("counter"), py::arg("recv") = py::none(), py::arg("wait_flags") = py::none(),
+        py::arg("residual") = py::none(), py::arg("timeout_ns") = 20000000000LL, py::arg("status") = py::none());
   m.def("shared_empty", &shared_empty);
   m.def("shared_open", &shared_open);
   m.def("shared_close", &shared_close);

@@ -342,6 +342,49 @@ __global__ void __launch_bounds__(kThreads)
       if (tid < a.ar_tp)
         asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(a.ar_flag[tid]), "r"(epoch) : "memory");
       if (tid == 0) *a.counter = 0u;
+      if (a.ar_recv != nullptr) {
+        // fused reduction (replaces a separate reduce kernel): wait (bounded)
+        // for every rank's partial, sum them in rank order, add the residual
+        // with the HF rounding order (residual + bf16(sum))
+        __shared__ int s_fail;
+        if (tid == 0) {
+          s_fail = (a.status != nullptr && *((volatile int*)a.status) != 0) ? 1 : 0;
+          unsigned long long t0;
+          asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t0));
+          for (int r = 0; r < a.ar_tp && !s_fail; ++r) {
+            while (true) {
+              int v;
+              asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(a.ar_wait_flags + r) : "memory");
+              if (v >= epoch) break;
+              unsigned long long t1;
+              asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t1));
+              if ((long long)(t1 - t0) > a.ar_timeout_ns) {
+                report_status(a.status, kStatusTimeoutPeerFlag);
+                s_fail = 1;
+                break;
+              }
+              __nanosleep(64);
+            }
+          }
+        }
+        __syncthreads();
+        if (!s_fail) {
+          const int n4 = a.N / 4;
+          for (int i = tid; i < M * n4; i += kThreads) {
+            const int m = i / n4, c = i - m * n4;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = 0; r < a.ar_tp; ++r) {
+              const float4 p = __ldcg(reinterpret_cast<const float4*>(a.ar_recv + ((size_t)r * M + m) * a.N) + c);
+              acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+            }
+            const uint2 rr = *reinterpret_cast<const uint2*>(a.ar_residual + (size_t)m * a.N + 4 * c);
+            const float2 r0 = unpack_bf16x2(rr.x), r1 = unpack_bf16x2(rr.y);
+            *reinterpret_cast<uint2*>(a.ar_out + (size_t)m * a.N + 4 * c) =
+                make_uint2(pack_bf16x2(r0.x + bf16_round(acc.x), r0.y + bf16_round(acc.y)),
+                           pack_bf16x2(r1.x + bf16_round(acc.z), r1.y + bf16_round(acc.w)));
+          }
+        }
+      }
     }
     return;
   }

@@ -152,6 +152,15 @@ struct GemvArgs {
   int ar_epoch;          // epoch = ar_epoch_ptr ? *ar_epoch_ptr * ar_epoch_mul + ar_epoch : ar_epoch
   const int* ar_epoch_ptr;
   int ar_epoch_mul;
+  // optional fused reduction by the last CTA (null ar_recv: a separate reduce
+  // kernel follows): wait until ar_wait_flags[0..tp) reach the epoch, then
+  // ar_out[m] = ar_residual[m] + bf16(sum_r ar_recv[r][m][N]) in rank order
+  const float* ar_recv;
+  const int* ar_wait_flags;
+  const __nv_bfloat16* ar_residual;
+  __nv_bfloat16* ar_out;
+  long long ar_timeout_ns;
+  int* status;
   int num_sms;
 };
 

@@ -46,6 +46,7 @@ all-reduces so that the two receive buffers strictly alternate.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import replace
 
 import torch
@@ -62,6 +63,9 @@ FLAG_STAGE_X, FLAG_STAGE_X2 = 8, 9  # local: a peer shard has landed in the stag
 FLAG_DEV, FLAG_H, FLAG_STAGE_H = 10, 11, 12  # CacheBlend: deviation partials, residual all-gather
 N_FLAG_KINDS = 13
 TIMEOUT_NS = int(20e9)
+# decode all-reduce: the sending GEMV's last CTA also performs the reduction
+# (SC_TP_FUSED_REDUCE=0 keeps the separate reduce kernel, for A/B measurements)
+FUSED_REDUCE = os.environ.get("SC_TP_FUSED_REDUCE", "1") != "0"
 # Guard bands around every peer-mapped buffer: peers write into these buffers
 # from their kernels (partial tiles, all-reduce rows, flags), so an index bug
 # shows up as a changed guard band, checked by ``TPGroup.check_canaries``.
@@ -469,13 +473,20 @@ class TPEngine:
         kind = FLAG_AR_O if odd else FLAG_AR_D
         flags = [self._flag_addr(r, kind, self.rank) for r in range(self.tp)]
         counter = self.ar_counters[0:1] if odd else self.ar_counters[1:2]
+        recv = buf.view(torch.float32)[: self.tp * M * d].view(self.tp, M, d)
         if skinny:
             if norm_w is not None:
                 raise ValueError("the skinny all-reduce takes normalised rows")
             ext.skinny_allreduce(x, w, ptrs, flags, self.rank, k, step, self.ar_stride, counter, self.skinny_ws)
+        elif FUSED_REDUCE:
+            # the GEMV's last CTA waits for every rank's partial and adds the sum to the residual:
+            # no separate reduce kernel (one kernel boundary less per all-reduce)
+            ext.gemv_allreduce(x, w, norm_w, cfg.rms_eps, ptrs, flags, self.rank, k, step, self.ar_stride, counter,
+                               recv=recv, wait_flags=self.flags[kind], residual=residual, timeout_ns=TIMEOUT_NS,
+                               status=self.status)
+            return
         else:
             ext.gemv_allreduce(x, w, norm_w, cfg.rms_eps, ptrs, flags, self.rank, k, step, self.ar_stride, counter)
-        recv = buf.view(torch.float32)[: self.tp * M * d].view(self.tp, M, d)
         ext.rs_reduce(recv, self.flags[kind], k, TIMEOUT_NS, self.status, residual, residual, None, None,
                       cfg.rms_eps, step, self.ar_stride)
 
