@@ -27,6 +27,7 @@ Reference behaviour: modeling.py:33-417, reuse_cacheblend_pipeline.py:322-893.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -170,6 +171,11 @@ class PushTarget:
 # vectors][max, sum, o[128]] fp32, and one ticket counter per 4-vector z-block
 ATTN_WS_PER_KVH = 16 * 64 * 130
 ATTN_CNT_PER_KVH = 16
+# Bytes of the following projections' weights (o, then the start of gate/up)
+# that decode attention prefetches into L2 while its key loop runs: the loop
+# reads a few MB of K/V, so HBM would otherwise idle for its ~10 us.
+DECODE_L2_PREFETCH = int(os.environ.get("SC_DECODE_L2_PREFETCH", str(64 << 20)))
+BATCH_L2_PREFETCH = int(os.environ.get("SC_BATCH_L2_PREFETCH", str(96 << 20)))
 
 
 class _Workspace:
@@ -634,7 +640,8 @@ class B200Engine:
             ext.attention_decode(b["q"][:M], slot.k(layer), slot.v(layer), pos[0:1], H, self.scale, splits,
                                  b["attn"][:M], page_table=view, page_shift=0,
                                  n_virtual=pos[2:3] if view is not None else None, ws=b["attn_ws"],
-                                 counters=b["attn_cnt"])
+                                 counters=b["attn_cnt"], l2_prefetch=[lw.w_o, lw.w_gu],
+                                 l2_prefetch_bytes=DECODE_L2_PREFETCH)
             ext.gemv_residual(b["attn"][:M], lw.w_o, None, cfg.rms_eps, h, h)
             ext.gemv_swiglu(h, lw.w_gu, lw.ln2, cfg.rms_eps, b["act"][:M])
             ext.gemv_residual(b["act"][:M], lw.w_down, None, cfg.rms_eps, h, h)
@@ -777,7 +784,8 @@ class B200Engine:
             ext.skinny_qkv(x, lw.w_qkv, bb["q"][:B], slots[0].k(layer), slots[0].v(layer), pos_rows, self.rope,
                            cfg.n_heads, cfg.n_kv_heads, ws, pos_rows=pos_rows, seq_stride=stride)
             ext.attention_decode(bb["q"][:B], slots[0].k(layer), slots[0].v(layer), pos_rows, cfg.n_heads,
-                                 self.scale, splits, bb["attn"][:B], pos_rows=pos_rows, seq_stride=stride)
+                                 self.scale, splits, bb["attn"][:B], pos_rows=pos_rows, seq_stride=stride,
+                                 l2_prefetch=[lw.w_o, lw.w_gu], l2_prefetch_bytes=BATCH_L2_PREFETCH)
             ext.skinny_gemm(bb["attn"][:B], lw.w_o, 1, h, h, ws)
             ext.rmsnorm(h, None, lw.ln2, cfg.rms_eps, x)
             ext.skinny_gemm(x, lw.w_gu, 2, bb["act"][:B], None, ws)

@@ -109,6 +109,10 @@ __global__ void __launch_bounds__(kThreads)
   const int page_mask = (1 << a.page_shift) - 1;
   pdl_wait();  // q and the new rows come from the QKV kernel right before
   pdl_launch_dependents();
+  if (warp == kWarps - 1 && (a.pf_bytes[0] > 0 || a.pf_bytes[1] > 0)) {
+    const int cta = ((int)blockIdx.z * (int)gridDim.y + (int)blockIdx.y) * (int)gridDim.x + (int)blockIdx.x;
+    prefetch_l2_share(a.pf_ptr, a.pf_bytes, 2, cta, (int)(gridDim.x * gridDim.y * gridDim.z), lane);
+  }
   const int n_keys = a.pos_rows != nullptr ? a.pos_rows[seq] + 1 : (a.n_virtual != nullptr ? *a.n_virtual : *a.pos + a.M);
   const int pos0 = n_keys - a.M;
   const int k_begin = blockIdx.x * chunk;

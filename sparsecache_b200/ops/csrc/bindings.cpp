@@ -721,7 +721,7 @@ void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int6
                       double scale, int64_t splits, Tensor out, c10::optional<Tensor> page_table,
                       int64_t page_shift, c10::optional<Tensor> n_virtual, c10::optional<Tensor> ws,
                       c10::optional<Tensor> counters, int64_t outer, c10::optional<Tensor> pos_rows,
-                      int64_t seq_stride) {
+                      int64_t seq_stride, std::vector<Tensor> l2_prefetch, int64_t l2_prefetch_bytes) {
   const c10::cuda::CUDAGuard guard(q.device());
   CHECK_BF16(q); CHECK_BF16(out); CHECK_I32(pos);
   TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(2) == 128 && k_cache.is_contiguous(), "k_cache");
@@ -765,6 +765,21 @@ void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int6
     a.seq_stride = seq_stride;
     a.n_seq = (int)pos_rows->numel();
     a.M = 1;
+  }
+  // L2 prefetch: the listed tensors in order, the first fully, the rest while
+  // the byte budget lasts (whole 16-byte units)
+  TORCH_CHECK(l2_prefetch.size() <= 2, "at most two l2_prefetch tensors");
+  TORCH_CHECK(l2_prefetch_bytes >= 0, "l2_prefetch_bytes");
+  long long left = l2_prefetch_bytes;
+  for (size_t i = 0; i < l2_prefetch.size(); ++i) {
+    const Tensor& t = l2_prefetch[i];
+    TORCH_CHECK(t.is_cuda() && t.device() == q.device() && t.is_contiguous(), "l2_prefetch: contiguous tensors on q's device");
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, "l2_prefetch: 16-byte aligned base");
+    const long long nb = (long long)(t.numel() * t.element_size()) & ~15LL;
+    const long long take = std::min(nb, left);
+    a.pf_ptr[i] = t.data_ptr();
+    a.pf_bytes[i] = take;
+    left -= take;
   }
   check_cuda(sc::attention_decode(a, cur_stream()), "attention_decode");
 }
@@ -1342,7 +1357,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("pos"), py::arg("n_heads"), py::arg("scale"), py::arg("splits"), py::arg("out"),
         py::arg("page_table") = py::none(), py::arg("page_shift") = 6, py::arg("n_virtual") = py::none(),
         py::arg("ws") = py::none(), py::arg("counters") = py::none(), py::arg("outer") = 0,
-        py::arg("pos_rows") = py::none(), py::arg("seq_stride") = 0);
+        py::arg("pos_rows") = py::none(), py::arg("seq_stride") = 0,
+        py::arg("l2_prefetch") = std::vector<Tensor>{}, py::arg("l2_prefetch_bytes") = 0);
   m.def("attention_decode_outer", [](int64_t cap, int64_t kvh, int64_t cluster, int64_t sms) {
     return sc::attention_decode_outer((int)cap, (int)kvh, (int)cluster, (int)sms);
   });

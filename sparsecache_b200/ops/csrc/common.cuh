@@ -152,6 +152,34 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x
                : "memory");
 }
 
+// Untiled bulk prefetch of [p, p + bytes) into L2 (the copy engine of the
+// SM fetches it in the background; nothing waits on it).  p and bytes must be
+// multiples of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes)
+               : "memory");
+}
+
+// Spread the L2 prefetch of up to two byte ranges over every CTA of a grid:
+// CTA b takes the b-th of n_cta equal 16-byte-aligned shares of each range
+// and the 32 lanes of the calling warp issue it in 32 KB pieces.
+__device__ __forceinline__ void prefetch_l2_share(const void* const* ptr, const long long* bytes, int n_ranges,
+                                                  int cta, int n_cta, int lane) {
+  constexpr long long kPiece = 32 << 10;
+  for (int r = 0; r < n_ranges; ++r) {
+    const long long total = bytes[r];
+    if (ptr[r] == nullptr || total <= 0) continue;
+    const long long share = ((total + n_cta - 1) / n_cta + 15) & ~15LL;
+    const long long beg = (long long)cta * share;
+    const long long end = beg + share < total ? beg + share : total;
+    const char* base = static_cast<const char*>(ptr[r]);
+    for (long long off = beg + (long long)lane * kPiece; off < end; off += 32 * kPiece) {
+      const long long n = end - off < kPiece ? end - off : kPiece;
+      prefetch_l2_bulk(base + off, (unsigned)n);
+    }
+  }
+}
+
 // 3D box: coordinates (x innermost, y, z).
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map,
                                             uint64_t* bar, int x, int y, int z) {

@@ -253,6 +253,13 @@ struct AttnDecodeArgs {
   const int* pos_rows;
   long long seq_stride;
   int n_seq;
+  // Optional L2 prefetch of the next kernels' weights (bytes multiples of 16,
+  // 16-byte-aligned bases): the key loop leaves HBM mostly idle, so the
+  // o-projection and the start of the gate/up weights can stream into L2
+  // while it runs.  Issued after the wait on the predecessor, spread over all
+  // CTAs; a hint only, nothing waits on it.
+  const void* pf_ptr[2];
+  long long pf_bytes[2];
 };
 
 cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream);

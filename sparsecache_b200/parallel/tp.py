@@ -54,7 +54,8 @@ import torch.distributed as dist
 
 from .. import ops
 from ..config import ModelConfig
-from ..models.engine import B200Engine, EngineWeights, KVSlot, LayerWeights
+from ..models.engine import (BATCH_L2_PREFETCH, DECODE_L2_PREFETCH, B200Engine, EngineWeights, KVSlot,
+                             LayerWeights)
 from ..models.weights import GATE_UP_BLOCK
 
 FLAG_X, FLAG_X2, FLAG_RS_O, FLAG_RS_D = 0, 1, 2, 3
@@ -508,7 +509,8 @@ class TPEngine:
             ext.gemv_qkv(h, lw.w_qkv, lw.ln1, cfg.rms_eps, b["q"][:M], slot.k(layer), slot.v(layer), pos[0:1],
                          eng.rope, lc.n_heads, lc.n_kv_heads, slot=pos[1:2])
             ext.attention_decode(b["q"][:M], slot.k(layer), slot.v(layer), pos[0:1], lc.n_heads, eng.scale, splits,
-                                 b["attn"][:M], ws=b["attn_ws"], counters=b["attn_cnt"])
+                                 b["attn"][:M], ws=b["attn_ws"], counters=b["attn_cnt"],
+                                 l2_prefetch=[lw.w_o, lw.w_gu], l2_prefetch_bytes=DECODE_L2_PREFETCH)
             self.allreduce(b["attn"][:M], lw.w_o, 2 * layer + 1, h)
             ext.gemv_swiglu(h, lw.w_gu, lw.ln2, cfg.rms_eps, b["act"][:M])
             self.allreduce(b["act"][:M], lw.w_down, 2 * layer + 2, h)
@@ -727,7 +729,8 @@ class TPEngine:
                            lc.n_heads, lc.n_kv_heads, ws, pos_rows=pos_rows, seq_stride=stride)
             # every sequence in one launch: row b reads its own slot (stride apart) at pos_rows[b]
             ext.attention_decode(bb["q"][:B], slots[0].k(layer), slots[0].v(layer), pos_rows, lc.n_heads, eng.scale,
-                                 splits, bb["attn"][:B], pos_rows=pos_rows, seq_stride=stride)
+                                 splits, bb["attn"][:B], pos_rows=pos_rows, seq_stride=stride,
+                                 l2_prefetch=[lw.w_o, lw.w_gu], l2_prefetch_bytes=BATCH_L2_PREFETCH)
             self.allreduce(bb["attn"][:B], lw.w_o, 2 * layer + 1, h, skinny=True)
             ext.rmsnorm(h, None, lw.ln2, cfg.rms_eps, x)
             ext.skinny_gemm(x, lw.w_gu, 2, bb["act"][:B], None, ws)

@@ -154,17 +154,17 @@ def main() -> None:
                 a = torch.randn(M, K, device=dev).to(bf)
                 w = (torch.randn(N, K, device=dev) * 0.02).to(bf)
                 o = torch.empty(M, N // 2 if kind == "swiglu" else N, device=dev, dtype=bf)
-                for rows in (128, 256, 0):
+                for rows, bn in ((128, 128), (128, 256), (256, 256), (0, 256)):
                     ext.set_gemm_rows_per_tile(rows)
                     if kind == "store":
-                        fn = lambda: ext.gemm_store(a, w, o, 256, -1)  # noqa: E731
+                        fn = lambda: ext.gemm_store(a, w, o, bn, -1)  # noqa: E731
                     elif kind == "residual":
-                        fn = lambda: ext.gemm_residual(a, w, o, o, 256, -1)  # noqa: E731
+                        fn = lambda: ext.gemm_residual(a, w, o, o, bn, -1)  # noqa: E731
                     else:
-                        fn = lambda: ext.gemm_swiglu(a, w, o, 256)  # noqa: E731
+                        fn = lambda: ext.gemm_swiglu(a, w, o, bn)  # noqa: E731
                     t = timeit(fn, n=20)
                     tf = 2 * M * N * K / (t * 1e-6) / 1e12
-                    res[f"gemm_M{M}_{name}_rows{rows or 'auto'}"] = {
+                    res[f"gemm_M{M}_{name}_rows{rows or 'auto'}_bn{bn}"] = {
                         "us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS}
                 ext.set_gemm_rows_per_tile(0)
                 del a, w, o
