@@ -172,10 +172,15 @@ class PushTarget:
 ATTN_WS_PER_KVH = 16 * 64 * 130
 ATTN_CNT_PER_KVH = 16
 # Bytes of the following projections' weights (o, then the start of gate/up)
-# that decode attention prefetches into L2 while its key loop runs: the loop
-# reads a few MB of K/V, so HBM would otherwise idle for its ~10 us.
-DECODE_L2_PREFETCH = int(os.environ.get("SC_DECODE_L2_PREFETCH", str(64 << 20)))
-BATCH_L2_PREFETCH = int(os.environ.get("SC_BATCH_L2_PREFETCH", str(96 << 20)))
+# that decode attention may prefetch into L2 while its key loop runs (the loop
+# reads a few MB of K/V and leaves HBM mostly idle).  Off by default: with
+# 64 MB the 8B greedy step measured slower (3.28 vs 3.19 ms per token).
+DECODE_L2_PREFETCH = int(os.environ.get("SC_DECODE_L2_PREFETCH", "0"))
+BATCH_L2_PREFETCH = int(os.environ.get("SC_BATCH_L2_PREFETCH", "0"))
+# Row counts run on the token-column GEMM (weights as the MMA's M, tokens as
+# its N): CacheBlend's active rows.  SC_WIDE_GEMM=0 keeps them on row tiles.
+WIDE_ROWS = (65, 512)
+USE_WIDE_GEMM = os.environ.get("SC_WIDE_GEMM", "1") != "0"
 
 
 class _Workspace:
@@ -198,10 +203,11 @@ class _CountingExt:
     """Proxy over the extension that counts kernel launches issued from the host."""
 
     _NOT_KERNELS = {"status", "num_sms", "gemv_argmax_grid", "attention_decode_cluster", "attention_decode_outer",
-                    "skinny_splits", "attention_prefill_splits",
+                    "skinny_splits", "attention_prefill_splits", "wide_plan",
                     "shared_empty",
                     "shared_open", "shared_close"}
-    _MULTI = {"gemm_store", "gemm_residual", "skinny_gemm", "skinny_qkv", "skinny_allreduce", "attention_prefill"}
+    _MULTI = {"gemm_store", "gemm_residual", "skinny_gemm", "skinny_qkv", "skinny_allreduce", "attention_prefill",
+              "wide_swiglu", "wide_residual", "wide_qkv"}
 
     def __init__(self, ext) -> None:
         self._ext = ext
@@ -288,13 +294,28 @@ class B200Engine:
         ext.attention_prefill(q, q_rows, qpos, slot.k(layer), slot.v(layer), kpos, n_keys, cfg.n_heads, self.scale, attn,
                               ws=split_ws)
         x = self.ws.get("x", (n_rows, cfg.d_model), torch.bfloat16)
-        ext.gemm_residual(attn, lw.w_o, h, h, self.bn, norm_w=lw.ln2, eps=cfg.rms_eps, norm_out=x)
         act = self.ws.get("act", (n_rows, cfg.ffn), torch.bfloat16)
+        if self._wide(n_rows):
+            ext.wide_residual(attn, lw.w_o, h, h, norm_w=lw.ln2, eps=cfg.rms_eps, norm_out=x)
+            ext.wide_swiglu(x, lw.w_gu, act)
+            if next_norm is None:
+                ext.wide_residual(act, lw.w_down, h, h)
+            else:
+                ext.wide_residual(act, lw.w_down, h, h, norm_w=next_norm, eps=cfg.rms_eps, norm_out=x)
+            return
+        ext.gemm_residual(attn, lw.w_o, h, h, self.bn, norm_w=lw.ln2, eps=cfg.rms_eps, norm_out=x)
         ext.gemm_swiglu(x, lw.w_gu, act, self.bn)
         if next_norm is None:
             ext.gemm_residual(act, lw.w_down, h, h, self.bn)
         else:
             ext.gemm_residual(act, lw.w_down, h, h, self.bn, norm_w=next_norm, eps=cfg.rms_eps, norm_out=x)
+
+    def _wide(self, rows: int) -> bool:
+        """Whether ``rows`` token rows run on the token-column GEMM (every projection of the
+        layer must tile: 128-row weight tiles, 256-row gate/up blocks, 64-deep k-blocks)."""
+        cfg = self.cfg
+        return (USE_WIDE_GEMM and WIDE_ROWS[0] <= rows <= WIDE_ROWS[1] and cfg.d_model % 128 == 0
+                and cfg.ffn % 128 == 0 and cfg.d_model % 64 == 0 and cfg.q_size % 64 == 0 and cfg.d_model <= 8192)
 
     def _qkv_bn(self, rows: int) -> int:
         """128-column tiles when 256-column tiles would leave SMs idle (small M)."""
@@ -320,6 +341,10 @@ class B200Engine:
         if not x_ready:  # else the previous layer's down_proj left RMSNorm(h) in x
             ext.rmsnorm(h, None, lw.ln1, cfg.rms_eps, x)
         q = self.ws.get("q", (n, cfg.q_size), torch.bfloat16)
+        if dev_part is None and push is None and self._wide(n):
+            ext.wide_qkv(x, lw.w_qkv, q, slot.k(layer), slot.v(layer), pos, slots, self.rope, cfg.n_heads,
+                         cfg.n_kv_heads)
+            return q
         ext.gemm_qkv(x, lw.w_qkv, q, slot.k(layer), slot.v(layer), pos, slots, self.rope,
                      cfg.n_heads, cfg.n_kv_heads, dev_part, dev_mode, self._qkv_bn(n),
                      push.k(layer) if push else 0, push.v(layer) if push else 0)

@@ -21,7 +21,7 @@
 // the kv head: the 128 rows of the tcgen05 tile are (query head g, position
 // i) pairs, so every K/V tile is loaded once for the whole GQA group (a
 // kv-head-major packing; K/V traffic from L2 drops by G against one CTA per
-// query head).  320 threads:
+// query head).  192 threads:
 //   warp 0     TMA producer: K and V tiles of 128 keys (two 128-byte-swizzled
 //              boxes of 64 dims each) into a 2-deep ring; rows past n_keys
 //              are zero-filled by the tensor map, never read from the cache.
@@ -32,23 +32,16 @@
 //              MN-major B operand straight from its [keys][dims] tile.  QK of
 //              tile j+1 is issued before PV of tile j, so the tensor core
 //              works on the next scores while the softmax of this tile runs.
-//   warps 2-9  softmax + epilogue, two threads per tile row (its TMEM lane):
-//              warps 2-5 own the row's columns 0-63 of S, P and O, warps 6-9
-//              columns 64-127.  Each tcgen05.ld's its 64 scores, masks by
-//              nvis, takes its partial max and swaps it with the other half
-//              through shared memory (bounded mbarrier waits), so both take
-//              the same online-softmax decisions in exp2 space; each writes
-//              its 64 keys of P_j as bf16 (one K-major smem k-block) and
-//              arrives.  The running max is rescaled lazily: O in TMEM is
-//              rescaled (tcgen05.ld/st, each half its columns) only when a row
-//              max grows by more than 2^8, so P stays <= 256 and most tiles
-//              touch O not at all.  The epilogue swaps the partial row sums,
-//              reads its half of O once, divides and stores bf16.  Splitting
-//              the row halves the serial softmax work per tile, which (one
-//              thread per row) was longer than the tile's 1024 tensor cycles.
+//   warps 2-5  softmax + epilogue, one tile row per thread (its TMEM lane):
+//              tcgen05.ld the 128 scores, mask by nvis, online softmax in
+//              exp2 space, P_j as bf16 into the swizzled K-major smem tile,
+//              then one arrive.  The running max is rescaled lazily: O in
+//              TMEM is rescaled (tcgen05.ld/st) only when a row max grows by
+//              more than 2^8, so P stays <= 256 and most tiles touch O not at
+//              all.  The epilogue reads O once, divides by the row sum and
+//              stores bf16.
 // TMEM: S[0] cols 0-127, S[1] cols 128-255, O cols 256-383 (512 allocated).
-// Shared memory: Q 32 KB + 2 x (K 32 KB + V 32 KB) + 2 x P 32 KB = 224 KB,
-// + 1 KB for the row exchange.
+// Shared memory: Q 32 KB + 2 x (K 32 KB + V 32 KB) + 2 x P 32 KB = 224 KB.
 // Every wait is bounded; an expired wait records a status code and the CTA
 // winds down (TMA loads in flight are drained, TMEM is freed).  No cluster,
 // no multicast: safe inside multi-GPU programs.
@@ -63,7 +56,7 @@ constexpr int kD = 128;
 constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kStages = 2;
-constexpr int kThreads = 320;  // TMA warp, MMA warp, 8 softmax warps (two per row)
+constexpr int kThreads = 192;
 constexpr float kRescaleLog2 = 8.0f;
 
 constexpr int kQBytes = kBM * kD * 2;      // two 16 KB k-blocks (dims 0-63, 64-127)
@@ -74,8 +67,7 @@ constexpr int kPBlock = kBM * 128;
 constexpr int kOffK = kQBytes;
 constexpr int kOffV = kOffK + kStages * kKVBytes;
 constexpr int kOffP = kOffV + kStages * kKVBytes;
-constexpr int kOffX = kOffP + 2 * kPBytes;        // row-max / row-sum exchange [2 halves][128 rows] fp32
-constexpr int kOffBars = kOffX + 2 * kBM * 4;
+constexpr int kOffBars = kOffP + 2 * kPBytes;
 
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemO = 256;
@@ -90,8 +82,6 @@ struct alignas(8) AttnBars {
   uint64_t o_done;
   uint64_t o_final;
   uint64_t drain;
-  uint64_t x_put;   // both softmax halves wrote their partial row maxima
-  uint64_t x_took;  // both halves read them (the buffer may be written again)
   uint32_t tmem_base;
   int max_vis;
 };
@@ -161,10 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->s_full[b], 1);
-      mbar_init(&bars->p_full[b], 256);
+      mbar_init(&bars->p_full[b], 128);
     }
-    mbar_init(&bars->x_put, 256);
-    mbar_init(&bars->x_took, 256);
     mbar_init(&bars->o_done, 1);
     mbar_init(&bars->o_final, 1);
     mbar_init(&bars->drain, 1);
@@ -182,8 +170,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // kvh * G + row / span, position r0 + row % span)
   const int quarter = warp & 3;  // TMEM lane quarter this warp may access
   const int row = quarter * 32 + lane;
-  // softmax warps 2-5 take S / P / O columns 0-63 of their rows, warps 6-9 columns 64-127
-  const int half = warp >= 6 ? 1 : 0;
   const int head = kvh * G + row / span;
   const int g = r0 + row % span;  // query row index of this tile row
   int nvis = 0;
@@ -195,11 +181,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int src = p.q_rows ? p.q_rows[g] : g;
       const uint4* qsrc = reinterpret_cast<const uint4*>(p.q + (size_t)src * p.ldq + (size_t)head * kD);
 #pragma unroll
-      for (int c = half * 8; c < half * 8 + 8; ++c)
+      for (int c = 0; c < 16; ++c)
         *reinterpret_cast<uint4*>(sq + (c >> 3) * (kBM * 128) + sw128(row, c & 7)) = qsrc[c];
     } else {
 #pragma unroll
-      for (int c = half * 8; c < half * 8 + 8; ++c)
+      for (int c = 0; c < 16; ++c)
         *reinterpret_cast<uint4*>(sq + (c >> 3) * (kBM * 128) + sw128(row, c & 7)) = make_uint4(0, 0, 0, 0);
     }
     if (qp >= 0) {
@@ -318,26 +304,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(&bars->o_final);
     }
   } else {
-    // ---------------- softmax (warps 2-9: two threads per tile row) ----------------
-    // thread (half, row) owns S / P / O columns [64 half, 64 half + 64) of its
-    // row; the two halves swap partial row maxima (and at the end row sums)
-    // through shared memory, so both take the same rescale decisions
+    // ---------------- softmax (warps 2-5: one tile row per thread) ----------------
     const float c = p.scale * 1.4426950408889634f;
     const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
-    const int col0 = half * (kBN / 2);
-    float* xbuf = reinterpret_cast<float*>(smem + kOffX);  // [2 halves][128 rows]
     float m_ref = -INFINITY;
-    float l = 0.f;  // this half's share of the row sum
+    float l = 0.f;
     bool ok = true;
-    // bounded exchange of one value with the other half of the row (phase = exchange count parity)
-    auto exchange = [&](float mine, uint32_t ph, float& other) -> bool {
-      xbuf[half * kBM + row] = mine;
-      mbar_arrive(&bars->x_put);
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars->x_put, ph, status, kStatusTimeoutTmemFull))) return false;
-      other = xbuf[(1 - half) * kBM + row];
-      mbar_arrive(&bars->x_took);
-      return __all_sync(0xffffffffu, mbar_wait(&bars->x_took, ph, status, kStatusTimeoutTmemFull));
-    };
     for (int j = 0; j < n_tiles; ++j) {
       const int b = j & 1;
       // exits stay warp-uniform: the tcgen05 loads below are warp-collective
@@ -348,34 +320,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (warp == 2 && lane == 0) trace_at(p, j, 5);
       tc_fence_after();
-      uint32_t sv[kBN / 2];
+      uint32_t sv[kBN];
 #pragma unroll
-      for (int q4 = 0; q4 < kBN / 64; ++q4)
-        tmem_ld_32x32b_x32(lane_base + b * kBN + col0 + q4 * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[q4 * 32]));
+      for (int q4 = 0; q4 < kBN / 32; ++q4)
+        tmem_ld_32x32b_x32(lane_base + b * kBN + q4 * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[q4 * 32]));
       tmem_ld_wait();
       if (warp == 2 && lane == 0) trace_at(p, j, 6);
-      const int vis = nvis - (t0 + j) * kBN - col0;  // my columns [0, vis) are visible to my row
-      if (!__all_sync(0xffffffffu, vis >= kBN / 2)) {
+      const int vis = nvis - (t0 + j) * kBN;  // keys [0, vis) of this tile are visible to my row
+      if (!__all_sync(0xffffffffu, vis >= kBN)) {
 #pragma unroll
-        for (int i = 0; i < kBN / 2; ++i)
+        for (int i = 0; i < kBN; ++i)
           if (i >= vis) sv[i] = 0xff800000u;  // -inf
       }
       float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < kBN / 2; i += 4) {
+      for (int i = 0; i < kBN; i += 4) {
         mx0 = fmaxf(mx0, __uint_as_float(sv[i]));
         mx1 = fmaxf(mx1, __uint_as_float(sv[i + 1]));
         mx2 = fmaxf(mx2, __uint_as_float(sv[i + 2]));
         mx3 = fmaxf(mx3, __uint_as_float(sv[i + 3]));
       }
-      const float m_half = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-      float m_other;
-      if (!exchange(m_half, (uint32_t)j & 1u, m_other)) {
-        ok = false;
-        break;
-      }
       if (warp == 2 && lane == 0) trace_at(p, j, 7);
-      const float m_tile = fmaxf(m_half, m_other) * c;  // identical in both halves
+      const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;
       const bool need = m_tile > m_ref + kRescaleLog2;  // false when the tile is fully masked
       float f = 1.f;
       if (need) {
@@ -383,9 +349,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_ref = m_tile;
         l *= f;
       }
-      // O holds P_0..P_{j-1} V: rescale this half's columns (warp-uniformly,
-      // tcgen05 ld/st are warp-collective) once PV(j-1) has completed.
-      // s_full(j) implies PV(j-2) completed, so o_done's phase j-1 is unambiguous.
+      // O holds P_0..P_{j-1} V: rescale it (warp-uniformly, tcgen05 ld/st are
+      // warp-collective) once PV(j-1) has completed.  s_full(j) implies PV(j-2)
+      // completed, so waiting on o_done's phase j-1 is unambiguous.
       if (j > 0 && __any_sync(0xffffffffu, need)) {
         const bool done = mbar_wait(&bars->o_done, (uint32_t)(j - 1) & 1u, status, kStatusTimeoutTmemFull);
         if (!__all_sync(0xffffffffu, done)) {
@@ -394,9 +360,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
 #pragma unroll 1
-        for (int cc = 0; cc < kD / 64; ++cc) {
+        for (int cc = 0; cc < kD / 32; ++cc) {
           uint32_t o[32];
-          const uint32_t at = lane_base + kTmemO + col0 + cc * 32;
+          const uint32_t at = lane_base + kTmemO + cc * 32;
           tmem_ld_32x32b_x32(at, o);
           tmem_ld_wait();
           uint32_t lo[16], hi[16];
@@ -412,15 +378,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float base = (m_ref == -INFINITY) ? 0.f : m_ref;
       float sum0 = 0.f, sum1 = 0.f;
-      uint8_t* sp = smem + kOffP + b * kPBytes + half * kPBlock;  // my 64 keys = one P k-block
+      uint8_t* sp = smem + kOffP + b * kPBytes;
 #pragma unroll
-      for (int cc = 0; cc < kBN / 16; ++cc) {  // 8 keys = one 16-byte chunk of the P row
+      for (int cc = 0; cc < kBN / 8; ++cc) {  // 8 keys = one 16-byte chunk of the P row
         float e[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) e[i] = exp2_approx(fmaf(__uint_as_float(sv[8 * cc + i]), c, -base));
         sum0 += (e[0] + e[1]) + (e[2] + e[3]);
         sum1 += (e[4] + e[5]) + (e[6] + e[7]);
-        *reinterpret_cast<uint4*>(sp + sw128(row, cc)) =
+        *reinterpret_cast<uint4*>(sp + (cc >> 3) * kPBlock + sw128(row, cc & 7)) =
             make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
                        pack_bf16x2(e[6], e[7]));
       }
@@ -431,13 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&bars->p_full[b]);
       if (warp == 2 && lane == 0) trace_at(p, j, 9);
     }
-    // ---- epilogue: O / l -> bf16 (or the fp32 partial of a key split), this half's 64 dims ----
+    // ---- epilogue: O / l -> bf16 (or the fp32 partial of a key split) ----
     if (n_tiles > 0 && ok) ok = mbar_wait(&bars->o_final, 0, status, kStatusTimeoutTmemFull);
-    if (n_tiles > 0 && __all_sync(0xffffffffu, ok)) {
-      float l_other = 0.f;
-      ok = exchange(l, (uint32_t)n_tiles & 1u, l_other);
-      l = l + l_other;  // the full row sum (the same in both halves: addition commutes)
-    }
     if (warp == 2 && lane == 0) trace_at(p, 63, 2);
     __nv_bfloat16* dst = p.out + (size_t)g * p.ldo + (size_t)head * kD;
     if (gridDim.z > 1) {
@@ -447,14 +408,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool have = n_tiles > 0 && __all_sync(0xffffffffu, ok);
       if (have) tc_fence_after();
 #pragma unroll 1
-      for (int cc = 0; cc < kD / 64; ++cc) {
+      for (int cc = 0; cc < kD / 32; ++cc) {
         uint32_t o[32];
         if (have) {
-          tmem_ld_32x32b_x32(lane_base + kTmemO + col0 + cc * 32, o);
+          tmem_ld_32x32b_x32(lane_base + kTmemO + cc * 32, o);
           tmem_ld_wait();
         }
         if (g < p.n_rows) {
-          float4* d4 = reinterpret_cast<float4*>(part + col0 + cc * 32);
+          float4* d4 = reinterpret_cast<float4*>(part + cc * 32);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
             d4[i] = have ? make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
@@ -462,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
-      if (g < p.n_rows && half == 0) {
+      if (g < p.n_rows) {
         part[128] = have ? m_ref : -INFINITY;
         part[129] = have ? l : 0.f;
       }
@@ -470,12 +431,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
-      for (int cc = 0; cc < kD / 64; ++cc) {
+      for (int cc = 0; cc < kD / 32; ++cc) {
         uint32_t o[32];
-        tmem_ld_32x32b_x32(lane_base + kTmemO + col0 + cc * 32, o);
+        tmem_ld_32x32b_x32(lane_base + kTmemO + cc * 32, o);
         tmem_ld_wait();
         if (g < p.n_rows) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + col0 + cc * 32);
+          uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 32);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
             d4[i] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * i]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
@@ -485,9 +446,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     } else if (g < p.n_rows && n_tiles == 0) {
-      uint4* d4 = reinterpret_cast<uint4*>(dst + col0);
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) d4[i] = make_uint4(0, 0, 0, 0);
+      for (int i = 0; i < 16; ++i) d4[i] = make_uint4(0, 0, 0, 0);
     }
   }
 

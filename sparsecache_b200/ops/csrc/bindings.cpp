@@ -1030,6 +1030,132 @@ int64_t skinny_allreduce(Tensor x, Tensor w, std::vector<int64_t> dst_ptrs, std:
   return 2;
 }
 
+// ------------------------------------------- token-column GEMM (64 < M <= 512)
+static sc::WideArgs wide_base(const Tensor& x, const Tensor& w, int epi, int64_t acc, int64_t n_tt, int64_t splits) {
+  check_matrix(x, "x");
+  check_matrix(w, "w");
+  TORCH_CHECK(x.size(1) == w.size(1), "K mismatch");
+  sc::WideArgs a{};
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  a.M = (int)x.size(0);
+  a.N = (int)w.size(0);
+  a.K = (int)w.size(1);
+  a.ldx = (int)x.stride(0);
+  a.ldw = (int)w.stride(0);
+  a.epi = epi;
+  a.num_sms = num_sms();
+  a.status = status_tensor(w).data_ptr<int>();
+  TORCH_CHECK(a.M >= 1 && a.M <= 512, "the token-column GEMM takes 1..512 rows");
+  sc::WidePlan p{};
+  TORCH_CHECK(sc::wide_plan(a.M, a.N, a.K, epi, a.num_sms, (int)acc, (int)n_tt, (int)splits, &p),
+              "no token-column GEMM plan for this shape (K % 64, N % 128 or % 256 for SwiGLU)");
+  static_cast<sc::WidePlan&>(a) = p;
+  return a;
+}
+
+static Tensor wide_partials(sc::WideArgs& a, const Tensor& like) {
+  Tensor ws = torch::empty({a.splits, a.M, a.N}, like.options().dtype(torch::kFloat32));
+  a.ws = ws.data_ptr<float>();
+  check_cuda(sc::wide_gemm(a, cur_stream()), "wide_gemm");
+  return ws;
+}
+
+// out = silu(gate) * up for gate/up interleaved in 128-row blocks; one kernel.
+int64_t wide_swiglu(Tensor x, Tensor w_gu, Tensor out) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto a = wide_base(x, w_gu, sc::WIDE_SWIGLU, 2, 0, 1);
+  check_matrix(out, "out");
+  TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) == w_gu.size(0) / 2, "out shape");
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.ldo = (int)out.stride(0);
+  check_cuda(sc::wide_gemm(a, cur_stream()), "wide_swiglu");
+  return 1;
+}
+
+// out = [residual +] bf16(x @ w^T), optionally norm_out = RMSNorm(out) (fused
+// into the reduce); two kernels.
+int64_t wide_residual(Tensor x, Tensor w, Tensor out, c10::optional<Tensor> residual, c10::optional<Tensor> norm_w,
+                      double eps, c10::optional<Tensor> norm_out, int64_t acc, int64_t n_tt, int64_t splits) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto a = wide_base(x, w, sc::WIDE_PARTIAL, acc, n_tt, splits);
+  check_matrix(out, "out");
+  TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) == w.size(0), "out shape");
+  TORCH_CHECK(a.N % 8 == 0, "N % 8");
+  const __nv_bfloat16* res = nullptr;
+  int ldr = 0;
+  if (residual.has_value() && residual->defined()) {
+    check_matrix(*residual, "residual");
+    TORCH_CHECK(residual->sizes() == out.sizes(), "residual shape");
+    res = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    ldr = (int)residual->stride(0);
+  }
+  Tensor ws = wide_partials(a, x);
+  __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  if (norm_w.has_value() && norm_w->defined()) {
+    TORCH_CHECK(res != nullptr, "the fused norm needs the residual epilogue");
+    TORCH_CHECK(norm_out.has_value() && norm_out->defined(), "norm_out required with norm_w");
+    CHECK_BF16(*norm_w); check_matrix(*norm_out, "norm_out");
+    TORCH_CHECK(norm_w->numel() == a.N && norm_out->sizes() == out.sizes() && a.N <= 8192, "norm shapes");
+    check_cuda(sc::splitk_reduce_norm(a.ws, a.splits, a.M, a.N, res, ldr, o, (int)out.stride(0),
+                                      reinterpret_cast<const __nv_bfloat16*>(norm_w->data_ptr()), (float)eps,
+                                      reinterpret_cast<__nv_bfloat16*>(norm_out->data_ptr()), (int)norm_out->stride(0),
+                                      cur_stream()),
+               "splitk_reduce_norm");
+  } else {
+    check_cuda(sc::splitk_reduce(a.ws, a.splits, a.M, a.N, res, ldr, o, (int)out.stride(0), cur_stream()),
+               "splitk_reduce");
+  }
+  return 2;
+}
+
+// Fused QKV rows -> RoPE at rope_pos[m], Q to q_out, K/V to cache slot cache_slot[m]; two kernels.
+int64_t wide_qkv(Tensor x, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_cache, Tensor rope_pos,
+                 Tensor cache_slot, Tensor rope_table, int64_t n_q_heads, int64_t n_kv_heads, int64_t acc,
+                 int64_t n_tt, int64_t splits) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto a = wide_base(x, w_qkv, sc::WIDE_PARTIAL, acc, n_tt, splits);
+  TORCH_CHECK(w_qkv.size(0) == (n_q_heads + 2 * n_kv_heads) * 128, "w_qkv rows");
+  check_matrix(q_out, "q_out");
+  TORCH_CHECK(q_out.size(0) >= x.size(0) && q_out.size(1) == n_q_heads * 128, "q_out shape");
+  TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(0) == n_kv_heads && k_cache.size(2) == 128 &&
+                  k_cache.is_contiguous() && v_cache.sizes() == k_cache.sizes() && v_cache.is_contiguous(),
+              "k_cache / v_cache [n_kv_heads, cap, 128]");
+  CHECK_I32(rope_pos); CHECK_I32(cache_slot); CHECK_F32(rope_table);
+  TORCH_CHECK(rope_pos.numel() >= x.size(0) && cache_slot.numel() >= x.size(0), "positions");
+  Tensor ws = wide_partials(a, x);
+  sc::SkinnyArgs r{};
+  r.M = a.M;
+  r.N = a.N;
+  r.K = a.K;
+  r.epi = sc::SKINNY_QKV;
+  r.ws = a.ws;
+  r.splits = a.splits;
+  r.num_sms = a.num_sms;
+  r.status = a.status;
+  r.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
+  r.ldq = (int)q_out.stride(0);
+  r.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr());
+  r.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
+  r.cache_cap = (int)k_cache.size(1);
+  r.pos_rows = rope_pos.data_ptr<int>();
+  r.slot_rows = cache_slot.data_ptr<int>();
+  r.rope_table = reinterpret_cast<const float2*>(rope_table.data_ptr<float>());
+  r.n_q_heads = (int)n_q_heads;
+  r.n_kv_heads = (int)n_kv_heads;
+  check_cuda(sc::skinny_reduce(r, cur_stream()), "wide_qkv reduce");
+  return 2;
+}
+
+py::tuple wide_plan(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t acc, int64_t n_tt, int64_t splits,
+                    int64_t sms) {
+  sc::WidePlan p{};
+  if (!sc::wide_plan((int)M, (int)N, (int)K, (int)epi, sms > 0 ? (int)sms : num_sms(), (int)acc, (int)n_tt,
+                     (int)splits, &p))
+    return py::make_tuple();
+  return py::make_tuple(p.acc, p.bn, p.n_tt, p.splits, p.stages, p.nbuf, p.tmem_cols, p.smem);
+}
+
 void row_argmax(Tensor logits, Tensor out_token) {
   const c10::cuda::CUDAGuard guard(logits.device());
   check_matrix(logits, "logits");
@@ -1378,6 +1504,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("skinny_gemm", &skinny_gemm, py::arg("x"), py::arg("w"), py::arg("epi"), py::arg("out"),
         py::arg("residual") = py::none(), py::arg("ws"), py::arg("splits") = -1);
   m.def("skinny_splits", &skinny_splits);
+  m.def("wide_swiglu", &wide_swiglu, py::arg("x"), py::arg("w_gu"), py::arg("out"));
+  m.def("wide_residual", &wide_residual, py::arg("x"), py::arg("w"), py::arg("out"), py::arg("residual") = py::none(),
+        py::arg("norm_w") = py::none(), py::arg("eps") = 1e-5, py::arg("norm_out") = py::none(), py::arg("acc") = 0,
+        py::arg("n_tt") = 0, py::arg("splits") = 0);
+  m.def("wide_qkv", &wide_qkv, py::arg("x"), py::arg("w_qkv"), py::arg("q_out"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("rope_pos"), py::arg("cache_slot"), py::arg("rope_table"), py::arg("n_q_heads"),
+        py::arg("n_kv_heads"), py::arg("acc") = 0, py::arg("n_tt") = 0, py::arg("splits") = 0);
+  m.def("wide_plan", &wide_plan, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"), py::arg("acc") = 0,
+        py::arg("n_tt") = 0, py::arg("splits") = 0, py::arg("sms") = 0);
   m.def("skinny_qkv", &skinny_qkv, py::arg("x"), py::arg("w_qkv"), py::arg("q_out"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("pos"), py::arg("rope_table"), py::arg("n_q_heads"), py::arg("n_kv_heads"),
         py::arg("ws"), py::arg("slot") = py::none(), py::arg("pos_rows") = py::none(), py::arg("seq_stride") = 0);

@@ -351,6 +351,9 @@ struct SkinnyArgs {
   // its cache starts seq_stride elements after row m-1's (null: one sequence)
   const int* pos_rows;
   long long seq_stride;
+  // with pos_rows: row m's K/V go to cache slot slot_rows[m] of the one
+  // sequence (CacheBlend's active rows: RoPE position and slot differ)
+  const int* slot_rows;
   // SKINNY_ALLREDUCE: fp32 partial rows to every rank's receive slot
   // ar_dst[r][sender][m][N], then the last CTA releases ar_flag[r] = epoch
   float* ar_dst[8];
@@ -361,6 +364,38 @@ struct SkinnyArgs {
   unsigned int* counter;
 };
 int skinny_splits(int N, int K, int num_sms);
+// The reduce + epilogue half of skinny_gemm alone (a.ws holds the [splits][M][N]
+// partials of another producer, e.g. the token-column GEMM); any M.
+cudaError_t skinny_reduce(const SkinnyArgs& a, cudaStream_t stream);
+
+// Token-column tensor-core GEMM for 64 < M <= 512 token rows (gemm_wide.cu):
+// weight tiles are the MMA's 128-row M, token rows its N (multiple of 16).
+enum WideEpi { WIDE_PARTIAL = 0, WIDE_SWIGLU = 1 };
+struct WidePlan {
+  int acc;        // 128-row weight tiles per unit (1, or 2 = a SwiGLU gate/up block pair)
+  int bn;         // token columns per unit (multiple of 16, <= 256)
+  int n_tt;       // token tiles (n_tt * bn >= M)
+  int splits;     // K slices
+  int stages;     // TMA ring depth
+  int nbuf;       // TMEM accumulator buffers
+  int tmem_cols;  // TMEM allocation (power of two)
+  int smem;       // dynamic shared memory bytes
+};
+struct WideArgs : WidePlan {
+  const __nv_bfloat16* x;  // [M, K] row stride ldx
+  const __nv_bfloat16* w;  // [N, K] row stride ldw
+  int M, N, K, ldx, ldw;
+  int epi;
+  float* ws;               // WIDE_PARTIAL: [splits][M][N] fp32
+  __nv_bfloat16* out;      // WIDE_SWIGLU: [M, N / 2] row stride ldo
+  int ldo;
+  int num_sms;
+  int* status;
+};
+// Cheapest plan for the shape (a *_req of 0 leaves that choice free); false if none fits.
+bool wide_plan(int M, int N, int K, int epi, int num_sms, int acc_req, int n_tt_req, int splits_req,
+               WidePlan* plan);
+cudaError_t wide_gemm(const WideArgs& a, cudaStream_t stream);
 // token-row tile of the skinny GEMM for M rows: 16 (M <= 16), 32 (M <= 32) or 64 (M <= 64)
 int skinny_bn(int M);
 cudaError_t skinny_gemm(const SkinnyArgs& a, cudaStream_t stream);

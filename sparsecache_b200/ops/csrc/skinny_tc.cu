@@ -236,7 +236,10 @@ __global__ void skinny_reduce_kernel(SkinnyArgs a) {
       const float v0 = sum_row(r0), v1 = sum_row(r0 + 64);
       int pos, slot;
       size_t seq_off = 0;
-      if (a.pos_rows != nullptr) {  // batched decode: one sequence per row
+      if (a.pos_rows != nullptr && a.slot_rows != nullptr) {  // one sequence, per-row position and slot
+        pos = a.pos_rows[m];
+        slot = a.slot_rows[m];
+      } else if (a.pos_rows != nullptr) {  // batched decode: one sequence per row
         pos = slot = a.pos_rows[m];
         seq_off = (size_t)m * (size_t)a.seq_stride;
       } else {
@@ -388,10 +391,25 @@ cudaError_t skinny_gemm(const SkinnyArgs& args, cudaStream_t stream) {
       : a.bn == 32 ? cudaLaunchKernelEx(&cfg, skinny_mma_kernel<32>, tw, tx, a.M, a.N, a.K, a.splits, a.ws, a.status)
                    : cudaLaunchKernelEx(&cfg, skinny_mma_kernel<64>, tw, tx, a.M, a.N, a.K, a.splits, a.ws, a.status);
   if (e != cudaSuccess) return e;
+  return skinny_reduce(a, stream);
+}
+
+cudaError_t skinny_reduce(const SkinnyArgs& a, cudaStream_t stream) {
+  if (a.M < 1 || a.splits < 1 || a.ws == nullptr || a.N % 2 != 0) return cudaErrorInvalidValue;
+  if (a.epi == SKINNY_SWIGLU && a.N % 256 != 0) return cudaErrorInvalidValue;
+  if (a.epi == SKINNY_QKV && (a.N % 128 != 0 || a.N != (a.n_q_heads + 2 * a.n_kv_heads) * 128))
+    return cudaErrorInvalidValue;
   const int outs = ((a.epi == SKINNY_SWIGLU || a.epi == SKINNY_QKV) ? a.N / 2 : a.N) * a.M;
+  cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((outs + 255) / 256, 1, 1);
   cfg.blockDim = dim3(256, 1, 1);
   cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, skinny_reduce_kernel, a);
 }
 

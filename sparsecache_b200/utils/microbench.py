@@ -169,6 +169,46 @@ def main() -> None:
                 ext.set_gemm_rows_per_tile(0)
                 del a, w, o
 
+    if "gemm_wide" in only:
+        # token-column GEMM (weights as the MMA's M, tokens as its N) against the row-tile GEMM at
+        # CacheBlend's active-row counts; weights cycled over copies so every call streams them
+        # from HBM (as in a layer loop), inputs of the real shapes
+        for M in (300, 330, 512):
+            for name, N, K, kind in (("qkv", 6144, 4096, "qkv"), ("o", 4096, 4096, "residual"),
+                                     ("gate_up", 28672, 4096, "swiglu"), ("down", 4096, 14336, "residual")):
+                copies = max(1, -(-(256 << 20) // (N * K * 2)))
+                ws_ = [(torch.randn(N, K, device=dev) * 0.02).to(bf) for _ in range(copies)]
+                a = torch.randn(M, K, device=dev).to(bf)
+                o = torch.empty(M, N // 2 if kind == "swiglu" else N, device=dev, dtype=bf)
+                cap, nq, nkv = 2048, 32, 8
+                qo = torch.empty(M, nq * 128, device=dev, dtype=bf)
+                kc = torch.zeros(nkv, cap, 128, device=dev, dtype=bf)
+                vc = torch.zeros(nkv, cap, 128, device=dev, dtype=bf)
+                pos = torch.arange(M, device=dev, dtype=torch.int32) * 5
+                table = torch.zeros(4096, 128, device=dev)
+                it = [0]
+
+                def nxt():
+                    it[0] = (it[0] + 1) % copies
+                    return ws_[it[0]]
+
+                if kind == "qkv":
+                    tc = lambda: ext.gemm_qkv(a, nxt(), qo, kc, vc, pos, pos, table, nq, nkv, None, 0,  # noqa: E731
+                                              128 if -(-M // 128) * (N // 256) < ext.num_sms() else 256, 0, 0)
+                    wd = lambda: ext.wide_qkv(a, nxt(), qo, kc, vc, pos, pos, table, nq, nkv)  # noqa: E731
+                elif kind == "residual":
+                    tc = lambda: ext.gemm_residual(a, nxt(), o, o, 256, -1)  # noqa: E731
+                    wd = lambda: ext.wide_residual(a, nxt(), o, o)  # noqa: E731
+                else:
+                    tc = lambda: ext.gemm_swiglu(a, nxt(), o, 256)  # noqa: E731
+                    wd = lambda: ext.wide_swiglu(a, nxt(), o)  # noqa: E731
+                for arm, fn in (("rowtile", tc), ("tokencol", wd)):
+                    t = timeit(fn, n=20)
+                    tf = 2 * M * N * K / (t * 1e-6) / 1e12
+                    res[f"gemm_M{M}_{name}_{arm}"] = {"us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS}
+                res[f"gemm_M{M}_{name}_tokencol"]["plan"] = list(ext.wide_plan(M, N, K, 1 if kind == "swiglu" else 0))
+                del ws_, a, o
+
     if "attn_decode" in only or "attn_decode_sweep" in only:
         H, Hkv = 32, 8
         for cap in (2048, 18000):
@@ -230,16 +270,16 @@ def main() -> None:
         q = torch.randn(B, H * 128, device=dev).to(bf)
         out = torch.empty(B, H * 128, device=dev, dtype=bf)
         pos_rows = torch.full((B,), 1675, device=dev, dtype=torch.int32)
-        S = int(ext.attention_decode_cluster(cap, Hkv))
-
-        def run_layers():
-            for i in range(layers):
-                ext.attention_decode(q, kbuf[i][:per].view(Hkv, cap, 128), vbuf[i][:per].view(Hkv, cap, 128),
-                                     pos_rows, H, 1 / math.sqrt(128), S, out, pos_rows=pos_rows, seq_stride=per)
-        t = timeit(run_layers, n=10, warm=3) / layers
+        S_auto = int(ext.attention_decode_cluster(cap, Hkv))
         kv_bytes = B * 2 * Hkv * 1676 * 128 * 2
-        res["attn_decode_batch32_keys1676"] = {"us": t, "frac_of_measured_hbm": kv_bytes / (t * 1e-6) / 1e9 / HBM_GBS,
-                                               "cluster": S}
+        for S in sorted({1, 2, 4, 8, S_auto}):
+            def run_layers():
+                for i in range(layers):
+                    ext.attention_decode(q, kbuf[i][:per].view(Hkv, cap, 128), vbuf[i][:per].view(Hkv, cap, 128),
+                                         pos_rows, H, 1 / math.sqrt(128), S, out, pos_rows=pos_rows, seq_stride=per)
+            t = timeit(run_layers, n=10, warm=3) / layers
+            res[f"attn_decode_batch32_keys1676_S{S}"] = {
+                "us": t, "frac_of_measured_hbm": kv_bytes / (t * 1e-6) / 1e9 / HBM_GBS, "cluster": S}
 
     if "attn_decode_grid" in only:
         # cluster size x (one / several clusters per kv head) for the decode shapes that matter

@@ -723,3 +723,87 @@ def test_page_token_scores_match_fp32_softmax(cuda_device, L, R, H, Hkv, T):
     ref /= L
     torch.testing.assert_close(got, ref, rtol=2e-3, atol=1e-6)
     assert abs(float(got.sum()) - 1.0) < 1e-3
+
+
+# ------------------------------------------------ token-column GEMM (64 < M <= 512)
+@pytest.mark.parametrize("M", [65, 130, 300, 512])
+@pytest.mark.parametrize("acc,n_tt,splits", [(1, 0, 1), (2, 0, 3), (1, 3, 2), (0, 0, 0)])
+def test_wide_gemm_store_and_residual(cuda_device, M, acc, n_tt, splits):
+    """Weight tiles as the MMA's M, tokens as its N: every plan (weight tiles per unit, token
+    tiles, K split) matches the fp32 reference, stored and with the residual epilogue."""
+    ext = _ext()
+    N, K = 1024, 1280
+    if n_tt and -(-M // n_tt) > 256:
+        pytest.skip("token tile wider than 256")
+    g = torch.Generator(device="cpu").manual_seed(M * 3 + splits)
+    x = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.03).to(cuda_device, torch.bfloat16)
+    res = torch.randn(M, N, generator=g).to(cuda_device, torch.bfloat16)
+    out = torch.empty(M, N, device=cuda_device, dtype=torch.bfloat16)
+    assert ext.wide_residual(x, w, out, None, acc=acc, n_tt=n_tt, splits=splits) == 2
+    out_r = res.clone()
+    ext.wide_residual(x, w, out_r, out_r, acc=acc, n_tt=n_tt, splits=splits)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    y = x.float() @ w.float().T
+    assert _rel_err(out, y) < 1e-2
+    assert _rel_err(out_r, res.float() + y.to(torch.bfloat16).float()) < 1e-2
+
+
+@pytest.mark.parametrize("M", [100, 300, 330])
+def test_wide_swiglu_and_fused_norm(cuda_device, M):
+    """Gate/up block pairs per unit with the SwiGLU epilogue; residual + RMSNorm through the
+    split-K reduce is bit-identical to the norm kernel on the stored rows."""
+    ext = _ext()
+    K, F = 1024, 2048
+    g = torch.Generator(device="cpu").manual_seed(M)
+    x = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
+    wg = (torch.randn(F, K, generator=g) * 0.05).to(cuda_device, torch.bfloat16)
+    wu = (torch.randn(F, K, generator=g) * 0.05).to(cuda_device, torch.bfloat16)
+    act = torch.empty(M, F, device=cuda_device, dtype=torch.bfloat16)
+    assert ext.wide_swiglu(x, interleave_gate_up(wg, wu), act) == 1
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    gate = (x.float() @ wg.float().T).to(torch.bfloat16)
+    up = (x.float() @ wu.float().T).to(torch.bfloat16)
+    ref = torch.nn.functional.silu(gate.float()).to(torch.bfloat16).float() * up.float()
+    assert _rel_err(act, ref) < 2e-2
+
+    wd = (torch.randn(K, F, generator=g) * 0.02).to(cuda_device, torch.bfloat16)
+    res = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(K, generator=g)).to(cuda_device, torch.bfloat16)
+    h, normed = res.clone(), torch.empty(M, K, device=cuda_device, dtype=torch.bfloat16)
+    ext.wide_residual(act, wd, h, h, norm_w=nw, eps=1e-5, norm_out=normed)
+    ref_norm = torch.empty_like(normed)
+    ext.rmsnorm(h, None, nw, 1e-5, ref_norm)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    assert torch.equal(normed, ref_norm)
+    assert _rel_err(h, res.float() + (act.float() @ wd.float().T).to(torch.bfloat16).float()) < 1e-2
+
+
+@pytest.mark.parametrize("M", [90, 300])
+def test_wide_qkv_rope_scatter(cuda_device, M):
+    """Token-column QKV: RoPE at per-row positions, Q rows out, K/V at per-row cache slots."""
+    cfg = get_model_config("tiny128")
+    nq, nkv, K, cap = 4, 2, 512, 600
+    a = torch.randn(M, K, device=cuda_device).to(torch.bfloat16)
+    w = (torch.randn((nq + 2 * nkv) * 128, K, device=cuda_device) * 0.05).to(torch.bfloat16)
+    pos = torch.sort(torch.randperm(500)[:M]).values.to(torch.int32).to(cuda_device) + 7
+    slot = torch.sort(torch.randperm(cap)[:M]).values.to(torch.int32).to(cuda_device)
+    kc = torch.randn(nkv, cap, 128, device=cuda_device).to(torch.bfloat16)
+    vc = torch.randn(nkv, cap, 128, device=cuda_device).to(torch.bfloat16)
+    kc0 = kc.clone()
+    q_out = torch.empty(M, nq * 128, device=cuda_device, dtype=torch.bfloat16)
+    table = rope_table(cfg, 1024, cuda_device)
+    assert _ext().wide_qkv(a, w, q_out, kc, vc, pos, slot, table, nq, nkv) == 2
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    q, k, v = _qkv_reference(a, w, cfg, pos, nq, nkv)
+    assert _rel_err(q_out.reshape(M, nq, 128), q) < 1e-2
+    sl = slot.long()
+    assert _rel_err(kc[:, sl].transpose(0, 1), k) < 1e-2
+    assert _rel_err(vc[:, sl].transpose(0, 1), v) < 1e-2
+    untouched = torch.ones(cap, dtype=torch.bool, device=cuda_device)
+    untouched[sl] = False
+    assert torch.equal(kc[:, untouched], kc0[:, untouched])
