@@ -126,6 +126,11 @@ def _spec_worker(rank, world, port, out_dir):
         full = EngineWeights.from_oracle(oracle, dev)
         group = TPGroup()
         tpe = TPEngine.from_full(cfg, full, group, max_rows=2048 // world)
+        # the TP layers run the row-tile GEMM at every row count; the single-GPU reference does
+        # the same here so that one rank reproduces its partial sums bit for bit
+        import sparsecache_b200.models.engine as engine_module
+
+        engine_module.USE_WIDE_GEMM = False
         ref = B200Engine(cfg, full, dev, max_positions=8192)
         req = make_requests("tiny_plumbing", cfg)[0]
         T, n_new = req.prompt_tokens, 12
