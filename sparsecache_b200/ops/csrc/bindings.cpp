@@ -5,6 +5,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <map>
+#include <mutex>
+
 #include "kernels.h"
 
 namespace {
@@ -1031,6 +1034,20 @@ int64_t skinny_allreduce(Tensor x, Tensor w, std::vector<int64_t> dst_ptrs, std:
 }
 
 // ------------------------------------------- token-column GEMM (64 < M <= 512)
+// stream-K arrival counters of the token-column GEMM: one zeroed buffer per
+// device, every counter returned to zero by the launch that used it
+static Tensor wide_tickets(const Tensor& like) {
+  static std::mutex lock;
+  static std::map<int, Tensor> bufs;
+  std::lock_guard<std::mutex> guard(lock);
+  const int dev = like.get_device();
+  auto it = bufs.find(dev);
+  if (it == bufs.end()) it = bufs.emplace(dev, torch::zeros({4096}, like.options().dtype(torch::kInt32))).first;
+  return it->second;
+}
+
+static bool g_wide_stream_k = true;
+
 static sc::WideArgs wide_base(const Tensor& x, const Tensor& w, int epi, int64_t acc, int64_t n_tt, int64_t splits) {
   check_matrix(x, "x");
   check_matrix(w, "w");
@@ -1048,15 +1065,27 @@ static sc::WideArgs wide_base(const Tensor& x, const Tensor& w, int epi, int64_t
   a.status = status_tensor(w).data_ptr<int>();
   TORCH_CHECK(a.M >= 1 && a.M <= 512, "the token-column GEMM takes 1..512 rows");
   sc::WidePlan p{};
-  TORCH_CHECK(sc::wide_plan(a.M, a.N, a.K, epi, a.num_sms, (int)acc, (int)n_tt, (int)splits, &p),
+  TORCH_CHECK(sc::wide_plan(a.M, a.N, a.K, epi, a.num_sms, (int)acc, (int)n_tt, (int)splits, g_wide_stream_k, &p),
               "no token-column GEMM plan for this shape (K % 64, N % 128 or % 256 for SwiGLU)");
   static_cast<sc::WidePlan&>(a) = p;
   return a;
 }
 
+// stream-K tail workspace (allocated by the caller's stream-ordered allocator)
+static Tensor wide_stream_k(sc::WideArgs& a, const Tensor& like) {
+  if (a.sk_tail <= 0) return Tensor();
+  TORCH_CHECK(a.sk_tail <= 4096, "too many stream-K tail units");
+  Tensor ws = torch::empty({(int64_t)a.sk_tail * a.sk_max_pieces * a.acc * a.bn * 128},
+                           like.options().dtype(torch::kFloat32));
+  a.sk_ws = ws.data_ptr<float>();
+  a.sk_tickets = reinterpret_cast<unsigned*>(wide_tickets(like).data_ptr<int>());
+  return ws;
+}
+
 static Tensor wide_partials(sc::WideArgs& a, const Tensor& like) {
   Tensor ws = torch::empty({a.splits, a.M, a.N}, like.options().dtype(torch::kFloat32));
   a.ws = ws.data_ptr<float>();
+  Tensor sk = wide_stream_k(a, like);
   check_cuda(sc::wide_gemm(a, cur_stream()), "wide_gemm");
   return ws;
 }
@@ -1069,6 +1098,7 @@ int64_t wide_swiglu(Tensor x, Tensor w_gu, Tensor out) {
   TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) == w_gu.size(0) / 2, "out shape");
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   a.ldo = (int)out.stride(0);
+  Tensor sk = wide_stream_k(a, x);
   check_cuda(sc::wide_gemm(a, cur_stream()), "wide_swiglu");
   return 1;
 }
@@ -1147,14 +1177,21 @@ int64_t wide_qkv(Tensor x, Tensor w_qkv, Tensor q_out, Tensor k_cache, Tensor v_
   return 2;
 }
 
-py::tuple wide_plan(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t acc, int64_t n_tt, int64_t splits,
-                    int64_t sms) {
+py::dict wide_plan(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t acc, int64_t n_tt, int64_t splits,
+                   int64_t sms) {
   sc::WidePlan p{};
+  py::dict d;
   if (!sc::wide_plan((int)M, (int)N, (int)K, (int)epi, sms > 0 ? (int)sms : num_sms(), (int)acc, (int)n_tt,
-                     (int)splits, &p))
-    return py::make_tuple();
-  return py::make_tuple(p.acc, p.bn, p.n_tt, p.splits, p.stages, p.nbuf, p.tmem_cols, p.smem);
+                     (int)splits, g_wide_stream_k, &p))
+    return d;
+  d["acc"] = p.acc; d["bn"] = p.bn; d["n_tt"] = p.n_tt; d["splits"] = p.splits; d["stages"] = p.stages;
+  d["nbuf"] = p.nbuf; d["tmem_cols"] = p.tmem_cols; d["smem"] = p.smem; d["grid"] = p.grid;
+  d["sk_tail"] = p.sk_tail; d["sk_ctas"] = p.sk_ctas; d["sk_max_pieces"] = p.sk_max_pieces;
+  return d;
 }
+
+// experiment switch: stream-K tail of the token-column GEMM on / off
+void set_wide_stream_k(bool on) { g_wide_stream_k = on; }
 
 void row_argmax(Tensor logits, Tensor out_token) {
   const c10::cuda::CUDAGuard guard(logits.device());
@@ -1511,6 +1548,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("wide_qkv", &wide_qkv, py::arg("x"), py::arg("w_qkv"), py::arg("q_out"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("rope_pos"), py::arg("cache_slot"), py::arg("rope_table"), py::arg("n_q_heads"),
         py::arg("n_kv_heads"), py::arg("acc") = 0, py::arg("n_tt") = 0, py::arg("splits") = 0);
+  m.def("set_wide_stream_k", &set_wide_stream_k);
   m.def("wide_plan", &wide_plan, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"), py::arg("acc") = 0,
         py::arg("n_tt") = 0, py::arg("splits") = 0, py::arg("sms") = 0);
   m.def("skinny_qkv", &skinny_qkv, py::arg("x"), py::arg("w_qkv"), py::arg("q_out"), py::arg("k_cache"),

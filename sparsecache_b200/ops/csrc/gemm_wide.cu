@@ -45,6 +45,7 @@ struct alignas(8) WdBars {
   uint64_t tmem_empty[2];
   uint64_t drain;
   uint32_t tmem_base;
+  uint32_t sk_ticket;
 };
 
 __device__ __forceinline__ void wd_tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
@@ -58,20 +59,80 @@ __device__ __forceinline__ void wd_tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) 
       : "memory");
 }
 
-struct WdUnit {
+// One work item of a CTA: a whole unit, or a run of k-blocks of a stream-K
+// tail unit (piece `piece` of `n_pieces`; n_pieces == 1 is a whole unit).
+struct WdItem {
   int g, t, s, kb0, kb1;
+  int tail;      // index among the tail units (-1: data-parallel unit)
+  int piece, n_pieces;
 };
 
-__device__ __forceinline__ WdUnit wd_unit(const WideArgs& a, int u, int num_kb) {
-  WdUnit w;
-  w.t = u % a.n_tt;
+// Walks the items of one CTA in order: its data-parallel units (one per
+// round of the grid), then its run [lo, hi) of the tail's k-block space.
+struct WdIter {
+  int r;
+  long long w, hi;
+  bool tail;
+};
+
+__device__ __forceinline__ void wd_decode(const WideArgs& a, int u, int num_kb, WdItem& it) {
+  it.t = u % a.n_tt;
   const int r = u / a.n_tt;
-  w.s = r % a.splits;
-  w.g = r / a.splits;
-  w.kb0 = w.s * num_kb / a.splits;
-  w.kb1 = (w.s + 1) * num_kb / a.splits;
-  return w;
+  it.s = r % a.splits;
+  it.g = r / a.splits;
+  it.kb0 = it.s * num_kb / a.splits;
+  it.kb1 = (it.s + 1) * num_kb / a.splits;
 }
+
+// CTA whose tail run holds k-block x: the largest c with floor(c * Wt / C) <= x
+__device__ __forceinline__ int wd_sk_owner(long long x, long long Wt, int C) {
+  long long c = ((x + 1) * C + Wt - 1) / Wt - 1;
+  return (int)(c < 0 ? 0 : (c >= C ? C - 1 : c));
+}
+
+__device__ __forceinline__ void wd_begin(const WideArgs& a, int num_kb, WdIter& it) {
+  it.r = 0;
+  it.tail = false;
+  it.w = it.hi = 0;
+  if (a.sk_tail > 0 && (int)blockIdx.x < a.sk_ctas) {
+    const long long Wt = (long long)a.sk_tail * num_kb;
+    it.w = (long long)blockIdx.x * Wt / a.sk_ctas;
+    it.hi = (long long)(blockIdx.x + 1) * Wt / a.sk_ctas;
+  }
+}
+
+__device__ __forceinline__ bool wd_next(const WideArgs& a, int num_kb, int units, WdIter& it, WdItem& out) {
+  const int dp_units = units - a.sk_tail;
+  if (!it.tail) {
+    const int u = (int)blockIdx.x + it.r * (int)gridDim.x;
+    if (u < dp_units) {
+      ++it.r;
+      wd_decode(a, u, num_kb, out);
+      out.tail = -1;
+      out.piece = 0;
+      out.n_pieces = 1;
+      return true;
+    }
+    it.tail = true;
+  }
+  if (it.w >= it.hi) return false;
+  const long long Wt = (long long)a.sk_tail * num_kb;
+  const int tu = (int)(it.w / num_kb);
+  const long long u0 = (long long)tu * num_kb;
+  const int kb0 = (int)(it.w - u0);
+  const int kb1 = (int)((it.hi < u0 + num_kb ? it.hi : u0 + num_kb) - u0);
+  it.w = u0 + kb1;
+  wd_decode(a, dp_units + tu, num_kb, out);
+  out.kb0 = kb0;
+  out.kb1 = kb1;
+  const int first = wd_sk_owner(u0, Wt, a.sk_ctas);
+  out.n_pieces = wd_sk_owner(u0 + num_kb - 1, Wt, a.sk_ctas) - first + 1;
+  out.piece = (int)blockIdx.x - first;
+  out.tail = tu;
+  return true;
+}
+
+__device__ __forceinline__ void wd_epi_barrier() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 }  // namespace
 
 template <int ACC, int EPI>
@@ -118,9 +179,10 @@ __global__ void __launch_bounds__(kWdThreads, 1)
       bool ok = true;
       int pre = 0;  // stages whose weight half was issued before the wait
       {
-        int u = blockIdx.x;
-        if (u < units) {
-          const WdUnit w = wd_unit(a, u, num_kb);
+        WdIter it;
+        WdItem w;
+        wd_begin(a, num_kb, it);
+        if (wd_next(a, num_kb, units, it, w)) {
           for (int kb = w.kb0; kb < w.kb1 && pre < stages; ++kb, ++pre) {
             uint8_t* sa = smem + pre * stage_bytes;
             mbar_arrive_expect_tx(&bars->full[pre], (uint32_t)stage_bytes);
@@ -134,8 +196,10 @@ __global__ void __launch_bounds__(kWdThreads, 1)
       uint32_t issued_phase[kWdMaxStages];
       for (int s = 0; s < kWdMaxStages; ++s) issued[s] = false, issued_phase[s] = 0;
       int done_pre = 0;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const WdUnit w = wd_unit(a, u, num_kb);
+      WdIter it;
+      WdItem w;
+      wd_begin(a, num_kb, it);
+      while (ok && wd_next(a, num_kb, units, it, w)) {
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           uint8_t* sa = smem + stage * stage_bytes;
           if (done_pre < pre) {
@@ -171,8 +235,10 @@ __global__ void __launch_bounds__(kWdThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true, any = false;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
-        const WdUnit w = wd_unit(a, u, num_kb);
+      WdIter it;
+      WdItem w;
+      wd_begin(a, num_kb, it);
+      for (; ok && wd_next(a, num_kb, units, it, w); ++local) {
         const int buf = local % a.nbuf;
         const uint32_t tphase = (uint32_t)((local / a.nbuf) & 1);
         if (!mbar_wait(&bars->tmem_empty[buf], tphase ^ 1, a.status, kStatusTimeoutTmemEmpty)) {
@@ -215,43 +281,91 @@ __global__ void __launch_bounds__(kWdThreads, 1)
     const int quarter = warp & 3;
     const int i = quarter * 32 + lane;  // row of the 128-row weight tile
     int local = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
-      const WdUnit w = wd_unit(a, u, num_kb);
+    WdIter it;
+    WdItem w;
+    wd_begin(a, num_kb, it);
+    for (; wd_next(a, num_kb, units, it, w); ++local) {
       const int buf = local % a.nbuf;
       const uint32_t tphase = (uint32_t)((local / a.nbuf) & 1);
       if (!mbar_wait(&bars->tmem_full[buf], tphase, a.status, kStatusTimeoutTmemFull)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * acc_cols);
       const int m0 = w.t * a.bn;
+      bool finish = true;  // this CTA applies the epilogue of the unit
+      const float* others = nullptr;  // the unit's piece partials (stream-K), [piece][acc][bn][128]
+      if (w.n_pieces > 1) {
+        // stream-K piece: leave the fp32 partial, count the arrival; the last
+        // piece to arrive sums all pieces in piece order and finishes the unit
+        float* slots = a.sk_ws + (size_t)w.tail * a.sk_max_pieces * acc_cols * kWdBM;
+        float* mine = slots + (size_t)w.piece * acc_cols * kWdBM;
 #pragma unroll 1
-      for (int c0 = 0; c0 < a.bn; c0 += 16) {
-        if constexpr (EPI == WIDE_SWIGLU) {
-          uint32_t gr[16], ur[16];
-          wd_tmem_ld16(tbase + c0, gr);
-          wd_tmem_ld16(tbase + a.bn + c0, ur);
+        for (int c0 = 0; c0 < acc_cols; c0 += 16) {
+          uint32_t r[16];
+          wd_tmem_ld16(tbase + c0, r);
           tmem_ld_wait();
-          __nv_bfloat16* dst = a.out + (size_t)w.g * kWdBM + i;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int m = m0 + c0 + j;
-            if (m < a.M) {
-              const float gb = bf16_round(__uint_as_float(gr[j]));
-              const float ub = bf16_round(__uint_as_float(ur[j]));
-              dst[(size_t)m * a.ldo] = __float2bfloat16_rn(bf16_round(silu_f(gb)) * ub);
-            }
-          }
-        } else {
+          for (int j = 0; j < 16; ++j) mine[(size_t)(c0 + j) * kWdBM + i] = __uint_as_float(r[j]);
+        }
+        __threadfence();
+        wd_epi_barrier();
+        if (warp == 2 && lane == 0) bars->sk_ticket = atomicAdd(a.sk_tickets + w.tail, 1u);
+        wd_epi_barrier();
+        finish = bars->sk_ticket == (uint32_t)(w.n_pieces - 1);
+        if (finish) {
+          __threadfence();
+          others = slots;
+          if (warp == 2 && lane == 0) a.sk_tickets[w.tail] = 0u;
+        }
+      }
+      if (finish) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < a.bn; c0 += 16) {
+          float v[ACC][16];
 #pragma unroll
           for (int c = 0; c < ACC; ++c) {
             uint32_t r[16];
             wd_tmem_ld16(tbase + (uint32_t)(c * a.bn + c0), r);
             tmem_ld_wait();
-            const int n = (w.g * ACC + c) * kWdBM + i;
-            float* dst = a.ws + (size_t)w.s * a.M * a.N + n;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[c][j] = __uint_as_float(r[j]);
+          }
+          if (others != nullptr) {
+            // fixed piece order: the sum does not depend on which piece came last
+#pragma unroll
+            for (int c = 0; c < ACC; ++c) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                float sum = 0.f;
+                for (int p = 0; p < w.n_pieces; ++p) {
+                  const float x = p == w.piece ? v[c][j]
+                                               : __ldcg(others + ((size_t)p * acc_cols + c * a.bn + c0 + j) * kWdBM + i);
+                  sum = p == 0 ? x : sum + x;
+                }
+                v[c][j] = sum;
+              }
+            }
+          }
+          if constexpr (EPI == WIDE_SWIGLU) {
+            __nv_bfloat16* dst = a.out + (size_t)w.g * kWdBM + i;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int m = m0 + c0 + j;
-              if (m < a.M) dst[(size_t)m * a.N] = __uint_as_float(r[j]);
+              if (m < a.M) {
+                const float gb = bf16_round(v[0][j]);
+                const float ub = bf16_round(v[ACC - 1][j]);
+                dst[(size_t)m * a.ldo] = __float2bfloat16_rn(bf16_round(silu_f(gb)) * ub);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < ACC; ++c) {
+              const int n = (w.g * ACC + c) * kWdBM + i;
+              float* dst = a.ws + (size_t)w.s * a.M * a.N + n;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int m = m0 + c0 + j;
+                if (m < a.M) dst[(size_t)m * a.N] = v[c][j];
+              }
             }
           }
         }
@@ -273,7 +387,8 @@ __global__ void __launch_bounds__(kWdThreads, 1)
 // fixed pipeline fill and the epilogue), times the rounds of units over the
 // SMs, plus the split-K partials' round trip; the cheapest plan wins.
 // ---------------------------------------------------------------------------
-static double wide_cost(int M, int N, int K, int acc, int n_tt, int splits, int epi, int num_sms, WidePlan* out) {
+static double wide_cost(int M, int N, int K, int acc, int n_tt, int splits, int epi, int num_sms, bool stream_k,
+                        WidePlan* out) {
   const int bn = ((M + n_tt - 1) / n_tt + 15) / 16 * 16;
   if (bn < 16 || bn > 256) return -1.0;
   if (N % (kWdBM * acc) != 0) return -1.0;
@@ -289,8 +404,22 @@ static double wide_cost(int M, int N, int K, int acc, int n_tt, int splits, int 
   while (alloc < nbuf * cols) alloc *= 2;
   if (alloc > 512) return -1.0;
   const long long units = (long long)(N / (kWdBM * acc)) * n_tt * splits;
+  const int grid = units < num_sms ? (int)units : num_sms;
   const long long rounds = (units + num_sms - 1) / num_sms;
-  const double busy = units < num_sms ? (double)units : (double)num_sms;
+  const double busy = (double)grid;
+  // stream-K tail (SwiGLU only: the other epilogues balance through the K split)
+  int sk_tail = 0, sk_ctas = 0, sk_max_pieces = 0;
+  if (stream_k && epi == WIDE_SWIGLU && units > grid && units % grid != 0) {
+    sk_tail = (int)(units % grid);
+    const long long Wt = (long long)sk_tail * num_kb;
+    sk_ctas = (int)(Wt / 8 < grid ? Wt / 8 : grid);  // at least 8 k-blocks per piece
+    if (sk_ctas < 2) {
+      sk_tail = sk_ctas = 0;
+    } else {
+      const long long run = Wt / sk_ctas;  // shortest run of k-blocks of a CTA
+      sk_max_pieces = (int)((num_kb + run - 1) / run) + 1;
+    }
+  }
   // per-SM rates (B200, measured): ~11.2 TFLOP/s of bf16 MMA, L2->SM share of ~13 TB/s
   const double l2_per_sm = 13.0e12 / busy;
   const double kb_flops = 2.0 * kWdBM * acc * bn * kWdBK;
@@ -298,7 +427,16 @@ static double wide_cost(int M, int N, int K, int acc, int n_tt, int splits, int 
   const double kb_per_unit = (double)num_kb / splits;
   const double epi_time = (epi == WIDE_SWIGLU ? 1.0 : 2.0) * (double)kWdBM * cols * 2.0 / 60e9;
   const double unit_time = kb_per_unit * kb_time + 1.5e-6 + (nbuf == 2 ? 0.0 : epi_time);
-  double cost = rounds * unit_time + (nbuf == 2 ? epi_time : 0.0);
+  double cost;
+  if (sk_tail > 0) {
+    // whole rounds, then each CTA's run of the tail; the pieces' partials go
+    // through L2 (written by every piece, read by the last)
+    const double run_kb = (double)sk_tail * num_kb / sk_ctas;
+    const double fix = (double)sk_tail * (sk_max_pieces + 1) * cols * kWdBM * 4.0 / 5.0e12;
+    cost = (double)(units / grid) * unit_time + run_kb * kb_time + 1.5e-6 + 2.0 * epi_time + fix;
+  } else {
+    cost = rounds * unit_time + (nbuf == 2 ? epi_time : 0.0);
+  }
   if (epi == WIDE_PARTIAL) cost += ((double)M * N * 4.0 * (splits + 1) + (double)M * N * 2.0) / 5.0e12 + 2e-6;
   if (out != nullptr) {
     out->acc = acc;
@@ -309,12 +447,16 @@ static double wide_cost(int M, int N, int K, int acc, int n_tt, int splits, int 
     out->nbuf = nbuf;
     out->tmem_cols = alloc;
     out->smem = stages * stage_bytes + 1024 + (int)sizeof(WdBars);
+    out->grid = grid;
+    out->sk_tail = sk_tail;
+    out->sk_ctas = sk_ctas;
+    out->sk_max_pieces = sk_max_pieces;
   }
   return cost;
 }
 
 bool wide_plan(int M, int N, int K, int epi, int num_sms, int acc_req, int n_tt_req, int splits_req,
-               WidePlan* plan) {
+               bool stream_k, WidePlan* plan) {
   if (M < 1 || M > 512 || K % kWdBK != 0 || num_sms < 1) return false;
   double best = -1.0;
   WidePlan bp{};
@@ -327,7 +469,7 @@ bool wide_plan(int M, int N, int K, int epi, int num_sms, int acc_req, int n_tt_
       for (int s = 1; s <= (epi == WIDE_SWIGLU ? 1 : 16); ++s) {
         if (splits_req > 0 && s != splits_req) continue;
         WidePlan p{};
-        const double c = wide_cost(M, N, K, acc, n_tt, s, epi, num_sms, &p);
+        const double c = wide_cost(M, N, K, acc, n_tt, s, epi, num_sms, stream_k, &p);
         if (c < 0.0) continue;
         if (best < 0.0 || c < best) best = c, bp = p;
       }
@@ -368,7 +510,17 @@ cudaError_t wide_gemm(const WideArgs& args, cudaStream_t stream) {
   if (!make_tmap_2d_bf16(&tw, a.w, a.K, a.N, a.ldw, kWdBK, kWdBM * a.acc, true)) return cudaErrorInvalidValue;
   if (!make_tmap_2d_bf16(&tx, a.x, a.K, a.M, a.ldx, kWdBK, a.bn, true)) return cudaErrorInvalidValue;
   const int units = a.N / (kWdBM * a.acc) * a.n_tt * a.splits;
-  const int grid = units < a.num_sms ? units : a.num_sms;
+  const int grid = a.grid;
+  if (grid < 1 || grid > units || grid > a.num_sms) return cudaErrorInvalidValue;
+  if (a.sk_tail > 0) {
+    if (a.sk_tail >= units || a.sk_ctas < 1 || a.sk_ctas > grid || a.sk_ws == nullptr || a.sk_tickets == nullptr ||
+        (units - a.sk_tail) % grid != 0)
+      return cudaErrorInvalidValue;
+    const long long run = (long long)a.sk_tail * (a.K / kWdBK) / a.sk_ctas;
+    if (run < 1 || ((a.K / kWdBK) + run - 1) / run + 1 > a.sk_max_pieces) return cudaErrorInvalidValue;
+  } else if ((units + grid - 1) / grid * grid < units) {
+    return cudaErrorInvalidValue;
+  }
   if (a.epi == WIDE_SWIGLU) return launch_wide<2, WIDE_SWIGLU>(a, tw, tx, grid, stream);
   return a.acc == 2 ? launch_wide<2, WIDE_PARTIAL>(a, tw, tx, grid, stream)
                     : launch_wide<1, WIDE_PARTIAL>(a, tw, tx, grid, stream);

@@ -380,6 +380,14 @@ struct WidePlan {
   int nbuf;       // TMEM accumulator buffers
   int tmem_cols;  // TMEM allocation (power of two)
   int smem;       // dynamic shared memory bytes
+  int grid;       // persistent CTAs
+  // stream-K tail: when the units do not fill whole rounds of the grid, the
+  // last sk_tail units are cut into sk_ctas equal runs of k-blocks, one per
+  // CTA; the pieces of a unit meet in sk_ws and the last to finish applies
+  // the epilogue (0 = every unit runs whole)
+  int sk_tail;
+  int sk_ctas;
+  int sk_max_pieces;
 };
 struct WideArgs : WidePlan {
   const __nv_bfloat16* x;  // [M, K] row stride ldx
@@ -391,10 +399,12 @@ struct WideArgs : WidePlan {
   int ldo;
   int num_sms;
   int* status;
+  float* sk_ws;            // [sk_tail][sk_max_pieces][acc][bn][128] fp32 partials of split tail units
+  unsigned* sk_tickets;    // [sk_tail] arrival counters, zero between launches (the last arrival resets)
 };
 // Cheapest plan for the shape (a *_req of 0 leaves that choice free); false if none fits.
 bool wide_plan(int M, int N, int K, int epi, int num_sms, int acc_req, int n_tt_req, int splits_req,
-               WidePlan* plan);
+               bool stream_k, WidePlan* plan);
 cudaError_t wide_gemm(const WideArgs& a, cudaStream_t stream);
 // token-row tile of the skinny GEMM for M rows: 16 (M <= 16), 32 (M <= 32) or 64 (M <= 64)
 int skinny_bn(int M);

@@ -169,6 +169,21 @@ def main() -> None:
                 ext.set_gemm_rows_per_tile(0)
                 del a, w, o
 
+    if "gemm_wide_gu" in only:
+        # one shape for a profiler capture: the SwiGLU gate/up projection of the 8B layer at 330 rows
+        M, N, K = 330, 28672, 4096
+        w = (torch.randn(N, K, device=dev) * 0.02).to(bf)
+        a = torch.randn(M, K, device=dev).to(bf)
+        o = torch.empty(M, N // 2, device=dev, dtype=bf)
+        for sk in (True, False):
+            ext.set_wide_stream_k(sk)
+            t = timeit(lambda: ext.wide_swiglu(a, w, o), n=5, warm=3)
+            tf = 2 * M * N * K / (t * 1e-6) / 1e12
+            res[f"gemm_M330_gate_up_tokencol_streamk{int(sk)}"] = {
+                "us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS, "plan": ext.wide_plan(M, N, K, 1)}
+        ext.set_wide_stream_k(True)
+        del w, a, o
+
     if "gemm_wide" in only:
         # token-column GEMM (weights as the MMA's M, tokens as its N) against the row-tile GEMM at
         # CacheBlend's active-row counts; weights cycled over copies so every call streams them
@@ -206,7 +221,7 @@ def main() -> None:
                     t = timeit(fn, n=20)
                     tf = 2 * M * N * K / (t * 1e-6) / 1e12
                     res[f"gemm_M{M}_{name}_{arm}"] = {"us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS}
-                res[f"gemm_M{M}_{name}_tokencol"]["plan"] = list(ext.wide_plan(M, N, K, 1 if kind == "swiglu" else 0))
+                res[f"gemm_M{M}_{name}_tokencol"]["plan"] = ext.wide_plan(M, N, K, 1 if kind == "swiglu" else 0)
                 del ws_, a, o
 
     if "attn_decode" in only or "attn_decode_sweep" in only:

@@ -807,3 +807,40 @@ def test_wide_qkv_rope_scatter(cuda_device, M):
     untouched = torch.ones(cap, dtype=torch.bool, device=cuda_device)
     untouched[sl] = False
     assert torch.equal(kc[:, untouched], kc0[:, untouched])
+
+
+@pytest.mark.parametrize("M,K", [(330, 1024), (300, 512)])
+def test_wide_swiglu_stream_k_tail(cuda_device, M, K):
+    """Units that do not fill whole rounds of the grid: the tail is cut into equal runs of
+    k-blocks per CTA and the pieces of a unit are summed in piece order by the last one to
+    arrive.  Matches the fp32 reference, repeats bit for bit, and leaves the arrival
+    counters at zero (a second launch reads them)."""
+    ext = _ext()
+    F = 14336 if M == 330 else 10240
+    plan = ext.wide_plan(M, 2 * F, K, 1)
+    if ext.num_sms() == 148:
+        assert plan["sk_tail"] > 0, plan
+    g = torch.Generator(device="cpu").manual_seed(M + K)
+    x = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
+    wg = (torch.randn(F, K, generator=g) * 0.05).to(cuda_device, torch.bfloat16)
+    wu = (torch.randn(F, K, generator=g) * 0.05).to(cuda_device, torch.bfloat16)
+    wgu = interleave_gate_up(wg, wu)
+    outs = []
+    for _ in range(2):
+        act = torch.empty(M, F, device=cuda_device, dtype=torch.bfloat16)
+        ext.wide_swiglu(x, wgu, act)
+        outs.append(act)
+    ext.set_wide_stream_k(False)
+    try:
+        plain = torch.empty(M, F, device=cuda_device, dtype=torch.bfloat16)
+        ext.wide_swiglu(x, wgu, plain)
+    finally:
+        ext.set_wide_stream_k(True)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    gate = (x.float() @ wg.float().T).to(torch.bfloat16)
+    up = (x.float() @ wu.float().T).to(torch.bfloat16)
+    ref = torch.nn.functional.silu(gate.float()).to(torch.bfloat16).float() * up.float()
+    assert torch.equal(outs[0], outs[1])
+    assert _rel_err(outs[0], ref) < 2e-2
+    assert _rel_err(plain, ref) < 2e-2
