@@ -203,7 +203,7 @@ class _CountingExt:
     """Proxy over the extension that counts kernel launches issued from the host."""
 
     _NOT_KERNELS = {"status", "num_sms", "gemv_argmax_grid", "attention_decode_cluster", "attention_decode_outer",
-                    "skinny_splits", "attention_prefill_splits", "wide_plan", "set_wide_stream_k",
+                    "skinny_splits", "attention_prefill_splits", "wide_plan", "set_wide_stream_k", "set_attention_prefill_splits",
                     "shared_empty",
                     "shared_open", "shared_close"}
     _MULTI = {"gemm_store", "gemm_residual", "skinny_gemm", "skinny_qkv", "skinny_allreduce", "attention_prefill",

@@ -532,8 +532,18 @@ cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream) {
 // TMEM allocation, Q staging, pipeline fill - outweigh the shorter key loop;
 // 300 rows over 1676 keys ran 31.7 us whole and 41.5 us split three ways);
 // full prefills (a wave of row tiles or more) never split.
+static int g_forced_splits = 0;  // measurement hook: 0 = the cost rule below
+void set_attention_prefill_splits(int s) { g_forced_splits = s < 0 ? 0 : s; }
+
 int attention_prefill_splits(const AttnPrefillArgs& p, int num_sms) {
   if (p.ws == nullptr || p.n_rows <= 0 || p.n_kv_heads <= 0 || num_sms <= 0) return 1;
+  if (g_forced_splits > 0) {
+    const int key_tiles = (p.n_keys + kBN - 1) / kBN;
+    int s = g_forced_splits < key_tiles ? g_forced_splits : key_tiles;
+    if (s > 4) s = 4;
+    if ((long long)s * p.n_rows * p.n_heads * 132 > p.ws_floats) return 1;
+    return s < 1 ? 1 : s;
+  }
   const int span = kBM / (p.n_heads / p.n_kv_heads);
   const int ctas = p.n_kv_heads * ((p.n_rows + span - 1) / span);
   if (ctas >= num_sms) return 1;

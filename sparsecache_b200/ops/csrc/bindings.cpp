@@ -1549,6 +1549,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("v_cache"), py::arg("rope_pos"), py::arg("cache_slot"), py::arg("rope_table"), py::arg("n_q_heads"),
         py::arg("n_kv_heads"), py::arg("acc") = 0, py::arg("n_tt") = 0, py::arg("splits") = 0);
   m.def("set_wide_stream_k", &set_wide_stream_k);
+  m.def("set_attention_prefill_splits", [](int64_t s) { sc::set_attention_prefill_splits((int)s); });
   m.def("wide_plan", &wide_plan, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"), py::arg("acc") = 0,
         py::arg("n_tt") = 0, py::arg("splits") = 0, py::arg("sms") = 0);
   m.def("skinny_qkv", &skinny_qkv, py::arg("x"), py::arg("w_qkv"), py::arg("q_out"), py::arg("k_cache"),

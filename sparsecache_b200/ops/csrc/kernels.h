@@ -215,6 +215,7 @@ cudaError_t recurrent_attention_fwd(const RecurrentAttnArgs& a, cudaStream_t str
 cudaError_t recurrent_attention_bwd(const RecurrentAttnArgs& a, cudaStream_t stream);
 // key splits the launcher would use for these arguments (1 = none)
 int attention_prefill_splits(const AttnPrefillArgs& p, int num_sms);
+void set_attention_prefill_splits(int s);  // measurement hook (0 = automatic)
 // the mma.sync kernel the tcgen05 one replaced, kept for A/B measurement only
 cudaError_t attention_prefill_mma(const AttnPrefillArgs& p, cudaStream_t stream);
 

@@ -329,7 +329,7 @@ def main() -> None:
             t = timeit(lambda: ext.attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), S, out, **kw))
             res[f"attn_decode_tp8_70b_ctx{cap}_{name}"] = {"us": t, "GBps": kv_bytes / (t * 1e-6) / 1e9}
 
-    if "attn_prefill" in only or "attn_prefill_ab" in only:
+    if "attn_prefill" in only or "attn_prefill_ab" in only or "attn_prefill_split" in only:
         # CacheBlend shapes of the 8B serving case: the full layers (every row,
         # causal) and the selective layers (300 active rows over 1676 keys);
         # the tcgen05 kernel against the mma.sync kernel it replaced
@@ -356,6 +356,15 @@ def main() -> None:
                 t = timeit(call, n=20)
                 tf = flops / (t * 1e-6) / 1e12
                 res[f"{kern}_{name}_T{T}"] = {"us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS}
+            if "attn_prefill_split" in only and R <= 512:
+                # key split forced to 1..4 CTAs per row tile (+ the merge kernel)
+                for s_try in (1, 2, 3, 4):
+                    ext.set_attention_prefill_splits(s_try)
+                    t = timeit(lambda: ext.attention_prefill(q, rows, qpos, kc, vc, None, T, H, 1 / math.sqrt(128), out,
+                                                             ws=split_ws), n=20)
+                    res[f"attention_prefill_{name}_T{T}_splits{s_try}"] = {
+                        "us": t, "frac_of_measured_bf16": flops / (t * 1e-6) / 1e12 / BF16_TFLOPS}
+                ext.set_attention_prefill_splits(0)
     if "attn_trace" in only:
         # timeline of one CTA (head 0, the longest row tile) of the causal case
         H, Hkv, T = 32, 8, 1676
