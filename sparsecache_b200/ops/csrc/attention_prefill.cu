@@ -164,6 +164,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_v);
   }
   __syncthreads();
+  // q, the positions and the new K/V rows come from the previous kernels
+  pdl_wait();
+  pdl_launch_dependents();
 
   // ---- softmax warps: stage the (gathered) Q tile, find each row's visible prefix ----
   // tile row = TMEM lane = warp quarter * 32 + lane; row -> (query head
@@ -465,6 +468,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Merge of the key-split partials: one warp per (row, head), 4 dims a lane,
 // splits combined in split order (deterministic).
 __global__ void __launch_bounds__(256) attention_prefill_merge_kernel(AttnPrefillArgs p) {
+  pdl_wait();
+  pdl_launch_dependents();
   const long long pair = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (pair >= (long long)p.n_rows * p.n_heads) return;
   const int lane = threadIdx.x & 31;
@@ -518,12 +523,10 @@ cudaError_t attention_prefill(const AttnPrefillArgs& p, cudaStream_t stream) {
   AttnPrefillArgs a = p;
   a.splits = attention_prefill_splits(p, sms);
   dim3 grid(p.n_kv_heads, (p.n_rows + span - 1) / span, a.splits);
-  attention_prefill_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tk, tv, a);
-  cudaError_t err = cudaGetLastError();
+  cudaError_t err = launch_pdl(attention_prefill_tc_kernel, grid, dim3(kThreads), kSmemBytes, stream, tk, tv, a);
   if (err != cudaSuccess || a.splits == 1) return err;
   const long long pairs = (long long)p.n_rows * p.n_heads;
-  attention_prefill_merge_kernel<<<(unsigned)((pairs + 7) / 8), 256, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(attention_prefill_merge_kernel, dim3((unsigned)((pairs + 7) / 8)), dim3(256), 0, stream, a);
 }
 
 // A grid of fewer CTAs than SMs (a few hundred selective rows over a long

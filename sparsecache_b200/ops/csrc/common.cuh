@@ -15,6 +15,7 @@
 #include <stdlib.h>
 
 #include <mutex>
+#include <utility>
 
 namespace sc {
 
@@ -423,5 +424,24 @@ inline bool pdl_enabled() {
     enabled = (e != nullptr && e[0] == '0') ? 0 : 1;
   }
   return enabled != 0;
+}
+
+// Launch with programmatic stream serialization when PDL is on: the kernel
+// may start while its predecessor drains and must call pdl_wait() before it
+// touches anything the predecessor writes or reads.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 }  // namespace sc

@@ -364,6 +364,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, ACC>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
+  // the A rows (and the residual / cache rows of the epilogues) come from the
+  // previous kernel; the setup above overlapped its tail
+  pdl_wait();
+  pdl_launch_dependents();
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -585,8 +589,8 @@ static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   const int num_units = ((g.M + Cfg::kBM - 1) / Cfg::kBM) * ((g.N + BN - 1) / BN) * splits;
   int grid = num_units < g.num_sms ? num_units : g.num_sms;
   if (grid < 1) grid = 1;
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(maps, tb, g.M, g.N, g.K, g.ep, sh, splits, g.status);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, maps, tb, g.M, g.N, g.K, g.ep,
+                    sh, splits, g.status);
 }
 
 template <int EPI>
@@ -652,6 +656,8 @@ double gemm_cost_estimate(int M, int N, int K, int bn, int rows_per_tile, int sp
 // epilogue (out = residual + bf16(sum), the HF rounding order).
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N,
                                      const __nv_bfloat16* residual, int ldr, __nv_bfloat16* out, int ldo) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int n4 = N / 4;
   const long long total = (long long)M * n4;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -689,6 +695,8 @@ __global__ void __launch_bounds__(256) splitk_reduce_norm_kernel(const float* __
                                                                  const __nv_bfloat16* norm_w, float eps,
                                                                  __nv_bfloat16* norm_out, int ldn) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_launch_dependents();
   const int row = blockIdx.x;
   const int n8 = N / 8;
   uint32_t keep[kRedNormMaxChunks][4];
@@ -753,9 +761,8 @@ cudaError_t splitk_reduce_norm(const float* ws, int splits, int M, int N, const 
                                __nv_bfloat16* norm_out, int ldn, cudaStream_t stream) {
   if (N % 8 != 0 || N / 8 > 256 * kRedNormMaxChunks || splits < 1 || residual == nullptr) return cudaErrorInvalidValue;
   if (M <= 0) return cudaSuccess;
-  splitk_reduce_norm_kernel<<<M, 256, 0, stream>>>(ws, splits, M, N, residual, ldr, out, ldo, norm_w, eps, norm_out,
-                                                    ldn);
-  return cudaGetLastError();
+  return launch_pdl(splitk_reduce_norm_kernel, dim3(M), dim3(256), 0, stream, ws, splits, M, N, residual, ldr, out,
+                    ldo, norm_w, eps, norm_out, ldn);
 }
 
 cudaError_t splitk_reduce(const float* ws, int splits, int M, int N, const __nv_bfloat16* residual, int ldr,
@@ -763,8 +770,8 @@ cudaError_t splitk_reduce(const float* ws, int splits, int M, int N, const __nv_
   if (N % 4 != 0 || splits < 1) return cudaErrorInvalidValue;
   const long long total = (long long)M * (N / 4);
   const int grid = (int)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
-  splitk_reduce_kernel<<<grid < 1 ? 1 : grid, 256, 0, stream>>>(ws, splits, M, N, residual, ldr, out, ldo);
-  return cudaGetLastError();
+  return launch_pdl(splitk_reduce_kernel, dim3(grid < 1 ? 1 : grid), dim3(256), 0, stream, ws, splits, M, N, residual,
+                    ldr, out, ldo);
 }
 
 }  // namespace sc

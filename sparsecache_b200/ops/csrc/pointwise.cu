@@ -22,6 +22,8 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* x, int ldx, const int* rows,
                                const __nv_bfloat16* w, __nv_bfloat16* out, int ldo, int D,
                                float eps) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_launch_dependents();
   const int r = blockIdx.x;
   const int src_row = rows ? rows[r] : r;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)src_row * ldx);
@@ -66,8 +68,7 @@ cudaError_t rmsnorm_bf16(const __nv_bfloat16* x, int ldx, const int* rows, const
                          cudaStream_t stream) {
   if (M <= 0) return cudaSuccess;
   if (D % 8) return cudaErrorInvalidValue;
-  rmsnorm_kernel<<<M, 256, 0, stream>>>(x, ldx, rows, w, out, ldo, D, eps);
-  return cudaGetLastError();
+  return launch_pdl(rmsnorm_kernel, dim3(M), dim3(256), 0, stream, x, ldx, rows, w, out, ldo, D, eps);
 }
 
 // ---------------------------------------------------------------- gathers
