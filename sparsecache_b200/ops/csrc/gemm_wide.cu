@@ -292,19 +292,25 @@ __global__ void __launch_bounds__(kWdThreads, 1)
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * acc_cols);
       const int m0 = w.t * a.bn;
       bool finish = true;  // this CTA applies the epilogue of the unit
-      const float* others = nullptr;  // the unit's piece partials (stream-K), [piece][acc][bn][128]
+      // stream-K partials of the unit: [piece][acc * bn / 4][128 rows] float4
+      // (4 consecutive token columns of one weight row per float4)
+      const float4* others = nullptr;
+      int oth0 = 0, oth1 = 0;  // the other pieces, in piece order
       if (w.n_pieces > 1) {
         // stream-K piece: leave the fp32 partial, count the arrival; the last
         // piece to arrive sums all pieces in piece order and finishes the unit
-        float* slots = a.sk_ws + (size_t)w.tail * a.sk_max_pieces * acc_cols * kWdBM;
-        float* mine = slots + (size_t)w.piece * acc_cols * kWdBM;
+        float4* slots = reinterpret_cast<float4*>(a.sk_ws) + (size_t)w.tail * a.sk_max_pieces * (acc_cols / 4) * kWdBM;
+        float4* mine = slots + (size_t)w.piece * (acc_cols / 4) * kWdBM;
 #pragma unroll 1
         for (int c0 = 0; c0 < acc_cols; c0 += 16) {
           uint32_t r[16];
           wd_tmem_ld16(tbase + c0, r);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) mine[(size_t)(c0 + j) * kWdBM + i] = __uint_as_float(r[j]);
+          for (int q = 0; q < 4; ++q)
+            mine[(size_t)(c0 / 4 + q) * kWdBM + i] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                                                 __uint_as_float(r[4 * q + 2]),
+                                                                 __uint_as_float(r[4 * q + 3]));
         }
         __threadfence();
         wd_epi_barrier();
@@ -314,13 +320,29 @@ __global__ void __launch_bounds__(kWdThreads, 1)
         if (finish) {
           __threadfence();
           others = slots;
+          oth0 = w.piece == 0 ? 1 : 0;
+          oth1 = w.piece == 2 ? 1 : 2;  // used only with three pieces
           if (warp == 2 && lane == 0) a.sk_tickets[w.tail] = 0u;
         }
       }
       if (finish) {
-#pragma unroll 1
+#pragma unroll 2
         for (int c0 = 0; c0 < a.bn; c0 += 16) {
           float v[ACC][16];
+          float4 o0[ACC][4], o1[ACC][4];
+          if (others != nullptr) {
+            // every load of the chunk in flight before the first use
+#pragma unroll
+            for (int c = 0; c < ACC; ++c) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const size_t col4 = (size_t)((c * a.bn + c0) / 4 + q) * kWdBM + i;
+                o0[c][q] = __ldcg(others + (size_t)oth0 * (acc_cols / 4) * kWdBM + col4);
+                o1[c][q] = w.n_pieces == 3 ? __ldcg(others + (size_t)oth1 * (acc_cols / 4) * kWdBM + col4)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+            }
+          }
 #pragma unroll
           for (int c = 0; c < ACC; ++c) {
             uint32_t r[16];
@@ -330,18 +352,21 @@ __global__ void __launch_bounds__(kWdThreads, 1)
             for (int j = 0; j < 16; ++j) v[c][j] = __uint_as_float(r[j]);
           }
           if (others != nullptr) {
-            // fixed piece order: the sum does not depend on which piece came last
+            // fixed piece order (x0 + x1) + x2: the sum does not depend on
+            // which piece arrived last
 #pragma unroll
             for (int c = 0; c < ACC; ++c) {
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
-                float sum = 0.f;
-                for (int p = 0; p < w.n_pieces; ++p) {
-                  const float x = p == w.piece ? v[c][j]
-                                               : __ldcg(others + ((size_t)p * acc_cols + c * a.bn + c0 + j) * kWdBM + i);
-                  sum = p == 0 ? x : sum + x;
-                }
-                v[c][j] = sum;
+                const float4 f0 = o0[c][j / 4], f1 = o1[c][j / 4];
+                const float a0 = (j & 3) == 0 ? f0.x : (j & 3) == 1 ? f0.y : (j & 3) == 2 ? f0.z : f0.w;
+                const float a1 = (j & 3) == 0 ? f1.x : (j & 3) == 1 ? f1.y : (j & 3) == 2 ? f1.z : f1.w;
+                const float mine_v = v[c][j];
+                float x0, x1, x2;
+                if (w.piece == 0) x0 = mine_v, x1 = a0, x2 = a1;
+                else if (w.piece == 1) x0 = a0, x1 = mine_v, x2 = a1;
+                else x0 = a0, x1 = a1, x2 = mine_v;
+                v[c][j] = w.n_pieces == 3 ? (x0 + x1) + x2 : x0 + x1;
               }
             }
           }
@@ -412,12 +437,15 @@ static double wide_cost(int M, int N, int K, int acc, int n_tt, int splits, int 
   if (stream_k && epi == WIDE_SWIGLU && units > grid && units % grid != 0) {
     sk_tail = (int)(units % grid);
     const long long Wt = (long long)sk_tail * num_kb;
-    sk_ctas = (int)(Wt / 8 < grid ? Wt / 8 : grid);  // at least 8 k-blocks per piece
+    // runs of at least 8 k-blocks and half a unit: a unit meets at most 3 pieces
+    const long long min_run = num_kb / 2 > 8 ? (num_kb + 1) / 2 : 8;
+    sk_ctas = (int)(Wt / min_run < grid ? Wt / min_run : grid);
     if (sk_ctas < 2) {
       sk_tail = sk_ctas = 0;
     } else {
       const long long run = Wt / sk_ctas;  // shortest run of k-blocks of a CTA
       sk_max_pieces = (int)((num_kb + run - 1) / run) + 1;
+      if (sk_max_pieces > 3) sk_tail = sk_ctas = sk_max_pieces = 0;
     }
   }
   // per-SM rates (B200, measured): ~11.2 TFLOP/s of bf16 MMA, L2->SM share of ~13 TB/s
@@ -517,7 +545,8 @@ cudaError_t wide_gemm(const WideArgs& args, cudaStream_t stream) {
         (units - a.sk_tail) % grid != 0)
       return cudaErrorInvalidValue;
     const long long run = (long long)a.sk_tail * (a.K / kWdBK) / a.sk_ctas;
-    if (run < 1 || ((a.K / kWdBK) + run - 1) / run + 1 > a.sk_max_pieces) return cudaErrorInvalidValue;
+    if (run < 1 || ((a.K / kWdBK) + run - 1) / run + 1 > a.sk_max_pieces || a.sk_max_pieces > 3)
+      return cudaErrorInvalidValue;
   } else if ((units + grid - 1) / grid * grid < units) {
     return cudaErrorInvalidValue;
   }
