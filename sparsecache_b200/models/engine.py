@@ -627,6 +627,18 @@ class B200Engine:
         """CTAs per kv head (= thread-block cluster size) of the decode attention."""
         return int(self.ext.attention_decode_cluster(capacity, self.cfg.n_kv_heads))
 
+    def _batch_splits(self, capacity: int, n_seq: int, n_kv_heads: int | None = None) -> int:
+        """Cluster size of the batched decode attention: the smallest power of two that gives
+        every SM a CTA (sequences x kv heads x cluster >= SMs), at most the one-sequence size.
+        With 32 sequences of 8 kv heads one CTA per (sequence, kv head) suffices: 66 us per
+        layer at 1.7k keys against 206 us with 8-CTA clusters (B200, 0.51 of measured HBM)."""
+        kvh = self.cfg.n_kv_heads if n_kv_heads is None else n_kv_heads
+        cap = int(self.ext.attention_decode_cluster(capacity, kvh))
+        s = 1
+        while s < cap and n_seq * kvh * s < self.num_sms:
+            s *= 2
+        return s
+
     def set_decode_state(self, *, position: int, slot: int | None = None, n_virtual: int | None = None) -> None:
         """Host-side set of the device scalars (stream-ordered, before a step)."""
         b = self._decode_buffers()
@@ -829,7 +841,7 @@ class B200Engine:
             return
         if len({s.capacity for s in slots}) != 1:
             raise ValueError("batched slots share one capacity")
-        splits = self._decode_splits(slots[0].capacity)
+        splits = self._batch_splits(slots[0].capacity, len(slots))
         if not use_graph:
             for _ in range(n_steps):
                 self._batch_step(slots, splits)

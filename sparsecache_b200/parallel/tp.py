@@ -749,7 +749,7 @@ class TPEngine:
         eng = self.engine
         if len({s.capacity for s in slots}) != 1:
             raise ValueError("batched slots share one capacity")
-        splits = eng._decode_splits(slots[0].capacity)
+        splits = eng._batch_splits(slots[0].capacity, len(slots), self.lcfg.n_kv_heads)
         if not use_graph:
             for _ in range(n_steps):
                 self._batch_step(slots, splits)
