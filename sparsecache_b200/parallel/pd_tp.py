@@ -327,21 +327,33 @@ def main() -> None:
     p.add_argument("--tp", type=int, default=4)
     p.add_argument("--model", default="llama3-8b")
     p.add_argument("--layers", type=int, default=None)
-    p.add_argument("--mode", choices=("push", "nccl"), default="push")
+    p.add_argument("--mode", default="push",
+                   help="push | nccl | poisson, or a comma list run back to back in one process group "
+                        "(e.g. push,nccl,poisson); poisson serves open-loop arrivals at --arrival-rate")
     p.add_argument("--steps", type=int, default=6)
     p.add_argument("--warmup", type=int, default=2)
     p.add_argument("--new-tokens", type=int, default=128)
-    p.add_argument("--arrival-rate", type=float, default=0.0, help="requests/s; > 0 serves open-loop Poisson arrivals")
+    p.add_argument("--arrival-rate", type=float, default=0.0,
+                   help="requests/s of the poisson mode; > 0 with a single --mode push serves only Poisson arrivals")
     p.add_argument("--slots", type=int, default=2, help="decode slots (Poisson mode)")
     p.add_argument("--seed", type=int, default=0)
     args = p.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    modes = [m.strip() for m in args.mode.split(",") if m.strip()]
+    if any(m not in ("push", "nccl", "poisson") for m in modes) or not modes:
+        raise SystemExit(f"--mode: expected push, nccl or poisson (comma list), got {args.mode!r}")
+    if modes == ["push"] and args.arrival_rate > 0:
+        modes = ["poisson"]
+    if "poisson" in modes and args.arrival_rate <= 0:
+        raise SystemExit("--mode poisson needs --arrival-rate > 0")
     try:
-        out = run_poisson(args) if args.arrival_rate > 0 else run_closed_loop(args)
-        if out is not None:
-            print(json.dumps(out), flush=True)
+        for mode in modes:
+            run = argparse.Namespace(**{**vars(args), "mode": "push" if mode == "poisson" else mode})
+            out = run_poisson(run) if mode == "poisson" else run_closed_loop(run)
+            if out is not None:
+                print(json.dumps(out), flush=True)
     finally:
         dist.destroy_process_group()
 

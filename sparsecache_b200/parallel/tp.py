@@ -10,10 +10,13 @@ Layout (one process per GPU, TP group of size tp):
     position so causal attention never reads them).
 
 Per layer and rank (all inside ONE stream, no host sync, no NCCL):
-  1. AG -> QKV GEMM: the TMA producer reads every rank's normed shard
-     directly from its buffer (peer-mapped over CUDA IPC; plain TMA loads, no
-     multicast), own shard first, after a bounded wait on that shard's ready
-     flag; epilogue = RoPE + local K/V cache write.
+  1. AG -> QKV GEMM: a side stream pulls every peer's normed shard into
+     local staging with one copy-engine transfer over NVLink each (after a
+     bounded device wait on the owner's ready flag), so a remote tile crosses
+     NVLink once although every column tile of the GEMM reads it; the GEMM's
+     TMA producer (plain loads of local memory, no multicast) starts on its
+     own shard in place and reads each staged shard after a bounded wait on
+     that shard's local staged flag; epilogue = RoPE + local K/V cache write.
   2. attention of the local heads over all rows.
   3. o_proj GEMM -> RS: the epilogue stores every fp32 partial tile into the
      receive slot of the rank that owns the rows (NVLink stores), then a

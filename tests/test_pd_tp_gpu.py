@@ -8,7 +8,7 @@ run the TP greedy decode.  Checks:
   * the decode group's tokens equal the prefill group's own TP decode of the
     same prompt from its local cache;
   * no bounded wait timed out.
-TP1 -> TP1 runs on 2 GPUs, TP2 -> TP2 on 4.
+TP1 -> TP1 runs on 2 GPUs, TP2 -> TP2 on 4, TP4 -> TP4 on 8.
 """
 import json
 import os
@@ -86,7 +86,7 @@ def _worker(rank, world, tp, port, out_dir):
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("tp", [1, 2])
+@pytest.mark.parametrize("tp", [1, 2, 4])
 def test_tp_prefill_group_pushes_to_tp_decode_group(tmp_path, tp):
     world = 2 * tp
     if torch.cuda.device_count() < world:
