@@ -1361,7 +1361,7 @@ void dp_adamw_step(int64_t world, int64_t rank, int64_t n_total, int64_t shard, 
                    std::vector<int64_t> params, std::vector<int64_t> norms, Tensor flag_grads, Tensor flag_norms,
                    std::vector<int64_t> peer_flag_norms, std::vector<int64_t> peer_flag_params, Tensor epoch,
                    int64_t timeout_ns, Tensor status, Tensor red_grad, Tensor exp_avg, Tensor exp_avg_sq,
-                   Tensor hyper, Tensor state, Tensor partial, Tensor counter) {
+                   Tensor hyper, Tensor state, Tensor partial, Tensor counter, bool pre_reduced) {
   const c10::cuda::CUDAGuard guard(red_grad.device());
   TORCH_CHECK(world >= 1 && world <= sc::kMaxShards && rank >= 0 && rank < world, "world/rank");
   TORCH_CHECK((int64_t)grads.size() == world && (int64_t)params.size() == world && (int64_t)norms.size() == world &&
@@ -1395,9 +1395,55 @@ void dp_adamw_step(int64_t world, int64_t rank, int64_t n_total, int64_t shard, 
   a.state = state.data_ptr<float>();
   a.partial = partial.data_ptr<float>();
   a.counter = reinterpret_cast<unsigned*>(counter.data_ptr<int>());
+  a.pre_reduced = pre_reduced ? 1 : 0;
   const int grid = (int)partial.numel();
   check_cuda(sc::dp_reduce_norm(a, grid, cur_stream()), "dp_reduce_norm");
   check_cuda(sc::dp_adamw_gather(a, grid, cur_stream()), "dp_adamw_gather");
+}
+
+// One bucket of the data-parallel reduce-scatter (flat range [lo, hi)):
+// bounded wait on flags[0..world) (one per sender) for the current epoch,
+// then this rank's shard of the range, summed over every rank's gradient in
+// rank order, into red_grad.  grid CTAs (a few: it shares the GPU with the
+// backward's GEMMs).
+void dp_reduce_range(int64_t world, int64_t rank, int64_t n_total, int64_t shard, std::vector<int64_t> grads,
+                     Tensor flags, Tensor epoch, int64_t lo, int64_t hi, int64_t timeout_ns, Tensor status,
+                     Tensor red_grad, int64_t grid) {
+  const c10::cuda::CUDAGuard guard(red_grad.device());
+  TORCH_CHECK(world >= 1 && world <= sc::kMaxShards && rank >= 0 && rank < world, "world/rank");
+  TORCH_CHECK((int64_t)grads.size() == world, "one gradient pointer per rank");
+  TORCH_CHECK(shard * world >= n_total, "shards do not cover the buffer");
+  TORCH_CHECK(lo >= 0 && lo <= hi && hi <= n_total, "bucket range");
+  TORCH_CHECK(grid >= 1 && grid <= 1024, "grid");
+  CHECK_CUDA(red_grad); CHECK_F32(red_grad);
+  TORCH_CHECK(red_grad.numel() >= shard, "red_grad holds a shard");
+  CHECK_I32(flags); CHECK_I32(epoch); CHECK_I32(status);
+  TORCH_CHECK(flags.numel() >= world, "one flag per rank");
+  sc::DpArgs a{};
+  a.world = (int)world; a.rank = (int)rank; a.n_total = n_total; a.shard = shard;
+  for (int s = 0; s < world; ++s) a.grads[s] = reinterpret_cast<const float*>(grads[s]);
+  a.epoch_ptr = epoch.data_ptr<int>();
+  a.timeout_ns = timeout_ns;
+  a.status = status.data_ptr<int>();
+  a.red_grad = red_grad.data_ptr<float>();
+  check_cuda(sc::dp_reduce_range(a, flags.data_ptr<int>(), lo, hi, (int)grid, cur_stream()), "dp_reduce_range");
+}
+
+// out (fp32, [M, N], contiguous) = a @ w^T on the tensor cores with no
+// epilogue: the weight gradient of a linear layer over a whole batch of
+// positions (a = dY^T [out, rows], w = X^T [in, rows]; K = rows).
+void gemm_f32(Tensor a, Tensor w, Tensor out) {
+  const c10::cuda::CUDAGuard guard(a.device());
+  auto g = base_gemm(a, w, sc::EPI_PARTIAL, 256);
+  CHECK_CUDA(out); CHECK_F32(out);
+  TORCH_CHECK(out.is_contiguous() && out.dim() == 2 && out.size(0) == a.size(0) && out.size(1) == w.size(0),
+              "out must be a contiguous [M, N] fp32 matrix");
+  CHECK_ALIGN16(out);
+  TORCH_CHECK(g.N % 32 == 0, "N must be a multiple of 32");
+  g.splits = 1;
+  g.ep.ws = out.data_ptr<float>();
+  g.rows_per_tile = 128;  // one accumulator per tile: the partial epilogue's tested layout
+  run_gemm(g);
 }
 
 void bump_counter(Tensor counter) {
@@ -1565,7 +1611,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mem_attn_fwd", &mem_attn_fwd);
   m.def("mem_attn_bwd", &mem_attn_bwd);
   m.def("adamw_step", &adamw_step);
-  m.def("dp_adamw_step", &dp_adamw_step);
+  m.def("dp_adamw_step", &dp_adamw_step, py::arg("world"), py::arg("rank"), py::arg("n_total"), py::arg("shard"),
+        py::arg("grads"), py::arg("params"), py::arg("norms"), py::arg("flag_grads"), py::arg("flag_norms"),
+        py::arg("peer_flag_norms"), py::arg("peer_flag_params"), py::arg("epoch"), py::arg("timeout_ns"),
+        py::arg("status"), py::arg("red_grad"), py::arg("exp_avg"), py::arg("exp_avg_sq"), py::arg("hyper"),
+        py::arg("state"), py::arg("partial"), py::arg("counter"), py::arg("pre_reduced") = false);
+  m.def("dp_reduce_range", &dp_reduce_range);
+  m.def("gemm_f32", &gemm_f32, py::arg("a"), py::arg("w"), py::arg("out"));
   m.def("bump_counter", &bump_counter);
   m.def("signal_epoch", &signal_epoch);
   m.def("wait_all", &wait_all);

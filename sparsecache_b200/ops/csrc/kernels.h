@@ -552,8 +552,11 @@ struct DpArgs {
   float* state;
   float* partial;
   unsigned* counter;
+  int pre_reduced;                  // 1: red_grad already holds the reduced shard (bucketed reduce)
 };
 cudaError_t dp_reduce_norm(const DpArgs& a, int grid, cudaStream_t stream);
+cudaError_t dp_reduce_range(const DpArgs& a, const int* flags, long long lo, long long hi, int grid,
+                            cudaStream_t stream);
 cudaError_t dp_adamw_gather(const DpArgs& a, int grid, cudaStream_t stream);
 cudaError_t bump_counter(int* counter, cudaStream_t stream);
 

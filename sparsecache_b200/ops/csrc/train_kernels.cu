@@ -158,20 +158,32 @@ cudaError_t adamw_update(const AdamArgs& a, cudaStream_t stream) {
 }
 
 // ------------------------------------------------------------ data parallel
+// Mean over ranks of one gradient element, summed in rank order (the same
+// bits on every rank whichever kernel reduces it).
+__device__ __forceinline__ float rank_mean(const DpArgs& a, long long i) {
+  float g = 0.f;
+  for (int s = 0; s < a.world; ++s) g += __ldcg(a.grads[s] + i);
+  return g * (1.f / (float)a.world);  // each rank's loss is a mean over its rows
+}
+
 __global__ void __launch_bounds__(kOptThreads) dp_reduce_norm_kernel(DpArgs a) {
   const int epoch = *a.epoch_ptr;
-  if (!block_wait_all(a.flag_grads, a.world, epoch, a.timeout_ns, a.status)) return;
+  // pre_reduced: per-bucket kernels already wrote red_grad (overlapped with
+  // the backward); only the sum of squares is left
+  if (!a.pre_reduced && !block_wait_all(a.flag_grads, a.world, epoch, a.timeout_ns, a.status)) return;
   const long long base = (long long)a.rank * a.shard;
   long long len = a.n_total - base;
   len = len < 0 ? 0 : (len > a.shard ? a.shard : len);
   float ss = 0.f;
-  const float inv_world = 1.f / (float)a.world;
   for (long long i = blockIdx.x * (long long)kOptThreads + threadIdx.x; i < len;
        i += (long long)gridDim.x * kOptThreads) {
-    float g = 0.f;
-    for (int s = 0; s < a.world; ++s) g += __ldcg(a.grads[s] + base + i);
-    g *= inv_world;  // mean over ranks, as each rank's loss is a mean over its rows
-    a.red_grad[i] = g;
+    float g;
+    if (a.pre_reduced) {
+      g = a.red_grad[i];
+    } else {
+      g = rank_mean(a, base + i);
+      a.red_grad[i] = g;
+    }
     ss = fmaf(g, g, ss);
   }
   ss = block_sum(ss);
@@ -218,6 +230,49 @@ __global__ void __launch_bounds__(kOptThreads) dp_adamw_gather_kernel(DpArgs a) 
     for (int s = 0; s < a.world; ++s) st_release(a.peer_flag_params[s], epoch);
     *a.counter = 0u;
   }
+}
+
+// One gradient bucket (flat range [lo, hi)) of the reduce-scatter: after a
+// bounded wait until every rank released the bucket's flag for this epoch,
+// this rank sums its shard's part of the range over all ranks into red_grad.
+// Launched on a side stream while the backward still computes later buckets.
+__global__ void __launch_bounds__(kOptThreads) dp_reduce_range_kernel(DpArgs a, const int* flags, long long lo,
+                                                                     long long hi) {
+  const int epoch = *a.epoch_ptr;
+  if (!block_wait_all(flags, a.world, epoch, a.timeout_ns, a.status)) return;
+  const long long base = (long long)a.rank * a.shard;
+  long long end = a.n_total < base + a.shard ? a.n_total : base + a.shard;
+  if (hi < end) end = hi;
+  const long long begin = lo > base ? lo : base;
+  // 4 elements per thread and iteration when the range and the shard allow 16-byte loads
+  const bool vec = ((begin | end | base) & 3) == 0;
+  if (vec) {
+    const long long n4 = (end - begin) / 4;
+    for (long long j = blockIdx.x * (long long)kOptThreads + threadIdx.x; j < n4;
+         j += (long long)gridDim.x * kOptThreads) {
+      const long long i = begin + 4 * j;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int s = 0; s < a.world; ++s) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(a.grads[s] + i));
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
+      const float inv = 1.f / (float)a.world;
+      acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
+      *reinterpret_cast<float4*>(a.red_grad + (i - base)) = acc;
+    }
+  } else {
+    for (long long i = begin + blockIdx.x * (long long)kOptThreads + threadIdx.x; i < end;
+         i += (long long)gridDim.x * kOptThreads)
+      a.red_grad[i - base] = rank_mean(a, i);
+  }
+}
+
+cudaError_t dp_reduce_range(const DpArgs& a, const int* flags, long long lo, long long hi, int grid,
+                            cudaStream_t stream) {
+  if (a.world < 1 || a.world > kMaxShards || a.rank < 0 || a.rank >= a.world || grid < 1 || lo < 0 || hi < lo)
+    return cudaErrorInvalidValue;
+  dp_reduce_range_kernel<<<grid, kOptThreads, 0, stream>>>(a, flags, lo, hi);
+  return cudaGetLastError();
 }
 
 cudaError_t dp_reduce_norm(const DpArgs& a, int grid, cudaStream_t stream) {

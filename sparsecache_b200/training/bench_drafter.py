@@ -50,6 +50,10 @@ def main(argv=None) -> None:
     p.add_argument("--tc-linears", action="store_true",
                    help="frozen trunk projections on this package's tensor-core GEMMs instead of autograd's linears")
     p.add_argument("--no-k14", action="store_true", help="trunk self-attention on SDPA instead of the K14 kernels")
+    p.add_argument("--no-defer", action="store_true",
+                   help="adapter weight gradients through autograd (per position) instead of one GEMM per weight")
+    p.add_argument("--no-overlap", action="store_true",
+                   help="data parallel: one reduce-scatter after the backward instead of per-bucket overlap")
     p.add_argument("--small", action="store_true", help="tiny geometry (smoke runs)")
     args = p.parse_args(argv)
 
@@ -103,7 +107,8 @@ def main(argv=None) -> None:
         cos, sin = rope_cos_sin(target, torch.arange(args.prompt_tokens + args.horizon + 8), device=dev)
         train_bank_rows = args.samples
         tcfg = DrafterTrainConfig(global_batch=args.global_batch, use_graph=not args.no_graph,
-                                  tc_linears=args.tc_linears)
+                                  tc_linears=args.tc_linears, defer_weight_grads=not args.no_defer,
+                                  overlap_exchange=not args.no_overlap)
         trainer = EagleDrafterTrainer(model, _head(bank, train_bank_rows), cos, sin, tcfg, distributed=distributed)
         trainer.warmup_and_capture(warmup=max(1, args.warmup))
         if distributed:
@@ -144,11 +149,42 @@ def main(argv=None) -> None:
         e1.record()
         torch.cuda.synchronize(dev)
         opt_ms = e0.elapsed_time(e1) / 3
+        # the pieces of the overlapped exchange, each timed on its own: the deferred weight-gradient
+        # GEMMs, the bucketed reduce-scatter (side stream, joined) and the tail that stays exposed
+        # after the last bucket (clip + AdamW + all-gather)
+        parts = {}
+        if trainer.stash is not None:
+            ev = [torch.cuda.Event(True) for _ in range(2)]
+            ev[0].record()
+            for _ in range(3):
+                trainer.stash.finish()
+            ev[1].record()
+            torch.cuda.synchronize(dev)
+            parts["dw_gemms_ms"] = ev[0].elapsed_time(ev[1]) / 3
+        if distributed and getattr(trainer.opt, "buckets", None):
+            rs = tail = 0.0
+            for _ in range(3):
+                ev = [torch.cuda.Event(True) for _ in range(3)]
+                trainer.opt.begin_step()
+                ev[0].record()
+                for b in range(len(trainer.opt.buckets)):
+                    trainer.opt.bucket_ready(b)
+                torch.cuda.current_stream().wait_stream(trainer.opt.comm)
+                ev[1].record()
+                trainer.opt.step_reduced()
+                ev[2].record()
+                torch.cuda.synchronize(dev)
+                rs += ev[0].elapsed_time(ev[1]) / 3
+                tail += ev[1].elapsed_time(ev[2]) / 3
+            parts["bucketed_reduce_scatter_ms"] = rs
+            parts["exposed_tail_ms"] = tail
         if distributed:
             trainer.opt.check()
-            mt = torch.tensor([opt_ms], device=dev, dtype=torch.float64)
+            keys = sorted(parts)
+            mt = torch.tensor([opt_ms] + [parts[k] for k in keys], device=dev, dtype=torch.float64)
             dist.all_reduce(mt, op=dist.ReduceOp.MAX)
-            opt_ms = float(mt.item())
+            opt_ms = float(mt[0].item())
+            parts = {k: float(v) for k, v in zip(keys, mt[1:].tolist())}
         tokens = args.global_batch * trainer.horizon
         trainable = sum(p.numel() for p in model.adapter_parameters())
         if rank == 0:
@@ -167,8 +203,12 @@ def main(argv=None) -> None:
                            "inputs": "bank resident in HBM (larger than L2)"},
                 "final_loss": row["loss"], "grad_norm": row["grad_norm"],
                 "optimizer_exchange_ms": opt_ms,
-                "optimizer_exchange": ("peer-memory reduce-scatter + clip + AdamW + all-gather, after backward "
-                                       "(exposed)" if distributed else "fused clip + AdamW"),
+                "optimizer_exchange": ("peer-memory reduce-scatter + clip + AdamW + all-gather of the whole "
+                                       "buffer, timed alone" if distributed else "fused clip + AdamW"),
+                "weight_grads": "deferred: one GEMM per adapter weight" if trainer.stash is not None
+                                else "autograd, per position",
+                "exchange_overlap": bool(distributed and getattr(trainer.opt, "buckets", None)),
+                **parts,
                 "acceptance_4tok": {k: v["mean_accepted_prefix"] for k, v in evals.items()},
                 "teacher_forced_top1": {k: v["teacher_forced_top1"] for k, v in evals.items()},
                 "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9,

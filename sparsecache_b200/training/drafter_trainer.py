@@ -21,12 +21,17 @@ What is different is how a step runs:
     gradients accumulate into one flat fp32 buffer, so the optimizer is one
     fused AdamW kernel pair (global-norm clip + update, step count and
     learning rate on the device) instead of per-tensor launches;
+  * the adapter's memory projections form their weight gradients after the
+    recurrence, one tensor-core GEMM per weight over all positions with fp32
+    sums (``deferred_grad.py``), instead of 256 per-position products;
   * with several GPUs the flat gradient/parameter buffers are CUDA-IPC peer
     memory: each rank sums its 1/N shard of every peer's gradients in rank
-    order, all ranks agree on the clip coefficient, each rank runs AdamW on
-    its shard (ZeRO-1 optimizer state) and stores the result straight into
-    every peer's parameter buffer; flags with bounded waits order the
-    phases.  No NCCL call is on the step path;
+    order, bucket by bucket as the backward finishes them (everything
+    autograd wrote, then each deferred weight right after its GEMM, on a
+    side stream while the next GEMM runs), all ranks agree on the clip
+    coefficient, each rank runs AdamW on its shard (ZeRO-1 optimizer state)
+    and stores the result straight into every peer's parameter buffer; flags
+    with bounded waits order the phases.  No NCCL call is on the step path;
   * the whole step (gather of the batch from the bank, recurrent forward,
     loss, backward, optimizer, DP exchange) is captured once as a CUDA graph
     and replayed; the host only writes the next batch's indices;
@@ -82,6 +87,13 @@ class DrafterTrainConfig:
     # default: at 64 rows per recurrent position the library's single-kernel small GEMMs are
     # faster (8B width, B200: 570 vs 484 ms per step), see ops/linear.py
     tc_linears: bool = False
+    # the adapter's memory projections form their weight gradients after the recurrence, one
+    # tensor-core GEMM per weight (fp32 sums over all positions); with data parallelism each
+    # finished weight's reduce-scatter overlaps the next weight's GEMM (training/deferred_grad.py)
+    defer_weight_grads: bool = True
+    # with several GPUs: reduce each gradient bucket as soon as it is final (False: one
+    # reduce-scatter of the whole buffer after the backward, the A/B control)
+    overlap_exchange: bool = True
     seed: int = 0
 
     def to_dict(self) -> dict[str, Any]:
@@ -168,6 +180,7 @@ class FlatTrainables:
         self.param = alloc(self.padded)
         self.grad = alloc(self.padded)
         self.grad.zero_()
+        self.offsets: dict[int, tuple[int, int]] = {}  # id(param) -> (offset, numel)
         off = 0
         for p in self.params:
             k = p.numel()
@@ -175,10 +188,32 @@ class FlatTrainables:
             view.copy_(p.detach().float())
             p.data = view
             p.grad = self.grad[off:off + k].view_as(p)
+            self.offsets[id(p)] = (off, k)
             off += k
 
     def shard(self, world: int) -> int:
         return self.padded // world
+
+    def buckets(self, late: Sequence[nn.Parameter]) -> list[list[tuple[int, int]]]:
+        """Flat ranges of the exchange buckets: everything but ``late`` first, then each of ``late``.
+
+        Bucket 0 (gradients final when autograd's backward returns) is the
+        complement of the late parameters' ranges within the padded buffer;
+        bucket 1 + i is the range of ``late[i]``.
+        """
+        spans = sorted(self.offsets[id(p)] for p in late)
+        rest, cur = [], 0
+        for off, k in spans:
+            if off > cur:
+                rest.append((cur, off))
+            cur = off + k
+        if cur < self.padded:
+            rest.append((cur, self.padded))
+        out = [rest]
+        for p in late:
+            off, k = self.offsets[id(p)]
+            out.append([(off, off + k)])
+        return out
 
 
 class FusedAdamW:
@@ -250,10 +285,45 @@ class DataParallelAdamW(FusedAdamW):
         self.flag_ptrs = flag_ptrs
         self.epoch = torch.zeros(1, device=dev, dtype=torch.int32)
         self.status = torch.zeros(1, device=dev, dtype=torch.int32)
+        self.buckets: list[list[tuple[int, int]]] | None = None
 
     def _peer_flag(self, kind: int, peer: int) -> int:
         # flag block of ``peer``: [kind][source rank]
         return self.flag_ptrs[peer] + 4 * (kind * 8 + self.rank)
+
+    # -------------------------------------------- reduce-scatter overlapped with the backward
+    def enable_buckets(self, buckets: list[list[tuple[int, int]]], *, grid: int = 32) -> None:
+        """Reduce the gradient bucket by bucket as the backward finishes them.
+
+        ``buckets[b]`` lists flat ranges.  Each rank releases bucket b's flag
+        in every peer once its own gradients of the bucket are final
+        (``bucket_ready``); a side stream then waits (bounded) for every
+        rank's release and sums this rank's shard of the bucket, while the
+        main stream goes on with the backward.  ``grid`` CTAs per bucket
+        kernel leave the SMs to the backward's GEMMs.
+        """
+        nb = len(buckets)
+        self.buckets = buckets
+        self.bucket_buf, self.bucket_ptrs = self.group.shared(4 * 8 * nb)
+        self.bucket_flags = self.bucket_buf.view(torch.int32).view(nb, 8)
+        self.comm = torch.cuda.Stream(self.flat.param.device)
+        self.reduce_grid = grid
+
+    def bucket_ready(self, b: int) -> None:
+        x = ops.ext()
+        main = torch.cuda.current_stream()
+        x.signal_epoch([self.bucket_ptrs[p] + 4 * (b * 8 + self.rank) for p in range(self.world)], self.epoch, 0)
+        self.comm.wait_stream(main)
+        with torch.cuda.stream(self.comm):
+            for lo, hi in self.buckets[b]:
+                x.dp_reduce_range(self.world, self.rank, self.flat.padded, self.flat.shard(self.world),
+                                  self.grad_ptrs, self.bucket_flags[b], self.epoch, lo, hi, TIMEOUT_NS,
+                                  self.status, self.red_grad, self.reduce_grid)
+
+    def step_reduced(self) -> None:
+        """Clip + AdamW + all-gather after every bucket was reduced (joins the side stream)."""
+        torch.cuda.current_stream().wait_stream(self.comm)
+        self._dp_step(pre_reduced=True)
 
     def begin_step(self) -> None:
         """Advance the device epoch and wait until every rank's last update landed here."""
@@ -262,14 +332,17 @@ class DataParallelAdamW(FusedAdamW):
         x.wait_all(self.flags[16:24], self.world, self.epoch, -1, TIMEOUT_NS, self.status)
 
     def step(self) -> None:
-        x = ops.ext()
-        x.signal_epoch([self._peer_flag(0, p) for p in range(self.world)], self.epoch, 0)
-        x.dp_adamw_step(self.world, self.rank, self.flat.padded, self.flat.shard(self.world), self.grad_ptrs,
-                        self.param_ptrs, self.norm_ptrs, self.flags[0:8], self.flags[8:16],
-                        [self._peer_flag(1, p) for p in range(self.world)],
-                        [self._peer_flag(2, p) for p in range(self.world)], self.epoch, TIMEOUT_NS, self.status,
-                        self.red_grad, self.exp_avg, self.exp_avg_sq, self.hyper, self.state, self.partial,
-                        self.counter)
+        """Reduce-scatter of the whole gradient, clip, AdamW, all-gather (after the backward)."""
+        ops.ext().signal_epoch([self._peer_flag(0, p) for p in range(self.world)], self.epoch, 0)
+        self._dp_step(pre_reduced=False)
+
+    def _dp_step(self, *, pre_reduced: bool) -> None:
+        ops.ext().dp_adamw_step(
+            self.world, self.rank, self.flat.padded, self.flat.shard(self.world), self.grad_ptrs, self.param_ptrs,
+            self.norm_ptrs, self.flags[0:8], self.flags[8:16], [self._peer_flag(1, p) for p in range(self.world)],
+            [self._peer_flag(2, p) for p in range(self.world)], self.epoch, TIMEOUT_NS, self.status, self.red_grad,
+            self.exp_avg, self.exp_avg_sq, self.hyper, self.state, self.partial, self.counter,
+            pre_reduced=pre_reduced)
 
     def check(self) -> None:
         code = int(self.status.item())
@@ -332,6 +405,11 @@ class EagleDrafterTrainer:
             raise ValueError("the global batch must divide evenly over the ranks")
         self.local_batch = cfg.global_batch // self.world
         self.horizon = bank.horizon if cfg.window_tokens <= 0 else min(cfg.window_tokens, bank.horizon)
+        self.stash = None
+        if cfg.defer_weight_grads:
+            from .deferred_grad import defer_adapter_linears
+
+            self.stash = defer_adapter_linears(model, self.device)
         params = model.adapter_parameters()
         self.group = None
         if distributed:
@@ -344,6 +422,8 @@ class EagleDrafterTrainer:
             self.flat = FlatTrainables(params, world=self.world, alloc=lambda m: next(bufs)[:m])
             dist.broadcast(self.flat.param, src=0)  # identical start on every rank
             self.opt = DataParallelAdamW(self.flat, cfg, self.group, pptrs, gptrs)
+            if self.stash is not None and cfg.overlap_exchange:
+                self.opt.enable_buckets(self.flat.buckets([lin.weight for lin in self.stash.linears]))
             torch.cuda.synchronize(self.device)
             dist.barrier()
         else:
@@ -408,6 +488,8 @@ class EagleDrafterTrainer:
         mem = MemoryBatch(bank.mem_k, bank.mem_v, bank.idx, bank.n_vis, rows)
         two = lambda x: torch.cat((x, x))  # noqa: E731  (the contrast rows reuse the inputs)
         B = idx.shape[0]
+        if self.stash is not None:
+            self.stash.begin(2 * B, t)
         with torch.autocast("cuda", dtype=torch.bfloat16, enabled=self.device.type == "cuda"):
             feats = model.recurrent_forward(two(ids), two(seeds), mem, None, two(cos), two(sin), two(stage))
             if self.head is not None:
@@ -455,7 +537,17 @@ class EagleDrafterTrainer:
             base_contrast = F.relu(cfg.contrast_margin / 2 - pos_score + base_score).mean()
             loss = loss + cfg.contrast_weight * contrast + cfg.base_contrast_weight * base_contrast
         loss.backward()
-        self.opt.step()
+        if self.stash is None:
+            self.opt.step()
+        elif self.world > 1 and self.cfg.overlap_exchange:
+            # bucket 0 (every gradient autograd wrote) is final now; each deferred weight is
+            # final after its GEMM: its reduce-scatter runs on the side stream during the next GEMM
+            self.opt.bucket_ready(0)
+            self.stash.finish(on_weight=lambda k: self.opt.bucket_ready(1 + k))
+            self.opt.step_reduced()
+        else:
+            self.stash.finish()
+            self.opt.step()
         self.loss.copy_(loss.detach())
         comps["contrast_loss"] = contrast.detach()
         comps["base_contrast_loss"] = base_contrast.detach()
@@ -511,6 +603,10 @@ class EagleDrafterTrainer:
 
     def release(self) -> None:
         self._graph = None
+        from .deferred_grad import restore_linears
+
+        restore_linears(self.stash)
+        self.stash = None
         if self.group is not None:
             torch.cuda.synchronize(self.device)
             self.group.close()

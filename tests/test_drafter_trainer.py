@@ -158,3 +158,52 @@ def test_batch_indices_are_disjoint_across_ranks():
     tr.rank = 1
     b, _ = tr.batch_indices(0)
     assert not set(a) & set(b)
+
+
+def _trainer_with(defer: bool):
+    torch.manual_seed(0)
+    cfg = _cfg()
+    model = random_eagle_drafter(cfg, seed=0, std=0.2)
+    model.bind_target_embedding(torch.randn(cfg.target_vocab_size, cfg.target_hidden_size))
+    model.freeze_eagle()
+    configure_trainable_modules(model, train_fc=False, train_midlayer=False, adapter_scale_init=0.0)
+    bank = synthetic_bank(n_samples=8, horizon=5, n_layers=2, n_heads=2, n_seed=2, target_hidden=16, hidden=16,
+                          vocab=24, visible=6, prompt_tokens=30, topk=4, device="cpu", head_dim=8)
+    cos, sin = torch.randn(64, 8), torch.randn(64, 8)
+    tcfg = DrafterTrainConfig(lr=3e-2, global_batch=4, use_graph=False, feature_weight=0.5,
+                              defer_weight_grads=defer)
+    return model, EagleDrafterTrainer(model, bank, cos, sin, tcfg)
+
+
+def test_deferred_weight_gradients_equal_autograd():
+    """One GEMM per adapter weight after the recurrence == autograd's per-position sums."""
+    grads = {}
+    for defer in (False, True):
+        model, tr = _trainer_with(defer)
+        assert (tr.stash is not None) == defer
+        if defer:  # the four memory projections (2 layers x query/output) are deferred
+            assert len(tr.stash.linears) == 4
+        seen = []
+        tr.opt.step = lambda tr=tr, seen=seen: seen.append(tr.flat.grad.clone())  # keep the gradient, no update
+        tr.train_step()
+        grads[defer] = seen[0]
+        tr.release()
+        assert all(type(m) is torch.nn.Linear for m in (*model.memory_attention.query, *model.memory_attention.output))
+    a, b = grads[False], grads[True]
+    assert float(a.abs().max()) > 0
+    assert torch.allclose(a, b, rtol=1e-4, atol=1e-6), float((a - b).abs().max())
+
+
+def test_flat_buckets_cover_the_buffer_once():
+    _, tr = _trainer_with(True)
+    late = [lin.weight for lin in tr.stash.linears]
+    buckets = tr.flat.buckets(late)
+    assert len(buckets) == 1 + len(late)
+    cover = torch.zeros(tr.flat.padded, dtype=torch.int32)
+    for ranges in buckets:
+        for lo, hi in ranges:
+            cover[lo:hi] += 1
+    assert bool((cover == 1).all())
+    for p, ranges in zip(late, buckets[1:]):
+        (lo, hi), = ranges
+        assert hi - lo == p.numel() and p.grad.data_ptr() == tr.flat.grad[lo:].data_ptr()

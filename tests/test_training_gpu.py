@@ -153,7 +153,7 @@ def test_trainer_with_tc_linears_matches_library_linears(cuda_device):
     t2.release()
 
 
-def _small_setup(dev, seed=0, global_batch=4, use_graph=True, distributed=False, tc_linears=False):
+def _small_setup(dev, seed=0, global_batch=4, use_graph=True, distributed=False, tc_linears=False, defer=True):
     from sparsecache_b200.models.sparse_kv_eagle import SparseKVEagleConfig
     from sparsecache_b200.training.drafter_trainer import (DrafterTrainConfig, EagleDrafterTrainer,
                                                            prepare_for_training, random_eagle_drafter)
@@ -174,8 +174,42 @@ def _small_setup(dev, seed=0, global_batch=4, use_graph=True, distributed=False,
     pos = torch.arange(1024, dtype=torch.float32)[:, None] * torch.logspace(0, -4, 64)[None, :]
     cos = torch.cat((pos.cos(), pos.cos()), -1)
     sin = torch.cat((pos.sin(), pos.sin()), -1)
-    tcfg = DrafterTrainConfig(lr=1e-3, global_batch=global_batch, use_graph=use_graph, tc_linears=tc_linears)
+    tcfg = DrafterTrainConfig(lr=1e-3, global_batch=global_batch, use_graph=use_graph, tc_linears=tc_linears,
+                              defer_weight_grads=defer)
     return model, EagleDrafterTrainer(model, bank, cos, sin, tcfg, distributed=distributed)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (1024, 4096, 2048), (4096, 1024, 200)])
+def test_gemm_f32_matches_fp32_matmul(cuda_device, M, N, K):
+    """Tensor-core GEMM with an fp32 result (the deferred weight gradients) vs an fp32 matmul."""
+    from sparsecache_b200 import ops
+
+    g = torch.Generator(device=cuda_device).manual_seed(M + N + K)
+    a = torch.randn(M, K, device=cuda_device, generator=g).to(torch.bfloat16)
+    w = torch.randn(N, K, device=cuda_device, generator=g).to(torch.bfloat16)
+    out = torch.full((M, N), float("nan"), device=cuda_device)
+    ops.ext().gemm_f32(a, w, out)
+    ref = a.float() @ w.float().t()
+    err = ((out - ref).abs().max() / ref.abs().max()).item()
+    assert err < 1e-5, err
+
+
+def test_deferred_weight_gradients_match_autograd(cuda_device):
+    """Adapter weight gradients from one GEMM per weight after the recurrence vs autograd's per-position
+    products (bf16 sums over positions there, fp32 here)."""
+    grads = {}
+    for defer in (False, True):
+        model, tr = _small_setup(cuda_device, use_graph=False, defer=defer)
+        assert (tr.stash is not None) == defer
+        seen = []
+        tr.opt.step = lambda tr=tr, seen=seen: seen.append(tr.flat.grad.clone())
+        tr.train_step()
+        torch.cuda.synchronize()
+        grads[defer] = seen[0]
+        tr.release()
+    a, b = grads[False], grads[True]
+    rel = ((a - b).norm() / a.norm()).item()
+    assert a.norm().item() > 0 and rel < 1e-2, rel
 
 
 def test_graph_captured_trainer_matches_eager(cuda_device):
