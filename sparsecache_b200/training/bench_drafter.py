@@ -52,6 +52,8 @@ def main(argv=None) -> None:
     p.add_argument("--no-k14", action="store_true", help="trunk self-attention on SDPA instead of the K14 kernels")
     p.add_argument("--no-defer", action="store_true",
                    help="adapter weight gradients through autograd (per position) instead of one GEMM per weight")
+    p.add_argument("--nccl-control", action="store_true",
+                   help="data parallel: ncclAllReduce of the gradient after the backward (the control arm)")
     p.add_argument("--no-overlap", action="store_true",
                    help="data parallel: one reduce-scatter after the backward instead of per-bucket overlap")
     p.add_argument("--small", action="store_true", help="tiny geometry (smoke runs)")
@@ -108,7 +110,7 @@ def main(argv=None) -> None:
         train_bank_rows = args.samples
         tcfg = DrafterTrainConfig(global_batch=args.global_batch, use_graph=not args.no_graph,
                                   tc_linears=args.tc_linears, defer_weight_grads=not args.no_defer,
-                                  overlap_exchange=not args.no_overlap)
+                                  overlap_exchange=not args.no_overlap, nccl_exchange=args.nccl_control)
         trainer = EagleDrafterTrainer(model, _head(bank, train_bank_rows), cos, sin, tcfg, distributed=distributed)
         trainer.warmup_and_capture(warmup=max(1, args.warmup))
         if distributed:
@@ -122,7 +124,8 @@ def main(argv=None) -> None:
         torch.cuda.synchronize(dev)
         ms = t0.elapsed_time(t1) / args.steps
         if distributed:
-            trainer.opt.check()
+            if not trainer.nccl:
+                trainer.opt.check()
             mt = torch.tensor([ms], device=dev, dtype=torch.float64)
             dist.all_reduce(mt, op=dist.ReduceOp.MAX)
             ms = float(mt.item())
@@ -143,7 +146,9 @@ def main(argv=None) -> None:
         e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
         e0.record()
         for _ in range(3):
-            if distributed:
+            if trainer.nccl:
+                dist.all_reduce(trainer.flat.grad, op=dist.ReduceOp.AVG)
+            elif distributed:
                 trainer.opt.begin_step()
             trainer.opt.step()
         e1.record()
@@ -179,7 +184,8 @@ def main(argv=None) -> None:
             parts["bucketed_reduce_scatter_ms"] = rs
             parts["exposed_tail_ms"] = tail
         if distributed:
-            trainer.opt.check()
+            if not trainer.nccl:
+                trainer.opt.check()
             keys = sorted(parts)
             mt = torch.tensor([opt_ms] + [parts[k] for k in keys], device=dev, dtype=torch.float64)
             dist.all_reduce(mt, op=dist.ReduceOp.MAX)
@@ -203,7 +209,9 @@ def main(argv=None) -> None:
                            "inputs": "bank resident in HBM (larger than L2)"},
                 "final_loss": row["loss"], "grad_norm": row["grad_norm"],
                 "optimizer_exchange_ms": opt_ms,
-                "optimizer_exchange": ("peer-memory reduce-scatter + clip + AdamW + all-gather of the whole "
+                "optimizer_exchange": ("ncclAllReduce of the whole gradient + clip + AdamW on every rank, timed "
+                                       "alone" if trainer.nccl else
+                                       "peer-memory reduce-scatter + clip + AdamW + all-gather of the whole "
                                        "buffer, timed alone" if distributed else "fused clip + AdamW"),
                 "weight_grads": "deferred: one GEMM per adapter weight" if trainer.stash is not None
                                 else "autograd, per position",

@@ -94,6 +94,9 @@ class DrafterTrainConfig:
     # with several GPUs: reduce each gradient bucket as soon as it is final (False: one
     # reduce-scatter of the whole buffer after the backward, the A/B control)
     overlap_exchange: bool = True
+    # with several GPUs: the NCCL control instead of the peer-memory exchange (every rank keeps
+    # the whole buffer, ncclAllReduce of the flat gradient after the backward, AdamW everywhere)
+    nccl_exchange: bool = False
     seed: int = 0
 
     def to_dict(self) -> dict[str, Any]:
@@ -412,7 +415,12 @@ class EagleDrafterTrainer:
             self.stash = defer_adapter_linears(model, self.device)
         params = model.adapter_parameters()
         self.group = None
-        if distributed:
+        self.nccl = distributed and cfg.nccl_exchange
+        if self.nccl:
+            self.flat = FlatTrainables(params, device=self.device)
+            dist.broadcast(self.flat.param, src=0)
+            self.opt = FusedAdamW(self.flat, cfg)
+        elif distributed:
             self.group = _DPGroup()
             n = sum(p.numel() for p in params)
             padded = -(-n // (4 * self.world)) * (4 * self.world)
@@ -472,7 +480,7 @@ class EagleDrafterTrainer:
     # ------------------------------------------------------------ step body
     def _body(self) -> None:
         cfg, bank, model = self.cfg, self.bank, self.model
-        if self.world > 1:
+        if self.world > 1 and not self.nccl:
             self.opt.begin_step()
         self.flat.grad.zero_()
         t = self.horizon
@@ -537,7 +545,14 @@ class EagleDrafterTrainer:
             base_contrast = F.relu(cfg.contrast_margin / 2 - pos_score + base_score).mean()
             loss = loss + cfg.contrast_weight * contrast + cfg.base_contrast_weight * base_contrast
         loss.backward()
-        if self.stash is None:
+        if self.nccl:  # control: one NCCL all-reduce (mean) of the whole gradient, then AdamW on every rank
+            import torch.distributed as dist
+
+            if self.stash is not None:
+                self.stash.finish()
+            dist.all_reduce(self.flat.grad, op=dist.ReduceOp.AVG)
+            self.opt.step()
+        elif self.stash is None:
             self.opt.step()
         elif self.world > 1 and self.cfg.overlap_exchange:
             # bucket 0 (every gradient autograd wrote) is final now; each deferred weight is
@@ -629,7 +644,7 @@ class EagleDrafterTrainer:
         opt = ckpt.get("optimizer")
         if restore_optimizer and opt is not None and ckpt.get("world") == self.world:
             self.opt.load_state_dict(opt)
-            if self.world > 1:  # flags restart at epoch 0; the bias correction continues
+            if self.world > 1 and not self.nccl:  # flags restart at epoch 0; the bias correction continues
                 self.opt.hyper[6].fill_(float(opt["state"][0]))
         return ckpt
 
