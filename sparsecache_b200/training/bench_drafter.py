@@ -154,35 +154,16 @@ def main(argv=None) -> None:
         e1.record()
         torch.cuda.synchronize(dev)
         opt_ms = e0.elapsed_time(e1) / 3
-        # the pieces of the overlapped exchange, each timed on its own: the deferred weight-gradient
-        # GEMMs, the bucketed reduce-scatter (side stream, joined) and the tail that stays exposed
-        # after the last bucket (clip + AdamW + all-gather)
+        # the backward's tail as captured CUDA graphs (launch costs as inside the step): the deferred
+        # weight-gradient GEMMs alone, then the GEMMs followed by each exchange variant; the difference
+        # is the exchange time the step cannot hide
         parts = {}
         if trainer.stash is not None:
-            ev = [torch.cuda.Event(True) for _ in range(2)]
-            ev[0].record()
-            for _ in range(3):
-                trainer.stash.finish()
-            ev[1].record()
-            torch.cuda.synchronize(dev)
-            parts["dw_gemms_ms"] = ev[0].elapsed_time(ev[1]) / 3
-        if distributed and getattr(trainer.opt, "buckets", None):
-            rs = tail = 0.0
-            for _ in range(3):
-                ev = [torch.cuda.Event(True) for _ in range(3)]
-                trainer.opt.begin_step()
-                ev[0].record()
-                for b in range(len(trainer.opt.buckets)):
-                    trainer.opt.bucket_ready(b)
-                torch.cuda.current_stream().wait_stream(trainer.opt.comm)
-                ev[1].record()
-                trainer.opt.step_reduced()
-                ev[2].record()
-                torch.cuda.synchronize(dev)
-                rs += ev[0].elapsed_time(ev[1]) / 3
-                tail += ev[1].elapsed_time(ev[2]) / 3
-            parts["bucketed_reduce_scatter_ms"] = rs
-            parts["exposed_tail_ms"] = tail
+            tail = _tail_graph_ms(trainer, dev, distributed)
+            parts.update({f"tail_{k}_ms": v for k, v in tail.items()})
+            for k, v in tail.items():
+                if k != "dw_gemms":
+                    parts[f"exposed_{k}_ms"] = v - tail["dw_gemms"]
         if distributed:
             if not trainer.nccl:
                 trainer.opt.check()
@@ -226,6 +207,61 @@ def main(argv=None) -> None:
         if distributed:
             dist.barrier()
             dist.destroy_process_group()
+
+
+def _tail_graph_ms(trainer, dev, distributed: bool, reps: int = 10) -> dict[str, float]:
+    """Per-replay device time of the backward's tail variants, each captured once as a CUDA graph.
+
+    Every variant runs the same kernels on every rank in the same order (the
+    exchanges wait on each other across ranks); each replay also applies one
+    optimizer update, harmless after the timed steps.
+    """
+    import torch.distributed as dist
+
+    st, opt = trainer.stash, trainer.opt
+    variants = {"dw_gemms": lambda: st.finish()}
+    if trainer.nccl:
+        def nccl():
+            st.finish()
+            dist.all_reduce(trainer.flat.grad, op=dist.ReduceOp.AVG)
+            opt.step()
+        variants["nccl_allreduce"] = nccl
+    elif distributed:
+        def serial():
+            opt.begin_step()
+            st.finish()
+            opt.step()
+        variants["peer_serial"] = serial
+        if getattr(opt, "buckets", None):
+            def overlap():
+                opt.begin_step()
+                opt.bucket_ready(0)
+                st.finish(on_weight=lambda k: opt.bucket_ready(1 + k))
+                opt.step_reduced()
+            variants["peer_overlap"] = overlap
+    out = {}
+    for name, fn in variants.items():
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fn()  # eager once: workspaces and communicators exist before the capture
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        if distributed:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        out[name] = e0.elapsed_time(e1) / reps
+        del g
+    return out
 
 
 def _head(bank, n):
