@@ -20,6 +20,7 @@ same telemetry, used by the harness tests.
 from __future__ import annotations
 
 import json
+import math
 import threading
 import time
 from dataclasses import dataclass, field
@@ -159,10 +160,20 @@ class EngineWorker:
     """This package's engine on one GPU: prefill, first token, CUDA-graph decode.
 
     Both roles may run in one process on one GPU ("aggregated"): the decode
-    side then finds the prompt KV in the slot the prefill wrote.  Progressive
-    drafting uses the sparse-view decode of ``B200Engine.decode(view=...)``
-    followed by one batched verification.
+    side then holds the whole prompt's K/V after its own prefill, and the
+    link is modeled (one bundle per 256-token chunk, in the request's
+    priority order).  A progressive request drafts ``max_draft_tokens``
+    tokens as single-token forwards over a sparse view of the prompt (the
+    chunks that would have arrived: the first stage for ``fixed_s1``, one
+    more priority chunk per draft for ``continuous``), verifies
+    [seed, drafts] in one batched forward over the full prompt, and
+    continues with greedy decoding; the verifier's rows equal greedy
+    decoding's bit for bit, so every arm streams the same tokens.  The
+    scheduler and input-trace records are those the aggregator and the
+    trace verifier read (``ToyWorker`` writes the same).
     """
+
+    CHUNK = 256  # tokens per link bundle
 
     def __init__(self, engine, *, capacity: int = 32768, model_name: str = "sparsecache-b200",
                  telemetry: TelemetrySink | None = None) -> None:
@@ -171,34 +182,113 @@ class EngineWorker:
         self.engine, self.model_name = engine, model_name
         self.telemetry = telemetry or TelemetrySink()
         self.slot = engine.new_slot(capacity)
-        self._prompts: dict[str, tuple[list[int], int]] = {}
         self._torch = torch
         self._lock = threading.Lock()
+        cfg = engine.cfg
+        self.kv_bytes_per_token = cfg.n_layers * 2 * cfg.n_kv_heads * cfg.head_dim * 2
+
+    def _prefill_seed(self, prompt: Sequence[int], max_new: int) -> int:
+        torch = self._torch
+        ids = torch.tensor(list(prompt), dtype=torch.int32, device=self.engine.device)
+        h = self.engine.prefill(ids, self.slot)
+        b = self.engine.first_token(h[-1:], position=len(prompt), max_new=max_new)
+        return int(b["tok"][0].item())
 
     def prefill(self, request_id: str, prompt: Sequence[int]) -> int:
-        torch = self._torch
         with self._lock:
-            ids = torch.tensor(list(prompt), dtype=torch.int32, device=self.engine.device)
-            t0 = now_ns()
-            h = self.engine.prefill(ids, self.slot)
-            b = self.engine.first_token(h[-1:], position=len(prompt), max_new=1)
-            seed = int(b["tok"][0].item())
-            self.telemetry.emit("link", {"request_id": request_id, "bundles": [
-                {"index": 0, "chunks": list(range(-(-len(prompt) // 256))), "bytes": 0,
-                 "wire_ms": (now_ns() - t0) / 1e6}], "residual_modeled_wire_ms": 0.0})
-            self._prompts[request_id] = (list(prompt), seed)
-            return seed
+            return self._prefill_seed(prompt, 1)
+
+    def _chunk_order(self, s: DecodeSettings, n_chunks: int) -> list[int]:
+        order = [int(c) for c in (s.priority_chunks or range(n_chunks)) if 0 <= int(c) < n_chunks]
+        seen = set()
+        order = [c for c in order if not (c in seen or seen.add(c))]
+        return order + [c for c in range(n_chunks) if c not in seen]
+
+    def _link_trace(self, request_id: str, T: int, order: Sequence[int]) -> None:
+        bundles = [{"index": i, "chunks": [c], "wire_ms": 0.0,
+                    "bytes": (min(T, (c + 1) * self.CHUNK) - c * self.CHUNK) * self.kv_bytes_per_token}
+                   for i, c in enumerate(order)]
+        self.telemetry.emit("link", {"request_id": request_id, "bundles": bundles, "residual_modeled_wire_ms": 0.0})
+
+    def _continue(self, out: list[int], T: int, n: int) -> list[int]:
+        """Greedy decode after ``out`` (its last token's K/V not yet written) up to ``n`` tokens."""
+        eng = self.engine
+        if len(out) >= n:
+            return out[:n]
+        b = eng._decode_buffers(n)
+        b["ids"][:1].fill_(out[-1])
+        eng.ext.embedding(b["ids"][:1], eng.w.embed, b["h"][:1])
+        b["gen"].zero_()
+        eng.set_decode_state(position=T + len(out) - 1)
+        eng.decode(self.slot, n - len(out), max_new=n)
+        return out + eng.generated_tokens(n - len(out)).tolist()
+
+    def _progressive(self, request_id: str, prompt: Sequence[int], s: DecodeSettings, n: int,
+                     order: Sequence[int]) -> list[int]:
+        torch, eng, emit = self._torch, self.engine, self.telemetry.emit
+        p = s.progressive
+        T = len(prompt)
+        seed = int(p["seed_token_id"])
+        gamma = max(1, min(int(p["max_draft_tokens"]), eng.MAX_ROWS - 1))  # one verifier batch of gamma + 1 rows
+        mode = str(p["visibility_mode"])
+        n_chunks = len(order)
+        first = max(1, min(n_chunks, math.ceil(float(p["start_fraction"]) * n_chunks)))
+        view = torch.zeros(self.slot.capacity, dtype=torch.int32, device=eng.device)
+        started = now_ns()
+        drafts, done_at = [], []
+        tok = seed
+        for i in range(gamma):
+            k = first if mode == "fixed_s1" else min(n_chunks, first + i)
+            vis = sorted(t for c in order[:k] for t in range(c * self.CHUNK, min(T, (c + 1) * self.CHUNK)))
+            view[: len(vis) + i].copy_(torch.tensor(vis + list(range(T, T + i)), dtype=torch.int32))
+            t_in = now_ns()
+            pred = eng.verify(self.slot, torch.tensor([tok], dtype=torch.int32), position=T + i, slot_start=T + i,
+                              view=view, n_visible=len(vis) + i)
+            emit("input_trace", {"request_id": request_id, "recorded_at_ns": t_in, "input_token_ids": [tok],
+                                 "positions": [T + i], "num_scheduled_tokens": 1})
+            tok = int(pred[0].item())
+            drafts.append(tok)
+            done_at.append(now_ns())
+        last_draft = now_ns()
+        full_arrival = now_ns()  # aggregated: the whole prompt's K/V is resident
+        verify_start = now_ns()
+        seq = [seed] + drafts
+        t_in = now_ns()
+        preds = eng.verify(self.slot, torch.tensor(seq, dtype=torch.int32), position=T, slot_start=T).tolist()
+        emit("input_trace", {"request_id": request_id, "recorded_at_ns": t_in, "input_token_ids": seq,
+                             "positions": list(range(T, T + len(seq))), "num_scheduled_tokens": len(seq)})
+        verify_done = now_ns()
+        accepted = 0
+        for d, t in zip(drafts, preds):
+            if d != t:
+                break
+            accepted += 1
+        out = [seed] + drafts[:accepted] + [int(preds[accepted])]
+        emit("scheduler", {
+            "request_id": request_id, "seed_token_id": seed, "draft_token_ids": drafts, "draft_tokens": gamma,
+            "max_draft_tokens": gamma, "accepted_tokens": accepted, "visibility_mode": mode,
+            "priority_chunks": s.priority_chunks,
+            "transitions": ["WAIT_ANCHOR", "DRAFT_WHILE_LOADING", "READY_TO_VERIFY", "TARGET_DECODING", "FINISHED"],
+            "started_at_ns": started, "draft_completed_at_ns": done_at, "last_draft_at_ns": last_draft,
+            "full_arrival_at_ns": full_arrival, "verify_started_at_ns": verify_start,
+            "verify_completed_at_ns": verify_done, "verify_ns": verify_done - verify_start})
+        return self._continue(out, T, n)
 
     def decode(self, request_id: str, prompt: Sequence[int], s: DecodeSettings) -> Iterator[int]:
-        torch = self._torch
         with self._lock:
             n = max(1, s.max_tokens)
-            h = self.engine.prefill(torch.tensor(list(prompt), dtype=torch.int32, device=self.engine.device),
-                                    self.slot)
-            self.engine.first_token(h[-1:], position=len(prompt), max_new=n)
-            if n > 1:
-                self.engine.decode(self.slot, n - 1, max_new=n)
-            toks = self.engine.generated_tokens(n).cpu().tolist()
+            T = len(prompt)
+            order = self._chunk_order(s, max(1, -(-T // self.CHUNK)))
+            seed = self._prefill_seed(prompt, n)  # stands for the transferred prompt K/V
+            if s.progressive is None:
+                if n > 1:
+                    self.engine.decode(self.slot, n - 1, max_new=n)
+                toks = self.engine.generated_tokens(n).cpu().tolist()
+            else:
+                if int(s.progressive["seed_token_id"]) != seed:
+                    raise RuntimeError("the producer seed differs from this worker's prefill")
+                toks = self._progressive(request_id, prompt, s, n, order)
+            self._link_trace(request_id, T, order)
         yield from toks
 
 

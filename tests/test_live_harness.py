@@ -395,3 +395,118 @@ def test_pd_pipeline_exclusive_gpu_check(monkeypatch):
     monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "1,0")
     with pytest.raises(SystemExit, match="GPU 1 is not exclusive"):
         exclusive_gpu_or_exit(command_runner=runner)
+
+
+class _FakeEngine:
+    """Host stand-in of the engine calls ``EngineWorker`` makes (greedy rule of the toy worker).
+
+    A row with input token t at position q predicts (31 t + 7 q + S) % V, where S sums the prompt
+    tokens the row can see: the whole prompt, or the visible ones of a sparse view (so sparse
+    drafts can differ from the verifier while verified rows equal greedy decoding).
+    """
+
+    MAX_ROWS = 8
+    V = 1000
+
+    def __init__(self):
+        import torch
+        from types import SimpleNamespace
+
+        self.torch = torch
+        self.device = torch.device("cpu")
+        self.cfg = SimpleNamespace(n_layers=2, n_kv_heads=2, head_dim=8)
+        self.w = SimpleNamespace(embed=None)
+        self.ext = SimpleNamespace(embedding=lambda ids, table, h: None)
+        self.prompt = []
+        self.b = {k: torch.zeros(64, dtype=torch.int64) for k in ("ids", "tok", "log")}
+        self.b["h"] = torch.zeros(1)
+        self.b["gen"] = torch.zeros(1, dtype=torch.int64)
+        self.pos = 0
+
+    def new_slot(self, capacity):
+        from types import SimpleNamespace
+
+        return SimpleNamespace(capacity=capacity)
+
+    def _rule(self, t, q, s):
+        return (31 * int(t) + 7 * int(q) + s) % self.V
+
+    def prefill(self, ids, slot):
+        self.prompt = [int(x) for x in ids.tolist()]
+        return self.torch.zeros(len(self.prompt), 1)
+
+    def first_token(self, h, position, max_new):
+        tok = (sum(self.prompt) * 13 + len(self.prompt)) % self.V
+        self.b["tok"][0] = tok
+        self.b["log"][0] = tok
+        self.b["gen"][0] = 1
+        self.b["ids"][0] = tok
+        self.pos = position
+        return self.b
+
+    def _decode_buffers(self, n=0):
+        return self.b
+
+    def set_decode_state(self, *, position, slot=None, n_virtual=None):
+        self.pos = position
+
+    def decode(self, slot, n_steps, *, max_new, use_graph=True):
+        s = sum(self.prompt)
+        tok = int(self.b["ids"][0])
+        for _ in range(n_steps):
+            tok = self._rule(tok, self.pos, s)
+            self.b["log"][int(self.b["gen"][0])] = tok
+            self.b["gen"][0] += 1
+            self.b["ids"][0] = tok
+            self.pos += 1
+
+    def generated_tokens(self, n):
+        return self.b["log"][:n]
+
+    def verify(self, slot, tokens, *, position, slot_start=None, view=None, n_visible=None):
+        T = len(self.prompt)
+        if view is None:
+            s = sum(self.prompt)
+        else:
+            s = sum(self.prompt[int(i)] for i in view[:n_visible].tolist() if int(i) < T)
+        return self.torch.tensor([self._rule(t, position + j, s) for j, t in enumerate(tokens.tolist())])
+
+
+def test_engine_worker_progressive_chain_on_a_host_engine(tmp_path):
+    """EngineWorker's draft / verify / continue logic and telemetry pass the aggregator's gates and the
+    input-trace audit, and its progressive arms stream the baseline's tokens."""
+    from sparsecache_b200.serving.live.worker import EngineWorker
+
+    sink = TelemetrySink(tmp_path / "telemetry")
+    worker = EngineWorker(_FakeEngine(), capacity=4096, telemetry=sink)
+    cfg = proxy.ProxyConfig(max_draft_tokens=6)
+    holder = {}
+    apps = {cfg.prefiller_url: make_app(worker, "prefill", notify=lambda rid: holder["proxy"].notify(rid)),
+            cfg.decoder_url: make_app(worker, "decode")}
+    px = proxy.Proxy(cfg, client_factory=lambda url: httpx.AsyncClient(transport=httpx.ASGITransport(app=apps[url]),
+                                                                      base_url=url))
+    holder["proxy"] = px
+    reqs = [{"model": "m", "prompt": [(37 * j + 11 * i) % 900 + 1 for j in range(600 + 150 * i)], "max_tokens": 12,
+             "temperature": 0} for i in range(3)]
+    arms = ("baseline", "fixed_s1", "continuous")
+
+    async def go():
+        async with httpx.AsyncClient(transport=httpx.ASGITransport(app=px.app), base_url="http://proxy") as c:
+            return await client.run_benchmark(c, "/v1/completions", reqs, arms, warmup=1,
+                                              output=tmp_path / "results.jsonl", run_id="fake")
+
+    records, summ = asyncio.run(go())
+    assert summ["pairs"] == 3
+    assert all(v["token_equality_rate"] == 1.0 for v in summ["comparisons"].values())
+    meta = [{"request_index": i, "dataset": "hotpotqa", "answers": ["x"]} for i in range(3)]
+    summary, _ = aggregate.aggregate_live_run(
+        records, meta, sink.records["scheduler"], sink.records["link"], arms=arms, expected_requests=3,
+        fixed_output_tokens=12, bootstrap_samples=200, seed=0, protected_chunks=1)
+    failed = {k: v for k, v in summary["gates"].items() if not v["passed"]}
+    assert not failed, failed
+    sched = sink.records["scheduler"]
+    assert {s["visibility_mode"] for s in sched} == {"fixed_s1", "continuous"}
+    assert all(s["draft_tokens"] == 6 for s in sched)
+    assert any(s["accepted_tokens"] < 6 for s in sched)  # sparse views do change some drafts
+    rep = trace.verify_input_trace(sched, sink.records["input_trace"], expected_requests=len(sched))
+    assert rep["status"] == "passed" and rep["verify_forwards"] == len(sched)
