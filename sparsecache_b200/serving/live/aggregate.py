@@ -10,7 +10,9 @@ wire time (:527-602); paired comparisons with bootstrap CIs (:605-685); and
 the validity gates of a run (:688-1130):
   complete_paired_matrix, request_protocol, single_paired_prefill,
   fixed_output_horizon, one_scheduler_transition_per_method,
-  scheduler_transition_invariants, fair_controlled_link,
+  scheduler_transition_invariants, request_attributed_sparse_attention
+  (the per-step sparse-view records of every progressive request, :416-504),
+  fair_controlled_link,
   protected_anchor_arrival, request_scoped_priority_schedule,
   latency_model_telemetry, exact_greedy_output_equivalence, overall.
 Quality is scored with the LongBench metrics of the request's dataset.
@@ -145,12 +147,76 @@ def _scheduler_errors(s: dict, result: dict) -> list[str]:
     return errs
 
 
+def sparse_attention_summary(rows: Sequence[dict], scheduler: dict, arm: str) -> tuple[dict, list[str]]:
+    """Check and summarise the sparse-view records of one progressive request.
+
+    Every draft step 0 .. draft_tokens-1 has records (one per layer, or one
+    covering ``layers`` layers) carrying the request's id, the arm as
+    visibility mode, the visible fraction, the exact visible token ranges and
+    visible / candidate page counts; the records of a step agree.  A
+    ``continuous`` view never shrinks (fraction, pages, token ranges); a
+    ``fixed_s1`` view keeps one partial snapshot.
+    """
+    errs: list[str] = []
+    if any(r.get("request_id") != scheduler.get("request_id") for r in rows):
+        errs.append("sparse-attention record of another request")
+    if any(r.get("visibility_mode") != arm for r in rows):
+        errs.append("sparse-attention visibility mode differs from the arm")
+    by_step: dict[int, list[dict]] = {}
+    for r in rows:
+        st = r.get("decode_step")
+        if not isinstance(st, int) or isinstance(st, bool) or st < 0:
+            errs.append("invalid sparse-attention decode step")
+            continue
+        by_step.setdefault(st, []).append(r)
+    n_draft = scheduler.get("draft_tokens")
+    if not isinstance(n_draft, int) or set(by_step) != set(range(n_draft)):
+        errs.append("sparse-attention steps do not cover the scheduler's draft tokens exactly")
+    steps, prev, partial = [], None, set()
+    for st in sorted(by_step):
+        snaps = {(float(r.get("visible_fraction", -1.0)), json.dumps(r.get("visible_token_ranges")),
+                  r.get("candidate_pages"), r.get("visible_pages")) for r in by_step[st]}
+        if len(snaps) != 1:
+            errs.append(f"step {st}: records disagree on the view")
+        frac, ranges_json, cand, vis = next(iter(snaps))
+        ranges = json.loads(ranges_json) if ranges_json != "null" else None
+        if not isinstance(cand, int) or not isinstance(vis, int) or cand <= 0 or not 0 <= vis <= cand:
+            errs.append(f"step {st}: invalid page counts")
+            continue
+        if not 0.0 < frac <= 1.0:
+            errs.append(f"step {st}: visible fraction outside (0, 1]")
+        if not isinstance(ranges, list) or any(not isinstance(x, list) or len(x) != 2 or not x[0] < x[1]
+                                               for x in ranges):
+            errs.append(f"step {st}: invalid visible token ranges")
+            continue
+        tokens = {t for lo, hi in ranges for t in range(int(lo), int(hi))}
+        if arm == "continuous" and prev is not None:
+            if frac < prev[0] or vis < prev[1] or not prev[2] <= tokens:
+                errs.append(f"step {st}: the continuous view shrank")
+        if arm == "fixed_s1" and frac < 1.0:
+            partial.add((frac, ranges_json, vis))
+        prev = (frac, vis, tokens)
+        steps.append({"decode_step": st, "records": len(by_step[st]), "visible_fraction": frac,
+                      "visible_pages": vis, "candidate_pages": cand})
+    if len(partial) > 1:
+        errs.append("the fixed first-stage view changed between steps")
+    sparse = sum(x["visible_pages"] < x["candidate_pages"] for x in steps)
+    return {"steps": len(steps), "sparse_steps": sparse, "sparse_step_rate": sparse / len(steps) if steps else 0.0,
+            "distinct_visible_fractions": len({x["visible_fraction"] for x in steps}),
+            "first_visible_fraction": steps[0]["visible_fraction"] if steps else None,
+            "last_visible_fraction": steps[-1]["visible_fraction"] if steps else None}, errs
+
+
 def aggregate_live_run(results: Sequence[dict], metadata: Sequence[dict], scheduler_rows: Sequence[dict],
                        link_rows: Sequence[dict], *, arms: Sequence[str], expected_requests: int,
                        fixed_output_tokens: int | None = None, bootstrap_samples: int = 10000, seed: int = 0,
                        priority_rows: Sequence[dict] | None = None, protected_chunks: int = 0,
-                       enforce_paired_prefill: bool = True):
-    """(summary with gates, paired rows) of one live run."""
+                       enforce_paired_prefill: bool = True, attention_rows: Sequence[dict] = ()):
+    """(summary with gates, paired rows) of one live run.
+
+    ``attention_rows`` are the workers' request-attributed sparse-view records;
+    a progressive request without them fails ``request_attributed_sparse_attention``.
+    """
     arms = tuple(arms)
     if expected_requests <= 0 or bootstrap_samples <= 0:
         raise ValueError("expected requests and bootstrap samples must be positive")
@@ -195,6 +261,10 @@ def aggregate_live_run(results: Sequence[dict], metadata: Sequence[dict], schedu
     link_by = {}
     for ln in link_rows:
         link_by.setdefault(str(ln.get("request_id", "")), []).append(ln)
+    attn_by: dict[str, list[dict]] = {}
+    for at in attention_rows:
+        attn_by.setdefault(str(at.get("request_id", "")), []).append(at)
+    attn_errors, with_attention = [], 0
     prefill_errors, sched_errors, link_errors, anchor_errors, priority_errors, model_errors = [], [], [], [], [], []
     horizon_errors, one_sched, method_records = [], 0, 0
     groups_seen: set[str] = set()
@@ -244,6 +314,14 @@ def aggregate_live_run(results: Sequence[dict], metadata: Sequence[dict], schedu
                     one_sched += 1
                     e["scheduler"] = sch[0]
                     sched_errors += [f"{i}/{arm}: {x}" for x in _scheduler_errors(sch[0], r)]
+                    attn = attn_by.get(str(sch[0].get("request_id", "")), [])
+                    if attn:
+                        with_attention += 1
+                        e["attention"], errs = sparse_attention_summary(attn, sch[0], arm)
+                        attn_errors += [f"{i}/{arm}: {x}" for x in errs]
+                    else:
+                        e["attention"] = None
+                        attn_errors.append(f"{i}/{arm}: no request-attributed sparse-attention records")
                     if i in priorities and sch[0].get("priority_chunks") != priorities[i]:
                         priority_errors.append(f"{i}/{arm}: scheduler priority differs from the sidecar")
                 else:
@@ -268,6 +346,9 @@ def aggregate_live_run(results: Sequence[dict], metadata: Sequence[dict], schedu
         "one_scheduler_transition_per_method": gate(one_sched == method_records, records=method_records,
                                                     with_one_scheduler=one_sched),
         "scheduler_transition_invariants": gate(not sched_errors, errors=sched_errors),
+        "request_attributed_sparse_attention": gate(with_attention == method_records and not attn_errors,
+                                                    records=method_records, with_attention=with_attention,
+                                                    errors=attn_errors),
         "fair_controlled_link": gate(not link_errors, errors=link_errors),
         "protected_anchor_arrival": gate(not anchor_errors, errors=anchor_errors),
         "request_scoped_priority_schedule": gate(not priority_errors, errors=priority_errors),
@@ -319,7 +400,7 @@ def write_artifacts(out_dir: Path, summary: dict, rows: Sequence[dict]) -> None:
 
 
 def main(argv=None) -> int:
-    """Aggregate one live run directory (results / metadata / scheduler / link JSONL) into gated artifacts.
+    """Aggregate one live run directory (results / metadata / scheduler / link / attention JSONL) into gated artifacts.
 
     Counterpart of the reference's experiments/aggregate_progressive_pd_live.py CLI;
     exits 1 when a validity gate fails (the artifacts are written either way).
@@ -333,6 +414,8 @@ def main(argv=None) -> int:
     p.add_argument("--metadata", type=Path, required=True)
     p.add_argument("--scheduler-trace", type=Path, required=True)
     p.add_argument("--link-trace", type=Path, required=True)
+    p.add_argument("--attention-trace", type=Path, required=True,
+                   help="workers' sparse-view records (attention.jsonl)")
     p.add_argument("--arms", default="baseline,fixed_s1,continuous")
     p.add_argument("--expected-requests", type=int, required=True)
     p.add_argument("--fixed-output-tokens", type=int, default=None)
@@ -347,7 +430,7 @@ def main(argv=None) -> int:
         arms=a.arms.split(","), expected_requests=a.expected_requests, fixed_output_tokens=a.fixed_output_tokens,
         bootstrap_samples=a.bootstrap_samples, seed=a.seed,
         priority_rows=load_jsonl(a.priority_jsonl) if a.priority_jsonl else None,
-        protected_chunks=a.protected_chunks)
+        protected_chunks=a.protected_chunks, attention_rows=load_jsonl(a.attention_trace))
     write_artifacts(a.output_dir, summary, rows)
     print(json.dumps({"status": summary["status"], "output_dir": str(a.output_dir)}))
     return 0 if summary["status"] == "passed" else 1

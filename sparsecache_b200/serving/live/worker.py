@@ -8,8 +8,9 @@ A worker process serves one role of a 1P1D deployment:
   * ``decode``: given the prompt and the proxy-owned ``kv_transfer_params``
     (the producer seed token, progressive-draft settings, the request's chunk
     priority), streams the greedy continuation as server-sent events, one
-    token per event, and appends scheduler / input-trace records to JSONL
-    telemetry files for the aggregator and the trace verifier.
+    token per event, and appends scheduler / input-trace / sparse-attention
+    (the prompt view each draft step read) records to JSONL telemetry files
+    for the aggregator and the trace verifier.
 
 The HTTP contract is the one the reference's vLLM/LMCache workers expose to
 its proxy (experiments/progressive_pd_proxy.py:123-214), so the same proxy
@@ -68,6 +69,36 @@ class TelemetrySink:
                     f.write(json.dumps(row) + "\n")
 
 
+def visibility_snapshot(prompt_tokens: int, order: Sequence[int], k: int, chunk: int) -> dict:
+    """The prompt view after the first ``k`` chunks of ``order`` arrived: merged [lo, hi) token ranges,
+    visible token fraction, visible / candidate chunk counts."""
+    n_chunks = max(1, -(-prompt_tokens // chunk))
+    vis = sorted({int(c) for c in order[:k] if 0 <= int(c) < n_chunks})
+    ranges: list[list[int]] = []
+    for c in vis:
+        lo, hi = c * chunk, min(prompt_tokens, (c + 1) * chunk)
+        if ranges and ranges[-1][1] == lo:
+            ranges[-1][1] = hi
+        else:
+            ranges.append([lo, hi])
+    seen = sum(hi - lo for lo, hi in ranges)
+    return {"visible_token_ranges": ranges, "visible_fraction": seen / max(1, prompt_tokens),
+            "visible_pages": len(vis), "candidate_pages": n_chunks}
+
+
+def emit_attention_step(telemetry: "TelemetrySink", request_id: str, mode: str, step: int, snapshot: dict,
+                        layers: int) -> None:
+    """One request-attributed record of the view a sparse draft step attended to (every layer reads it)."""
+    telemetry.emit("attention", {"request_id": request_id, "visibility_mode": mode, "decode_step": step,
+                                 "layers": layers, **snapshot})
+
+
+def stage_chunks(mode: str, start_fraction: float, n_chunks: int, step: int) -> int:
+    """Chunks visible to draft ``step``: the first stage for ``fixed_s1``, one more per step for ``continuous``."""
+    first = max(1, min(n_chunks, math.ceil(float(start_fraction) * n_chunks)))
+    return first if mode == "fixed_s1" else min(n_chunks, first + step)
+
+
 class ToyWorker:
     """Deterministic greedy "model" on the CPU with the real worker's telemetry.
 
@@ -114,10 +145,15 @@ class ToyWorker:
         target = out[1:gamma + 1] + [0] * max(0, gamma + 1 - len(out))
         drafts = [t if i < accept else (t + 1) % self.vocab for i, t in enumerate(target[:gamma])]
         pos0 = len(prompt)
+        n_chunks = max(1, -(-pos0 // 256))
+        order = list(s.priority_chunks or range(n_chunks))
         t = now_ns()
         started = t
         for i, tok in enumerate([seed] + drafts[:-1]):
             t += 1000
+            k = stage_chunks(s.progressive["visibility_mode"], s.progressive["start_fraction"], n_chunks, i)
+            emit_attention_step(self.telemetry, request_id, s.progressive["visibility_mode"], i,
+                                visibility_snapshot(pos0, order, k, 256), layers=1)
             self.telemetry.emit("input_trace", {"request_id": request_id, "recorded_at_ns": t,
                                                 "input_token_ids": [tok], "positions": [pos0 + i],
                                                 "num_scheduled_tokens": 1})
@@ -232,14 +268,14 @@ class EngineWorker:
         gamma = max(1, min(int(p["max_draft_tokens"]), eng.MAX_ROWS - 1))  # one verifier batch of gamma + 1 rows
         mode = str(p["visibility_mode"])
         n_chunks = len(order)
-        first = max(1, min(n_chunks, math.ceil(float(p["start_fraction"]) * n_chunks)))
         view = torch.zeros(self.slot.capacity, dtype=torch.int32, device=eng.device)
         started = now_ns()
         drafts, done_at = [], []
         tok = seed
         for i in range(gamma):
-            k = first if mode == "fixed_s1" else min(n_chunks, first + i)
-            vis = sorted(t for c in order[:k] for t in range(c * self.CHUNK, min(T, (c + 1) * self.CHUNK)))
+            snap = visibility_snapshot(T, order, stage_chunks(mode, p["start_fraction"], n_chunks, i), self.CHUNK)
+            emit_attention_step(self.telemetry, request_id, mode, i, snap, layers=eng.cfg.n_layers)
+            vis = [t for lo, hi in snap["visible_token_ranges"] for t in range(lo, hi)]
             view[: len(vis) + i].copy_(torch.tensor(vis + list(range(T, T + i)), dtype=torch.int32))
             t_in = now_ns()
             pred = eng.verify(self.slot, torch.tensor([tok], dtype=torch.int32), position=T + i, slot_start=T + i,

@@ -47,7 +47,8 @@ def test_live_chain_with_engine_workers(tmp_path, cuda_device):
     meta = [{"request_index": i, "dataset": "hotpotqa", "answers": ["x"]} for i in range(3)]
     summary, _ = aggregate.aggregate_live_run(
         records, meta, sink.records["scheduler"], sink.records["link"], arms=arms, expected_requests=3,
-        fixed_output_tokens=12, bootstrap_samples=200, seed=0, protected_chunks=1)
+        fixed_output_tokens=12, bootstrap_samples=200, seed=0, protected_chunks=1,
+        attention_rows=sink.records["attention"])
     failed = {k: v for k, v in summary["gates"].items() if not v["passed"]}
     assert not failed, failed
     # every progressive request: gamma single-token sparse forwards, then one verifier batch

@@ -177,7 +177,8 @@ def test_full_chain_paired_run_aggregate_and_trace(tmp_path):
     assert sorted(reused) == [False, True, True]  # one producer prefill per paired execution
     meta = [{"request_index": i, "dataset": "hotpotqa", "answers": ["x"]} for i in range(4)]
     summary, rows = aggregate.aggregate_live_run(
-        records, meta, sink.records["scheduler"], sink.records["link"], arms=("baseline", "fixed_s1", "continuous"),
+        records, meta, sink.records["scheduler"], sink.records["link"], attention_rows=sink.records["attention"],
+        arms=("baseline", "fixed_s1", "continuous"),
         expected_requests=4, fixed_output_tokens=12, bootstrap_samples=200, seed=0, protected_chunks=1)
     failed = {k: v for k, v in summary["gates"].items() if not v["passed"]}
     # the warm-up execution's scheduler/link records belong to other proxy ids; all gates hold
@@ -185,11 +186,13 @@ def test_full_chain_paired_run_aggregate_and_trace(tmp_path):
     aggregate.write_artifacts(tmp_path / "agg", summary, rows)
     assert (tmp_path / "agg" / "paper_table.csv").exists()
     # the same run through the aggregator's command line
-    for name, recs in (("meta", meta), ("sched", sink.records["scheduler"]), ("link", sink.records["link"])):
+    for name, recs in (("meta", meta), ("sched", sink.records["scheduler"]), ("link", sink.records["link"]),
+                       ("attn", sink.records["attention"])):
         (tmp_path / f"{name}.jsonl").write_text("".join(json.dumps(r) + "\n" for r in recs))
     rc = aggregate.main(["--results", str(tmp_path / "results.jsonl"), "--metadata", str(tmp_path / "meta.jsonl"),
                          "--scheduler-trace", str(tmp_path / "sched.jsonl"), "--link-trace",
-                         str(tmp_path / "link.jsonl"), "--expected-requests", "4", "--fixed-output-tokens", "12",
+                         str(tmp_path / "link.jsonl"), "--attention-trace", str(tmp_path / "attn.jsonl"),
+                         "--expected-requests", "4", "--fixed-output-tokens", "12",
                          "--bootstrap-samples", "200", "--protected-chunks", "1", "--output-dir",
                          str(tmp_path / "agg_cli")])
     assert rc == 0 and (tmp_path / "agg_cli" / "summary.md").exists()
@@ -499,14 +502,41 @@ def test_engine_worker_progressive_chain_on_a_host_engine(tmp_path):
     assert summ["pairs"] == 3
     assert all(v["token_equality_rate"] == 1.0 for v in summ["comparisons"].values())
     meta = [{"request_index": i, "dataset": "hotpotqa", "answers": ["x"]} for i in range(3)]
-    summary, _ = aggregate.aggregate_live_run(
+    summary, rows = aggregate.aggregate_live_run(
         records, meta, sink.records["scheduler"], sink.records["link"], arms=arms, expected_requests=3,
-        fixed_output_tokens=12, bootstrap_samples=200, seed=0, protected_chunks=1)
+        fixed_output_tokens=12, bootstrap_samples=200, seed=0, protected_chunks=1,
+        attention_rows=sink.records["attention"])
     failed = {k: v for k, v in summary["gates"].items() if not v["passed"]}
     assert not failed, failed
+    for row in rows:  # continuous views grow over the steps, the fixed first stage does not
+        assert row["arms"]["continuous"]["attention"]["distinct_visible_fractions"] > 1
+        assert row["arms"]["fixed_s1"]["attention"]["distinct_visible_fractions"] == 1
     sched = sink.records["scheduler"]
     assert {s["visibility_mode"] for s in sched} == {"fixed_s1", "continuous"}
     assert all(s["draft_tokens"] == 6 for s in sched)
     assert any(s["accepted_tokens"] < 6 for s in sched)  # sparse views do change some drafts
     rep = trace.verify_input_trace(sched, sink.records["input_trace"], expected_requests=len(sched))
     assert rep["status"] == "passed" and rep["verify_forwards"] == len(sched)
+
+
+def test_sparse_attention_gate_rejects_bad_views():
+    sched = {"request_id": "r", "draft_tokens": 3}
+
+    def rec(step, frac, ranges, vis, mode="continuous", rid="r"):
+        return {"request_id": rid, "visibility_mode": mode, "decode_step": step, "visible_fraction": frac,
+                "visible_token_ranges": ranges, "visible_pages": vis, "candidate_pages": 4}
+
+    good = [rec(0, 0.25, [[0, 256]], 1), rec(1, 0.5, [[0, 512]], 2), rec(2, 0.75, [[0, 768]], 3)]
+    summ, errs = aggregate.sparse_attention_summary(good, sched, "continuous")
+    assert not errs and summ["sparse_steps"] == 3 and summ["distinct_visible_fractions"] == 3
+    shrink = [good[0], rec(1, 0.25, [[256, 512]], 1), good[2]]
+    assert any("shrank" in e for e in aggregate.sparse_attention_summary(shrink, sched, "continuous")[1])
+    fixed = [rec(0, 0.25, [[0, 256]], 1, "fixed_s1"), rec(1, 0.5, [[0, 512]], 2, "fixed_s1"),
+             rec(2, 0.25, [[0, 256]], 1, "fixed_s1")]
+    assert any("fixed" in e for e in aggregate.sparse_attention_summary(fixed, sched, "fixed_s1")[1])
+    missing = good[:2]
+    assert any("cover" in e for e in aggregate.sparse_attention_summary(missing, sched, "continuous")[1])
+    other = [rec(0, 0.25, [[0, 256]], 1, rid="x")] + good[1:]
+    assert any("another request" in e for e in aggregate.sparse_attention_summary(other, sched, "continuous")[1])
+    disagree = good + [rec(1, 0.75, [[0, 768]], 3)]
+    assert any("disagree" in e for e in aggregate.sparse_attention_summary(disagree, sched, "continuous")[1])
