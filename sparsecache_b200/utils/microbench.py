@@ -1,6 +1,6 @@
 """Isolated timings of the sm_100a kernels at Llama-3.1-8B shapes.
 
-    python -m sparsecache_b200.utils.microbench [--only gemm,gemv,attn_decode,attn_prefill,mem_attn,adamw]
+    python -m sparsecache_b200.utils.microbench [--only gemm,gemv,gemm_f32,attn_decode,attn_prefill,mem_attn,adamw]
 
 CUDA events on the launching stream, 10 warm-up launches, mean over N timed
 launches; every case uses tensors that are re-read each launch, so the
@@ -96,6 +96,18 @@ def main() -> None:
                 res[f"skinny_{name}_M{M}"] = {"us": t, "GBps": gbs, "frac_of_measured_hbm": gbs / HBM_GBS,
                                                "splits": splits}
             del w
+
+    if "gemm_f32" in only:
+        # drafter weight gradients: dW [out, in] = dY^T X over 64 rows x 256 positions (fp32 result)
+        R = 64 * 256
+        for name, M, N in (("query_dw", 1024, 4096), ("output_dw", 4096, 1024)):
+            a = (torch.randn(M, R, device=dev) * 0.02).to(bf)
+            w = (torch.randn(N, R, device=dev) * 0.02).to(bf)
+            out = torch.empty(M, N, device=dev)
+            t = timeit(lambda: ext.gemm_f32(a, w, out), n=20)
+            tf = 2.0 * M * N * R / (t * 1e-6) / 1e12
+            res[f"gemm_f32_{name}"] = {"us": t, "TFLOPs": tf, "frac_of_measured_bf16": tf / BF16_TFLOPS}
+            del a, w, out
 
     if "gemv" in only:
         for name, N, K in (("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 28672, 4096),
