@@ -276,7 +276,8 @@ class EngineWorker:
             snap = visibility_snapshot(T, order, stage_chunks(mode, p["start_fraction"], n_chunks, i), self.CHUNK)
             emit_attention_step(self.telemetry, request_id, mode, i, snap, layers=eng.cfg.n_layers)
             vis = [t for lo, hi in snap["visible_token_ranges"] for t in range(lo, hi)]
-            view[: len(vis) + i].copy_(torch.tensor(vis + list(range(T, T + i)), dtype=torch.int32))
+            # virtual keys: the visible prompt slots, the earlier drafts' slots, then this row's own slot
+            view[: len(vis) + i + 1].copy_(torch.tensor(vis + list(range(T, T + i + 1)), dtype=torch.int32))
             t_in = now_ns()
             pred = eng.verify(self.slot, torch.tensor([tok], dtype=torch.int32), position=T + i, slot_start=T + i,
                               view=view, n_visible=len(vis) + i)

@@ -471,7 +471,10 @@ class _FakeEngine:
         if view is None:
             s = sum(self.prompt)
         else:
-            s = sum(self.prompt[int(i)] for i in view[:n_visible].tolist() if int(i) < T)
+            keys = [int(i) for i in view[:n_visible + len(tokens)].tolist()]
+            # the engine attends view[0 : n_visible + M]: the new rows' own slots come last
+            assert keys[n_visible:] == list(range(slot_start, slot_start + len(tokens))), keys[n_visible:]
+            s = sum(self.prompt[i] for i in keys[:n_visible] if i < T)
         return self.torch.tensor([self._rule(t, position + j, s) for j, t in enumerate(tokens.tolist())])
 
 
