@@ -657,7 +657,7 @@ class B200Engine:
         return b
 
     def _forward_rows(self, slot: KVSlot, b: dict, M: int, splits: int, *, view: torch.Tensor | None,
-                      log: bool, feedback: bool, layers=None) -> None:
+                      log: bool, feedback: bool, layers=None, key_capacity: int = 0) -> None:
         """One forward of the M rows in b['h'][:M] at the device positions in b['pos'].
 
         With ``view`` (an int32 slot map of the slot), attention reads the
@@ -678,7 +678,7 @@ class B200Engine:
                                  b["attn"][:M], page_table=view, page_shift=0,
                                  n_virtual=pos[2:3] if view is not None else None, ws=b["attn_ws"],
                                  counters=b["attn_cnt"], l2_prefetch=[lw.w_o, lw.w_gu],
-                                 l2_prefetch_bytes=DECODE_L2_PREFETCH)
+                                 l2_prefetch_bytes=DECODE_L2_PREFETCH, key_capacity=key_capacity)
             ext.gemv_residual(b["attn"][:M], lw.w_o, None, cfg.rms_eps, h, h)
             ext.gemv_swiglu(h, lw.w_gu, lw.ln2, cfg.rms_eps, b["act"][:M])
             ext.gemv_residual(b["act"][:M], lw.w_down, None, cfg.rms_eps, h, h)
@@ -726,24 +726,34 @@ class B200Engine:
         self.ext.launches += n_steps * (5 * self.cfg.n_layers + 1)
 
     def verify(self, slot: KVSlot, tokens: torch.Tensor, *, position: int, slot_start: int | None = None,
-               view: torch.Tensor | None = None, n_visible: int | None = None) -> torch.Tensor:
+               view: torch.Tensor | None = None, n_visible: int | None = None, sparse: bool = False) -> torch.Tensor:
         """Batched verifier: forward M <= 8 tokens at positions position.. in one pass.
 
         Writes their K/V (cache slots slot_start.., default = positions) and
         returns the device int32 argmax prediction after every row (the
         target's next token given the prefix through that row).  With a
         ``view`` the keys are view[0 : n_visible] followed by the M new rows.
+
+        ``sparse`` (views only): size the attention's key split for the view's
+        n_visible + M keys instead of the slot's capacity, so a small view of a
+        long cache spreads over all CTAs.  The split boundaries then differ
+        from those of decoding, so a row's rounding can differ from the
+        verifier's: for draft steps, whose tokens are verified afterwards; a
+        verification that must equal greedy decoding keeps the default.
         """
         M = int(tokens.numel())
         if not 1 <= M <= self.MAX_ROWS:
             raise ValueError("verify handles 1..8 tokens")
+        if sparse and view is None:
+            raise ValueError("sparse applies to verification over a view")
         b = self._decode_buffers()
-        splits = self._decode_splits(slot.capacity)
+        nv = None if view is None else int(n_visible) + M
+        key_cap = nv if sparse else 0
+        splits = self._decode_splits(key_cap if sparse else slot.capacity)
         b["ids"][:M].copy_(tokens.to(torch.int32), non_blocking=True)
         self.ext.embedding(b["ids"][:M], self.w.embed, b["h"][:M])
-        nv = None if view is None else int(n_visible) + M
         self.set_decode_state(position=position, slot=slot_start, n_virtual=nv)
-        self._forward_rows(slot, b, M, splits, view=view, log=False, feedback=False)
+        self._forward_rows(slot, b, M, splits, view=view, log=False, feedback=False, key_capacity=key_cap)
         return b["tok"][:M]
 
     def generated_tokens(self, max_new: int) -> torch.Tensor:

@@ -367,20 +367,22 @@ cudaError_t attention_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
   const int S = a.splits;
   if (S < 1 || S > 16) return cudaErrorInvalidValue;
   if (a.pos_rows != nullptr && (a.M != 1 || a.n_seq < 1 || a.page_table != nullptr)) return cudaErrorInvalidValue;
+  if (a.key_cap < 0) return cudaErrorInvalidValue;
+  const int cap = a.key_cap > 0 ? a.key_cap : a.cache_cap;  // keys the geometry is sized for
   int outer = 1;
   if (a.ws != nullptr && a.counters != nullptr && a.pos_rows == nullptr) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    outer = a.outer > 0 ? a.outer : attention_decode_outer(a.cache_cap, a.n_kv_heads, S, sms);
+    outer = a.outer > 0 ? a.outer : attention_decode_outer(cap, a.n_kv_heads, S, sms);
     if (outer > kMaxOuter) return cudaErrorInvalidValue;
   }
-  // keys per CTA: the cache capacity (+ the largest row block) split evenly
-  // over all S * outer CTAs, rounded to 16 keys; independent of M so a row
-  // sees the same split boundaries (and the same rounding) in decode and in
+  // keys per CTA: the capacity (+ the largest row block) split evenly over
+  // all S * outer CTAs, rounded to 16 keys; independent of M so a row sees
+  // the same split boundaries (and the same rounding) in decode and in
   // batched verification
   const int total = S * outer;
-  int chunk = (a.cache_cap + kMaxRows + total - 1) / total;
+  int chunk = (cap + kMaxRows + total - 1) / total;
   chunk = (chunk + 15) / 16 * 16;
   const int qv = a.M * G;
   auto kern = attention_decode_reg_kernel;

@@ -724,9 +724,15 @@ void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int6
                       double scale, int64_t splits, Tensor out, c10::optional<Tensor> page_table,
                       int64_t page_shift, c10::optional<Tensor> n_virtual, c10::optional<Tensor> ws,
                       c10::optional<Tensor> counters, int64_t outer, c10::optional<Tensor> pos_rows,
-                      int64_t seq_stride, std::vector<Tensor> l2_prefetch, int64_t l2_prefetch_bytes) {
+                      int64_t seq_stride, std::vector<Tensor> l2_prefetch, int64_t l2_prefetch_bytes,
+                      int64_t key_capacity) {
   const c10::cuda::CUDAGuard guard(q.device());
   CHECK_BF16(q); CHECK_BF16(out); CHECK_I32(pos);
+  // key_capacity > 0 sizes the split for that many keys (it must bound the call's key count:
+  // a sparse view's visible keys plus the query rows); 0 sizes it for the whole cache
+  TORCH_CHECK(key_capacity >= 0 && key_capacity <= k_cache.size(1) + 64, "key_capacity");
+  TORCH_CHECK(key_capacity == 0 || (page_table.has_value() && page_table->defined()),
+              "key_capacity applies to paged views only");
   TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(2) == 128 && k_cache.is_contiguous(), "k_cache");
   sc::AttnDecodeArgs a{};
   a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
@@ -739,6 +745,7 @@ void attention_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, int6
   a.n_kv_heads = (int)k_cache.size(0);
   a.scale = (float)scale;
   a.splits = (int)splits;
+  a.key_cap = (int)key_capacity;
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   if (page_table.has_value() && page_table->defined()) {
     CHECK_I32(*page_table);
@@ -1567,7 +1574,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("page_table") = py::none(), py::arg("page_shift") = 6, py::arg("n_virtual") = py::none(),
         py::arg("ws") = py::none(), py::arg("counters") = py::none(), py::arg("outer") = 0,
         py::arg("pos_rows") = py::none(), py::arg("seq_stride") = 0,
-        py::arg("l2_prefetch") = std::vector<Tensor>{}, py::arg("l2_prefetch_bytes") = 0);
+        py::arg("l2_prefetch") = std::vector<Tensor>{}, py::arg("l2_prefetch_bytes") = 0,
+        py::arg("key_capacity") = 0);
   m.def("attention_decode_outer", [](int64_t cap, int64_t kvh, int64_t cluster, int64_t sms) {
     return sc::attention_decode_outer((int)cap, (int)kvh, (int)cluster, (int)sms);
   });

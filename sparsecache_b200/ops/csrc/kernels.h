@@ -254,6 +254,13 @@ struct AttnDecodeArgs {
   const int* pos_rows;
   long long seq_stride;
   int n_seq;
+  // Geometry key count (0: cache_cap): keys per CTA and clusters per kv head
+  // are sized for this many keys instead of the whole cache.  Must bound the
+  // call's key count.  Sparse draft steps over a small view of a long cache
+  // set it to the view's keys (their boundaries need not match the verifier's);
+  // decode and verification keep 0, so a row sees the same split boundaries
+  // in both.
+  int key_cap;
   // Optional L2 prefetch of the next kernels' weights (bytes multiples of 16,
   // 16-byte-aligned bases): the key loop leaves HBM mostly idle, so the
   // o-projection and the start of the gate/up weights can stream into L2

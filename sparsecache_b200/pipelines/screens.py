@@ -124,11 +124,11 @@ def sparse_page_crossover(engine, context_lengths: Sequence[int], fractions: Seq
         tok = torch.tensor([1], dtype=torch.int32)
         view = torch.zeros(slot.capacity, dtype=torch.int32, device=dev)
 
-        def step(n_vis=None):
+        def step(n_vis=None, sparse=False):
             if n_vis is None:
                 engine.verify(slot, tok, position=T)
             else:
-                engine.verify(slot, tok, position=T, slot_start=T, view=view, n_visible=n_vis)
+                engine.verify(slot, tok, position=T, slot_start=T, view=view, n_visible=n_vis, sparse=sparse)
 
         def timed(fn):
             for _ in range(3):
@@ -146,9 +146,12 @@ def sparse_page_crossover(engine, context_lengths: Sequence[int], fractions: Seq
             idx = page_view(T, f)
             view[: idx.numel()].copy_(idx.to(torch.int32))
             view[idx.numel()] = T  # the draft row's own slot follows the visible keys
-            ms = timed(lambda: step(idx.numel()))
+            ms = timed(lambda: step(idx.numel(), sparse=True))
+            # the same view with the attention split sized for the whole cache (the verifier's geometry)
+            ms_cap = timed(lambda: step(idx.numel()))
             rows.append({"context_tokens": T, "visible_fraction": idx.numel() / T, "requested_fraction": f,
-                         "draft_step_ms": ms, "full_step_ms": full_ms, "speedup": full_ms / ms})
+                         "draft_step_ms": ms, "draft_step_capacity_split_ms": ms_cap, "full_step_ms": full_ms,
+                         "speedup": full_ms / ms})
     return rows
 
 

@@ -280,7 +280,7 @@ class EngineWorker:
             view[: len(vis) + i + 1].copy_(torch.tensor(vis + list(range(T, T + i + 1)), dtype=torch.int32))
             t_in = now_ns()
             pred = eng.verify(self.slot, torch.tensor([tok], dtype=torch.int32), position=T + i, slot_start=T + i,
-                              view=view, n_visible=len(vis) + i)
+                              view=view, n_visible=len(vis) + i, sparse=True)
             emit("input_trace", {"request_id": request_id, "recorded_at_ns": t_in, "input_token_ids": [tok],
                                  "positions": [T + i], "num_scheduled_tokens": 1})
             tok = int(pred[0].item())

@@ -592,7 +592,8 @@ def continuous_graft_chain(engine, stager: TrancheStager, *, seed_token: int, pr
         t0 = clock()
         refresh_view(arrived_tokens)
         pred = engine.verify(slot, torch.tensor([token], dtype=torch.int32), position=T + len(drafts),
-                             slot_start=tail[len(drafts)], view=view, n_visible=arrived_tokens + len(drafts))
+                             slot_start=tail[len(drafts)], view=view, n_visible=arrived_tokens + len(drafts),
+                             sparse=True)
         token = int(pred[0].item())
         draft_ms += (clock() - t0) * 1000
         state.record_draft_token(token)

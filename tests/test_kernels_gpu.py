@@ -362,6 +362,43 @@ def test_attention_decode_two_level_split(cuda_device, M, hkv, cap):
         assert int(cnt.sum()) == 0
 
 
+@pytest.mark.parametrize("M", [1, 3])
+@pytest.mark.parametrize("n_vis", [700, 5000])
+def test_attention_decode_sparse_view_key_capacity(cuda_device, M, n_vis):
+    """A small page view of a long cache: the split sized for the view's keys (key_capacity) and the
+    split sized for the whole cache both equal the fp32 reference over the gathered keys."""
+    hkv, G, cap = 8, 4, 40000
+    H = hkv * G
+    g = torch.Generator(device="cpu").manual_seed(n_vis + M)
+    kc = torch.randn(hkv, cap, 128, generator=g).to(cuda_device, torch.bfloat16)
+    vc = torch.randn(hkv, cap, 128, generator=g).to(cuda_device, torch.bfloat16)
+    q = torch.randn(M, H * 128, generator=g).to(cuda_device, torch.bfloat16)
+    p0 = cap - 64  # the query rows' own slots (their K/V already in the cache)
+    vis = torch.sort(torch.randperm(p0, generator=g)[:n_vis]).values
+    table = torch.cat((vis, torch.arange(p0, p0 + M))).to(torch.int32).to(cuda_device)
+    view = torch.zeros(cap, dtype=torch.int32, device=cuda_device)
+    view[: table.numel()] = table
+    nv = torch.tensor([n_vis + M], dtype=torch.int32, device=cuda_device)
+    pos = torch.tensor([p0], dtype=torch.int32, device=cuda_device)
+    idx = table.long()
+    ref = _attn_reference(q, kc[:, idx], vc[:, idx], n_vis + torch.arange(M, device=cuda_device),
+                          torch.arange(n_vis + M, device=cuda_device), H)
+    ws = torch.zeros(hkv * 16 * 64 * 130, device=cuda_device)
+    cnt = torch.zeros(hkv * 16, device=cuda_device, dtype=torch.int32)
+    outs = []
+    for key_cap in (n_vis + M, 0):
+        S = _ext().attention_decode_cluster(key_cap or cap, hkv)
+        out = torch.empty(M, H * 128, device=cuda_device, dtype=torch.bfloat16)
+        _ext().attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), S, out, page_table=view, page_shift=0,
+                                n_virtual=nv, ws=ws, counters=cnt, key_capacity=key_cap)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+        assert int(cnt.sum()) == 0
+        outs.append(out)
+    with pytest.raises(RuntimeError):  # the key-count split is for paged views only
+        _ext().attention_decode(q, kc, vc, pos, H, 1 / math.sqrt(128), 8, outs[0], key_capacity=n_vis + M)
+
+
 def _rms_ref(x, w, eps):
     xf = x.float()
     r = torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps)

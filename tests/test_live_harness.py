@@ -466,7 +466,8 @@ class _FakeEngine:
     def generated_tokens(self, n):
         return self.b["log"][:n]
 
-    def verify(self, slot, tokens, *, position, slot_start=None, view=None, n_visible=None):
+    def verify(self, slot, tokens, *, position, slot_start=None, view=None, n_visible=None, sparse=False):
+        assert not sparse or view is not None  # the split sized for the view applies to views only
         T = len(self.prompt)
         if view is None:
             s = sum(self.prompt)
