@@ -90,9 +90,8 @@ __device__ __forceinline__ void load_batch(const uint4* w0, const uint4* w1, int
 // in shared memory; used when M * K * 2 bytes exceed the shared-memory budget
 // (the batched verifier's down projection at large FFN widths).  No prologue
 // RMSNorm in that mode.
-template <int MR, bool kXG = false>
-__global__ void __launch_bounds__(kThreads)
-    gemv_kernel(GemvArgs a) {
+template <int MR, bool kXG>
+__device__ __forceinline__ void gemv_body(const GemvArgs& a) {
   extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);  // [MR][K]
   __shared__ float red[kWarps][MR];
@@ -460,6 +459,27 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+template <int MR, bool kXG = false>
+__global__ void __launch_bounds__(kThreads) gemv_kernel(GemvArgs a) {
+  gemv_body<MR, kXG>(a);
+}
+
+// One-row calls whose grid needs 2-3 waves at 2 CTAs per SM (e.g. the 8B QKV
+// projection's 384 CTAs): registers capped so three CTAs fit an SM and the
+// grid runs as one wave.  The same body, so the same arithmetic and bits.
+__global__ void __launch_bounds__(kThreads, 3) gemv_kernel_one_wave(GemvArgs a) {
+  gemv_body<1, false>(a);
+}
+
+// One-wave variant for 2-3-wave one-row grids; SC_GEMV_THREE_PER_SM=0 turns it off (A/B runs).
+static bool gemv_three_per_sm() {
+  static const bool on = [] {
+    const char* e = getenv("SC_GEMV_THREE_PER_SM");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
 cudaError_t gemv_bf16(const GemvArgs& a, cudaStream_t stream) {
   if (a.M < 1 || a.M > 8 || (a.K % 8) != 0 || (a.N % 2) != 0) return cudaErrorInvalidValue;
   const size_t smem = (size_t)a.M * a.K * 2;
@@ -493,6 +513,11 @@ cudaError_t gemv_bf16(const GemvArgs& a, cudaStream_t stream) {
   if (xg) {
     if (a.M <= 4) return cudaLaunchKernelEx(&cfg, gemv_kernel<4, true>, a);
     return cudaLaunchKernelEx(&cfg, gemv_kernel<8, true>, a);
+  }
+  if (a.M == 1 && gemv_three_per_sm() && grid > 2 * (a.num_sms > 0 ? a.num_sms : 148) &&
+      grid <= 3 * (a.num_sms > 0 ? a.num_sms : 148)) {
+    ensure_smem_attr(gemv_kernel_one_wave, 200 * 1024);
+    return cudaLaunchKernelEx(&cfg, gemv_kernel_one_wave, a);
   }
   if (a.M == 1) SC_LAUNCH_GEMV(1)
   else if (a.M <= 2) SC_LAUNCH_GEMV(2)
