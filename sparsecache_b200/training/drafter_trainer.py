@@ -44,6 +44,7 @@ from __future__ import annotations
 
 import json
 import math
+import os
 import time
 from dataclasses import asdict, dataclass
 from pathlib import Path
@@ -295,7 +296,7 @@ class DataParallelAdamW(FusedAdamW):
         return self.flag_ptrs[peer] + 4 * (kind * 8 + self.rank)
 
     # -------------------------------------------- reduce-scatter overlapped with the backward
-    def enable_buckets(self, buckets: list[list[tuple[int, int]]], *, grid: int = 32) -> None:
+    def enable_buckets(self, buckets: list[list[tuple[int, int]]], *, grid: int | None = None) -> None:
         """Reduce the gradient bucket by bucket as the backward finishes them.
 
         ``buckets[b]`` lists flat ranges.  Each rank releases bucket b's flag
@@ -303,14 +304,18 @@ class DataParallelAdamW(FusedAdamW):
         (``bucket_ready``); a side stream then waits (bounded) for every
         rank's release and sums this rank's shard of the bucket, while the
         main stream goes on with the backward.  ``grid`` CTAs per bucket
-        kernel leave the SMs to the backward's GEMMs.
+        kernel (default 2 per SM: the reduction is NVLink- and HBM-bound, and
+        32 CTAs measured slower than no overlap at all).
         """
         nb = len(buckets)
         self.buckets = buckets
         self.bucket_buf, self.bucket_ptrs = self.group.shared(4 * 8 * nb)
         self.bucket_flags = self.bucket_buf.view(torch.int32).view(nb, 8)
         self.comm = torch.cuda.Stream(self.flat.param.device)
-        self.reduce_grid = grid
+        if grid is None:  # 2 CTAs per SM; SC_DP_BUCKET_GRID overrides (A/B runs)
+            sms = torch.cuda.get_device_properties(self.flat.param.device).multi_processor_count
+            grid = int(os.environ.get("SC_DP_BUCKET_GRID", str(2 * sms)))
+        self.reduce_grid = max(1, min(1024, grid))
 
     def bucket_ready(self, b: int) -> None:
         x = ops.ext()
