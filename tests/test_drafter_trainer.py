@@ -207,3 +207,23 @@ def test_flat_buckets_cover_the_buffer_once():
     for p, ranges in zip(late, buckets[1:]):
         (lo, hi), = ranges
         assert hi - lo == p.numel() and p.grad.data_ptr() == tr.flat.grad[lo:].data_ptr()
+
+
+def test_weight_grad_stash_rejects_misuse():
+    import pytest
+
+    from sparsecache_b200.training.deferred_grad import WeightGradStash
+
+    lin = torch.nn.Linear(8, 4, bias=False)
+    st = WeightGradStash(torch.device("cpu"))
+    st.register(lin)
+    st.begin(rows_per_call=3, max_calls=2)
+    assert st.xT[0].shape == (8, 64) and st.dyT[0].shape == (4, 64)  # padded to the GEMM's K tile
+    st.next_call(0, lin.weight)
+    st.next_call(0, lin.weight)
+    with pytest.raises(RuntimeError):
+        st.next_call(0, lin.weight)
+    with pytest.raises(ValueError):
+        st.put_x(0, 0, torch.zeros(5, 8))  # 5 rows where each call has 3
+    with pytest.raises(ValueError):
+        WeightGradStash(torch.device("cpu")).register(torch.nn.Linear(8, 4))  # biased linears are not deferred

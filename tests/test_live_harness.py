@@ -544,3 +544,18 @@ def test_sparse_attention_gate_rejects_bad_views():
     assert any("another request" in e for e in aggregate.sparse_attention_summary(other, sched, "continuous")[1])
     disagree = good + [rec(1, 0.75, [[0, 768]], 3)]
     assert any("disagree" in e for e in aggregate.sparse_attention_summary(disagree, sched, "continuous")[1])
+
+
+def test_visibility_snapshot_and_stage_chunks():
+    from sparsecache_b200.serving.live.worker import stage_chunks, visibility_snapshot
+
+    snap = visibility_snapshot(700, [0, 2, 1], 2, 256)  # chunks 0 and 2 of [0,256) [256,512) [512,700)
+    assert snap["visible_token_ranges"] == [[0, 256], [512, 700]]
+    assert snap["visible_pages"] == 2 and snap["candidate_pages"] == 3
+    assert abs(snap["visible_fraction"] - (256 + 188) / 700) < 1e-12
+    merged = visibility_snapshot(700, [1, 0], 2, 256)  # adjacent chunks merge into one range
+    assert merged["visible_token_ranges"] == [[0, 512]]
+    assert visibility_snapshot(700, [5, 0], 2, 256)["visible_pages"] == 1  # out-of-range chunk ids are ignored
+    assert [stage_chunks("fixed_s1", 0.05, 4, i) for i in range(5)] == [1] * 5
+    assert [stage_chunks("continuous", 0.05, 4, i) for i in range(5)] == [1, 2, 3, 4, 4]
+    assert stage_chunks("continuous", 0.6, 4, 0) == 3
