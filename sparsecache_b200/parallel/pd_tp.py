@@ -53,6 +53,7 @@ CUDA events on the decode ranks, max over ranks.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import random
@@ -349,7 +350,12 @@ def main() -> None:
     if "poisson" in modes and args.arrival_rate <= 0:
         raise SystemExit("--mode poisson needs --arrival-rate > 0")
     try:
-        for mode in modes:
+        for i, mode in enumerate(modes):
+            if i:  # the previous arm's engines, peer mappings and cached blocks are gone before the next
+                gc.collect()
+                torch.cuda.synchronize()
+                torch.cuda.empty_cache()
+                dist.barrier()
             run = argparse.Namespace(**{**vars(args), "mode": "push" if mode == "poisson" else mode})
             out = run_poisson(run) if mode == "poisson" else run_closed_loop(run)
             if out is not None:
