@@ -323,6 +323,24 @@ def run_poisson(args) -> dict | None:
                                                                  "decoder_queue_ms") for q in (0.5, 0.99)}}
 
 
+def parse_modes(mode: str, arrival_rate: float) -> list[str]:
+    """The arms of one run: ``push`` / ``nccl`` (closed loop) and ``poisson`` (open loop), in order.
+
+    A lone ``push`` with an arrival rate means Poisson arrivals only (the
+    single-mode form of the command line).
+    """
+    modes = [m.strip() for m in mode.split(",") if m.strip()]
+    if not modes or any(m not in ("push", "nccl", "poisson") for m in modes):
+        raise ValueError(f"--mode: expected push, nccl or poisson (comma list), got {mode!r}")
+    if len(set(modes)) != len(modes):
+        raise ValueError(f"--mode: an arm is listed twice in {mode!r}")
+    if modes == ["push"] and arrival_rate > 0:
+        modes = ["poisson"]
+    if "poisson" in modes and arrival_rate <= 0:
+        raise ValueError("--mode poisson needs --arrival-rate > 0")
+    return modes
+
+
 def main() -> None:
     p = argparse.ArgumentParser(description="TPn prefill -> TPn decode with the fused NVLink KV push")
     p.add_argument("--tp", type=int, default=4)
@@ -342,13 +360,10 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
-    modes = [m.strip() for m in args.mode.split(",") if m.strip()]
-    if any(m not in ("push", "nccl", "poisson") for m in modes) or not modes:
-        raise SystemExit(f"--mode: expected push, nccl or poisson (comma list), got {args.mode!r}")
-    if modes == ["push"] and args.arrival_rate > 0:
-        modes = ["poisson"]
-    if "poisson" in modes and args.arrival_rate <= 0:
-        raise SystemExit("--mode poisson needs --arrival-rate > 0")
+    try:
+        modes = parse_modes(args.mode, args.arrival_rate)
+    except ValueError as exc:
+        raise SystemExit(str(exc)) from None
     try:
         for i, mode in enumerate(modes):
             if i:  # the previous arm's engines, peer mappings and cached blocks are gone before the next

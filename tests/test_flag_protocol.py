@@ -187,3 +187,17 @@ def test_pd_slot_reuse_waits_for_the_decoder(n_slots):
 def test_pd_slot_reuse_without_the_free_flag_races():
     """Dropping the free-flag wait lets a fast prefill overwrite a slot the decoder is still reading."""
     assert any(_serve_pair(24, 2, wait_free=False, seed=s) for s in range(3))
+
+
+def test_pd_tp_mode_list():
+    import pytest
+
+    from sparsecache_b200.parallel.pd_tp import parse_modes
+
+    assert parse_modes("push", 0.0) == ["push"]
+    assert parse_modes("push", 2.0) == ["poisson"]  # the single-mode form with a rate
+    assert parse_modes("push,nccl,poisson", 2.0) == ["push", "nccl", "poisson"]
+    assert parse_modes(" nccl , push ", 0.0) == ["nccl", "push"]
+    for bad, rate in (("push,poisson", 0.0), ("tcp", 0.0), ("", 0.0), ("push,push", 0.0)):
+        with pytest.raises(ValueError):
+            parse_modes(bad, rate)
