@@ -14,6 +14,9 @@ backends, the drafts run on this package's engine.
   * ``sparse_page_crossover``: per-token cost of a draft step whose attention reads a page view
     (64 sink + 512 recent + evenly spaced 64-token pages up to the visible fraction) against a
     full-context step, over fractions and context lengths: where sparse drafting stops paying.
+    The draft step sizes its attention split for the view's keys (``verify(..., sparse=True)``);
+    each row also times the same view with the split sized for the whole cache (the verifier's
+    geometry), which shows what that sizing is worth.
 The EAGLE drafter's screen is ``training.drafter_trainer.evaluate_drafter``.
 """
 from __future__ import annotations

@@ -229,3 +229,16 @@ def test_speculative_loop_host_logic():
         assert all(a == right for a in out["accepted"][:-1])
         # every verify after the first starts right after the previously committed tokens
         assert [p for p, _ in calls][:3] == [T, T + 1, T + 2 + right]
+
+
+def test_page_view_sink_recent_and_budget():
+    from sparsecache_b200.pipelines.screens import page_view
+
+    T = 32768
+    v = page_view(T, 0.05)
+    idx = v.tolist()
+    assert idx == sorted(set(idx)) and idx[-1] == T - 1
+    assert set(range(64)) <= set(idx) and set(range(T - 512, T)) <= set(idx)  # sink and recent always visible
+    assert abs(len(idx) / T - 0.05) < 0.01
+    small = page_view(T, 0.001)  # the budget never drops below sink + recent
+    assert len(small) >= 64 + 512
